@@ -1,0 +1,49 @@
+/* zonos3_b200.h — C ABI of libzonos3_b200.so, the B200 (sm_100a) kernels of the ZONOS3-Mini LM-backbone hot path.
+ *
+ * Conventions shared by every entry point:
+ *  - All tensor pointers are DEVICE pointers owned by the caller; the library allocates nothing unless an entry
+ *    point says so. bf16 tensors are passed as uint16_t* (raw bf16 bits), fp32 as float*.
+ *  - Every call is asynchronous on `stream` and never synchronises the host, so it can be captured in a CUDA graph.
+ *  - Every call returns an int status: 0 ok, 1 invalid argument (rejected before any launch), 2 CUDA error,
+ *    3 unsupported size, 4 a bounded device-side wait expired. zb_last_error() gives the message of the last
+ *    failure on the calling host thread. No C++ exception crosses this boundary.
+ *  - Strides are in elements. "[B, H, d]" means B rows of H*d contiguous elements with a caller-given row stride.
+ */
+#ifndef ZONOS3_B200_H_
+#define ZONOS3_B200_H_
+
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* zb_last_error(void);
+void zb_clear_error(void);
+int zb_version(void);
+
+/* ------------------------------------------------------------------------------------------- gated DeltaNet */
+
+/* One recurrent gated-delta-rule step per stream, state updated in place.
+ * Replaces the per-token recurrence of model/src/zonos3/reference/lm.py:576-582 and the decode use of
+ * FLA chunk_gated_delta_rule_fwd in servers/sgl/src/zonos3_sgl/models/gdn.py:418-434 (via _forward_decode_static,
+ * gdn.py:329-355).
+ *   q, k   [B, H, dk] bf16, L2-normalised per head; row strides q_stride_b, k_stride_b (multiples of 4)
+ *   v      [B, H, dv] bf16, row stride v_stride_b
+ *   g      [B, H] fp32 log-decay (decay = exp(g)); beta [B, H] fp32; both with row stride gb_stride_b
+ *   state  [num_slots, H, dv, dk] fp32 (V-first), 16-byte aligned; stream b uses slot slots[b] (slots == NULL:
+ *          slot b); a negative or out-of-range slot marks a padding row: its output is 0 and no state changes
+ *   out    [B, H, dv] bf16 = S_new (q * scale), row stride out_stride_b
+ *   dk in {64, 128}. */
+int zb_gdn_decode_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q_stride_b,
+                       int64_t k_stride_b, int64_t v_stride_b, const float* g, const float* beta,
+                       int64_t gb_stride_b, float* state, const int64_t* slots, int64_t num_slots, uint16_t* out,
+                       int64_t out_stride_b, int B, int H, int dk, int dv, float scale, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZONOS3_B200_H_ */

@@ -1,0 +1,77 @@
+"""ctypes binding of ``libzonos3_b200.so``, the C-ABI library every op of this package calls.
+
+There is no fallback: when the library is missing or a call fails, the op raises. Status codes follow
+``include/zonos3_b200.h``: 1 (invalid argument) raises ``ValueError``, every other non-zero status raises
+``RuntimeError`` with the library's ``zb_last_error()`` message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "libzonos3_b200.so"
+
+_p = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+# name -> argument types (every entry point returns int status unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "zb_last_error": [],
+    "zb_clear_error": [],
+    "zb_version": [],
+    # q, k, v, q_stride_b, k_stride_b, v_stride_b, g, beta, gb_stride_b, state, slots, num_slots,
+    # out, out_stride_b, B, H, dk, dv, scale, stream
+    "zb_gdn_decode_step": [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64,
+                           _i32, _i32, _i32, _i32, _f32, _p],
+}
+_RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and declare every entry point's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY.exists():
+                raise LibraryMissing(
+                    f"{LIBRARY.name} is not built; run __graft_entry__.build() (nvcc, sm_100a) first"
+                )
+            lib = ctypes.CDLL(str(LIBRARY))
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().zb_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status == 0:
+        return
+    msg = f"{what}: {last_error()} (status {status})"
+    if status == 1:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def call(name: str, *args) -> None:
+    """Call entry point ``name`` and raise on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
