@@ -268,10 +268,20 @@ def run_ours(args, dist, rank, world, local):
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks.summary(),
     }
-    traffic = ROOT / "profiles" / "gdn_decode_traffic.json"
-    if traffic.exists():
-        line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("bytes_per_launch")
+    line["roofline"]["traffic"] = profiled_traffic("gdn_decode_cfg2.md")
     return line
+
+
+def profiled_traffic(summary: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in the
+    committed summary under profiles/, or None."""
+    path = ROOT / "profiles" / summary
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1])
+    return None
 
 
 def cpu_reference(updates: int, streams=STREAMS):

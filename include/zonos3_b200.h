@@ -24,6 +24,12 @@ const char* zb_last_error(void);
 void zb_clear_error(void);
 int zb_version(void);
 
+/* Reads the current device's status word (bits set by kernels whose bounded device-side waits expired:
+ * 1 = AttnRes source load, 2 = grouped GEMM pipeline, 4 = chunked prefill pipeline); clear != 0 resets it.
+ * Synchronous (a device-to-host copy); for diagnostics and tests, not for the hot path. No reference counterpart:
+ * the reference's kernels have no device-side waits. */
+int zb_device_status(unsigned* flags, int clear);
+
 /* ------------------------------------------------------------------------------------------- gated DeltaNet */
 
 /* One recurrent gated-delta-rule step per stream, state updated in place.
@@ -41,6 +47,25 @@ int zb_gdn_decode_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int64_t k_stride_b, int64_t v_stride_b, const float* g, const float* beta,
                        int64_t gb_stride_b, float* state, const int64_t* slots, int64_t num_slots, uint16_t* out,
                        int64_t out_stride_b, int B, int H, int dk, int dv, float scale, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------------------- Full AttnRes */
+
+/* Full AttnRes route of every token over bank sources [0, S) plus, if `source` is non-NULL, `source` as the last
+ * source; reads every source row from HBM once (one TMA bulk copy per source slice into shared memory).
+ * Replaces full_attnres_route (model/src/zonos3/reference/lm.py:384-389; servers/sgl/src/zonos3_sgl/models/
+ * zonos3.py:99-113) and _FusedFullAttnRes.forward / _block_attnres_fwd_kernel
+ * (servers/sgl/src/zonos3_sgl/models/training_attnres_kernels.py:2727-2779, :1268-1348), with the bank append of
+ * FusedBlockAttnResContext.route_metadata (training_attnres_kernels.py:1491-1513) and the RMSNorm that follows each
+ * route (servers/sgl/src/zonos3_sgl/models/training_attnres.py:67-70) fused in.
+ *   bank        [>= S, T, D] bf16, bank_stride elements between sources (multiple of 8), rows [T, D] contiguous
+ *   source      [T, D] bf16 or NULL; append: [T, D] bf16 destination for `source` or NULL
+ *   query       [D] bf16; eps: the key RMSNorm epsilon
+ *   norm_weight [D] bf16 or NULL: out = RMSNorm(mix; norm_weight, norm_eps) and mix_out (optional) = mix;
+ *               NULL: out = mix (mix_out must be NULL)
+ *   D a multiple of 256 (at most 16384), S + (source != NULL) in [1, 256]; all pointers 16-byte aligned. */
+int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, const uint16_t* source, uint16_t* append,
+                     const uint16_t* query, float eps, const uint16_t* norm_weight, float norm_eps, uint16_t* out,
+                     uint16_t* mix_out, int T, int D, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

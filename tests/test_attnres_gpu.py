@@ -1,0 +1,93 @@
+"""GPU parity of the Full AttnRes route (zb_attnres_route) against the CPU oracle (lm.py:384-389).
+
+The kernel keeps the reference Triton kernel's bf16 rounding points, so besides the north_star tolerance (bf16
+activations within 2e-2 relative) nearly every element is expected to be bit-identical to the oracle; the tests
+require at least 99% identical elements."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import attnres as oattn
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+EPS = 1e-5
+
+
+def make_bank(S, T, D, seed):
+    gen = torch.Generator().manual_seed(seed)
+    bank = torch.stack([torch.randn(T, D, generator=gen) * (0.5 + s % 3) for s in range(S)]).bfloat16()
+    query = (0.02 * torch.randn(D, generator=gen) * 10).bfloat16()
+    return bank, query
+
+
+def identical_fraction(a, b):
+    return (a.cpu().view(torch.int16) == b.cpu().view(torch.int16)).float().mean().item()
+
+
+def test_reference_golden_routes(zb, golden):
+    g = golden("attnres.npz")
+    for tag in ("bf16", "one"):
+        sources = g[f"{tag}_sources"].bfloat16()
+        query = g[f"{tag}_query"].bfloat16()
+        ref = g[f"{tag}_out"].bfloat16()
+        out = zb.ops.attnres_route(sources.cuda(), sources.shape[0], query.cuda(), EPS)
+        torch.cuda.synchronize()
+        assert rel_err(out.float(), ref.float()) < TOL, tag
+        assert identical_fraction(out, ref) > 0.99, tag
+
+
+@pytest.mark.parametrize("S,T,D", [(1, 1, 256), (2, 5, 512), (9, 33, 1024), (17, 64, 2048), (49, 256, 2048),
+                                   (25, 7, 4096), (3, 4, 1536)])
+def test_route_matches_oracle(zb, S, T, D):
+    bank, query = make_bank(S, T, D, seed=S * 31 + T)
+    ref = oattn.full_attnres_route(bank, query, EPS)
+    out = zb.ops.attnres_route(bank.cuda(), S, query.cuda(), EPS)
+    torch.cuda.synchronize()
+    assert rel_err(out.float(), ref.float()) < TOL
+    assert identical_fraction(out, ref) > 0.99
+
+
+def test_source_append_and_fused_norm(zb):
+    """Route over bank[:S] + source with the source appended to bank[S] and the following RMSNorm fused."""
+    S, T, D = 12, 40, 2048
+    bank, query = make_bank(S + 1, T, D, seed=77)
+    source = bank[S].clone()
+    gen = torch.Generator().manual_seed(78)
+    norm_w = (1 + 0.1 * torch.randn(D, generator=gen)).bfloat16()
+    ref_mix = oattn.full_attnres_route(bank, query, EPS)
+    ref_norm = oattn.weighted_rms_norm(ref_mix, norm_w, EPS)
+    d_bank = bank.cuda()
+    d_bank[S].zero_()
+    mix = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    out = zb.ops.attnres_route(d_bank, S, query.cuda(), EPS, source=source.cuda(), append_to=d_bank[S],
+                               norm_weight=norm_w.cuda(), norm_eps=EPS, mix_out=mix)
+    torch.cuda.synchronize()
+    assert torch.equal(d_bank[S].cpu(), source)
+    assert rel_err(mix.float(), ref_mix.float()) < TOL and identical_fraction(mix, ref_mix) > 0.99
+    assert rel_err(out.float(), ref_norm.float()) < TOL and identical_fraction(out, ref_norm) > 0.99
+    assert zb.ops.device_status() == 0
+
+
+def test_first_route_has_only_the_source(zb):
+    T, D = 6, 1024
+    bank, query = make_bank(1, T, D, seed=5)
+    out = zb.ops.attnres_route(None, 0, query.cuda(), EPS, source=bank[0].cuda())
+    torch.cuda.synchronize()
+    # one source: its softmax weight is exactly 1, so the route returns the source itself
+    assert torch.equal(out.cpu(), bank[0])
+
+
+def test_bank_with_padding_stride(zb):
+    """A bank allocated for more tokens than routed (graph padding) is addressed through its stride."""
+    S, T, D = 5, 10, 512
+    bank, query = make_bank(S, 16, D, seed=3)
+    view = bank.cuda()[:, :T]
+    ref = oattn.full_attnres_route(bank[:, :T], query, EPS)
+    out = zb.ops.attnres_route(view, S, query.cuda(), EPS)
+    torch.cuda.synchronize()
+    assert rel_err(out.float(), ref.float()) < TOL

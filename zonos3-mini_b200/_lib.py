@@ -23,10 +23,13 @@ SIGNATURES: dict[str, list] = {
     "zb_last_error": [],
     "zb_clear_error": [],
     "zb_version": [],
+    "zb_device_status": [_p, _i32],
     # q, k, v, q_stride_b, k_stride_b, v_stride_b, g, beta, gb_stride_b, state, slots, num_slots,
     # out, out_stride_b, B, H, dk, dv, scale, stream
     "zb_gdn_decode_step": [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64,
                            _i32, _i32, _i32, _i32, _f32, _p],
+    # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream
+    "zb_attnres_route": [_p, _i64, _i32, _p, _p, _p, _f32, _p, _f32, _p, _p, _i32, _i32, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None}
 

@@ -1,0 +1,107 @@
+"""Full AttnRes with the reference's module-level API, on the B200 route kernel (``zb_attnres_route``).
+
+Drop-in names and signatures:
+
+* ``full_attnres_route(sources, query, norm_eps)`` — servers/sgl/src/zonos3_sgl/models/zonos3.py:99-113
+  (and model/src/zonos3/reference/lm.py:384-389, which takes a list of sources);
+* ``FusedBlockAttnResContext(max_completed_blocks, reference, gradient_dtype)`` — the persistent bank of
+  servers/sgl/src/zonos3_sgl/models/training_attnres_kernels.py:1438-1513 (forward use: ``blocks``,
+  ``completed_count``, ``call_count``, ``validate_owner``, ``completed_view``);
+* ``fused_full_attnres(state, source, query, norm_eps, append_current)`` — training_attnres_kernels.py:2826-2840.
+
+Inference only: the reference's autograd backward (used by its trainer) is not part of the serving hot path.
+The bank append happens inside the route kernel, and when the caller already wrote ``source`` into the next bank
+row (``state.next_row()``), the route reads it from there and nothing is copied.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+def full_attnres_route(sources, query: torch.Tensor, norm_eps: float) -> torch.Tensor:
+    """One softmax mix over every source: ``sources`` is a [S, T, D] bf16 bank (or a list of [T, D] rows)."""
+    if not isinstance(sources, torch.Tensor):
+        sources = torch.stack(list(sources))
+    if sources.dim() != 3:
+        raise ValueError(f"sources must be [S, T, D], got {tuple(sources.shape)}")
+    return ops.attnres_route(sources, sources.shape[0], query, norm_eps)
+
+
+class FusedBlockAttnResContext:
+    """One forward's bank of completed sources, allocated once and reused (graph-safe)."""
+
+    def __init__(self, max_completed_blocks: int, reference: torch.Tensor, gradient_dtype=torch.float32, **_):
+        if not reference.is_cuda:
+            raise RuntimeError("fused AttnRes requires CUDA")
+        if reference.dtype != torch.bfloat16:
+            raise RuntimeError("fused AttnRes runs on bf16 activations")
+        self.token_shape = tuple(reference.shape[:-1])
+        self.dim = int(reference.shape[-1])
+        self.bt = 1
+        for n in self.token_shape:
+            self.bt *= int(n)
+        self.max_completed_blocks = int(max_completed_blocks)
+        self.gradient_dtype = gradient_dtype
+        self.blocks = torch.empty((self.max_completed_blocks, self.bt, self.dim), device=reference.device,
+                                  dtype=reference.dtype)
+        self.completed_count = 0
+        self.call_count = 0
+
+    def reset(self) -> None:
+        self.completed_count = 0
+        self.call_count = 0
+
+    def validate_owner(self, partial: torch.Tensor) -> None:
+        if tuple(partial.shape[:-1]) != self.token_shape or partial.shape[-1] != self.dim:
+            raise RuntimeError(
+                "Block AttnRes context shape changed within one model forward: "
+                f"expected {(*self.token_shape, self.dim)}, got {tuple(partial.shape)}"
+            )
+        if partial.device != self.blocks.device:
+            raise RuntimeError(f"Block AttnRes context device changed: {partial.device} vs {self.blocks.device}")
+        if partial.dtype != self.blocks.dtype:
+            raise RuntimeError(f"Block AttnRes context dtype changed: {partial.dtype} vs {self.blocks.dtype}")
+
+    def completed_view(self) -> torch.Tensor:
+        return self.blocks[: self.completed_count]
+
+    def next_row(self) -> torch.Tensor:
+        """The bank row the next appended source lands in: a producer can write its output here directly."""
+        if self.completed_count >= self.max_completed_blocks:
+            raise RuntimeError("Block AttnRes completed-block buffer overflow")
+        return self.blocks[self.completed_count]
+
+    def route(self, source: torch.Tensor, query: torch.Tensor, norm_eps: float, append_current: bool, *,
+              norm_weight: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              mix_out: torch.Tensor | None = None) -> torch.Tensor:
+        """Route over the completed rows + ``source`` (then append it when ``append_current``); with
+        ``norm_weight`` the following RMSNorm is fused and ``out`` is the normalised mix."""
+        src = source.reshape(self.bt, self.dim)
+        self.validate_owner(source)
+        completed = self.completed_count
+        if append_current and completed >= self.max_completed_blocks:
+            raise RuntimeError("Block AttnRes completed-block buffer overflow")
+        in_place = completed < self.max_completed_blocks and src.data_ptr() == self.blocks[completed].data_ptr()
+        if out is not None:
+            out = out.reshape(self.bt, self.dim)
+        if in_place:
+            result = ops.attnres_route(self.blocks, completed + 1, query, norm_eps, norm_weight=norm_weight,
+                                       norm_eps=norm_eps, out=out, mix_out=mix_out)
+        else:
+            result = ops.attnres_route(
+                self.blocks if completed else None, completed, query, norm_eps, source=src.contiguous(),
+                append_to=self.blocks[completed] if append_current else None, norm_weight=norm_weight,
+                norm_eps=norm_eps, out=out, mix_out=mix_out)
+        if append_current:
+            self.completed_count += 1
+        self.call_count += 1
+        return result.view(*self.token_shape, self.dim)
+
+
+def fused_full_attnres(state: FusedBlockAttnResContext, source: torch.Tensor, query: torch.Tensor,
+                       norm_eps: float, append_current: bool) -> torch.Tensor:
+    """Route ``source`` with every completed bank row (training_attnres_kernels.py:2826)."""
+    return state.route(source, query, float(norm_eps), bool(append_current))

@@ -8,6 +8,9 @@ namespace {
 thread_local char g_last_error[1024] = "";
 }
 
+// Library status word (one per device): bits set by kernels whose bounded waits expired.
+__device__ unsigned g_zb_device_status;
+
 namespace zb {
 
 int fail(int code, const char* fmt, ...) {
@@ -36,7 +39,29 @@ int sm_count() {
   return cached[dev];
 }
 
+unsigned* device_status_ptr() {
+  static unsigned* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_zb_device_status) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<unsigned*>(p);
+  }
+  return cached[dev];
+}
+
 }  // namespace zb
+
+// Reads (and with clear != 0 resets) the current device's status word. Synchronous; for diagnostics and tests.
+ZB_API int zb_device_status(unsigned* flags, int clear) {
+  ZB_REQUIRE(flags != nullptr, "zb_device_status: flags is null");
+  unsigned* p = zb::device_status_ptr();
+  if (p == nullptr) return zb::fail(zb::kCudaError, "zb_device_status: status word unavailable");
+  ZB_CUDA(cudaMemcpy(flags, p, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (clear) ZB_CUDA(cudaMemset(p, 0, sizeof(unsigned)));
+  return zb::kOk;
+}
 
 ZB_API const char* zb_last_error(void) { return g_last_error; }
 

@@ -33,6 +33,16 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Device address of the library's status word on the current device (bit flags that kernels set with atomicOr
+// when a bounded wait expires; zb_device_status() reads and clears it). nullptr if it cannot be resolved.
+unsigned* device_status_ptr();
+
+enum DeviceStatusBits : unsigned {
+  kStatusAttnresLoadTimeout = 1u << 0,
+  kStatusGemmTimeout = 1u << 1,
+  kStatusPrefillTimeout = 1u << 2,
+};
+
 }  // namespace zb
 
 #define ZB_REQUIRE(cond, ...)                                   \
@@ -95,6 +105,68 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float v[8]) {
     w[i] = *reinterpret_cast<uint32_t*>(&h);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ------------------------------------------------------------------------------ mbarrier / bulk-copy helpers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async proxy (TMA) and the rest of the cluster.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for phase `parity` of an mbarrier for at most ~`limit_ns`; on expiry ORs `code` into *status and
+// returns false (the caller carries on without hanging the GPU).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* status, unsigned code,
+                                                  uint64_t limit_ns = 1000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - start > limit_ns) {
+      if (status) atomicOr(status, code);
+      return false;
+    }
+  }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing `bytes` of transaction on mbarrier `bar`.
+// src and dst 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -95,3 +95,78 @@ def gdn_decode_step(
         out.data_ptr(), os_, B, H, dk, dv, float(scale), _stream(dev),
     )
     return out
+
+
+# --------------------------------------------------------------------------------------------- Full AttnRes
+
+
+def attnres_route(
+    bank: torch.Tensor | None,
+    num_sources: int,
+    query: torch.Tensor,
+    eps: float,
+    *,
+    source: torch.Tensor | None = None,
+    append_to: torch.Tensor | None = None,
+    norm_weight: torch.Tensor | None = None,
+    norm_eps: float = 1e-5,
+    out: torch.Tensor | None = None,
+    mix_out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Full AttnRes route over ``bank[:num_sources]`` (+ ``source`` as the last source) for every token.
+
+    bank [>= num_sources, T, D] bf16 (rows contiguous [T, D]); source [T, D] bf16; query [D] bf16. The mix follows
+    full_attnres_route (model/src/zonos3/reference/lm.py:384-389) with the fused Triton kernel's bf16 rounding
+    points. ``norm_weight`` fuses the RMSNorm after the route (out = RMSNorm(mix) and, if given, mix_out = mix);
+    ``append_to`` (a [T, D] bank row) receives ``source`` in the same pass.
+    """
+    _check_cuda("query", query, torch.bfloat16)
+    dev = query.device
+    (D,) = query.shape
+    T = None
+    bank_stride = 0
+    if num_sources:
+        _check_cuda("bank", bank, torch.bfloat16, dev)
+        _require(bank.dim() == 3 and bank.shape[0] >= num_sources and bank.shape[2] == D,
+                 f"bank must be [>= {num_sources}, T, {D}], got {tuple(bank.shape)}")
+        _require(bank.stride(2) == 1 and bank.stride(1) == D, "bank rows must be contiguous [T, D]")
+        T = bank.shape[1]
+        bank_stride = bank.stride(0)
+    if source is not None:
+        _check_cuda("source", source, torch.bfloat16, dev)
+        _require(source.dim() == 2 and source.shape[1] == D and source.is_contiguous(),
+                 f"source must be a contiguous [T, {D}] tensor")
+        _require(T is None or source.shape[0] == T, "source rows differ from the bank's")
+        T = source.shape[0]
+    _require(T is not None, "nothing to route: no bank sources and no source")
+    if append_to is not None:
+        _require(source is not None, "append_to needs a source")
+        _check_cuda("append_to", append_to, torch.bfloat16, dev)
+        _require(append_to.shape == (T, D) and append_to.is_contiguous(), "append_to must be a contiguous [T, D] row")
+    if norm_weight is not None:
+        _check_cuda("norm_weight", norm_weight, torch.bfloat16, dev)
+        _require(norm_weight.shape == (D,), "norm_weight must be [D]")
+    if out is None:
+        out = torch.empty((T, D), device=dev, dtype=torch.bfloat16)
+    for name, t in (("out", out), ("mix_out", mix_out)):
+        if t is not None:
+            _check_cuda(name, t, torch.bfloat16, dev)
+            _require(t.shape == (T, D) and t.is_contiguous(), f"{name} must be a contiguous [T, D] tensor")
+    _require(mix_out is None or norm_weight is not None, "mix_out is only produced with norm_weight")
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call(
+        "zb_attnres_route",
+        ptr(bank) if num_sources else None, bank_stride, num_sources, ptr(source), ptr(append_to),
+        query.data_ptr(), float(eps), ptr(norm_weight), float(norm_eps), out.data_ptr(), ptr(mix_out), T, D,
+        _stream(dev),
+    )
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Bits set by kernels whose bounded device-side waits expired on the current device (synchronous)."""
+    import ctypes
+
+    flags = ctypes.c_uint(0)
+    _lib.call("zb_device_status", ctypes.byref(flags), int(clear))
+    return flags.value
