@@ -67,6 +67,60 @@ int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, const uin
                      const uint16_t* query, float eps, const uint16_t* norm_weight, float norm_eps, uint16_t* out,
                      uint16_t* mix_out, int T, int D, cudaStream_t stream);
 
+/* ----------------------------------------------------------------------------------------------------- MoE */
+
+/* Fused router: logits = bf16(rmsnorm_eda(x) @ w_router^T), the top-k experts by (float(logit) - bias descending,
+ * expert index ascending), and their gate weights: weight_mode 0 = softmax over the k selected logits (the
+ * training-router weights), 1 = the selected entries of the softmax over all experts; renormalize != 0 divides by
+ * (sum + 1e-8). Replaces Router.forward / _select_balanced_topk (servers/sgl/src/zonos3_sgl/models/zonos3.py:746-828),
+ * the router lines of Zonos3LM._feed_forward (model/src/zonos3/reference/lm.py:610-617) and the renormalisation of
+ * FusedMoE.forward (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/layer.py:159-161).
+ *   x [T, D] bf16 (row stride x_stride); norm_weight [D] bf16; w_router [E, D] bf16; bias [E] fp32 or NULL
+ *   logits_out [T, E] bf16 or NULL; ids [T, k] int32; weights [T, k] fp32.  E <= 128, k <= min(E, 32),
+ *   D a multiple of 64. */
+int zb_moe_router(const uint16_t* x, int64_t x_stride, const uint16_t* norm_weight, float eps,
+                  const uint16_t* w_router, const float* bias, int T, int D, int E, int k, int weight_mode,
+                  int renormalize, uint16_t* logits_out, int32_t* ids, float* weights, cudaStream_t stream);
+
+/* The selection and weights of zb_moe_router from given logits [T, E] (fp32, or bf16 if logits_bf16 != 0). */
+int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T, int E, int k, int weight_mode,
+                  int renormalize, int32_t* ids, float* weights, cudaStream_t stream);
+
+/* Stable counting sort of the T*k (token, slot) pairs p = t*k + slot by expert, each expert's segment padded to a
+ * multiple of `block` rows: counts [E] (the per-expert token histogram), offsets [E+1] (padded segment starts,
+ * offsets[E] = rows in use), sorted_pairs [capacity] (pair of each row, -1 for padding and unused rows),
+ * position [T*k] (row of each pair). capacity >= roundup(T*k + E*(block-1), block). Replaces
+ * moe_align_block_size (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:28-86; sgl_kernel). */
+int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* counts,
+                   int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream);
+
+/* out[r] = x[sorted_pairs[r] / k] for r < rows (zero rows where sorted_pairs[r] < 0): the A operand of the
+ * grouped GEMM, the row gather fused_moe_kernel does through `offs_token // top_k`
+ * (servers/sgl/src/zonos3_sgl/kernel/triton/fused_moe.py:145). */
+int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sorted_pairs, int k, int64_t rows, int D,
+                  uint16_t* out, cudaStream_t stream);
+
+/* GEMM1 of the routed experts on tcgen05 tensor cores, SwiGLU fused in the epilogue:
+ * h[r, :] = bf16(silu(bf16(x_perm[r] . gate_up[e, 0:I]^T)) * bf16(x_perm[r] . gate_up[e, I:2I]^T)) for rows r of
+ * expert e's segment [offsets[e], offsets[e+1]). Replaces the first fused_moe_kernel call plus silu_and_mul of
+ * fused_experts_impl (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:218-234).
+ *   x_perm [capacity, D] bf16; gate_up [E, 2I, D] bf16 (gate rows first, zonos3.py:488-490); h [capacity, I] bf16
+ *   D a multiple of 64, I a multiple of 128, capacity a multiple of 128. */
+int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, int E, int D, int I,
+                       const int32_t* offsets, uint16_t* h, cudaStream_t stream);
+
+/* GEMM2 of the routed experts on tcgen05 tensor cores with the routing weight fused:
+ * y[p, :] = bf16((h[r] . down[e]^T) * weights[p]) for every row r with pair p = sorted_pairs[r] >= 0.
+ * Replaces the second fused_moe_kernel call (MUL_ROUTED_WEIGHT) of fused_experts_impl (fused_moe_impl.py:236-259).
+ *   h [capacity, I] bf16; down [E, D, I] bf16; weights [T*k] fp32; y [T*k, D] bf16.  I % 64 == 0, D % 256 == 0. */
+int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                     const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
+                     cudaStream_t stream);
+
+/* out[t, :] = bf16(sum over slots s of float(y[t*k + s, :])): the un-permute combine (the add / moe_sum_reduce of
+ * fused_experts_impl, fused_moe_impl.py:267-288). out has row stride out_stride. */
+int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_t out_stride, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

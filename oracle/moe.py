@@ -1,4 +1,5 @@
-"""MoE oracle (CPU): router, top-k selection, token permutation and the routed SwiGLU experts.
+"""MoE oracle (CPU; the expert functions also run unchanged on CUDA tensors as a plain fp32 PyTorch reference
+for sizes the CPU cannot finish quickly, with TF32 off): router, top-k selection, token permutation and the routed SwiGLU experts.
 
 Restates ``Zonos3LM._feed_forward`` (model/src/zonos3/reference/lm.py:604-639), the serving router
 (servers/sgl/src/zonos3_sgl/models/zonos3.py:746-828) and FusedMoE's renormalisation
@@ -82,13 +83,13 @@ def experts_fp32(x, gate_up, down, ids, weights):
     accumulation over ranks keeps rank order."""
     T, k = ids.shape
     half = gate_up.shape[1] // 2
-    terms = torch.zeros(T, k, down.shape[1], dtype=torch.float32)
+    terms = torch.zeros(T, k, down.shape[1], dtype=torch.float32, device=x.device)
     for e in torch.unique(ids).tolist():
         tok, rank = torch.nonzero(ids == e, as_tuple=True)
         gu = F.linear(x[tok].float(), gate_up[e].float())
         h = F.silu(gu[:, :half]) * gu[:, half:]
         terms[tok, rank] = F.linear(h, down[e].float()) * weights[tok, rank].float()[:, None]
-    out = torch.zeros(T, down.shape[1], dtype=x.dtype)
+    out = torch.zeros(T, down.shape[1], dtype=x.dtype, device=x.device)
     for rank in range(k):
         out += terms[:, rank].to(x.dtype)
     return out
@@ -100,7 +101,7 @@ def experts_bf16(x, gate_up, down, ids, weights):
     summed in float32 and rounded once. GEMM accumulation is float32."""
     T, k = ids.shape
     half = gate_up.shape[1] // 2
-    terms = torch.zeros(T, k, down.shape[1], dtype=torch.bfloat16)
+    terms = torch.zeros(T, k, down.shape[1], dtype=torch.bfloat16, device=x.device)
     for e in torch.unique(ids).tolist():
         tok, rank = torch.nonzero(ids == e, as_tuple=True)
         gu = F.linear(x[tok].float(), gate_up[e].float()).bfloat16().float()

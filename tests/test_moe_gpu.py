@@ -1,0 +1,177 @@
+"""GPU parity of the MoE path against the CPU oracle (lm.py:604-639; zonos3.py:746-828; fused_moe_impl.py).
+
+Bars (north_star): router top-k indices and the token permutation bit-exact; bf16 activations within 2e-2
+relative error. Selection parity is checked on identical logits (the kernel's top-k fed the oracle's logits);
+the router GEMM's logits themselves are checked separately (fp32 accumulation order differs from the CPU)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import moe as omoe
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def router_inputs(T, D, E, seed, bias_scale=0.0):
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, D, generator=gen).bfloat16()
+    norm_w = (1 + 0.1 * torch.randn(D, generator=gen)).bfloat16()
+    w_r = (0.02 * torch.randn(E, D, generator=gen)).bfloat16()
+    bias = bias_scale * torch.randn(E, generator=gen)
+    return x, norm_w, w_r, bias
+
+
+@pytest.mark.parametrize("T,D,E,k", [(1, 2048, 64, 8), (300, 2048, 64, 8), (77, 256, 8, 2), (64, 512, 128, 6),
+                                     (33, 1024, 16, 2)])
+def test_router_logits_and_selection(zb, T, D, E, k):
+    x, norm_w, w_r, bias = router_inputs(T, D, E, seed=T + E, bias_scale=0.05)
+    dev = torch.device("cuda")
+    logits = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+    ids, w = zb.ops.moe_router(x.cuda(), norm_w.cuda(), 1e-5, w_r.cuda(), bias.cuda(), k, logits=logits)
+    torch.cuda.synchronize()
+    ref_logits = omoe.router_logits(x, norm_w, w_r, 1e-5)
+    same = (logits.cpu().view(torch.int16) == ref_logits.view(torch.int16)).float().mean().item()
+    assert same > 0.995 and rel_err(logits.float(), ref_logits.float()) < 1e-2
+    # selection parity on the kernel's own logits: bit-exact ids, weights to fp32 rounding
+    ref_ids, ref_w = omoe.route(logits.cpu(), bias, k)
+    assert torch.equal(ids.cpu(), ref_ids)
+    torch.testing.assert_close(w.cpu(), ref_w, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("mode,renorm", [("selected_softmax", False), ("full_softmax", True), ("full_softmax", False)])
+def test_selection_is_bit_exact_with_ties(zb, mode, renorm):
+    """bf16 logits on a coarse grid tie constantly; the kernel must follow the documented order exactly."""
+    gen = torch.Generator().manual_seed(3)
+    T, E, k = 512, 64, 8
+    logits = (torch.randint(-6, 7, (T, E), generator=gen).float() / 4).bfloat16()
+    bias = torch.zeros(E)
+    bias[::7] = 0.25
+    ids, w = zb.ops.moe_select(logits.cuda(), bias.cuda(), k, weights=mode, renormalize=renorm)
+    torch.cuda.synchronize()
+    ref_ids, ref_w = omoe.route(logits, bias, k, weights=mode, renormalize=renorm)
+    assert torch.equal(ids.cpu(), ref_ids)
+    torch.testing.assert_close(w.cpu(), ref_w, rtol=1e-5, atol=1e-6)
+    # the fp32-logit path too
+    ids32, _ = zb.ops.moe_select(logits.float().cuda(), bias.cuda(), k, weights=mode, renormalize=renorm)
+    assert torch.equal(ids32.cpu(), ref_ids)
+
+
+def check_permutation(zb, ids_cpu, E):
+    perm = zb.ops.moe_permute(ids_cpu.cuda(), E)
+    torch.cuda.synchronize()
+    ref = omoe.permutation(ids_cpu.numpy(), E, block=zb.ops.GEMM_BLOCK)
+    assert np.array_equal(perm["counts"].cpu().numpy(), ref["counts"])
+    assert np.array_equal(perm["offsets"].cpu().numpy(), ref["offsets"])
+    cap = perm["sorted_pairs"].shape[0]
+    expect_sorted = np.full(cap, -1)
+    expect_sorted[: ref["sorted_pairs"].size] = ref["sorted_pairs"]
+    assert np.array_equal(perm["sorted_pairs"].cpu().numpy(), expect_sorted)
+    assert np.array_equal(perm["position"].cpu().numpy(), ref["position"])
+
+
+@pytest.mark.parametrize("T,E,k,kind", [(4096, 64, 8, "random"), (1, 64, 8, "random"), (257, 8, 2, "random"),
+                                        (500, 64, 4, "one_expert"), (100, 128, 8, "skewed"), (3000, 16, 1, "random")])
+def test_permutation_is_bit_exact(zb, T, E, k, kind):
+    gen = torch.Generator().manual_seed(T * 7 + E)
+    if kind == "random":
+        ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)])
+    elif kind == "one_expert":  # every token routes to expert 5 plus k-1 others
+        others = torch.tensor([e for e in range(E) if e != 5])
+        ids = torch.stack([torch.cat([torch.tensor([5]), others[torch.randperm(E - 1, generator=gen)[: k - 1]]])
+                           for _ in range(T)])
+    else:  # most pairs on a few experts, many experts empty
+        ids = torch.stack([torch.randperm(12, generator=gen)[:k] * 3 for _ in range(T)])
+    check_permutation(zb, ids.int(), E)
+
+
+def test_gather_rows(zb):
+    T, E, k, D = 37, 8, 2, 512
+    gen = torch.Generator().manual_seed(11)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)]).int()
+    x = torch.randn(T, D, generator=gen).bfloat16()
+    perm = zb.ops.moe_permute(ids.cuda(), E)
+    out = torch.full((perm["sorted_pairs"].shape[0], D), 7.0, device="cuda", dtype=torch.bfloat16)
+    zb.ops.moe_gather(x.cuda(), perm["sorted_pairs"], k, out)
+    torch.cuda.synchronize()
+    sp = perm["sorted_pairs"].cpu()
+    expect = torch.zeros(out.shape, dtype=torch.bfloat16)
+    live = sp >= 0
+    expect[live] = x[sp[live].long() // k]
+    assert torch.equal(out.cpu(), expect)
+
+
+def expert_weights(E, D, I, seed, scale=0.02):
+    gen = torch.Generator().manual_seed(seed)
+    gate_up = (scale * torch.randn(E, 2 * I, D, generator=gen)).bfloat16()
+    down = (scale * torch.randn(E, D, I, generator=gen)).bfloat16()
+    return gate_up, down
+
+
+@pytest.mark.parametrize("T,D,E,k,I", [(64, 256, 8, 2, 512), (200, 1024, 16, 4, 256), (1, 2048, 64, 8, 768),
+                                       (513, 2048, 64, 8, 768)])
+def test_grouped_gemms_match_oracle(zb, T, D, E, k, I):
+    gen = torch.Generator().manual_seed(T + D)
+    x = torch.randn(T, D, generator=gen).bfloat16()
+    gate_up, down = expert_weights(E, D, I, seed=T)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)]).int()
+    w = torch.softmax(torch.randn(T, k, generator=gen), -1)
+    dev = torch.device("cuda")
+    ws = zb.ops.MoEWorkspace(T, k, E, D, I, dev)
+    d_gu, d_down = gate_up.to(dev), down.to(dev)
+    out = zb.ops.moe_experts(x.to(dev), d_gu, d_down, ids.to(dev), w.to(dev), ws)
+    torch.cuda.synchronize()
+    assert zb.ops.device_status() == 0
+    # GEMM1 + SwiGLU rows against the oracle's rounding points
+    sp = ws.perm["sorted_pairs"].cpu()
+    rows = torch.nonzero(sp >= 0).squeeze(1)
+    pairs = sp[rows].long()
+    tok, slot = pairs // k, pairs % k
+    e_of = ids[tok, slot].long()
+    h_ref = torch.empty(len(rows), I, device=dev)
+    gu_all, x_d = gate_up.to(dev), x.to(dev)
+    for e in e_of.unique().tolist():
+        sel = (e_of == e).to(dev)
+        gu = (x_d[tok.to(dev)[sel]].float() @ gu_all[e].float().T).bfloat16().float()
+        h_ref[sel] = (torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]).bfloat16().float()
+    assert rel_err(ws.h[rows.to(dev)].float(), h_ref) < TOL
+    # the oracle's expert functions as a plain fp32 torch reference on the device (TF32 off)
+    ref = omoe.experts_bf16(x_d, d_gu, d_down, ids.to(dev), w.to(dev))
+    assert rel_err(out.float(), ref.float()) < TOL
+    ref32 = omoe.experts_fp32(x_d.float(), d_gu, d_down, ids.to(dev), w.to(dev))
+    assert rel_err(out.float(), ref32.float()) < TOL
+
+
+def test_full_moe_layer_cfg4(zb):
+    """cfg4: 4096 tokens x hidden 2048, router N(0, 0.02) -> softmax -> top-8 of 64 -> renormalised gates,
+    SwiGLU experts I=768 with bf16 weights N(0, 0.02); ids bit-exact on the kernel's logits, output within 2e-2."""
+    T, D, E, k, I = 4096, 2048, 64, 8, 768
+    x, norm_w, w_r, _ = router_inputs(T, D, E, seed=44)
+    gate_up, down = expert_weights(E, D, I, seed=45)
+    dev = torch.device("cuda")
+    logits = torch.empty(T, E, device=dev, dtype=torch.bfloat16)
+    ids, w = zb.ops.moe_router(x.to(dev), norm_w.to(dev), 1e-5, w_r.to(dev), None, k, weights="full_softmax",
+                               renormalize=True, logits=logits)
+    ws = zb.ops.MoEWorkspace(T, k, E, D, I, dev)
+    out = zb.ops.moe_experts(x.to(dev), gate_up.to(dev), down.to(dev), ids, w, ws)
+    torch.cuda.synchronize()
+    ref_ids, ref_w = omoe.route(logits.cpu(), torch.zeros(E), k, weights="full_softmax", renormalize=True)
+    assert torch.equal(ids.cpu(), ref_ids)
+    check = omoe.permutation(ids.cpu().numpy(), E, block=zb.ops.GEMM_BLOCK)
+    assert np.array_equal(ws.perm["position"].cpu().numpy(), check["position"])
+    ref = omoe.experts_bf16(x.to(dev), gate_up.to(dev), down.to(dev), ref_ids.to(dev), ref_w.to(dev))
+    assert rel_err(out.float(), ref.float()) < TOL
+    assert zb.ops.device_status() == 0

@@ -1,0 +1,420 @@
+// Grouped expert GEMMs of the MoE layer on 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   GEMM1 (gate/up + SwiGLU): H[r, n] = bf16( silu(bf16(A[r].Wg[e,n])) * bf16(A[r].Wu[e,n]) )
+//   GEMM2 (down + routing weight): Y[pair(r), n] = bf16( (H[r].W2[e,n]) * weight[pair(r)] )
+// A rows are the permuted (token, slot) pairs, grouped by expert and padded to 128-row tiles (zb_moe_permute);
+// expert e owns rows [offsets[e], offsets[e+1]). The k slots of a token are summed afterwards (zb_moe_combine).
+// Reference: fused_experts_impl (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:127-289)
+// with fused_moe_kernel (servers/sgl/src/zonos3_sgl/kernel/triton/fused_moe.py:54-192) and silu_and_mul; weight
+// layouts gate_up_proj [E, 2I, D] (gate rows first) and down_proj [E, D, I] (zonos3.py:450-637); the math of
+// lm.py:618-639. Rounding points follow the server: GEMM1 output bf16, SwiGLU bf16, GEMM2 * weight bf16.
+//
+// Kernel structure (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: per k-block, A tile [128 x 64] and B tile [256 x 64] (two 128-row boxes), both
+//               128B-swizzled, into a 4-stage shared-memory ring (48 KB per stage);
+//   warp 1      owns the TMEM allocation (512 columns = two 128x256 fp32 accumulators) and, on one lane, issues
+//               tcgen05.mma (M=128, N=256, K=16 per instruction) and the tcgen05.commit arrivals;
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp its 32-lane TMEM quarter), SwiGLU or the
+//               routing-weight scale, bf16 stores; the accumulator is double-buffered so the epilogue of one
+//               tile overlaps the MMAs of the next.
+// Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the CTAs running at one time share the
+// same weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the kernel sets a status bit,
+// stops issuing, drains its own copies and MMAs (again bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;      // 16 KB
+constexpr uint32_t B_BYTES = BN * BK * 2;      // 32 KB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int kTmemCols = 512;
+constexpr int kMaxExperts = 128;
+
+enum Mode : int { kSwiGLU = 0, kDown = 1 };
+
+struct GemmParams {
+  const int32_t* offsets;  // [E + 1] padded row offsets (multiples of BM)
+  int E;
+  int K;                   // reduction length (multiple of BK)
+  int n_tiles;             // output column tiles per expert
+  int64_t b_rows_per_expert;  // rows of B per expert (2I for GEMM1, D for GEMM2)
+  int b_second_offset;     // row offset of the second 128-row B box (I for GEMM1, 128 for GEMM2)
+  int b_tile_step;         // B row advance per n-tile (128 for GEMM1, 256 for GEMM2)
+  __nv_bfloat16* out;      // GEMM1: H [rows, I]; GEMM2: Y [pairs, D]
+  int64_t out_stride;
+  const int32_t* sorted_pairs;  // GEMM2
+  const float* weights;         // GEMM2: [pairs]
+  unsigned* status;
+};
+
+// ------------------------------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);          // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused for swizzled K-major) = 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+struct Shared {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int item_start[kMaxExperts + 1];
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    GemmParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // stage buffers first, 1024-byte aligned (the 128B swizzle pattern repeats every 1024 bytes)
+  const uint32_t raw_addr = zb::smem_addr(smem_raw);
+  const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
+  unsigned char* stages = smem_raw + pad;
+  Shared* sh = reinterpret_cast<Shared*>(stages + STAGES * STAGE_BYTES);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  volatile int* abort_flag = &sh->abort;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      zb::mbar_init(zb::smem_addr(&sh->full[s]), 1);
+      zb::mbar_init(zb::smem_addr(&sh->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      zb::mbar_init(zb::smem_addr(&sh->tmem_full[a]), 1);
+      zb::mbar_init(zb::smem_addr(&sh->tmem_empty[a]), 4);
+    }
+    zb::mbar_init(zb::smem_addr(&sh->drain), 1);
+    sh->abort = 0;
+    zb::fence_mbar_init();
+  }
+  for (int e = tid; e <= p.E; e += kThreads) sh->item_start[e] = (p.offsets[e] / BM) * p.n_tiles;
+  if (warp == 1) tmem_alloc(zb::smem_addr(&sh->tmem_base), kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = sh->tmem_base;
+  const int total_items = sh->item_start[p.E];
+  const int E = p.E;
+  const int k_blocks = p.K / BK;
+
+  // item -> (expert, n-tile, first row of the m-tile)
+  auto decode = [&](int item, int& e, int& n, int& row0) {
+    int lo = 0, hi = E;  // largest e with item_start[e] <= item
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) / 2;
+      if (sh->item_start[mid] <= item) lo = mid; else hi = mid;
+    }
+    e = lo;
+    while (e + 1 < E && sh->item_start[e + 1] <= item) ++e;  // skip experts without tiles
+    const int m_tiles = (sh->item_start[e + 1] - sh->item_start[e]) / p.n_tiles;
+    const int local = item - sh->item_start[e];
+    n = local / m_tiles;
+    row0 = (sh->item_start[e] / p.n_tiles + local % m_tiles) * BM;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t q = 0;  // k-blocks issued so far
+      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x) {
+        int e, n, row0;
+        decode(item, e, n, row0);
+        const int b_row0 = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step;
+        for (int kb = 0; kb < k_blocks; ++kb, ++q) {
+          const int s = q % STAGES;
+          const uint32_t parity = ((q / STAGES) & 1) ^ 1;
+          if (!zb::mbar_wait_bounded(zb::smem_addr(&sh->empty[s]), parity, p.status, zb::kStatusGemmTimeout)) {
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t full = zb::smem_addr(&sh->full[s]);
+          const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
+          const uint32_t b_dst = a_dst + A_BYTES;
+          zb::mbar_arrive_expect_tx(full, STAGE_BYTES);
+          tma_load_2d(a_dst, &tmap_a, kb * BK, row0, full);
+          tma_load_2d(b_dst, &tmap_b, kb * BK, b_row0, full);
+          tma_load_2d(b_dst + B_BYTES / 2, &tmap_b, kb * BK, b_row0 + p.b_second_offset, full);
+        }
+      }
+      // drain: wait (bounded) for the copies still in flight before the CTA may exit
+      for (uint32_t d = 0; d < STAGES && d < q; ++d) {
+        const uint32_t qq = q - 1 - d;
+        zb::mbar_wait_bounded(zb::smem_addr(&sh->full[qq % STAGES]), (qq / STAGES) & 1, nullptr, 0, 200000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t q = 0;
+      int it = 0;
+      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t use = it >> 1;
+        if (!zb::mbar_wait_bounded(zb::smem_addr(&sh->tmem_empty[acc]), (use & 1) ^ 1, p.status,
+                                   zb::kStatusGemmTimeout)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb, ++q) {
+          const int s = q % STAGES;
+          if (!zb::mbar_wait_bounded(zb::smem_addr(&sh->full[s]), (q / STAGES) & 1, p.status,
+                                     zb::kStatusGemmTimeout)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = zb::smem_addr(stages + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            tc_mma(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), kIdesc,
+                   (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(zb::smem_addr(&sh->empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(zb::smem_addr(&sh->tmem_full[acc]));
+      }
+      // every MMA issued by this thread has completed before TMEM is released
+      tc_commit(zb::smem_addr(&sh->drain));
+      zb::mbar_wait_bounded(zb::smem_addr(&sh->drain), 0, nullptr, 0, 200000000ull);
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter (warp % 4)
+    const int quarter = warp % 4;
+    const int row_in_tile = quarter * 32 + lane;
+    int it = 0;
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = it >> 1;
+      bool ok = !*abort_flag &&
+                zb::mbar_wait_bounded(zb::smem_addr(&sh->tmem_full[acc]), use & 1, p.status, zb::kStatusGemmTimeout);
+      // the tcgen05.ld below are warp-collective: every lane takes the same branch
+      if (!__all_sync(0xffffffffu, ok)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int e, n, row0;
+      decode(item, e, n, row0);
+      const int64_t row = row0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (MODE == kSwiGLU) {
+        __nv_bfloat16* dst = p.out + row * p.out_stride + (int64_t)n * 128;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          float gate[32], up[32];
+          tmem_ld32(t_row + c, gate);
+          tmem_ld32(t_row + 128 + c, up);
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              h[i] = silu(zb::bf16_round(gate[j + i])) * zb::bf16_round(up[j + i]);
+            *reinterpret_cast<uint4*>(dst + c + j) = zb::pack_bf16x8(h);
+          }
+        }
+      } else {
+        const int pair = p.sorted_pairs[row];
+        const float w = pair >= 0 ? p.weights[pair] : 0.f;
+        __nv_bfloat16* dst = p.out + (int64_t)(pair >= 0 ? pair : 0) * p.out_stride + (int64_t)n * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float y[32];
+          tmem_ld32(t_row + c, y);
+          if (pair >= 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float o[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = y[j + i] * w;
+              *reinterpret_cast<uint4*>(dst + c + j) = zb::pack_bf16x8(o);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) zb::mbar_arrive(zb::smem_addr(&sh->tmem_empty[acc]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] tensor map with a [128 rows x 64 cols] box and 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return zb::fail(zb::kCudaError, "moe_gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
+  cuuint32_t box[2] = {BK, 128};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return zb::fail(zb::kCudaError, "moe_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return zb::kOk;
+}
+
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + sizeof(Shared);
+
+template <int MODE>
+int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int64_t capacity,
+           cudaStream_t stream) {
+  auto kernel = moe_gemm_kernel<MODE>;
+  static int configured[64] = {0};
+  int dev = 0;
+  ZB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  const int64_t upper_items = capacity / BM * p.n_tiles;
+  const int grid = (int)std::min<int64_t>(upper_items, zb::sm_count());
+  if (grid <= 0) return zb::kOk;
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, b, p);
+  return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
+}
+
+int check_common(const void* a, const int32_t* offsets, int E, int64_t capacity) {
+  ZB_REQUIRE(a && offsets, "moe_gemm: null pointer");
+  ZB_REQUIRE(E > 0 && E <= kMaxExperts, "moe_gemm: E=%d (1..%d)", E, kMaxExperts);
+  ZB_REQUIRE(capacity > 0 && capacity % BM == 0, "moe_gemm: capacity %lld must be a positive multiple of %d",
+             (long long)capacity, BM);
+  ZB_REQUIRE_ALIGNED(a, 16, "A");
+  return zb::kOk;
+}
+
+}  // namespace
+
+ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, int E, int D, int I,
+                              const int32_t* offsets, uint16_t* h, cudaStream_t stream) {
+  if (int rc = check_common(x_perm, offsets, E, capacity)) return rc;
+  ZB_REQUIRE(gate_up && h, "moe_gemm_swiglu: null pointer");
+  if (D % BK != 0 || I % 128 != 0)
+    return zb::fail(zb::kUnsupported, "moe_gemm_swiglu: D=%d must be a multiple of 64 and I=%d of 128", D, I);
+  ZB_REQUIRE_ALIGNED(gate_up, 16, "gate_up");
+  ZB_REQUIRE_ALIGNED(h, 16, "h");
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, x_perm, capacity, D, D)) return rc;
+  if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
+  GemmParams p{offsets, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, nullptr,
+               nullptr, zb::device_status_ptr()};
+  return launch<kSwiGLU>(ma, mb, p, capacity, stream);
+}
+
+ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                            const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
+                            cudaStream_t stream) {
+  if (int rc = check_common(h, offsets, E, capacity)) return rc;
+  ZB_REQUIRE(down && sorted_pairs && weights && y, "moe_gemm_down: null pointer");
+  if (I % BK != 0 || D % BN != 0)
+    return zb::fail(zb::kUnsupported, "moe_gemm_down: I=%d must be a multiple of 64 and D=%d of 256", I, D);
+  ZB_REQUIRE_ALIGNED(down, 16, "down");
+  ZB_REQUIRE_ALIGNED(y, 16, "y");
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, h, capacity, I, I)) return rc;
+  if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
+  GemmParams p{offsets, E, I, D / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D, sorted_pairs,
+               weights, zb::device_status_ptr()};
+  return launch<kDown>(ma, mb, p, capacity, stream);
+}

@@ -170,3 +170,193 @@ def device_status(clear: bool = True) -> int:
     flags = ctypes.c_uint(0)
     _lib.call("zb_device_status", ctypes.byref(flags), int(clear))
     return flags.value
+
+
+# --------------------------------------------------------------------------------------------- MoE
+
+WEIGHT_MODES = {"selected_softmax": 0, "full_softmax": 1}
+GEMM_BLOCK = 128  # rows of one grouped-GEMM tile; every expert segment is padded to a multiple of it
+
+
+def moe_capacity(tokens: int, top_k: int, num_experts: int, block: int = GEMM_BLOCK) -> int:
+    """Rows of the permuted, tile-padded pair layout: enough for any routing of ``tokens * top_k`` pairs."""
+    pairs = tokens * top_k
+    return -(-(pairs + num_experts * (block - 1)) // block) * block
+
+
+def moe_router(x, norm_weight, eps, w_router, bias, top_k, *, weights="selected_softmax", renormalize=False,
+               ids=None, topk_weights=None, logits=None):
+    """Fused router: logits = router_linear(rmsnorm_eda(x)) (bf16), top-k by (logit - bias, index), gate weights.
+
+    x [T, D] bf16; norm_weight [D] bf16; w_router [E, D] bf16; bias [E] fp32. Returns (ids [T, k] int32,
+    weights [T, k] fp32); ``logits`` ([T, E] bf16) optionally receives the router logits.
+    Follows servers/sgl/src/zonos3_sgl/models/zonos3.py:787-828 and model/src/zonos3/reference/lm.py:610-617.
+    """
+    _check_cuda("x", x, torch.bfloat16)
+    dev = x.device
+    T, D = x.shape
+    _require(x.stride(1) == 1, "x rows must be contiguous")
+    _check_cuda("w_router", w_router, torch.bfloat16, dev)
+    E = w_router.shape[0]
+    _require(w_router.shape == (E, D) and w_router.is_contiguous(), "w_router must be a contiguous [E, D] tensor")
+    _check_cuda("norm_weight", norm_weight, torch.bfloat16, dev)
+    _require(norm_weight.shape == (D,), "norm_weight must be [D]")
+    if bias is not None:
+        _check_cuda("bias", bias, torch.float32, dev)
+        _require(bias.shape == (E,), "bias must be [E]")
+    if ids is None:
+        ids = torch.empty((T, top_k), device=dev, dtype=torch.int32)
+    if topk_weights is None:
+        topk_weights = torch.empty((T, top_k), device=dev, dtype=torch.float32)
+    _check_cuda("ids", ids, torch.int32, dev)
+    _check_cuda("topk_weights", topk_weights, torch.float32, dev)
+    _require(ids.shape == (T, top_k) and ids.is_contiguous(), "ids must be a contiguous [T, k] int32 tensor")
+    _require(topk_weights.shape == (T, top_k) and topk_weights.is_contiguous(), "topk_weights must be [T, k]")
+    if logits is not None:
+        _check_cuda("logits", logits, torch.bfloat16, dev)
+        _require(logits.shape == (T, E) and logits.is_contiguous(), "logits must be a contiguous [T, E] tensor")
+    _lib.call("zb_moe_router", x.data_ptr(), x.stride(0) if T > 1 else D, norm_weight.data_ptr(), float(eps),
+              w_router.data_ptr(), None if bias is None else bias.data_ptr(), T, D, E, top_k,
+              WEIGHT_MODES[weights], int(bool(renormalize)), None if logits is None else logits.data_ptr(),
+              ids.data_ptr(), topk_weights.data_ptr(), _stream(dev))
+    return ids, topk_weights
+
+
+def moe_select(logits, bias, top_k, *, weights="selected_softmax", renormalize=False, ids=None, topk_weights=None):
+    """Top-k selection and gate weights from given router logits [T, E] (fp32 or bf16); same contract as
+    ``moe_router`` (used to check selection parity on identical logits)."""
+    _require(logits.is_cuda and logits.dtype in (torch.float32, torch.bfloat16) and logits.is_contiguous(),
+             "logits must be a contiguous CUDA fp32/bf16 [T, E] tensor")
+    dev = logits.device
+    T, E = logits.shape
+    if bias is not None:
+        _check_cuda("bias", bias, torch.float32, dev)
+        _require(bias.shape == (E,), "bias must be [E]")
+    if ids is None:
+        ids = torch.empty((T, top_k), device=dev, dtype=torch.int32)
+    if topk_weights is None:
+        topk_weights = torch.empty((T, top_k), device=dev, dtype=torch.float32)
+    _lib.call("zb_moe_select", logits.data_ptr(), int(logits.dtype == torch.bfloat16),
+              None if bias is None else bias.data_ptr(), T, E, top_k, WEIGHT_MODES[weights], int(bool(renormalize)),
+              ids.data_ptr(), topk_weights.data_ptr(), _stream(dev))
+    return ids, topk_weights
+
+
+def moe_permute(ids, num_experts, *, block=GEMM_BLOCK, capacity=None, out=None):
+    """Stable sort of the (token, slot) pairs by expert, segments padded to ``block`` rows.
+
+    Returns dict(counts [E], offsets [E+1], sorted_pairs [capacity] (-1 = padding), position [T*k]) as int32
+    device tensors; ``out`` may supply them (graph-safe reuse)."""
+    _check_cuda("ids", ids, torch.int32)
+    dev = ids.device
+    T, k = ids.shape
+    _require(ids.is_contiguous(), "ids must be contiguous")
+    if capacity is None:
+        capacity = moe_capacity(T, k, num_experts, block)
+    if out is None:
+        out = {
+            "counts": torch.empty(num_experts, device=dev, dtype=torch.int32),
+            "offsets": torch.empty(num_experts + 1, device=dev, dtype=torch.int32),
+            "sorted_pairs": torch.empty(capacity, device=dev, dtype=torch.int32),
+            "position": torch.empty(T * k, device=dev, dtype=torch.int32),
+        }
+    _lib.call("zb_moe_permute", ids.data_ptr(), T, k, num_experts, block, capacity, out["counts"].data_ptr(),
+              out["offsets"].data_ptr(), out["sorted_pairs"].data_ptr(), out["position"].data_ptr(), _stream(dev))
+    return out
+
+
+def moe_gather(x, sorted_pairs, top_k, out):
+    """out[r] = x[sorted_pairs[r] // k] (zero rows for padding)."""
+    dev = x.device
+    _check_cuda("x", x, torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    _require(out.shape == (sorted_pairs.shape[0], x.shape[1]) and out.is_contiguous(), "out must be [rows, D]")
+    _lib.call("zb_moe_gather", x.data_ptr(), x.stride(0), sorted_pairs.data_ptr(), top_k, out.shape[0], x.shape[1],
+              out.data_ptr(), _stream(dev))
+    return out
+
+
+def moe_gemm_swiglu(x_perm, gate_up, offsets, out):
+    """H = SwiGLU(x_perm @ gate_up[e].T) per expert segment (tcgen05 grouped GEMM, gate rows first)."""
+    dev = x_perm.device
+    E, two_i, D = gate_up.shape
+    for name, t in (("x_perm", x_perm), ("gate_up", gate_up), ("out", out)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _require(x_perm.shape[1] == D and out.shape == (x_perm.shape[0], two_i // 2), "shape mismatch")
+    _lib.call("zb_moe_gemm_swiglu", x_perm.data_ptr(), x_perm.shape[0], gate_up.data_ptr(), E, D, two_i // 2,
+              offsets.data_ptr(), out.data_ptr(), _stream(dev))
+    return out
+
+
+def moe_gemm_down(h, down, offsets, sorted_pairs, topk_weights, out):
+    """Y[pair] = (H[r] @ down[e].T) * weight[pair] for every non-padding row r (tcgen05 grouped GEMM)."""
+    dev = h.device
+    E, D, I = down.shape
+    for name, t in (("h", h), ("down", down), ("out", out)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _check_cuda("topk_weights", topk_weights, torch.float32, dev)
+    _require(h.shape[1] == I and out.shape == (topk_weights.numel(), D), "shape mismatch")
+    _lib.call("zb_moe_gemm_down", h.data_ptr(), h.shape[0], down.data_ptr(), E, D, I, offsets.data_ptr(),
+              sorted_pairs.data_ptr(), topk_weights.data_ptr(), out.data_ptr(), _stream(dev))
+    return out
+
+
+def moe_combine(y, top_k, out):
+    """out[t] = sum over slots of y[t * k + slot] (fp32 sum, bf16 result)."""
+    dev = y.device
+    _check_cuda("y", y, torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    T, D = out.shape
+    _require(y.shape == (T * top_k, D) and y.is_contiguous() and out.stride(1) == 1, "shape mismatch")
+    _lib.call("zb_moe_combine", y.data_ptr(), T, top_k, D, out.data_ptr(), out.stride(0) if T > 1 else D,
+              _stream(dev))
+    return out
+
+
+class MoEWorkspace:
+    """Device buffers of one MoE call shape (tokens, top-k, experts, hidden, intermediate), allocated once and
+    reused, so repeated calls and CUDA-graph captures allocate nothing."""
+
+    def __init__(self, tokens, top_k, num_experts, hidden, intermediate, device):
+        self.key = (tokens, top_k, num_experts, hidden, intermediate, torch.device(device))
+        cap = moe_capacity(tokens, top_k, num_experts)
+        self.capacity = cap
+        i32 = dict(device=device, dtype=torch.int32)
+        bf = dict(device=device, dtype=torch.bfloat16)
+        self.ids = torch.empty(tokens, top_k, **i32)
+        self.weights = torch.empty(tokens, top_k, device=device, dtype=torch.float32)
+        self.perm = {
+            "counts": torch.empty(num_experts, **i32),
+            "offsets": torch.empty(num_experts + 1, **i32),
+            "sorted_pairs": torch.empty(cap, **i32),
+            "position": torch.empty(tokens * top_k, **i32),
+        }
+        self.x_perm = torch.empty(cap, hidden, **bf)
+        self.h = torch.empty(cap, intermediate, **bf)
+        self.y = torch.empty(tokens * top_k, hidden, **bf)
+
+    @classmethod
+    def for_shape(cls, cache: dict, tokens, top_k, num_experts, hidden, intermediate, device):
+        key = (tokens, top_k, num_experts, hidden, intermediate, torch.device(device))
+        ws = cache.get(key)
+        if ws is None:
+            ws = cache[key] = cls(tokens, top_k, num_experts, hidden, intermediate, device)
+        return ws
+
+
+def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, out=None):
+    """Routed SwiGLU experts for precomputed (ids, weights): permute -> gather -> GEMM1+SwiGLU -> GEMM2*w ->
+    combine. x [T, D] bf16; gate_up [E, 2I, D]; down [E, D, I]. Returns out [T, D] bf16."""
+    T, D = x.shape
+    E = gate_up.shape[0]
+    k = ids.shape[1]
+    ws = workspace
+    perm = moe_permute(ids, E, capacity=ws.capacity, out=ws.perm)
+    moe_gather(x, perm["sorted_pairs"], k, ws.x_perm)
+    moe_gemm_swiglu(ws.x_perm, gate_up, perm["offsets"], ws.h)
+    moe_gemm_down(ws.h, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.y)
+    if out is None:
+        out = torch.empty((T, D), device=x.device, dtype=torch.bfloat16)
+    return moe_combine(ws.y, k, out)
