@@ -121,6 +121,18 @@ int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, 
  * fused_experts_impl, fused_moe_impl.py:267-288). out has row stride out_stride. */
 int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_t out_stride, cudaStream_t stream);
 
+/* zb_moe_gemm_down followed by zb_moe_combine, without the caller's [T*k, D] intermediate buffer. No counterpart in
+ * the reference: it is for callers that cannot call cudaMalloc (a serving runtime that reserves its device memory
+ * at start-up and forbids allocation afterwards, or a C / Go / Java binding with no device allocator of its own).
+ * The intermediate rows live in a static device array of 4,194,304 bf16 elements (8 MiB) that every GPU loading the
+ * library holds until exit, so T*k*D must be at most 4,194,304 (status 3 otherwise, nothing queued). Calls share
+ * the array: each clears the rows it uses first, and calls that overlap on the GPU race. The first call on a
+ * device looks up the array's address with that device current; make it before any stream capture. Allocates
+ * nothing. Arguments as zb_moe_gemm_down (h .. weights) and zb_moe_combine (T, k, out, out_stride). */
+int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                                const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, int T, int k,
+                                uint16_t* out, int64_t out_stride, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

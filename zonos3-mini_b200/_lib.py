@@ -44,6 +44,8 @@ SIGNATURES: dict[str, list] = {
     "zb_moe_gemm_down": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p],
     # y, T, k, D, out, out_stride, stream
     "zb_moe_combine": [_p, _i32, _i32, _i32, _p, _i64, _p],
+    # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, T, k, out, out_stride, stream
+    "zb_moe_down_combine_noalloc": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _i32, _i32, _p, _i64, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None}
 
