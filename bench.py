@@ -272,6 +272,163 @@ def run_ours(args, dist, rank, world, local):
     return line
 
 
+# --------------------------------------------------------------------------------------------- operator timings
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+class L2Flush:
+    """Reads a 256 MB buffer (twice the 126 MB L2) so the next kernel starts from HBM. A read leaves clean lines
+    behind, so the timed kernel pays no write-back of the flush (a write-based flush would)."""
+
+    def __init__(self, dev):
+        self.buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+        self.out = torch.empty(1, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        torch.sum(self.buf, dim=0, keepdim=True, out=self.out)
+
+
+def flush_l2(flush) -> None:
+    flush()
+
+
+def moe_cfg4_inputs(dev, seed=4):
+    """cfg4: 4096 tokens x hidden 2048 bf16 N(0,1); router N(0,0.02) [64, 2048]; 64 SwiGLU experts, I=768,
+    bf16 weights N(0,0.02)."""
+    T, D, E, I = 4096, 2048, 64, 768
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, D, generator=gen).bfloat16()
+    norm_w = torch.ones(D).bfloat16()
+    w_r = (0.02 * torch.randn(E, D, generator=gen)).bfloat16()
+    gate_up = (0.02 * torch.randn(E, 2 * I, D, generator=gen)).bfloat16()
+    down = (0.02 * torch.randn(E, D, I, generator=gen)).bfloat16()
+    return [t.to(dev) for t in (x, norm_w, w_r, gate_up, down)]
+
+
+def graph_ms(fn, stream, reps=5, warmup=2) -> float:
+    """Milliseconds per call of fn() captured in a CUDA graph and replayed `reps` times between two events on
+    `stream` (no host work inside the timed region)."""
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        for _ in range(warmup):
+            graph.replay()
+        a, b = _events()
+        a.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / reps
+
+
+def flushed_ms(fn, flush, stream, reps=5) -> float:
+    """Device time of fn() starting from a cold L2: graph[flush, fn] minus graph[flush]."""
+    return graph_ms(lambda: (flush_l2(flush), fn()), stream, reps) - graph_ms(lambda: flush_l2(flush), stream, reps)
+
+
+def bench_moe_cfg4(ops, dev, stream, steps=10, warmup=3):
+    """The MoE layer of cfg4 (router -> permutation -> gather -> GEMM1+SwiGLU -> GEMM2*w -> combine) as one CUDA
+    graph, plus each kernel's device time from a cold L2 (graph of [flush, kernel] minus graph of [flush])."""
+    x, norm_w, w_r, gate_up, down = moe_cfg4_inputs(dev)
+    T, D = x.shape
+    E, two_i, _ = gate_up.shape
+    I, k = two_i // 2, 8
+    ws = ops.MoEWorkspace(T, k, E, D, I, dev)
+    out = torch.empty(T, D, device=dev, dtype=torch.bfloat16)
+    flush = L2Flush(dev)
+
+    def router():
+        ops.moe_router(x, norm_w, 1e-5, w_r, None, k, weights="full_softmax", renormalize=True, ids=ws.ids,
+                       topk_weights=ws.weights)
+
+    def permute():
+        ops.moe_permute(ws.ids, E, capacity=ws.capacity, out=ws.perm)
+
+    def gather():
+        ops.moe_gather(x, ws.perm["sorted_pairs"], k, ws.x_perm)
+
+    def gemm1():
+        ops.moe_gemm_swiglu(ws.x_perm, gate_up, ws.perm["offsets"], ws.h)
+
+    def gemm2():
+        ops.moe_gemm_down(ws.h, down, ws.perm["offsets"], ws.perm["sorted_pairs"], ws.weights, ws.y)
+
+    def combine():
+        ops.moe_combine(ws.y, k, out)
+
+    parts = [("router", router), ("permute", permute), ("gather", gather), ("gemm_swiglu", gemm1),
+             ("gemm_down", gemm2), ("combine", combine)]
+
+    def layer():
+        for _, fn in parts:
+            fn()
+
+    layer_ms = graph_ms(layer, stream, reps=steps, warmup=warmup)
+    per = {name: flushed_ms(fn, flush, stream) for name, fn in parts}
+    status = ops.device_status()
+    pk = peaks()
+    pairs = T * k
+    f1, f2 = 2 * pairs * D * 2 * I, 2 * pairs * I * D
+    gemm_ms = per["gemm_swiglu"] + per["gemm_down"]
+    tflops = (f1 + f2) / (gemm_ms / 1e3) / 1e12
+    return {
+        "workload": "cfg4 MoE layer: 4096 tokens x 2048, top-8 of 64 experts, SwiGLU I=768 (router, permutation, "
+                    "gather, grouped GEMMs, combine)",
+        "ms_per_layer": layer_ms, "tokens_per_s": T / (layer_ms / 1e3),
+        "kernel_ms_cold_l2": per,
+        "roofline": {"kernel": "moe_gemm_kernel (SwiGLU + Down)", "bound": "tensor", "achieved": tflops,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"],
+                     "flops_per_layer": f1 + f2, "peak_source": pk["source"] + " burst"},
+        "gemm_swiglu_tflops": f1 / (per["gemm_swiglu"] / 1e3) / 1e12,
+        "gemm_down_tflops": f2 / (per["gemm_down"] / 1e3) / 1e12,
+        "device_status": status,
+    }
+
+
+def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps=3):
+    """cfg5's AttnRes schedule for one decode step: 2L+1 routes over a growing bank (S = 1 .. 2L+1 sources) of
+    `tokens` rows, each with the following RMSNorm fused. The L2 is flushed before every route (as the layers
+    between routes would); route time = graph[flush, route] x (2L+1) minus graph[flush] x (2L+1)."""
+    gen = torch.Generator().manual_seed(7)
+    n_src = 2 * layers + 1
+    bank = torch.randn(n_src, tokens, dim, generator=gen).bfloat16().to(dev)
+    queries = (0.02 * torch.randn(n_src, dim, generator=gen)).bfloat16().to(dev)
+    norm_w = torch.ones(dim, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(tokens, dim, device=dev, dtype=torch.bfloat16)
+    flush = L2Flush(dev)
+
+    def schedule(with_routes):
+        for r in range(n_src):
+            flush_l2(flush)
+            if with_routes:
+                ops.attnres_route(bank, r + 1, queries[r], 1e-5, norm_weight=norm_w, out=out)
+
+    total_ms = graph_ms(lambda: schedule(True), stream, reps) - graph_ms(lambda: schedule(False), stream, reps)
+    big_ms = flushed_ms(lambda: ops.attnres_route(bank, n_src, queries[-1], 1e-5, norm_weight=norm_w, out=out),
+                        flush, stream, reps=10)
+    total_bytes = sum(((r + 1) * tokens * dim + tokens * dim + 2 * dim) * 2 for r in range(n_src))
+    pk = peaks()
+    gbs = total_bytes / (total_ms / 1e3) / 1e9
+    big_bytes = (n_src * tokens * dim + tokens * dim + 2 * dim) * 2
+    return {
+        "workload": f"cfg5 AttnRes decode schedule: {n_src} routes over a growing bank, {tokens} tokens x {dim}, "
+                    "fused RMSNorm, L2 flushed before each route",
+        "ms_per_step": total_ms, "bytes_per_step": total_bytes,
+        "roofline": {"kernel": "attnres_route (logits + mix kernels)", "bound": "hbm", "achieved": gbs,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"]},
+        "largest_route": {"sources": n_src, "us": big_ms * 1e3, "gbs": big_bytes / (big_ms / 1e3) / 1e9,
+                          "frac": big_bytes / (big_ms / 1e3) / 1e9 / pk["hbm_gbs"]},
+    }
+
+
 def profiled_traffic(summary: str):
     """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in the
     committed summary under profiles/, or None."""
@@ -301,10 +458,36 @@ def cpu_reference(updates: int, streams=STREAMS):
     return streams * updates / dt, torch.get_num_threads(), dt
 
 
-def profile_launches(n: int) -> None:
-    """n eager cfg2 decode updates cycling the layer states (the bench's own launches, without graphs or timing)."""
+def profile_launches(n: int, workload: str = "gdn_decode") -> None:
+    """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
+    updates cycling the layer states, cfg4 MoE layers, or the largest cfg5 AttnRes route."""
     ops = __import__("__graft_entry__").load_package().ops
     dev = torch.device("cuda", 0)
+    if workload == "moe":
+        x, norm_w, w_r, gate_up, down = moe_cfg4_inputs(dev)
+        T, D = x.shape
+        E, two_i, _ = gate_up.shape
+        ws = ops.MoEWorkspace(T, 8, E, D, two_i // 2, dev)
+        out = torch.empty(T, D, device=dev, dtype=torch.bfloat16)
+        for _ in range(n):
+            ids, w = ops.moe_router(x, norm_w, 1e-5, w_r, None, 8, weights="full_softmax", renormalize=True,
+                                    ids=ws.ids, topk_weights=ws.weights)
+            ops.moe_experts(x, gate_up, down, ids, w, ws, out=out)
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg4 MoE layers done, status {ops.device_status()}")
+        return
+    if workload == "attnres":
+        gen = torch.Generator().manual_seed(7)
+        bank = torch.randn(49, 256, 2048, generator=gen).bfloat16().to(dev)
+        query = (0.02 * torch.randn(2048, generator=gen)).bfloat16().to(dev)
+        norm_w = torch.ones(2048, dtype=torch.bfloat16, device=dev)
+        flush = L2Flush(dev)
+        for _ in range(n):
+            flush_l2(flush)
+            ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w)
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} AttnRes routes (49 sources x 256 tokens x 2048) done")
+        return
     q, k, v, g, beta = cfg2_inputs(1234, dev)
     states = [cfg2_state(1235 + l, dev) for l in range(LAYERS)]
     out = torch.empty(STREAMS, HEADS, DV, device=dev, dtype=torch.bfloat16)
@@ -324,9 +507,13 @@ def main():
     ap.add_argument("--cpu-updates", type=int, default=256, help="updates in the CPU-baseline sample")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
+    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres"),
+                    help="workload whose launches --profile-launches runs")
+    ap.add_argument("--operators", type=int, default=1,
+                    help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
     args = ap.parse_args()
     if args.profile_launches:
-        profile_launches(args.profile_launches)
+        profile_launches(args.profile_launches, args.profile_workload)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -360,6 +547,14 @@ def main():
                 "sample": f"{args.cpu_updates} sequential updates of 64 streams x 16 heads ({dt:.1f} s), "
                           "oracle/gdn.py restating lm.py:576-582",
             }
+            if args.operators and world == 1:
+                ops = __import__("__graft_entry__").load_package().ops
+                dev = torch.device("cuda", local)
+                stream = torch.cuda.Stream(dev)
+                line["operators"] = {
+                    "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
+                    "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
+                }
             print(json.dumps(line), flush=True)
     finally:
         if dist is not None:

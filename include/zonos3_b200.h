@@ -48,6 +48,20 @@ int zb_gdn_decode_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int64_t gb_stride_b, float* state, const int64_t* slots, int64_t num_slots, uint16_t* out,
                        int64_t out_stride_b, int B, int H, int dk, int dv, float scale, cudaStream_t stream);
 
+/* Chunked (C = 64) gated delta rule over packed variable-length sequences: the prefill / continuation pass.
+ * Replaces FLA chunk_gated_delta_rule_fwd as called by OriginalGDN._run_packed
+ * (servers/sgl/src/zonos3_sgl/models/gdn.py:418-434; use_gate_in_kernel, state_v_first, cu_seqlens, chunk 64);
+ * result equal to the per-token recurrence of model/src/zonos3/reference/lm.py:576-582.
+ *   q, k [N, H, dk], v [N, H, dv] bf16 contiguous (16-byte aligned); g (log decay), beta [N, H] fp32
+ *   cu_seqlens [num_seqs + 1] int32 (device): sequence i is tokens [cu[i], cu[i+1])
+ *   init_state / final_state [rows, H, dv, dk] fp32 V-first or NULL (zero start / not written); sequence i uses
+ *   row state_slots[i] (int64) or row i when state_slots is NULL; out [N, H, dv] bf16 = S_t (q_t * scale)
+ *   dk == dv in {64, 128}. One CTA per (sequence, head); the fp32 state stays in shared memory. */
+int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const float* beta,
+                         const int32_t* cu_seqlens, int num_seqs, int H, int dk, int dv, float scale,
+                         const float* init_state, const int64_t* state_slots, float* final_state, uint16_t* out,
+                         cudaStream_t stream);
+
 /* ------------------------------------------------------------------------------------------- Full AttnRes */
 
 /* Full AttnRes route of every token over bank sources [0, S) plus, if `source` is non-NULL, `source` as the last
@@ -89,10 +103,11 @@ int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T,
 /* Stable counting sort of the T*k (token, slot) pairs p = t*k + slot by expert, each expert's segment padded to a
  * multiple of `block` rows: counts [E] (the per-expert token histogram), offsets [E+1] (padded segment starts,
  * offsets[E] = rows in use), sorted_pairs [capacity] (pair of each row, -1 for padding and unused rows),
- * position [T*k] (row of each pair). capacity >= roundup(T*k + E*(block-1), block). Replaces
- * moe_align_block_size (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:28-86; sgl_kernel). */
-int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* counts,
-                   int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream);
+ * position [T*k] (row of each pair). capacity >= roundup(T*k + E*(block-1), block); hist is scratch of
+ * ceil(T*k / 256) * E int32 (one expert histogram per 256-pair slice). Replaces moe_align_block_size
+ * (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:28-86; sgl_kernel). */
+int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
+                   int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream);
 
 /* out[r] = x[sorted_pairs[r] / k] for r < rows (zero rows where sorted_pairs[r] < 0): the A operand of the
  * grouped GEMM, the row gather fused_moe_kernel does through `offs_token // top_k`

@@ -28,14 +28,16 @@ SIGNATURES: dict[str, list] = {
     # out, out_stride_b, B, H, dk, dv, scale, stream
     "zb_gdn_decode_step": [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64,
                            _i32, _i32, _i32, _i32, _f32, _p],
+    # q, k, v, g, beta, cu_seqlens, num_seqs, H, dk, dv, scale, init_state, state_slots, final_state, out, stream
+    "zb_gdn_chunk_prefill": [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p, _p],
     # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream
     "zb_attnres_route": [_p, _i64, _i32, _p, _p, _p, _f32, _p, _f32, _p, _p, _i32, _i32, _p],
     # x, x_stride, norm_weight, eps, w_router, bias, T, D, E, k, weight_mode, renormalize, logits, ids, weights, stream
     "zb_moe_router": [_p, _i64, _p, _f32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p],
     # logits, logits_bf16, bias, T, E, k, weight_mode, renormalize, ids, weights, stream
     "zb_moe_select": [_p, _i32, _p, _i32, _i32, _i32, _i32, _i32, _p, _p, _p],
-    # ids, T, k, E, block, capacity, counts, offsets, sorted_pairs, position, stream
-    "zb_moe_permute": [_p, _i32, _i32, _i32, _i32, _i64, _p, _p, _p, _p, _p],
+    # ids, T, k, E, block, capacity, hist, counts, offsets, sorted_pairs, position, stream
+    "zb_moe_permute": [_p, _i32, _i32, _i32, _i32, _i64, _p, _p, _p, _p, _p, _p],
     # x, x_stride, sorted_pairs, k, rows, D, out, stream
     "zb_moe_gather": [_p, _i64, _p, _i32, _i64, _i32, _p, _p],
     # x_perm, capacity, gate_up, E, D, I, offsets, h, stream

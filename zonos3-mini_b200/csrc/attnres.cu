@@ -5,22 +5,15 @@
 // zonos3.py:99-113) and the fused Triton route _block_attnres_fwd_kernel (servers/sgl/src/zonos3_sgl/models/
 // training_attnres_kernels.py:1268-1348), whose rounding points this kernel keeps: key = bf16(v * inv_rms),
 // product = bf16(key * q), logit = fp32 sum, fp32 softmax, weight = bf16, term = bf16(v * weight), fp32 sum of
-// terms, bf16 output. The Triton kernel reads every bank row twice (logit pass, mix pass); here a token's
-// sources are staged in shared memory by one TMA bulk copy per source and read from HBM exactly once.
-//
-// Parallel layout: a token is one thread-block cluster of CL CTAs; CTA r of the cluster owns columns
-// [r*256W, (r+1)*256W) of every source (W warps, 8 bf16 = 16 bytes per thread). The per-source sums that need
-// the full row (sum of squares, logit, and the optional norm of the mix) are reduced inside each CTA with warp
-// shuffles, then across the cluster through distributed shared memory.
-#include <cooperative_groups.h>
-
+// terms, bf16 output. The Triton kernel runs one warp per token over the bank twice; here the logit pass is spread
+// over one warp per (source, token) row and the mix pass re-reads the rows the logit pass streamed just before,
+// so they come from L2 and HBM delivers each source row once.
 #include "common.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace {
 
 constexpr int kMaxSources = 256;
+constexpr int kThreads = 256;  // 8 warps per token
 
 struct RouteParams {
   const __nv_bfloat16* bank;  // [>= S, T, D]
@@ -38,101 +31,81 @@ struct RouteParams {
   unsigned* status;
 };
 
-template <int W>
-__global__ void __launch_bounds__(32 * W) attnres_route_kernel(RouteParams p) {
-  constexpr int kThreads = 32 * W;
-  constexpr int kCols = 256 * W;  // columns of one CTA
-  cg::cluster_group cluster = cg::this_cluster();
-  const int CL = (int)cluster.num_blocks();
-  const int rank = (int)cluster.block_rank();
-  const int64_t t = blockIdx.x / CL;
-  const int c0 = rank * kCols;
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+// Two kernels per route.
+//  attnres_logits_kernel: one warp per (source, token) row — every row of every token is an independent unit of
+//  work, so the whole bank streams from HBM with full parallelism. A lane holds VPL 16-byte vectors of the row
+//  (D = 256 * VPL, all loads in flight at once); the row's sum of squares and then its logit are warp-shuffle
+//  reductions with the reference rounding points. Logits of token t are parked in the first 4*ns bytes of its own
+//  output row (ns <= D/2), so the route needs no scratch memory.
+//  attnres_mix_kernel: one CTA per token: softmax over its logits (fp32, bf16 weights), then thread i sums the
+//  weighted terms of 16-byte column vectors i, i + 256, ... over all sources, 16 sources' loads in flight. Those
+//  rows were streamed by the logits kernel just before and are served by L2, so HBM delivers each row once.
+constexpr int kLogitWarps = 4;
+constexpr int kLogitRows = 2;  // rows per warp, all loads in flight together
+
+template <int VPL>
+__global__ void __launch_bounds__(32 * kLogitWarps) attnres_logits_kernel(RouteParams p) {
+  const int lane = threadIdx.x % 32;
   const int ns = p.S + (p.source ? 1 : 0);
-
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __nv_bfloat16* tiles = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [ns][kCols]
-  float* red = reinterpret_cast<float*>(smem_raw + (size_t)ns * kCols * 2);  // [ns][W]
-  float* part_ss = red + ns * W;                                           // [ns] this CTA's sum of squares
-  float* part_lg = part_ss + ns;                                           // [ns] this CTA's logit part
-  float* inv_rms = part_lg + ns;                                           // [ns]
-  float* weight = inv_rms + ns;                                            // [ns] logits, then bf16 weights
-  float* part_n = weight + ns;                                             // [1] norm partial of the mix
-  const size_t bar_off = ((size_t)ns * kCols * 2 + (size_t)(ns * W + 4 * ns + 2) * 4 + 7) & ~(size_t)7;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + bar_off);
-  const uint32_t bar_addr = zb::smem_addr(bar);
-
-  if (tid == 0) {
-    zb::mbar_init(bar_addr, 1);
-    zb::fence_mbar_init();
+  const int64_t total = (int64_t)ns * p.T;
+  const int64_t row0 = ((int64_t)blockIdx.x * kLogitWarps + threadIdx.x / 32) * kLogitRows;  // rows s * T + t
+  const int D = p.D;
+  // every load of the warp is issued before any is used: its rows, then its query columns
+  uint4 v4[kLogitRows][VPL];
+#pragma unroll
+  for (int r = 0; r < kLogitRows; ++r) {
+    const int64_t row = row0 + r < total ? row0 + r : total - 1;
+    const int s = (int)(row / p.T);
+    const int64_t t = row % p.T;
+    const __nv_bfloat16* src = (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * D;
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) v4[r][u] = __ldcs(reinterpret_cast<const uint4*>(src + u * 256 + lane * 8));
   }
-  __syncthreads();
-  if (tid == 0) {
-    const uint32_t slice_bytes = kCols * 2;
-    zb::mbar_arrive_expect_tx(bar_addr, slice_bytes * ns);
-    for (int s = 0; s < ns; ++s) {
-      const __nv_bfloat16* src = (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * p.D + c0;
-      zb::bulk_g2s(zb::smem_addr(tiles + (size_t)s * kCols), src, slice_bytes, bar_addr);
-    }
-  }
-  float q[8];
-  zb::ld_bf16x8(p.query + c0 + tid * 8, q);
-  zb::mbar_wait_bounded(bar_addr, 0, p.status, zb::kStatusAttnresLoadTimeout);
-
-  // sweep 1: sum of squares of every source row (this CTA's columns)
-  for (int s = 0; s < ns; ++s) {
-    float v[8];
-    zb::ld_bf16x8(tiles + (size_t)s * kCols + tid * 8, v);
+  uint4 q4[VPL];
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) q4[u] = *reinterpret_cast<const uint4*>(p.query + u * 256 + lane * 8);
+#pragma unroll
+  for (int r = 0; r < kLogitRows; ++r) {
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
-    ss = zb::warp_sum(ss);
-    if (lane == 0) red[s * W + warp] = ss;
-  }
-  __syncthreads();
-  for (int s = tid; s < ns; s += kThreads) {
-    float acc = 0.f;
+    for (int u = 0; u < VPL; ++u) {
+      float v[8];
+      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v4[r][u]), v);
 #pragma unroll
-    for (int w = 0; w < W; ++w) acc += red[s * W + w];
-    part_ss[s] = acc;
-  }
-  cluster.sync();
-  const float inv_d = 1.0f / (float)p.D;
-  for (int s = tid; s < ns; s += kThreads) {
-    float total = 0.f;
-    for (int r = 0; r < CL; ++r) total += cluster.map_shared_rank(part_ss, r)[s];
-    inv_rms[s] = rsqrtf(total * inv_d + p.eps);
-  }
-  __syncthreads();
-
-  // sweep 2: logits = sum bf16(bf16(v * inv_rms) * q)
-  for (int s = 0; s < ns; ++s) {
-    float v[8];
-    zb::ld_bf16x8(tiles + (size_t)s * kCols + tid * 8, v);
-    const float r = inv_rms[s];
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+    }
+    const float rr = rsqrtf(zb::warp_sum(ss) / (float)D + p.eps);
     float lg = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) lg += zb::bf16_round(zb::bf16_round(v[j] * r) * q[j]);
-    lg = zb::warp_sum(lg);
-    if (lane == 0) red[s * W + warp] = lg;
-  }
-  __syncthreads();
-  for (int s = tid; s < ns; s += kThreads) {
-    float acc = 0.f;
+    for (int u = 0; u < VPL; ++u) {
+      float v[8], qv[8];
+      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v4[r][u]), v);
+      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&q4[u]), qv);
 #pragma unroll
-    for (int w = 0; w < W; ++w) acc += red[s * W + w];
-    part_lg[s] = acc;
+      for (int j = 0; j < 8; ++j) lg += zb::bf16_round(zb::bf16_round(v[j] * rr) * qv[j]);
+    }
+    lg = zb::warp_sum(lg);
+    const int64_t row = row0 + r;
+    if (lane == 0 && row < total) reinterpret_cast<float*>(p.out + (row % p.T) * D)[row / p.T] = lg;
   }
-  cluster.sync();
-  for (int s = tid; s < ns; s += kThreads) {
-    float total = 0.f;
-    for (int r = 0; r < CL; ++r) total += cluster.map_shared_rank(part_lg, r)[s];
-    weight[s] = total;
-  }
-  __syncthreads();
+}
 
-  // softmax over the sources (fp32), weights rounded to bf16
-  if (warp == 0) {
+constexpr int kMixBatch = 16;  // source rows in flight per thread in the mix
+
+template <int VPL>
+__global__ void __launch_bounds__(kThreads) attnres_mix_kernel(RouteParams p) {
+  constexpr int kWarps = kThreads / 32;
+  constexpr int kVecs = (32 * VPL + kThreads - 1) / kThreads;  // 16-byte column vectors per thread
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int ns = p.S + (p.source ? 1 : 0);
+  const int D = p.D;
+  __shared__ float weight[kMaxSources];
+  __shared__ float red[kWarps];
+  const float* logits = reinterpret_cast<const float*>(p.out + t * D);
+  for (int s = tid; s < ns; s += kThreads) weight[s] = logits[s];
+  __syncthreads();
+  if (warp == 0) {  // softmax over the sources (fp32), weights rounded to bf16
     float m = -INFINITY;
     for (int s = lane; s < ns; s += 32) m = fmaxf(m, weight[s]);
     m = zb::warp_max(m);
@@ -142,74 +115,87 @@ __global__ void __launch_bounds__(32 * W) attnres_route_kernel(RouteParams p) {
     __syncwarp();
     for (int s = lane; s < ns; s += 32) weight[s] = zb::bf16_round(expf(weight[s] - m) / den);
   }
-  __syncthreads();
+  __syncthreads();  // every thread has read the logits before any output is written over them
 
-  // sweep 3: mix = sum bf16(v * w) in fp32
-  float mix[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < ns; ++s) {
-    float v[8];
-    zb::ld_bf16x8(tiles + (size_t)s * kCols + tid * 8, v);
-    const float w = weight[s];
+  auto row_ptr = [&](int s) -> const __nv_bfloat16* {
+    return (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * D;
+  };
+  const int nvec = D / 8;
+  float mix[kVecs][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mix[j] += zb::bf16_round(v[j] * w);
+  for (int c = 0; c < kVecs; ++c) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mix[c][j] = 0.f;
+    const int vec = tid + c * kThreads;
+    if (vec >= nvec) continue;
+    for (int s0 = 0; s0 < ns; s0 += kMixBatch) {
+      uint4 raw[kMixBatch];
+#pragma unroll
+      for (int i = 0; i < kMixBatch; ++i)
+        if (s0 + i < ns) raw[i] = __ldcg(reinterpret_cast<const uint4*>(row_ptr(s0 + i) + vec * 8));
+#pragma unroll
+      for (int i = 0; i < kMixBatch; ++i) {
+        if (s0 + i < ns) {
+          float v[8];
+          zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&raw[i]), v);
+          const float w = weight[s0 + i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) mix[c][j] += zb::bf16_round(v[j] * w);
+        }
+      }
+      if (p.append && s0 + kMixBatch >= ns) {  // the current source is the last one routed: append it
+#pragma unroll
+        for (int i = 0; i < kMixBatch; ++i)
+          if (s0 + i == ns - 1) *reinterpret_cast<uint4*>(p.append + t * D + vec * 8) = raw[i];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mix[c][j] = zb::bf16_round(mix[c][j]);
   }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) mix[j] = zb::bf16_round(mix[j]);
-  const int64_t off = t * p.D + c0 + tid * 8;
   if (p.norm_weight) {
-    if (p.mix_out) *reinterpret_cast<uint4*>(p.mix_out + off) = zb::pack_bf16x8(mix);
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(mix[j], mix[j], ss);
+    for (int c = 0; c < kVecs; ++c)
+      if (tid + c * kThreads < nvec)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(mix[c][j], mix[c][j], ss);
     ss = zb::warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
-    if (tid == 0) {
-      float acc = 0.f;
-      for (int w = 0; w < W; ++w) acc += red[w];
-      part_n[0] = acc;
-    }
-    cluster.sync();
     float total = 0.f;
-    for (int r = 0; r < CL; ++r) total += cluster.map_shared_rank(part_n, r)[0];
-    const float rn = rsqrtf(total * inv_d + p.norm_eps);
-    float nw[8], y[8];
-    zb::ld_bf16x8(p.norm_weight + c0 + tid * 8, nw);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) y[j] = mix[j] * rn * nw[j];
-    *reinterpret_cast<uint4*>(p.out + off) = zb::pack_bf16x8(y);
+    for (int w = 0; w < kWarps; ++w) total += red[w];
+    const float rn = rsqrtf(total / (float)D + p.norm_eps);
+#pragma unroll
+    for (int c = 0; c < kVecs; ++c) {
+      const int vec = tid + c * kThreads;
+      if (vec >= nvec) continue;
+      float nw[8], y[8];
+      zb::ld_bf16x8(p.norm_weight + vec * 8, nw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = mix[c][j] * rn * nw[j];
+      if (p.mix_out) *reinterpret_cast<uint4*>(p.mix_out + t * D + vec * 8) = zb::pack_bf16x8(mix[c]);
+      *reinterpret_cast<uint4*>(p.out + t * D + vec * 8) = zb::pack_bf16x8(y);
+    }
   } else {
-    *reinterpret_cast<uint4*>(p.out + off) = zb::pack_bf16x8(mix);
+#pragma unroll
+    for (int c = 0; c < kVecs; ++c) {
+      const int vec = tid + c * kThreads;
+      if (vec >= nvec) continue;
+      *reinterpret_cast<uint4*>(p.out + t * D + vec * 8) = zb::pack_bf16x8(mix[c]);
+    }
   }
-  if (p.append) {
-    *reinterpret_cast<uint4*>(p.append + off) =
-        *reinterpret_cast<const uint4*>(tiles + (size_t)(ns - 1) * kCols + tid * 8);
-  }
-  cluster.sync();  // keep this CTA's shared memory alive until every cluster peer has read it
 }
 
-template <int W>
-int launch(const RouteParams& p, int CL, cudaStream_t stream) {
+template <int VPL>
+int launch(const RouteParams& p, cudaStream_t stream) {
   const int ns = p.S + (p.source ? 1 : 0);
-  const size_t smem = (size_t)ns * 256 * W * 2 + (size_t)(ns * W + ns * 4 + 2) * sizeof(float) + 16;
-  auto kernel = attnres_route_kernel<W>;
-  if (smem > 48 * 1024) {
-    ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.T * CL));
-  cfg.blockDim = dim3(32 * W);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CL;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
-  return zb::check_launch("attnres_route");
+  const int64_t rows = (int64_t)ns * p.T;
+  const int64_t per_cta = (int64_t)kLogitWarps * kLogitRows;
+  attnres_logits_kernel<VPL><<<(unsigned)((rows + per_cta - 1) / per_cta), 32 * kLogitWarps, 0, stream>>>(p);
+  if (int rc = zb::check_launch("attnres_route(logits)")) return rc;
+  attnres_mix_kernel<VPL><<<(unsigned)p.T, kThreads, 0, stream>>>(p);
+  return zb::check_launch("attnres_route(mix)");
 }
 
 }  // namespace
@@ -221,10 +207,15 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
   ZB_REQUIRE(S >= 0 && T >= 0 && D > 0, "attnres_route: bad sizes S=%d T=%d D=%d", S, T, D);
   ZB_REQUIRE(ns >= 1, "attnres_route: no source to route over");
   if (ns > kMaxSources) return zb::fail(zb::kUnsupported, "attnres_route: %d sources (max %d)", ns, kMaxSources);
-  if (D % 256 != 0 || D > 8 * 8 * 256)
-    return zb::fail(zb::kUnsupported, "attnres_route: D=%d (a multiple of 256, at most 16384)", D);
+  if (D % 256 != 0 || D > 8 * 512)
+    return zb::fail(zb::kUnsupported, "attnres_route: D=%d (a multiple of 256, at most 4096)", D);
+  if (ns > D / 2)
+    return zb::fail(zb::kUnsupported, "attnres_route: %d sources need D >= %d (the logits park in the output row)",
+                    ns, 2 * ns);
   if (T == 0) return zb::kOk;
   ZB_REQUIRE(query && out, "attnres_route: null query/out");
+  ZB_REQUIRE(out != source && out != append && (mix_out == nullptr || (mix_out != out && mix_out != source)),
+             "attnres_route: out / mix_out must not alias the sources");
   ZB_REQUIRE(S == 0 || bank, "attnres_route: null bank with S=%d", S);
   ZB_REQUIRE(!append || source, "attnres_route: append needs a source");
   ZB_REQUIRE(!mix_out || norm_weight, "attnres_route: mix_out is only written with norm_weight");
@@ -240,24 +231,15 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
                 reinterpret_cast<const __nv_bfloat16*>(norm_weight), norm_eps,
                 reinterpret_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(mix_out), T, D,
                 zb::device_status_ptr()};
-  // W warps per CTA and CL CTAs per cluster with 256*W*CL == D: the smallest W whose cluster fits in the
-  // portable limit of 8, preferring clusters of at most 4 (several small CTAs per SM keep more loads in flight).
-  const int units = D / 256;  // = W * CL
-  int W = 0, CL = 0;
-  for (int w : {1, 2, 4, 8}) {
-    if (units % w == 0 && units / w <= 4) { W = w; CL = units / w; break; }
-  }
-  if (W == 0) {
-    for (int w : {1, 2, 4, 8}) {
-      if (units % w == 0 && units / w <= 8) { W = w; CL = units / w; break; }
-    }
-  }
-  if (W == 0) return zb::fail(zb::kUnsupported, "attnres_route: D=%d has no cluster split", D);
-  switch (W) {
-    case 1: return launch<1>(p, CL, stream);
-    case 2: return launch<2>(p, CL, stream);
-    case 4: return launch<4>(p, CL, stream);
-    case 8: return launch<8>(p, CL, stream);
-    default: return zb::fail(zb::kUnsupported, "attnres_route: D=%d", D);
+  switch (D / 256) {
+    case 1: return launch<1>(p, stream);
+    case 2: return launch<2>(p, stream);
+    case 3: return launch<3>(p, stream);
+    case 4: return launch<4>(p, stream);
+    case 6: return launch<6>(p, stream);
+    case 8: return launch<8>(p, stream);
+    case 12: return launch<12>(p, stream);
+    case 16: return launch<16>(p, stream);
+    default: return zb::fail(zb::kUnsupported, "attnres_route: D=%d (256, 512, 768, 1024, 1536, 2048, 3072 or 4096)", D);
   }
 }

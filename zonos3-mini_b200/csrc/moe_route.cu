@@ -16,8 +16,7 @@
 
 namespace {
 
-constexpr int kRouterWarps = 2;              // 16 tokens per warp
-constexpr int kRouterTokens = 16 * kRouterWarps;
+constexpr int kRouterTokens = 16;           // tokens of one router CTA (one m16 tile)
 constexpr int kChunk = 64;                   // K columns per smem chunk
 constexpr int kPad = 8;                      // row padding (elements) against bank conflicts
 constexpr int kMaxExperts = 128;
@@ -129,27 +128,83 @@ __device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// NT = number of 8-expert column tiles (E <= 8 * NT).
-template <int NT>
-__global__ void __launch_bounds__(32 * kRouterWarps) moe_router_kernel(RouterParams p) {
-  __shared__ __align__(16) __nv_bfloat16 a_s[kRouterTokens][kChunk + kPad];
-  __shared__ __align__(16) __nv_bfloat16 b_s[NT * 8][kChunk + kPad];
-  __shared__ float rms_s[kRouterTokens];
-  __shared__ float logit_s[kRouterTokens][NT * 8 + 1];
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = zb::smem_addr(dst);
+  const int bytes = valid ? 16 : 0;  // zero-fill when invalid
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// bf16x2 word scaled elementwise by (s * w0, s * w1) and rounded back to bf16x2: the router input
+// bf16(x * inv_rms * rmsnorm_eda.weight) formed in registers from the raw x tile.
+__device__ __forceinline__ uint32_t scale_bf16x2(uint32_t raw, float s, uint32_t wraw) {
+  const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw));
+  const float2 w = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wraw));
+  __nv_bfloat162 o = __floats2bfloat162_rn(v.x * s * w.x, v.y * s * w.y);
+  return *reinterpret_cast<uint32_t*>(&o);
+}
+
+constexpr int kRouterThreads = 128;  // 4 warps, each a quarter of the experts
+constexpr int kRouterStages = 4;
+constexpr int kRow = kChunk + kPad;  // smem row length (elements)
+
+// One CTA routes 16 tokens. A 4-stage cp.async pipeline streams K chunks of x [16 x 64], the router weight
+// [NE x 64] and the norm weight [64]; warp w computes the logits of experts [w*8*NH, (w+1)*8*NH) for the 16 tokens
+// with mma.sync m16n8k16 (bf16 in, fp32 accumulate), the A fragments scaled by inv_rms * norm weight in registers.
+// The inverse RMS of the tokens comes first (4 tokens per warp, 8 independent 16-byte loads per lane in flight),
+// and every warp then selects the top-k of 4 tokens.
+template <int NH>  // n-tiles (8 experts each) per warp: E <= 32 * NH
+__global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(RouterParams p) {
+  constexpr int NE = 32 * NH;  // experts covered by the CTA
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* a_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);               // [stages][16][kRow]
+  __nv_bfloat16* b_s = a_s + kRouterStages * kRouterTokens * kRow;                // [stages][NE][kRow]
+  __nv_bfloat16* w_s = b_s + kRouterStages * NE * kRow;                            // [stages][kChunk]
+  float* rms_s = reinterpret_cast<float*>(w_s + kRouterStages * kChunk);          // [16]
+  float* logit_s = rms_s + kRouterTokens;                                         // [16][NE + 1]
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int tok0 = blockIdx.x * kRouterTokens;
+  const int n_chunks = p.D / kChunk;
 
-  // inverse RMS of every token of the tile (fp32), the rmsnorm_eda factor
-  for (int r = warp; r < kRouterTokens; r += kRouterWarps) {
+  auto load_chunk = [&](int chunk, int stage) {
+    const int k0 = chunk * kChunk;
+    __nv_bfloat16* a = a_s + stage * kRouterTokens * kRow;
+    __nv_bfloat16* b = b_s + stage * NE * kRow;
+    for (int idx = tid; idx < kRouterTokens * (kChunk / 8); idx += kRouterThreads) {
+      const int r = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
+      const int t = tok0 + r;
+      cp_async16(a + r * kRow + c, p.x + (int64_t)(t < p.T ? t : 0) * p.x_stride + k0 + c, t < p.T);
+    }
+    for (int idx = tid; idx < NE * (kChunk / 8); idx += kRouterThreads) {
+      const int e = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
+      cp_async16(b + e * kRow + c, p.w_router + (int64_t)(e < p.E ? e : 0) * p.D + k0 + c, e < p.E);
+    }
+    if (tid < kChunk / 8) cp_async16(w_s + stage * kChunk + tid * 8, p.norm_w + k0 + tid * 8, true);
+  };
+
+  // prologue: start the first stages while the inverse RMS is computed
+#pragma unroll
+  for (int s = 0; s < kRouterStages - 1; ++s) {
+    if (s < n_chunks) load_chunk(s, s);
+    cp_async_commit();
+  }
+  for (int r = warp; r < kRouterTokens; r += kRouterThreads / 32) {
     const int t = tok0 + r;
     float ss = 0.f;
     if (t < p.T) {
       const __nv_bfloat16* row = p.x + (int64_t)t * p.x_stride;
-      for (int c = lane * 8; c < p.D; c += 256) {
-        float v[8];
-        zb::ld_bf16x8(row + c, v);
+      for (int c0 = lane * 8; c0 < p.D; c0 += 256 * 8) {
+        float v[8][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * 256 < p.D) zb::ld_bf16x8(row + c0 + u * 256, v[u]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + u * 256 < p.D)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(v[u][j], v[u][j], ss);
       }
     }
     ss = zb::warp_sum(ss);
@@ -157,71 +212,77 @@ __global__ void __launch_bounds__(32 * kRouterWarps) moe_router_kernel(RouterPar
   }
   __syncthreads();
 
-  float acc[NT][4];
-#pragma unroll
-  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const int nbase = warp * NH;  // first n-tile of this warp
   const int g = lane >> 2, tq = lane & 3;
-  for (int k0 = 0; k0 < p.D; k0 += kChunk) {
-    // A chunk: router input = bf16(x * inv_rms * norm_weight)
-    for (int idx = tid; idx < kRouterTokens * (kChunk / 8); idx += 32 * kRouterWarps) {
-      const int r = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
-      const int t = tok0 + r;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (t < p.T) {
-        float w[8];
-        zb::ld_bf16x8(p.x + (int64_t)t * p.x_stride + k0 + c, v);
-        zb::ld_bf16x8(p.norm_w + k0 + c, w);
-        const float s = rms_s[r];
+  const float s_lo = rms_s[g], s_hi = rms_s[g + 8];
+  float acc[NH][4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = v[j] * s * w[j];
-      }
-      *reinterpret_cast<uint4*>(&a_s[r][c]) = zb::pack_bf16x8(v);
-    }
-    for (int idx = tid; idx < NT * 8 * (kChunk / 8); idx += 32 * kRouterWarps) {
-      const int e = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (e < p.E) w = *reinterpret_cast<const uint4*>(p.w_router + (int64_t)e * p.D + k0 + c);
-      *reinterpret_cast<uint4*>(&b_s[e][c]) = w;
-    }
+  for (int n = 0; n < NH; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  for (int chunk = 0; chunk < n_chunks; ++chunk) {
+    const int stage = chunk % kRouterStages;
+    cp_async_wait<kRouterStages - 2>();
     __syncthreads();
+    // refill the stage consumed in the previous iteration
+    const int next = chunk + kRouterStages - 1;
+    if (next < n_chunks) load_chunk(next, next % kRouterStages);
+    cp_async_commit();
+    if (nbase * 8 >= p.E) continue;  // this warp's experts are all padding
+    const __nv_bfloat16* a = a_s + stage * kRouterTokens * kRow;
+    const __nv_bfloat16* b = b_s + stage * NE * kRow;
+    const __nv_bfloat16* wv = w_s + stage * kChunk;
 #pragma unroll
     for (int kk = 0; kk < kChunk; kk += 16) {
-      uint32_t a[4];
-      const int r0 = warp * 16 + g;
-      a[0] = *reinterpret_cast<const uint32_t*>(&a_s[r0][kk + 2 * tq]);
-      a[1] = *reinterpret_cast<const uint32_t*>(&a_s[r0 + 8][kk + 2 * tq]);
-      a[2] = *reinterpret_cast<const uint32_t*>(&a_s[r0][kk + 2 * tq + 8]);
-      a[3] = *reinterpret_cast<const uint32_t*>(&a_s[r0 + 8][kk + 2 * tq + 8]);
+      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(wv + kk + 2 * tq);
+      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(wv + kk + 2 * tq + 8);
+      uint32_t af[4];
+      af[0] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + g * kRow + kk + 2 * tq), s_lo, w0);
+      af[1] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + (g + 8) * kRow + kk + 2 * tq), s_hi, w0);
+      af[2] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + g * kRow + kk + 2 * tq + 8), s_lo, w1);
+      af[3] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + (g + 8) * kRow + kk + 2 * tq + 8), s_hi, w1);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        uint32_t b[2];
-        b[0] = *reinterpret_cast<const uint32_t*>(&b_s[n * 8 + g][kk + 2 * tq]);
-        b[1] = *reinterpret_cast<const uint32_t*>(&b_s[n * 8 + g][kk + 2 * tq + 8]);
-        mma_bf16_16816(acc[n], a, b);
+      for (int n = 0; n < NH; ++n) {
+        const int e = (nbase + n) * 8 + g;
+        uint32_t bf[2];
+        bf[0] = *reinterpret_cast<const uint32_t*>(b + e * kRow + kk + 2 * tq);
+        bf[1] = *reinterpret_cast<const uint32_t*>(b + e * kRow + kk + 2 * tq + 8);
+        mma_bf16_16816(acc[n], af, bf);
       }
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
   // logits rounded to bf16 (the router_linear output dtype)
 #pragma unroll
-  for (int n = 0; n < NT; ++n) {
-    const int r0 = warp * 16 + g, c0 = n * 8 + 2 * tq;
-    logit_s[r0][c0] = zb::bf16_round(acc[n][0]);
-    logit_s[r0][c0 + 1] = zb::bf16_round(acc[n][1]);
-    logit_s[r0 + 8][c0] = zb::bf16_round(acc[n][2]);
-    logit_s[r0 + 8][c0 + 1] = zb::bf16_round(acc[n][3]);
+  for (int n = 0; n < NH; ++n) {
+    const int c0 = (nbase + n) * 8 + 2 * tq;
+    logit_s[g * (NE + 1) + c0] = zb::bf16_round(acc[n][0]);
+    logit_s[g * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][1]);
+    logit_s[(g + 8) * (NE + 1) + c0] = zb::bf16_round(acc[n][2]);
+    logit_s[(g + 8) * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][3]);
   }
   __syncthreads();
-  for (int r = warp; r < kRouterTokens; r += kRouterWarps) {
+  for (int r = warp; r < kRouterTokens; r += kRouterThreads / 32) {
     const int t = tok0 + r;
     if (t >= p.T) break;
+    const float* lrow = logit_s + r * (NE + 1);
     if (p.logits_out) {
-      for (int e = lane; e < p.E; e += 32)
-        p.logits_out[(int64_t)t * p.E + e] = __float2bfloat16_rn(logit_s[r][e]);
+      for (int e = lane; e < p.E; e += 32) p.logits_out[(int64_t)t * p.E + e] = __float2bfloat16_rn(lrow[e]);
     }
-    select_token([&](int e) { return logit_s[r][e]; }, p.bias, p.E, p.k, p.mode, p.renorm,
-                 p.ids + (int64_t)t * p.k, p.weights + (int64_t)t * p.k);
+    select_token([&](int e) { return lrow[e]; }, p.bias, p.E, p.k, p.mode, p.renorm, p.ids + (int64_t)t * p.k,
+                 p.weights + (int64_t)t * p.k);
   }
+}
+
+template <int NH>
+int launch_router(const RouterParams& p, cudaStream_t stream) {
+  constexpr int NE = 32 * NH;
+  const size_t smem = (size_t)kRouterStages * (kRouterTokens + NE) * kRow * 2 + kRouterStages * kChunk * 2 +
+                      kRouterTokens * 4 + (size_t)kRouterTokens * (NE + 1) * 4;
+  auto kernel = moe_router_kernel<NH>;
+  if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const unsigned grid = (unsigned)((p.T + kRouterTokens - 1) / kRouterTokens);
+  kernel<<<grid, kRouterThreads, smem, stream>>>(p);
+  return zb::check_launch("moe_router");
 }
 
 struct SelectParams {
@@ -250,88 +311,127 @@ __global__ void __launch_bounds__(256) moe_select_kernel(SelectParams p) {
 
 // ----------------------------------------------------------------------------------------------- permutation
 
-constexpr int kPermWarps = 32;
+constexpr int kPermPairs = 256;  // pairs of one CTA (8 warps x 32)
+constexpr int kPermThreads = 256;
 
 struct PermuteParams {
   const int32_t* ids;  // [P] flattened (token, slot) experts
   int P, E, block;
-  int64_t capacity;    // rows of sorted_pairs
-  int32_t* counts;     // [E]
-  int32_t* offsets;    // [E + 1] padded segment starts; offsets[E] = padded rows in use
+  int64_t capacity;       // rows of sorted_pairs
+  int32_t* hist;          // scratch [num_ctas][E]: per-CTA expert counts
+  int32_t* counts;        // [E]
+  int32_t* offsets;       // [E + 1] padded segment starts; offsets[E] = padded rows in use
   int32_t* sorted_pairs;  // [capacity], -1 = padding
   int32_t* position;      // [P]
 };
 
-// One CTA of 32 warps. Warp w owns the contiguous pair range [w*C, (w+1)*C); pass 1 counts per (warp, expert),
-// the scan turns the counts into per-(warp, expert) write cursors, pass 2 re-reads the range in order and places
-// every pair at cursor + its rank among the equal experts of its 32-pair group (match.any), which keeps the
-// sort stable without atomics on the output order.
-__global__ void __launch_bounds__(32 * kPermWarps) moe_permute_kernel(PermuteParams p) {
-  extern __shared__ int32_t hist[];  // [kPermWarps][E] counts, then cursors
-  __shared__ int32_t seg[kMaxExperts + 1];
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  for (int i = tid; i < kPermWarps * p.E; i += blockDim.x) hist[i] = 0;
+// Pass 1: the expert histogram of each 256-pair slice (order-free shared-memory atomics).
+__global__ void __launch_bounds__(kPermThreads) moe_count_kernel(PermuteParams p) {
+  __shared__ int32_t h[kMaxExperts];
+  for (int e = threadIdx.x; e < p.E; e += kPermThreads) h[e] = 0;
   __syncthreads();
-  const int chunk = (p.P + kPermWarps - 1) / kPermWarps;
-  const int lo = warp * chunk, hi = min(p.P, lo + chunk);
-  for (int i = lo + lane; i < hi; i += 32) {
+  const int i = blockIdx.x * kPermPairs + threadIdx.x;
+  if (i < p.P) {
     const int e = p.ids[i];
-    if (e >= 0 && e < p.E) atomicAdd(&hist[warp * p.E + e], 1);
+    if (e >= 0 && e < p.E) atomicAdd(&h[e], 1);
   }
   __syncthreads();
-  if (tid < p.E) {
-    int total = 0;
-    for (int w = 0; w < kPermWarps; ++w) total += hist[w * p.E + tid];
-    p.counts[tid] = total;
-    seg[tid] = (total + p.block - 1) / p.block * p.block;
+  for (int e = threadIdx.x; e < p.E; e += kPermThreads) p.hist[(int64_t)blockIdx.x * p.E + e] = h[e];
+}
+
+// Pass 2: every CTA derives the padded segment starts and its own write cursor per expert from all slice
+// histograms (slices before it, in order), then places its 256 pairs: warp w handles pairs [32w, 32w+32) of the
+// slice, ranks among equal experts inside the warp come from match.any, and the per-(warp, expert) counts are
+// scanned across the warps. Pairs of one expert therefore keep ascending p (stable), with no atomics on order.
+__global__ void __launch_bounds__(kPermThreads) moe_scatter_kernel(PermuteParams p) {
+  __shared__ int32_t base[kMaxExperts];      // write cursor of this slice per expert
+  __shared__ int32_t seg[kMaxExperts + 1];   // padded segment starts
+  __shared__ int32_t total[kMaxExperts];
+  __shared__ int32_t wcount[kPermThreads / 32][kMaxExperts];
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int nslices = gridDim.x, me = blockIdx.x;
+  {  // totals and this slice's prefix per expert: thread (group g, expert e) sums a strided share of the slices
+    int* part_all = &wcount[0][0];  // reused as [groups][E] partial sums before the rank pass
+    int* part_before = part_all + kMaxExperts * 4;
+    const int groups = min(kPermThreads / p.E, 4);
+    const int e = tid % p.E, gi = tid / p.E;
+    if (gi < groups) {
+      int before = 0, all = 0;
+#pragma unroll 8
+      for (int c = gi; c < nslices; c += groups) {
+        const int n = p.hist[(int64_t)c * p.E + e];
+        before += c < me ? n : 0;
+        all += n;
+      }
+      part_all[gi * kMaxExperts + e] = all;
+      part_before[gi * kMaxExperts + e] = before;
+    }
+    __syncthreads();
+    if (tid < p.E) {
+      int all = 0, before = 0;
+      for (int g = 0; g < groups; ++g) {
+        all += part_all[g * kMaxExperts + tid];
+        before += part_before[g * kMaxExperts + tid];
+      }
+      total[tid] = all;
+      base[tid] = before;
+    }
+    __syncthreads();
   }
+  for (int i = tid; i < (kPermThreads / 32) * kMaxExperts; i += kPermThreads) (&wcount[0][0])[i] = 0;
   __syncthreads();
-  if (tid == 0) {
+  if (warp == 0) {  // exclusive scan of the padded totals (E <= 128: 4 per lane)
+    int local[kMaxExperts / 32];
     int run = 0;
-    for (int e = 0; e < p.E; ++e) {
-      const int n = seg[e];
-      seg[e] = run;
-      run += n;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int e = lane * (kMaxExperts / 32) + j;
+      local[j] = e < p.E ? (total[e] + p.block - 1) / p.block * p.block : 0;
+      run += local[j];
     }
-    seg[p.E] = run;
+    int incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int start = incl - run;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int e = lane * (kMaxExperts / 32) + j;
+      if (e < p.E) seg[e] = start;
+      start += local[j];
+    }
+    if (lane == 31) seg[p.E] = incl;
   }
   __syncthreads();
-  if (tid <= p.E) p.offsets[tid] = seg[tid];
-  if (tid < p.E) {
-    int cursor = seg[tid];
-    for (int w = 0; w < kPermWarps; ++w) {
-      const int n = hist[w * p.E + tid];
-      hist[w * p.E + tid] = cursor;
-      cursor += n;
-    }
-  }
+  // ranks inside this slice
+  const int i = me * kPermPairs + tid;
+  const bool live = i < p.P;
+  const int e = live ? p.ids[i] : -1;
+  const bool ok = live && e >= 0 && e < p.E;
+  const unsigned peers = __match_any_sync(0xffffffffu, ok ? e : -1);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (ok && rank == 0) wcount[warp][e] = __popc(peers);
   __syncthreads();
-  for (int base = lo; base < hi; base += 32) {
-    const int i = base + lane;
-    const bool live = i < hi;
-    const int e = live ? p.ids[i] : -1;
-    const bool ok = live && e >= 0 && e < p.E;
-    const unsigned peers = __match_any_sync(0xffffffffu, ok ? e : -1);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    int pos = -1;
-    if (ok) {
-      pos = hist[warp * p.E + e] + rank;
-      p.sorted_pairs[pos] = i;
-      p.position[i] = pos;
-    } else if (live) {
-      p.position[i] = -1;
-    }
-    __syncwarp();
-    if (ok && rank == 0) hist[warp * p.E + e] += __popc(peers);
-    __syncwarp();
+  if (ok) {
+    int pos = seg[e] + base[e] + rank;
+    for (int w = 0; w < warp; ++w) pos += wcount[w][e];
+    p.sorted_pairs[pos] = i;
+    p.position[i] = pos;
+  } else if (live) {
+    p.position[i] = -1;
   }
-  __syncthreads();
-  // padding rows of every segment (from the last warp's final cursor), and everything past the last segment
-  for (int e = warp; e < p.E; e += kPermWarps) {
-    const int start = hist[(kPermWarps - 1) * p.E + e];
-    for (int r = start + lane; r < seg[e + 1]; r += 32) p.sorted_pairs[r] = -1;
+  // padding rows of every segment (expert e handled by slice e % nslices), then rows past the last segment
+  for (int x = me; x < p.E; x += nslices) {
+    for (int r = seg[x] + total[x] + tid; r < seg[x + 1]; r += kPermThreads) p.sorted_pairs[r] = -1;
   }
-  for (int64_t r = seg[p.E] + tid; r < p.capacity; r += blockDim.x) p.sorted_pairs[r] = -1;
+  for (int64_t r = seg[p.E] + (int64_t)me * kPermThreads + tid; r < p.capacity; r += (int64_t)nslices * kPermThreads)
+    p.sorted_pairs[r] = -1;
+  if (me == 0) {
+    for (int x = tid; x < p.E; x += kPermThreads) p.counts[x] = total[x];
+    for (int x = tid; x <= p.E; x += kPermThreads) p.offsets[x] = seg[x];
+  }
 }
 
 struct GatherParams {
@@ -373,11 +473,20 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(CombineParams p) {
     const int64_t t = i / vec_per_row;
     const int c = (int)(i % vec_per_row) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < p.k; ++s) {
-      float v[8];
-      zb::ld_bf16x8(p.y + (t * p.k + s) * p.D + c, v);
+    for (int s0 = 0; s0 < p.k; s0 += 8) {  // up to 8 slot rows in flight, summed in slot order
+      uint4 raw[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+      for (int s = 0; s < 8; ++s)
+        if (s0 + s < p.k) raw[s] = *reinterpret_cast<const uint4*>(p.y + (t * p.k + s0 + s) * p.D + c);
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s0 + s < p.k) {
+          float v[8];
+          zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&raw[s]), v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += v[j];
+        }
+      }
     }
     *reinterpret_cast<uint4*>(p.out + t * p.out_stride + c) = zb::pack_bf16x8(acc);
   }
@@ -419,14 +528,10 @@ ZB_API int zb_moe_router(const uint16_t* x, int64_t x_stride, const uint16_t* no
                  reinterpret_cast<const __nv_bfloat16*>(norm_weight), eps,
                  reinterpret_cast<const __nv_bfloat16*>(w_router), bias, T, D, E, k, weight_mode, renormalize,
                  reinterpret_cast<__nv_bfloat16*>(logits_out), ids, weights};
-  const unsigned grid = (unsigned)((T + kRouterTokens - 1) / kRouterTokens);
-  const int nt = (E + 7) / 8;
-  if (nt <= 1) moe_router_kernel<1><<<grid, 32 * kRouterWarps, 0, stream>>>(p);
-  else if (nt <= 2) moe_router_kernel<2><<<grid, 32 * kRouterWarps, 0, stream>>>(p);
-  else if (nt <= 4) moe_router_kernel<4><<<grid, 32 * kRouterWarps, 0, stream>>>(p);
-  else if (nt <= 8) moe_router_kernel<8><<<grid, 32 * kRouterWarps, 0, stream>>>(p);
-  else moe_router_kernel<16><<<grid, 32 * kRouterWarps, 0, stream>>>(p);
-  return zb::check_launch("moe_router");
+  const int nh = (E + 31) / 32;
+  if (nh <= 1) return launch_router<1>(p, stream);
+  if (nh <= 2) return launch_router<2>(p, stream);
+  return launch_router<4>(p, stream);
 }
 
 ZB_API int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T, int E, int k,
@@ -442,19 +547,22 @@ ZB_API int zb_moe_select(const void* logits, int logits_bf16, const float* bias,
   return zb::check_launch("moe_select");
 }
 
-ZB_API int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* counts,
-                          int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream) {
+ZB_API int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
+                          int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position,
+                          cudaStream_t stream) {
   ZB_REQUIRE(T >= 0 && k > 0 && E > 0 && block > 0, "moe_permute: bad sizes T=%d k=%d E=%d block=%d", T, k, E, block);
   if (E > kMaxExperts) return zb::fail(zb::kUnsupported, "moe_permute: E=%d (max %d)", E, kMaxExperts);
   const int64_t P = (int64_t)T * k;
   const int64_t need = ((P + (int64_t)E * (block - 1)) + block - 1) / block * block;
   ZB_REQUIRE(capacity >= need, "moe_permute: capacity %lld < %lld padded rows", (long long)capacity, (long long)need);
   ZB_REQUIRE(P < (1ll << 30), "moe_permute: %lld pairs", (long long)P);
-  ZB_REQUIRE(counts && offsets && sorted_pairs && position && (P == 0 || ids), "moe_permute: null pointer");
-  PermuteParams p{ids, (int)P, E, block, capacity, counts, offsets, sorted_pairs, position};
-  const size_t smem = (size_t)kPermWarps * E * sizeof(int32_t);
-  moe_permute_kernel<<<1, 32 * kPermWarps, smem, stream>>>(p);
-  return zb::check_launch("moe_permute");
+  ZB_REQUIRE(hist && counts && offsets && sorted_pairs && position && (P == 0 || ids), "moe_permute: null pointer");
+  PermuteParams p{ids, (int)P, E, block, capacity, hist, counts, offsets, sorted_pairs, position};
+  const unsigned slices = (unsigned)std::max<int64_t>(1, (P + kPermPairs - 1) / kPermPairs);
+  moe_count_kernel<<<slices, kPermThreads, 0, stream>>>(p);
+  if (int rc = zb::check_launch("moe_permute(count)")) return rc;
+  moe_scatter_kernel<<<slices, kPermThreads, 0, stream>>>(p);
+  return zb::check_launch("moe_permute(scatter)");
 }
 
 ZB_API int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sorted_pairs, int k, int64_t rows,

@@ -242,11 +242,19 @@ def moe_select(logits, bias, top_k, *, weights="selected_softmax", renormalize=F
     return ids, topk_weights
 
 
+PERMUTE_SLICE = 256  # pairs per CTA of the permutation kernels
+
+
+def permute_hist_size(pairs: int, num_experts: int) -> int:
+    """int32 elements of the permutation's scratch (one expert histogram per 256-pair slice)."""
+    return max(1, -(-pairs // PERMUTE_SLICE)) * num_experts
+
+
 def moe_permute(ids, num_experts, *, block=GEMM_BLOCK, capacity=None, out=None):
     """Stable sort of the (token, slot) pairs by expert, segments padded to ``block`` rows.
 
-    Returns dict(counts [E], offsets [E+1], sorted_pairs [capacity] (-1 = padding), position [T*k]) as int32
-    device tensors; ``out`` may supply them (graph-safe reuse)."""
+    Returns dict(counts [E], offsets [E+1], sorted_pairs [capacity] (-1 = padding), position [T*k], hist (scratch))
+    as int32 device tensors; ``out`` may supply them (graph-safe reuse)."""
     _check_cuda("ids", ids, torch.int32)
     dev = ids.device
     T, k = ids.shape
@@ -259,8 +267,11 @@ def moe_permute(ids, num_experts, *, block=GEMM_BLOCK, capacity=None, out=None):
             "offsets": torch.empty(num_experts + 1, device=dev, dtype=torch.int32),
             "sorted_pairs": torch.empty(capacity, device=dev, dtype=torch.int32),
             "position": torch.empty(T * k, device=dev, dtype=torch.int32),
+            "hist": torch.empty(permute_hist_size(T * k, num_experts), device=dev, dtype=torch.int32),
         }
-    _lib.call("zb_moe_permute", ids.data_ptr(), T, k, num_experts, block, capacity, out["counts"].data_ptr(),
+    _require(out["hist"].numel() >= permute_hist_size(T * k, num_experts), "permutation scratch too small")
+    _lib.call("zb_moe_permute", ids.data_ptr(), T, k, num_experts, block, capacity, out["hist"].data_ptr(),
+              out["counts"].data_ptr(),
               out["offsets"].data_ptr(), out["sorted_pairs"].data_ptr(), out["position"].data_ptr(), _stream(dev))
     return out
 
@@ -332,6 +343,7 @@ class MoEWorkspace:
             "offsets": torch.empty(num_experts + 1, **i32),
             "sorted_pairs": torch.empty(cap, **i32),
             "position": torch.empty(tokens * top_k, **i32),
+            "hist": torch.empty(permute_hist_size(tokens * top_k, num_experts), **i32),
         }
         self.x_perm = torch.empty(cap, hidden, **bf)
         self.h = torch.empty(cap, intermediate, **bf)
@@ -360,3 +372,52 @@ def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, ou
     if out is None:
         out = torch.empty((T, D), device=x.device, dtype=torch.bfloat16)
     return moe_combine(ws.y, k, out)
+
+
+def gdn_chunk_prefill(q, k, v, g, beta, cu_seqlens, *, initial_state=None, output_final_state=True, scale=None,
+                      state_slots=None, final_state=None, out=None):
+    """Chunked (C = 64) gated delta rule over packed variable-length sequences, fp32 state.
+
+    The call FLA's chunk_gated_delta_rule_fwd makes for OriginalGDN._run_packed
+    (servers/sgl/src/zonos3_sgl/models/gdn.py:418-434), with the per-token math of
+    model/src/zonos3/reference/lm.py:576-582. q, k [N, H, d] bf16 (L2-normalised), v [N, H, d] bf16, g / beta
+    [N, H] fp32 (g = log decay), cu_seqlens [n+1] int32 (device). initial_state / final_state [n or slots, H, d, d]
+    fp32 V-first (``state_slots`` [n] int64 maps sequence i to a state row). Returns (out [N, H, d] bf16,
+    final_state or None)."""
+    _check_cuda("q", q, torch.bfloat16)
+    dev = q.device
+    N, H, dk = q.shape
+    dv = v.shape[-1]
+    for name, t in (("k", k), ("v", v)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+        _require(t.is_contiguous() and t.shape[:2] == (N, H), f"{name} must be a contiguous [N, H, d] tensor")
+    _require(q.is_contiguous(), "q must be contiguous")
+    for name, t in (("g", g), ("beta", beta)):
+        _check_cuda(name, t, torch.float32, dev)
+        _require(t.shape == (N, H) and t.is_contiguous(), f"{name} must be a contiguous [N, H] tensor")
+    _check_cuda("cu_seqlens", cu_seqlens, torch.int32, dev)
+    n = cu_seqlens.numel() - 1
+    _require(n >= 0 and cu_seqlens.is_contiguous(), "cu_seqlens must be a contiguous [n + 1] tensor")
+    rows = n
+    if state_slots is not None:
+        _check_cuda("state_slots", state_slots, torch.int64, dev)
+        _require(state_slots.shape == (n,), "state_slots must be [n]")
+    for name, t in (("initial_state", initial_state), ("final_state", final_state)):
+        if t is not None:
+            _check_cuda(name, t, torch.float32, dev)
+            _require(t.dim() == 4 and tuple(t.shape[1:]) == (H, dv, dk) and t.is_contiguous(),
+                     f"{name} must be a contiguous [*, {H}, {dv}, {dk}] tensor")
+            _require(state_slots is not None or t.shape[0] >= n, f"{name} has fewer rows than sequences")
+    if output_final_state and final_state is None:
+        final_state = torch.empty((rows, H, dv, dk), device=dev, dtype=torch.float32)
+    if out is None:
+        out = torch.empty((N, H, dv), device=dev, dtype=torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    _require(out.shape == (N, H, dv) and out.is_contiguous(), "out must be a contiguous [N, H, dv] tensor")
+    if scale is None:
+        scale = dk ** -0.5
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call("zb_gdn_chunk_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(),
+              cu_seqlens.data_ptr(), n, H, dk, dv, float(scale), ptr(initial_state), ptr(state_slots),
+              ptr(final_state) if output_final_state else None, out.data_ptr(), _stream(dev))
+    return out, (final_state if output_final_state else None)
