@@ -429,6 +429,37 @@ def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps
     }
 
 
+def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
+    """cfg3: chunked prefill of B=8 sequences x T=2048 tokens, 16 heads, dk=dv=128, zero initial state, bf16 out and
+    fp32 final state. Inputs (201 MB of q/k/v) exceed L2, so no flush is needed between replays."""
+    B, T, H, d = 8, 2048, 16, 128
+    gen = torch.Generator().manual_seed(3)
+    N = B * T
+    q = F.normalize(torch.randn(N, H, d, generator=gen), dim=-1).bfloat16().to(dev)
+    k = F.normalize(torch.randn(N, H, d, generator=gen), dim=-1).bfloat16().to(dev)
+    v = torch.randn(N, H, d, generator=gen).bfloat16().to(dev)
+    beta = torch.sigmoid(torch.randn(N, H, generator=gen)).to(dev)
+    g = (-F.softplus(torch.randn(N, H, generator=gen))).to(dev)
+    cu = torch.arange(0, N + 1, T, dtype=torch.int32, device=dev)
+    out = torch.empty(N, H, d, device=dev, dtype=torch.bfloat16)
+    final = torch.empty(B, H, d, d, device=dev, dtype=torch.float32)
+    ms = graph_ms(lambda: ops.gdn_chunk_prefill(q, k, v, g, beta, cu, final_state=final, out=out), stream, reps)
+    nbytes = N * H * (3 * d * 2 + 2 * 4 + d * 2) + B * H * d * d * 4
+    chunk_heads = B * H * (T // 64)
+    flops = chunk_heads * 2 * (64 * 64 * (3 * d + 2 * d) + 3 * 64 * d * d + 64 ** 3 // 3)
+    pk = peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {
+        "workload": "cfg3 GDN chunked prefill: B=8 x T=2048, 16 heads, dk=dv=128, chunk 64, zero initial state",
+        "ms": ms, "tokens_per_s": N / (ms / 1e3),
+        "roofline": {"kernel": "gdn_chunk_prefill_kernel<128>", "bound": "hbm", "achieved": gbs,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "algorithmic_bytes": nbytes,
+                     "peak_source": pk["source"]},
+        "tensor": {"algorithmic_flops": flops, "tflops": flops / (ms / 1e3) / 1e12,
+                   "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / pk["bf16_tflops"]},
+    }
+
+
 def profiled_traffic(summary: str):
     """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in the
     committed summary under profiles/, or None."""
@@ -476,6 +507,21 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg4 MoE layers done, status {ops.device_status()}")
         return
+    if workload == "prefill":
+        B, T, H, d = 8, 2048, 16, 128
+        N = B * T
+        gen = torch.Generator().manual_seed(3)
+        q = F.normalize(torch.randn(N, H, d, generator=gen), dim=-1).bfloat16().to(dev)
+        k = F.normalize(torch.randn(N, H, d, generator=gen), dim=-1).bfloat16().to(dev)
+        v = torch.randn(N, H, d, generator=gen).bfloat16().to(dev)
+        beta = torch.sigmoid(torch.randn(N, H, generator=gen)).to(dev)
+        g = (-F.softplus(torch.randn(N, H, generator=gen))).to(dev)
+        cu = torch.arange(0, N + 1, T, dtype=torch.int32, device=dev)
+        for _ in range(n):
+            ops.gdn_chunk_prefill(q, k, v, g, beta, cu)
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg3 chunked prefills done")
+        return
     if workload == "attnres":
         gen = torch.Generator().manual_seed(7)
         bank = torch.randn(49, 256, 2048, generator=gen).bfloat16().to(dev)
@@ -507,7 +553,7 @@ def main():
     ap.add_argument("--cpu-updates", type=int, default=256, help="updates in the CPU-baseline sample")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
-    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres"),
+    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
@@ -554,6 +600,7 @@ def main():
                 line["operators"] = {
                     "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
                     "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
+                    "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
                 }
             print(json.dumps(line), flush=True)
     finally:

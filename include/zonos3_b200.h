@@ -62,6 +62,28 @@ int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          const float* init_state, const int64_t* state_slots, float* final_state, uint16_t* out,
                          cudaStream_t stream);
 
+/* GDN prologue: from the in_proj output rows mixed [N, 4*H*D + 2*H] (qkv | z | a | b, row stride mixed_stride):
+ * depthwise causal conv (kernel 4, conv_weight [3*H*D, 1, 4] bf16) + SiLU over the qkv channels continuing each
+ * sequence's history, per-head L2 norm (eps 1e-6) of q and k, g = -exp(A_log) * softplus(a + dt_bias), beta =
+ * sigmoid(b). Sequences: cu_seqlens [num_seqs + 1] int32, seq_of_token [N] int32, slots [num_seqs] int64 (row of
+ * conv_state [conv_rows, 3*H*D, 3] bf16, read as history and replaced by the sequence's last 3 inputs; a slot
+ * outside [0, conv_rows) is a padding sequence: zero history, nothing written), fresh [num_seqs] uint8 or NULL
+ * (1 = zero history). Outputs q, k, v [N, H, D] bf16, g, beta [N, H] fp32.
+ * Replaces FLA causal_conv1d_fwd / l2norm_fwd / fused_beta_sigmoid_fwd and the gate of
+ * chunk_gated_delta_rule_fwd in OriginalGDN._run_packed (servers/sgl/src/zonos3_sgl/models/gdn.py:403-434);
+ * math of model/src/zonos3/reference/lm.py:561-573. D a multiple of 32, at most 128. */
+int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const uint16_t* conv_weight, const float* A_log,
+                    const float* dt_bias, const int32_t* cu_seqlens, const int32_t* seq_of_token, const int64_t* slots,
+                    const uint8_t* fresh, uint16_t* conv_state, int64_t conv_rows, int num_seqs, int N, int H, int D,
+                    uint16_t* q,
+                    uint16_t* k, uint16_t* v, float* g, float* beta, cudaStream_t stream);
+
+/* GDN epilogue: out[N, H*D] = bf16(RMSNorm(o; weight [D], eps) * SiLU(z)) per (token, head), o [N, H, D] bf16,
+ * z [N, H*D] bf16 with row stride z_stride. Replaces FLA layer_norm_gated_fwd (swish gate, RMS) in
+ * OriginalGDN._run_packed (servers/sgl/src/zonos3_sgl/models/gdn.py:435-445); lm.py:585-587. */
+int zb_gdn_gated_norm(const uint16_t* o, const uint16_t* z, int64_t z_stride, const uint16_t* weight, float eps, int N,
+                      int H, int D, uint16_t* out, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------------------------- Full AttnRes */
 
 /* Full AttnRes route of every token over bank sources [0, S) plus, if `source` is non-NULL, `source` as the last
@@ -127,7 +149,7 @@ int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const uint16_t*
 /* GEMM2 of the routed experts on tcgen05 tensor cores with the routing weight fused:
  * y[p, :] = bf16((h[r] . down[e]^T) * weights[p]) for every row r with pair p = sorted_pairs[r] >= 0.
  * Replaces the second fused_moe_kernel call (MUL_ROUTED_WEIGHT) of fused_experts_impl (fused_moe_impl.py:236-259).
- *   h [capacity, I] bf16; down [E, D, I] bf16; weights [T*k] fp32; y [T*k, D] bf16.  I % 64 == 0, D % 256 == 0. */
+ *   h [capacity, I] bf16; down [E, D, I] bf16; weights [T*k] fp32; y [T*k, D] bf16.  I % 64 == 0, D % 128 == 0. */
 int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
                      const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
                      cudaStream_t stream);

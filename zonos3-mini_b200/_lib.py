@@ -30,6 +30,12 @@ SIGNATURES: dict[str, list] = {
                            _i32, _i32, _i32, _i32, _f32, _p],
     # q, k, v, g, beta, cu_seqlens, num_seqs, H, dk, dv, scale, init_state, state_slots, final_state, out, stream
     "zb_gdn_chunk_prefill": [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p, _p],
+    # mixed, mixed_stride, conv_weight, A_log, dt_bias, cu_seqlens, seq_of_token, slots, fresh, conv_state,
+    # conv_rows, num_seqs, N, H, D, q, k, v, g, beta, stream
+    "zb_gdn_prologue": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p,
+                        _p],
+    # o, z, z_stride, weight, eps, N, H, D, out, stream
+    "zb_gdn_gated_norm": [_p, _p, _i64, _p, _f32, _i32, _i32, _i32, _p, _p],
     # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream
     "zb_attnres_route": [_p, _i64, _i32, _p, _p, _p, _f32, _p, _f32, _p, _p, _i32, _i32, _p],
     # x, x_stride, norm_weight, eps, w_router, bias, T, D, E, k, weight_mode, renormalize, logits, ids, weights, stream

@@ -49,6 +49,7 @@ struct GemmParams {
   int b_tile_step;         // B row advance per n-tile (128 for GEMM1, 256 for GEMM2)
   __nv_bfloat16* out;      // GEMM1: H [rows, I]; GEMM2: Y [pairs, D]
   int64_t out_stride;
+  int out_cols;            // valid output columns (GEMM2: D, a multiple of 128; the last tile may be half)
   const int32_t* sorted_pairs;  // GEMM2
   const float* weights;         // GEMM2: [pairs]
   unsigned* status;
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float w = pair >= 0 ? p.weights[pair] : 0.f;
         __nv_bfloat16* dst = p.out + (int64_t)(pair >= 0 ? pair : 0) * p.out_stride + (int64_t)n * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < BN && n * BN + c < p.out_cols; c += 32) {
           float y[32];
           tmem_ld32(t_row + c, y);
           if (pair >= 0) {
@@ -397,7 +398,7 @@ ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const ui
   CUtensorMap ma, mb;
   if (int rc = make_map(&ma, x_perm, capacity, D, D)) return rc;
   if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
-  GemmParams p{offsets, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, nullptr,
+  GemmParams p{offsets, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I, nullptr,
                nullptr, zb::device_status_ptr()};
   return launch<kSwiGLU>(ma, mb, p, capacity, stream);
 }
@@ -407,14 +408,14 @@ ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t*
                             cudaStream_t stream) {
   if (int rc = check_common(h, offsets, E, capacity)) return rc;
   ZB_REQUIRE(down && sorted_pairs && weights && y, "moe_gemm_down: null pointer");
-  if (I % BK != 0 || D % BN != 0)
-    return zb::fail(zb::kUnsupported, "moe_gemm_down: I=%d must be a multiple of 64 and D=%d of 256", I, D);
+  if (I % BK != 0 || D % 128 != 0)
+    return zb::fail(zb::kUnsupported, "moe_gemm_down: I=%d must be a multiple of 64 and D=%d of 128", I, D);
   ZB_REQUIRE_ALIGNED(down, 16, "down");
   ZB_REQUIRE_ALIGNED(y, 16, "y");
   CUtensorMap ma, mb;
   if (int rc = make_map(&ma, h, capacity, I, I)) return rc;
   if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
-  GemmParams p{offsets, E, I, D / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D, sorted_pairs,
-               weights, zb::device_status_ptr()};
+  GemmParams p{offsets, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D, D,
+               sorted_pairs, weights, zb::device_status_ptr()};
   return launch<kDown>(ma, mb, p, capacity, stream);
 }

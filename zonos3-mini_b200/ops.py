@@ -421,3 +421,60 @@ def gdn_chunk_prefill(q, k, v, g, beta, cu_seqlens, *, initial_state=None, outpu
               cu_seqlens.data_ptr(), n, H, dk, dv, float(scale), ptr(initial_state), ptr(state_slots),
               ptr(final_state) if output_final_state else None, out.data_ptr(), _stream(dev))
     return out, (final_state if output_final_state else None)
+
+
+def gdn_prologue(mixed, conv_weight, A_log, dt_bias, cu_seqlens, seq_of_token, slots, conv_state, *, heads,
+                 head_dim, fresh=None, q=None, k=None, v=None, g=None, beta=None):
+    """Causal conv + SiLU over the qkv channels, per-head L2 norm of q and k, log decay g and beta from the in_proj
+    output rows [qkv | z | a | b] (lm.py:561-573; gdn.py:403-423). conv_state [rows, 3*inner, W-1] (bf16) is read
+    as each sequence's history and replaced by its last W-1 inputs; ``fresh`` [n] uint8 starts a sequence from a
+    zero history. Returns (q, k, v [N, H, d] bf16, g, beta [N, H] fp32)."""
+    _check_cuda("mixed", mixed, torch.bfloat16)
+    dev = mixed.device
+    N = mixed.shape[0]
+    H, D = heads, head_dim
+    inner = H * D
+    _require(mixed.dim() == 2 and mixed.shape[1] >= 4 * inner + 2 * H and mixed.stride(1) == 1,
+             "mixed must be [N, 4*inner + 2*H] with contiguous rows")
+    _check_cuda("conv_weight", conv_weight, torch.bfloat16, dev)
+    _require(conv_weight.numel() == 3 * inner * 4 and conv_weight.is_contiguous(), "conv_weight must be [3*inner, 1, 4]")
+    _check_cuda("conv_state", conv_state, torch.bfloat16, dev)
+    _require(conv_state.dim() == 3 and conv_state.shape[1:] == (3 * inner, 3) and conv_state.is_contiguous(),
+             "conv_state must be a contiguous [rows, 3*inner, 3] tensor")
+    for name, t in (("A_log", A_log), ("dt_bias", dt_bias)):
+        _check_cuda(name, t, torch.float32, dev)
+    n = cu_seqlens.numel() - 1
+    _check_cuda("cu_seqlens", cu_seqlens, torch.int32, dev)
+    _check_cuda("seq_of_token", seq_of_token, torch.int32, dev)
+    _check_cuda("slots", slots, torch.int64, dev)
+    if fresh is not None:
+        _check_cuda("fresh", fresh, torch.uint8, dev)
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    q = torch.empty(N, H, D, **bf) if q is None else q
+    k = torch.empty(N, H, D, **bf) if k is None else k
+    v = torch.empty(N, H, D, **bf) if v is None else v
+    g = torch.empty(N, H, device=dev, dtype=torch.float32) if g is None else g
+    beta = torch.empty(N, H, device=dev, dtype=torch.float32) if beta is None else beta
+    _lib.call("zb_gdn_prologue", mixed.data_ptr(), mixed.stride(0), conv_weight.data_ptr(), A_log.data_ptr(),
+              dt_bias.data_ptr(), cu_seqlens.data_ptr(), seq_of_token.data_ptr(), slots.data_ptr(),
+              None if fresh is None else fresh.data_ptr(), conv_state.data_ptr(), conv_state.shape[0], n, N, H, D,
+              q.data_ptr(),
+              k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _stream(dev))
+    return q, k, v, g, beta
+
+
+def gdn_gated_norm(o, z, weight, eps=1e-5, out=None):
+    """Per-head RMSNorm(o; weight, eps) * SiLU(z), rounded once to bf16 (gdn.py:435-445; lm.py:585-587).
+    o [N, H, d] bf16; z [N, H*d] bf16 view (row stride allowed); returns [N, H*d] bf16."""
+    _check_cuda("o", o, torch.bfloat16)
+    dev = o.device
+    N, H, D = o.shape
+    _require(o.is_contiguous(), "o must be contiguous")
+    _check_cuda("z", z, torch.bfloat16, dev)
+    _require(z.shape == (N, H * D) and z.stride(1) == 1, "z must be [N, H*d] with contiguous rows")
+    _check_cuda("weight", weight, torch.bfloat16, dev)
+    if out is None:
+        out = torch.empty(N, H * D, device=dev, dtype=torch.bfloat16)
+    _lib.call("zb_gdn_gated_norm", o.data_ptr(), z.data_ptr(), z.stride(0) if N > 1 else H * D, weight.data_ptr(),
+              float(eps), N, H, D, out.data_ptr(), _stream(dev))
+    return out
