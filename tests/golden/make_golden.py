@@ -15,6 +15,11 @@ reference at run time. What each file pins:
   ``torch.topk`` indices the reference computed, and the layer output.
 * ``moe_ties.npz``   — the same layer cast to bf16 with zero balancing biases, where bf16 logits tie often:
   the reference's ``torch.topk`` indices, to measure where its tie order is arbitrary.
+* ``lm_tiny.npz``    — ``Zonos3LM.forward`` (lm.py:660-735) of a whole 2-layer model (GDN layer + global attention
+  layer, dense FFN then MoE, Full AttnRes, dim 32): every weight, a 12-row prompt and two 1-row decode calls, and
+  the softcapped logits of all three calls.
+
+``python tests/golden/make_golden.py /path/to/reference [fixture ...]`` regenerates only the named fixtures.
 """
 
 from __future__ import annotations
@@ -170,17 +175,33 @@ def moe_fixture(lm):
     np.savez_compressed(HERE / "moe_ties.npz", scores=scores.numpy(), topk=indices.numpy())
 
 
-def main(reference: str) -> None:
+def lm_fixture(lm):
+    model = build_model(lm, seed=41, dim=32)
+    gen = torch.Generator().manual_seed(42)
+    rows = 14
+    ids = torch.full((rows, CONFIG["n_codebooks"] + 1), CONFIG["codebook_size"] + 1, dtype=torch.long)
+    ids[:, -1] = torch.randint(4, CONFIG["text_vocab"], (rows,), generator=gen)
+    ids[8:, :-1] = torch.randint(0, CONFIG["codebook_size"], (rows - 8, CONFIG["n_codebooks"]), generator=gen)
+    cache = lm.LMCache()
+    logits = [model(ids[:12], cache).logits, model(ids[12:13], cache).logits, model(ids[13:14], cache).logits]
+    out = {"ids": ids.numpy(), "logits": torch.cat(logits).numpy()}
+    out.update({"w." + k: v.detach().float().numpy().copy() for k, v in model.state_dict().items()})
+    np.savez_compressed(HERE / "lm_tiny.npz", **out)
+
+
+FIXTURES = {"gdn": "gdn_fixture", "attnres": "attnres_fixture", "moe": "moe_fixture", "lm": "lm_fixture"}
+
+
+def main(reference: str, which: list[str]) -> None:
     sys.path.insert(0, str(Path(reference) / "model" / "src"))
     import zonos3.reference.lm as lm
 
     torch.set_num_threads(1)
-    gdn_fixture(lm)
-    attnres_fixture(lm)
-    moe_fixture(lm)
+    for name in which or list(FIXTURES):
+        globals()[FIXTURES[name]](lm)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])

@@ -106,3 +106,23 @@ def test_permutation_contract():
     assert p["offsets"].tolist() == [0, 0, 4, 8, 12]
     assert p["sorted_pairs"].tolist() == [2, 4, 6, -1, 0, 3, 7, -1, 1, 5, -1, -1]
     assert np.array_equal(p["sorted_pairs"][p["position"]], np.arange(8))
+
+
+def test_whole_lm_matches_reference(golden):
+    """The restated LM (oracle/lm.py) reproduces the reference Zonos3LM's logits for a prompt and two decode calls
+    (a GDN layer, a global attention layer, dense FFN then MoE, Full AttnRes)."""
+    from oracle import lm as olm
+
+    g = golden("lm_tiny.npz")
+    w = {k[2:]: v for k, v in g.items() if k.startswith("w.")}
+    c = olm.LMConfig(dim=32, n_layers=2, gdn_period=2, gdn_heads=4, gdn_head_dim=128, n_heads=4, n_kv_heads=2,
+                     head_dim=16, n_experts=4, topk=2, moe_hidden=32, moe_routed_dim=16, latent=True,
+                     dense_first_layer=True, ffn_hidden=64, n_codebooks=10, codebook_size=16, text_rows=21)
+    assert set(olm.weight_shapes(c)) <= set(w)
+    for name, shape in olm.weight_shapes(c).items():
+        assert tuple(w[name].shape) == shape, name
+    ids = g["ids"].long()
+    cache = olm.Cache()
+    logits = torch.cat([olm.forward(c, w, ids[:12], cache), olm.forward(c, w, ids[12:13], cache),
+                        olm.forward(c, w, ids[13:14], cache)])
+    torch.testing.assert_close(logits, g["logits"], rtol=1e-4, atol=1e-5)

@@ -105,3 +105,25 @@ def fused_full_attnres(state: FusedBlockAttnResContext, source: torch.Tensor, qu
                        norm_eps: float, append_current: bool) -> torch.Tensor:
     """Route ``source`` with every completed bank row (training_attnres_kernels.py:2826)."""
     return state.route(source, query, float(norm_eps), bool(append_current))
+
+
+def forward_layers_full(layers, x: torch.Tensor, queries: torch.Tensor, eps: float, state: FusedBlockAttnResContext,
+                        out_norm_weight: torch.Tensor, router_states=None) -> torch.Tensor:
+    """The Full AttnRes layer schedule (servers/sgl/src/zonos3_sgl/models/training_attnres.py:59-78; lm.py:699-721):
+    before each sublayer one route over the bank with the sublayer's RMSNorm fused (attention_norm, ffn_norm), the
+    sublayer's input appended to the bank by the same kernel; a final route with out_norm. ``layers`` expose
+    ``attention_norm.weight``, ``ffn_norm.weight``, ``attention.forward(x)`` and ``feed_forward.forward(x,
+    router_states) -> (out, router_states)`` (MoE) or ``feed_forward.forward(x)`` (dense, ``is_moe`` False).
+    Returns the normalised final mix [T, D]."""
+    state.reset()
+    source = x
+    for i, layer in enumerate(layers):
+        h = state.route(source, queries[2 * i], eps, True, norm_weight=layer.attention_norm.weight)
+        attention_out = layer.attention.forward(h)
+        h = state.route(attention_out, queries[2 * i + 1], eps, True, norm_weight=layer.ffn_norm.weight)
+        if getattr(layer, "is_moe", True):
+            source, router_states = layer.feed_forward.forward(h, router_states)
+        else:
+            source = layer.feed_forward.forward(h)
+            router_states = None
+    return state.route(source, queries[-1], eps, False, norm_weight=out_norm_weight)
