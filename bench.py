@@ -395,34 +395,41 @@ def bench_moe_cfg4(ops, dev, stream, steps=10, warmup=3):
 
 def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps=3):
     """cfg5's AttnRes schedule for one decode step: 2L+1 routes over a growing bank (S = 1 .. 2L+1 sources) of
-    `tokens` rows, each with the following RMSNorm fused. The L2 is flushed before every route (as the layers
-    between routes would); route time = graph[flush, route] x (2L+1) minus graph[flush] x (2L+1)."""
+    `tokens` rows, each with the following RMSNorm fused and the bank rows' inverse RMS cached as
+    FusedBlockAttnResContext caches them (route r computes row r's and reads rows < r from the cache). The L2 is
+    flushed before every route (as the layers between routes would); route time = graph[flush, route] x (2L+1)
+    minus graph[flush] x (2L+1)."""
     gen = torch.Generator().manual_seed(7)
     n_src = 2 * layers + 1
     bank = torch.randn(n_src, tokens, dim, generator=gen).bfloat16().to(dev)
     queries = (0.02 * torch.randn(n_src, dim, generator=gen)).bfloat16().to(dev)
     norm_w = torch.ones(dim, dtype=torch.bfloat16, device=dev)
     out = torch.empty(tokens, dim, device=dev, dtype=torch.bfloat16)
+    rms_cache = torch.zeros(n_src, tokens, device=dev, dtype=torch.float32)
     flush = L2Flush(dev)
 
     def schedule(with_routes):
         for r in range(n_src):
             flush_l2(flush)
             if with_routes:
-                ops.attnres_route(bank, r + 1, queries[r], 1e-5, norm_weight=norm_w, out=out)
+                ops.attnres_route(bank, r + 1, queries[r], 1e-5, norm_weight=norm_w, out=out, rms_cache=rms_cache,
+                                  cached=r)
 
     total_ms = graph_ms(lambda: schedule(True), stream, reps) - graph_ms(lambda: schedule(False), stream, reps)
-    big_ms = flushed_ms(lambda: ops.attnres_route(bank, n_src, queries[-1], 1e-5, norm_weight=norm_w, out=out),
-                        flush, stream, reps=10)
-    total_bytes = sum(((r + 1) * tokens * dim + tokens * dim + 2 * dim) * 2 for r in range(n_src))
+    big_ms = flushed_ms(lambda: ops.attnres_route(bank, n_src, queries[-1], 1e-5, norm_weight=norm_w, out=out,
+                                                  rms_cache=rms_cache, cached=n_src - 1), flush, stream, reps=10)
+    # algorithmic bytes of route r: r + 1 bank rows read, the output row written, query + norm weight, and the
+    # cache (r rows read, one written)
+    total_bytes = sum(((r + 1) * tokens * dim + tokens * dim + 2 * dim) * 2 + (r + 1) * tokens * 4
+                      for r in range(n_src))
     pk = peaks()
     gbs = total_bytes / (total_ms / 1e3) / 1e9
-    big_bytes = (n_src * tokens * dim + tokens * dim + 2 * dim) * 2
+    big_bytes = (n_src * tokens * dim + tokens * dim + 2 * dim) * 2 + n_src * tokens * 4
     return {
         "workload": f"cfg5 AttnRes decode schedule: {n_src} routes over a growing bank, {tokens} tokens x {dim}, "
                     "fused RMSNorm, L2 flushed before each route",
         "ms_per_step": total_ms, "bytes_per_step": total_bytes,
-        "roofline": {"kernel": "attnres_route (logits + mix kernels)", "bound": "hbm", "achieved": gbs,
+        "roofline": {"kernel": "attnres_route_kernel", "bound": "hbm", "achieved": gbs,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"]},
         "largest_route": {"sources": n_src, "us": big_ms * 1e3, "gbs": big_bytes / (big_ms / 1e3) / 1e9,
                           "frac": big_bytes / (big_ms / 1e3) / 1e9 / pk["hbm_gbs"]},
@@ -527,10 +534,12 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
         bank = torch.randn(49, 256, 2048, generator=gen).bfloat16().to(dev)
         query = (0.02 * torch.randn(2048, generator=gen)).bfloat16().to(dev)
         norm_w = torch.ones(2048, dtype=torch.bfloat16, device=dev)
+        rms_cache = torch.zeros(49, 256, device=dev, dtype=torch.float32)
+        ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w, rms_cache=rms_cache, cached=0)
         flush = L2Flush(dev)
         for _ in range(n):
             flush_l2(flush)
-            ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w)
+            ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w, rms_cache=rms_cache, cached=48)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} AttnRes routes (49 sources x 256 tokens x 2048) done")
         return

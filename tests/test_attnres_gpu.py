@@ -91,3 +91,51 @@ def test_bank_with_padding_stride(zb):
     out = zb.ops.attnres_route(view, S, query.cuda(), EPS)
     torch.cuda.synchronize()
     assert rel_err(out.float(), ref.float()) < TOL
+
+
+def test_rms_cache_reads_and_fills(zb):
+    """Rows below ``cached`` take their inverse RMS from the cache, later rows compute and store it: a cached route is
+    bit-identical to an uncached one, and the cache holds 1 / rms(row) per token."""
+    S, T, D = 10, 24, 2048
+    bank, query = make_bank(S, T, D, seed=91)
+    d_bank, d_query = bank.cuda(), query.cuda()
+    cache = torch.full((S + 1, T), float("nan"), device="cuda")
+    first = zb.ops.attnres_route(d_bank, 4, d_query, EPS, rms_cache=cache, cached=0)
+    ref_first = zb.ops.attnres_route(d_bank, 4, d_query, EPS)
+    full = zb.ops.attnres_route(d_bank, S, d_query, EPS, rms_cache=cache, cached=4)
+    ref_full = zb.ops.attnres_route(d_bank, S, d_query, EPS)
+    torch.cuda.synchronize()
+    assert torch.equal(first, ref_first) and torch.equal(full, ref_full)
+    inv = torch.rsqrt(bank.float().pow(2).mean(-1) + EPS)
+    assert torch.isnan(cache[S]).all()
+    assert torch.allclose(cache[:S].cpu(), inv, rtol=1e-5)
+    # a stale cache entry below ``cached`` is used as given: the route trusts the caller's bookkeeping
+    cache[0].fill_(0.0)
+    skewed = zb.ops.attnres_route(d_bank, S, d_query, EPS, rms_cache=cache, cached=1)
+    torch.cuda.synchronize()
+    assert not torch.equal(skewed, ref_full)
+
+
+def test_context_schedule_with_cache(zb):
+    """FusedBlockAttnResContext over a Full AttnRes schedule (routes with appends, the bank growing one row per
+    route, the cache reused) against the oracle on the same sources."""
+    T, D, routes = 16, 1024, 9
+    gen = torch.Generator().manual_seed(5)
+    sources = [(torch.randn(T, D, generator=gen) * (0.5 + i % 3)).bfloat16() for i in range(routes)]
+    queries = (0.2 * torch.randn(routes, D, generator=gen)).bfloat16()
+    norm_w = (1 + 0.1 * torch.randn(D, generator=gen)).bfloat16()
+    ctx = zb.attnres.FusedBlockAttnResContext(routes, sources[0].cuda())
+    for trial in range(2):  # the second forward reuses the bank and the cache after reset()
+        ctx.reset()
+        for i in range(routes):
+            src = sources[i].cuda()
+            if i % 2:  # the producer writes straight into the next bank row
+                ctx.next_row().copy_(src)
+                src = ctx.next_row()
+            out = ctx.route(src, queries[i].cuda(), EPS, True, norm_weight=norm_w.cuda())
+            ref = oattn.weighted_rms_norm(oattn.full_attnres_route(torch.stack(sources[: i + 1]), queries[i], EPS),
+                                          norm_w, EPS)
+            torch.cuda.synchronize()
+            assert rel_err(out.float().cpu(), ref.float()) < TOL, (trial, i)
+            assert identical_fraction(out, ref) > 0.99, (trial, i)
+    assert zb.ops.device_status() == 0

@@ -47,12 +47,18 @@ class FusedBlockAttnResContext:
         self.gradient_dtype = gradient_dtype
         self.blocks = torch.empty((self.max_completed_blocks, self.bt, self.dim), device=reference.device,
                                   dtype=reference.dtype)
+        # key inverse RMS of every bank row (and of the routed source), filled by the route kernel: each row's sum
+        # of squares is read from HBM once per forward instead of once per later route
+        self.rms_cache = torch.empty((self.max_completed_blocks + 1, self.bt), device=reference.device,
+                                     dtype=torch.float32)
+        self._rms_eps = None
         self.completed_count = 0
         self.call_count = 0
 
     def reset(self) -> None:
         self.completed_count = 0
         self.call_count = 0
+        self._rms_eps = None
 
     def validate_owner(self, partial: torch.Tensor) -> None:
         if tuple(partial.shape[:-1]) != self.token_shape or partial.shape[-1] != self.dim:
@@ -87,14 +93,17 @@ class FusedBlockAttnResContext:
         in_place = completed < self.max_completed_blocks and src.data_ptr() == self.blocks[completed].data_ptr()
         if out is not None:
             out = out.reshape(self.bt, self.dim)
+        cached = completed if self._rms_eps == norm_eps else 0  # cached rows hold 1 / rms at this eps
+        self._rms_eps = norm_eps
         if in_place:
             result = ops.attnres_route(self.blocks, completed + 1, query, norm_eps, norm_weight=norm_weight,
-                                       norm_eps=norm_eps, out=out, mix_out=mix_out)
+                                       norm_eps=norm_eps, out=out, mix_out=mix_out, rms_cache=self.rms_cache,
+                                       cached=cached)
         else:
             result = ops.attnres_route(
                 self.blocks if completed else None, completed, query, norm_eps, source=src.contiguous(),
                 append_to=self.blocks[completed] if append_current else None, norm_weight=norm_weight,
-                norm_eps=norm_eps, out=out, mix_out=mix_out)
+                norm_eps=norm_eps, out=out, mix_out=mix_out, rms_cache=self.rms_cache, cached=cached)
         if append_current:
             self.completed_count += 1
         self.call_count += 1

@@ -5,14 +5,19 @@
 // zonos3.py:99-113) and the fused Triton route _block_attnres_fwd_kernel (servers/sgl/src/zonos3_sgl/models/
 // training_attnres_kernels.py:1268-1348), whose rounding points this kernel keeps: key = bf16(v * inv_rms),
 // product = bf16(key * q), logit = fp32 sum, fp32 softmax, weight = bf16, term = bf16(v * weight), fp32 sum of
-// terms, bf16 output. The Triton kernel runs one warp per token over the bank twice; here the logit pass is spread
-// over one warp per (source, token) row and the mix pass re-reads the rows the logit pass streamed just before,
-// so they come from L2 and HBM delivers each source row once.
+// terms, bf16 output. The Triton kernel runs one warp per token and reads the bank twice; here each token's sources
+// are staged on chip once and every sweep reads shared memory.
+#include <cooperative_groups.h>
+
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
 constexpr int kMaxSources = 256;
+constexpr size_t kRouteSmemBudget = 200 * 1024;
 constexpr int kThreads = 256;  // 8 warps per token
 
 struct RouteParams {
@@ -27,191 +32,354 @@ struct RouteParams {
   float norm_eps;
   __nv_bfloat16* out;      // [T, D]: normalised mix if norm_weight, else the mix
   __nv_bfloat16* mix_out;  // optional [T, D]: the un-normalised mix (when norm_weight is given)
+  float* rms_cache;        // optional [rows, rms_stride]: inverse RMS of bank row s for token t at s * stride + t
+  int64_t rms_stride;
+  int cached;              // bank rows [0, cached) have valid cache entries; later rows compute and store theirs
   int T, D;
   unsigned* status;
 };
 
-// Two kernels per route.
-//  attnres_logits_kernel: one warp per (source, token) row — every row of every token is an independent unit of
-//  work, so the whole bank streams from HBM with full parallelism. A lane holds VPL 16-byte vectors of the row
-//  (D = 256 * VPL, all loads in flight at once); the row's sum of squares and then its logit are warp-shuffle
-//  reductions with the reference rounding points. Logits of token t are parked in the first 4*ns bytes of its own
-//  output row (ns <= D/2), so the route needs no scratch memory.
-//  attnres_mix_kernel: one CTA per token: softmax over its logits (fp32, bf16 weights), then thread i sums the
-//  weighted terms of 16-byte column vectors i, i + 256, ... over all sources, 16 sources' loads in flight. Those
-//  rows were streamed by the logits kernel just before and are served by L2, so HBM delivers each row once.
-constexpr int kLogitWarps = 4;
-constexpr int kLogitRows = 2;  // rows per warp, all loads in flight together
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(float x, float y) {
+  __nv_bfloat162 r = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
 
-template <int VPL>
-__global__ void __launch_bounds__(32 * kLogitWarps) attnres_logits_kernel(RouteParams p) {
-  const int lane = threadIdx.x % 32;
-  const int ns = p.S + (p.source ? 1 : 0);
-  const int64_t total = (int64_t)ns * p.T;
-  const int64_t row0 = ((int64_t)blockIdx.x * kLogitWarps + threadIdx.x / 32) * kLogitRows;  // rows s * T + t
-  const int D = p.D;
-  // every load of the warp is issued before any is used: its rows, then its query columns
-  uint4 v4[kLogitRows][VPL];
-#pragma unroll
-  for (int r = 0; r < kLogitRows; ++r) {
-    const int64_t row = row0 + r < total ? row0 + r : total - 1;
-    const int s = (int)(row / p.T);
-    const int64_t t = row % p.T;
-    const __nv_bfloat16* src = (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * D;
-#pragma unroll
-    for (int u = 0; u < VPL; ++u) v4[r][u] = __ldcs(reinterpret_cast<const uint4*>(src + u * 256 + lane * 8));
+// Packed fp32 pairs (one 64-bit register pair; sm_100 executes add / mul / fma on both halves at once).
+__device__ __forceinline__ uint64_t bf2_to_x2(uint32_t w) {  // bf16x2 word -> (lo, hi) fp32 pair
+  return ((uint64_t)(w & 0xffff0000u) << 32) | (uint64_t)(w << 16);
+}
+__device__ __forceinline__ uint64_t add_x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma_x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t splat_x2(float x) {
+  const uint64_t u = __float_as_uint(x);
+  return (u << 32) | u;
+}
+__device__ __forceinline__ float sum_x2(uint64_t v) {
+  return __uint_as_float((uint32_t)v) + __uint_as_float((uint32_t)(v >> 32));
+}
+__device__ __forceinline__ uint32_t x2_to_bf2(uint64_t v) {  // round both halves to bf16 (lo in the low half)
+  return f2_to_bf2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
+}
+
+// One route, one pass over HBM. A token is a cluster of CL CTAs; CTA r owns columns [r*C, (r+1)*C) of every source
+// and stages that slice of all ns sources in shared memory (one cp.async.bulk per source, each with its own
+// mbarrier, all issued at once; the sources without a cached inverse RMS first). The 8 warps then take work units
+// round-robin, each as soon as its source has landed:
+//   sum-of-squares units (sources without a cached inverse RMS): partial sum of squares of the slice;
+//   logit units (every source): inverse RMS (cached, or from the exchanged sums of squares), then the partial logit
+//   sum of bf16(bf16(v * inv_rms) * q) — one cvt rounds two keys, one bf16x2 multiply gives two rounded products.
+// Every warp then forms the logits, the fp32 softmax and the bf16 weights itself, and mixes 4 (or 2) columns per
+// thread: sum over sources of bf16(v * w) in fp32, from shared memory; the optional RMSNorm of the mix and the
+// append of the current source follow.
+// Partial sums cross the cluster by push: st.async stores into every peer's shared memory that complete bytes on
+// the peer's exchange mbarrier, summed in rank order so that every CTA of a token computes identical values. No
+// cluster-wide barrier follows the start (whose relaxed arrive only publishes the mbarrier initialisation), so no
+// CTA waits on a memory fence or on its peers' progress beyond the data it needs.
+constexpr int kRouteThreads = 256;
+constexpr int kRouteWarps = kRouteThreads / 32;
+
+// Shared-memory layout of one CTA: ns source slices of C columns, ns + 4 mbarriers, the exchange buffers.
+struct RouteLayout {
+  size_t bars, xss, xlg, xnrm, inv_rms, wp, red, total;
+  __host__ __device__ RouteLayout(int ns, int C, int CL) {
+    bars = (size_t)ns * C * 2;               // [ns] source copies + [4] exchanges
+    xss = bars + (size_t)(ns + 4) * 8;       // [CL][ns] fp32 partial sums of squares
+    xlg = xss + (size_t)CL * ns * 4;         // [CL][ns] fp32 partial logits
+    xnrm = xlg + (size_t)CL * ns * 4;        // [8] fp32 partial sums of squares of the mix
+    inv_rms = xnrm + 8 * 4;                  // [ns] fp32 cached inverse RMS
+    wp = inv_rms + (size_t)ns * 4;           // [kRouteWarps][ns] bf16x2 weights (each warp its own row)
+    red = wp + (size_t)kRouteWarps * ns * 4; // [kRouteWarps]
+    total = red + kRouteWarps * 4;
   }
-  uint4 q4[VPL];
-#pragma unroll
-  for (int u = 0; u < VPL; ++u) q4[u] = *reinterpret_cast<const uint4*>(p.query + u * 256 + lane * 8);
-#pragma unroll
-  for (int r = 0; r < kLogitRows; ++r) {
-    float ss = 0.f;
-#pragma unroll
-    for (int u = 0; u < VPL; ++u) {
-      float v[8];
-      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v4[r][u]), v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+};
+
+// Writes `v` into slot `idx` of this CTA's exchange buffer `buf` and of every peer's (the CTA's own rank row),
+// completing 4 bytes on each peer's mbarrier `bar` and arriving on the local one. Called by a whole warp.
+__device__ __forceinline__ void publish(float v, float* buf, uint64_t* bar, int CL, int rank, int lane) {
+  if (lane < CL) {
+    if (lane == rank) {
+      *buf = v;
+      zb::mbar_arrive(zb::smem_addr(bar));
+    } else {
+      zb::st_async_b32(zb::mapa_shared(zb::smem_addr(buf), lane), __float_as_uint(v),
+                       zb::mapa_shared(zb::smem_addr(bar), lane));
     }
-    const float rr = rsqrtf(zb::warp_sum(ss) / (float)D + p.eps);
-    float lg = 0.f;
-#pragma unroll
-    for (int u = 0; u < VPL; ++u) {
-      float v[8], qv[8];
-      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v4[r][u]), v);
-      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&q4[u]), qv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) lg += zb::bf16_round(zb::bf16_round(v[j] * rr) * qv[j]);
-    }
-    lg = zb::warp_sum(lg);
-    const int64_t row = row0 + r;
-    if (lane == 0 && row < total) reinterpret_cast<float*>(p.out + (row % p.T) * D)[row / p.T] = lg;
   }
 }
 
-constexpr int kMixBatch = 16;  // source rows in flight per thread in the mix
-
-template <int VPL>
-__global__ void __launch_bounds__(kThreads) attnres_mix_kernel(RouteParams p) {
-  constexpr int kWarps = kThreads / 32;
-  constexpr int kVecs = (32 * VPL + kThreads - 1) / kThreads;  // 16-byte column vectors per thread
-  const int64_t t = blockIdx.x;
+template <int C>
+__global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParams p) {
+  constexpr int kWarps = kRouteWarps;
+  constexpr int kLaneVecs = C / 256;   // 16-byte vectors of a lane in the per-source sweeps
+  // columns of a thread in the mix: 4 (C = 1024) or 2; with C = 256 only the first 128 threads mix
+  constexpr int kColsT = C / kRouteThreads >= 2 ? C / kRouteThreads : 2;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CL = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  const int64_t t = blockIdx.x / CL;
+  const int c0 = rank * C;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int ns = p.S + (p.source ? 1 : 0);
   const int D = p.D;
-  __shared__ float weight[kMaxSources];
-  __shared__ float red[kWarps];
-  const float* logits = reinterpret_cast<const float*>(p.out + t * D);
-  for (int s = tid; s < ns; s += kThreads) weight[s] = logits[s];
-  __syncthreads();
-  if (warp == 0) {  // softmax over the sources (fp32), weights rounded to bf16
-    float m = -INFINITY;
-    for (int s = lane; s < ns; s += 32) m = fmaxf(m, weight[s]);
-    m = zb::warp_max(m);
-    float den = 0.f;
-    for (int s = lane; s < ns; s += 32) den += expf(weight[s] - m);
-    den = zb::warp_sum(den);
-    __syncwarp();
-    for (int s = lane; s < ns; s += 32) weight[s] = zb::bf16_round(expf(weight[s] - m) / den);
-  }
-  __syncthreads();  // every thread has read the logits before any output is written over them
+  const bool cache = p.rms_cache != nullptr;
+  const int first = cache ? p.cached : 0;  // sources [0, first) take their inverse RMS from the cache
+  const int nnew = ns - first;
 
-  auto row_ptr = [&](int s) -> const __nv_bfloat16* {
-    return (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * D;
-  };
-  const int nvec = D / 8;
-  float mix[kVecs][8];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const RouteLayout lay(ns, C, CL);
+  __nv_bfloat16* tiles = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [ns][C]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + lay.bars);
+  uint64_t* xbar = bars + ns;  // [0] sums of squares, [1] logits, [2] mix norm (peers), [3] mix norm (local warps)
+  float* xss = reinterpret_cast<float*>(smem_raw + lay.xss);
+  float* xlg = reinterpret_cast<float*>(smem_raw + lay.xlg);
+  float* xnrm = reinterpret_cast<float*>(smem_raw + lay.xnrm);
+  float* inv_rms = reinterpret_cast<float*>(smem_raw + lay.inv_rms);
+  uint32_t* wp = reinterpret_cast<uint32_t*>(smem_raw + lay.wp) + (size_t)warp * ns;
+  float* red = reinterpret_cast<float*>(smem_raw + lay.red);
+
+  if (tid == 0) {
+    for (int s = 0; s < ns; ++s) zb::mbar_init(zb::smem_addr(&bars[s]), 1);
+    if (nnew) zb::mbar_init(zb::smem_addr(&xbar[0]), nnew);
+    zb::mbar_init(zb::smem_addr(&xbar[1]), ns);
+    zb::mbar_init(zb::smem_addr(&xbar[2]), 1);
+    zb::mbar_init(zb::smem_addr(&xbar[3]), kWarps);
+    if (CL > 1) {  // the bytes the peers push
+      if (nnew) zb::mbar_expect_tx(zb::smem_addr(&xbar[0]), (CL - 1) * nnew * 4);
+      zb::mbar_expect_tx(zb::smem_addr(&xbar[1]), (CL - 1) * ns * 4);
+      zb::mbar_arrive_expect_tx(zb::smem_addr(&xbar[2]), (CL - 1) * 4);
+    }
+    zb::fence_mbar_init();
+  }
+  if (warp == 0) {  // lanes of warp 0 issue the copies: the sources without a cached inverse RMS first
+    __syncwarp();
+    constexpr uint32_t kSlice = C * 2;
+    for (int i = lane; i < ns; i += 32) {
+      const int s = i < nnew ? first + i : i - nnew;
+      const uint32_t bar = zb::smem_addr(&bars[s]);
+      const __nv_bfloat16* src = (s < p.S ? p.bank + (int64_t)s * p.bank_stride : p.source) + t * D + c0;
+      zb::mbar_arrive_expect_tx(bar, kSlice);
+      zb::bulk_g2s(zb::smem_addr(tiles + (size_t)s * C), src, kSlice, bar);
+    }
+  } else {
+    for (int s = tid - 32; s < first; s += kRouteThreads - 32) inv_rms[s] = p.rms_cache[(int64_t)s * p.rms_stride + t];
+  }
+  __syncthreads();
+  if (CL > 1) zb::cluster_arrive_relaxed();
+  uint4 q4[kLaneVecs];
 #pragma unroll
-  for (int c = 0; c < kVecs; ++c) {
+  for (int u = 0; u < kLaneVecs; ++u) q4[u] = *reinterpret_cast<const uint4*>(p.query + c0 + u * 256 + lane * 8);
+  if (CL > 1) zb::cluster_wait();  // every peer's exchange mbarriers are initialised from here on
+
+  const float inv_d = 1.0f / (float)D;
+  for (int u = warp; u < nnew + ns; u += kWarps) {
+    if (u < nnew) {  // sum-of-squares unit
+      const int s = first + u;
+      zb::mbar_wait_bounded(zb::smem_addr(&bars[s]), 0, p.status, zb::kStatusAttnresLoadTimeout);
+      const __nv_bfloat16* row = tiles + (size_t)s * C;
+      uint64_t ss2 = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mix[c][j] = 0.f;
-    const int vec = tid + c * kThreads;
-    if (vec >= nvec) continue;
-    for (int s0 = 0; s0 < ns; s0 += kMixBatch) {
-      uint4 raw[kMixBatch];
+      for (int v = 0; v < kLaneVecs; ++v) {
+        const uint4 x = *reinterpret_cast<const uint4*>(row + v * 256 + lane * 8);
+        const uint32_t w[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-      for (int i = 0; i < kMixBatch; ++i)
-        if (s0 + i < ns) raw[i] = __ldcg(reinterpret_cast<const uint4*>(row_ptr(s0 + i) + vec * 8));
-#pragma unroll
-      for (int i = 0; i < kMixBatch; ++i) {
-        if (s0 + i < ns) {
-          float v[8];
-          zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&raw[i]), v);
-          const float w = weight[s0 + i];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) mix[c][j] += zb::bf16_round(v[j] * w);
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t f = bf2_to_x2(w[k]);
+          ss2 = fma_x2(f, f, ss2);
         }
       }
-      if (p.append && s0 + kMixBatch >= ns) {  // the current source is the last one routed: append it
+      publish(zb::warp_sum(sum_x2(ss2)), xss + (size_t)rank * ns + s, &xbar[0], CL, rank, lane);
+      continue;
+    }
+    const int s = u - nnew;  // logit unit of source s (cached sources first, so their units run first)
+    float inv;
+    if (s < first) {
+      inv = inv_rms[s];
+    } else {
+      zb::mbar_wait_bounded(zb::smem_addr(&xbar[0]), 0, p.status, zb::kStatusAttnresExchangeTimeout);
+      float total = 0.f;
+      for (int r = 0; r < CL; ++r) total += xss[(size_t)r * ns + s];
+      inv = rsqrtf(total * inv_d + p.eps);
+      if (cache && rank == 0 && lane == 0) p.rms_cache[(int64_t)s * p.rms_stride + t] = inv;
+    }
+    zb::mbar_wait_bounded(zb::smem_addr(&bars[s]), 0, p.status, zb::kStatusAttnresLoadTimeout);
+    const __nv_bfloat16* row = tiles + (size_t)s * C;
+    const uint64_t rr2 = splat_x2(inv);
+    uint64_t lg2 = 0;
 #pragma unroll
-        for (int i = 0; i < kMixBatch; ++i)
-          if (s0 + i == ns - 1) *reinterpret_cast<uint4*>(p.append + t * D + vec * 8) = raw[i];
+    for (int v = 0; v < kLaneVecs; ++v) {
+      const uint4 x = *reinterpret_cast<const uint4*>(row + v * 256 + lane * 8);
+      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+      const uint32_t qq[4] = {q4[v].x, q4[v].y, q4[v].z, q4[v].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t key = x2_to_bf2(mul_x2(bf2_to_x2(w[k]), rr2));  // bf16(v * inv_rms), two at once
+        lg2 = add_x2(lg2, bf2_to_x2(hmul2_bits(key, qq[k])));          // + bf16(key * q)
+      }
+    }
+    publish(zb::warp_sum(sum_x2(lg2)), xlg + (size_t)rank * ns + s, &xbar[1], CL, rank, lane);
+  }
+
+  // every warp: logits (rank-ordered sums), fp32 softmax, bf16 weights into its own row
+  zb::mbar_wait_bounded(zb::smem_addr(&xbar[1]), 0, p.status, zb::kStatusAttnresExchangeTimeout);
+  auto logit = [&](int s) {
+    float total = 0.f;
+    for (int r = 0; r < CL; ++r) total += xlg[(size_t)r * ns + s];
+    return total;
+  };
+  float m = -INFINITY;
+  for (int s = lane; s < ns; s += 32) m = fmaxf(m, logit(s));
+  m = zb::warp_max(m);
+  float den = 0.f;
+  for (int s = lane; s < ns; s += 32) den += expf(logit(s) - m);
+  den = zb::warp_sum(den);
+  for (int s = lane; s < ns; s += 32) {
+    const __nv_bfloat16 wb = __float2bfloat16_rn(expf(logit(s) - m) / den);
+    wp[s] = (uint32_t)__bfloat16_as_ushort(wb) * 0x10001u;
+  }
+  __syncwarp();
+
+  // mix: thread per kColsT columns, all sources from shared memory
+  float mix[kColsT];
+  const int cc = tid * kColsT;
+  const bool mixer = cc < C;
+  {
+    uint64_t acc[kColsT / 2];
+#pragma unroll
+    for (int j = 0; j < kColsT / 2; ++j) acc[j] = 0;
+    if (mixer) {
+#pragma unroll 4
+      for (int s = 0; s < ns; ++s) {
+        const uint32_t w2 = wp[s];
+        const __nv_bfloat16* row = tiles + (size_t)s * C + cc;
+        if constexpr (kColsT == 4) {
+          const uint2 v = *reinterpret_cast<const uint2*>(row);
+          acc[0] = add_x2(acc[0], bf2_to_x2(hmul2_bits(v.x, w2)));  // + bf16(v * w), two at once
+          acc[1] = add_x2(acc[1], bf2_to_x2(hmul2_bits(v.y, w2)));
+        } else {
+          acc[0] = add_x2(acc[0], bf2_to_x2(hmul2_bits(*reinterpret_cast<const uint32_t*>(row), w2)));
+        }
       }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) mix[c][j] = zb::bf16_round(mix[c][j]);
+    for (int j = 0; j < kColsT / 2; ++j) {
+      mix[2 * j] = __uint_as_float((uint32_t)acc[j]);
+      mix[2 * j + 1] = __uint_as_float((uint32_t)(acc[j] >> 32));
+    }
   }
+#pragma unroll
+  for (int j = 0; j < kColsT; ++j) mix[j] = zb::bf16_round(mix[j]);
+  const int64_t off = t * D + c0 + cc;
+  auto store = [&](__nv_bfloat16* dst, const float* vals) {
+    if constexpr (kColsT == 4) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(f2_to_bf2(vals[0], vals[1]), f2_to_bf2(vals[2], vals[3]));
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = f2_to_bf2(vals[0], vals[1]);
+    }
+  };
   if (p.norm_weight) {
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kVecs; ++c)
-      if (tid + c * kThreads < nvec)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss = fmaf(mix[c][j], mix[c][j], ss);
+    for (int j = 0; j < kColsT; ++j) ss = fmaf(mix[j], mix[j], ss);  // zero for threads that do not mix
     ss = zb::warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    float total = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) total += red[w];
-    const float rn = rsqrtf(total / (float)D + p.norm_eps);
-#pragma unroll
-    for (int c = 0; c < kVecs; ++c) {
-      const int vec = tid + c * kThreads;
-      if (vec >= nvec) continue;
-      float nw[8], y[8];
-      zb::ld_bf16x8(p.norm_weight + vec * 8, nw);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = mix[c][j] * rn * nw[j];
-      if (p.mix_out) *reinterpret_cast<uint4*>(p.mix_out + t * D + vec * 8) = zb::pack_bf16x8(mix[c]);
-      *reinterpret_cast<uint4*>(p.out + t * D + vec * 8) = zb::pack_bf16x8(y);
+    if (lane == 0) {
+      red[warp] = ss;
+      zb::mbar_arrive(zb::smem_addr(&xbar[3]));
     }
-  } else {
-#pragma unroll
-    for (int c = 0; c < kVecs; ++c) {
-      const int vec = tid + c * kThreads;
-      if (vec >= nvec) continue;
-      *reinterpret_cast<uint4*>(p.out + t * D + vec * 8) = zb::pack_bf16x8(mix[c]);
+    zb::mbar_wait_bounded(zb::smem_addr(&xbar[3]), 0, p.status, zb::kStatusAttnresExchangeTimeout);
+    float local = 0.f;
+    for (int w = 0; w < kWarps; ++w) local += red[w];
+    float total = local;
+    if (CL > 1) {
+      if (warp == 0 && lane < CL && lane != rank)
+        zb::st_async_b32(zb::mapa_shared(zb::smem_addr(&xnrm[rank]), lane), __float_as_uint(local),
+                         zb::mapa_shared(zb::smem_addr(&xbar[2]), lane));
+      zb::mbar_wait_bounded(zb::smem_addr(&xbar[2]), 0, p.status, zb::kStatusAttnresExchangeTimeout);
+      total = 0.f;
+      for (int r = 0; r < CL; ++r) total += r == rank ? local : xnrm[r];
     }
+    const float rn = rsqrtf(total * inv_d + p.norm_eps);
+    if (mixer) {
+      float y[kColsT];
+#pragma unroll
+      for (int j = 0; j < kColsT; ++j) y[j] = mix[j] * rn * __bfloat162float(p.norm_weight[c0 + cc + j]);
+      if (p.mix_out) store(p.mix_out + off, mix);
+      store(p.out + off, y);
+    }
+  } else if (mixer) {
+    store(p.out + off, mix);
+  }
+  if (p.append) {
+    for (int i = tid; i < C / 8; i += kRouteThreads)
+      *reinterpret_cast<uint4*>(p.append + t * D + c0 + 8 * i) =
+          *reinterpret_cast<const uint4*>(tiles + (size_t)(ns - 1) * C + 8 * i);
   }
 }
 
-template <int VPL>
+template <int C>
 int launch(const RouteParams& p, cudaStream_t stream) {
   const int ns = p.S + (p.source ? 1 : 0);
-  const int64_t rows = (int64_t)ns * p.T;
-  const int64_t per_cta = (int64_t)kLogitWarps * kLogitRows;
-  attnres_logits_kernel<VPL><<<(unsigned)((rows + per_cta - 1) / per_cta), 32 * kLogitWarps, 0, stream>>>(p);
-  if (int rc = zb::check_launch("attnres_route(logits)")) return rc;
-  attnres_mix_kernel<VPL><<<(unsigned)p.T, kThreads, 0, stream>>>(p);
-  return zb::check_launch("attnres_route(mix)");
+  const size_t smem = RouteLayout(ns, C, p.D / C).total;
+  auto kernel = attnres_route_kernel<C>;
+  if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int CL = p.D / C;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.T * CL));
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
+  return zb::check_launch("attnres_route");
 }
 
 }  // namespace
 
 ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, const uint16_t* source,
                             uint16_t* append, const uint16_t* query, float eps, const uint16_t* norm_weight,
-                            float norm_eps, uint16_t* out, uint16_t* mix_out, int T, int D, cudaStream_t stream) {
+                            float norm_eps, uint16_t* out, uint16_t* mix_out, float* rms_cache, int64_t rms_stride,
+                            int cached, int T, int D, cudaStream_t stream) {
   const int ns = S + (source ? 1 : 0);
   ZB_REQUIRE(S >= 0 && T >= 0 && D > 0, "attnres_route: bad sizes S=%d T=%d D=%d", S, T, D);
   ZB_REQUIRE(ns >= 1, "attnres_route: no source to route over");
   if (ns > kMaxSources) return zb::fail(zb::kUnsupported, "attnres_route: %d sources (max %d)", ns, kMaxSources);
-  if (D % 256 != 0 || D > 8 * 512)
-    return zb::fail(zb::kUnsupported, "attnres_route: D=%d (a multiple of 256, at most 4096)", D);
-  if (ns > D / 2)
-    return zb::fail(zb::kUnsupported, "attnres_route: %d sources need D >= %d (the logits park in the output row)",
-                    ns, 2 * ns);
+  if (D % 256 != 0 || D > 8192)
+    return zb::fail(zb::kUnsupported, "attnres_route: D=%d (a multiple of 256, at most 8192)", D);
+  // C = columns per CTA: the widest of 1024 / 512 / 256 that divides D into at most 8 CTAs and whose ns slices
+  // fit the shared-memory budget (1024 at D=2048 and 49 sources: two CTAs per SM)
+  int C = 0;
+  for (int c : {1024, 512, 256}) {
+    if (D % c == 0 && D / c <= 8 && RouteLayout(ns, c, D / c).total <= kRouteSmemBudget) {
+      C = c;
+      break;
+    }
+  }
+  if (C == 0) return zb::fail(zb::kUnsupported, "attnres_route: %d sources of D=%d exceed shared memory", ns, D);
   if (T == 0) return zb::kOk;
   ZB_REQUIRE(query && out, "attnres_route: null query/out");
   ZB_REQUIRE(out != source && out != append && (mix_out == nullptr || (mix_out != out && mix_out != source)),
@@ -221,6 +389,8 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
   ZB_REQUIRE(!mix_out || norm_weight, "attnres_route: mix_out is only written with norm_weight");
   ZB_REQUIRE(S == 0 || bank_stride >= (int64_t)T * D, "attnres_route: bank_stride smaller than T*D");
   ZB_REQUIRE(bank_stride % 8 == 0, "attnres_route: bank_stride must be a multiple of 8 elements");
+  ZB_REQUIRE(!rms_cache || (rms_stride >= T && cached >= 0 && cached <= S),
+             "attnres_route: rms cache needs rms_stride >= T and 0 <= cached <= S");
   for (const void* ptr : {(const void*)bank, (const void*)source, (const void*)append, (const void*)query,
                           (const void*)norm_weight, (const void*)out, (const void*)mix_out}) {
     ZB_REQUIRE_ALIGNED(ptr, 16, "attnres_route tensors");
@@ -229,17 +399,9 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
                 reinterpret_cast<const __nv_bfloat16*>(source), reinterpret_cast<__nv_bfloat16*>(append),
                 reinterpret_cast<const __nv_bfloat16*>(query), eps,
                 reinterpret_cast<const __nv_bfloat16*>(norm_weight), norm_eps,
-                reinterpret_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(mix_out), T, D,
-                zb::device_status_ptr()};
-  switch (D / 256) {
-    case 1: return launch<1>(p, stream);
-    case 2: return launch<2>(p, stream);
-    case 3: return launch<3>(p, stream);
-    case 4: return launch<4>(p, stream);
-    case 6: return launch<6>(p, stream);
-    case 8: return launch<8>(p, stream);
-    case 12: return launch<12>(p, stream);
-    case 16: return launch<16>(p, stream);
-    default: return zb::fail(zb::kUnsupported, "attnres_route: D=%d (256, 512, 768, 1024, 1536, 2048, 3072 or 4096)", D);
-  }
+                reinterpret_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(mix_out), rms_cache,
+                rms_stride, cached, T, D, zb::device_status_ptr()};
+  if (C == 1024) return launch<1024>(p, stream);
+  if (C == 512) return launch<512>(p, stream);
+  return launch<256>(p, stream);
 }

@@ -41,6 +41,7 @@ enum DeviceStatusBits : unsigned {
   kStatusAttnresLoadTimeout = 1u << 0,
   kStatusGemmTimeout = 1u << 1,
   kStatusPrefillTimeout = 1u << 2,
+  kStatusAttnresExchangeTimeout = 1u << 3,
 };
 
 }  // namespace zb
@@ -130,6 +131,32 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Adds `bytes` of expected transaction to the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Cluster barrier split in two: a relaxed arrival (orders nothing; pairs with fence_mbar_init for barrier
+// initialisation) and the wait for every thread of the cluster to have arrived.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// The shared::cluster address of this CTA's shared-memory word `local` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+// 4-byte store into another cluster CTA's shared memory, completing 4 bytes of transaction on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_b32(uint32_t remote_addr, uint32_t value, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_addr),
+               "r"(value), "r"(remote_bar)
+               : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {

@@ -112,13 +112,16 @@ def attnres_route(
     norm_eps: float = 1e-5,
     out: torch.Tensor | None = None,
     mix_out: torch.Tensor | None = None,
+    rms_cache: torch.Tensor | None = None,
+    cached: int = 0,
 ) -> torch.Tensor:
     """Full AttnRes route over ``bank[:num_sources]`` (+ ``source`` as the last source) for every token.
 
     bank [>= num_sources, T, D] bf16 (rows contiguous [T, D]); source [T, D] bf16; query [D] bf16. The mix follows
     full_attnres_route (model/src/zonos3/reference/lm.py:384-389) with the fused Triton kernel's bf16 rounding
     points. ``norm_weight`` fuses the RMSNorm after the route (out = RMSNorm(mix) and, if given, mix_out = mix);
-    ``append_to`` (a [T, D] bank row) receives ``source`` in the same pass.
+    ``append_to`` (a [T, D] bank row) receives ``source`` in the same pass. ``rms_cache`` (fp32 [>= sources, T])
+    holds each source's key inverse RMS: rows below ``cached`` are read, the others computed and stored.
     """
     _check_cuda("query", query, torch.bfloat16)
     dev = query.device
@@ -153,12 +156,22 @@ def attnres_route(
             _check_cuda(name, t, torch.bfloat16, dev)
             _require(t.shape == (T, D) and t.is_contiguous(), f"{name} must be a contiguous [T, D] tensor")
     _require(mix_out is None or norm_weight is not None, "mix_out is only produced with norm_weight")
+    rms_stride = 0
+    if rms_cache is not None:
+        _check_cuda("rms_cache", rms_cache, torch.float32, dev)
+        routed = num_sources + (source is not None)
+        _require(rms_cache.dim() == 2 and rms_cache.shape[0] >= routed and rms_cache.shape[1] >= T
+                 and rms_cache.stride(1) == 1, f"rms_cache must be [>= {routed}, >= {T}] with unit column stride")
+        _require(0 <= cached <= num_sources, f"cached must be in [0, {num_sources}]")
+        rms_stride = rms_cache.stride(0)
+    else:
+        cached = 0
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
     _lib.call(
         "zb_attnres_route",
         ptr(bank) if num_sources else None, bank_stride, num_sources, ptr(source), ptr(append_to),
-        query.data_ptr(), float(eps), ptr(norm_weight), float(norm_eps), out.data_ptr(), ptr(mix_out), T, D,
-        _stream(dev),
+        query.data_ptr(), float(eps), ptr(norm_weight), float(norm_eps), out.data_ptr(), ptr(mix_out),
+        ptr(rms_cache), rms_stride, int(cached), T, D, _stream(dev),
     )
     return out
 
