@@ -405,7 +405,7 @@ def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps
     queries = (0.02 * torch.randn(n_src, dim, generator=gen)).bfloat16().to(dev)
     norm_w = torch.ones(dim, dtype=torch.bfloat16, device=dev)
     out = torch.empty(tokens, dim, device=dev, dtype=torch.bfloat16)
-    rms_cache = torch.zeros(n_src, tokens, device=dev, dtype=torch.float32)
+    rms_cache = torch.zeros(tokens, (n_src + 3) // 4 * 4, device=dev, dtype=torch.float32)
     flush = L2Flush(dev)
 
     def schedule(with_routes):
@@ -534,7 +534,7 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
         bank = torch.randn(49, 256, 2048, generator=gen).bfloat16().to(dev)
         query = (0.02 * torch.randn(2048, generator=gen)).bfloat16().to(dev)
         norm_w = torch.ones(2048, dtype=torch.bfloat16, device=dev)
-        rms_cache = torch.zeros(49, 256, device=dev, dtype=torch.float32)
+        rms_cache = torch.zeros(256, 52, device=dev, dtype=torch.float32)
         ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w, rms_cache=rms_cache, cached=0)
         flush = L2Flush(dev)
         for _ in range(n):

@@ -98,8 +98,9 @@ int zb_gdn_gated_norm(const uint16_t* o, const uint16_t* z, int64_t z_stride, co
  *   query       [D] bf16; eps: the key RMSNorm epsilon
  *   norm_weight [D] bf16 or NULL: out = RMSNorm(mix; norm_weight, norm_eps) and mix_out (optional) = mix;
  *               NULL: out = mix (mix_out must be NULL)
- *   rms_cache   fp32 [>= S + (source != NULL), rms_stride] or NULL: the key inverse RMS of source s for token t at
- *               s * rms_stride + t (rms_stride >= T). Rows [0, cached) are read from it; every later source's value
+ *   rms_cache   fp32 [T, rms_stride] or NULL (16-byte aligned; rms_stride a multiple of 4, at least the routed
+ *               sources rounded up to 4): the key inverse RMS of source s for token t at t * rms_stride + s.
+ *               Sources [0, cached) are read from it; every later source's value
  *               is computed and written back, so a bank that grows by one row per route reads each row's sum of
  *               squares once (the cached_norm mode of training_attnres_kernels.py:1268-1348).
  *   D a multiple of 256 (at most 8192), S + (source != NULL) in [1, 256]; all pointers 16-byte aligned. */

@@ -99,18 +99,18 @@ def test_rms_cache_reads_and_fills(zb):
     S, T, D = 10, 24, 2048
     bank, query = make_bank(S, T, D, seed=91)
     d_bank, d_query = bank.cuda(), query.cuda()
-    cache = torch.full((S + 1, T), float("nan"), device="cuda")
+    cache = torch.full((T, 12), float("nan"), device="cuda")
     first = zb.ops.attnres_route(d_bank, 4, d_query, EPS, rms_cache=cache, cached=0)
     ref_first = zb.ops.attnres_route(d_bank, 4, d_query, EPS)
     full = zb.ops.attnres_route(d_bank, S, d_query, EPS, rms_cache=cache, cached=4)
     ref_full = zb.ops.attnres_route(d_bank, S, d_query, EPS)
     torch.cuda.synchronize()
     assert torch.equal(first, ref_first) and torch.equal(full, ref_full)
-    inv = torch.rsqrt(bank.float().pow(2).mean(-1) + EPS)
-    assert torch.isnan(cache[S]).all()
-    assert torch.allclose(cache[:S].cpu(), inv, rtol=1e-5)
+    inv = torch.rsqrt(bank.float().pow(2).mean(-1) + EPS)  # [S, T]
+    assert torch.isnan(cache[:, S:]).all()
+    assert torch.allclose(cache[:, :S].cpu(), inv.T, rtol=1e-5)
     # a stale cache entry below ``cached`` is used as given: the route trusts the caller's bookkeeping
-    cache[0].fill_(0.0)
+    cache[:, 0].fill_(0.0)
     skewed = zb.ops.attnres_route(d_bank, S, d_query, EPS, rms_cache=cache, cached=1)
     torch.cuda.synchronize()
     assert not torch.equal(skewed, ref_full)

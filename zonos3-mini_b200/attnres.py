@@ -49,7 +49,7 @@ class FusedBlockAttnResContext:
                                   dtype=reference.dtype)
         # key inverse RMS of every bank row (and of the routed source), filled by the route kernel: each row's sum
         # of squares is read from HBM once per forward instead of once per later route
-        self.rms_cache = torch.empty((self.max_completed_blocks + 1, self.bt), device=reference.device,
+        self.rms_cache = torch.empty((self.bt, (self.max_completed_blocks + 4) // 4 * 4), device=reference.device,
                                      dtype=torch.float32)
         self._rms_eps = None
         self.completed_count = 0

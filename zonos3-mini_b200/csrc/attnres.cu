@@ -18,7 +18,6 @@ namespace {
 
 constexpr int kMaxSources = 256;
 constexpr size_t kRouteSmemBudget = 200 * 1024;
-constexpr int kThreads = 256;  // 8 warps per token
 
 struct RouteParams {
   const __nv_bfloat16* bank;  // [>= S, T, D]
@@ -32,16 +31,13 @@ struct RouteParams {
   float norm_eps;
   __nv_bfloat16* out;      // [T, D]: normalised mix if norm_weight, else the mix
   __nv_bfloat16* mix_out;  // optional [T, D]: the un-normalised mix (when norm_weight is given)
-  float* rms_cache;        // optional [rows, rms_stride]: inverse RMS of bank row s for token t at s * stride + t
+  float* rms_cache;        // optional [T, rms_stride]: inverse RMS of source s for token t at t * rms_stride + s
   int64_t rms_stride;
   int cached;              // bank rows [0, cached) have valid cache entries; later rows compute and store theirs
   int T, D;
   unsigned* status;
 };
 
-__device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
-}
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -83,7 +79,8 @@ __device__ __forceinline__ uint32_t x2_to_bf2(uint64_t v) {  // round both halve
 
 // One route, one pass over HBM. A token is a cluster of CL CTAs; CTA r owns columns [r*C, (r+1)*C) of every source
 // and stages that slice of all ns sources in shared memory (one cp.async.bulk per source, each with its own
-// mbarrier, all issued at once; the sources without a cached inverse RMS first). The 8 warps then take work units
+// mbarrier, all issued at once; the sources without a cached inverse RMS first, behind one copy of the query slice
+// and the token's cached inverse RMS row). The 8 warps then take work units
 // round-robin, each as soon as its source has landed:
 //   sum-of-squares units (sources without a cached inverse RMS): partial sum of squares of the slice;
 //   logit units (every source): inverse RMS (cached, or from the exchanged sums of squares), then the partial logit
@@ -100,14 +97,15 @@ constexpr int kRouteWarps = kRouteThreads / 32;
 
 // Shared-memory layout of one CTA: ns source slices of C columns, ns + 4 mbarriers, the exchange buffers.
 struct RouteLayout {
-  size_t bars, xss, xlg, xnrm, inv_rms, wp, red, total;
+  size_t bars, qs, inv_rms, xss, xlg, xnrm, wp, red, total;
   __host__ __device__ RouteLayout(int ns, int C, int CL) {
-    bars = (size_t)ns * C * 2;               // [ns] source copies + [4] exchanges
-    xss = bars + (size_t)(ns + 4) * 8;       // [CL][ns] fp32 partial sums of squares
+    bars = (size_t)ns * C * 2;               // [ns] source copies + [4] exchanges + [1] query / cache row
+    qs = (bars + (size_t)(ns + 6) * 8 + 15) / 16 * 16;  // [C] bf16 query slice
+    inv_rms = qs + (size_t)C * 2;            // [ns rounded up to 4] fp32 cached inverse RMS
+    xss = inv_rms + (size_t)(ns + 3) / 4 * 16;  // [CL][ns] fp32 partial sums of squares
     xlg = xss + (size_t)CL * ns * 4;         // [CL][ns] fp32 partial logits
     xnrm = xlg + (size_t)CL * ns * 4;        // [8] fp32 partial sums of squares of the mix
-    inv_rms = xnrm + 8 * 4;                  // [ns] fp32 cached inverse RMS
-    wp = inv_rms + (size_t)ns * 4;           // [kRouteWarps][ns] bf16x2 weights (each warp its own row)
+    wp = xnrm + 8 * 4;                       // [kRouteWarps][ns] bf16x2 weights (each warp its own row)
     red = wp + (size_t)kRouteWarps * ns * 4; // [kRouteWarps]
     total = red + kRouteWarps * 4;
   }
@@ -150,6 +148,8 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
   __nv_bfloat16* tiles = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [ns][C]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + lay.bars);
   uint64_t* xbar = bars + ns;  // [0] sums of squares, [1] logits, [2] mix norm (peers), [3] mix norm (local warps)
+  uint64_t* meta = xbar + 4;   // query slice and cached inverse RMS row landed
+  const __nv_bfloat16* qs = reinterpret_cast<const __nv_bfloat16*>(smem_raw + lay.qs);
   float* xss = reinterpret_cast<float*>(smem_raw + lay.xss);
   float* xlg = reinterpret_cast<float*>(smem_raw + lay.xlg);
   float* xnrm = reinterpret_cast<float*>(smem_raw + lay.xnrm);
@@ -163,12 +163,19 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
     zb::mbar_init(zb::smem_addr(&xbar[1]), ns);
     zb::mbar_init(zb::smem_addr(&xbar[2]), 1);
     zb::mbar_init(zb::smem_addr(&xbar[3]), kWarps);
+    zb::mbar_init(zb::smem_addr(meta), 1);
     if (CL > 1) {  // the bytes the peers push
       if (nnew) zb::mbar_expect_tx(zb::smem_addr(&xbar[0]), (CL - 1) * nnew * 4);
       zb::mbar_expect_tx(zb::smem_addr(&xbar[1]), (CL - 1) * ns * 4);
       zb::mbar_arrive_expect_tx(zb::smem_addr(&xbar[2]), (CL - 1) * 4);
     }
     zb::fence_mbar_init();
+    // ahead of the sources: the query slice and the token's cached inverse RMS prefix (a token-major cache row)
+    const uint32_t inv_bytes = first ? (uint32_t)((first * 4 + 15) / 16 * 16) : 0u;
+    zb::mbar_arrive_expect_tx(zb::smem_addr(meta), (uint32_t)C * 2 + inv_bytes);
+    zb::bulk_g2s(zb::smem_addr(qs), p.query + c0, C * 2, zb::smem_addr(meta));
+    if (inv_bytes)
+      zb::bulk_g2s(zb::smem_addr(inv_rms), p.rms_cache + t * p.rms_stride, inv_bytes, zb::smem_addr(meta));
   }
   if (warp == 0) {  // lanes of warp 0 issue the copies: the sources without a cached inverse RMS first
     __syncwarp();
@@ -180,15 +187,14 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
       zb::mbar_arrive_expect_tx(bar, kSlice);
       zb::bulk_g2s(zb::smem_addr(tiles + (size_t)s * C), src, kSlice, bar);
     }
-  } else {
-    for (int s = tid - 32; s < first; s += kRouteThreads - 32) inv_rms[s] = p.rms_cache[(int64_t)s * p.rms_stride + t];
   }
   __syncthreads();
   if (CL > 1) zb::cluster_arrive_relaxed();
+  if (CL > 1) zb::cluster_wait();  // every peer's exchange mbarriers are initialised from here on
+  zb::mbar_wait_bounded(zb::smem_addr(meta), 0, p.status, zb::kStatusAttnresLoadTimeout);
   uint4 q4[kLaneVecs];
 #pragma unroll
-  for (int u = 0; u < kLaneVecs; ++u) q4[u] = *reinterpret_cast<const uint4*>(p.query + c0 + u * 256 + lane * 8);
-  if (CL > 1) zb::cluster_wait();  // every peer's exchange mbarriers are initialised from here on
+  for (int u = 0; u < kLaneVecs; ++u) q4[u] = *reinterpret_cast<const uint4*>(qs + u * 256 + lane * 8);
 
   const float inv_d = 1.0f / (float)D;
   for (int u = warp; u < nnew + ns; u += kWarps) {
@@ -219,7 +225,7 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
       float total = 0.f;
       for (int r = 0; r < CL; ++r) total += xss[(size_t)r * ns + s];
       inv = rsqrtf(total * inv_d + p.eps);
-      if (cache && rank == 0 && lane == 0) p.rms_cache[(int64_t)s * p.rms_stride + t] = inv;
+      if (cache && rank == 0 && lane == 0) p.rms_cache[t * p.rms_stride + s] = inv;
     }
     zb::mbar_wait_bounded(zb::smem_addr(&bars[s]), 0, p.status, zb::kStatusAttnresLoadTimeout);
     const __nv_bfloat16* row = tiles + (size_t)s * C;
@@ -389,10 +395,12 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
   ZB_REQUIRE(!mix_out || norm_weight, "attnres_route: mix_out is only written with norm_weight");
   ZB_REQUIRE(S == 0 || bank_stride >= (int64_t)T * D, "attnres_route: bank_stride smaller than T*D");
   ZB_REQUIRE(bank_stride % 8 == 0, "attnres_route: bank_stride must be a multiple of 8 elements");
-  ZB_REQUIRE(!rms_cache || (rms_stride >= T && cached >= 0 && cached <= S),
-             "attnres_route: rms cache needs rms_stride >= T and 0 <= cached <= S");
+  ZB_REQUIRE(!rms_cache || (rms_stride >= (ns + 3) / 4 * 4 && rms_stride % 4 == 0 && cached >= 0 && cached <= S),
+             "attnres_route: rms cache rows need a stride >= the sources rounded up to 4 (a multiple of 4) and "
+             "0 <= cached <= S");
   for (const void* ptr : {(const void*)bank, (const void*)source, (const void*)append, (const void*)query,
-                          (const void*)norm_weight, (const void*)out, (const void*)mix_out}) {
+                          (const void*)norm_weight, (const void*)out, (const void*)mix_out,
+                          (const void*)rms_cache}) {
     ZB_REQUIRE_ALIGNED(ptr, 16, "attnres_route tensors");
   }
   RouteParams p{reinterpret_cast<const __nv_bfloat16*>(bank), bank_stride, S,

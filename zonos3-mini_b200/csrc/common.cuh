@@ -173,6 +173,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` until the phase completes (the thread resumes as soon as
+// it does), so that waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for phase `parity` of an mbarrier for at most ~`limit_ns`; on expiry ORs `code` into *status and
 // returns false (the caller carries on without hanging the GPU).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned* status, unsigned code,
@@ -180,7 +192,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (globaltimer_ns() - start > limit_ns) {
       if (status) atomicOr(status, code);
       return false;

@@ -120,8 +120,9 @@ def attnres_route(
     bank [>= num_sources, T, D] bf16 (rows contiguous [T, D]); source [T, D] bf16; query [D] bf16. The mix follows
     full_attnres_route (model/src/zonos3/reference/lm.py:384-389) with the fused Triton kernel's bf16 rounding
     points. ``norm_weight`` fuses the RMSNorm after the route (out = RMSNorm(mix) and, if given, mix_out = mix);
-    ``append_to`` (a [T, D] bank row) receives ``source`` in the same pass. ``rms_cache`` (fp32 [>= sources, T])
-    holds each source's key inverse RMS: rows below ``cached`` are read, the others computed and stored.
+    ``append_to`` (a [T, D] bank row) receives ``source`` in the same pass. ``rms_cache`` (fp32 [>= T, >= sources
+    rounded up to 4], token-major) holds each source's key inverse RMS: sources below ``cached`` are read, the
+    others computed and stored.
     """
     _check_cuda("query", query, torch.bfloat16)
     dev = query.device
@@ -160,8 +161,10 @@ def attnres_route(
     if rms_cache is not None:
         _check_cuda("rms_cache", rms_cache, torch.float32, dev)
         routed = num_sources + (source is not None)
-        _require(rms_cache.dim() == 2 and rms_cache.shape[0] >= routed and rms_cache.shape[1] >= T
-                 and rms_cache.stride(1) == 1, f"rms_cache must be [>= {routed}, >= {T}] with unit column stride")
+        need = (routed + 3) // 4 * 4
+        _require(rms_cache.dim() == 2 and rms_cache.shape[0] >= T and rms_cache.shape[1] >= need
+                 and rms_cache.stride(1) == 1 and rms_cache.stride(0) % 4 == 0,
+                 f"rms_cache must be [>= {T}, >= {need}] with unit column stride and a row stride multiple of 4")
         _require(0 <= cached <= num_sources, f"cached must be in [0, {num_sources}]")
         rms_stride = rms_cache.stride(0)
     else:
