@@ -9,17 +9,22 @@
 // layouts gate_up_proj [E, 2I, D] (gate rows first) and down_proj [E, D, I] (zonos3.py:450-637); the math of
 // lm.py:618-639. Rounding points follow the server: GEMM1 output bf16, SwiGLU bf16, GEMM2 * weight bf16.
 //
-// Kernel structure (one persistent CTA per SM, 6 warps):
-//   warp 0      TMA producer: per k-block, A tile [128 x 64] and B tile [256 x 64] (two 128-row boxes), both
-//               128B-swizzled, into a 4-stage shared-memory ring (48 KB per stage);
-//   warp 1      owns the TMEM allocation (512 columns = two 128x256 fp32 accumulators) and, on one lane, issues
-//               tcgen05.mma (M=128, N=256, K=16 per instruction) and the tcgen05.commit arrivals;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp its 32-lane TMEM quarter), SwiGLU or the
-//               routing-weight scale, bf16 stores; the accumulator is double-buffered so the epilogue of one
+// Kernel structure: persistent CTA pairs (clusters of 2, one CTA per SM, 6 warps each) computing 256 x 256 output
+// tiles with the pair-wide tcgen05.mma.cta_group::2 (M = 256: each CTA holds 128 rows of A and 128 of the 256 B
+// rows, and its 128 accumulator rows in its own TMEM), so every SM stages half of the B tile it used to:
+//   warp 0      TMA producer of its CTA: per k-block, its A tile [128 x 64] and its B half [128 x 64], both
+//               128B-swizzled, into a 6-stage ring (32 KB per stage); both CTAs' copies complete bytes on the
+//               leader CTA's full barrier (plain tensor loads, no multicast);
+//   warp 1      TMEM (512 columns = two 128x256 fp32 accumulators, allocated pair-wide); on the leader CTA one
+//               lane issues the M=256 MMAs (K=16 each) and commits to both CTAs' barriers;
+//   warps 2-9   epilogue of each CTA: tcgen05.ld of its accumulator rows (two warps per 32-lane TMEM quarter,
+//               each half of the columns), SwiGLU or the routing-weight scale, bf16 stores, then an arrival on
+//               the leader's accumulator-empty barrier; the accumulator is double-buffered so the epilogue of one
 //               tile overlaps the MMAs of the next.
-// Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the CTAs running at one time share the
-// same weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the kernel sets a status bit,
-// stops issuing, drains its own copies and MMAs (again bounded), frees TMEM and returns.
+// Expert row groups are padded to 128 rows; a 256-row tile whose second half belongs to the next expert computes
+// it and the epilogue drops those rows. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
+// pairs running at one time share weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the
+// kernel sets a status bit, stops issuing, drains (bounded), frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,10 +34,12 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int kThreads = 192;
-constexpr uint32_t A_BYTES = BM * BK * 2;      // 16 KB
-constexpr uint32_t B_BYTES = BN * BK * 2;      // 32 KB
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
+constexpr int PAIR_M = 2 * BM;                 // rows of a pair tile
+constexpr int kEpilogueWarps = 8;               // two per TMEM lane quarter, each half of the columns
+constexpr int kThreads = (2 + kEpilogueWarps) * 32;
+constexpr uint32_t A_BYTES = BM * BK * 2;      // 16 KB: this CTA's A rows
+constexpr uint32_t B_BYTES = BM * BK * 2;      // 16 KB: this CTA's half of the 256 B rows
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kTmemCols = 512;
 constexpr int kMaxExperts = 128;
@@ -57,21 +64,25 @@ struct GemmParams {
 
 // ------------------------------------------------------------------------------------------ PTX wrappers
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+// Tensor load into this CTA's shared memory whose completed bytes count on `bar`, an mbarrier of either CTA of the
+// pair (here always the leader's). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
 
+// Pair-wide TMEM allocation: the same warp of both CTAs executes it; each CTA receives its base address.
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -81,18 +92,29 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Pair-wide MMA (issued by one thread of the leader CTA): D[256 x N] over both CTAs' TMEM from both CTAs' A and B
+// halves at the same shared-memory offsets.
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrives once on `bar` when every tcgen05.mma issued so far by this thread has completed.
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+// Arrives once on the mbarrier at offset `bar` in each CTA of `mask` when every tcgen05.mma issued so far by this
+// thread has completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+// Plain arrival on an mbarrier of any CTA of the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
 // 32 consecutive fp32 columns of this thread's TMEM lane.
@@ -122,11 +144,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M=128, N=256.
+// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M=256 (the pair), N=256.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+                            ((uint32_t)(PAIR_M >> 4) << 24);
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// SiLU with the fast exponential and division: the product silu(gate) * up is rounded to bf16, where their
+// few-ulp fp32 error is far below the rounding step.
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 struct Shared {
   uint64_t full[STAGES];
@@ -136,20 +160,25 @@ struct Shared {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int item_start[kMaxExperts + 1];
+  int item_start[kMaxExperts + 1];  // first work item of each expert (pair tiles x n-tiles)
+  int row_off[kMaxExperts + 1];     // padded row offsets
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     GemmParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // stage buffers first, 1024-byte aligned (the 128B swizzle pattern repeats every 1024 bytes)
+  // stage buffers first, 1024-byte aligned (the 128B swizzle pattern repeats every 1024 bytes); the dynamic
+  // shared-memory base is the same in both CTAs, so every buffer sits at the same offset in the pair
   const uint32_t raw_addr = zb::smem_addr(smem_raw);
   const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
   unsigned char* stages = smem_raw + pad;
   Shared* sh = reinterpret_cast<Shared*>(stages + STAGES * STAGE_BYTES);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const uint32_t rank = blockIdx.x & 1;  // cluster of 2 along x: rank 0 leads the pair
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   volatile int* abort_flag = &sh->abort;
 
   if (tid == 0) {
@@ -159,23 +188,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       zb::mbar_init(zb::smem_addr(&sh->tmem_full[a]), 1);
-      zb::mbar_init(zb::smem_addr(&sh->tmem_empty[a]), 4);
+      zb::mbar_init(zb::smem_addr(&sh->tmem_empty[a]), 2 * kEpilogueWarps);  // the epilogue warps of both CTAs
     }
     zb::mbar_init(zb::smem_addr(&sh->drain), 1);
     sh->abort = 0;
     zb::fence_mbar_init();
   }
-  for (int e = tid; e <= p.E; e += kThreads) sh->item_start[e] = (p.offsets[e] / BM) * p.n_tiles;
+  for (int e = tid; e <= p.E; e += kThreads) sh->row_off[e] = p.offsets[e];
+  __syncthreads();
+  if (tid == 0) {  // work items per expert: ceil(128-row tiles / 2) pair tiles x n-tiles
+    int acc = 0;
+    for (int e = 0; e < p.E; ++e) {
+      sh->item_start[e] = acc;
+      const int m128 = (sh->row_off[e + 1] - sh->row_off[e]) / BM;
+      acc += (m128 + 1) / 2 * p.n_tiles;
+    }
+    sh->item_start[p.E] = acc;
+  }
   if (warp == 1) tmem_alloc(zb::smem_addr(&sh->tmem_base), kTmemCols);
   tc_fence_before();
   __syncthreads();
+  zb::cluster_arrive_relaxed();  // both CTAs' barriers are initialised before either signals the other's
+  zb::cluster_wait();
   tc_fence_after();
   const uint32_t tmem_base = sh->tmem_base;
   const int total_items = sh->item_start[p.E];
   const int E = p.E;
   const int k_blocks = p.K / BK;
 
-  // item -> (expert, n-tile, first row of the m-tile)
+  // item -> (expert, n-tile, first row of the 256-row pair tile)
   auto decode = [&](int item, int& e, int& n, int& row0) {
     int lo = 0, hi = E;  // largest e with item_start[e] <= item
     while (hi - lo > 1) {
@@ -187,16 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m_tiles = (sh->item_start[e + 1] - sh->item_start[e]) / p.n_tiles;
     const int local = item - sh->item_start[e];
     n = local / m_tiles;
-    row0 = (sh->item_start[e] / p.n_tiles + local % m_tiles) * BM;
+    row0 = sh->row_off[e] + (local % m_tiles) * PAIR_M;
   };
 
   if (warp == 0) {
-    if (lane == 0) {
-      uint32_t q = 0;  // k-blocks issued so far
-      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x) {
+    if (lane == 0) {  // producer of this CTA's halves; bytes complete on the leader's full barrier
+      uint32_t q = 0;
+      for (int item = pair; item < total_items && !*abort_flag; item += npairs) {
         int e, n, row0;
         decode(item, e, n, row0);
-        const int b_row0 = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step;
+        const int a_row = row0 + (int)rank * BM;
+        const int b_row = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step + (rank ? p.b_second_offset : 0);
         for (int kb = 0; kb < k_blocks; ++kb, ++q) {
           const int s = q % STAGES;
           const uint32_t parity = ((q / STAGES) & 1) ^ 1;
@@ -204,26 +246,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             *abort_flag = 1;
             break;
           }
-          const uint32_t full = zb::smem_addr(&sh->full[s]);
+          const uint32_t full_local = zb::smem_addr(&sh->full[s]);
+          if (leader) zb::mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
+          const uint32_t full_leader = zb::mapa_shared(full_local, 0);
           const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
-          const uint32_t b_dst = a_dst + A_BYTES;
-          zb::mbar_arrive_expect_tx(full, STAGE_BYTES);
-          tma_load_2d(a_dst, &tmap_a, kb * BK, row0, full);
-          tma_load_2d(b_dst, &tmap_b, kb * BK, b_row0, full);
-          tma_load_2d(b_dst + B_BYTES / 2, &tmap_b, kb * BK, b_row0 + p.b_second_offset, full);
+          tma_load_2d_pair(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+          tma_load_2d_pair(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
         }
       }
-      // drain: wait (bounded) for the copies still in flight before the CTA may exit
-      for (uint32_t d = 0; d < STAGES && d < q; ++d) {
-        const uint32_t qq = q - 1 - d;
-        zb::mbar_wait_bounded(zb::smem_addr(&sh->full[qq % STAGES]), (qq / STAGES) & 1, nullptr, 0, 200000000ull);
+      if (leader) {  // drain: wait (bounded) for the copies still in flight before the CTA may exit
+        for (uint32_t d = 0; d < STAGES && d < q; ++d) {
+          const uint32_t qq = q - 1 - d;
+          zb::mbar_wait_bounded(zb::smem_addr(&sh->full[qq % STAGES]), (qq / STAGES) & 1, nullptr, 0, 200000000ull);
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {  // the pair's MMA issuer
       uint32_t q = 0;
       int it = 0;
-      for (int item = blockIdx.x; item < total_items && !*abort_flag; item += gridDim.x, ++it) {
+      for (int item = pair; item < total_items && !*abort_flag; item += npairs, ++it) {
         const int acc = it & 1;
         const uint32_t use = it >> 1;
         if (!zb::mbar_wait_bounded(zb::smem_addr(&sh->tmem_empty[acc]), (use & 1) ^ 1, p.status,
@@ -250,23 +292,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_mma(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), kIdesc,
                    (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(zb::smem_addr(&sh->empty[s]));
+          tc_commit_pair(zb::smem_addr(&sh->empty[s]), 0x3);  // stage s of both CTAs is free
         }
         if (!ok) break;
-        tc_commit(zb::smem_addr(&sh->tmem_full[acc]));
+        tc_commit_pair(zb::smem_addr(&sh->tmem_full[acc]), 0x3);
       }
       // every MMA issued by this thread has completed before TMEM is released
-      tc_commit(zb::smem_addr(&sh->drain));
+      tc_commit_pair(zb::smem_addr(&sh->drain), 0x1);
       zb::mbar_wait_bounded(zb::smem_addr(&sh->drain), 0, nullptr, 0, 200000000ull);
     }
   } else {
-    // epilogue warps 2..5: TMEM lane quarter (warp % 4)
-    const int quarter = warp % 4;
-    const int row_in_tile = quarter * 32 + lane;
+    // epilogue warps 2..9: TMEM lane quarter (warp % 4) of this CTA's 128 accumulator rows, column half
+    // (warp - 2) / 4 of the tile
+    const int quarter = warp % 4, chalf = (warp - 2) / 4;
+    const int row_in_tile = (int)rank * BM + quarter * 32 + lane;
     int it = 0;
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++it) {
+    for (int item = pair; item < total_items; item += npairs, ++it) {
       const int acc = it & 1;
       const uint32_t use = it >> 1;
+      // the tile's rows (and, for the down projection, their pairs and routing weights) are looked up while the
+      // MMAs still run
+      int e, n, row0;
+      decode(item, e, n, row0);
+      const int64_t row = row0 + row_in_tile;
+      const bool valid = row < sh->row_off[e + 1];  // rows past the expert's group belong to the next expert
+      int pr = -1;
+      float w = 0.f;
+      if (MODE == kDown) {
+        pr = valid ? p.sorted_pairs[row] : -1;
+        w = pr >= 0 ? p.weights[pr] : 0.f;
+      }
       bool ok = !*abort_flag &&
                 zb::mbar_wait_bounded(zb::smem_addr(&sh->tmem_full[acc]), use & 1, p.status, zb::kStatusGemmTimeout);
       // the tcgen05.ld below are warp-collective: every lane takes the same branch
@@ -275,35 +330,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      int e, n, row0;
-      decode(item, e, n, row0);
-      const int64_t row = row0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (MODE == kSwiGLU) {
         __nv_bfloat16* dst = p.out + row * p.out_stride + (int64_t)n * 128;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
+        for (int c = chalf * 64; c < chalf * 64 + 64; c += 32) {
           float gate[32], up[32];
           tmem_ld32(t_row + c, gate);
           tmem_ld32(t_row + 128 + c, up);
+          if (valid) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float h[8];
+            for (int j = 0; j < 32; j += 8) {
+              float h[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              h[i] = silu(zb::bf16_round(gate[j + i])) * zb::bf16_round(up[j + i]);
-            *reinterpret_cast<uint4*>(dst + c + j) = zb::pack_bf16x8(h);
+              for (int i = 0; i < 8; ++i)
+                h[i] = silu(zb::bf16_round(gate[j + i])) * zb::bf16_round(up[j + i]);
+              *reinterpret_cast<uint4*>(dst + c + j) = zb::pack_bf16x8(h);
+            }
           }
         }
       } else {
-        const int pair = p.sorted_pairs[row];
-        const float w = pair >= 0 ? p.weights[pair] : 0.f;
-        __nv_bfloat16* dst = p.out + (int64_t)(pair >= 0 ? pair : 0) * p.out_stride + (int64_t)n * BN;
+        __nv_bfloat16* dst = p.out + (int64_t)(pr >= 0 ? pr : 0) * p.out_stride + (int64_t)n * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN && n * BN + c < p.out_cols; c += 32) {
+        for (int c = chalf * (BN / 2); c < chalf * (BN / 2) + BN / 2 && n * BN + c < p.out_cols; c += 32) {
           float y[32];
           tmem_ld32(t_row + c, y);
-          if (pair >= 0) {
+          if (pr >= 0) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
               float o[8];
@@ -316,11 +368,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) zb::mbar_arrive(zb::smem_addr(&sh->tmem_empty[acc]));
+      if (lane == 0) mbar_arrive_cluster(zb::mapa_shared(zb::smem_addr(&sh->tmem_empty[acc]), 0));
     }
   }
   tc_fence_before();
   __syncthreads();
+  zb::cluster_arrive_relaxed();  // neither CTA frees TMEM or exits while the pair may still use it
+  zb::cluster_wait();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -369,10 +423,24 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int6
     ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
-  const int64_t upper_items = capacity / BM * p.n_tiles;
-  const int grid = (int)std::min<int64_t>(upper_items, zb::sm_count());
-  if (grid <= 0) return zb::kOk;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, b, p);
+  // the persistent loop assumes every pair is resident at once: as many pairs as the GPU co-schedules (a pair
+  // needs two SMs of one GPC), cached per device
+  static int resident_pairs[64] = {0};
+  int max_pairs = dev >= 0 && dev < 64 ? resident_pairs[dev] : 0;
+  if (max_pairs == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    ZB_CUDA(cudaOccupancyMaxActiveClusters(&max_pairs, kernel, &cfg));
+    if (max_pairs < 1) return zb::fail(zb::kUnsupported, "moe_gemm: no CTA pair fits on this GPU");
+    if (dev >= 0 && dev < 64) resident_pairs[dev] = max_pairs;
+  }
+  // pair tiles: at most half of the 128-row tiles plus one per expert
+  const int64_t upper_items = (capacity / BM / 2 + p.E) * p.n_tiles;
+  const int pairs = (int)std::min<int64_t>(upper_items, max_pairs);
+  if (pairs <= 0) return zb::kOk;
+  kernel<<<2 * pairs, kThreads, kSmemBytes, stream>>>(a, b, p);
   return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
 }
 
