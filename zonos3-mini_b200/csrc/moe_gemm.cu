@@ -37,6 +37,7 @@ namespace {
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
 constexpr int PAIR_M = 2 * BM;                 // rows of a pair tile
 constexpr int kEpilogueWarps = 8;               // two per TMEM lane quarter, each half of the columns
+constexpr uint32_t kStageOutBytes = 32 * 64;     // per epilogue warp: 32 rows x 32 bf16 output columns
 constexpr int kThreads = (2 + kEpilogueWarps) * 32;
 constexpr uint32_t A_BYTES = BM * BK * 2;      // 16 KB: this CTA's A rows
 constexpr uint32_t B_BYTES = BM * BK * 2;      // 16 KB: this CTA's half of the 256 B rows
@@ -163,6 +164,7 @@ struct Shared {
   int item_start[kMaxExperts + 1];  // first work item of each expert (pair tiles x n-tiles)
   int row_off[kMaxExperts + 1];     // padded row offsets
 };
+constexpr uint32_t kSharedBytes = (sizeof(Shared) + 127) / 128 * 128;
 
 template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -175,6 +177,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
   unsigned char* stages = smem_raw + pad;
   Shared* sh = reinterpret_cast<Shared*>(stages + STAGES * STAGE_BYTES);
+  // [kEpilogueWarps][32 rows x 64 B], 128-byte aligned after the barrier block
+  unsigned char* out_stage = stages + STAGES * STAGE_BYTES + kSharedBytes;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const uint32_t rank = blockIdx.x & 1;  // cluster of 2 along x: rank 0 leads the pair
   const bool leader = rank == 0;
@@ -350,20 +354,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        __nv_bfloat16* dst = p.out + (int64_t)(pr >= 0 ? pr : 0) * p.out_stride + (int64_t)n * BN;
+        // rows go to scattered pair slots: each 32-column chunk of the warp's 32 rows is staged in shared memory
+        // (16-byte units swizzled by row so that neither the row-wise writes nor the column-wise reads conflict)
+        // and written back as 64-byte row segments, four lanes per row
+        unsigned char* stg = out_stage + (warp - 2) * kStageOutBytes;
+        const int sub = lane & 3, rsub = lane >> 2;
 #pragma unroll 1
         for (int c = chalf * (BN / 2); c < chalf * (BN / 2) + BN / 2 && n * BN + c < p.out_cols; c += 32) {
           float y[32];
           tmem_ld32(t_row + c, y);
-          if (pr >= 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float o[8];
+          for (int j = 0; j < 4; ++j) {
+            float o[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) o[i] = y[j + i] * w;
-              *reinterpret_cast<uint4*>(dst + c + j) = zb::pack_bf16x8(o);
-            }
+            for (int i = 0; i < 8; ++i) o[i] = y[8 * j + i] * w;
+            const int unit = 4 * (lane & 1) + (j ^ ((lane >> 1) & 3));
+            *reinterpret_cast<uint4*>(stg + (lane >> 1) * 128 + unit * 16) = zb::pack_bf16x8(o);
           }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int r = it * 8 + rsub;  // row of the warp handled by this lane; segment `sub`
+            const int rp = __shfl_sync(0xffffffffu, pr, r);
+            const int unit = 4 * (r & 1) + (sub ^ ((r >> 1) & 3));
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + (r >> 1) * 128 + unit * 16);
+            if (rp >= 0) *reinterpret_cast<uint4*>(p.out + (int64_t)rp * p.out_stride + (int64_t)n * BN + c + 8 * sub) = v;
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
@@ -410,7 +427,7 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   return zb::kOk;
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + sizeof(Shared);
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + kSharedBytes + kEpilogueWarps * kStageOutBytes;
 
 template <int MODE>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int64_t capacity,
