@@ -65,15 +65,21 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 template <int D>
 struct Smem {
   static constexpr int LB = D + 8;   // bf16 row length (elements): conflict-free fragment loads
-  static constexpr int LF = D + 4;   // fp32 row length of [*, D] arrays
   static constexpr int LC = C + 4;   // fp32 row length of [C, C] arrays
   __nv_bfloat16 q[C * LB];
   __nv_bfloat16 kb[2][C * LB];       // K, double-buffered across chunks
   __nv_bfloat16 v[C * LB];
-  float S[D * LF];                   // state, K-first: S[key][value]
+  static constexpr int LY = C + 8;   // bf16 row length of [value][t] arrays
+  // state S (K-first, S[key][value]) kept transposed and split, S^T[value][key] = Sh + Sl (bf16 hi + lo): the
+  // mma B fragments of K S0 and Q S0 load as 32-bit words, each element split once per chunk
+  __nv_bfloat16 Sh[D * LB];
+  __nv_bfloat16 Sl[D * LB];
   float T[C * LC];                   // A, then T = (I + A)^{-1}
   float P[C * LC];
-  float Z[C * LF];                   // Y = diag(beta)(V - diag(gamma) K S0), then U; scratch of the inverse
+  // Y = diag(beta)(V - diag(gamma) K S0), then U, transposed and split: Y^T[value][t] = Yh + Yl
+  // (fp32 scratch of the inverse before that)
+  __nv_bfloat16 Yh[D * LY];
+  __nv_bfloat16 Yl[D * LY];
   float G[C];                        // cumulative log decay inside the chunk
   float gam[C];                      // exp(G)
   float bet[C];
@@ -84,7 +90,7 @@ struct Smem {
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillParams p) {
   using SM = Smem<D>;
-  constexpr int LB = SM::LB, LF = SM::LF, LC = SM::LC;
+  constexpr int LB = SM::LB, LC = SM::LC, LY = SM::LY;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SM& sm = *reinterpret_cast<SM*>(smem_raw);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -101,7 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
     const int vi = i / D, ki = i % D;
     float s = 0.f;
     if (p.init_state) s = p.init_state[((slot * p.H + h) * D + vi) * (int64_t)D + ki];
-    sm.S[ki * LF + vi] = s;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+    sm.Sh[vi * LB + ki] = hi;
+    sm.Sl[vi * LB + ki] = __float2bfloat16_rn(s - __bfloat162float(hi));
   }
 
   auto load_rows = [&](__nv_bfloat16* dst, const __nv_bfloat16* src, int c) {
@@ -222,9 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
       __syncthreads();
       // (b) off-diagonal blocks: X_ij = -X_ii * sum_{k=j}^{i-1} A_ik X_kj, by distance i - j = 1, 2, 3.
       // Results park in Z (free here): block (i, j) at Z + blk(i, j) * 256, row-major 16 x 16; tmp after them.
-      float* X = sm.Z;
+      float* X = reinterpret_cast<float*>(sm.Yh);  // Y / U are not live during the inverse
       auto blk = [](int i, int jj) { return (i * (i - 1)) / 2 + jj; };  // (1,0)=0 (2,0)=1 (2,1)=2 (3,0)=3 ...
-      float* tmp = sm.Z + 6 * 256;
+      float* tmp = X + 6 * 256;
       auto Xat = [&](int i, int jj, int r, int cc) -> float {
         return i == jj ? sm.T[(16 * i + r) * LC + 16 * jj + cc] : X[blk(i, jj) * 256 + r * 16 + cc];
       };
@@ -281,10 +289,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
         aQ[3] = *reinterpret_cast<const uint32_t*>(sm.q + (r0 + 8) * LB + k0 + 2 * tq + 8);
 #pragma unroll
         for (int n = 0; n < NW; ++n) {
-          const int col = cbase + 8 * n + g8;  // B[kk][n] = S[k0 + kk][col]
+          const int col = cbase + 8 * n + g8;  // B[kk][n] = S[k0 + kk][col] = S^T[col][k0 + kk]
+          const __nv_bfloat16* sh = sm.Sh + col * LB + k0 + 2 * tq;
+          const __nv_bfloat16* sl = sm.Sl + col * LB + k0 + 2 * tq;
           uint32_t bh[2], bl[2];
-          split2(sm.S[(k0 + 2 * tq) * LF + col], sm.S[(k0 + 2 * tq + 1) * LF + col], bh[0], bl[0]);
-          split2(sm.S[(k0 + 2 * tq + 8) * LF + col], sm.S[(k0 + 2 * tq + 9) * LF + col], bh[1], bl[1]);
+          bh[0] = *reinterpret_cast<const uint32_t*>(sh);
+          bh[1] = *reinterpret_cast<const uint32_t*>(sh + 8);
+          bl[0] = *reinterpret_cast<const uint32_t*>(sl);
+          bl[1] = *reinterpret_cast<const uint32_t*>(sl + 8);
           mma16816(accK[n], aK, bh);
           mma16816(accK[n], aK, bl);
           mma16816(oacc[n], aQ, bh);
@@ -298,7 +310,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
           const int t = 16 * mt + g8 + (e >= 2 ? 8 : 0);
           const int col = cbase + 8 * n + 2 * tq + (e & 1);
           const float vv = __bfloat162float(sm.v[t * LB + col]);
-          sm.Z[t * LF + col] = sm.bet[t] * (vv - sm.gam[t] * accK[n][e]);
+          const float y = sm.bet[t] * (vv - sm.gam[t] * accK[n][e]);
+          const __nv_bfloat16 hi = __float2bfloat16_rn(y);
+          sm.Yh[col * LY + t] = hi;
+          sm.Yl[col * LY + t] = __float2bfloat16_rn(y - __bfloat162float(hi));
           oacc[n][e] *= sm.gam[t] * p.scale;
         }
       }
@@ -323,10 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
         split2(sm.T[(r0 + 8) * LC + k0 + 2 * tq + 8], sm.T[(r0 + 8) * LC + k0 + 2 * tq + 9], ah[3], al[3]);
 #pragma unroll
         for (int n = 0; n < NW; ++n) {
-          const int col = cbase + 8 * n + g8;  // B[kk][n] = Y[k0 + kk][col]
+          const int col = cbase + 8 * n + g8;  // B[kk][n] = Y[k0 + kk][col] = Y^T[col][k0 + kk]
+          const __nv_bfloat16* yh = sm.Yh + col * LY + k0 + 2 * tq;
+          const __nv_bfloat16* yl = sm.Yl + col * LY + k0 + 2 * tq;
           uint32_t bh[2], bl[2];
-          split2(sm.Z[(k0 + 2 * tq) * LF + col], sm.Z[(k0 + 2 * tq + 1) * LF + col], bh[0], bl[0]);
-          split2(sm.Z[(k0 + 2 * tq + 8) * LF + col], sm.Z[(k0 + 2 * tq + 9) * LF + col], bh[1], bl[1]);
+          bh[0] = *reinterpret_cast<const uint32_t*>(yh);
+          bh[1] = *reinterpret_cast<const uint32_t*>(yh + 8);
+          bl[0] = *reinterpret_cast<const uint32_t*>(yl);
+          bl[1] = *reinterpret_cast<const uint32_t*>(yl + 8);
           mma16816(accU[n], ah, bh);
           mma16816(accU[n], ah, bl);
           mma16816(accU[n], al, bh);
@@ -339,7 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
         for (int e = 0; e < 4; ++e) {
           const int t = 16 * mt + g8 + (e >= 2 ? 8 : 0);
           const int col = cbase + 8 * n + 2 * tq + (e & 1);
-          sm.Z[t * LF + col] = accU[n][e];
+          const __nv_bfloat16 hi = __float2bfloat16_rn(accU[n][e]);
+          sm.Yh[col * LY + t] = hi;
+          sm.Yl[col * LY + t] = __float2bfloat16_rn(accU[n][e] - __bfloat162float(hi));
         }
       }
     }
@@ -356,10 +377,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
         split2(sm.P[(r0 + 8) * LC + k0 + 2 * tq + 8], sm.P[(r0 + 8) * LC + k0 + 2 * tq + 9], ah[3], al[3]);
 #pragma unroll
         for (int n = 0; n < NW; ++n) {
-          const int col = cbase + 8 * n + g8;
+          const int col = cbase + 8 * n + g8;  // B[kk][n] = U[k0 + kk][col] = U^T[col][k0 + kk]
+          const __nv_bfloat16* uh = sm.Yh + col * LY + k0 + 2 * tq;
+          const __nv_bfloat16* ul = sm.Yl + col * LY + k0 + 2 * tq;
           uint32_t bh[2], bl[2];
-          split2(sm.Z[(k0 + 2 * tq) * LF + col], sm.Z[(k0 + 2 * tq + 1) * LF + col], bh[0], bl[0]);
-          split2(sm.Z[(k0 + 2 * tq + 8) * LF + col], sm.Z[(k0 + 2 * tq + 9) * LF + col], bh[1], bl[1]);
+          bh[0] = *reinterpret_cast<const uint32_t*>(uh);
+          bh[1] = *reinterpret_cast<const uint32_t*>(uh + 8);
+          bl[0] = *reinterpret_cast<const uint32_t*>(ul);
+          bl[1] = *reinterpret_cast<const uint32_t*>(ul + 8);
           mma16816(oacc[n], ah, bh);
           mma16816(oacc[n], ah, bl);
           mma16816(oacc[n], al, bh);
@@ -394,27 +419,33 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int row = m0 + g8 + (e >= 2 ? 8 : 0), col = 8 * n + 2 * tq + (e & 1);
-            acc[n][e] = gamC * sm.S[row * LF + col];
+            acc[n][e] = gamC * (__bfloat162float(sm.Sh[col * LB + row]) + __bfloat162float(sm.Sl[col * LB + row]));
           }
         }
 #pragma unroll
         for (int k0 = 0; k0 < C; k0 += 16) {
-          // A[m][kk] = K[k0 + kk][m0 + m] (K^T), assembled from 16-bit reads
-          uint32_t a[4];
-          a[0] = pack2(K[(k0 + 2 * tq) * LB + m0 + g8], K[(k0 + 2 * tq + 1) * LB + m0 + g8]);
-          a[1] = pack2(K[(k0 + 2 * tq) * LB + m0 + g8 + 8], K[(k0 + 2 * tq + 1) * LB + m0 + g8 + 8]);
-          a[2] = pack2(K[(k0 + 2 * tq + 8) * LB + m0 + g8], K[(k0 + 2 * tq + 9) * LB + m0 + g8]);
-          a[3] = pack2(K[(k0 + 2 * tq + 8) * LB + m0 + g8 + 8], K[(k0 + 2 * tq + 9) * LB + m0 + g8 + 8]);
+          // A[m][kk] = exp(G_C - G_t) K[t = k0 + kk][m0 + m] (diag(f) K, transposed), split into bf16 hi + lo
           const float f0 = expf(gC - sm.G[k0 + 2 * tq]), f1 = expf(gC - sm.G[k0 + 2 * tq + 1]);
           const float f8 = expf(gC - sm.G[k0 + 2 * tq + 8]), f9 = expf(gC - sm.G[k0 + 2 * tq + 9]);
+          auto kv = [&](int t, int m) { return __bfloat162float(K[t * LB + m0 + m]); };
+          uint32_t ah[4], al[4];
+          split2(f0 * kv(k0 + 2 * tq, g8), f1 * kv(k0 + 2 * tq + 1, g8), ah[0], al[0]);
+          split2(f0 * kv(k0 + 2 * tq, g8 + 8), f1 * kv(k0 + 2 * tq + 1, g8 + 8), ah[1], al[1]);
+          split2(f8 * kv(k0 + 2 * tq + 8, g8), f9 * kv(k0 + 2 * tq + 9, g8), ah[2], al[2]);
+          split2(f8 * kv(k0 + 2 * tq + 8, g8 + 8), f9 * kv(k0 + 2 * tq + 9, g8 + 8), ah[3], al[3]);
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
-            const int col = 8 * n + g8;  // B[kk][n] = f(kk) U[k0 + kk][col]
+            const int col = 8 * n + g8;  // B[kk][n] = U[k0 + kk][col] = U^T[col][k0 + kk]
+            const __nv_bfloat16* uh = sm.Yh + col * LY + k0 + 2 * tq;
+            const __nv_bfloat16* ul = sm.Yl + col * LY + k0 + 2 * tq;
             uint32_t bh[2], bl[2];
-            split2(f0 * sm.Z[(k0 + 2 * tq) * LF + col], f1 * sm.Z[(k0 + 2 * tq + 1) * LF + col], bh[0], bl[0]);
-            split2(f8 * sm.Z[(k0 + 2 * tq + 8) * LF + col], f9 * sm.Z[(k0 + 2 * tq + 9) * LF + col], bh[1], bl[1]);
-            mma16816(acc[n], a, bh);
-            mma16816(acc[n], a, bl);
+            bh[0] = *reinterpret_cast<const uint32_t*>(uh);
+            bh[1] = *reinterpret_cast<const uint32_t*>(uh + 8);
+            bl[0] = *reinterpret_cast<const uint32_t*>(ul);
+            bl[1] = *reinterpret_cast<const uint32_t*>(ul + 8);
+            mma16816(acc[n], ah, bh);
+            mma16816(acc[n], ah, bl);
+            mma16816(acc[n], al, bh);
           }
         }
       }
@@ -425,7 +456,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int row = m0 + g8 + (e >= 2 ? 8 : 0), col = 8 * n + 2 * tq + (e & 1);
-            sm.S[row * LF + col] = acc[n][e];
+            const __nv_bfloat16 hi = __float2bfloat16_rn(acc[n][e]);
+            sm.Sh[col * LB + row] = hi;
+            sm.Sl[col * LB + row] = __float2bfloat16_rn(acc[n][e] - __bfloat162float(hi));
           }
         }
       }
@@ -436,7 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
   if (p.final_state) {
     for (int i = tid; i < D * D; i += kThreads) {
       const int vi = i / D, ki = i % D;
-      p.final_state[((slot * p.H + h) * D + vi) * (int64_t)D + ki] = sm.S[ki * LF + vi];
+      p.final_state[((slot * p.H + h) * D + vi) * (int64_t)D + ki] =
+          __bfloat162float(sm.Sh[vi * LB + ki]) + __bfloat162float(sm.Sl[vi * LB + ki]);
     }
   }
 }
