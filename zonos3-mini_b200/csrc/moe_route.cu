@@ -16,8 +16,6 @@
 
 namespace {
 
-constexpr int kRouterTokens = 16;           // tokens of one router CTA (one m16 tile)
-constexpr int kChunk = 64;                   // K columns per smem chunk
 constexpr int kPad = 8;                      // row padding (elements) against bank conflicts
 constexpr int kMaxExperts = 128;
 
@@ -107,6 +105,164 @@ __device__ __forceinline__ void select_token(LogitFn logit, const float* bias, i
   }
 }
 
+// The top-k of NT tokens by one warp at once (their shuffle reductions interleave): token i's expert e logit is
+// logits[i * row_stride + e]; tokens i >= nt are skipped. Same selection and weights as select_token.
+template <int NT>
+__device__ __forceinline__ void select_tokens(const float* logits, int row_stride, int nt, const float* bias, int E,
+                                              int k, int mode, int renorm, int32_t* ids_out, float* w_out) {
+  const int lane = threadIdx.x % 32;
+  float lg[NT][kMaxExperts / 32];
+  unsigned long long key[NT][kMaxExperts / 32];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int e = lane + 32 * j;
+      if (i < nt && e < E) {
+        lg[i][j] = logits[i * row_stride + e];
+        key[i][j] = score_key(lg[i][j] - (bias ? bias[e] : 0.f), e);
+      } else {
+        lg[i][j] = -INFINITY;
+        key[i][j] = 0ull;
+      }
+    }
+  }
+  float sel_logit[NT];
+  int sel_id[NT];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    sel_logit[i] = 0.f;
+    sel_id[i] = 0;
+  }
+  for (int r = 0; r < k; ++r) {
+    unsigned long long best[NT];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      best[i] = 0ull;
+#pragma unroll
+      for (int j = 0; j < kMaxExperts / 32; ++j) best[i] = key[i][j] > best[i] ? key[i][j] : best[i];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best[i], off);
+        best[i] = o > best[i] ? o : best[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const int e = (int)(0xFFFFFFFFu - (unsigned)(best[i] & 0xFFFFFFFFull));
+      float l = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxExperts / 32; ++j) {
+        if (lane + 32 * j == e) {
+          l = lg[i][j];
+          key[i][j] = 0ull;  // removed
+        }
+      }
+      l = __shfl_sync(0xffffffffu, l, e % 32);
+      if (lane == r) {
+        sel_logit[i] = l;
+        sel_id[i] = e;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    float w;
+    if (mode == kSelectedSoftmax) {
+      float m = lane < k ? sel_logit[i] : -INFINITY;
+      m = zb::warp_max(m);
+      const float ex = lane < k ? expf(sel_logit[i] - m) : 0.f;
+      w = ex / zb::warp_sum(ex);
+    } else {
+      float m = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kMaxExperts / 32; ++j) m = fmaxf(m, lg[i][j]);
+      m = zb::warp_max(m);
+      float den = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxExperts / 32; ++j)
+        if (lane + 32 * j < E) den += expf(lg[i][j] - m);
+      den = zb::warp_sum(den);
+      w = lane < k ? expf(sel_logit[i] - m) / den : 0.f;
+    }
+    if (renorm) {
+      const float total = zb::warp_sum(lane < k ? w : 0.f);
+      w = w / (total + 1e-8f);
+    }
+    if (i < nt && lane < k) {
+      ids_out[i * k + lane] = sel_id[i];
+      w_out[i * k + lane] = w;
+    }
+  }
+}
+
+// The top-k of NT tokens with E <= 64 by one warp (lane l holds experts l and l + 32): every key counts the keys
+// above it (all 64 compared, no serial rounds; keys are unique, so the ranks are a permutation), the winners of
+// ranks < k are placed through `slots` ([NT][k] shared scratch of this warp), then weights as select_token.
+template <int NT>
+__device__ __forceinline__ void select_tokens_rank(const float* logits, int row_stride, int nt, const float* bias,
+                                                   int E, int k, int mode, int renorm, int32_t* ids_out,
+                                                   float* w_out, float2* slots) {
+  const int lane = threadIdx.x % 32;
+  unsigned long long ka[NT], kb[NT];
+  float la[NT], lb[NT];
+  int ra[NT], rb[NT];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int e0 = lane, e1 = lane + 32;
+    la[i] = (i < nt && e0 < E) ? logits[i * row_stride + e0] : -INFINITY;
+    lb[i] = (i < nt && e1 < E) ? logits[i * row_stride + e1] : -INFINITY;
+    ka[i] = e0 < E ? score_key(la[i] - (bias ? bias[e0] : 0.f), e0) : 0ull;
+    kb[i] = e1 < E ? score_key(lb[i] - (bias ? bias[e1] : 0.f), e1) : 0ull;
+    ra[i] = rb[i] = 0;
+  }
+#pragma unroll 4
+  for (int src = 0; src < 32; ++src) {
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const unsigned long long x = __shfl_sync(0xffffffffu, ka[i], src);
+      const unsigned long long y = __shfl_sync(0xffffffffu, kb[i], src);
+      ra[i] += (x > ka[i]) + (y > ka[i]);
+      rb[i] += (x > kb[i]) + (y > kb[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    if (ra[i] < k) slots[i * k + ra[i]] = make_float2(la[i], __int_as_float(lane));
+    if (rb[i] < k) slots[i * k + rb[i]] = make_float2(lb[i], __int_as_float(lane + 32));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const float2 sl = lane < k ? slots[i * k + lane] : make_float2(0.f, 0.f);
+    const float sel_logit = sl.x;
+    const int sel_id = __float_as_int(sl.y);
+    float w;
+    if (mode == kSelectedSoftmax) {
+      float m = lane < k ? sel_logit : -INFINITY;
+      m = zb::warp_max(m);
+      const float ex = lane < k ? expf(sel_logit - m) : 0.f;
+      w = ex / zb::warp_sum(ex);
+    } else {
+      const float m = zb::warp_max(fmaxf(la[i], lb[i]));
+      float den = (lane < E ? expf(la[i] - m) : 0.f) + (lane + 32 < E ? expf(lb[i] - m) : 0.f);
+      den = zb::warp_sum(den);
+      w = lane < k ? expf(sel_logit - m) / den : 0.f;
+    }
+    if (renorm) {
+      const float total = zb::warp_sum(lane < k ? w : 0.f);
+      w = w / (total + 1e-8f);
+    }
+    if (i < nt && lane < k) {
+      ids_out[i * k + lane] = sel_id;
+      w_out[i * k + lane] = w;
+    }
+  }
+}
+
 struct RouterParams {
   const __nv_bfloat16* x;
   int64_t x_stride;
@@ -146,143 +302,175 @@ __device__ __forceinline__ uint32_t scale_bf16x2(uint32_t raw, float s, uint32_t
   return *reinterpret_cast<uint32_t*>(&o);
 }
 
-constexpr int kRouterThreads = 128;  // 4 warps, each a quarter of the experts
-constexpr int kRouterStages = 4;
-constexpr int kRow = kChunk + kPad;  // smem row length (elements)
+constexpr int kRouterThreads = 256;  // 8 warps
+constexpr int kRouterStages = 4;     // router-weight chunks in flight
+constexpr int kRouterChunk = 128;    // columns of a router-weight chunk
+constexpr int kRouterWRow = kRouterChunk + kPad;
+constexpr size_t kRouterSmemBudget = 220 * 1024;
 
-// One CTA routes 16 tokens. A 4-stage cp.async pipeline streams K chunks of x [16 x 64], the router weight
-// [NE x 64] and the norm weight [64]; warp w computes the logits of experts [w*8*NH, (w+1)*8*NH) for the 16 tokens
-// with mma.sync m16n8k16 (bf16 in, fp32 accumulate), the A fragments scaled by inv_rms * norm weight in registers.
-// The inverse RMS of the tokens comes first (4 tokens per warp, 8 independent 16-byte loads per lane in flight),
-// and every warp then selects the top-k of 4 tokens.
-template <int NH>  // n-tiles (8 experts each) per warp: E <= 32 * NH
+size_t router_smem(int TOK, int NE, int D) {
+  return (size_t)TOK * (D + kPad) * 2 + (size_t)D * 2 + (size_t)kRouterStages * NE * kRouterWRow * 2 +
+         (size_t)TOK * 4 + (size_t)TOK * (NE + 1) * 4;
+}
+
+// One CTA routes TOK tokens (32, or 16 for wide rows). Its [TOK x D] block of x is loaded into shared memory once
+// (cp.async, next to the norm weight) while the first router-weight chunks start streaming; 8 threads per row
+// (16 for TOK = 16) form the inverse RMS from shared memory and every element becomes the router input
+// bf16(x * inv_rms * rmsnorm_eda.weight) once, in place. The router weight then streams through a 4-stage ring of
+// [NE x 128] chunks; warp w computes the logits of token tile (w % MT) x its expert group with mma.sync m16n8k16
+// (bf16 in, fp32 accumulate). Logits are rounded to bf16 (the router_linear output dtype) and each warp selects
+// the top-k of TOK / 8 tokens at once.
+template <int NH, int TOK>
 __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(RouterParams p) {
-  constexpr int NE = 32 * NH;  // experts covered by the CTA
+  constexpr int NE = 32 * NH;           // experts covered by the CTA
+  constexpr int MT = TOK / 16;          // token tiles
+  constexpr int NG = 8 / MT;            // expert groups
+  constexpr int NPW = NE / 8 / NG > 0 ? NE / 8 / NG : 1;  // n-tiles (8 experts) of a warp
+  constexpr int TPW = TOK / 8;          // tokens selected by a warp
+  const int D = p.D, LX = D + kPad;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __nv_bfloat16* a_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);               // [stages][16][kRow]
-  __nv_bfloat16* b_s = a_s + kRouterStages * kRouterTokens * kRow;                // [stages][NE][kRow]
-  __nv_bfloat16* w_s = b_s + kRouterStages * NE * kRow;                            // [stages][kChunk]
-  float* rms_s = reinterpret_cast<float*>(w_s + kRouterStages * kChunk);          // [16]
-  float* logit_s = rms_s + kRouterTokens;                                         // [16][NE + 1]
+  __nv_bfloat16* x_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);                // [TOK][LX]
+  __nv_bfloat16* nw_s = x_s + (size_t)TOK * LX;                                    // [D]
+  __nv_bfloat16* w_s = nw_s + D;                                                   // [stages][NE][kRouterWRow]
+  float* rms_s = reinterpret_cast<float*>(w_s + (size_t)kRouterStages * NE * kRouterWRow);  // [TOK]
+  float* logit_s = rms_s + TOK;                                                    // [TOK][NE + 1]
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int tok0 = blockIdx.x * kRouterTokens;
-  const int n_chunks = p.D / kChunk;
+  const int tok0 = blockIdx.x * TOK;
+  const int vecs = D / 8;
+  const int n_chunks = D / kRouterChunk;
 
-  auto load_chunk = [&](int chunk, int stage) {
-    const int k0 = chunk * kChunk;
-    __nv_bfloat16* a = a_s + stage * kRouterTokens * kRow;
-    __nv_bfloat16* b = b_s + stage * NE * kRow;
-    for (int idx = tid; idx < kRouterTokens * (kChunk / 8); idx += kRouterThreads) {
-      const int r = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
-      const int t = tok0 + r;
-      cp_async16(a + r * kRow + c, p.x + (int64_t)(t < p.T ? t : 0) * p.x_stride + k0 + c, t < p.T);
+  // CTAs walk the router-weight chunks from different starting points, so they do not all request the same L2
+  // lines at once (each token's logits still sum its chunks in one fixed order)
+  const int rot = (int)(blockIdx.x % (unsigned)(n_chunks > 0 ? n_chunks : 1));
+  auto load_w = [&](int chunk, int stage) {
+    const int k0 = ((chunk + rot) % n_chunks) * kRouterChunk;
+    __nv_bfloat16* b = w_s + (size_t)stage * NE * kRouterWRow;
+    for (int idx = tid; idx < NE * (kRouterChunk / 8); idx += kRouterThreads) {
+      const int e = idx / (kRouterChunk / 8), c = (idx % (kRouterChunk / 8)) * 8;
+      cp_async16(b + e * kRouterWRow + c, p.w_router + (int64_t)(e < p.E ? e : 0) * D + k0 + c, e < p.E);
     }
-    for (int idx = tid; idx < NE * (kChunk / 8); idx += kRouterThreads) {
-      const int e = idx / (kChunk / 8), c = (idx % (kChunk / 8)) * 8;
-      cp_async16(b + e * kRow + c, p.w_router + (int64_t)(e < p.E ? e : 0) * p.D + k0 + c, e < p.E);
-    }
-    if (tid < kChunk / 8) cp_async16(w_s + stage * kChunk + tid * 8, p.norm_w + k0 + tid * 8, true);
   };
-
-  // prologue: start the first stages while the inverse RMS is computed
+  // x block and norm weight (group 0), then the first router-weight chunks
+  for (int idx = tid; idx < TOK * vecs; idx += kRouterThreads) {
+    const int r = idx / vecs, c = (idx % vecs) * 8;
+    const int t = tok0 + r;
+    cp_async16(x_s + (size_t)r * LX + c, p.x + (int64_t)(t < p.T ? t : 0) * p.x_stride + c, t < p.T);
+  }
+  for (int idx = tid; idx < vecs; idx += kRouterThreads) cp_async16(nw_s + idx * 8, p.norm_w + idx * 8, true);
+  cp_async_commit();
 #pragma unroll
-  for (int s = 0; s < kRouterStages - 1; ++s) {
-    if (s < n_chunks) load_chunk(s, s);
+  for (int st = 0; st < kRouterStages - 1; ++st) {
+    if (st < n_chunks) load_w(st, st);
     cp_async_commit();
   }
-  for (int r = warp; r < kRouterTokens; r += kRouterThreads / 32) {
-    const int t = tok0 + r;
+  cp_async_wait<kRouterStages - 1>();  // the x block has landed
+  __syncthreads();
+  {  // inverse RMS of every row: 256 / TOK threads per row
+    constexpr int TPR = kRouterThreads / TOK;
+    const int r = tid / TPR, part = tid % TPR;
+    const uint4* row = reinterpret_cast<const uint4*>(x_s + (size_t)r * LX);
     float ss = 0.f;
-    if (t < p.T) {
-      const __nv_bfloat16* row = p.x + (int64_t)t * p.x_stride;
-      for (int c0 = lane * 8; c0 < p.D; c0 += 256 * 8) {
-        float v[8][8];
+    for (int j = part; j < vecs; j += TPR) {
+      float f[8];
+      const uint4 v = row[j];
+      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v), f);
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (c0 + u * 256 < p.D) zb::ld_bf16x8(row + c0 + u * 256, v[u]);
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (c0 + u * 256 < p.D)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(v[u][j], v[u][j], ss);
-      }
+      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
     }
-    ss = zb::warp_sum(ss);
-    if (lane == 0) rms_s[r] = rsqrtf(ss / (float)p.D + p.eps);
+#pragma unroll
+    for (int off = 1; off < TPR; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (part == 0) rms_s[r] = rsqrtf(ss / (float)D + p.eps);
   }
   __syncthreads();
+  for (int idx = tid; idx < TOK * vecs; idx += kRouterThreads) {  // the router input, in place
+    const int r = idx / vecs, c = (idx % vecs) * 8;
+    uint4* cell = reinterpret_cast<uint4*>(x_s + (size_t)r * LX + c);
+    const uint4 raw = *cell, wr = *reinterpret_cast<const uint4*>(nw_s + c);
+    const float s = rms_s[r];
+    *cell = make_uint4(scale_bf16x2(raw.x, s, wr.x), scale_bf16x2(raw.y, s, wr.y), scale_bf16x2(raw.z, s, wr.z),
+                       scale_bf16x2(raw.w, s, wr.w));
+  }
 
-  const int nbase = warp * NH;  // first n-tile of this warp
+  const int mt = warp % MT, nbase = (warp / MT) * NPW;  // token tile, first n-tile of this warp
   const int g = lane >> 2, tq = lane & 3;
-  const float s_lo = rms_s[g], s_hi = rms_s[g + 8];
-  float acc[NH][4];
+  float acc[NPW][4];
 #pragma unroll
-  for (int n = 0; n < NH; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-
+  for (int n = 0; n < NPW; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const __nv_bfloat16* a = x_s + (size_t)(mt * 16) * LX;
   for (int chunk = 0; chunk < n_chunks; ++chunk) {
     const int stage = chunk % kRouterStages;
-    cp_async_wait<kRouterStages - 2>();
-    __syncthreads();
-    // refill the stage consumed in the previous iteration
+    cp_async_wait<kRouterStages - 2>();  // this chunk has landed
+    __syncthreads();                      // (first pass: the router input is complete) the previous stage is free
     const int next = chunk + kRouterStages - 1;
-    if (next < n_chunks) load_chunk(next, next % kRouterStages);
+    if (next < n_chunks) load_w(next, next % kRouterStages);
     cp_async_commit();
     if (nbase * 8 >= p.E) continue;  // this warp's experts are all padding
-    const __nv_bfloat16* a = a_s + stage * kRouterTokens * kRow;
-    const __nv_bfloat16* b = b_s + stage * NE * kRow;
-    const __nv_bfloat16* wv = w_s + stage * kChunk;
+    const __nv_bfloat16* b = w_s + (size_t)stage * NE * kRouterWRow;
+    const int k0 = ((chunk + rot) % n_chunks) * kRouterChunk;
 #pragma unroll
-    for (int kk = 0; kk < kChunk; kk += 16) {
-      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(wv + kk + 2 * tq);
-      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(wv + kk + 2 * tq + 8);
+    for (int kk = 0; kk < kRouterChunk; kk += 16) {
       uint32_t af[4];
-      af[0] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + g * kRow + kk + 2 * tq), s_lo, w0);
-      af[1] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + (g + 8) * kRow + kk + 2 * tq), s_hi, w0);
-      af[2] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + g * kRow + kk + 2 * tq + 8), s_lo, w1);
-      af[3] = scale_bf16x2(*reinterpret_cast<const uint32_t*>(a + (g + 8) * kRow + kk + 2 * tq + 8), s_hi, w1);
+      af[0] = *reinterpret_cast<const uint32_t*>(a + g * LX + k0 + kk + 2 * tq);
+      af[1] = *reinterpret_cast<const uint32_t*>(a + (g + 8) * LX + k0 + kk + 2 * tq);
+      af[2] = *reinterpret_cast<const uint32_t*>(a + g * LX + k0 + kk + 2 * tq + 8);
+      af[3] = *reinterpret_cast<const uint32_t*>(a + (g + 8) * LX + k0 + kk + 2 * tq + 8);
 #pragma unroll
-      for (int n = 0; n < NH; ++n) {
+      for (int n = 0; n < NPW; ++n) {
         const int e = (nbase + n) * 8 + g;
         uint32_t bf[2];
-        bf[0] = *reinterpret_cast<const uint32_t*>(b + e * kRow + kk + 2 * tq);
-        bf[1] = *reinterpret_cast<const uint32_t*>(b + e * kRow + kk + 2 * tq + 8);
+        bf[0] = *reinterpret_cast<const uint32_t*>(b + e * kRouterWRow + kk + 2 * tq);
+        bf[1] = *reinterpret_cast<const uint32_t*>(b + e * kRouterWRow + kk + 2 * tq + 8);
         mma_bf16_16816(acc[n], af, bf);
       }
     }
   }
   cp_async_wait<0>();
   // logits rounded to bf16 (the router_linear output dtype)
+  if (nbase * 8 < NE) {
 #pragma unroll
-  for (int n = 0; n < NH; ++n) {
-    const int c0 = (nbase + n) * 8 + 2 * tq;
-    logit_s[g * (NE + 1) + c0] = zb::bf16_round(acc[n][0]);
-    logit_s[g * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][1]);
-    logit_s[(g + 8) * (NE + 1) + c0] = zb::bf16_round(acc[n][2]);
-    logit_s[(g + 8) * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][3]);
+    for (int n = 0; n < NPW; ++n) {
+      const int c0 = (nbase + n) * 8 + 2 * tq;
+      const int r0 = mt * 16 + g;
+      logit_s[r0 * (NE + 1) + c0] = zb::bf16_round(acc[n][0]);
+      logit_s[r0 * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][1]);
+      logit_s[(r0 + 8) * (NE + 1) + c0] = zb::bf16_round(acc[n][2]);
+      logit_s[(r0 + 8) * (NE + 1) + c0 + 1] = zb::bf16_round(acc[n][3]);
+    }
   }
   __syncthreads();
-  for (int r = warp; r < kRouterTokens; r += kRouterThreads / 32) {
-    const int t = tok0 + r;
-    if (t >= p.T) break;
-    const float* lrow = logit_s + r * (NE + 1);
-    if (p.logits_out) {
-      for (int e = lane; e < p.E; e += 32) p.logits_out[(int64_t)t * p.E + e] = __float2bfloat16_rn(lrow[e]);
-    }
-    select_token([&](int e) { return lrow[e]; }, p.bias, p.E, p.k, p.mode, p.renorm, p.ids + (int64_t)t * p.k,
-                 p.weights + (int64_t)t * p.k);
+  const int r0 = warp * TPW;
+  const int nt = min(TPW, p.T - (tok0 + r0));
+  if (nt <= 0) return;
+  if (p.logits_out) {
+    for (int i = 0; i < nt; ++i)
+      for (int e = lane; e < p.E; e += 32)
+        p.logits_out[(int64_t)(tok0 + r0 + i) * p.E + e] = __float2bfloat16_rn(logit_s[(r0 + i) * (NE + 1) + e]);
+  }
+  if (p.E <= 64) {  // slot scratch: the router-weight ring is free now
+    float2* slots = reinterpret_cast<float2*>(w_s) + warp * TPW * 32;
+    select_tokens_rank<TPW>(logit_s + r0 * (NE + 1), NE + 1, nt, p.bias, p.E, p.k, p.mode, p.renorm,
+                            p.ids + (int64_t)(tok0 + r0) * p.k, p.weights + (int64_t)(tok0 + r0) * p.k, slots);
+  } else {
+    select_tokens<TPW>(logit_s + r0 * (NE + 1), NE + 1, nt, p.bias, p.E, p.k, p.mode, p.renorm,
+                       p.ids + (int64_t)(tok0 + r0) * p.k, p.weights + (int64_t)(tok0 + r0) * p.k);
   }
 }
 
-template <int NH>
+template <int NH, int TOK>
 int launch_router(const RouterParams& p, cudaStream_t stream) {
-  constexpr int NE = 32 * NH;
-  const size_t smem = (size_t)kRouterStages * (kRouterTokens + NE) * kRow * 2 + kRouterStages * kChunk * 2 +
-                      kRouterTokens * 4 + (size_t)kRouterTokens * (NE + 1) * 4;
-  auto kernel = moe_router_kernel<NH>;
-  if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const unsigned grid = (unsigned)((p.T + kRouterTokens - 1) / kRouterTokens);
+  const size_t smem = router_smem(TOK, 32 * NH, p.D);
+  auto kernel = moe_router_kernel<NH, TOK>;
+  ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const unsigned grid = (unsigned)((p.T + TOK - 1) / TOK);
   kernel<<<grid, kRouterThreads, smem, stream>>>(p);
   return zb::check_launch("moe_router");
+}
+
+template <int NH>
+int launch_router_nh(const RouterParams& p, cudaStream_t stream) {
+  if (router_smem(32, 32 * NH, p.D) <= kRouterSmemBudget) return launch_router<NH, 32>(p, stream);
+  if (router_smem(16, 32 * NH, p.D) <= kRouterSmemBudget) return launch_router<NH, 16>(p, stream);
+  return zb::fail(zb::kUnsupported, "moe_router: D=%d with %d experts exceeds shared memory", p.D, 32 * NH);
 }
 
 struct SelectParams {
@@ -444,17 +632,28 @@ struct GatherParams {
   __nv_bfloat16* out;  // [rows, D]
 };
 
-// Row r of the permuted activations = x[sorted_pairs[r] / k] (zeros for padding rows); 16-byte vectors.
+// Row r of the permuted activations = x[sorted_pairs[r] / k] (zeros for padding rows). A warp copies whole rows:
+// the row's pair index is read once, then every lane keeps 8 independent 16-byte loads in flight.
 __global__ void __launch_bounds__(256) moe_gather_kernel(GatherParams p) {
+  const int lane = threadIdx.x % 32;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int vec_per_row = p.D / 8;
-  const int64_t total = p.rows * vec_per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vec_per_row;
-    const int c = (int)(i % vec_per_row) * 8;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < p.rows; r += warps) {
     const int pair = p.sorted_pairs[r];
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (pair >= 0) v = *reinterpret_cast<const uint4*>(p.x + (int64_t)(pair / p.k) * p.x_stride + c);
-    *reinterpret_cast<uint4*>(p.out + r * p.D + c) = v;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)(pair >= 0 ? pair / p.k : 0) * p.x_stride);
+    uint4* dst = reinterpret_cast<uint4*>(p.out + r * p.D);
+    for (int c0 = lane; c0 < vec_per_row; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + 32 * j;
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (pair >= 0 && c < vec_per_row) v[j] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + 32 * j < vec_per_row) dst[c0 + 32 * j] = v[j];
+    }
   }
 }
 
@@ -465,30 +664,45 @@ struct CombineParams {
   int64_t out_stride;
 };
 
-// out[t] = bf16( sum over slots of float(y[t * k + slot]) ), slots in order (the server's moe_sum_reduce).
+// out[t] = bf16( sum over slots of float(y[t * k + slot]) ), slots in order (the server's moe_sum_reduce). A warp
+// sums whole token rows: every lane keeps the 16-byte vectors of 2 columns x up to 8 slots in flight.
 __global__ void __launch_bounds__(256) moe_combine_kernel(CombineParams p) {
+  const int lane = threadIdx.x % 32;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int vec_per_row = p.D / 8;
-  const int64_t total = (int64_t)p.T * vec_per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / vec_per_row;
-    const int c = (int)(i % vec_per_row) * 8;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < p.k; s0 += 8) {  // up to 8 slot rows in flight, summed in slot order
-      uint4 raw[8];
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < p.T; t += warps) {
+    const uint4* rows = reinterpret_cast<const uint4*>(p.y + t * p.k * p.D);
+    uint4* dst = reinterpret_cast<uint4*>(p.out + t * p.out_stride);
+    for (int c0 = lane; c0 < vec_per_row; c0 += 64) {
+      const bool has1 = c0 + 32 < vec_per_row;
+      float acc0[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, acc1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int s0 = 0; s0 < p.k; s0 += 8) {
+        uint4 r0[8], r1[8];
 #pragma unroll
-      for (int s = 0; s < 8; ++s)
-        if (s0 + s < p.k) raw[s] = *reinterpret_cast<const uint4*>(p.y + (t * p.k + s0 + s) * p.D + c);
+        for (int s = 0; s < 8; ++s) {
+          if (s0 + s < p.k) {
+            r0[s] = __ldcs(rows + (int64_t)(s0 + s) * vec_per_row + c0);
+            if (has1) r1[s] = __ldcs(rows + (int64_t)(s0 + s) * vec_per_row + c0 + 32);
+          }
+        }
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s0 + s < p.k) {
-          float v[8];
-          zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&raw[s]), v);
+        for (int s = 0; s < 8; ++s) {
+          if (s0 + s < p.k) {
+            float v[8];
+            zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&r0[s]), v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] += v[j];
+            for (int j = 0; j < 8; ++j) acc0[j] += v[j];
+            if (has1) {
+              zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&r1[s]), v);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc1[j] += v[j];
+            }
+          }
         }
       }
+      dst[c0] = zb::pack_bf16x8(acc0);
+      if (has1) dst[c0 + 32] = zb::pack_bf16x8(acc1);
     }
-    *reinterpret_cast<uint4*>(p.out + t * p.out_stride + c) = zb::pack_bf16x8(acc);
   }
 }
 
@@ -504,8 +718,7 @@ ZB_API int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out,
   ZB_REQUIRE_ALIGNED(out, 16, "out");
   CombineParams p{reinterpret_cast<const __nv_bfloat16*>(y), T, k, D, reinterpret_cast<__nv_bfloat16*>(out),
                   out_stride};
-  const int64_t vecs = (int64_t)T * (D / 8);
-  const int64_t grid = std::min<int64_t>((vecs + 255) / 256, (int64_t)zb::sm_count() * 8);
+  const int64_t grid = std::min<int64_t>(((int64_t)T + 7) / 8, (int64_t)zb::sm_count() * 8);  // a warp per token
   moe_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
   return zb::check_launch("moe_combine");
 }
@@ -516,7 +729,8 @@ ZB_API int zb_moe_router(const uint16_t* x, int64_t x_stride, const uint16_t* no
   ZB_REQUIRE(T >= 0 && D > 0 && E > 0 && k > 0, "moe_router: bad sizes T=%d D=%d E=%d k=%d", T, D, E, k);
   if (E > kMaxExperts || k > E || k > 32)
     return zb::fail(zb::kUnsupported, "moe_router: E=%d k=%d (E <= %d, k <= min(E, 32))", E, k, kMaxExperts);
-  if (D % kChunk != 0) return zb::fail(zb::kUnsupported, "moe_router: D=%d must be a multiple of %d", D, kChunk);
+  if (D % kRouterChunk != 0)
+    return zb::fail(zb::kUnsupported, "moe_router: D=%d must be a multiple of %d", D, kRouterChunk);
   ZB_REQUIRE(weight_mode == kSelectedSoftmax || weight_mode == kFullSoftmax, "moe_router: weight_mode %d", weight_mode);
   if (T == 0) return zb::kOk;
   ZB_REQUIRE(x && norm_weight && w_router && ids && weights, "moe_router: null pointer");
@@ -529,9 +743,9 @@ ZB_API int zb_moe_router(const uint16_t* x, int64_t x_stride, const uint16_t* no
                  reinterpret_cast<const __nv_bfloat16*>(w_router), bias, T, D, E, k, weight_mode, renormalize,
                  reinterpret_cast<__nv_bfloat16*>(logits_out), ids, weights};
   const int nh = (E + 31) / 32;
-  if (nh <= 1) return launch_router<1>(p, stream);
-  if (nh <= 2) return launch_router<2>(p, stream);
-  return launch_router<4>(p, stream);
+  if (nh <= 1) return launch_router_nh<1>(p, stream);
+  if (nh <= 2) return launch_router_nh<2>(p, stream);
+  return launch_router_nh<4>(p, stream);
 }
 
 ZB_API int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T, int E, int k,
@@ -576,8 +790,7 @@ ZB_API int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sor
   ZB_REQUIRE_ALIGNED(out, 16, "out");
   GatherParams p{reinterpret_cast<const __nv_bfloat16*>(x), x_stride, sorted_pairs, k, rows, D,
                  reinterpret_cast<__nv_bfloat16*>(out)};
-  const int64_t vecs = rows * (D / 8);
-  const int64_t grid = std::min<int64_t>((vecs + 255) / 256, (int64_t)zb::sm_count() * 8);
+  const int64_t grid = std::min<int64_t>((rows + 7) / 8, (int64_t)zb::sm_count() * 8);  // a warp per row
   moe_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
   return zb::check_launch("moe_gather");
 }
