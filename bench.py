@@ -436,6 +436,63 @@ def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps
     }
 
 
+def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5):
+    """cfg5 decode step of one DeltaNet + MoE layer through the drop-in modules, for `streams` concurrent streams
+    (one new row each): AttnRes route (bank of `bank_rows` sources + the layer input, attention_norm fused) ->
+    OriginalGDN.forward in its static decode mode (in_proj GEMM, prologue, recurrent update of 256 slot states,
+    gated norm, wo GEMM) -> AttnRes route (ffn_norm fused) -> MoEFeedForward.forward (router, permutation,
+    grouped GEMMs over 604 MB of expert weights, combine). Hidden 2048, GDN 16 x 128/128, 64 experts top-8, I=768;
+    bf16 random-init weights (N(0, 0.02)); captured in one CUDA graph. The L2 is not flushed: the expert weights
+    alone exceed it."""
+    ops, core = pkg.ops, pkg.core
+    D, H, d, E, k, I = 2048, 16, 128, 64, 8, 768
+    cfg = pkg.config.ModelConfig(hidden_size=D, gdn_num_heads=H, gdn_head_dim=d, moe_n_experts=E, moe_topk=k,
+                                 moe_intermediate_size=I, norm_topk_prob=True, use_training_router_weights=False)
+    gen = torch.Generator().manual_seed(11)
+    rnd = lambda *shape, s=0.02: (s * torch.randn(*shape, generator=gen)).bfloat16()  # noqa: E731
+    inner = H * d
+    gdn = pkg.gdn.OriginalGDN(cfg, 1)
+    gdn.load_state_dict({"in_proj.weight": rnd(4 * inner + 2 * H, D), "conv.weight": rnd(3 * inner, 1, 4, s=0.3),
+                         "out_weight": torch.ones(d).bfloat16(), "A_log": torch.zeros(H), "dt_bias": torch.zeros(H),
+                         "wo.weight": rnd(D, inner)})
+    gdn.to(dev, torch.bfloat16)
+    gdn.allocate_cache(streams, dev, torch.bfloat16)
+    slots = torch.arange(streams, device=dev, dtype=torch.int64)
+    gdn.enable_graph_decode(slots, pkg.gdn.OriginalGDN.static_tables(dev, [streams]))
+    gdn.set_static_mode(True)
+    moe = pkg.moe.MoEFeedForward(cfg, 1)
+    moe.load_state_dict({"router.router_linear.weight": rnd(E, D), "router.rmsnorm_eda.weight": torch.ones(D).bfloat16(),
+                         "router.balancing_biases": torch.zeros(E), "experts.gate_up_proj": rnd(E, 2 * I, D),
+                         "experts.down_proj": rnd(E, D, I)})
+    moe.to(dev, torch.bfloat16)
+    bank = torch.randn(bank_rows + 2, streams, D, generator=gen).bfloat16().to(dev)
+    queries = (0.02 * torch.randn(2, D, generator=gen)).bfloat16().to(dev)
+    norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    rms_cache = torch.zeros(streams, (bank_rows + 5) // 4 * 4, device=dev, dtype=torch.float32)
+    h = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
+    batch = core.Batch(reqs=[core.Req(i, 1, cached_len=100) for i in range(streams)], is_decode=True,
+                       padded_size=streams)
+
+    def layer():
+        ops.attnres_route(bank, bank_rows + 1, queries[0], 1e-5, norm_weight=norm_w, out=h, rms_cache=rms_cache,
+                          cached=bank_rows)
+        a = gdn.forward(h)
+        ops.attnres_route(bank, bank_rows + 1, queries[1], 1e-5, source=a, append_to=bank[bank_rows + 1],
+                          norm_weight=norm_w, out=h, rms_cache=rms_cache, cached=bank_rows)
+        out, _ = moe.forward(h)
+        return out
+
+    with core.forward_batch(batch):
+        ms = graph_ms(layer, stream, reps)
+    return {
+        "workload": f"cfg5 DeltaNet + MoE layer decode step: {streams} streams x hidden {D}; AttnRes route over "
+                    f"{bank_rows + 1} sources before each sublayer; GDN 16 x 128/128 recurrent update; MoE 64 experts "
+                    "top-8, I=768 (604 MB of expert weights); CUDA graph of one layer",
+        "layer_ms": ms, "layer_tokens_per_s": streams / (ms / 1e3),
+        "expert_weight_bytes": E * 3 * I * D * 2,
+    }
+
+
 def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
     """cfg3: chunked prefill of B=8 sequences x T=2048 tokens, 16 heads, dk=dv=128, zero initial state, bf16 out and
     fp32 final state. Inputs (201 MB of q/k/v) exceed L2, so no flush is needed between replays."""
@@ -610,6 +667,8 @@ def main():
                     "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
                     "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
                     "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
+                    "decode_layer_cfg5": bench_decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev,
+                                                                 stream),
                 }
             print(json.dumps(line), flush=True)
     finally:
