@@ -507,7 +507,9 @@ def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
     cu = torch.arange(0, N + 1, T, dtype=torch.int32, device=dev)
     out = torch.empty(N, H, d, device=dev, dtype=torch.bfloat16)
     final = torch.empty(B, H, d, d, device=dev, dtype=torch.float32)
-    ms = graph_ms(lambda: ops.gdn_chunk_prefill(q, k, v, g, beta, cu, final_state=final, out=out), stream, reps)
+    ws = torch.empty(ops.gdn_chunk_prefill_workspace_bytes(N, B, H, d), device=dev, dtype=torch.uint8)
+    ms = graph_ms(lambda: ops.gdn_chunk_prefill(q, k, v, g, beta, cu, final_state=final, out=out, workspace=ws),
+                  stream, reps)
     nbytes = N * H * (3 * d * 2 + 2 * 4 + d * 2) + B * H * d * d * 4
     chunk_heads = B * H * (T // 64)
     flops = chunk_heads * 2 * (64 * 64 * (3 * d + 2 * d) + 3 * 64 * d * d + 64 ** 3 // 3)
@@ -516,7 +518,7 @@ def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
     return {
         "workload": "cfg3 GDN chunked prefill: B=8 x T=2048, 16 heads, dk=dv=128, chunk 64, zero initial state",
         "ms": ms, "tokens_per_s": N / (ms / 1e3),
-        "roofline": {"kernel": "gdn_chunk_prefill_kernel<128>", "bound": "hbm", "achieved": gbs,
+        "roofline": {"kernel": "gdn_prefill_prep_kernel + gdn_prefill_state_kernel", "bound": "hbm", "achieved": gbs,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "algorithmic_bytes": nbytes,
                      "peak_source": pk["source"]},
         "tensor": {"algorithmic_flops": flops, "tflops": flops / (ms / 1e3) / 1e12,

@@ -53,14 +53,21 @@ int zb_gdn_decode_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
  * (servers/sgl/src/zonos3_sgl/models/gdn.py:418-434; use_gate_in_kernel, state_v_first, cu_seqlens, chunk 64);
  * result equal to the per-token recurrence of model/src/zonos3/reference/lm.py:576-582.
  *   q, k [N, H, dk], v [N, H, dv] bf16 contiguous (16-byte aligned); g (log decay), beta [N, H] fp32
- *   cu_seqlens [num_seqs + 1] int32 (device): sequence i is tokens [cu[i], cu[i+1])
+ *   cu_seqlens [num_seqs + 1] int32 (device): sequence i is tokens [cu[i], cu[i+1]); total_tokens = N
  *   init_state / final_state [rows, H, dv, dk] fp32 V-first or NULL (zero start / not written); sequence i uses
  *   row state_slots[i] (int64) or row i when state_slots is NULL; out [N, H, dv] bf16 = S_t (q_t * scale)
- *   dk == dv in {64, 128}. One CTA per (sequence, head); the fp32 state stays in shared memory. */
+ *   dk == dv in {64, 128}. dk = 128 runs on tcgen05 in two kernels (a parallel chunk preparation, then one CTA per
+ *   (sequence, head) with the fp32 state in tensor memory) and needs a 16-byte aligned device workspace of
+ *   zb_gdn_chunk_prefill_workspace_bytes(N, num_seqs, H, dk) bytes; dk = 64 needs none (NULL, 0). */
 int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const float* beta,
                          const int32_t* cu_seqlens, int num_seqs, int H, int dk, int dv, float scale,
                          const float* init_state, const int64_t* state_slots, float* final_state, uint16_t* out,
-                         cudaStream_t stream);
+                         int64_t total_tokens, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+
+/* Workspace bytes zb_gdn_chunk_prefill needs for N = total_tokens tokens in num_seqs sequences (0 when dk != 128):
+ * 33,792 bytes per (chunk record, head), (ceil(N / 64) + num_seqs) records. The torch-side equivalent is the
+ * intermediate tensors FLA's chunk_gated_delta_rule_fwd allocates per call. */
+int64_t zb_gdn_chunk_prefill_workspace_bytes(int64_t total_tokens, int num_seqs, int H, int dk);
 
 /* GDN prologue: from the in_proj output rows mixed [N, 4*H*D + 2*H] (qkv | z | a | b, row stride mixed_stride):
  * depthwise causal conv (kernel 4, conv_weight [3*H*D, 1, 4] bf16) + SiLU over the qkv channels continuing each

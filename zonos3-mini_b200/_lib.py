@@ -28,8 +28,12 @@ SIGNATURES: dict[str, list] = {
     # out, out_stride_b, B, H, dk, dv, scale, stream
     "zb_gdn_decode_step": [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64,
                            _i32, _i32, _i32, _i32, _f32, _p],
-    # q, k, v, g, beta, cu_seqlens, num_seqs, H, dk, dv, scale, init_state, state_slots, final_state, out, stream
-    "zb_gdn_chunk_prefill": [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p, _p],
+    # q, k, v, g, beta, cu_seqlens, num_seqs, H, dk, dv, scale, init_state, state_slots, final_state, out,
+    # total_tokens, workspace, workspace_bytes, stream
+    "zb_gdn_chunk_prefill": [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _p, _p, _p, _p, _i64, _p, _i64,
+                             _p],
+    # total_tokens, num_seqs, H, dk -> bytes (int64)
+    "zb_gdn_chunk_prefill_workspace_bytes": [_i64, _i32, _i32, _i32],
     # mixed, mixed_stride, conv_weight, A_log, dt_bias, cu_seqlens, seq_of_token, slots, fresh, conv_state,
     # conv_rows, num_seqs, N, H, D, q, k, v, g, beta, stream
     "zb_gdn_prologue": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p,
@@ -55,7 +59,8 @@ SIGNATURES: dict[str, list] = {
     # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, T, k, out, out_stride, stream
     "zb_moe_down_combine_noalloc": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _i32, _i32, _p, _i64, _p],
 }
-_RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None}
+_RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None,
+             "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -9,6 +9,7 @@
 //   (I + A) U = diag(beta) (V - diag(gamma) K S_0),   A_ts = beta_t exp(G_t - G_s) k_t.k_s  (s < t)
 //   O = diag(gamma) Q S_0 + P U,                      P_ts = scale exp(G_t - G_s) q_t.k_s   (s <= t)
 //   S_C = gamma_C S_0 + K^T diag(exp(G_C - G_t)) U
+// This file holds the d_k = d_v = 64 kernel and the entry point; d = 128 runs on tcgen05 (gdn_prefill_tc.cu).
 // One CTA owns one (sequence, head) and walks its chunks in order with the fp32 state resident in shared memory.
 // Per chunk: K K^T and Q K^T on tensor cores (mma.sync m16n8k16, bf16 inputs exact); T = (I + A)^{-1} by blocked
 // 16x16 forward substitution in fp32; K S_0, Q S_0, T Y, P U and K^T U on tensor cores with every fp32 operand
@@ -477,11 +478,26 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillP
 
 }  // namespace
 
+namespace zb {
+int64_t gdn_prefill_tc_workspace_bytes(int64_t total_tokens, int num_seqs, int H);
+int gdn_prefill_tc_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const float* beta,
+                          const int32_t* cu_seqlens, int num_seqs, int H, float scale, const float* init_state,
+                          const int64_t* state_slots, float* final_state, uint16_t* out, int64_t total_tokens,
+                          void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+}
+
+ZB_API int64_t zb_gdn_chunk_prefill_workspace_bytes(int64_t total_tokens, int num_seqs, int H, int dk) {
+  if (total_tokens < 0 || num_seqs < 0 || H <= 0 || dk != 128) return 0;
+  return zb::gdn_prefill_tc_workspace_bytes(total_tokens, num_seqs, H);
+}
+
 ZB_API int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
                                 const float* beta, const int32_t* cu_seqlens, int num_seqs, int H, int dk, int dv,
                                 float scale, const float* init_state, const int64_t* state_slots, float* final_state,
-                                uint16_t* out, cudaStream_t stream) {
-  ZB_REQUIRE(num_seqs >= 0 && H > 0, "gdn_chunk_prefill: bad sizes num_seqs=%d H=%d", num_seqs, H);
+                                uint16_t* out, int64_t total_tokens, void* workspace, int64_t workspace_bytes,
+                                cudaStream_t stream) {
+  ZB_REQUIRE(num_seqs >= 0 && H > 0 && total_tokens >= 0, "gdn_chunk_prefill: bad sizes num_seqs=%d H=%d N=%lld",
+             num_seqs, H, (long long)total_tokens);
   if (dk != dv || (dk != 64 && dk != 128))
     return zb::fail(zb::kUnsupported, "gdn_chunk_prefill: dk=%d dv=%d (equal, 64 or 128)", dk, dv);
   if (num_seqs == 0) return zb::kOk;
@@ -489,20 +505,15 @@ ZB_API int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint
   for (const void* ptr : {(const void*)q, (const void*)k, (const void*)v, (const void*)out})
     ZB_REQUIRE_ALIGNED(ptr, 16, "gdn_chunk_prefill q/k/v/out");
   ZB_REQUIRE(H <= 65535, "gdn_chunk_prefill: H=%d (grid y limit)", H);
+  if (dk == 128)
+    return zb::gdn_prefill_tc_launch(q, k, v, g, beta, cu_seqlens, num_seqs, H, scale, init_state, state_slots,
+                                     final_state, out, total_tokens, workspace, workspace_bytes, stream);
   PrefillParams p{reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
                   reinterpret_cast<const __nv_bfloat16*>(v), g, beta, cu_seqlens, init_state, state_slots,
                   final_state, reinterpret_cast<__nv_bfloat16*>(out), H, scale};
-  dim3 grid((unsigned)num_seqs, (unsigned)H);
-  if (dk == 128) {
-    const size_t smem = sizeof(Smem<128>);
-    ZB_CUDA(cudaFuncSetAttribute(gdn_chunk_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    gdn_chunk_prefill_kernel<128><<<grid, kThreads, smem, stream>>>(p);
-  } else {
-    const size_t smem = sizeof(Smem<64>);
-    ZB_CUDA(cudaFuncSetAttribute(gdn_chunk_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
-    gdn_chunk_prefill_kernel<64><<<grid, kThreads, smem, stream>>>(p);
-  }
+  const size_t smem = sizeof(Smem<64>);
+  ZB_CUDA(cudaFuncSetAttribute(gdn_chunk_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  gdn_chunk_prefill_kernel<64><<<dim3((unsigned)num_seqs, (unsigned)H), kThreads, smem, stream>>>(p);
   return zb::check_launch("gdn_chunk_prefill");
 }

@@ -1,0 +1,818 @@
+// Gated-DeltaNet chunked prefill for d_k = d_v = 128 on 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Same algorithm and rounding class as the d = 64 kernel in gdn_prefill.cu (WY / UT form, chunk C = 64, fp32 state,
+// every fp32 operand of a product split into bf16 hi + lo); reference: FLA chunk_gated_delta_rule_fwd as called by
+// OriginalGDN._run_packed (servers/sgl/src/zonos3_sgl/models/gdn.py:418-434), equal to the per-token recurrence of
+// model/src/zonos3/reference/lm.py:576-582. With S the K-first state (S^T = the reference's V-first M), per chunk:
+//   A_ts = beta_t e^{G_t - G_s} k_t.k_s (s < t),  T = (I + A)^{-1},  P_ts = scale e^{G_t - G_s} q_t.k_s (s <= t)
+//   Y = diag(beta)(V - diag(gamma) K S0),  U = T Y,  O = scale diag(gamma) Q S0 + P U
+//   S_C = gamma_C S0 + (diag(f) K)^T U,  f_t = e^{G_C - G_t}
+//
+// Two kernels. The state-independent part of every chunk runs first, all (chunk, head) pairs in parallel:
+//   gdn_prefill_prep_kernel (one CTA of 4 warps per chunk and head): decay scan (G, gamma, f), [K;Q] K^T on tcgen05
+//   (M = 128 rows of K then Q, N = 64, K = 128, accumulator in TMEM), A and P from it, T = (I + A)^{-1} by blocked
+//   16 x 16 substitution in fp32, and T and P split into bf16 hi + lo in the 128B-swizzled K-major layout the
+//   tensor cores read; one 33 KB record per (chunk, head) goes to a workspace with one bulk copy.
+// Then the sequential state pass, gdn_prefill_state_kernel: one CTA (8 warps) per (sequence, head) walks its chunks
+// in order. Every product is a tcgen05.mma with the accumulator in tensor memory; the operands that change with the
+// state (S^T, Y^T, U^T; rows = value index) are the A operand read from TMEM, the state-independent ones (K, Q, T,
+// P, (fK)^T) are B operands in swizzled shared memory. TMEM columns (512, lane = value index v):
+//   [  0,128) S^T fp32 master            [128,192) S^T bf16 hi (packed pairs)   [192,256) S^T bf16 lo
+//   [256,320) (K S0)^T                   [320,384) (Q S0)^T, then O^T            [384,448) U^T
+//   [448,480) Y^T / U^T bf16 hi          [480,512) Y^T / U^T bf16 lo
+// Per chunk:  M2  S^T [K;Q]^T  (S hi, S lo)   (A: TMEM, B: K and Q rows)  -> (K S0)^T, (Q S0)^T
+//             threads: (fK)^T hi/lo from K; Y^T hi/lo from M2 and V into TMEM; O^T *= scale gamma_t; S^T *= gamma_C
+//             M3  Y^T T^T  (hh, hl, lh)                                   -> U^T
+//             threads: U^T hi/lo into TMEM
+//             M4  S^T += U^T (fK)  and  O^T += U^T P^T  (hh, hl, lh each)
+//             threads: S^T master -> hi/lo for the next chunk; O^T -> bf16 rows of the output
+// The next chunk's K, Q, V (cp.async, zero-filled past the sequence end) and its prep record (one bulk copy) load
+// while the current one runs. Every mbarrier wait is bounded (~1 s); on expiry the kernel records
+// kStatusPrefillTimeout, stops, frees TMEM and returns.
+//
+// Chunk records are addressed by id = cu[s] / 64 + s + c for chunk c of sequence s: ids of one sequence are
+// consecutive and those of the next start higher, so ids lie in [0, ceil(N / 64) + num_seqs).
+#include "common.cuh"
+
+namespace {
+
+constexpr int C = 64;          // chunk length
+constexpr int D = 128;         // d_k = d_v
+constexpr int LC = C + 4;      // fp32 row length of the inverse workspace
+
+// prep record (workspace, per (chunk id, head)); the tiles are 128B-swizzled as if based at a 1024-aligned address
+constexpr uint32_t kRecTh = 0, kRecTl = 8192, kRecPh = 16384, kRecPl = 24576;
+constexpr uint32_t kRecG = 32768, kRecGam = kRecG + 256, kRecBet = kRecG + 512, kRecEf = kRecG + 768;
+constexpr uint32_t kRecBytes = kRecG + 1024;  // 33,792
+
+// ---- prep kernel
+constexpr int kPrepThreads = 128;
+constexpr uint32_t kPrepKQ = 0;                       // KQ tile (32 KB); after M1 the record staging over it
+constexpr uint32_t kPrepTf = kRecBytes;               // fp32 [C][LC]
+constexpr uint32_t kPrepSmall = kPrepTf + C * LC * 4;
+struct PrepSmall {
+  float graw[C];
+  float braw[C];
+  uint64_t bar;
+  uint32_t tmem_base;
+};
+constexpr uint32_t kPrepSmem = 1024 + kPrepSmall + sizeof(PrepSmall);
+
+// ---- state kernel
+constexpr int kThreads = 256;  // 8 warps
+constexpr uint32_t kColMaster = 0, kColSh = 128, kColSl = 192, kColKS = 256, kColQS = 320, kColU = 384,
+                   kColYh = 448, kColYl = 480;
+constexpr uint32_t kKQBytes = 2 * 128 * 128;           // 2 k-atoms of [128 rows][128 B]
+constexpr uint32_t kVBytes = C * D * 2;                // row-major [t][v]
+constexpr uint32_t kFKTBytes = D * 128;                // [dk][t], one k-atom
+constexpr uint32_t kRecSlot = (kRecBytes + 1023) / 1024 * 1024;
+constexpr uint32_t kOffKQ = 0;                         // [2]
+constexpr uint32_t kOffV = kOffKQ + 2 * kKQBytes;      // [2]
+constexpr uint32_t kOffRec = kOffV + 2 * kVBytes;      // [2]
+constexpr uint32_t kOffFKTh = kOffRec + 2 * kRecSlot;
+constexpr uint32_t kOffFKTl = kOffFKTh + kFKTBytes;
+constexpr uint32_t kOffSmall = kOffFKTl + kFKTBytes;
+struct Small {
+  uint64_t bar_rec[2];
+  uint64_t bar_m2, bar_m3, bar_m4;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr uint32_t kSmemBytes = 1024 + kOffSmall + sizeof(Small);
+
+struct PrepParams {
+  const __nv_bfloat16* q;  // [N, H, D]
+  const __nv_bfloat16* k;
+  const float* g;          // [N, H]
+  const float* beta;
+  const int32_t* cu_seqlens;
+  int num_seqs;
+  int H;
+  float scale;
+  unsigned char* records;  // [ids, H] x kRecBytes
+  unsigned* status;
+};
+
+struct StateParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const int32_t* cu_seqlens;
+  const float* init_state;     // [*, H, D(v), D(k)] or null
+  const int64_t* state_slots;  // optional row of init/final per sequence
+  float* final_state;
+  __nv_bfloat16* out;          // [N, H, D]
+  const unsigned char* records;
+  int H;
+  float scale;
+  unsigned* status;
+};
+
+// ------------------------------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] B[smem]^T
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] B[smem]^T
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 128B-swizzled K-major operand descriptor (8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// kind::f16, bf16 A and B (K-major), fp32 accumulator, M = 128.
+__host__ __device__ constexpr uint32_t idesc_m128(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack_bf2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+// (x0, x1) = hi + lo, each a packed bf16 pair
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+  hi = pack_bf2(h0, h1);
+  lo = pack_bf2(__float2bfloat16_rn(x0 - __bfloat162float(h0)), __float2bfloat16_rn(x1 - __bfloat162float(h1)));
+}
+
+// byte offset of element (row, col) in a one-atom 128B-swizzled K-major tile (bf16, 64 columns per row)
+__device__ __forceinline__ uint32_t sw128(int row, int col) {
+  return (uint32_t)(row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2);
+}
+// byte offset of 16-byte chunk `ch` (8 columns) of `row`
+__device__ __forceinline__ uint32_t sw128_chunk(int row, int ch) {
+  return (uint32_t)(row * 128 + (((ch ^ row) & 7) << 4));
+}
+
+// bulk copy shared -> global (this CTA's bulk group)
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// K / Q rows of chunk c of the sequence at t_begin (len tokens) into a KQ tile: rows 0-63 K, 64-127 Q, 2 k-atoms
+// of 128B-swizzled rows; rows past the end are zero-filled.
+__device__ __forceinline__ void load_kq(uint32_t kq, const __nv_bfloat16* kp, const __nv_bfloat16* qp,
+                                        int64_t t_begin, int64_t len, int c, int64_t row_stride, int h, int tid,
+                                        int nthreads) {
+  for (int i = tid; i < 2 * C * 16; i += nthreads) {
+    const int r = i >> 4, cidx = i & 15;
+    const int t = r & (C - 1);
+    const int64_t tok = (int64_t)c * C + t;
+    const bool ok = tok < len;
+    const __nv_bfloat16* src = (r < C ? kp : qp) + (t_begin + (ok ? tok : 0)) * row_stride + (int64_t)h * D + cidx * 8;
+    cp_async16(kq + (cidx >> 3) * (128 * 128) + sw128_chunk(r, cidx & 7), src, ok);
+  }
+}
+
+__global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw_addr = zb::smem_addr(smem_raw);
+  const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
+  unsigned char* base = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  PrepSmall& sm = *reinterpret_cast<PrepSmall*>(base + kPrepSmall);
+  float* Tf = reinterpret_cast<float*>(base + kPrepTf);
+  float* G = reinterpret_cast<float*>(base + kRecG);
+  float* gam = reinterpret_cast<float*>(base + kRecGam);
+  float* bet = reinterpret_cast<float*>(base + kRecBet);
+  float* ef = reinterpret_cast<float*>(base + kRecEf);
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int id = blockIdx.x, h = blockIdx.y;
+  // sequence of this chunk id: the last s with cu[s] / 64 + s <= id
+  if (p.num_seqs <= 0) return;
+  int lo = 0, hi = p.num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.cu_seqlens[mid] / C + mid <= id) lo = mid; else hi = mid - 1;
+  }
+  const int seq = lo;
+  const int64_t t_begin = p.cu_seqlens[seq], len = p.cu_seqlens[seq + 1] - t_begin;
+  const int c = id - (int)(t_begin / C) - seq;
+  if (c < 0 || (int64_t)c * C >= len) return;  // an unused id (uniform over the CTA)
+  const int64_t row_stride = (int64_t)p.H * D;
+
+  load_kq(sbase + kPrepKQ, p.k, p.q, t_begin, len, c, row_stride, h, tid, kPrepThreads);
+  if (tid < 2 * C) {
+    const int t = tid & (C - 1);
+    const int64_t tok = (int64_t)c * C + t;
+    const bool ok = tok < len;
+    cp_async4(zb::smem_addr(tid < C ? &sm.graw[t] : &sm.braw[t]),
+              (tid < C ? p.g : p.beta) + (t_begin + (ok ? tok : 0)) * p.H + h, ok);
+  }
+  cp_async_commit();
+  const uint32_t bar = zb::smem_addr(&sm.bar);
+  if (tid == 0) {
+    zb::mbar_init(bar, 1);
+    zb::fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(zb::smem_addr(&sm.tmem_base), 64);
+  cp_async_wait_all();
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  // ---- M1: [K;Q] K^T -> TMEM lanes 0-63 (K K^T), 64-127 (Q K^T)
+  if (tid == 0) {
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = sbase + kPrepKQ + (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+      mma_ss(tmem, desc_sw128(off), desc_sw128(off), idesc_m128(64), ks > 0);
+    }
+    mma_commit(bar);
+  }
+  // ---- decay scan (the record's vectors sit after the KQ tile, outside what M1 reads)
+  if (warp == 0) {
+    const float a0 = sm.graw[2 * lane], a1 = sm.graw[2 * lane + 1];
+    float incl = a0 + a1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    const float g0 = incl - a1, g1 = incl;
+    const float gC = __shfl_sync(0xffffffffu, incl, 31);
+    G[2 * lane] = g0;
+    G[2 * lane + 1] = g1;
+    gam[2 * lane] = expf(g0);
+    gam[2 * lane + 1] = expf(g1);
+    ef[2 * lane] = expf(gC - g0);
+    ef[2 * lane + 1] = expf(gC - g1);
+    bet[2 * lane] = sm.braw[2 * lane];
+    bet[2 * lane + 1] = sm.braw[2 * lane + 1];
+  }
+  __syncthreads();
+  bool ok = zb::mbar_wait_bounded(bar, 0, p.status, zb::kStatusPrefillTimeout);
+  tc_fence_after();
+  // ---- A (rows 0-63) into the fp32 workspace; P hi / lo (rows 64-127) into the record (over the dead KQ tile)
+  {
+    uint32_t r0[32], r1[32];
+    const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+    tmem_ld32_nowait(tl, r0);
+    tmem_ld32_nowait(tl + 32, r1);
+    tmem_ld_wait();
+    const int row = tid, t = row & (C - 1);
+    const float Gt = G[t];
+    if (row < C) {
+      const float bt = bet[t];
+      float* dst = Tf + t * LC;
+#pragma unroll
+      for (int s = 0; s < C; s += 4) {
+        float4 a;
+        float* av = &a.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int ss = s + e;
+          const float x = __uint_as_float(ss < 32 ? r0[ss] : r1[ss - 32]);
+          av[e] = ss < t ? bt * expf(Gt - G[ss]) * x : 0.f;
+        }
+        *reinterpret_cast<float4*>(dst + s) = a;
+      }
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int s0 = 8 * ch + e;
+          const float x0 = __uint_as_float(s0 < 32 ? r0[s0] : r1[s0 - 32]);
+          const float x1 = __uint_as_float(s0 + 1 < 32 ? r0[s0 + 1] : r1[s0 + 1 - 32]);
+          const float p0 = s0 <= t ? p.scale * expf(Gt - G[s0]) * x0 : 0.f;
+          const float p1 = s0 + 1 <= t ? p.scale * expf(Gt - G[s0 + 1]) * x1 : 0.f;
+          split_pair(p0, p1, hv[e / 2], lv[e / 2]);
+        }
+        *reinterpret_cast<uint4*>(base + kRecPh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(base + kRecPl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- T = (I + A)^{-1}. Diagonal 16 x 16 blocks by forward substitution (thread = block b, column j)
+  if (tid < 64) {
+    const int b = tid >> 4, j = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.f : 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+#pragma unroll
+      for (int r2 = r + 1; r2 < 16; ++r2) x[r2] -= Tf[(16 * b + r2) * LC + 16 * b + r] * x[r];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Tf[(16 * b + r) * LC + 16 * b + j] = x[r];
+  }
+  __syncthreads();
+  if (warp < 3) {
+    // block column jb = warp: X_ij = -T_ii sum_{k=jb}^{i-1} A_ik X_kj for i = jb+1 .. 3 (X_jj = T_jj); thread =
+    // column j of the block column and half rh of every block's rows; results go straight into T hi / lo
+    const int jb = warp, j = lane & 15, rh = lane >> 4;
+    const int col = 16 * jb + j;
+    float Tk[4][16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int m = 0; m < 16; ++m) Tk[k][m] = k == jb ? Tf[(16 * k + m) * LC + 16 * k + j] : 0.f;
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+      if (i <= jb) continue;
+      float y[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) y[r] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        if (k < jb || k >= i) continue;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float* arow = Tf + (16 * i + 8 * rh + r) * LC + 16 * k;
+#pragma unroll
+          for (int m = 0; m < 16; m += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(arow + m);
+            y[r] = fmaf(a.x, Tk[k][m], fmaf(a.y, Tk[k][m + 1], fmaf(a.z, Tk[k][m + 2], fmaf(a.w, Tk[k][m + 3], y[r]))));
+          }
+        }
+      }
+      float yf[16];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float other = __shfl_xor_sync(0xffffffffu, y[r], 16);
+        yf[r] = rh ? other : y[r];
+        yf[8 + r] = rh ? y[r] : other;
+      }
+      float x[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float* trow = Tf + (16 * i + 8 * rh + r) * LC + 16 * i;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; m += 4) {
+          const float4 tv = *reinterpret_cast<const float4*>(trow + m);
+          acc = fmaf(tv.x, yf[m], fmaf(tv.y, yf[m + 1], fmaf(tv.z, yf[m + 2], fmaf(tv.w, yf[m + 3], acc))));
+        }
+        x[r] = -acc;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[r], 16);
+        Tk[i][r] = rh ? other : x[r];
+        Tk[i][8 + r] = rh ? x[r] : other;
+        const int t = 16 * i + 8 * rh + r;
+        const __nv_bfloat16 xh = __float2bfloat16_rn(x[r]);
+        *reinterpret_cast<__nv_bfloat16*>(base + kRecTh + sw128(t, col)) = xh;
+        *reinterpret_cast<__nv_bfloat16*>(base + kRecTl + sw128(t, col)) =
+            __float2bfloat16_rn(x[r] - __bfloat162float(xh));
+      }
+    }
+  } else {
+    // warp 3: the diagonal blocks and the zeros above them, 8 columns per store
+    for (int e = lane; e < C * 8; e += 32) {
+      const int t = e >> 3, ch = e & 7;
+      const int bi = t >> 4;
+      if (ch < 2 * bi) continue;  // strictly below the diagonal block: written by warps 0-2
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int u = 0; u < 8; u += 2) {
+        const int s = 8 * ch + u;
+        const float v0 = (s >> 4) == bi ? Tf[t * LC + s] : 0.f;
+        const float v1 = (s >> 4) == bi ? Tf[t * LC + s + 1] : 0.f;
+        split_pair(v0, v1, hv[u / 2], lv[u / 2]);
+      }
+      *reinterpret_cast<uint4*>(base + kRecTh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<uint4*>(base + kRecTl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+  }
+  fence_proxy_async();  // record staging (generic writes) -> bulk copy
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    bulk_s2g(p.records + ((int64_t)id * p.H + h) * kRecBytes, sbase, kRecBytes);
+    bulk_wait_all();
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StateParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw_addr = zb::smem_addr(smem_raw);
+  const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
+  unsigned char* base = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  Small& sm = *reinterpret_cast<Small*>(base + kOffSmall);
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int quarter = warp & 3;             // TMEM lane quarter of this warp
+  const int half = warp >> 2;               // warps 0-3 and 4-7 split columns
+  const int row = 32 * quarter + lane;      // this thread's TMEM lane (value index)
+  const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+  const int seq = blockIdx.x, h = blockIdx.y;
+  const int64_t t_begin = p.cu_seqlens[seq], t_end = p.cu_seqlens[seq + 1];
+  const int64_t len = t_end - t_begin;
+  const int nchunks = (int)((len + C - 1) / C);
+  const int64_t row_stride = (int64_t)p.H * D;
+  const int64_t slot = p.state_slots ? p.state_slots[seq] : seq;
+  const int64_t id0 = t_begin / C + seq;  // record id of chunk 0
+  const uint32_t bar_m2 = zb::smem_addr(&sm.bar_m2), bar_m3 = zb::smem_addr(&sm.bar_m3);
+  const uint32_t bar_m4 = zb::smem_addr(&sm.bar_m4);
+
+  if (tid == 0) {
+    zb::mbar_init(zb::smem_addr(&sm.bar_rec[0]), 1);
+    zb::mbar_init(zb::smem_addr(&sm.bar_rec[1]), 1);
+    zb::mbar_init(bar_m2, 1);
+    zb::mbar_init(bar_m3, 1);
+    zb::mbar_init(bar_m4, 1);
+    sm.abort = 0;
+    zb::fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(zb::smem_addr(&sm.tmem_base), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tl = tmem + lane_off;  // this warp's lane quarter
+
+  // ---- loads of chunk c into buffer b: K / Q / V rows by cp.async, the prep record by one bulk copy
+  int last_issued = -1;  // thread 0: chunk of the last record copy
+  auto load_chunk = [&](int b, int c) {
+    load_kq(sbase + kOffKQ + b * kKQBytes, p.k, p.q, t_begin, len, c, row_stride, h, tid, kThreads);
+    const uint32_t vb = sbase + kOffV + b * kVBytes;
+    for (int i = tid; i < C * 16; i += kThreads) {
+      const int t = i >> 4, cidx = i & 15;
+      const int64_t tok = (int64_t)c * C + t;
+      const bool ok = tok < len;
+      cp_async16(vb + t * 256 + cidx * 16, p.v + (t_begin + (ok ? tok : 0)) * row_stride + (int64_t)h * D + cidx * 8,
+                 ok);
+    }
+    cp_async_commit();
+    if (tid == 0) {
+      last_issued = c;
+      const uint32_t bar = zb::smem_addr(&sm.bar_rec[b]);
+      zb::mbar_arrive_expect_tx(bar, kRecBytes);
+      zb::bulk_g2s(sbase + kOffRec + b * kRecSlot, p.records + ((id0 + c) * p.H + h) * kRecBytes, kRecBytes, bar);
+    }
+  };
+
+  // ---- initial state: S^T master and its hi / lo split (thread = value row, warp halves split the keys)
+  {
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const int k0 = 64 * half + 32 * part;
+      uint32_t m[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.init_state)
+          s = *reinterpret_cast<const float4*>(p.init_state + ((slot * p.H + h) * D + row) * (int64_t)D + k0 + j);
+        m[j] = __float_as_uint(s.x);
+        m[j + 1] = __float_as_uint(s.y);
+        m[j + 2] = __float_as_uint(s.z);
+        m[j + 3] = __float_as_uint(s.w);
+      }
+      tmem_st32(tl + kColMaster + k0, m);
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(m[j]), __uint_as_float(m[j + 1]), hi[j / 2], lo[j / 2]);
+      tmem_st16(tl + kColSh + 32 * half + 16 * part, hi);
+      tmem_st16(tl + kColSl + 32 * half + 16 * part, lo);
+    }
+    tmem_st_wait();
+  }
+
+  if (nchunks > 0) load_chunk(0, 0);
+
+  auto wait_bar = [&](uint32_t bar, uint32_t parity) {
+    if (!zb::mbar_wait_bounded(bar, parity, p.status, zb::kStatusPrefillTimeout)) sm.abort = 1;
+  };
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int b = c & 1;
+    const uint32_t ph = (uint32_t)(c & 1);
+    const uint32_t kq = sbase + kOffKQ + b * kKQBytes;
+    const uint32_t rec = sbase + kOffRec + b * kRecSlot;
+    const unsigned char* recp = base + kOffRec + b * kRecSlot;
+    const float* gam = reinterpret_cast<const float*>(recp + kRecGam);
+    const float* bet = reinterpret_cast<const float*>(recp + kRecBet);
+    const float* ef = reinterpret_cast<const float*>(recp + kRecEf);
+    const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(base + kOffV + b * kVBytes);
+    cp_async_wait_all();
+    wait_bar(zb::smem_addr(&sm.bar_rec[b]), (uint32_t)((c >> 1) & 1));
+    fence_proxy_async();  // cp.async data -> tensor-core reads
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+    if (c + 1 < nchunks) load_chunk(b ^ 1, c + 1);
+
+    // ---- M2: (K S0)^T, (Q S0)^T
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+        mma_ts(tmem + kColKS, tmem + kColSh + 8 * ks, desc_sw128(kq + off), idesc_m128(128), ks > 0);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+        mma_ts(tmem + kColKS, tmem + kColSl + 8 * ks, desc_sw128(kq + off), idesc_m128(128), 1);
+      }
+      mma_commit(bar_m2);
+    }
+
+    if (half == 1) {
+      // (fK)^T hi / lo: row dk, columns t (from the K rows of the KQ tile), while M2 runs
+      const int dk = tid - 128;
+      const unsigned char* kqp = base + kOffKQ + b * kKQBytes + (dk >> 6) * (128 * 128);
+      const int dcol = dk & 63;
+#pragma unroll 2
+      for (int tb = 0; tb < 8; ++tb) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const int t = 8 * tb + i;
+          const float k0 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(kqp + sw128(t, dcol)));
+          const float k1 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(kqp + sw128(t + 1, dcol)));
+          split_pair(ef[t] * k0, ef[t + 1] * k1, hv[i / 2], lv[i / 2]);
+        }
+        *reinterpret_cast<uint4*>(base + kOffFKTh + sw128_chunk(dk, tb)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(base + kOffFKTl + sw128_chunk(dk, tb)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+      }
+    }
+
+    // ---- after M2: Y^T hi / lo into TMEM (warps 0-3); O^T *= scale gamma_t and S^T *= gamma_C (warps 4-7)
+    wait_bar(bar_m2, ph);
+    tc_fence_after();
+    if (half == 0) {
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t r[32];
+        tmem_ld32_nowait(tl + kColKS + 32 * part, r);
+        tmem_ld_wait();
+        uint32_t hv[16], lv[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int t = 32 * part + j;
+          const float y0 = bet[t] * (__bfloat162float(Vs[t * D + row]) - gam[t] * __uint_as_float(r[j]));
+          const float y1 =
+              bet[t + 1] * (__bfloat162float(Vs[(t + 1) * D + row]) - gam[t + 1] * __uint_as_float(r[j + 1]));
+          split_pair(y0, y1, hv[j / 2], lv[j / 2]);
+        }
+        tmem_st16(tl + kColYh + 16 * part, hv);
+        tmem_st16(tl + kColYl + 16 * part, lv);
+      }
+    } else {
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t r[32];
+        tmem_ld32_nowait(tl + kColQS + 32 * part, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * (p.scale * gam[32 * part + j]));
+        tmem_st32(tl + kColQS + 32 * part, r);
+      }
+      const float gamC = gam[C - 1];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        uint32_t m[32];
+        tmem_ld32_nowait(tl + kColMaster + 32 * part, m);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
+        tmem_st32(tl + kColMaster + 32 * part, m);
+      }
+    }
+    tmem_st_wait();
+    fence_proxy_async();  // (fK)^T tiles -> tensor-core reads
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+
+    // ---- M3: U^T = Y^T T^T
+    if (tid == 0) {
+      const uint32_t th = rec + kRecTh, tlo = rec + kRecTl;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts(tmem + kColU, tmem + kColYh + 8 * ks, desc_sw128(th + 32 * ks), idesc_m128(64), ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts(tmem + kColU, tmem + kColYh + 8 * ks, desc_sw128(tlo + 32 * ks), idesc_m128(64), 1);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_ts(tmem + kColU, tmem + kColYl + 8 * ks, desc_sw128(th + 32 * ks), idesc_m128(64), 1);
+      mma_commit(bar_m3);
+    }
+    wait_bar(bar_m3, ph);
+    tc_fence_after();
+    // ---- U^T hi / lo into TMEM (over Y^T): warps 0-3 columns t 0..31, warps 4-7 t 32..63
+    {
+      uint32_t r[32];
+      tmem_ld32_nowait(tl + kColU + 32 * half, r);
+      tmem_ld_wait();
+      uint32_t hv[16], lv[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), hv[j / 2], lv[j / 2]);
+      tmem_st16(tl + kColYh + 16 * half, hv);
+      tmem_st16(tl + kColYl + 16 * half, lv);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (sm.abort) break;
+
+    // ---- M4: S^T += U^T (fK);  O^T += U^T P^T
+    if (tid == 0) {
+      const uint32_t fh = sbase + kOffFKTh, fl = sbase + kOffFKTl, pph = rec + kRecPh, ppl = rec + kRecPl;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        mma_ts(tmem + kColMaster, tmem + kColYh + 8 * ks, desc_sw128(fh + 32 * ks), idesc_m128(128), 1);
+        mma_ts(tmem + kColMaster, tmem + kColYh + 8 * ks, desc_sw128(fl + 32 * ks), idesc_m128(128), 1);
+        mma_ts(tmem + kColMaster, tmem + kColYl + 8 * ks, desc_sw128(fh + 32 * ks), idesc_m128(128), 1);
+        mma_ts(tmem + kColQS, tmem + kColYh + 8 * ks, desc_sw128(pph + 32 * ks), idesc_m128(64), 1);
+        mma_ts(tmem + kColQS, tmem + kColYh + 8 * ks, desc_sw128(ppl + 32 * ks), idesc_m128(64), 1);
+        mma_ts(tmem + kColQS, tmem + kColYl + 8 * ks, desc_sw128(pph + 32 * ks), idesc_m128(64), 1);
+      }
+      mma_commit(bar_m4);
+    }
+    wait_bar(bar_m4, ph);
+    tc_fence_after();
+    // ---- S^T master -> hi / lo (warps 0-3 keys 0..63, warps 4-7 keys 64..127); O^T -> output rows
+    {
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t m[32];
+        tmem_ld32_nowait(tl + kColMaster + 64 * half + 32 * part, m);
+        tmem_ld_wait();
+        uint32_t hv[16], lv[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(m[j]), __uint_as_float(m[j + 1]), hv[j / 2], lv[j / 2]);
+        tmem_st16(tl + kColSh + 32 * half + 16 * part, hv);
+        tmem_st16(tl + kColSl + 32 * half + 16 * part, lv);
+      }
+      uint32_t o[32];
+      tmem_ld32_nowait(tl + kColQS + 32 * half, o);
+      tmem_ld_wait();
+      __nv_bfloat16* orow = p.out + (t_begin + (int64_t)c * C) * row_stride + (int64_t)h * D + row;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int t = 32 * half + j;
+        if ((int64_t)c * C + t < len) orow[(int64_t)t * row_stride] = __float2bfloat16_rn(__uint_as_float(o[j]));
+      }
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+
+  if (p.final_state && !sm.abort) {
+    float* dst = p.final_state + ((slot * p.H + h) * D + row) * (int64_t)D + 64 * half;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      uint32_t m[32];
+      tmem_ld32_nowait(tl + kColMaster + 64 * half + 32 * part, m);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(dst + 32 * part + j) = make_float4(
+            __uint_as_float(m[j]), __uint_as_float(m[j + 1]), __uint_as_float(m[j + 2]), __uint_as_float(m[j + 3]));
+    }
+  }
+  cp_async_wait_all();
+  // after an abort, the last record copy issued may still be in flight: it must land before the CTA's shared
+  // memory is released
+  if (tid == 0 && sm.abort && last_issued >= 0)
+    zb::mbar_wait_bounded(zb::smem_addr(&sm.bar_rec[last_issued & 1]), (uint32_t)((last_issued >> 1) & 1), nullptr,
+                          0);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+namespace zb {
+
+int64_t gdn_prefill_tc_workspace_bytes(int64_t total_tokens, int num_seqs, int H) {
+  return ((total_tokens + C - 1) / C + num_seqs) * (int64_t)H * kRecBytes;
+}
+
+// d_k = d_v = 128 chunked prefill on tcgen05 (called by zb_gdn_chunk_prefill after its argument checks).
+int gdn_prefill_tc_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const float* beta,
+                          const int32_t* cu_seqlens, int num_seqs, int H, float scale, const float* init_state,
+                          const int64_t* state_slots, float* final_state, uint16_t* out, int64_t total_tokens,
+                          void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  if (init_state) ZB_REQUIRE_ALIGNED(init_state, 16, "gdn_chunk_prefill init_state");
+  if (final_state) ZB_REQUIRE_ALIGNED(final_state, 16, "gdn_chunk_prefill final_state");
+  const int64_t need = gdn_prefill_tc_workspace_bytes(total_tokens, num_seqs, H);
+  ZB_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+             "gdn_chunk_prefill: workspace of %lld bytes needed (got %lld)", (long long)need,
+             (long long)workspace_bytes);
+  ZB_REQUIRE_ALIGNED(workspace, 16, "gdn_chunk_prefill workspace");
+  const int64_t ids = (total_tokens + C - 1) / C + num_seqs;
+  ZB_REQUIRE(ids <= 0x7fffffff, "gdn_chunk_prefill: too many chunks");
+  unsigned* status = device_status_ptr();
+  if (ids > 0) {
+    PrepParams pp{reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k), g, beta,
+                  cu_seqlens, num_seqs, H, scale, static_cast<unsigned char*>(workspace), status};
+    ZB_CUDA(cudaFuncSetAttribute(gdn_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPrepSmem));
+    gdn_prefill_prep_kernel<<<dim3((unsigned)ids, (unsigned)H), kPrepThreads, kPrepSmem, stream>>>(pp);
+    if (int rc = check_launch("gdn_chunk_prefill (prep)")) return rc;
+  }
+  StateParams sp{reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+                 reinterpret_cast<const __nv_bfloat16*>(v), cu_seqlens, init_state, state_slots, final_state,
+                 reinterpret_cast<__nv_bfloat16*>(out), static_cast<const unsigned char*>(workspace), H, scale, status};
+  ZB_CUDA(cudaFuncSetAttribute(gdn_prefill_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kSmemBytes));
+  gdn_prefill_state_kernel<<<dim3((unsigned)num_seqs, (unsigned)H), kThreads, kSmemBytes, stream>>>(sp);
+  return check_launch("gdn_chunk_prefill (state)");
+}
+
+}  // namespace zb

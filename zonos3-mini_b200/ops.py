@@ -390,16 +390,24 @@ def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, ou
     return moe_combine(ws.y, k, out)
 
 
+def gdn_chunk_prefill_workspace_bytes(total_tokens: int, num_seqs: int, heads: int, head_dim: int) -> int:
+    """Bytes of device workspace ``gdn_chunk_prefill`` needs (0 for head_dim 64): one 33 KB record of the chunk
+    preparation (T, P, decays) per (chunk, head)."""
+    return int(_lib.load().zb_gdn_chunk_prefill_workspace_bytes(int(total_tokens), int(num_seqs), int(heads),
+                                                                int(head_dim)))
+
+
 def gdn_chunk_prefill(q, k, v, g, beta, cu_seqlens, *, initial_state=None, output_final_state=True, scale=None,
-                      state_slots=None, final_state=None, out=None):
+                      state_slots=None, final_state=None, out=None, workspace=None):
     """Chunked (C = 64) gated delta rule over packed variable-length sequences, fp32 state.
 
     The call FLA's chunk_gated_delta_rule_fwd makes for OriginalGDN._run_packed
     (servers/sgl/src/zonos3_sgl/models/gdn.py:418-434), with the per-token math of
     model/src/zonos3/reference/lm.py:576-582. q, k [N, H, d] bf16 (L2-normalised), v [N, H, d] bf16, g / beta
     [N, H] fp32 (g = log decay), cu_seqlens [n+1] int32 (device). initial_state / final_state [n or slots, H, d, d]
-    fp32 V-first (``state_slots`` [n] int64 maps sequence i to a state row). Returns (out [N, H, d] bf16,
-    final_state or None)."""
+    fp32 V-first (``state_slots`` [n] int64 maps sequence i to a state row). ``workspace``: optional uint8 device
+    buffer of at least ``gdn_chunk_prefill_workspace_bytes(N, n, H, d)`` bytes (allocated per call when absent).
+    Returns (out [N, H, d] bf16, final_state or None)."""
     _check_cuda("q", q, torch.bfloat16)
     dev = q.device
     N, H, dk = q.shape
@@ -432,10 +440,18 @@ def gdn_chunk_prefill(q, k, v, g, beta, cu_seqlens, *, initial_state=None, outpu
     _require(out.shape == (N, H, dv) and out.is_contiguous(), "out must be a contiguous [N, H, dv] tensor")
     if scale is None:
         scale = dk ** -0.5
+    ws_bytes = gdn_chunk_prefill_workspace_bytes(N, n, H, dk)
+    if workspace is None:
+        workspace = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8) if ws_bytes else None
+    else:
+        _check_cuda("workspace", workspace, torch.uint8, dev)
+        _require(workspace.is_contiguous() and workspace.numel() >= ws_bytes,
+                 f"workspace must be a contiguous uint8 buffer of at least {ws_bytes} bytes")
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
     _lib.call("zb_gdn_chunk_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(),
               cu_seqlens.data_ptr(), n, H, dk, dv, float(scale), ptr(initial_state), ptr(state_slots),
-              ptr(final_state) if output_final_state else None, out.data_ptr(), _stream(dev))
+              ptr(final_state) if output_final_state else None, out.data_ptr(), N, ptr(workspace),
+              0 if workspace is None else workspace.numel(), _stream(dev))
     return out, (final_state if output_final_state else None)
 
 
