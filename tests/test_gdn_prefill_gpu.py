@@ -53,6 +53,26 @@ def test_chunked_prefill_matches_recurrence(zb, lengths, H, d):
     assert rel_err(out.float(), ref_out) < OUT_TOL
 
 
+@pytest.mark.parametrize("regime", ["strong_decay", "mixed_sign"])
+def test_decay_regimes(zb, regime):
+    """Chunks outside the factored-decay fast path of the d=128 kernel: more than 80 of log decay inside a 16-token
+    block (g about -6.5 per token), and a log decay that is positive for some tokens (G not monotone)."""
+    lengths, H, d = [130, 64], 2, 128
+    q, k, v, g, beta, cu, init = packed_inputs(lengths, H, d, seed=5, state_scale=0.3)
+    gen = torch.Generator().manual_seed(6)
+    if regime == "strong_decay":
+        g = -8.0 * F.softplus(torch.randn(g.shape, generator=gen))
+    else:
+        g = 0.05 * torch.randn(g.shape, generator=gen)
+    ref_out, ref_state = reference(q, k, v, g, beta, cu, init)
+    out, state = zb.ops.gdn_chunk_prefill(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), cu.cuda(),
+                                          initial_state=init.cuda())
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all() and torch.isfinite(state).all()
+    assert max_rel_err(state, ref_state) < STATE_TOL
+    assert rel_err(out.float(), ref_out) < OUT_TOL
+
+
 def test_initial_state_and_slots(zb):
     """A continuation from given states (the prefill of a request with cached rows), states addressed by slot."""
     lengths, H, d = [70, 33], 2, 128

@@ -10,9 +10,10 @@
 //
 // Two kernels. The state-independent part of every chunk runs first, all (chunk, head) pairs in parallel:
 //   gdn_prefill_prep_kernel (one CTA of 4 warps per chunk and head): decay scan (G, gamma, f), [K;Q] K^T on tcgen05
-//   (M = 128 rows of K then Q, N = 64, K = 128, accumulator in TMEM), A and P from it, T = (I + A)^{-1} by blocked
-//   16 x 16 substitution in fp32, and T and P split into bf16 hi + lo in the 128B-swizzled K-major layout the
-//   tensor cores read; one 33 KB record per (chunk, head) goes to a workspace with one bulk copy.
+//   (M = 128 rows of K then Q, N = 64, K = 128, accumulator in TMEM), A and P from it, T = (I + A)^{-1} in fp32
+//   (16 x 16 diagonal blocks by substitution, then the off-diagonal blocks row-block by row-block), and T and P
+//   split into bf16 hi + lo in the 128B-swizzled K-major layout the tensor cores read; one 33 KB record per
+//   (chunk, head) goes to a workspace with one bulk copy.
 // Then the sequential state pass, gdn_prefill_state_kernel: one CTA (8 warps) per (sequence, head) walks its chunks
 // in order. Every product is a tcgen05.mma with the accumulator in tensor memory; the operands that change with the
 // state (S^T, Y^T, U^T; rows = value index) are the A operand read from TMEM, the state-independent ones (K, Q, T,
@@ -21,11 +22,13 @@
 //   [256,320) (K S0)^T                   [320,384) (Q S0)^T, then O^T            [384,448) U^T
 //   [448,480) Y^T / U^T bf16 hi          [480,512) Y^T / U^T bf16 lo
 // Per chunk:  M2  S^T [K;Q]^T  (S hi, S lo)   (A: TMEM, B: K and Q rows)  -> (K S0)^T, (Q S0)^T
-//             threads: (fK)^T hi/lo from K; Y^T hi/lo from M2 and V into TMEM; O^T *= scale gamma_t; S^T *= gamma_C
+//             threads: S^T *= gamma_C and (fK)^T hi/lo from K (during M2); Y^T hi/lo from M2 and V into TMEM;
+//             O^T *= scale gamma_t
 //             M3  Y^T T^T  (hh, hl, lh)                                   -> U^T
 //             threads: U^T hi/lo into TMEM
 //             M4  S^T += U^T (fK)  and  O^T += U^T P^T  (hh, hl, lh each)
-//             threads: S^T master -> hi/lo for the next chunk; O^T -> bf16 rows of the output
+//             threads: S^T master -> hi/lo for the next chunk; O^T -> bf16 rows staged in shared memory, then
+//             written as 256-byte rows
 // The next chunk's K, Q, V (cp.async, zero-filled past the sequence end) and its prep record (one bulk copy) load
 // while the current one runs. Every mbarrier wait is bounded (~1 s); on expiry the kernel records
 // kStatusPrefillTimeout, stops, frees TMEM and returns.
@@ -48,11 +51,15 @@ constexpr uint32_t kRecBytes = kRecG + 1024;  // 33,792
 // ---- prep kernel
 constexpr int kPrepThreads = 128;
 constexpr uint32_t kPrepKQ = 0;                       // KQ tile (32 KB); after M1 the record staging over it
-constexpr uint32_t kPrepTf = kRecBytes;               // fp32 [C][LC]
-constexpr uint32_t kPrepSmall = kPrepTf + C * LC * 4;
+constexpr uint32_t kPrepTf = kRecBytes;               // fp32 [C][LC]: A, then T
+constexpr uint32_t kPrepYs = kPrepTf + C * LC * 4;    // fp32 [3][16][16]: sums of the off-diagonal blocks
+constexpr uint32_t kPrepSmall = kPrepYs + 3 * 256 * 4;
 struct PrepSmall {
   float graw[C];
   float braw[C];
+  float rf[C];       // e^{G_t - G_{16 (t / 16)}}
+  float cf[4 * C];   // [row block i][s]: e^{G_{16 i} - G_s} for s < 16 (i + 1)
+  int fast;          // factored decays usable for this chunk
   uint64_t bar;
   uint32_t tmem_base;
 };
@@ -193,14 +200,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ uint32_t pack_bf2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
-  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
-}
-// (x0, x1) = hi + lo, each a packed bf16 pair
+// (x0, x1) = hi + lo, each a packed bf16 pair (x0 in the low half); two-wide conversions
 __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-  hi = pack_bf2(h0, h1);
-  lo = pack_bf2(__float2bfloat16_rn(x0 - __bfloat162float(h0)), __float2bfloat16_rn(x1 - __bfloat162float(h1)));
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 // byte offset of element (row, col) in a one-atom 128B-swizzled K-major tile (bf16, 64 columns per row)
@@ -244,6 +250,52 @@ __device__ __forceinline__ void load_kq(uint32_t kq, const __nv_bfloat16* kp, co
   }
 }
 
+// A row t (is_a: beta_t e^{G_t - G_s} (K K^T)_ts for s < t, fp32 into Tf) or P row t (scale e^{G_t - G_s} (Q K^T)_ts
+// for s <= t, split into the record's P hi / lo tiles) from the 64 accumulator columns of this thread's TMEM lane.
+// kFactored: decays from the factors rf / cf; otherwise one fast exponential per element (its relative error, a
+// few 1e-6 for exponents down to -40, is below the ~2^-17 of the bf16 hi + lo operands it feeds).
+template <bool kFactored>
+__device__ __forceinline__ void decay_epilogue(bool is_a, int t, const uint32_t (&r0)[32], const uint32_t (&r1)[32],
+                                               const float* G, const float* bet, const float* rf, const float* cf,
+                                               float scale, float* Tf, unsigned char* base) {
+  const float Gt = G[t];
+  const float* cfr = cf + C * (t >> 4);
+  auto decay = [&](int s) { return kFactored ? cfr[s] : __expf(Gt - G[s]); };
+  if (is_a) {
+    const float rowf = bet[t] * (kFactored ? rf[t] : 1.f);
+    float* dst = Tf + t * LC;
+#pragma unroll
+    for (int s = 0; s < C; s += 4) {
+      float4 a;
+      float* av = &a.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ss = s + e;
+        const float x = __uint_as_float(ss < 32 ? r0[ss] : r1[ss - 32]);
+        av[e] = ss < t ? rowf * decay(ss) * x : 0.f;
+      }
+      *reinterpret_cast<float4*>(dst + s) = a;
+    }
+  } else {
+    const float rowf = scale * (kFactored ? rf[t] : 1.f);
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const int s0 = 8 * ch + e;
+        const float x0 = __uint_as_float(s0 < 32 ? r0[s0] : r1[s0 - 32]);
+        const float x1 = __uint_as_float(s0 + 1 < 32 ? r0[s0 + 1] : r1[s0 + 1 - 32]);
+        const float p0 = s0 <= t ? rowf * decay(s0) * x0 : 0.f;
+        const float p1 = s0 + 1 <= t ? rowf * decay(s0 + 1) * x1 : 0.f;
+        split_pair(p0, p1, hv[e / 2], lv[e / 2]);
+      }
+      *reinterpret_cast<uint4*>(base + kRecPh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<uint4*>(base + kRecPl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = zb::smem_addr(smem_raw);
@@ -252,6 +304,7 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepPara
   const uint32_t sbase = raw_addr + pad;
   PrepSmall& sm = *reinterpret_cast<PrepSmall*>(base + kPrepSmall);
   float* Tf = reinterpret_cast<float*>(base + kPrepTf);
+  float* Ys = reinterpret_cast<float*>(base + kPrepYs);
   float* G = reinterpret_cast<float*>(base + kRecG);
   float* gam = reinterpret_cast<float*>(base + kRecGam);
   float* bet = reinterpret_cast<float*>(base + kRecBet);
@@ -322,6 +375,25 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepPara
     ef[2 * lane + 1] = expf(gC - g1);
     bet[2 * lane] = sm.braw[2 * lane];
     bet[2 * lane + 1] = sm.braw[2 * lane + 1];
+    // factored decays: e^{G_t - G_s} = e^{G_t - G_{16i}} e^{G_{16i} - G_s} for t in row block i and s <= t. With
+    // every g <= 0 (G non-increasing) and at most 80 of decay inside any 16-token block, both factors lie in
+    // [0, e^80] and the product is the decay to rounding; otherwise the per-element path is used.
+    __syncwarp();
+    const float blk_range = G[(lane & 3) * 16] - G[(lane & 3) * 16 + 15];
+    const bool fast = __all_sync(0xffffffffu, a0 <= 0.f && a1 <= 0.f && blk_range <= 80.f);
+    if (lane == 0) sm.fast = fast ? 1 : 0;
+    if (fast) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = 2 * lane + u;
+        sm.rf[t] = expf(G[t] - G[t & ~15]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = 32 * u + lane, i = e >> 6, sidx = e & 63;
+        sm.cf[e] = sidx < 16 * (i + 1) ? expf(G[16 * i] - G[sidx]) : 0.f;
+      }
+    }
   }
   __syncthreads();
   bool ok = zb::mbar_wait_bounded(bar, 0, p.status, zb::kStatusPrefillTimeout);
@@ -333,40 +405,11 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepPara
     tmem_ld32_nowait(tl, r0);
     tmem_ld32_nowait(tl + 32, r1);
     tmem_ld_wait();
-    const int row = tid, t = row & (C - 1);
-    const float Gt = G[t];
-    if (row < C) {
-      const float bt = bet[t];
-      float* dst = Tf + t * LC;
-#pragma unroll
-      for (int s = 0; s < C; s += 4) {
-        float4 a;
-        float* av = &a.x;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int ss = s + e;
-          const float x = __uint_as_float(ss < 32 ? r0[ss] : r1[ss - 32]);
-          av[e] = ss < t ? bt * expf(Gt - G[ss]) * x : 0.f;
-        }
-        *reinterpret_cast<float4*>(dst + s) = a;
-      }
-    } else {
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int s0 = 8 * ch + e;
-          const float x0 = __uint_as_float(s0 < 32 ? r0[s0] : r1[s0 - 32]);
-          const float x1 = __uint_as_float(s0 + 1 < 32 ? r0[s0 + 1] : r1[s0 + 1 - 32]);
-          const float p0 = s0 <= t ? p.scale * expf(Gt - G[s0]) * x0 : 0.f;
-          const float p1 = s0 + 1 <= t ? p.scale * expf(Gt - G[s0 + 1]) * x1 : 0.f;
-          split_pair(p0, p1, hv[e / 2], lv[e / 2]);
-        }
-        *reinterpret_cast<uint4*>(base + kRecPh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(base + kRecPl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-      }
-    }
+    const int t = tid & (C - 1);
+    if (sm.fast)
+      decay_epilogue<true>(tid < C, t, r0, r1, G, bet, sm.rf, sm.cf, p.scale, Tf, base);
+    else
+      decay_epilogue<false>(tid < C, t, r0, r1, G, bet, sm.rf, sm.cf, p.scale, Tf, base);
   }
   __syncthreads();
 
@@ -384,83 +427,59 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepPara
     for (int r = 0; r < 16; ++r) Tf[(16 * b + r) * LC + 16 * b + j] = x[r];
   }
   __syncthreads();
-  if (warp < 3) {
-    // block column jb = warp: X_ij = -T_ii sum_{k=jb}^{i-1} A_ik X_kj for i = jb+1 .. 3 (X_jj = T_jj); thread =
-    // column j of the block column and half rh of every block's rows; results go straight into T hi / lo
-    const int jb = warp, j = lane & 15, rh = lane >> 4;
-    const int col = 16 * jb + j;
-    float Tk[4][16];
+  // ---- off-diagonal blocks row-block by row-block: for i = 1..3 and every j < i, Y_ij = sum_{k=j}^{i-1} A_ik T_kj,
+  // then T_ij = -T_ii Y_ij, written over A_ij (row-block i of A is not read again). Work unit: 4 columns of one row
+  // of one block (a strip); all 128 threads share each step.
+  for (int i = 1; i < 4; ++i) {
+    for (int st = tid; st < 64 * i; st += kPrepThreads) {
+      const int j = st >> 6, r = (st >> 2) & 15, cq = st & 3;
+      const float* arow = Tf + (16 * i + r) * LC;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = j; k < i; ++k) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int m = 0; m < 16; ++m) Tk[k][m] = k == jb ? Tf[(16 * k + m) * LC + 16 * k + j] : 0.f;
-#pragma unroll
-    for (int i = 1; i < 4; ++i) {
-      if (i <= jb) continue;
-      float y[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) y[r] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        if (k < jb || k >= i) continue;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const float* arow = Tf + (16 * i + 8 * rh + r) * LC + 16 * k;
-#pragma unroll
-          for (int m = 0; m < 16; m += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(arow + m);
-            y[r] = fmaf(a.x, Tk[k][m], fmaf(a.y, Tk[k][m + 1], fmaf(a.z, Tk[k][m + 2], fmaf(a.w, Tk[k][m + 3], y[r]))));
-          }
+        for (int m = 0; m < 16; ++m) {
+          const float a = arow[16 * k + m];
+          const float4 tv = *reinterpret_cast<const float4*>(Tf + (16 * k + m) * LC + 16 * j + 4 * cq);
+          acc.x = fmaf(a, tv.x, acc.x);
+          acc.y = fmaf(a, tv.y, acc.y);
+          acc.z = fmaf(a, tv.z, acc.z);
+          acc.w = fmaf(a, tv.w, acc.w);
         }
       }
-      float yf[16];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float other = __shfl_xor_sync(0xffffffffu, y[r], 16);
-        yf[r] = rh ? other : y[r];
-        yf[8 + r] = rh ? y[r] : other;
-      }
-      float x[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float* trow = Tf + (16 * i + 8 * rh + r) * LC + 16 * i;
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; m += 4) {
-          const float4 tv = *reinterpret_cast<const float4*>(trow + m);
-          acc = fmaf(tv.x, yf[m], fmaf(tv.y, yf[m + 1], fmaf(tv.z, yf[m + 2], fmaf(tv.w, yf[m + 3], acc))));
-        }
-        x[r] = -acc;
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float other = __shfl_xor_sync(0xffffffffu, x[r], 16);
-        Tk[i][r] = rh ? other : x[r];
-        Tk[i][8 + r] = rh ? x[r] : other;
-        const int t = 16 * i + 8 * rh + r;
-        const __nv_bfloat16 xh = __float2bfloat16_rn(x[r]);
-        *reinterpret_cast<__nv_bfloat16*>(base + kRecTh + sw128(t, col)) = xh;
-        *reinterpret_cast<__nv_bfloat16*>(base + kRecTl + sw128(t, col)) =
-            __float2bfloat16_rn(x[r] - __bfloat162float(xh));
-      }
+      *reinterpret_cast<float4*>(Ys + j * 256 + r * 16 + 4 * cq) = acc;
     }
-  } else {
-    // warp 3: the diagonal blocks and the zeros above them, 8 columns per store
-    for (int e = lane; e < C * 8; e += 32) {
-      const int t = e >> 3, ch = e & 7;
-      const int bi = t >> 4;
-      if (ch < 2 * bi) continue;  // strictly below the diagonal block: written by warps 0-2
-      uint32_t hv[4], lv[4];
+    __syncthreads();
+    for (int st = tid; st < 64 * i; st += kPrepThreads) {
+      const int j = st >> 6, r = (st >> 2) & 15, cq = st & 3;
+      const float* trow = Tf + (16 * i + r) * LC + 16 * i;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; u += 2) {
-        const int s = 8 * ch + u;
-        const float v0 = (s >> 4) == bi ? Tf[t * LC + s] : 0.f;
-        const float v1 = (s >> 4) == bi ? Tf[t * LC + s + 1] : 0.f;
-        split_pair(v0, v1, hv[u / 2], lv[u / 2]);
+      for (int m = 0; m < 16; ++m) {
+        const float tv = trow[m];
+        const float4 y = *reinterpret_cast<const float4*>(Ys + j * 256 + m * 16 + 4 * cq);
+        acc.x = fmaf(tv, y.x, acc.x);
+        acc.y = fmaf(tv, y.y, acc.y);
+        acc.z = fmaf(tv, y.z, acc.z);
+        acc.w = fmaf(tv, y.w, acc.w);
       }
-      *reinterpret_cast<uint4*>(base + kRecTh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-      *reinterpret_cast<uint4*>(base + kRecTl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+      *reinterpret_cast<float4*>(Tf + (16 * i + r) * LC + 16 * j + 4 * cq) =
+          make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
+    __syncthreads();
+  }
+  // ---- T hi / lo into the record: Tf below and on the diagonal blocks, zero above them (8 columns per store)
+  for (int e = tid; e < C * 8; e += kPrepThreads) {
+    const int t = e >> 3, ch = e & 7;
+    const bool zero = (ch >> 1) > (t >> 4);
+    uint32_t hv[4], lv[4];
+#pragma unroll
+    for (int u = 0; u < 8; u += 2) {
+      const float v0 = zero ? 0.f : Tf[t * LC + 8 * ch + u];
+      const float v1 = zero ? 0.f : Tf[t * LC + 8 * ch + u + 1];
+      split_pair(v0, v1, hv[u / 2], lv[u / 2]);
+    }
+    *reinterpret_cast<uint4*>(base + kRecTh + sw128_chunk(t, ch)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4*>(base + kRecTl + sw128_chunk(t, ch)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
   }
   fence_proxy_async();  // record staging (generic writes) -> bulk copy
   tc_fence_before();
@@ -561,48 +580,70 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
     tmem_st_wait();
   }
 
-  if (nchunks > 0) load_chunk(0, 0);
-
   auto wait_bar = [&](uint32_t bar, uint32_t parity) {
     if (!zb::mbar_wait_bounded(bar, parity, p.status, zb::kStatusPrefillTimeout)) sm.abort = 1;
   };
+  // chunk c's K / Q / V and record have landed (this thread's cp.async and the record's bulk copy)
+  auto wait_loads = [&](int c) {
+    cp_async_wait_all();
+    wait_bar(zb::smem_addr(&sm.bar_rec[c & 1]), (uint32_t)((c >> 1) & 1));
+    fence_proxy_async();  // cp.async data -> tensor-core reads
+  };
+  // M2 of chunk c: (K S0)^T, (Q S0)^T
+  auto issue_m2 = [&](int c) {
+    if (tid != 0) return;
+    const uint32_t kq = sbase + kOffKQ + (c & 1) * kKQBytes;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+      mma_ts(tmem + kColKS, tmem + kColSh + 8 * ks, desc_sw128(kq + off), idesc_m128(128), ks > 0);
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+      mma_ts(tmem + kColKS, tmem + kColSl + 8 * ks, desc_sw128(kq + off), idesc_m128(128), 1);
+    }
+    mma_commit(bar_m2);
+  };
+
+  // Pipeline: M2 of a chunk is issued as soon as the previous chunk's state split is in TMEM, before that chunk's
+  // output rows are written and before the loads of the chunk after it are issued.
+  if (nchunks > 0) {
+    load_chunk(0, 0);
+    wait_loads(0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (!sm.abort) {
+      issue_m2(0);
+      if (nchunks > 1) load_chunk(1, 1);
+    }
+  }
 
   for (int c = 0; c < nchunks; ++c) {
+    if (sm.abort) break;
     const int b = c & 1;
     const uint32_t ph = (uint32_t)(c & 1);
-    const uint32_t kq = sbase + kOffKQ + b * kKQBytes;
     const uint32_t rec = sbase + kOffRec + b * kRecSlot;
     const unsigned char* recp = base + kOffRec + b * kRecSlot;
     const float* gam = reinterpret_cast<const float*>(recp + kRecGam);
     const float* bet = reinterpret_cast<const float*>(recp + kRecBet);
     const float* ef = reinterpret_cast<const float*>(recp + kRecEf);
     const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(base + kOffV + b * kVBytes);
-    cp_async_wait_all();
-    wait_bar(zb::smem_addr(&sm.bar_rec[b]), (uint32_t)((c >> 1) & 1));
-    fence_proxy_async();  // cp.async data -> tensor-core reads
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (sm.abort) break;
-    if (c + 1 < nchunks) load_chunk(b ^ 1, c + 1);
-
-    // ---- M2: (K S0)^T, (Q S0)^T
-    if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-        mma_ts(tmem + kColKS, tmem + kColSh + 8 * ks, desc_sw128(kq + off), idesc_m128(128), ks > 0);
-      }
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-        mma_ts(tmem + kColKS, tmem + kColSl + 8 * ks, desc_sw128(kq + off), idesc_m128(128), 1);
-      }
-      mma_commit(bar_m2);
-    }
 
     if (half == 1) {
-      // (fK)^T hi / lo: row dk, columns t (from the K rows of the KQ tile), while M2 runs
+      // while M2 runs (it does not touch the master): S^T *= gamma_C, then (fK)^T hi / lo (row dk, columns t, from
+      // the K rows of the KQ tile)
+      const float gamC = gam[C - 1];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        uint32_t m[32];
+        tmem_ld32_nowait(tl + kColMaster + 32 * part, m);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
+        tmem_st32(tl + kColMaster + 32 * part, m);
+      }
       const int dk = tid - 128;
       const unsigned char* kqp = base + kOffKQ + b * kKQBytes + (dk >> 6) * (128 * 128);
       const int dcol = dk & 63;
@@ -621,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
       }
     }
 
-    // ---- after M2: Y^T hi / lo into TMEM (warps 0-3); O^T *= scale gamma_t and S^T *= gamma_C (warps 4-7)
+    // ---- after M2: Y^T hi / lo into TMEM (warps 0-3); O^T *= scale gamma_t (warps 4-7)
     wait_bar(bar_m2, ph);
     tc_fence_after();
     if (half == 0) {
@@ -651,16 +692,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * (p.scale * gam[32 * part + j]));
         tmem_st32(tl + kColQS + 32 * part, r);
-      }
-      const float gamC = gam[C - 1];
-#pragma unroll
-      for (int part = 0; part < 4; ++part) {
-        uint32_t m[32];
-        tmem_ld32_nowait(tl + kColMaster + 32 * part, m);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
-        tmem_st32(tl + kColMaster + 32 * part, m);
       }
     }
     tmem_st_wait();
@@ -719,7 +750,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
     }
     wait_bar(bar_m4, ph);
     tc_fence_after();
-    // ---- S^T master -> hi / lo (warps 0-3 keys 0..63, warps 4-7 keys 64..127); O^T -> output rows
+    // ---- S^T master -> hi / lo for the next chunk (warps 0-3 keys 0..63, warps 4-7 keys 64..127); O^T into
+    // registers (M2 of the next chunk overwrites its columns)
+    uint32_t o[32];
     {
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
@@ -732,20 +765,33 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
         tmem_st16(tl + kColSh + 32 * half + 16 * part, hv);
         tmem_st16(tl + kColSl + 32 * half + 16 * part, lv);
       }
-      uint32_t o[32];
       tmem_ld32_nowait(tl + kColQS + 32 * half, o);
       tmem_ld_wait();
-      __nv_bfloat16* orow = p.out + (t_begin + (int64_t)c * C) * row_stride + (int64_t)h * D + row;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = 32 * half + j;
-        if ((int64_t)c * C + t < len) orow[(int64_t)t * row_stride] = __float2bfloat16_rn(__uint_as_float(o[j]));
-      }
     }
     tmem_st_wait();
+    if (c + 1 < nchunks) wait_loads(c + 1);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (c + 1 < nchunks && !sm.abort) {
+      issue_m2(c + 1);
+      if (c + 2 < nchunks) load_chunk(b, c + 2);  // chunk c's buffers are free: M4 has completed
+    }
+    // ---- O^T -> bf16 rows [t][v] staged over the (fK)^T hi tile (read by M4, which has completed), then written
+    // out as 256-byte rows (16 threads per row)
+    {
+      __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(base + kOffFKTh);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ostage[(32 * half + j) * D + row] = __float2bfloat16_rn(__uint_as_float(o[j]));
+    }
+    __syncthreads();
+    for (int e = tid; e < C * 16; e += kThreads) {
+      const int t = e >> 4, ch = e & 15;
+      if ((int64_t)c * C + t < len)
+        *reinterpret_cast<uint4*>(p.out + (t_begin + (int64_t)c * C + t) * row_stride + (int64_t)h * D + ch * 8) =
+            *reinterpret_cast<const uint4*>(base + kOffFKTh + t * 256 + ch * 16);
+    }
+    __syncthreads();  // the staging area is the next chunk's (fK)^T
   }
 
   if (p.final_state && !sm.abort) {
