@@ -22,16 +22,17 @@
 //   [256,320) (K S0)^T                   [320,384) (Q S0)^T, then O^T            [384,448) U^T
 //   [448,480) Y^T / U^T bf16 hi          [480,512) Y^T / U^T bf16 lo
 // Per chunk:  M2  S^T [K;Q]^T  (S hi, S lo)   (A: TMEM, B: K and Q rows)  -> (K S0)^T, (Q S0)^T
-//             threads: S^T *= gamma_C and (fK)^T hi/lo from K (during M2); Y^T hi/lo from M2 and V into TMEM;
-//             O^T *= scale gamma_t
+//             threads: Y^T hi/lo from M2 and V into TMEM; O^T *= scale gamma_t
 //             M3  Y^T T^T  (hh, hl, lh)                                   -> U^T
 //             threads: U^T hi/lo into TMEM
-//             M4  S^T += U^T (fK)  and  O^T += U^T P^T  (hh, hl, lh each)
-//             threads: S^T master -> hi/lo for the next chunk; O^T -> bf16 rows staged in shared memory, then
-//             written as 256-byte rows
-// The next chunk's K, Q, V (cp.async, zero-filled past the sequence end) and its prep record (one bulk copy) load
-// while the current one runs. Every mbarrier wait is bounded (~1 s); on expiry the kernel records
-// kStatusPrefillTimeout, stops, frees TMEM and returns.
+//             M4  S^T += U^T (fK)  and  O^T += U^T P^T  (hh, hl, lh each); meanwhile the threads build the next
+//                 chunk's (fK)^T hi/lo from its K rows (ldmatrix.trans / stmatrix, double-buffered tiles)
+//             threads: S^T master -> hi/lo for the next chunk's M2, master *= the next chunk's gamma_C (so M4 can
+//             accumulate onto it); then M2 of the next chunk is issued and this chunk's O^T is written as bf16 rows
+//             (staged in shared memory, 256-byte row stores) while it runs
+// K, Q and the prep record (one bulk copy) of a chunk load one chunk ahead (double-buffered); V has one buffer and
+// loads after the Y step of the chunk before; cp.async rows past the sequence end are zero-filled. Every mbarrier
+// wait is bounded (~1 s); on expiry the kernel records kStatusPrefillTimeout, stops, frees TMEM and returns.
 //
 // Chunk records are addressed by id = cu[s] / 64 + s + c for chunk c of sequence s: ids of one sequence are
 // consecutive and those of the next start higher, so ids lie in [0, ceil(N / 64) + num_seqs).
@@ -66,7 +67,8 @@ struct PrepSmall {
 constexpr uint32_t kPrepSmem = 1024 + kPrepSmall + sizeof(PrepSmall);
 
 // ---- state kernel
-constexpr int kThreads = 256;  // 8 warps
+constexpr int kEpiThreads = 256;             // warps 0-7: loads and the TMEM / shared-memory steps
+constexpr int kThreads = kEpiThreads + 32;   // warp 8: issues the tensor-core MMAs
 constexpr uint32_t kColMaster = 0, kColSh = 128, kColSl = 192, kColKS = 256, kColQS = 320, kColU = 384,
                    kColYh = 448, kColYl = 480;
 constexpr uint32_t kKQBytes = 2 * 128 * 128;           // 2 k-atoms of [128 rows][128 B]
@@ -74,11 +76,10 @@ constexpr uint32_t kVBytes = C * D * 2;                // row-major [t][v]
 constexpr uint32_t kFKTBytes = D * 128;                // [dk][t], one k-atom
 constexpr uint32_t kRecSlot = (kRecBytes + 1023) / 1024 * 1024;
 constexpr uint32_t kOffKQ = 0;                         // [2]
-constexpr uint32_t kOffV = kOffKQ + 2 * kKQBytes;      // [2]
-constexpr uint32_t kOffRec = kOffV + 2 * kVBytes;      // [2]
-constexpr uint32_t kOffFKTh = kOffRec + 2 * kRecSlot;
-constexpr uint32_t kOffFKTl = kOffFKTh + kFKTBytes;
-constexpr uint32_t kOffSmall = kOffFKTl + kFKTBytes;
+constexpr uint32_t kOffV = kOffKQ + 2 * kKQBytes;      // one buffer: the next chunk's V loads after this Y step
+constexpr uint32_t kOffRec = kOffV + kVBytes;          // [2]
+constexpr uint32_t kOffFKT = kOffRec + 2 * kRecSlot;   // [2] x (hi, lo)
+constexpr uint32_t kOffSmall = kOffFKT + 4 * kFKTBytes;
 struct Small {
   uint64_t bar_rec[2];
   uint64_t bar_m2, bar_m3, bar_m4;
@@ -209,10 +210,20 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// byte offset of element (row, col) in a one-atom 128B-swizzled K-major tile (bf16, 64 columns per row)
-__device__ __forceinline__ uint32_t sw128(int row, int col) {
-  return (uint32_t)(row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2);
+// four 8x8 b16 matrices, transposed on load: lane l addresses row (l % 8) of matrix (l / 8)
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
 }
+// four 8x8 b16 matrices stored (lane l addresses row (l % 8) of matrix (l / 8))
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
 // byte offset of 16-byte chunk `ch` (8 columns) of `row`
 __device__ __forceinline__ uint32_t sw128_chunk(int row, int ch) {
   return (uint32_t)(row * 128 + (((ch ^ row) & 7) << 4));
@@ -503,8 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
   Small& sm = *reinterpret_cast<Small*>(base + kOffSmall);
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const bool epi = tid < kEpiThreads;               // warps 0-7
+  const bool mma_thread = warp == kEpiThreads / 32 && lane == 0;
   const int quarter = warp & 3;             // TMEM lane quarter of this warp
-  const int half = warp >> 2;               // warps 0-3 and 4-7 split columns
+  const int half = (warp >> 2) & 1;         // warps 0-3 and 4-7 split columns
   const int row = 32 * quarter + lane;      // this thread's TMEM lane (value index)
   const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
   const int seq = blockIdx.x, h = blockIdx.y;
@@ -533,18 +546,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tl = tmem + lane_off;  // this warp's lane quarter
 
-  // ---- loads of chunk c into buffer b: K / Q / V rows by cp.async, the prep record by one bulk copy
+  // ---- loads: K / Q rows of chunk c into KQ[c & 1] (cp.async, one group) with its prep record (one bulk copy);
+  // V rows into the single V buffer (cp.async, its own group)
   int last_issued = -1;  // thread 0: chunk of the last record copy
-  auto load_chunk = [&](int b, int c) {
-    load_kq(sbase + kOffKQ + b * kKQBytes, p.k, p.q, t_begin, len, c, row_stride, h, tid, kThreads);
-    const uint32_t vb = sbase + kOffV + b * kVBytes;
-    for (int i = tid; i < C * 16; i += kThreads) {
-      const int t = i >> 4, cidx = i & 15;
-      const int64_t tok = (int64_t)c * C + t;
-      const bool ok = tok < len;
-      cp_async16(vb + t * 256 + cidx * 16, p.v + (t_begin + (ok ? tok : 0)) * row_stride + (int64_t)h * D + cidx * 8,
-                 ok);
-    }
+  auto load_kqrec = [&](int c) {
+    const int b = c & 1;
+    if (tid >= kEpiThreads) return;
+    load_kq(sbase + kOffKQ + b * kKQBytes, p.k, p.q, t_begin, len, c, row_stride, h, tid, kEpiThreads);
     cp_async_commit();
     if (tid == 0) {
       last_issued = c;
@@ -553,9 +561,91 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
       zb::bulk_g2s(sbase + kOffRec + b * kRecSlot, p.records + ((id0 + c) * p.H + h) * kRecBytes, kRecBytes, bar);
     }
   };
+  auto load_v = [&](int c) {
+    if (tid >= kEpiThreads) return;
+    for (int i = tid; i < C * 16; i += kEpiThreads) {
+      const int t = i >> 4, cidx = i & 15;
+      const int64_t tok = (int64_t)c * C + t;
+      const bool ok = tok < len;
+      cp_async16(sbase + kOffV + t * 256 + cidx * 16,
+                 p.v + (t_begin + (ok ? tok : 0)) * row_stride + (int64_t)h * D + cidx * 8, ok);
+    }
+    cp_async_commit();
+  };
+  auto wait_bar = [&](uint32_t bar, uint32_t parity) {
+    if (!zb::mbar_wait_bounded(bar, parity, p.status, zb::kStatusPrefillTimeout)) sm.abort = 1;
+  };
+  auto wait_rec = [&](int c) { wait_bar(zb::smem_addr(&sm.bar_rec[c & 1]), (uint32_t)((c >> 1) & 1)); };
+  auto rec_vec = [&](int c, uint32_t off) {
+    return reinterpret_cast<const float*>(base + kOffRec + (c & 1) * kRecSlot + off);
+  };
+  // M2 of chunk c: (K S0)^T, (Q S0)^T
+  auto issue_m2 = [&](int c) {
+    if (!mma_thread) return;
+    const uint32_t kq = sbase + kOffKQ + (c & 1) * kKQBytes;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+      mma_ts(tmem + kColKS, tmem + kColSh + 8 * ks, desc_sw128(kq + off), idesc_m128(128), ks > 0);
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+      mma_ts(tmem + kColKS, tmem + kColSl + 8 * ks, desc_sw128(kq + off), idesc_m128(128), 1);
+    }
+    mma_commit(bar_m2);
+  };
+  // (fK)^T hi / lo of chunk c into FKT[c & 1] from the K rows of KQ[c & 1]: ldmatrix.trans gives each lane the
+  // (t, t+1) pair of one key, stmatrix writes the [dk][t] tiles; per warp item: t-block tb (8 rows) x 32 keys
+  auto build_fkt = [&](int c) {
+    const uint32_t kqa = sbase + kOffKQ + (c & 1) * kKQBytes;
+    const uint32_t fh = sbase + kOffFKT + (c & 1) * 2 * kFKTBytes, fl = fh + kFKTBytes;
+    const float* ef = rec_vec(c, kRecEf);
+    const int mi = lane >> 3, r8 = lane & 7;
+#pragma unroll
+    for (int it = warp; it < 32; it += kEpiThreads / 32) {
+      const int tb = it & 7, dk0 = 32 * (it >> 3);
+      const int dkb = dk0 + 8 * mi;
+      uint32_t kv[4];
+      ldsm_x4_trans(kqa + (dkb >> 6) * (128 * 128) + sw128_chunk(8 * tb + r8, (dkb & 63) >> 3), kv);
+      const int t = 8 * tb + 2 * (lane & 3);
+      const float f0 = ef[t], f1 = ef[t + 1];
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kv[j]));
+        split_pair(f0 * kf.x, f1 * kf.y, hv[j], lv[j]);
+      }
+      const uint32_t drow = sw128_chunk(dk0 + 8 * mi + r8, tb);
+      stsm_x4(fh + drow, hv);
+      stsm_x4(fl + drow, lv);
+    }
+    fence_proxy_async();  // (fK)^T tiles -> tensor-core reads
+  };
 
-  // ---- initial state: S^T master and its hi / lo split (thread = value row, warp halves split the keys)
-  {
+  // output rows of chunk c from their staging tile (over (fK)^T hi of buffer c & 1): 16 threads per 256-byte row
+  auto write_rows = [&](int c) {
+    if (!epi) return;
+    const unsigned char* ostage = base + kOffFKT + (c & 1) * 2 * kFKTBytes;
+    for (int e = tid; e < C * 16; e += kEpiThreads) {
+      const int t = e >> 4, ch = e & 15;
+      if ((int64_t)c * C + t < len)
+        *reinterpret_cast<uint4*>(p.out + (t_begin + (int64_t)c * C + t) * row_stride + (int64_t)h * D + ch * 8) =
+            *reinterpret_cast<const uint4*>(ostage + t * 256 + ch * 16);
+    }
+  };
+
+  // ---- prologue: chunk 0's loads; S^T hi / lo = split(S0) for M2, master = gamma_C S0 (the decay of chunk 0
+  // applied ahead of M4); (fK)^T of chunk 0; M2 of chunk 0; chunk 1's K / Q and record
+  if (epi) {
+    if (nchunks > 0) {
+      load_kqrec(0);
+      load_v(0);
+      cp_async_wait_all();
+      wait_rec(0);
+      fence_proxy_async();
+    }
+    const float gamC = nchunks > 0 ? rec_vec(0, kRecGam)[C - 1] : 1.f;
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
       const int k0 = 64 * half + 32 * part;
@@ -570,139 +660,72 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
         m[j + 2] = __float_as_uint(s.z);
         m[j + 3] = __float_as_uint(s.w);
       }
-      tmem_st32(tl + kColMaster + k0, m);
       uint32_t hi[16], lo[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(m[j]), __uint_as_float(m[j + 1]), hi[j / 2], lo[j / 2]);
       tmem_st16(tl + kColSh + 32 * half + 16 * part, hi);
       tmem_st16(tl + kColSl + 32 * half + 16 * part, lo);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
+      tmem_st32(tl + kColMaster + k0, m);
     }
+    if (nchunks > 0) build_fkt(0);
     tmem_st_wait();
   }
-
-  auto wait_bar = [&](uint32_t bar, uint32_t parity) {
-    if (!zb::mbar_wait_bounded(bar, parity, p.status, zb::kStatusPrefillTimeout)) sm.abort = 1;
-  };
-  // chunk c's K / Q / V and record have landed (this thread's cp.async and the record's bulk copy)
-  auto wait_loads = [&](int c) {
-    cp_async_wait_all();
-    wait_bar(zb::smem_addr(&sm.bar_rec[c & 1]), (uint32_t)((c >> 1) & 1));
-    fence_proxy_async();  // cp.async data -> tensor-core reads
-  };
-  // M2 of chunk c: (K S0)^T, (Q S0)^T
-  auto issue_m2 = [&](int c) {
-    if (tid != 0) return;
-    const uint32_t kq = sbase + kOffKQ + (c & 1) * kKQBytes;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-      mma_ts(tmem + kColKS, tmem + kColSh + 8 * ks, desc_sw128(kq + off), idesc_m128(128), ks > 0);
-    }
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-      mma_ts(tmem + kColKS, tmem + kColSl + 8 * ks, desc_sw128(kq + off), idesc_m128(128), 1);
-    }
-    mma_commit(bar_m2);
-  };
-
-  // Pipeline: M2 of a chunk is issued as soon as the previous chunk's state split is in TMEM, before that chunk's
-  // output rows are written and before the loads of the chunk after it are issued.
-  if (nchunks > 0) {
-    load_chunk(0, 0);
-    wait_loads(0);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (!sm.abort) {
-      issue_m2(0);
-      if (nchunks > 1) load_chunk(1, 1);
-    }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (nchunks > 0 && !sm.abort) {
+    issue_m2(0);
+    if (nchunks > 1) load_kqrec(1);
   }
 
+  // ---- chunks. Per chunk c the tensor-core chain is M2 -> M3 -> M4 -> M2(c + 1), issued by warp 8; warps 0-7 do
+  // the Y, U and state-split steps between them, build (fK)^T of chunk c + 1 during M4 and write chunk c's output
+  // rows during M2(c + 1). Every __syncthreads below is reached by all nine warps.
   for (int c = 0; c < nchunks; ++c) {
     if (sm.abort) break;
     const int b = c & 1;
+    const bool has_next = c + 1 < nchunks;
     const uint32_t ph = (uint32_t)(c & 1);
     const uint32_t rec = sbase + kOffRec + b * kRecSlot;
-    const unsigned char* recp = base + kOffRec + b * kRecSlot;
-    const float* gam = reinterpret_cast<const float*>(recp + kRecGam);
-    const float* bet = reinterpret_cast<const float*>(recp + kRecBet);
-    const float* ef = reinterpret_cast<const float*>(recp + kRecEf);
-    const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(base + kOffV + b * kVBytes);
+    const float* gam = rec_vec(c, kRecGam);
+    const float* bet = rec_vec(c, kRecBet);
+    const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(base + kOffV);
 
-    if (half == 1) {
-      // while M2 runs (it does not touch the master): S^T *= gamma_C, then (fK)^T hi / lo (row dk, columns t, from
-      // the K rows of the KQ tile)
-      const float gamC = gam[C - 1];
+    // ---- after M2: Y^T hi / lo into TMEM and O^T *= scale gamma_t; warps 0-3 columns t 0..31, warps 4-7 t 32..63
+    if (epi) {
+      wait_bar(bar_m2, ph);
+      tc_fence_after();
+      const int t0 = 32 * half;
+      uint32_t r[32];
+      tmem_ld32_nowait(tl + kColKS + t0, r);
+      tmem_ld_wait();
+      uint32_t hv[16], lv[16];
 #pragma unroll
-      for (int part = 0; part < 4; ++part) {
-        uint32_t m[32];
-        tmem_ld32_nowait(tl + kColMaster + 32 * part, m);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
-        tmem_st32(tl + kColMaster + 32 * part, m);
+      for (int j = 0; j < 32; j += 2) {
+        const int t = t0 + j;
+        const float y0 = bet[t] * (__bfloat162float(Vs[t * D + row]) - gam[t] * __uint_as_float(r[j]));
+        const float y1 =
+            bet[t + 1] * (__bfloat162float(Vs[(t + 1) * D + row]) - gam[t + 1] * __uint_as_float(r[j + 1]));
+        split_pair(y0, y1, hv[j / 2], lv[j / 2]);
       }
-      const int dk = tid - 128;
-      const unsigned char* kqp = base + kOffKQ + b * kKQBytes + (dk >> 6) * (128 * 128);
-      const int dcol = dk & 63;
-#pragma unroll 2
-      for (int tb = 0; tb < 8; ++tb) {
-        uint32_t hv[4], lv[4];
+      tmem_st16(tl + kColYh + 16 * half, hv);
+      tmem_st16(tl + kColYl + 16 * half, lv);
+      tmem_ld32_nowait(tl + kColQS + t0, r);
+      tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const int t = 8 * tb + i;
-          const float k0 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(kqp + sw128(t, dcol)));
-          const float k1 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(kqp + sw128(t + 1, dcol)));
-          split_pair(ef[t] * k0, ef[t + 1] * k1, hv[i / 2], lv[i / 2]);
-        }
-        *reinterpret_cast<uint4*>(base + kOffFKTh + sw128_chunk(dk, tb)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(base + kOffFKTl + sw128_chunk(dk, tb)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-      }
+      for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * (p.scale * gam[t0 + j]));
+      tmem_st32(tl + kColQS + t0, r);
+      tmem_st_wait();
     }
-
-    // ---- after M2: Y^T hi / lo into TMEM (warps 0-3); O^T *= scale gamma_t (warps 4-7)
-    wait_bar(bar_m2, ph);
-    tc_fence_after();
-    if (half == 0) {
-#pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t r[32];
-        tmem_ld32_nowait(tl + kColKS + 32 * part, r);
-        tmem_ld_wait();
-        uint32_t hv[16], lv[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int t = 32 * part + j;
-          const float y0 = bet[t] * (__bfloat162float(Vs[t * D + row]) - gam[t] * __uint_as_float(r[j]));
-          const float y1 =
-              bet[t + 1] * (__bfloat162float(Vs[(t + 1) * D + row]) - gam[t + 1] * __uint_as_float(r[j + 1]));
-          split_pair(y0, y1, hv[j / 2], lv[j / 2]);
-        }
-        tmem_st16(tl + kColYh + 16 * part, hv);
-        tmem_st16(tl + kColYl + 16 * part, lv);
-      }
-    } else {
-#pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t r[32];
-        tmem_ld32_nowait(tl + kColQS + 32 * part, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * (p.scale * gam[32 * part + j]));
-        tmem_st32(tl + kColQS + 32 * part, r);
-      }
-    }
-    tmem_st_wait();
-    fence_proxy_async();  // (fK)^T tiles -> tensor-core reads
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (sm.abort) break;
 
-    // ---- M3: U^T = Y^T T^T
-    if (tid == 0) {
+    // ---- M3: U^T = Y^T T^T; the V buffer is free again: the next chunk's V loads meanwhile
+    if (mma_thread) {
       const uint32_t th = rec + kRecTh, tlo = rec + kRecTl;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
@@ -715,10 +738,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
         mma_ts(tmem + kColU, tmem + kColYl + 8 * ks, desc_sw128(th + 32 * ks), idesc_m128(64), 1);
       mma_commit(bar_m3);
     }
-    wait_bar(bar_m3, ph);
-    tc_fence_after();
-    // ---- U^T hi / lo into TMEM (over Y^T): warps 0-3 columns t 0..31, warps 4-7 t 32..63
-    {
+    if (epi) {
+      if (has_next) load_v(c + 1);
+      wait_bar(bar_m3, ph);
+      tc_fence_after();
+      // U^T hi / lo into TMEM (over Y^T): warps 0-3 columns t 0..31, warps 4-7 t 32..63
       uint32_t r[32];
       tmem_ld32_nowait(tl + kColU + 32 * half, r);
       tmem_ld_wait();
@@ -727,16 +751,22 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
       for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), hv[j / 2], lv[j / 2]);
       tmem_st16(tl + kColYh + 16 * half, hv);
       tmem_st16(tl + kColYl + 16 * half, lv);
+      tmem_st_wait();
+      if (has_next) {  // chunk c + 1's K / Q (all groups but the newest, its V) and record
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        wait_rec(c + 1);
+        fence_proxy_async();
+      }
     }
-    tmem_st_wait();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (sm.abort) break;
 
     // ---- M4: S^T += U^T (fK);  O^T += U^T P^T
-    if (tid == 0) {
-      const uint32_t fh = sbase + kOffFKTh, fl = sbase + kOffFKTl, pph = rec + kRecPh, ppl = rec + kRecPl;
+    if (mma_thread) {
+      const uint32_t fh = sbase + kOffFKT + b * 2 * kFKTBytes, fl = fh + kFKTBytes;
+      const uint32_t pph = rec + kRecPh, ppl = rec + kRecPl;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         mma_ts(tmem + kColMaster, tmem + kColYh + 8 * ks, desc_sw128(fh + 32 * ks), idesc_m128(128), 1);
@@ -748,53 +778,55 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
       }
       mma_commit(bar_m4);
     }
-    wait_bar(bar_m4, ph);
-    tc_fence_after();
-    // ---- S^T master -> hi / lo for the next chunk (warps 0-3 keys 0..63, warps 4-7 keys 64..127); O^T into
-    // registers (M2 of the next chunk overwrites its columns)
+    // ---- S^T master -> hi / lo for M2 of the next chunk and master *= its gamma_C (warps 0-3 keys 0..63, warps
+    // 4-7 keys 64..127); O^T into registers (M2 of the next chunk overwrites its columns)
     uint32_t o[32];
-    {
+    if (epi) {
+      if (has_next) build_fkt(c + 1);
+      wait_bar(bar_m4, ph);
+      tc_fence_after();
+      const float gamC = has_next ? rec_vec(c + 1, kRecGam)[C - 1] : 1.f;
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
+        const uint32_t col = 64 * half + 32 * part;
         uint32_t m[32];
-        tmem_ld32_nowait(tl + kColMaster + 64 * half + 32 * part, m);
+        tmem_ld32_nowait(tl + kColMaster + col, m);
         tmem_ld_wait();
         uint32_t hv[16], lv[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) split_pair(__uint_as_float(m[j]), __uint_as_float(m[j + 1]), hv[j / 2], lv[j / 2]);
         tmem_st16(tl + kColSh + 32 * half + 16 * part, hv);
         tmem_st16(tl + kColSl + 32 * half + 16 * part, lv);
+        if (has_next) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) m[j] = __float_as_uint(__uint_as_float(m[j]) * gamC);
+          tmem_st32(tl + kColMaster + col, m);
+        }
       }
       tmem_ld32_nowait(tl + kColQS + 32 * half, o);
       tmem_ld_wait();
+      tmem_st_wait();
+      if (has_next) cp_async_wait_all();  // chunk c + 1's V (read by its Y step)
     }
-    tmem_st_wait();
-    if (c + 1 < nchunks) wait_loads(c + 1);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (c + 1 < nchunks && !sm.abort) {
+    if (has_next && !sm.abort) {
       issue_m2(c + 1);
-      if (c + 2 < nchunks) load_chunk(b, c + 2);  // chunk c's buffers are free: M4 has completed
+      if (c + 2 < nchunks) load_kqrec(c + 2);  // chunk c's KQ and record buffers are free: M4 has completed
     }
-    // ---- O^T -> bf16 rows [t][v] staged over the (fK)^T hi tile (read by M4, which has completed), then written
-    // out as 256-byte rows (16 threads per row)
-    {
-      __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(base + kOffFKTh);
+    // ---- O^T -> bf16 rows [t][v] staged over chunk c's (fK)^T hi tile (M4 has completed; the tile is next written
+    // for chunk c + 2, during M4 of chunk c + 1), then written out as 256-byte rows while M2 of the next chunk runs
+    if (epi) {
+      __nv_bfloat16* os = reinterpret_cast<__nv_bfloat16*>(base + kOffFKT + b * 2 * kFKTBytes);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ostage[(32 * half + j) * D + row] = __float2bfloat16_rn(__uint_as_float(o[j]));
+      for (int j = 0; j < 32; ++j) os[(32 * half + j) * D + row] = __float2bfloat16_rn(__uint_as_float(o[j]));
     }
     __syncthreads();
-    for (int e = tid; e < C * 16; e += kThreads) {
-      const int t = e >> 4, ch = e & 15;
-      if ((int64_t)c * C + t < len)
-        *reinterpret_cast<uint4*>(p.out + (t_begin + (int64_t)c * C + t) * row_stride + (int64_t)h * D + ch * 8) =
-            *reinterpret_cast<const uint4*>(base + kOffFKTh + t * 256 + ch * 16);
-    }
-    __syncthreads();  // the staging area is the next chunk's (fK)^T
+    write_rows(c);
   }
 
-  if (p.final_state && !sm.abort) {
+  if (p.final_state && !sm.abort && epi) {
     float* dst = p.final_state + ((slot * p.H + h) * D + row) * (int64_t)D + 64 * half;
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
