@@ -82,7 +82,7 @@ constexpr uint32_t kOffFKT = kOffRec + 2 * kRecSlot;   // [2] x (hi, lo)
 constexpr uint32_t kOffSmall = kOffFKT + 4 * kFKTBytes;
 struct Small {
   uint64_t bar_rec[2];
-  uint64_t bar_m2, bar_m3, bar_m4;
+  uint64_t bar_m2, bar_m3, bar_m4, bar_m4o;
   uint32_t tmem_base;
   int abort;
 };
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
   const int64_t slot = p.state_slots ? p.state_slots[seq] : seq;
   const int64_t id0 = t_begin / C + seq;  // record id of chunk 0
   const uint32_t bar_m2 = zb::smem_addr(&sm.bar_m2), bar_m3 = zb::smem_addr(&sm.bar_m3);
-  const uint32_t bar_m4 = zb::smem_addr(&sm.bar_m4);
+  const uint32_t bar_m4 = zb::smem_addr(&sm.bar_m4), bar_m4o = zb::smem_addr(&sm.bar_m4o);
 
   if (tid == 0) {
     zb::mbar_init(zb::smem_addr(&sm.bar_rec[0]), 1);
@@ -536,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
     zb::mbar_init(bar_m2, 1);
     zb::mbar_init(bar_m3, 1);
     zb::mbar_init(bar_m4, 1);
+    zb::mbar_init(bar_m4o, 1);
     sm.abort = 0;
     zb::fence_mbar_init();
   }
@@ -763,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
     tc_fence_after();
     if (sm.abort) break;
 
-    // ---- M4: S^T += U^T (fK);  O^T += U^T P^T
+    // ---- M4: S^T += U^T (fK) (committed first: the state split starts while the rest runs);  O^T += U^T P^T
     if (mma_thread) {
       const uint32_t fh = sbase + kOffFKT + b * 2 * kFKTBytes, fl = fh + kFKTBytes;
       const uint32_t pph = rec + kRecPh, ppl = rec + kRecPl;
@@ -772,11 +773,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
         mma_ts(tmem + kColMaster, tmem + kColYh + 8 * ks, desc_sw128(fh + 32 * ks), idesc_m128(128), 1);
         mma_ts(tmem + kColMaster, tmem + kColYh + 8 * ks, desc_sw128(fl + 32 * ks), idesc_m128(128), 1);
         mma_ts(tmem + kColMaster, tmem + kColYl + 8 * ks, desc_sw128(fh + 32 * ks), idesc_m128(128), 1);
+      }
+      mma_commit(bar_m4);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
         mma_ts(tmem + kColQS, tmem + kColYh + 8 * ks, desc_sw128(pph + 32 * ks), idesc_m128(64), 1);
         mma_ts(tmem + kColQS, tmem + kColYh + 8 * ks, desc_sw128(ppl + 32 * ks), idesc_m128(64), 1);
         mma_ts(tmem + kColQS, tmem + kColYl + 8 * ks, desc_sw128(pph + 32 * ks), idesc_m128(64), 1);
       }
-      mma_commit(bar_m4);
+      mma_commit(bar_m4o);
     }
     // ---- S^T master -> hi / lo for M2 of the next chunk and master *= its gamma_C (warps 0-3 keys 0..63, warps
     // 4-7 keys 64..127); O^T into registers (M2 of the next chunk overwrites its columns)
@@ -803,6 +808,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StatePar
           tmem_st32(tl + kColMaster + col, m);
         }
       }
+      wait_bar(bar_m4o, ph);
+      tc_fence_after();
       tmem_ld32_nowait(tl + kColQS + 32 * half, o);
       tmem_ld_wait();
       tmem_st_wait();
