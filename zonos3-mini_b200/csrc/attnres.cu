@@ -230,19 +230,21 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
     zb::mbar_wait_bounded(zb::smem_addr(&bars[s]), 0, p.status, zb::kStatusAttnresLoadTimeout);
     const __nv_bfloat16* row = tiles + (size_t)s * C;
     const uint64_t rr2 = splat_x2(inv);
-    uint64_t lg2 = 0;
+    uint64_t lg2[2] = {0, 0};  // two accumulators: independent add chains
+    uint4 x[kLaneVecs];
+#pragma unroll
+    for (int v = 0; v < kLaneVecs; ++v) x[v] = *reinterpret_cast<const uint4*>(row + v * 256 + lane * 8);
 #pragma unroll
     for (int v = 0; v < kLaneVecs; ++v) {
-      const uint4 x = *reinterpret_cast<const uint4*>(row + v * 256 + lane * 8);
-      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+      const uint32_t w[4] = {x[v].x, x[v].y, x[v].z, x[v].w};
       const uint32_t qq[4] = {q4[v].x, q4[v].y, q4[v].z, q4[v].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t key = x2_to_bf2(mul_x2(bf2_to_x2(w[k]), rr2));  // bf16(v * inv_rms), two at once
-        lg2 = add_x2(lg2, bf2_to_x2(hmul2_bits(key, qq[k])));          // + bf16(key * q)
+        lg2[k & 1] = add_x2(lg2[k & 1], bf2_to_x2(hmul2_bits(key, qq[k])));  // + bf16(key * q)
       }
     }
-    publish(zb::warp_sum(sum_x2(lg2)), xlg + (size_t)rank * ns + s, &xbar[1], CL, rank, lane);
+    publish(zb::warp_sum(sum_x2(add_x2(lg2[0], lg2[1]))), xlg + (size_t)rank * ns + s, &xbar[1], CL, rank, lane);
   }
 
   // every warp: logits (rank-ordered sums), fp32 softmax, bf16 weights into its own row
@@ -252,15 +254,27 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
     for (int r = 0; r < CL; ++r) total += xlg[(size_t)r * ns + s];
     return total;
   };
+  constexpr int kPerLane = kMaxSources / 32;
+  float lv[kPerLane];
   float m = -INFINITY;
-  for (int s = lane; s < ns; s += 32) m = fmaxf(m, logit(s));
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int s = lane + 32 * i;
+    lv[i] = s < ns ? logit(s) : -INFINITY;
+    m = fmaxf(m, lv[i]);
+  }
   m = zb::warp_max(m);
   float den = 0.f;
-  for (int s = lane; s < ns; s += 32) den += expf(logit(s) - m);
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    lv[i] = lane + 32 * i < ns ? expf(lv[i] - m) : 0.f;
+    den += lv[i];
+  }
   den = zb::warp_sum(den);
-  for (int s = lane; s < ns; s += 32) {
-    const __nv_bfloat16 wb = __float2bfloat16_rn(expf(logit(s) - m) / den);
-    wp[s] = (uint32_t)__bfloat16_as_ushort(wb) * 0x10001u;
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int s = lane + 32 * i;
+    if (s < ns) wp[s] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lv[i] / den)) * 0x10001u;
   }
   __syncwarp();
 
@@ -269,23 +283,31 @@ __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParam
   const int cc = tid * kColsT;
   const bool mixer = cc < C;
   {
-    uint64_t acc[kColsT / 2];
+    uint64_t acc[kColsT / 2], acc_odd[kColsT / 2];  // even and odd sources: two independent add chains
 #pragma unroll
-    for (int j = 0; j < kColsT / 2; ++j) acc[j] = 0;
+    for (int j = 0; j < kColsT / 2; ++j) acc[j] = acc_odd[j] = 0;
     if (mixer) {
-#pragma unroll 4
-      for (int s = 0; s < ns; ++s) {
+      auto term = [&](int s, uint64_t (&a)[kColsT / 2]) {
         const uint32_t w2 = wp[s];
         const __nv_bfloat16* row = tiles + (size_t)s * C + cc;
         if constexpr (kColsT == 4) {
           const uint2 v = *reinterpret_cast<const uint2*>(row);
-          acc[0] = add_x2(acc[0], bf2_to_x2(hmul2_bits(v.x, w2)));  // + bf16(v * w), two at once
-          acc[1] = add_x2(acc[1], bf2_to_x2(hmul2_bits(v.y, w2)));
+          a[0] = add_x2(a[0], bf2_to_x2(hmul2_bits(v.x, w2)));  // + bf16(v * w), two at once
+          a[1] = add_x2(a[1], bf2_to_x2(hmul2_bits(v.y, w2)));
         } else {
-          acc[0] = add_x2(acc[0], bf2_to_x2(hmul2_bits(*reinterpret_cast<const uint32_t*>(row), w2)));
+          a[0] = add_x2(a[0], bf2_to_x2(hmul2_bits(*reinterpret_cast<const uint32_t*>(row), w2)));
         }
+      };
+      int s = 0;
+#pragma unroll 2
+      for (; s + 1 < ns; s += 2) {
+        term(s, acc);
+        term(s + 1, acc_odd);
       }
+      if (s < ns) term(s, acc);
     }
+#pragma unroll
+    for (int j = 0; j < kColsT / 2; ++j) acc[j] = add_x2(acc[j], acc_odd[j]);
 #pragma unroll
     for (int j = 0; j < kColsT / 2; ++j) {
       mix[2 * j] = __uint_as_float((uint32_t)acc[j]);
