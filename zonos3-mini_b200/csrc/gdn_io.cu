@@ -6,10 +6,10 @@
 //   conv = SiLU(depthwise causal conv, kernel W, over the qkv channels, continuing each sequence's history)
 //   q, k = conv_q, conv_k * rsqrt(sum^2 + 1e-6) per head;  v = conv_v
 //   g = -exp(A_log) * softplus(a + dt_bias)  (log decay);  beta = sigmoid(b)
-// One CTA per token; a warp covers one 128-wide head slice (4 channels per lane), so the per-head L2 norm is a warp
-// reduction. History rows before a sequence's first token come from conv_state [slot, channels, W-1] (the layout of
-// LMCache.conv_state); a second small kernel then writes each sequence's new history (its last W-1 inputs), after
-// every token has read the old one.
+// One CTA per (token, q / k / v part); a warp covers one head slice (D / 32 channels per lane), so the per-head L2
+// norm is a warp reduction. History rows before a sequence's first token come from conv_state [slot, channels, W-1]
+// (the layout of LMCache.conv_state); a second small kernel then writes each sequence's new history (its last W-1
+// inputs), after every token has read the old one.
 //
 // Epilogue (replaces FLA layer_norm_gated_fwd, gdn.py:435-445; lm.py:585-587): gated = RMSNorm(o; out_weight,
 // 1e-5) * SiLU(z) per head, computed in fp32 and rounded once to bf16; one warp per (token, head).
@@ -42,9 +42,33 @@ struct PrologueParams {
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 
-__global__ void __launch_bounds__(256) gdn_prologue_kernel(PrologueParams p) {
+// PL consecutive bf16 values (PL = 1, 2 or 4; 2- / 4- / 8-byte aligned) as floats
+template <int PL>
+__device__ __forceinline__ void load_bf(const __nv_bfloat16* src, float (&out)[PL]) {
+  if constexpr (PL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
+    out[0] = __uint_as_float(u.x << 16);
+    out[1] = __uint_as_float(u.x & 0xffff0000u);
+    out[2] = __uint_as_float(u.y << 16);
+    out[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else if constexpr (PL == 2) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
+    out[0] = __uint_as_float(u << 16);
+    out[1] = __uint_as_float(u & 0xffff0000u);
+  } else {
+#pragma unroll
+    for (int j = 0; j < PL; ++j) out[j] = __bfloat162float(src[j]);
+  }
+}
+
+// One CTA per (token, part): part 0 = q, 1 = k, 2 = v; warp h covers head h's D channels, lane owns PL = D / 32
+// consecutive channels. Every input of a lane (its PL x W weights, the history rows and the rows of this sequence)
+// is loaded before any arithmetic.
+template <int PL>
+__global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
   const int64_t tok = blockIdx.x;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int part = blockIdx.y;
+  const int h = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int inner = p.H * p.D;
   const int seq = p.seq_of_token[tok];
   const int64_t start = p.cu_seqlens[seq];
@@ -53,48 +77,68 @@ __global__ void __launch_bounds__(256) gdn_prologue_kernel(PrologueParams p) {
   // a padding sequence (graph padding rows) reads a zero history and never writes one
   const bool fresh = (p.fresh ? p.fresh[seq] != 0 : false) || slot < 0 || slot >= p.rows;
   const __nv_bfloat16* row = p.mixed + tok * p.mixed_stride;
-  // 3H head slices of D channels: slice s covers channels [s*D, (s+1)*D); lane owns D/32 consecutive channels
-  const int per_lane = p.D / 32;
-  for (int slice = warp; slice < 3 * p.H; slice += 8) {
-    float acc[4];
-    const int c0 = slice * p.D + lane * per_lane;
-    for (int j = 0; j < per_lane; ++j) {
-      const int ch = c0 + j;
-      float a = 0.f;
+  const int ch0 = part * inner + h * p.D + lane * PL;
+
+  float wt[PL * kW];  // conv weights [channel][tap]
+  {
+    float tmp[4];
 #pragma unroll
-      for (int w = 0; w < kW; ++w) {
-        const int64_t back = kW - 1 - w;  // weight[w] multiplies the input `back` steps before this token
-        float x;
-        if (back <= pos) {
-          x = __bfloat162float(row[-back * p.mixed_stride + ch]);
-        } else {  // from the history: history index (W-1) - (back - pos)
-          const int64_t hidx = (kW - 1) - (back - pos);
-          x = fresh ? 0.f : __bfloat162float(p.conv_state[(slot * 3 * inner + ch) * (kW - 1) + hidx]);
-        }
-        a = fmaf(__bfloat162float(p.conv_w[ch * kW + w]), x, a);
-      }
-      acc[j] = zb::bf16_round(silu(a));  // the conv output is an activation of the model dtype
+    for (int j = 0; j < PL * kW; j += 4) {
+      load_bf<4>(p.conv_w + (int64_t)ch0 * kW + j, tmp);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) wt[j + u] = tmp[u];
     }
-    const int part = slice / p.H, head = slice % p.H;  // 0 = q, 1 = k, 2 = v
-    float scale = 1.f;
-    if (part < 2) {
-      float ss = 0.f;
-      for (int j = 0; j < per_lane; ++j) ss = fmaf(acc[j], acc[j], ss);
-      scale = rsqrtf(zb::warp_sum(ss) + 1e-6f);
-    }
-    __nv_bfloat16* dst = (part == 0 ? p.q : part == 1 ? p.k : p.v) + (tok * p.H + head) * p.D + lane * per_lane;
-    for (int j = 0; j < per_lane; ++j) dst[j] = __float2bfloat16_rn(acc[j] * scale);
   }
-  if (threadIdx.x < p.H) {
-    const int h = threadIdx.x;
-    const float a = __bfloat162float(row[4 * inner + h]);
-    const float b = __bfloat162float(row[4 * inner + p.H + h]);
-    p.g[tok * p.H + h] = -expf(p.A_log[h]) * softplus(a + p.dt_bias[h]);
-    p.beta[tok * p.H + h] = 1.f / (1.f + expf(-b));
+  float hist[PL * (kW - 1)];  // history [channel][entry], zero for a fresh sequence
+  if (!fresh && pos < kW - 1) {
+    const __nv_bfloat16* hp = p.conv_state + (slot * 3 * inner + ch0) * (kW - 1);
+#pragma unroll
+    for (int j = 0; j < PL * (kW - 1); ++j) hist[j] = __bfloat162float(hp[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < PL * (kW - 1); ++j) hist[j] = 0.f;
+  }
+  float xin[kW][PL];  // tap w = the input (W-1-w) steps before this token
+#pragma unroll
+  for (int w = 0; w < kW; ++w) {
+    const int64_t back = kW - 1 - w;
+    if (back <= pos) {
+      load_bf<PL>(row - back * p.mixed_stride + ch0, xin[w]);
+    } else {  // from the history: entry (W-1) - (back - pos)
+      const int64_t hidx = (kW - 1) - (back - pos);
+#pragma unroll
+      for (int j = 0; j < PL; ++j) xin[w][j] = hist[j * (kW - 1) + hidx];
+    }
+  }
+  float acc[PL];
+#pragma unroll
+  for (int j = 0; j < PL; ++j) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) a = fmaf(wt[j * kW + w], xin[w][j], a);
+    acc[j] = zb::bf16_round(silu(a));  // the conv output is an activation of the model dtype
+  }
+  float scale = 1.f;
+  if (part < 2) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PL; ++j) ss = fmaf(acc[j], acc[j], ss);
+    scale = rsqrtf(zb::warp_sum(ss) + 1e-6f);
+  }
+  __nv_bfloat16* dst = (part == 0 ? p.q : part == 1 ? p.k : p.v) + (tok * p.H + h) * p.D + lane * PL;
+#pragma unroll
+  for (int j = 0; j < PL; ++j) dst[j] = __float2bfloat16_rn(acc[j] * scale);
+  if (part == 0 && threadIdx.x < p.H) {
+    const int hh = threadIdx.x;
+    const float a = __bfloat162float(row[4 * inner + hh]);
+    const float b = __bfloat162float(row[4 * inner + p.H + hh]);
+    p.g[tok * p.H + hh] = -expf(p.A_log[hh]) * softplus(a + p.dt_bias[hh]);
+    p.beta[tok * p.H + hh] = 1.f / (1.f + expf(-b));
   }
 }
 
 // New history of every sequence: its last W-1 conv inputs (shifted in after the old history when it is shorter).
+// Grid (sequence, channel block): a thread owns 8 consecutive channels (24 history entries, 48 contiguous bytes).
 __global__ void __launch_bounds__(256) gdn_conv_history_kernel(PrologueParams p) {
   const int seq = blockIdx.x;
   const int64_t start = p.cu_seqlens[seq], len = p.cu_seqlens[seq + 1] - start;
@@ -102,21 +146,44 @@ __global__ void __launch_bounds__(256) gdn_conv_history_kernel(PrologueParams p)
   if (slot < 0 || slot >= p.rows) return;
   const bool fresh = p.fresh ? p.fresh[seq] != 0 : false;
   const int channels = 3 * p.H * p.D;
-  for (int ch = threadIdx.x; ch < channels; ch += blockDim.x) {
-    __nv_bfloat16* hist = p.conv_state + (slot * channels + ch) * (kW - 1);
-    float old[kW - 1];
+  const int ch = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (ch >= channels) return;
+  uint4* hist = reinterpret_cast<uint4*>(p.conv_state + (slot * channels + ch) * (kW - 1));
+  uint4 ov[3] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (!fresh && len < kW - 1) {
 #pragma unroll
-    for (int j = 0; j < kW - 1; ++j) old[j] = fresh ? 0.f : __bfloat162float(hist[j]);
+    for (int i = 0; i < 3; ++i) ov[i] = hist[i];
+  }
+  const __nv_bfloat16* old = reinterpret_cast<const __nv_bfloat16*>(ov);  // [8 channels][W-1 entries]
+  uint2 rows[kW - 1][2];  // input rows (W-1-j) steps before the end, 8 channels each (two 8-byte loads)
 #pragma unroll
-    for (int j = 0; j < kW - 1; ++j) {
-      // new history entry j = input (W-1-j) steps before the end of the sequence
-      const int64_t back = kW - 1 - j;  // 1 .. W-1
-      float x;
-      if (back <= len) x = __bfloat162float(p.mixed[(start + len - back) * p.mixed_stride + ch]);
-      else x = old[j + len];
-      hist[j] = __float2bfloat16_rn(x);
+  for (int j = 0; j < kW - 1; ++j) {
+    const int64_t back = kW - 1 - j;  // 1 .. W-1
+    if (back <= len) {
+      const uint2* src = reinterpret_cast<const uint2*>(p.mixed + (start + len - back) * p.mixed_stride + ch);
+      rows[j][0] = src[0];
+      rows[j][1] = src[1];
     }
   }
+  uint4 nv[3];
+  __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(nv);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+#pragma unroll
+    for (int j = 0; j < kW - 1; ++j) {
+      const int64_t back = kW - 1 - j;
+      __nv_bfloat16 x;
+      if (back <= len) {
+        const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(rows[j]);
+        x = r[c];
+      } else {
+        x = old[c * (kW - 1) + j + len];
+      }
+      nb[c * (kW - 1) + j] = x;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 3; ++i) hist[i] = nv[i];
 }
 
 struct EpilogueParams {
@@ -166,14 +233,29 @@ ZB_API int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const ui
              "gdn_prologue: null pointer");
   ZB_REQUIRE(mixed_stride >= 4LL * H * D + 2 * H, "gdn_prologue: mixed row stride %lld too small",
              (long long)mixed_stride);
+  ZB_REQUIRE(H <= 32, "gdn_prologue: H=%d (at most 32)", H);
+  ZB_REQUIRE(mixed_stride % 4 == 0, "gdn_prologue: mixed row stride %lld must be a multiple of 4",
+             (long long)mixed_stride);
+  ZB_REQUIRE_ALIGNED(mixed, 16, "gdn_prologue mixed");
+  ZB_REQUIRE_ALIGNED(conv_weight, 16, "gdn_prologue conv_weight");
+  ZB_REQUIRE_ALIGNED(conv_state, 16, "gdn_prologue conv_state");
   PrologueParams p{reinterpret_cast<const __nv_bfloat16*>(mixed), mixed_stride,
                    reinterpret_cast<const __nv_bfloat16*>(conv_weight), A_log, dt_bias, cu_seqlens, seq_of_token,
                    slots, reinterpret_cast<__nv_bfloat16*>(conv_state), conv_rows, fresh,
                    reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k),
                    reinterpret_cast<__nv_bfloat16*>(v), g, beta, N, H, D};
-  gdn_prologue_kernel<<<(unsigned)N, 256, 0, stream>>>(p);
+  const dim3 grid((unsigned)N, 3);
+  const unsigned threads = 32u * (unsigned)H;
+  switch (D / 32) {
+    case 1: gdn_prologue_kernel<1><<<grid, threads, 0, stream>>>(p); break;
+    case 2: gdn_prologue_kernel<2><<<grid, threads, 0, stream>>>(p); break;
+    case 4: gdn_prologue_kernel<4><<<grid, threads, 0, stream>>>(p); break;
+    default: return zb::fail(zb::kUnsupported, "gdn_prologue: head dim %d (32, 64 or 128)", D);
+  }
   if (int rc = zb::check_launch("gdn_prologue")) return rc;
-  if (num_seqs > 0) gdn_conv_history_kernel<<<(unsigned)num_seqs, 256, 0, stream>>>(p);
+  const int channels = 3 * H * D;
+  if (num_seqs > 0)
+    gdn_conv_history_kernel<<<dim3((unsigned)num_seqs, (unsigned)((channels / 8 + 255) / 256)), 256, 0, stream>>>(p);
   return zb::check_launch("gdn_prologue(history)");
 }
 

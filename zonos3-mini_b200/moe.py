@@ -38,11 +38,13 @@ class Router(BaseOP):
         self.balancing_biases = torch.zeros(self.num_experts, dtype=torch.float32)
 
     def forward(self, hidden_states: torch.Tensor, router_states: torch.Tensor | None = None, *, ids=None,
-                weights=None, logits=None):
+                weights=None, logits=None, renormalize: bool = False):
+        """``renormalize``: divide the k weights by their sum + 1e-8 in the router kernel (the experts' own
+        renormalisation, fused by MoEFeedForward); the reference's Router returns them unnormalised."""
         ids, w = ops.moe_router(
             hidden_states, self.rmsnorm_eda.weight, self._eps, self.router_linear.weight, self.balancing_biases,
             self.top_k, weights="selected_softmax" if self._training_weights else "full_softmax",
-            renormalize=False, ids=ids, topk_weights=weights, logits=logits)
+            renormalize=renormalize, ids=ids, topk_weights=weights, logits=logits)
         # the states the next layer's EDA would blend in; the release routes without EDA, so no copy is made
         return w, ids, hidden_states
 
@@ -76,7 +78,7 @@ class FusedGroupedExperts(BaseOP):
         super().load_state_dict(state_dict, prefix=prefix, _internal=_internal)
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor | None = None, *, topk_weights=None,
-                topk_ids=None, out=None) -> torch.Tensor:
+                topk_ids=None, out=None, weights_normalized: bool = False) -> torch.Tensor:
         if topk_weights is None or topk_ids is None:
             if router_logits is None:
                 raise ValueError("router_logits must be provided when top-k routing is not precomputed.")
@@ -84,7 +86,7 @@ class FusedGroupedExperts(BaseOP):
                                                     weights="full_softmax", renormalize=self._renormalize)
         else:
             topk_weights = topk_weights.to(torch.float32)
-            if self._renormalize:
+            if self._renormalize and not weights_normalized:
                 topk_weights = topk_weights / (topk_weights.sum(dim=-1, keepdim=True) + 1e-8)
         topk_ids = topk_ids.to(torch.int32).contiguous()
         ws = ops.MoEWorkspace.for_shape(self._workspaces, x.shape[0], topk_ids.shape[1], self.num_experts,
@@ -106,9 +108,10 @@ class MoEFeedForward(BaseOP):
 
     def forward(self, x: torch.Tensor, router_states: torch.Tensor | None = None):
         num_tokens, hidden = x.shape
-        weights, ids, states_next = self.router.forward(x, router_states)
+        # the experts' renormalisation of the top-k weights runs inside the router kernel
+        weights, ids, states_next = self.router.forward(x, router_states, renormalize=self.experts._renormalize)
         routed = F.linear(x, self.latent_down.weight) if self.use_latent_moe else x
-        out = self.experts.forward(routed, topk_weights=weights, topk_ids=ids)
+        out = self.experts.forward(routed, topk_weights=weights, topk_ids=ids, weights_normalized=True)
         if self.use_latent_moe:
             out = F.linear(out, self.latent_up.weight)
         return out.view(num_tokens, hidden), states_next
