@@ -10,9 +10,13 @@
 // torch.topk leaves the order of equal scores unspecified; this total order is the documented contract.
 // Permutation: the flattened (token, slot) pairs p = token * k + slot, stably sorted by expert (ascending p within
 // an expert); each expert's segment is padded to a multiple of `block` rows (padding rows hold -1).
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -473,6 +477,166 @@ int launch_router_nh(const RouterParams& p, cudaStream_t stream) {
   return zb::fail(zb::kUnsupported, "moe_router: D=%d with %d experts exceeds shared memory", p.D, 32 * NH);
 }
 
+// Router for few tokens: the D columns split across a cluster of kSplit CTAs, so the router weight (E x D) is read
+// by kSplit CTAs in slices instead of whole by every CTA. CTA r of a cluster takes TOK = 32 tokens and columns
+// [r*D/kSplit, (r+1)*D/kSplit): it stages its x and router-weight slices, forms the partial sums of squares of its
+// rows, exchanges them through distributed shared memory (every CTA sums the ranks in order, so all agree on the
+// inverse RMS), builds the router input bf16(x * inv_rms * rmsnorm_eda.weight) of its slice and the partial logits
+// (mma.sync m16n8k16, fp32); after a cluster barrier CTA r sums the partial logits of tokens [4r, 4r + 4) over the
+// ranks in order, rounds them to bf16 and selects their top-k exactly as the one-CTA router does.
+constexpr int kSplit = 8;
+constexpr int kSplitTok = 32;
+
+size_t router_split_smem(int NE, int DS) {
+  const int LXS = DS + kPad;
+  return (size_t)kSplitTok * LXS * 2 + (size_t)NE * LXS * 2 + (size_t)DS * 2 + (size_t)kSplit * kSplitTok * 4 +
+         (size_t)kSplitTok * 4 + (size_t)kSplitTok * (NE + 1) * 4 + (size_t)(kSplitTok / kSplit) * (NE + 1) * 4;
+}
+
+template <int NH>
+__global__ void __launch_bounds__(kRouterThreads) moe_router_split_kernel(RouterParams p) {
+  constexpr int NE = 32 * NH;
+  constexpr int TOK = kSplitTok;
+  constexpr int MT = TOK / 16, NG = 8 / MT, NPW = NE / 8 / NG > 0 ? NE / 8 / NG : 1;
+  constexpr int TPC = TOK / kSplit;  // tokens a CTA selects
+  cg::cluster_group cluster = cg::this_cluster();
+  const int r = (int)cluster.block_rank();
+  const int tok0 = (int)(blockIdx.x / kSplit) * TOK;
+  const int D = p.D, DS = D / kSplit, LXS = DS + kPad, c0 = r * DS;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* x_s = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [TOK][LXS]
+  __nv_bfloat16* w_s = x_s + (size_t)TOK * LXS;                       // [NE][LXS]
+  __nv_bfloat16* nw_s = w_s + (size_t)NE * LXS;                       // [DS]
+  float* ssq = reinterpret_cast<float*>(nw_s + DS);                   // [kSplit][TOK] partial sums of squares
+  float* rms_s = ssq + kSplit * TOK;                                  // [TOK]
+  float* part = rms_s + TOK;                                          // [TOK][NE + 1] partial logits
+  float* lg = part + TOK * (NE + 1);                                  // [TPC][NE + 1] logits of the selected tokens
+
+  const int vs = DS / 8;
+  for (int idx = tid; idx < TOK * vs; idx += kRouterThreads) {
+    const int row = idx / vs, c = (idx % vs) * 8;
+    const int t = tok0 + row;
+    cp_async16(x_s + (size_t)row * LXS + c, p.x + (int64_t)(t < p.T ? t : 0) * p.x_stride + c0 + c, t < p.T);
+  }
+  for (int idx = tid; idx < NE * vs; idx += kRouterThreads) {
+    const int e = idx / vs, c = (idx % vs) * 8;
+    cp_async16(w_s + (size_t)e * LXS + c, p.w_router + (int64_t)(e < p.E ? e : 0) * D + c0 + c, e < p.E);
+  }
+  for (int idx = tid; idx < vs; idx += kRouterThreads) cp_async16(nw_s + idx * 8, p.norm_w + c0 + idx * 8, true);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  {  // partial sums of squares of this slice, 8 threads per row, pushed into every CTA's row r
+    constexpr int TPR = kRouterThreads / TOK;
+    const int row = tid / TPR, pt = tid % TPR;
+    const uint4* xr = reinterpret_cast<const uint4*>(x_s + (size_t)row * LXS);
+    float ss = 0.f;
+    for (int j = pt; j < vs; j += TPR) {
+      float f[8];
+      const uint4 v = xr[j];
+      zb::ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(&v), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+#pragma unroll
+    for (int off = 1; off < TPR; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (pt == 0)
+      for (int q = 0; q < kSplit; ++q) *cluster.map_shared_rank(ssq + r * TOK + row, q) = ss;
+  }
+  cluster.sync();
+  if (tid < TOK) {
+    float total = 0.f;
+    for (int q = 0; q < kSplit; ++q) total += ssq[q * TOK + tid];
+    rms_s[tid] = rsqrtf(total / (float)D + p.eps);
+  }
+  __syncthreads();
+  for (int idx = tid; idx < TOK * vs; idx += kRouterThreads) {  // the router input of this slice, in place
+    const int row = idx / vs, c = (idx % vs) * 8;
+    uint4* cell = reinterpret_cast<uint4*>(x_s + (size_t)row * LXS + c);
+    const uint4 raw = *cell, wr = *reinterpret_cast<const uint4*>(nw_s + c);
+    const float sc = rms_s[row];
+    *cell = make_uint4(scale_bf16x2(raw.x, sc, wr.x), scale_bf16x2(raw.y, sc, wr.y), scale_bf16x2(raw.z, sc, wr.z),
+                       scale_bf16x2(raw.w, sc, wr.w));
+  }
+  __syncthreads();
+  {  // partial logits of the slice
+    const int mt = warp % MT, nbase = (warp / MT) * NPW;
+    const int g = lane >> 2, tq = lane & 3;
+    float acc[NPW][4];
+#pragma unroll
+    for (int n = 0; n < NPW; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    const __nv_bfloat16* a = x_s + (size_t)(mt * 16) * LXS;
+    if (nbase * 8 < p.E) {
+      for (int kk = 0; kk < DS; kk += 16) {
+        uint32_t af[4];
+        af[0] = *reinterpret_cast<const uint32_t*>(a + g * LXS + kk + 2 * tq);
+        af[1] = *reinterpret_cast<const uint32_t*>(a + (g + 8) * LXS + kk + 2 * tq);
+        af[2] = *reinterpret_cast<const uint32_t*>(a + g * LXS + kk + 2 * tq + 8);
+        af[3] = *reinterpret_cast<const uint32_t*>(a + (g + 8) * LXS + kk + 2 * tq + 8);
+#pragma unroll
+        for (int n = 0; n < NPW; ++n) {
+          const int e = (nbase + n) * 8 + g;
+          uint32_t bf[2];
+          bf[0] = *reinterpret_cast<const uint32_t*>(w_s + (size_t)e * LXS + kk + 2 * tq);
+          bf[1] = *reinterpret_cast<const uint32_t*>(w_s + (size_t)e * LXS + kk + 2 * tq + 8);
+          mma_bf16_16816(acc[n], af, bf);
+        }
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < NPW; ++n) {
+      const int cc = (nbase + n) * 8 + 2 * tq, r0 = mt * 16 + g;
+      if (cc < NE) {
+        part[r0 * (NE + 1) + cc] = acc[n][0];
+        part[r0 * (NE + 1) + cc + 1] = acc[n][1];
+        part[(r0 + 8) * (NE + 1) + cc] = acc[n][2];
+        part[(r0 + 8) * (NE + 1) + cc + 1] = acc[n][3];
+      }
+    }
+  }
+  cluster.sync();  // every CTA's partial logits are complete
+  if (warp < TPC) {
+    const int lt = r * TPC + warp;  // token of the block this warp selects
+    const int t = tok0 + lt;
+    float* row = lg + warp * (NE + 1);
+    for (int e = lane; e < p.E; e += 32) {
+      float total = 0.f;
+      for (int q = 0; q < kSplit; ++q) total += *cluster.map_shared_rank(part + lt * (NE + 1) + e, q);
+      row[e] = zb::bf16_round(total);
+    }
+    __syncwarp();
+    if (t < p.T) {
+      if (p.logits_out)
+        for (int e = lane; e < p.E; e += 32) p.logits_out[(int64_t)t * p.E + e] = __float2bfloat16_rn(row[e]);
+      select_token([&](int e) { return row[e]; }, p.bias, p.E, p.k, p.mode, p.renorm, p.ids + (int64_t)t * p.k,
+                   p.weights + (int64_t)t * p.k);
+    }
+  }
+  cluster.sync();  // no CTA leaves while its peers still read its partial logits
+}
+
+template <int NH>
+int launch_router_split(const RouterParams& p, cudaStream_t stream) {
+  const size_t smem = router_split_smem(32 * NH, p.D / kSplit);
+  auto kernel = moe_router_split_kernel<NH>;
+  ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(((p.T + kSplitTok - 1) / kSplitTok) * kSplit));
+  cfg.blockDim = dim3(kRouterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
+  return zb::check_launch("moe_router(split)");
+}
+
 struct SelectParams {
   const void* logits;
   int bf16;
@@ -743,6 +907,14 @@ ZB_API int zb_moe_router(const uint16_t* x, int64_t x_stride, const uint16_t* no
                  reinterpret_cast<const __nv_bfloat16*>(w_router), bias, T, D, E, k, weight_mode, renormalize,
                  reinterpret_cast<__nv_bfloat16*>(logits_out), ids, weights};
   const int nh = (E + 31) / 32;
+  // few tokens: the one-CTA-per-32-tokens router would run on a handful of SMs, each streaming the whole router
+  // weight; split the columns across clusters instead
+  if ((int64_t)(T + kSplitTok - 1) / kSplitTok * kSplit <= 2 * (int64_t)zb::sm_count() && D % (kSplit * 16) == 0 &&
+      router_split_smem(32 * (nh <= 1 ? 1 : nh <= 2 ? 2 : 4), D / kSplit) <= kRouterSmemBudget) {
+    if (nh <= 1) return launch_router_split<1>(p, stream);
+    if (nh <= 2) return launch_router_split<2>(p, stream);
+    return launch_router_split<4>(p, stream);
+  }
   if (nh <= 1) return launch_router_nh<1>(p, stream);
   if (nh <= 2) return launch_router_nh<2>(p, stream);
   return launch_router_nh<4>(p, stream);
