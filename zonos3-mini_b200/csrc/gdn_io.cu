@@ -92,8 +92,18 @@ __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
   float hist[PL * (kW - 1)];  // history [channel][entry], zero for a fresh sequence
   if (!fresh && pos < kW - 1) {
     const __nv_bfloat16* hp = p.conv_state + (slot * 3 * inner + ch0) * (kW - 1);
+    if constexpr (PL == 4) {  // 12 entries, 8-byte aligned: three 8-byte loads
+      float tmp[4];
 #pragma unroll
-    for (int j = 0; j < PL * (kW - 1); ++j) hist[j] = __bfloat162float(hp[j]);
+      for (int j = 0; j < 12; j += 4) {
+        load_bf<4>(hp + j, tmp);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) hist[j + u] = tmp[u];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < PL * (kW - 1); ++j) hist[j] = __bfloat162float(hp[j]);
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < PL * (kW - 1); ++j) hist[j] = 0.f;
@@ -126,8 +136,15 @@ __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
     scale = rsqrtf(zb::warp_sum(ss) + 1e-6f);
   }
   __nv_bfloat16* dst = (part == 0 ? p.q : part == 1 ? p.k : p.v) + (tok * p.H + h) * p.D + lane * PL;
+  if constexpr (PL == 4) {
+    const __nv_bfloat162 o0 = __floats2bfloat162_rn(acc[0] * scale, acc[1] * scale);
+    const __nv_bfloat162 o1 = __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
+    *reinterpret_cast<uint2*>(dst) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&o0), *reinterpret_cast<const uint32_t*>(&o1));
+  } else {
 #pragma unroll
-  for (int j = 0; j < PL; ++j) dst[j] = __float2bfloat16_rn(acc[j] * scale);
+    for (int j = 0; j < PL; ++j) dst[j] = __float2bfloat16_rn(acc[j] * scale);
+  }
   if (part == 0 && threadIdx.x < p.H) {
     const int hh = threadIdx.x;
     const float a = __bfloat162float(row[4 * inner + hh]);
