@@ -395,55 +395,59 @@ def bench_moe_cfg4(ops, dev, stream, steps=10, warmup=3):
 
 def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps=3):
     """cfg5's AttnRes schedule for one decode step: 2L+1 routes over a growing bank (S = 1 .. 2L+1 sources) of
-    `tokens` rows, each with the following RMSNorm fused and the bank rows' inverse RMS cached as
-    FusedBlockAttnResContext caches them (route r computes row r's and reads rows < r from the cache). The L2 is
-    flushed before every route (as the layers between routes would); route time = graph[flush, route] x (2L+1)
-    minus graph[flush] x (2L+1)."""
+    `tokens` rows, each with the following RMSNorm fused, as FusedBlockAttnResContext runs them with the forward's
+    queries registered: route r reads the logits of rows < r from the table, computes its current source's (bank
+    row r) and, while it mixes, route r+1's logits of rows <= r. The L2 is flushed before every route (as the
+    layers between routes would); route time = graph[flush, route] x (2L+1) minus graph[flush] x (2L+1)."""
     gen = torch.Generator().manual_seed(7)
     n_src = 2 * layers + 1
     bank = torch.randn(n_src, tokens, dim, generator=gen).bfloat16().to(dev)
     queries = (0.02 * torch.randn(n_src, dim, generator=gen)).bfloat16().to(dev)
     norm_w = torch.ones(dim, dtype=torch.bfloat16, device=dev)
     out = torch.empty(tokens, dim, device=dev, dtype=torch.bfloat16)
-    rms_cache = torch.zeros(tokens, (n_src + 3) // 4 * 4, device=dev, dtype=torch.float32)
+    table = torch.zeros(n_src, tokens, (n_src + 3) // 4 * 4, device=dev, dtype=torch.float32)
+    inv_rms = torch.zeros(tokens, (n_src + 3) // 4 * 4, device=dev, dtype=torch.float32)
     flush = L2Flush(dev)
+
+    def route(r):
+        ops.attnres_route_tabled(bank, r, bank[r], queries, r, table, inv_rms, 1e-5, source_in_bank=r < n_src - 1,
+                                 norm_weight=norm_w, out=out)
 
     def schedule(with_routes):
         for r in range(n_src):
             flush_l2(flush)
             if with_routes:
-                ops.attnres_route(bank, r + 1, queries[r], 1e-5, norm_weight=norm_w, out=out, rms_cache=rms_cache,
-                                  cached=r)
+                route(r)
 
+    schedule(True)  # fills the table as a forward does
     total_ms = graph_ms(lambda: schedule(True), stream, reps) - graph_ms(lambda: schedule(False), stream, reps)
-    big_ms = flushed_ms(lambda: ops.attnres_route(bank, n_src, queries[-1], 1e-5, norm_weight=norm_w, out=out,
-                                                  rms_cache=rms_cache, cached=n_src - 1), flush, stream, reps=10)
-    # algorithmic bytes of route r: r + 1 bank rows read, the output row written, query + norm weight, and the
-    # cache (r rows read, one written)
-    total_bytes = sum(((r + 1) * tokens * dim + tokens * dim + 2 * dim) * 2 + (r + 1) * tokens * 4
-                      for r in range(n_src))
+    big_ms = flushed_ms(lambda: route(n_src - 1), flush, stream, reps=10)
+
+    # algorithmic bytes of route r: r + 1 bank rows read, the output row written, this and the next route's query
+    # and the norm weight, per token the r table logits and r inverse RMS read, the next route's r + 1 logits and
+    # the source's inverse RMS written
+    def route_bytes(r):
+        nxt = r + 1 if r + 1 < n_src else 0
+        return ((r + 1) * tokens * dim + tokens * dim + 3 * dim) * 2 + (2 * r + nxt + 1) * tokens * 4
+
+    total_bytes = sum(route_bytes(r) for r in range(n_src))
     pk = peaks()
     gbs = total_bytes / (total_ms / 1e3) / 1e9
-    big_bytes = (n_src * tokens * dim + tokens * dim + 2 * dim) * 2 + n_src * tokens * 4
+    big_bytes = route_bytes(n_src - 1)
     return {
         "workload": f"cfg5 AttnRes decode schedule: {n_src} routes over a growing bank, {tokens} tokens x {dim}, "
                     "fused RMSNorm, L2 flushed before each route",
         "ms_per_step": total_ms, "bytes_per_step": total_bytes,
-        "roofline": {"kernel": "attnres_route_kernel", "bound": "hbm", "achieved": gbs,
+        "roofline": {"kernel": "attnres_tabled_kernel", "bound": "hbm", "achieved": gbs,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"]},
         "largest_route": {"sources": n_src, "us": big_ms * 1e3, "gbs": big_bytes / (big_ms / 1e3) / 1e9,
                           "frac": big_bytes / (big_ms / 1e3) / 1e9 / pk["hbm_gbs"]},
     }
 
 
-def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5):
-    """cfg5 decode step of one DeltaNet + MoE layer through the drop-in modules, for `streams` concurrent streams
-    (one new row each): AttnRes route (bank of `bank_rows` sources + the layer input, attention_norm fused) ->
-    OriginalGDN.forward in its static decode mode (in_proj GEMM, prologue, recurrent update of 256 slot states,
-    gated norm, wo GEMM) -> AttnRes route (ffn_norm fused) -> MoEFeedForward.forward (router, permutation,
-    grouped GEMMs over 604 MB of expert weights, combine). Hidden 2048, GDN 16 x 128/128, 64 experts top-8, I=768;
-    bf16 random-init weights (N(0, 0.02)); captured in one CUDA graph. The L2 is not flushed: the expert weights
-    alone exceed it."""
+def decode_layer_cfg5(pkg, dev, streams=256, bank_rows=24):
+    """Builds the cfg5 DeltaNet + MoE decode layer of bench_decode_layer_cfg5; returns (layer, core, batch): call
+    layer() inside core.forward_batch(batch)."""
     ops, core = pkg.ops, pkg.core
     D, H, d, E, k, I = 2048, 16, 128, 64, 8, 768
     cfg = pkg.config.ModelConfig(hidden_size=D, gdn_num_heads=H, gdn_head_dim=d, moe_n_experts=E, moe_topk=k,
@@ -466,22 +470,39 @@ def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5)
                          "experts.down_proj": rnd(E, D, I)})
     moe.to(dev, torch.bfloat16)
     bank = torch.randn(bank_rows + 2, streams, D, generator=gen).bfloat16().to(dev)
-    queries = (0.02 * torch.randn(2, D, generator=gen)).bfloat16().to(dev)
+    # the layer's two routes are routes bank_rows and bank_rows + 1 of a forward of 2 * bank_rows + 1 routes (the
+    # middle layer of a 2 x bank_rows-sublayer stack), the route queries registered up front
+    n_routes = 2 * bank_rows + 1
+    queries = (0.02 * torch.randn(n_routes, D, generator=gen)).bfloat16().to(dev)
     norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
-    rms_cache = torch.zeros(streams, (bank_rows + 5) // 4 * 4, device=dev, dtype=torch.float32)
+    table = torch.zeros(n_routes, streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
+    inv_rms = torch.ones(streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
     h = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
     batch = core.Batch(reqs=[core.Req(i, 1, cached_len=100) for i in range(streams)], is_decode=True,
                        padded_size=streams)
 
     def layer():
-        ops.attnres_route(bank, bank_rows + 1, queries[0], 1e-5, norm_weight=norm_w, out=h, rms_cache=rms_cache,
-                          cached=bank_rows)
+        ops.attnres_route_tabled(bank, bank_rows, bank[bank_rows], queries, bank_rows, table, inv_rms, 1e-5,
+                                 source_in_bank=True, norm_weight=norm_w, out=h)
         a = gdn.forward(h)
-        ops.attnres_route(bank, bank_rows + 1, queries[1], 1e-5, source=a, append_to=bank[bank_rows + 1],
-                          norm_weight=norm_w, out=h, rms_cache=rms_cache, cached=bank_rows)
+        ops.attnres_route_tabled(bank, bank_rows + 1, a, queries, bank_rows + 1, table, inv_rms, 1e-5,
+                                 append_to=bank[bank_rows + 1], norm_weight=norm_w, out=h)
         out, _ = moe.forward(h)
         return out
 
+    return layer, core, batch
+
+
+def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5):
+    """cfg5 decode step of one DeltaNet + MoE layer through the drop-in modules, for `streams` concurrent streams
+    (one new row each): AttnRes route (bank of `bank_rows` sources + the layer input, attention_norm fused) ->
+    OriginalGDN.forward in its static decode mode (in_proj GEMM, prologue, recurrent update of 256 slot states,
+    gated norm, wo GEMM) -> AttnRes route (ffn_norm fused) -> MoEFeedForward.forward (router, permutation,
+    grouped GEMMs over 604 MB of expert weights, combine). Hidden 2048, GDN 16 x 128/128, 64 experts top-8, I=768;
+    bf16 random-init weights (N(0, 0.02)); captured in one CUDA graph. The L2 is not flushed: the expert weights
+    alone exceed it."""
+    D, E, I = 2048, 64, 768
+    layer, core, batch = decode_layer_cfg5(pkg, dev, streams, bank_rows)
     with core.forward_batch(batch):
         ms = graph_ms(layer, stream, reps)
     return {
@@ -557,7 +578,8 @@ def cpu_reference(updates: int, streams=STREAMS):
 
 def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
-    updates cycling the layer states, cfg4 MoE layers, or the largest cfg5 AttnRes route."""
+    updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, or cfg5
+    DeltaNet + MoE decode layers."""
     ops = __import__("__graft_entry__").load_package().ops
     dev = torch.device("cuda", 0)
     if workload == "moe":
@@ -572,6 +594,14 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
             ops.moe_experts(x, gate_up, down, ids, w, ws, out=out)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg4 MoE layers done, status {ops.device_status()}")
+        return
+    if workload == "decode_layer":
+        layer, core, batch = decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev)
+        with core.forward_batch(batch):
+            for _ in range(n):
+                layer()
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg5 DeltaNet + MoE decode layers done")
         return
     if workload == "prefill":
         B, T, H, d = 8, 2048, 16, 128
@@ -591,14 +621,19 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     if workload == "attnres":
         gen = torch.Generator().manual_seed(7)
         bank = torch.randn(49, 256, 2048, generator=gen).bfloat16().to(dev)
-        query = (0.02 * torch.randn(2048, generator=gen)).bfloat16().to(dev)
+        queries = (0.02 * torch.randn(49, 2048, generator=gen)).bfloat16().to(dev)
         norm_w = torch.ones(2048, dtype=torch.bfloat16, device=dev)
-        rms_cache = torch.zeros(256, 52, device=dev, dtype=torch.float32)
-        ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w, rms_cache=rms_cache, cached=0)
+        table = torch.zeros(49, 256, 52, device=dev, dtype=torch.float32)
+        inv_rms = torch.zeros(256, 52, device=dev, dtype=torch.float32)
+        for r in range(48):  # the earlier routes of the forward fill the logit table
+            ops.attnres_route_tabled(bank, r, bank[r], queries, r, table, inv_rms, 1e-5, source_in_bank=True,
+                                     norm_weight=norm_w)
         flush = L2Flush(dev)
-        for _ in range(n):
+        for i in range(n):  # alternately the last route with a look-ahead (47) and the largest route (48)
+            r = 47 + i % 2
             flush_l2(flush)
-            ops.attnres_route(bank, 49, query, 1e-5, norm_weight=norm_w, rms_cache=rms_cache, cached=48)
+            ops.attnres_route_tabled(bank, r, bank[r], queries, r, table, inv_rms, 1e-5, source_in_bank=r < 48,
+                                     norm_weight=norm_w)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} AttnRes routes (49 sources x 256 tokens x 2048) done")
         return
@@ -621,7 +656,8 @@ def main():
     ap.add_argument("--cpu-updates", type=int, default=256, help="updates in the CPU-baseline sample")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
-    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill"),
+    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill",
+                                                                         "decode_layer"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")

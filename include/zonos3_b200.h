@@ -116,6 +116,24 @@ int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, const uin
                      uint16_t* mix_out, float* rms_cache, int64_t rms_stride, int cached, int T, int D,
                      cudaStream_t stream);
 
+/* The same route for a forward whose route queries are registered up front (queries [num_routes, D]), with the
+ * logits carried from each route to the next in a table (fp32 [num_routes][T][table_stride]): route `route` takes
+ * the logits of bank rows [0, S) from table[route][t][s] and computes only its current source's (`source`); while
+ * its mix streams the bank rows it computes the next route's logits of those rows (keys from their inverse RMS in
+ * inv_rms [T][inv_stride]) and, when the current source becomes bank row S (append != NULL, or source_in_bank != 0
+ * for a source that already is bank row S), of the current source, storing them in table[route + 1]; that source's
+ * inverse RMS goes to inv_rms[t][S]. A (source, route) logit depends on nothing else, so the table holds what the
+ * reference's route recomputes (same rounding points as zb_attnres_route; the mix sums the terms in source order).
+ * Same reference interface as zb_attnres_route (FusedBlockAttnResContext.route over a forward's fixed route order,
+ * servers/sgl/src/zonos3_sgl/models/training_attnres.py:59-78).
+ *   D a multiple of 256 (at most 4096), S + 1 <= 256, table_stride and inv_stride >= S + (source becomes row S);
+ *   bank, source, append, queries, norm_weight, out, mix_out 16-byte aligned. */
+int zb_attnres_route_tabled(const uint16_t* bank, int64_t bank_stride, int S, const uint16_t* source,
+                            uint16_t* append, int source_in_bank, const uint16_t* queries, int num_routes, int route,
+                            float eps, const uint16_t* norm_weight, float norm_eps, uint16_t* out, uint16_t* mix_out,
+                            float* table, int64_t table_stride, float* inv_rms, int64_t inv_stride, int T, int D,
+                            cudaStream_t stream);
+
 /* ----------------------------------------------------------------------------------------------------- MoE */
 
 /* Fused router: logits = bf16(rmsnorm_eda(x) @ w_router^T), the top-k experts by (float(logit) - bias descending,

@@ -42,6 +42,10 @@ SIGNATURES: dict[str, list] = {
     "zb_gdn_gated_norm": [_p, _p, _i64, _p, _f32, _i32, _i32, _i32, _p, _p],
     # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream
     "zb_attnres_route": [_p, _i64, _i32, _p, _p, _p, _f32, _p, _f32, _p, _p, _p, _i64, _i32, _i32, _i32, _p],
+    # bank, bank_stride, S, source, append, source_in_bank, queries, num_routes, route, eps, norm_weight, norm_eps,
+    # out, mix_out, table, table_stride, inv_rms, inv_stride, T, D, stream
+    "zb_attnres_route_tabled": [_p, _i64, _i32, _p, _p, _i32, _p, _i32, _i32, _f32, _p, _f32, _p, _p, _p, _i64, _p,
+                                _i64, _i32, _i32, _p],
     # x, x_stride, norm_weight, eps, w_router, bias, T, D, E, k, weight_mode, renormalize, logits, ids, weights, stream
     "zb_moe_router": [_p, _i64, _p, _f32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p],
     # logits, logits_bf16, bias, T, E, k, weight_mode, renormalize, ids, weights, stream

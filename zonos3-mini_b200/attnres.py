@@ -9,6 +9,13 @@ Drop-in names and signatures:
   ``completed_count``, ``call_count``, ``validate_owner``, ``completed_view``);
 * ``fused_full_attnres(state, source, query, norm_eps, append_current)`` — training_attnres_kernels.py:2826-2840.
 
+A forward that knows its route queries up front (``forward_layers_full`` does) registers them with
+``FusedBlockAttnResContext.register_queries``: each route then computes the next route's logits of the rows it
+mixes, while they stream through registers, and leaves them in a [routes, T, rows] fp32 table, so that a route
+computes only its current source's logit before its softmax and reads the bank once (``zb_attnres_route_tabled``).
+A (source, route) logit depends on nothing but the source row, the route's query and the eps, so the table holds
+exactly what the reference's route recomputes.
+
 Inference only: the reference's autograd backward (used by its trainer) is not part of the serving hot path.
 The bank append happens inside the route kernel, and when the caller already wrote ``source`` into the next bank
 row (``state.next_row()``), the route reads it from there and nothing is copied.
@@ -33,6 +40,8 @@ def full_attnres_route(sources, query: torch.Tensor, norm_eps: float) -> torch.T
 class FusedBlockAttnResContext:
     """One forward's bank of completed sources, allocated once and reused (graph-safe)."""
 
+    TABLED_MAX_DIM = 4096  # hidden sizes the route over a logit table supports
+
     def __init__(self, max_completed_blocks: int, reference: torch.Tensor, gradient_dtype=torch.float32, **_):
         if not reference.is_cuda:
             raise RuntimeError("fused AttnRes requires CUDA")
@@ -52,13 +61,39 @@ class FusedBlockAttnResContext:
         self.rms_cache = torch.empty((self.bt, (self.max_completed_blocks + 4) // 4 * 4), device=reference.device,
                                      dtype=torch.float32)
         self._rms_eps = None
+        self._queries = None  # registered route queries [R, D] (call order) and their logit table
+        self._table = None
+        self._table_eps = None
         self.completed_count = 0
         self.call_count = 0
 
     def reset(self) -> None:
+        """Starts a new forward (the registered queries stay registered)."""
         self.completed_count = 0
         self.call_count = 0
         self._rms_eps = None
+
+    def register_queries(self, queries: torch.Tensor | None, norm_eps: float | None = None) -> None:
+        """Registers the queries of the forward's routes in call order (contiguous [R, D] bf16 on this device) and
+        the key RMSNorm eps they run with: route number ``call_count`` must then pass ``queries[call_count]`` (this
+        storage) and that eps. ``None`` unregisters."""
+        if queries is None:
+            self._queries = self._table = self._table_eps = None
+            return
+        if self.dim > self.TABLED_MAX_DIM:
+            raise RuntimeError(f"registered route queries need a hidden size <= {self.TABLED_MAX_DIM}")
+        if queries.dtype != torch.bfloat16 or queries.device != self.blocks.device or queries.dim() != 2 \
+                or queries.shape[1] != self.dim or not queries.is_contiguous():
+            raise RuntimeError(f"route queries must be a contiguous [R, {self.dim}] bf16 tensor on "
+                               f"{self.blocks.device}, got {tuple(queries.shape)} {queries.dtype} {queries.device}")
+        if norm_eps is None:
+            raise RuntimeError("register_queries needs the eps the routes run with")
+        rows = (self.max_completed_blocks + 3) // 4 * 4
+        shape = (queries.shape[0], self.bt, rows)
+        if self._table is None or tuple(self._table.shape) != shape:
+            self._table = torch.zeros(shape, device=self.blocks.device, dtype=torch.float32)
+        self._queries = queries
+        self._table_eps = float(norm_eps)
 
     def validate_owner(self, partial: torch.Tensor) -> None:
         if tuple(partial.shape[:-1]) != self.token_shape or partial.shape[-1] != self.dim:
@@ -93,6 +128,20 @@ class FusedBlockAttnResContext:
         in_place = completed < self.max_completed_blocks and src.data_ptr() == self.blocks[completed].data_ptr()
         if out is not None:
             out = out.reshape(self.bt, self.dim)
+        if self._queries is not None:
+            c = self.call_count
+            if c >= self._queries.shape[0] or query.data_ptr() != self._queries[c].data_ptr() \
+                    or float(norm_eps) != self._table_eps:
+                raise RuntimeError(f"route {c} does not match the registered route queries / eps")
+            result = ops.attnres_route_tabled(
+                self.blocks if completed else None, completed, src if in_place else src.contiguous(),
+                self._queries, c, self._table, self.rms_cache, norm_eps, source_in_bank=in_place and append_current,
+                append_to=self.blocks[completed] if append_current and not in_place else None,
+                norm_weight=norm_weight, norm_eps=norm_eps, out=out, mix_out=mix_out)
+            if append_current:
+                self.completed_count += 1
+            self.call_count += 1
+            return result.view(*self.token_shape, self.dim)
         cached = completed if self._rms_eps == norm_eps else 0  # cached rows hold 1 / rms at this eps
         self._rms_eps = norm_eps
         if in_place:
@@ -123,8 +172,14 @@ def forward_layers_full(layers, x: torch.Tensor, queries: torch.Tensor, eps: flo
     sublayer's input appended to the bank by the same kernel; a final route with out_norm. ``layers`` expose
     ``attention_norm.weight``, ``ffn_norm.weight``, ``attention.forward(x)`` and ``feed_forward.forward(x,
     router_states) -> (out, router_states)`` (MoE) or ``feed_forward.forward(x)`` (dense, ``is_moe`` False).
-    Returns the normalised final mix [T, D]."""
+    Returns the normalised final mix [T, D]. The 2L+1 route queries are registered with the context, so each route
+    leaves the next route's logits in the context's table."""
     state.reset()
+    if queries.dtype == torch.bfloat16 and queries.is_contiguous() and queries.device == state.blocks.device \
+            and state.dim <= state.TABLED_MAX_DIM:
+        state.register_queries(queries, eps)
+    else:
+        state.register_queries(None)
     source = x
     for i, layer in enumerate(layers):
         h = state.route(source, queries[2 * i], eps, True, norm_weight=layer.attention_norm.weight)

@@ -386,6 +386,319 @@ int launch(const RouteParams& p, cudaStream_t stream) {
   return zb::check_launch("attnres_route");
 }
 
+// ------------------------------------------------------------------------------ route over a logit table
+// A source's logit for a route depends only on the source row and the route's query: sum_d bf16(key_d * q_d) with
+// key = bf16(v * inv_rms(v)). When a forward registers the queries of its routes up front, route r computes route
+// r+1's logits of every bank row while its own mix streams those rows through registers (the key from the row's
+// cached inverse RMS, one bf16x2 multiply per two products with the next query), and of its current source, and
+// stores them in a table table[r+1][t][s] (fp32, `table_stride` floats per token, T * table_stride per route). Route
+// r+1 then needs only its own current source's logit before the softmax: no source is staged on chip, nothing is
+// read twice. One CTA per token, D / 8 threads, 8 columns of every source per thread, U loads of 16 bytes in flight
+// per thread (the first U issued before the logit work). Rounding points as in attnres_route_kernel; the mix sums
+// the terms in source order.
+struct TabledParams {
+  const __nv_bfloat16* bank;  // [>= S, T, D]: rows whose logits for this route are in the table
+  int64_t bank_stride;
+  int S;
+  const __nv_bfloat16* source;  // [T, D] current source (routed as source S)
+  __nv_bfloat16* append;        // optional: where to copy `source` (the next bank row)
+  int appended;                 // the current source is bank row S after this route (appended or in place)
+  const __nv_bfloat16* queries;  // [num_routes, D]
+  int num_routes, route;
+  float eps;
+  const __nv_bfloat16* norm_weight;
+  float norm_eps;
+  __nv_bfloat16* out;
+  __nv_bfloat16* mix_out;
+  float* table;  // [num_routes][T][table_stride]
+  int64_t table_stride;
+  float* inv_rms;  // [T][inv_stride]: key inverse RMS of bank row s at column s
+  int64_t inv_stride;
+  int T, D;
+};
+
+__device__ __forceinline__ uint4 ld_nc_u4(const __nv_bfloat16* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Shared memory of one tabled-route CTA: per-warp partial sums, the bank rows' inverse RMS, softmax weight rows.
+struct TabledLayout {
+  size_t stash, red_ss, red_lg, red_nrm, inv, red_next, wp, total;
+  __host__ __device__ TabledLayout(int nwarps, int ns) {
+    stash = 0;                                     // [2][nwarps * 32] uint4: current source, norm weight slices
+    red_ss = stash + (size_t)nwarps * 32 * 32;     // [nwarps] sums of squares of the current source
+    red_lg = red_ss + (size_t)nwarps * 4;          // [nwarps] partial logits of the current source for this route
+    red_nrm = red_lg + (size_t)nwarps * 4;         // [nwarps] sums of squares of the mix
+    inv = red_nrm + (size_t)nwarps * 4;            // [ns] inverse RMS of the bank rows
+    red_next = inv + (size_t)ns * 4;               // [nwarps][ns] partial logits for the next route
+    wp = (red_next + (size_t)nwarps * ns * 4 + 7) / 8 * 8;  // [nwarps][ns] (bf16x2 weight, inverse RMS) per source
+    total = wp + (size_t)nwarps * ns * 8;
+  }
+};
+
+// Warp sums of 16 values at once: lanes l and l + 16 end with the sum over the warp of v[l % 16] (31 shuffles
+// instead of 16 x 5).
+__device__ __forceinline__ float warp_transpose_sum16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16);
+#pragma unroll
+  for (int half = 8; half >= 1; half >>= 1) {
+    const bool upper = lane & half;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = upper ? v[i] : v[i + half];
+      const float keep = upper ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+    }
+  }
+  return v[0];
+}
+
+// lo += float(low bf16 of w), hi += float(high bf16 of w): sm_100's mixed-precision add takes the bf16 halves as
+// they are (the conversion is exact), so no unpacking precedes the fp32 adds.
+__device__ __forceinline__ void add_bf2(uint32_t w, float& lo, float& hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n add.rn.f32.bf16 %0, l, %0;\n add.rn.f32.bf16 %1, h, %1;\n}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(w));
+}
+
+// Sum over 8 columns of bf16(key * q) (two fp32 add chains: the low and the high halves).
+__device__ __forceinline__ float dot8(const uint32_t (&key)[4], const uint4& q) {
+  float lo = 0.f, hi = 0.f;
+  add_bf2(hmul2_bits(key[0], q.x), lo, hi);
+  add_bf2(hmul2_bits(key[1], q.y), lo, hi);
+  add_bf2(hmul2_bits(key[2], q.z), lo, hi);
+  add_bf2(hmul2_bits(key[3], q.w), lo, hi);
+  return lo + hi;
+}
+
+// The 8 keys bf16(v * inv_rms) of a 16-byte source vector.
+__device__ __forceinline__ void keys8(const uint4& x, uint64_t inv2, uint32_t (&key)[4]) {
+  key[0] = x2_to_bf2(mul_x2(bf2_to_x2(x.x), inv2));
+  key[1] = x2_to_bf2(mul_x2(bf2_to_x2(x.y), inv2));
+  key[2] = x2_to_bf2(mul_x2(bf2_to_x2(x.z), inv2));
+  key[3] = x2_to_bf2(mul_x2(bf2_to_x2(x.w), inv2));
+}
+
+template <int U, int kMaxThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel(TabledParams p) {
+  static_assert(U == 16, "a round of U sources is one 16-wide transposed warp sum");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  static_assert(kMaxThreads >= 128, "the inverse-RMS registers cover 256 sources with >= 128 threads");
+  const int nwarps = blockDim.x / 32;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int64_t t = blockIdx.x;
+  const int D = p.D, S = p.S, ns = S + 1;
+  const int c = tid * 8;
+  const bool ahead = p.route + 1 < p.num_routes;  // this route computes the next route's logits
+  const TabledLayout lay(nwarps, ns);
+  float* red_ss = reinterpret_cast<float*>(smem_raw + lay.red_ss);
+  float* red_lg = reinterpret_cast<float*>(smem_raw + lay.red_lg);
+  float* red_nrm = reinterpret_cast<float*>(smem_raw + lay.red_nrm);
+  float* inv_s = reinterpret_cast<float*>(smem_raw + lay.inv);
+  float* red_next = reinterpret_cast<float*>(smem_raw + lay.red_next);
+  uint2* wp = reinterpret_cast<uint2*>(smem_raw + lay.wp) + (size_t)warp * ns;
+  uint4* stash = reinterpret_cast<uint4*>(smem_raw + lay.stash);
+
+  // every load that depends on nothing, issued first: the first U bank sources, the current source, this and the
+  // next route's query slices, the norm weight slice, the route's table row and the bank rows' inverse RMS
+  const __nv_bfloat16* bank_t = p.bank + t * D + c;
+  uint4 buf[U];
+#pragma unroll
+  for (int i = 0; i < U; ++i)
+    if (i < S) buf[i] = ld_nc_u4(bank_t + (int64_t)i * p.bank_stride);
+  uint4 cur = *reinterpret_cast<const uint4*>(p.source + t * D + c);
+  const __nv_bfloat16* q_c = p.queries + (int64_t)p.route * D + c;
+  const uint4 q_route = *reinterpret_cast<const uint4*>(q_c);
+  uint4 q_next = make_uint4(0u, 0u, 0u, 0u);
+  if (ahead) q_next = *reinterpret_cast<const uint4*>(q_c + D);
+  if (p.norm_weight) stash[blockDim.x + tid] = *reinterpret_cast<const uint4*>(p.norm_weight + c);
+  constexpr int kPerLane = kMaxSources / 32;
+  const float* trow = p.table + ((int64_t)p.route * p.T + t) * p.table_stride;
+  float lv[kPerLane];
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int s = lane + 32 * i;
+    lv[i] = s < S ? trow[s] : -INFINITY;
+  }
+  // the bank rows' inverse RMS (for the look-ahead keys): loaded now, stored to shared memory once the logit work
+  // has hidden the load
+  constexpr int kInvRegs = kMaxSources / 128;  // blockDim >= 128
+  float inv_reg[kInvRegs];
+#pragma unroll
+  for (int j = 0; j < kInvRegs; ++j) {
+    const int s = tid + j * blockDim.x;
+    inv_reg[j] = ahead && s < S ? p.inv_rms[t * p.inv_stride + s] : 0.f;
+  }
+
+  // inverse RMS of the current source (kept for the later routes when it becomes bank row S)
+  const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+  {
+    uint64_t ss2 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint64_t f = bf2_to_x2(w[k]);
+      ss2 = fma_x2(f, f, ss2);
+    }
+    const float ss = zb::warp_sum(sum_x2(ss2));
+    if (lane == 0) red_ss[warp] = ss;
+  }
+  __syncthreads();
+  float ss_total = 0.f;
+  for (int i = 0; i < nwarps; ++i) ss_total += red_ss[i];
+  const float inv_cur = rsqrtf(ss_total * (1.0f / (float)D) + p.eps);
+  if (p.appended && tid == 0) p.inv_rms[t * p.inv_stride + S] = inv_cur;
+  uint32_t key[4];
+  keys8(cur, splat_x2(inv_cur), key);
+
+  // the current source's logit for this route
+  {
+    const float part = zb::warp_sum(dot8(key, q_route));
+    if (lane == 0) red_lg[warp] = part;
+  }
+#pragma unroll
+  for (int j = 0; j < kInvRegs; ++j) {
+    const int s = tid + j * blockDim.x;
+    if (ahead && s < S) inv_s[s] = inv_reg[j];
+  }
+  __syncthreads();
+  float lg_cur = 0.f;
+  for (int i = 0; i < nwarps; ++i) lg_cur += red_lg[i];
+
+  // every warp: fp32 softmax over the table row and the current logit, bf16 weights into its own row
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    if (lane + 32 * i == S) lv[i] = lg_cur;
+    m = fmaxf(m, lv[i]);
+  }
+  m = zb::warp_max(m);
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    lv[i] = lane + 32 * i < ns ? expf(lv[i] - m) : 0.f;
+    den += lv[i];
+  }
+  den = zb::warp_sum(den);
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int s = lane + 32 * i;
+    if (s < ns)
+      wp[s] = make_uint2((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lv[i] / den)) * 0x10001u,
+                         __float_as_uint(s < S ? inv_s[s] : 0.f));
+  }
+  // the current source's next-route logit (its keys are at hand); the source and the norm weight wait in shared
+  // memory while the mix holds the registers
+  if (ahead && p.appended) {
+    const float part = zb::warp_sum(dot8(key, q_next));
+    if (lane == 0) red_next[warp * ns + S] = part;
+  }
+  stash[tid] = cur;
+  __syncwarp();
+
+  // mix: sum over sources of bf16(v * w) in fp32, in source order; each consumed load is replaced by the one U
+  // sources ahead. Look-ahead: the partial next-route logit of every source, warp-summed 16 sources at a time.
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  auto term = [&](const uint4& v, uint32_t w2) {  // + bf16(v * w), column by column
+    add_bf2(hmul2_bits(v.x, w2), acc[0], acc[1]);
+    add_bf2(hmul2_bits(v.y, w2), acc[2], acc[3]);
+    add_bf2(hmul2_bits(v.z, w2), acc[4], acc[5]);
+    add_bf2(hmul2_bits(v.w, w2), acc[6], acc[7]);
+  };
+  auto step = [&](int s, const uint4& x, float& part) {
+    const uint2 wi = wp[s];
+    term(x, wi.x);
+    if (ahead) {
+      uint32_t kx[4];
+      keys8(x, splat_x2(__uint_as_float(wi.y)), kx);
+      part = dot8(kx, q_next);
+    }
+  };
+  const __nv_bfloat16* next_ld = bank_t + (int64_t)U * p.bank_stride;  // the row load U sources ahead
+  int s0 = 0;
+  for (; s0 + U <= S; s0 += U) {  // whole rounds of U sources
+    float part[U];
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      part[i] = 0.f;
+      step(s0 + i, buf[i], part[i]);
+      if (s0 + i + U < S) buf[i] = ld_nc_u4(next_ld);
+      next_ld += p.bank_stride;
+    }
+    if (ahead) {
+      const float total = warp_transpose_sum16(part, lane);
+      if (lane < U) red_next[warp * ns + s0 + lane] = total;
+    }
+  }
+  if (s0 < S) {  // the last S % U sources, already loaded
+    float part[U];
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      part[i] = 0.f;
+      if (s0 + i < S) step(s0 + i, buf[i], part[i]);
+    }
+    if (ahead) {
+      const float total = warp_transpose_sum16(part, lane);
+      if (lane < U && s0 + lane < S) red_next[warp * ns + s0 + lane] = total;
+    }
+  }
+  cur = stash[tid];
+  term(cur, wp[S].x);
+  float mix[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mix[j] = zb::bf16_round(acc[j]);
+  const int64_t off = t * D + c;
+  if (p.norm_weight) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(mix[j], mix[j], ss);
+    ss = zb::warp_sum(ss);
+    if (lane == 0) red_nrm[warp] = ss;
+    __syncthreads();
+    float total = 0.f;
+    for (int i = 0; i < nwarps; ++i) total += red_nrm[i];
+    const float rn = rsqrtf(total * (1.0f / (float)D) + p.norm_eps);
+    const uint4 nw = stash[blockDim.x + tid];
+    const uint32_t nww[4] = {nw.x, nw.y, nw.z, nw.w};
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      y[2 * j] = mix[2 * j] * rn * __uint_as_float(nww[j] << 16);
+      y[2 * j + 1] = mix[2 * j + 1] * rn * __uint_as_float(nww[j] & 0xffff0000u);
+    }
+    if (p.mix_out) *reinterpret_cast<uint4*>(p.mix_out + off) = zb::pack_bf16x8(mix);
+    *reinterpret_cast<uint4*>(p.out + off) = zb::pack_bf16x8(y);
+  } else {
+    *reinterpret_cast<uint4*>(p.out + off) = zb::pack_bf16x8(mix);
+  }
+  if (p.append) *reinterpret_cast<uint4*>(p.append + off) = cur;
+
+  // the next route's logits: each source's warp sums added in warp order
+  if (ahead) {
+    __syncthreads();
+    const int nnext = S + (p.appended ? 1 : 0);
+    float* next_row = p.table + ((int64_t)(p.route + 1) * p.T + t) * p.table_stride;
+    for (int s = tid; s < nnext; s += blockDim.x) {
+      float lg = 0.f;
+      for (int i = 0; i < nwarps; ++i) lg += red_next[i * ns + s];
+      next_row[s] = lg;
+    }
+  }
+}
+
+template <int U, int kMaxThreads, int kMinBlocks>
+int launch_tabled(const TabledParams& p, cudaStream_t stream) {
+  const size_t smem = TabledLayout(p.D / 256, p.S + 1).total;
+  auto kernel = attnres_tabled_kernel<U, kMaxThreads, kMinBlocks>;
+  if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kernel<<<(unsigned)p.T, p.D / 8, smem, stream>>>(p);
+  return zb::check_launch("attnres_route_tabled");
+}
+
 }  // namespace
 
 ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, const uint16_t* source,
@@ -434,4 +747,48 @@ ZB_API int zb_attnres_route(const uint16_t* bank, int64_t bank_stride, int S, co
   if (C == 1024) return launch<1024>(p, stream);
   if (C == 512) return launch<512>(p, stream);
   return launch<256>(p, stream);
+}
+
+ZB_API int zb_attnres_route_tabled(const uint16_t* bank, int64_t bank_stride, int S, const uint16_t* source,
+                                   uint16_t* append, int source_in_bank, const uint16_t* queries, int num_routes,
+                                   int route, float eps, const uint16_t* norm_weight, float norm_eps, uint16_t* out,
+                                   uint16_t* mix_out, float* table, int64_t table_stride, float* inv_rms,
+                                   int64_t inv_stride, int T, int D, cudaStream_t stream) {
+  ZB_REQUIRE(S >= 0 && T >= 0 && D > 0, "attnres_route_tabled: bad sizes S=%d T=%d D=%d", S, T, D);
+  ZB_REQUIRE(num_routes > 0 && route >= 0 && route < num_routes,
+             "attnres_route_tabled: route %d outside [0, %d)", route, num_routes);
+  if (D % 256 != 0 || D > 4096)
+    return zb::fail(zb::kUnsupported, "attnres_route_tabled: D=%d (a multiple of 256, at most 4096)", D);
+  // the look-ahead keeps each thread's share of the rows' inverse RMS in kMaxSources / 128 registers
+  if (S + 1 > std::min(kMaxSources, (kMaxSources / 128) * (D / 8)))
+    return zb::fail(zb::kUnsupported, "attnres_route_tabled: %d sources at D=%d (max %d)", S + 1, D,
+                    std::min(kMaxSources, (kMaxSources / 128) * (D / 8)));
+  if (D % 256 != 0 || D > 4096)
+    return zb::fail(zb::kUnsupported, "attnres_route_tabled: D=%d (a multiple of 256, at most 4096)", D);
+  if (T == 0) return zb::kOk;
+  const int appended = (append != nullptr || source_in_bank) ? 1 : 0;
+  ZB_REQUIRE(source && queries && out && table && inv_rms,
+             "attnres_route_tabled: null source/queries/out/table/inv_rms");
+  ZB_REQUIRE(!(append && source_in_bank), "attnres_route_tabled: a source already in the bank is not appended");
+  ZB_REQUIRE(S == 0 || bank, "attnres_route_tabled: null bank with S=%d", S);
+  ZB_REQUIRE(S == 0 || bank_stride >= (int64_t)T * D, "attnres_route_tabled: bank_stride smaller than T*D");
+  ZB_REQUIRE(bank_stride % 8 == 0, "attnres_route_tabled: bank_stride must be a multiple of 8 elements");
+  ZB_REQUIRE(table_stride >= S + appended && inv_stride >= S + appended,
+             "attnres_route_tabled: table / inverse-RMS rows (%lld / %lld floats) below the %d sources",
+             (long long)table_stride, (long long)inv_stride, S + appended);
+  ZB_REQUIRE(out != source && out != append && (mix_out == nullptr || (mix_out != out && mix_out != source)),
+             "attnres_route_tabled: out / mix_out must not alias the sources");
+  ZB_REQUIRE(!mix_out || norm_weight, "attnres_route_tabled: mix_out is only written with norm_weight");
+  for (const void* ptr : {(const void*)bank, (const void*)source, (const void*)append, (const void*)queries,
+                          (const void*)norm_weight, (const void*)out, (const void*)mix_out}) {
+    ZB_REQUIRE_ALIGNED(ptr, 16, "attnres_route_tabled tensors");
+  }
+  TabledParams p{reinterpret_cast<const __nv_bfloat16*>(bank), bank_stride, S,
+                 reinterpret_cast<const __nv_bfloat16*>(source), reinterpret_cast<__nv_bfloat16*>(append), appended,
+                 reinterpret_cast<const __nv_bfloat16*>(queries), num_routes, route, eps,
+                 reinterpret_cast<const __nv_bfloat16*>(norm_weight), norm_eps,
+                 reinterpret_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(mix_out), table,
+                 table_stride, inv_rms, inv_stride, T, D};
+  if (D <= 2048) return launch_tabled<16, 256, 2>(p, stream);
+  return launch_tabled<16, 512, 1>(p, stream);
 }

@@ -179,6 +179,81 @@ def attnres_route(
     return out
 
 
+def attnres_route_tabled(
+    bank: torch.Tensor | None,
+    num_sources: int,
+    source: torch.Tensor,
+    queries: torch.Tensor,
+    route: int,
+    table: torch.Tensor,
+    inv_rms: torch.Tensor,
+    eps: float,
+    *,
+    source_in_bank: bool = False,
+    append_to: torch.Tensor | None = None,
+    norm_weight: torch.Tensor | None = None,
+    norm_eps: float = 1e-5,
+    out: torch.Tensor | None = None,
+    mix_out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Route ``route`` of a forward whose route queries (``queries`` [R, D] bf16) are registered up front, over
+    ``bank[:num_sources]`` + ``source`` (the current source).
+
+    ``table`` (fp32 [R, T, >= sources]) carries the logits from route to route: this route reads its rows'
+    logits from ``table[route]`` and, while it mixes, writes the next route's logits of the same rows and, when
+    the source becomes bank row ``num_sources`` (``append_to`` given, or ``source_in_bank`` for a source that
+    already is that row), of the source, to ``table[route + 1]``. ``inv_rms`` (fp32 [>= T, >= sources]) holds the
+    bank rows' key inverse RMS; the source's is stored at column ``num_sources`` when it becomes that row. Same mix,
+    rounding points, fused RMSNorm and append as :func:`attnres_route`.
+    """
+    _check_cuda("queries", queries, torch.bfloat16)
+    dev = queries.device
+    _require(queries.dim() == 2 and queries.is_contiguous(), "queries must be a contiguous [R, D] tensor")
+    R, D = queries.shape
+    _require(0 <= route < R, f"route {route} outside [0, {R})")
+    _check_cuda("source", source, torch.bfloat16, dev)
+    _require(source.dim() == 2 and source.shape[1] == D and source.is_contiguous(),
+             f"source must be a contiguous [T, {D}] tensor")
+    T = source.shape[0]
+    bank_stride = 0
+    if num_sources:
+        _check_cuda("bank", bank, torch.bfloat16, dev)
+        _require(bank.dim() == 3 and bank.shape[0] >= num_sources and bank.shape[1] == T and bank.shape[2] == D,
+                 f"bank must be [>= {num_sources}, {T}, {D}], got {tuple(bank.shape)}")
+        _require(bank.stride(2) == 1 and bank.stride(1) == D, "bank rows must be contiguous [T, D]")
+        bank_stride = bank.stride(0)
+    _require(not (source_in_bank and append_to is not None), "a source already in the bank is not appended")
+    need = num_sources + (1 if source_in_bank or append_to is not None else 0)
+    _check_cuda("table", table, torch.float32, dev)
+    _require(table.dim() == 3 and table.shape[0] == R and table.shape[1] == T and table.shape[2] >= need
+             and table.is_contiguous(), f"table must be a contiguous [{R}, {T}, >= {need}] tensor")
+    _check_cuda("inv_rms", inv_rms, torch.float32, dev)
+    _require(inv_rms.dim() == 2 and inv_rms.shape[0] >= T and inv_rms.shape[1] >= need and inv_rms.stride(1) == 1,
+             f"inv_rms must be [>= {T}, >= {need}] with unit column stride")
+    if append_to is not None:
+        _check_cuda("append_to", append_to, torch.bfloat16, dev)
+        _require(append_to.shape == (T, D) and append_to.is_contiguous(), "append_to must be a contiguous [T, D] row")
+    if norm_weight is not None:
+        _check_cuda("norm_weight", norm_weight, torch.bfloat16, dev)
+        _require(norm_weight.shape == (D,), "norm_weight must be [D]")
+    if out is None:
+        out = torch.empty((T, D), device=dev, dtype=torch.bfloat16)
+    for name, t in (("out", out), ("mix_out", mix_out)):
+        if t is not None:
+            _check_cuda(name, t, torch.bfloat16, dev)
+            _require(t.shape == (T, D) and t.is_contiguous(), f"{name} must be a contiguous [T, D] tensor")
+    _require(mix_out is None or norm_weight is not None, "mix_out is only produced with norm_weight")
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call(
+        "zb_attnres_route_tabled",
+        ptr(bank) if num_sources else None, bank_stride, num_sources, source.data_ptr(), ptr(append_to),
+        int(bool(source_in_bank)), queries.data_ptr(), R, int(route), float(eps), ptr(norm_weight), float(norm_eps),
+        out.data_ptr(), ptr(mix_out), table.data_ptr(), table.shape[2], inv_rms.data_ptr(), inv_rms.stride(0), T, D,
+        _stream(dev),
+    )
+    return out
+
+
 def device_status(clear: bool = True) -> int:
     """Bits set by kernels whose bounded device-side waits expired on the current device (synchronous)."""
     import ctypes
