@@ -121,13 +121,20 @@ def expert_weights(E, D, I, seed, scale=0.02):
     return gate_up, down
 
 
-@pytest.mark.parametrize("T,D,E,k,I", [(64, 256, 8, 2, 512), (200, 1024, 16, 4, 256), (1, 2048, 64, 8, 768),
-                                       (513, 2048, 64, 8, 768)])
-def test_grouped_gemms_match_oracle(zb, T, D, E, k, I):
+@pytest.mark.parametrize("T,D,E,k,I,skew", [(64, 256, 8, 2, 512, False), (200, 1024, 16, 4, 256, False),
+                                            (1, 2048, 64, 8, 768, False), (513, 2048, 64, 8, 768, False),
+                                            (256, 2048, 64, 8, 768, True)])
+def test_grouped_gemms_match_oracle(zb, T, D, E, k, I, skew):
+    """Decode-sized batches run the 64-rows-per-CTA shape of the GEMMs, larger ones the 128-row shape; the skewed
+    case sends most pairs to a few experts (several 128-row blocks each at decode size)."""
     gen = torch.Generator().manual_seed(T + D)
     x = torch.randn(T, D, generator=gen).bfloat16()
     gate_up, down = expert_weights(E, D, I, seed=T)
-    ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)]).int()
+    if skew:  # expert e drawn with probability ~ exp(-e / 3)
+        prob = torch.exp(-torch.arange(E, dtype=torch.float32) / 3)
+        ids = torch.stack([torch.multinomial(prob, k, generator=gen) for _ in range(T)]).int()
+    else:
+        ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)]).int()
     w = torch.softmax(torch.randn(T, k, generator=gen), -1)
     dev = torch.device("cuda")
     ws = zb.ops.MoEWorkspace(T, k, E, D, I, dev)

@@ -22,7 +22,10 @@
 //               the leader's accumulator-empty barrier; the accumulator is double-buffered so the epilogue of one
 //               tile overlaps the MMAs of the next.
 // Expert row groups are padded to 128 rows; a 256-row tile whose second half belongs to the next expert computes
-// it and the epilogue drops those rows. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
+// it and the epilogue drops those rows. Decode-sized batches (a few dozen rows per expert) run a single-CTA shape of
+// the same kernel instead: tcgen05.mma.cta_group::1 with M = 128, N = 256 (the CTA loads its 128 A rows and all
+// 256 B rows, 48 KB per stage, 4 stages), because there the pair's M = 256 spends its tensor time on padding
+// rows: the 256 x 256 x K products per weight tile bound those GEMMs, not the weight stream. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
 // pairs running at one time share weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the
 // kernel sets a status bit, stops issuing, drains (bounded), frees TMEM and returns.
 #include <cuda.h>
@@ -34,14 +37,23 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
-constexpr int PAIR_M = 2 * BM;                 // rows of a pair tile
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kEpilogueWarps = 8;               // two per TMEM lane quarter, each half of the columns
 constexpr uint32_t kStageOutBytes = 32 * 64;     // per epilogue warp: 32 rows x 32 bf16 output columns
 constexpr int kThreads = (2 + kEpilogueWarps) * 32;
 constexpr uint32_t A_BYTES = BM * BK * 2;      // 16 KB: this CTA's A rows
-constexpr uint32_t B_BYTES = BM * BK * 2;      // 16 KB: this CTA's half of the 256 B rows
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t BOX_BYTES = BM * BK * 2;    // 16 KB: one 128-row B box
+// the two shapes: a CTA pair (M = 256 over the pair, each CTA one of the two B boxes of the 256-wide tile) or one
+// CTA (M = 128, both B boxes)
+template <bool PAIR>
+struct Shape {
+  static constexpr int CTAS = PAIR ? 2 : 1;
+  static constexpr int ROWS = CTAS * BM;                       // A rows of a tile
+  static constexpr uint32_t B_BYTES = PAIR ? BOX_BYTES : 2 * BOX_BYTES;  // this CTA's B rows
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = PAIR ? 6 : 4;
+};
+constexpr int kMaxStages = 6;
 constexpr int kTmemCols = 512;
 constexpr int kMaxExperts = 128;
 
@@ -67,23 +79,44 @@ struct GemmParams {
 
 // Tensor load into this CTA's shared memory whose completed bytes count on `bar`, an mbarrier of either CTA of the
 // pair (here always the leader's). No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-      "%3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
+template <bool PAIR>
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+  }
 }
 
-// Pair-wide TMEM allocation: the same warp of both CTAs executes it; each CTA receives its base address.
+// TMEM allocation (pair-wide: the same warp of both CTAs executes it; each CTA receives its base address).
+template <bool PAIR>
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  if constexpr (PAIR) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
 }
 
+template <bool PAIR>
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  if constexpr (PAIR) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  } else {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  }
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -93,24 +126,40 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Pair-wide MMA (issued by one thread of the leader CTA): D[256 x N] over both CTAs' TMEM from both CTAs' A and B
-// halves at the same shared-memory offsets.
+// MMA issued by one thread (of the leader CTA for a pair): D[M x N] from A and B in shared memory; for a pair over
+// both CTAs' TMEM from both CTAs' A and B halves at the same shared-memory offsets.
+template <bool PAIR>
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (PAIR) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
-// Arrives once on the mbarrier at offset `bar` in each CTA of `mask` when every tcgen05.mma issued so far by this
-// thread has completed.
-__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
-      "h"(mask)
-      : "memory");
+// Arrives once on the mbarrier at offset `bar` (in each CTA of `mask`, for a pair) when every tcgen05.mma issued so
+// far by this thread has completed.
+template <bool PAIR>
+__device__ __forceinline__ void tc_commit(uint32_t bar, uint16_t mask) {
+  if constexpr (PAIR) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            bar),
+        "h"(mask)
+        : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+  }
 }
 
 // Plain arrival on an mbarrier of any CTA of the cluster (shared::cluster address).
@@ -145,17 +194,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M=256 (the pair), N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(PAIR_M >> 4) << 24);
+// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M (256 for the pair, 128 for one
+// CTA), N = 256.
+template <int M>
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 
 // SiLU with the fast exponential and division: the product silu(gate) * up is rounded to bf16, where their
 // few-ulp fp32 error is far below the rounding step.
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 struct Shared {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
@@ -166,10 +216,13 @@ struct Shared {
 };
 constexpr uint32_t kSharedBytes = (sizeof(Shared) + 127) / 128 * 128;
 
-template <int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int MODE, bool PAIR>
+__global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     GemmParams p) {
+  using Sh = Shape<PAIR>;
+  constexpr int STAGES = Sh::STAGES, CTAS = Sh::CTAS, ROWS = Sh::ROWS;
+  constexpr uint32_t STAGE_BYTES = Sh::STAGE_BYTES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // stage buffers first, 1024-byte aligned (the 128B swizzle pattern repeats every 1024 bytes); the dynamic
   // shared-memory base is the same in both CTAs, so every buffer sits at the same offset in the pair
@@ -180,9 +233,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // [kEpilogueWarps][32 rows x 64 B], 128-byte aligned after the barrier block
   unsigned char* out_stage = stages + STAGES * STAGE_BYTES + kSharedBytes;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const uint32_t rank = blockIdx.x & 1;  // cluster of 2 along x: rank 0 leads the pair
+  const uint32_t rank = PAIR ? (blockIdx.x & 1) : 0;  // cluster of 2 along x: rank 0 leads the pair
   const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int pair = PAIR ? blockIdx.x >> 1 : blockIdx.x, npairs = PAIR ? gridDim.x >> 1 : gridDim.x;
   volatile int* abort_flag = &sh->abort;
 
   if (tid == 0) {
@@ -192,7 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       zb::mbar_init(zb::smem_addr(&sh->tmem_full[a]), 1);
-      zb::mbar_init(zb::smem_addr(&sh->tmem_empty[a]), 2 * kEpilogueWarps);  // the epilogue warps of both CTAs
+      zb::mbar_init(zb::smem_addr(&sh->tmem_empty[a]), CTAS * kEpilogueWarps);  // the epilogue warps of the CTAs
     }
     zb::mbar_init(zb::smem_addr(&sh->drain), 1);
     sh->abort = 0;
@@ -200,16 +253,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   for (int e = tid; e <= p.E; e += kThreads) sh->row_off[e] = p.offsets[e];
   __syncthreads();
-  if (tid == 0) {  // work items per expert: ceil(128-row tiles / 2) pair tiles x n-tiles
+  if (tid == 0) {  // work items per expert: ceil(128-row tiles / CTAS) tiles x n-tiles
     int acc = 0;
     for (int e = 0; e < p.E; ++e) {
       sh->item_start[e] = acc;
       const int m128 = (sh->row_off[e + 1] - sh->row_off[e]) / BM;
-      acc += (m128 + 1) / 2 * p.n_tiles;
+      acc += (m128 + CTAS - 1) / CTAS * p.n_tiles;
     }
     sh->item_start[p.E] = acc;
   }
-  if (warp == 1) tmem_alloc(zb::smem_addr(&sh->tmem_base), kTmemCols);
+  if (warp == 1) tmem_alloc<PAIR>(zb::smem_addr(&sh->tmem_base), kTmemCols);
   tc_fence_before();
   __syncthreads();
   zb::cluster_arrive_relaxed();  // both CTAs' barriers are initialised before either signals the other's
@@ -232,7 +285,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int m_tiles = (sh->item_start[e + 1] - sh->item_start[e]) / p.n_tiles;
     const int local = item - sh->item_start[e];
     n = local / m_tiles;
-    row0 = sh->row_off[e] + (local % m_tiles) * PAIR_M;
+    row0 = sh->row_off[e] + (local % m_tiles) * ROWS;
   };
 
   if (warp == 0) {
@@ -243,6 +296,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         decode(item, e, n, row0);
         const int a_row = row0 + (int)rank * BM;
         const int b_row = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step + (rank ? p.b_second_offset : 0);
+        const int b_row2 = b_row + p.b_second_offset;  // the second B box (one CTA only)
         for (int kb = 0; kb < k_blocks; ++kb, ++q) {
           const int s = q % STAGES;
           const uint32_t parity = ((q / STAGES) & 1) ^ 1;
@@ -251,11 +305,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t full_local = zb::smem_addr(&sh->full[s]);
-          if (leader) zb::mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
-          const uint32_t full_leader = zb::mapa_shared(full_local, 0);
+          if (leader) zb::mbar_arrive_expect_tx(full_local, CTAS * STAGE_BYTES);
+          const uint32_t full_leader = PAIR ? zb::mapa_shared(full_local, 0) : full_local;
           const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
-          tma_load_2d_pair(a_dst, &tmap_a, kb * BK, a_row, full_leader);
-          tma_load_2d_pair(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
+          tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+          tma_load_2d<PAIR>(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
+          if (!PAIR) tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, &tmap_b, kb * BK, b_row2, full_leader);
         }
       }
       if (leader) {  // drain: wait (bounded) for the copies still in flight before the CTA may exit
@@ -293,16 +348,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            tc_mma(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), kIdesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma<PAIR>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                         kIdesc<ROWS>, (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit_pair(zb::smem_addr(&sh->empty[s]), 0x3);  // stage s of both CTAs is free
+          tc_commit<PAIR>(zb::smem_addr(&sh->empty[s]), 0x3);  // stage s (of both CTAs of a pair) is free
         }
         if (!ok) break;
-        tc_commit_pair(zb::smem_addr(&sh->tmem_full[acc]), 0x3);
+        tc_commit<PAIR>(zb::smem_addr(&sh->tmem_full[acc]), 0x3);
       }
       // every MMA issued by this thread has completed before TMEM is released
-      tc_commit_pair(zb::smem_addr(&sh->drain), 0x1);
+      tc_commit<PAIR>(zb::smem_addr(&sh->drain), 0x1);
       zb::mbar_wait_bounded(zb::smem_addr(&sh->drain), 0, nullptr, 0, 200000000ull);
     }
   } else {
@@ -394,7 +449,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   zb::cluster_wait();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc<PAIR>(tmem_base, kTmemCols);
   }
 }
 
@@ -427,12 +482,24 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int
   return zb::kOk;
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + kSharedBytes + kEpilogueWarps * kStageOutBytes;
+template <bool PAIR>
+constexpr size_t smem_bytes() {
+  return 1024 + Shape<PAIR>::STAGES * Shape<PAIR>::STAGE_BYTES + kSharedBytes + kEpilogueWarps * kStageOutBytes;
+}
 
-template <int MODE>
+// The single-CTA shape for batches whose permuted layout (capacity rows over E experts) averages at most 96 routed
+// rows per expert (decode), the pair shape otherwise.
+bool use_pair(int64_t capacity, int E) {
+  const int64_t routed = capacity - (int64_t)E * (BM - 1);  // about the pairs the capacity was sized for
+  return routed > (int64_t)E * 96;
+}
+
+template <int MODE, bool PAIR>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int64_t capacity,
            cudaStream_t stream) {
-  auto kernel = moe_gemm_kernel<MODE>;
+  auto kernel = moe_gemm_kernel<MODE, PAIR>;
+  constexpr size_t kSmemBytes = smem_bytes<PAIR>();
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
   static int configured[64] = {0};
   int dev = 0;
   ZB_CUDA(cudaGetDevice(&dev));
@@ -440,24 +507,45 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int6
     ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
-  // the persistent loop assumes every pair is resident at once: as many pairs as the GPU co-schedules (a pair
+  // the persistent loop assumes every CTA (pair) is resident at once: as many as the GPU co-schedules (a pair
   // needs two SMs of one GPC), cached per device
-  static int resident_pairs[64] = {0};
-  int max_pairs = dev >= 0 && dev < 64 ? resident_pairs[dev] : 0;
-  if (max_pairs == 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    ZB_CUDA(cudaOccupancyMaxActiveClusters(&max_pairs, kernel, &cfg));
-    if (max_pairs < 1) return zb::fail(zb::kUnsupported, "moe_gemm: no CTA pair fits on this GPU");
-    if (dev >= 0 && dev < 64) resident_pairs[dev] = max_pairs;
+  static int resident[64] = {0};
+  int max_units = dev >= 0 && dev < 64 ? resident[dev] : 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = Shape<PAIR>::CTAS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  if (max_units == 0) {
+    if constexpr (PAIR) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      ZB_CUDA(cudaOccupancyMaxActiveClusters(&max_units, kernel, &cfg));
+    } else {
+      int per_sm = 0, sms = 0;
+      ZB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes));
+      ZB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      max_units = per_sm * sms;
+    }
+    if (max_units < 1) return zb::fail(zb::kUnsupported, "moe_gemm: no CTA (pair) fits on this GPU");
+    if (dev >= 0 && dev < 64) resident[dev] = max_units;
   }
-  // pair tiles: at most half of the 128-row tiles plus one per expert
-  const int64_t upper_items = (capacity / BM / 2 + p.E) * p.n_tiles;
-  const int pairs = (int)std::min<int64_t>(upper_items, max_pairs);
-  if (pairs <= 0) return zb::kOk;
-  kernel<<<2 * pairs, kThreads, kSmemBytes, stream>>>(a, b, p);
+  // tiles: at most capacity / tile rows plus one per expert
+  const int64_t upper_items = (capacity / Shape<PAIR>::ROWS + p.E) * p.n_tiles;
+  const int units = (int)std::min<int64_t>(upper_items, max_units);
+  if (units <= 0) return zb::kOk;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(Shape<PAIR>::CTAS * units));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, b, p));
   return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
 }
 
@@ -485,7 +573,8 @@ ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const ui
   if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
   GemmParams p{offsets, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I, nullptr,
                nullptr, zb::device_status_ptr()};
-  return launch<kSwiGLU>(ma, mb, p, capacity, stream);
+  return use_pair(capacity, E) ? launch<kSwiGLU, true>(ma, mb, p, capacity, stream)
+                                : launch<kSwiGLU, false>(ma, mb, p, capacity, stream);
 }
 
 ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
@@ -502,5 +591,6 @@ ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t*
   if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
   GemmParams p{offsets, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D, D,
                sorted_pairs, weights, zb::device_status_ptr()};
-  return launch<kDown>(ma, mb, p, capacity, stream);
+  return use_pair(capacity, E) ? launch<kDown, true>(ma, mb, p, capacity, stream)
+                                : launch<kDown, false>(ma, mb, p, capacity, stream);
 }
