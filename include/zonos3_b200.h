@@ -85,6 +85,17 @@ int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const uint16_t*
                     uint16_t* q,
                     uint16_t* k, uint16_t* v, float* g, float* beta, cudaStream_t stream);
 
+/* The GDN prologue of a decode batch: row i of mixed is the one new token of request i, whose conv history is row
+ * slots[i] of conv_state (a slot outside [0, conv_rows) is a padding row: zero history, nothing written); the same
+ * kernel replaces each history by its last 2 entries and the token's input, so no second launch follows. Same
+ * outputs as zb_gdn_prologue with cu_seqlens = 0..N, seq_of_token = 0..N-1, fresh = NULL. Replaces the conv / L2
+ * norm / gate steps of one OriginalGDN._forward_decode_static call (servers/sgl/src/zonos3_sgl/models/gdn.py:329-355
+ * through _run_packed, 395-434) for the new row; math of model/src/zonos3/reference/lm.py:561-573. */
+int zb_gdn_prologue_decode(const uint16_t* mixed, int64_t mixed_stride, const uint16_t* conv_weight,
+                           const float* A_log, const float* dt_bias, const int64_t* slots, uint16_t* conv_state,
+                           int64_t conv_rows, int N, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v, float* g,
+                           float* beta, cudaStream_t stream);
+
 /* GDN epilogue: out[N, H*D] = bf16(RMSNorm(o; weight [D], eps) * SiLU(z)) per (token, head), o [N, H, D] bf16,
  * z [N, H*D] bf16 with row stride z_stride. Replaces FLA layer_norm_gated_fwd (swish gate, RMS) in
  * OriginalGDN._run_packed (servers/sgl/src/zonos3_sgl/models/gdn.py:435-445); lm.py:585-587. */

@@ -38,6 +38,9 @@ SIGNATURES: dict[str, list] = {
     # conv_rows, num_seqs, N, H, D, q, k, v, g, beta, stream
     "zb_gdn_prologue": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _p, _p, _p, _p, _p,
                         _p],
+    # mixed, mixed_stride, conv_weight, A_log, dt_bias, slots, conv_state, conv_rows, N, H, D, q, k, v, g, beta,
+    # stream
+    "zb_gdn_prologue_decode": [_p, _i64, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p],
     # o, z, z_stride, weight, eps, N, H, D, out, stream
     "zb_gdn_gated_norm": [_p, _p, _i64, _p, _f32, _i32, _i32, _i32, _p, _p],
     # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream

@@ -9,7 +9,9 @@
 // One CTA per (token, q / k / v part); a warp covers one head slice (D / 32 channels per lane), so the per-head L2
 // norm is a warp reduction. History rows before a sequence's first token come from conv_state [slot, channels, W-1]
 // (the layout of LMCache.conv_state); a second small kernel then writes each sequence's new history (its last W-1
-// inputs), after every token has read the old one.
+// inputs), after every token has read the old one. Decode (one token per sequence, zb_gdn_prologue_decode): the CTA
+// that reads a sequence's history rows of its channels is their only reader, so it writes the shifted history
+// (the last W-2 entries and the token's input) itself and the second kernel is not launched.
 //
 // Epilogue (replaces FLA layer_norm_gated_fwd, gdn.py:435-445; lm.py:585-587): gated = RMSNorm(o; out_weight,
 // 1e-5) * SiLU(z) per head, computed in fp32 and rounded once to bf16; one warp per (token, head).
@@ -63,19 +65,21 @@ __device__ __forceinline__ void load_bf(const __nv_bfloat16* src, float (&out)[P
 
 // One CTA per (token, part): part 0 = q, 1 = k, 2 = v; warp h covers head h's D channels, lane owns PL = D / 32
 // consecutive channels. Every input of a lane (its PL x W weights, the history rows and the rows of this sequence)
-// is loaded before any arithmetic.
-template <int PL>
+// is loaded before any arithmetic. kDecode: token i is sequence i (no cu_seqlens / seq_of_token / fresh), and the
+// lane replaces its channels' history rows.
+template <int PL, bool kDecode>
 __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
   const int64_t tok = blockIdx.x;
   const int part = blockIdx.y;
   const int h = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int inner = p.H * p.D;
-  const int seq = p.seq_of_token[tok];
-  const int64_t start = p.cu_seqlens[seq];
+  const int seq = kDecode ? (int)tok : p.seq_of_token[tok];
+  const int64_t start = kDecode ? tok : p.cu_seqlens[seq];
   const int64_t pos = tok - start;  // position inside the sequence
   const int64_t slot = p.slots[seq];
   // a padding sequence (graph padding rows) reads a zero history and never writes one
-  const bool fresh = (p.fresh ? p.fresh[seq] != 0 : false) || slot < 0 || slot >= p.rows;
+  const bool padding = slot < 0 || slot >= p.rows;
+  const bool fresh = (!kDecode && p.fresh ? p.fresh[seq] != 0 : false) || padding;
   const __nv_bfloat16* row = p.mixed + tok * p.mixed_stride;
   const int ch0 = part * inner + h * p.D + lane * PL;
 
@@ -118,6 +122,28 @@ __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
       const int64_t hidx = (kW - 1) - (back - pos);
 #pragma unroll
       for (int j = 0; j < PL; ++j) xin[w][j] = hist[j * (kW - 1) + hidx];
+    }
+  }
+  if (kDecode && !padding) {  // new history of the lane's channels: old entries 1 .. W-2, then this token's input
+    float nh[PL * (kW - 1)];
+#pragma unroll
+    for (int j = 0; j < PL; ++j) {
+#pragma unroll
+      for (int e = 0; e < kW - 2; ++e) nh[j * (kW - 1) + e] = hist[j * (kW - 1) + e + 1];
+      nh[j * (kW - 1) + kW - 2] = xin[kW - 1][j];
+    }
+    __nv_bfloat16* hp = p.conv_state + (slot * 3 * inner + ch0) * (kW - 1);
+    if constexpr (PL == 4) {  // 12 entries, 8-byte aligned: three 8-byte stores
+#pragma unroll
+      for (int j = 0; j < 12; j += 4) {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(nh[j], nh[j + 1]);
+        const __nv_bfloat162 b = __floats2bfloat162_rn(nh[j + 2], nh[j + 3]);
+        *reinterpret_cast<uint2*>(hp + j) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < PL * (kW - 1); ++j) hp[j] = __float2bfloat16_rn(nh[j]);
     }
   }
   float acc[PL];
@@ -264,9 +290,9 @@ ZB_API int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const ui
   const dim3 grid((unsigned)N, 3);
   const unsigned threads = 32u * (unsigned)H;
   switch (D / 32) {
-    case 1: gdn_prologue_kernel<1><<<grid, threads, 0, stream>>>(p); break;
-    case 2: gdn_prologue_kernel<2><<<grid, threads, 0, stream>>>(p); break;
-    case 4: gdn_prologue_kernel<4><<<grid, threads, 0, stream>>>(p); break;
+    case 1: gdn_prologue_kernel<1, false><<<grid, threads, 0, stream>>>(p); break;
+    case 2: gdn_prologue_kernel<2, false><<<grid, threads, 0, stream>>>(p); break;
+    case 4: gdn_prologue_kernel<4, false><<<grid, threads, 0, stream>>>(p); break;
     default: return zb::fail(zb::kUnsupported, "gdn_prologue: head dim %d (32, 64 or 128)", D);
   }
   if (int rc = zb::check_launch("gdn_prologue")) return rc;
@@ -274,6 +300,39 @@ ZB_API int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const ui
   if (num_seqs > 0)
     gdn_conv_history_kernel<<<dim3((unsigned)num_seqs, (unsigned)((channels / 8 + 255) / 256)), 256, 0, stream>>>(p);
   return zb::check_launch("gdn_prologue(history)");
+}
+
+ZB_API int zb_gdn_prologue_decode(const uint16_t* mixed, int64_t mixed_stride, const uint16_t* conv_weight,
+                                  const float* A_log, const float* dt_bias, const int64_t* slots, uint16_t* conv_state,
+                                  int64_t conv_rows, int N, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v,
+                                  float* g, float* beta, cudaStream_t stream) {
+  ZB_REQUIRE(N >= 0 && H > 0, "gdn_prologue_decode: bad sizes N=%d H=%d", N, H);
+  if (D % 32 != 0 || D > 128) return zb::fail(zb::kUnsupported, "gdn_prologue_decode: head dim %d (32..128, /32)", D);
+  if (N == 0) return zb::kOk;
+  ZB_REQUIRE(mixed && conv_weight && A_log && dt_bias && slots && conv_state && q && k && v && g && beta,
+             "gdn_prologue_decode: null pointer");
+  ZB_REQUIRE(mixed_stride >= 4LL * H * D + 2 * H, "gdn_prologue_decode: mixed row stride %lld too small",
+             (long long)mixed_stride);
+  ZB_REQUIRE(H <= 32, "gdn_prologue_decode: H=%d (at most 32)", H);
+  ZB_REQUIRE(mixed_stride % 4 == 0, "gdn_prologue_decode: mixed row stride %lld must be a multiple of 4",
+             (long long)mixed_stride);
+  ZB_REQUIRE_ALIGNED(mixed, 16, "gdn_prologue_decode mixed");
+  ZB_REQUIRE_ALIGNED(conv_weight, 16, "gdn_prologue_decode conv_weight");
+  ZB_REQUIRE_ALIGNED(conv_state, 16, "gdn_prologue_decode conv_state");
+  PrologueParams p{reinterpret_cast<const __nv_bfloat16*>(mixed), mixed_stride,
+                   reinterpret_cast<const __nv_bfloat16*>(conv_weight), A_log, dt_bias, nullptr, nullptr, slots,
+                   reinterpret_cast<__nv_bfloat16*>(conv_state), conv_rows, nullptr,
+                   reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k),
+                   reinterpret_cast<__nv_bfloat16*>(v), g, beta, N, H, D};
+  const dim3 grid((unsigned)N, 3);
+  const unsigned threads = 32u * (unsigned)H;
+  switch (D / 32) {
+    case 1: gdn_prologue_kernel<1, true><<<grid, threads, 0, stream>>>(p); break;
+    case 2: gdn_prologue_kernel<2, true><<<grid, threads, 0, stream>>>(p); break;
+    case 4: gdn_prologue_kernel<4, true><<<grid, threads, 0, stream>>>(p); break;
+    default: return zb::fail(zb::kUnsupported, "gdn_prologue_decode: head dim %d (32, 64 or 128)", D);
+  }
+  return zb::check_launch("gdn_prologue_decode");
 }
 
 ZB_API int zb_gdn_gated_norm(const uint16_t* o, const uint16_t* z, int64_t z_stride, const uint16_t* weight, float eps,

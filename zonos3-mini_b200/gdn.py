@@ -147,8 +147,12 @@ class OriginalGDN(BaseOP):
         H, d = self._heads, self._head_dim
         inner = H * d
         mixed = F.linear(x, self.in_proj.weight)
-        q, k, v, g, beta = ops.gdn_prologue(mixed, self.conv.weight, self.A_log, self.dt_bias, cu, seq_of_token,
-                                            slots, self._conv_state, heads=H, head_dim=d, fresh=fresh)
+        if decode and not any_fresh:  # one token per request: the history update rides in the prologue kernel
+            q, k, v, g, beta = ops.gdn_prologue_decode(mixed, self.conv.weight, self.A_log, self.dt_bias, slots,
+                                                       self._conv_state, heads=H, head_dim=d)
+        else:
+            q, k, v, g, beta = ops.gdn_prologue(mixed, self.conv.weight, self.A_log, self.dt_bias, cu, seq_of_token,
+                                                slots, self._conv_state, heads=H, head_dim=d, fresh=fresh)
         if decode:
             o = ops.gdn_decode_step(q, k, v, g, beta, self._recurrent_state, slots=slots)
         else:

@@ -570,6 +570,39 @@ def gdn_prologue(mixed, conv_weight, A_log, dt_bias, cu_seqlens, seq_of_token, s
     return q, k, v, g, beta
 
 
+def gdn_prologue_decode(mixed, conv_weight, A_log, dt_bias, slots, conv_state, *, heads, head_dim, q=None, k=None,
+                        v=None, g=None, beta=None):
+    """:func:`gdn_prologue` for a decode batch: row i is the one new token of request i, whose conv history is row
+    ``slots[i]`` of conv_state (a slot outside [0, rows) is a padding row: zero history, nothing written). The
+    history update happens in the same kernel (no second launch). Returns (q, k, v, g, beta)."""
+    _check_cuda("mixed", mixed, torch.bfloat16)
+    dev = mixed.device
+    N = mixed.shape[0]
+    H, D = heads, head_dim
+    inner = H * D
+    _require(mixed.dim() == 2 and mixed.shape[1] >= 4 * inner + 2 * H and mixed.stride(1) == 1,
+             "mixed must be [N, 4*inner + 2*H] with contiguous rows")
+    _check_cuda("conv_weight", conv_weight, torch.bfloat16, dev)
+    _require(conv_weight.numel() == 3 * inner * 4 and conv_weight.is_contiguous(), "conv_weight must be [3*inner, 1, 4]")
+    _check_cuda("conv_state", conv_state, torch.bfloat16, dev)
+    _require(conv_state.dim() == 3 and conv_state.shape[1:] == (3 * inner, 3) and conv_state.is_contiguous(),
+             "conv_state must be a contiguous [rows, 3*inner, 3] tensor")
+    for name, t in (("A_log", A_log), ("dt_bias", dt_bias)):
+        _check_cuda(name, t, torch.float32, dev)
+    _check_cuda("slots", slots, torch.int64, dev)
+    _require(slots.numel() == N, f"slots must hold one row per token ({N}), got {slots.numel()}")
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    q = torch.empty(N, H, D, **bf) if q is None else q
+    k = torch.empty(N, H, D, **bf) if k is None else k
+    v = torch.empty(N, H, D, **bf) if v is None else v
+    g = torch.empty(N, H, device=dev, dtype=torch.float32) if g is None else g
+    beta = torch.empty(N, H, device=dev, dtype=torch.float32) if beta is None else beta
+    _lib.call("zb_gdn_prologue_decode", mixed.data_ptr(), mixed.stride(0), conv_weight.data_ptr(), A_log.data_ptr(),
+              dt_bias.data_ptr(), slots.data_ptr(), conv_state.data_ptr(), conv_state.shape[0], N, H, D,
+              q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _stream(dev))
+    return q, k, v, g, beta
+
+
 def gdn_gated_norm(o, z, weight, eps=1e-5, out=None):
     """Per-head RMSNorm(o; weight, eps) * SiLU(z), rounded once to bf16 (gdn.py:435-445; lm.py:585-587).
     o [N, H, d] bf16; z [N, H*d] bf16 view (row stride allowed); returns [N, H*d] bf16."""
