@@ -173,9 +173,10 @@ int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T,
 int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
                    int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream);
 
-/* out[r] = x[sorted_pairs[r] / k] for r < rows (zero rows where sorted_pairs[r] < 0): the A operand of the
- * grouped GEMM, the row gather fused_moe_kernel does through `offs_token // top_k`
- * (servers/sgl/src/zonos3_sgl/kernel/triton/fused_moe.py:145). */
+/* out[r] = x[sorted_pairs[r] / k] for r < rows where sorted_pairs[r] >= 0: the A operand of the grouped GEMM, the
+ * row gather fused_moe_kernel does through `offs_token // top_k` (servers/sgl/src/zonos3_sgl/kernel/triton/
+ * fused_moe.py:145). Padding rows (sorted_pairs[r] < 0) are left as they are: the reference masks them to zero,
+ * here the GEMMs compute them row-independently and drop their results, so no output depends on them. */
 int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sorted_pairs, int k, int64_t rows, int D,
                   uint16_t* out, cudaStream_t stream);
 

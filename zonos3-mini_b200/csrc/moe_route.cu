@@ -796,15 +796,18 @@ struct GatherParams {
   __nv_bfloat16* out;  // [rows, D]
 };
 
-// Row r of the permuted activations = x[sorted_pairs[r] / k] (zeros for padding rows). A warp copies whole rows:
-// the row's pair index is read once, then every lane keeps 8 independent 16-byte loads in flight.
+// Row r of the permuted activations = x[sorted_pairs[r] / k]; padding rows (sorted_pairs < 0) are not written: the
+// grouped GEMMs compute every row independently and drop the padding rows' results, so their content never reaches
+// an output (at decode most of the padded capacity is padding). A warp copies whole rows: the row's pair index is
+// read once, then every lane keeps 8 independent 16-byte loads in flight.
 __global__ void __launch_bounds__(256) moe_gather_kernel(GatherParams p) {
   const int lane = threadIdx.x % 32;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int vec_per_row = p.D / 8;
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < p.rows; r += warps) {
     const int pair = p.sorted_pairs[r];
-    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)(pair >= 0 ? pair / p.k : 0) * p.x_stride);
+    if (pair < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)(pair / p.k) * p.x_stride);
     uint4* dst = reinterpret_cast<uint4*>(p.out + r * p.D);
     for (int c0 = lane; c0 < vec_per_row; c0 += 32 * 8) {
       uint4 v[8];
@@ -812,7 +815,7 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(GatherParams p) {
       for (int j = 0; j < 8; ++j) {
         const int c = c0 + 32 * j;
         v[j] = make_uint4(0u, 0u, 0u, 0u);
-        if (pair >= 0 && c < vec_per_row) v[j] = __ldg(src + c);
+        if (c < vec_per_row) v[j] = __ldg(src + c);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j)

@@ -368,7 +368,7 @@ def moe_permute(ids, num_experts, *, block=GEMM_BLOCK, capacity=None, out=None):
 
 
 def moe_gather(x, sorted_pairs, top_k, out):
-    """out[r] = x[sorted_pairs[r] // k] (zero rows for padding)."""
+    """out[r] = x[sorted_pairs[r] // k] for live rows; padding rows (sorted_pairs < 0) are left as they are."""
     dev = x.device
     _check_cuda("x", x, torch.bfloat16)
     _check_cuda("out", out, torch.bfloat16, dev)
