@@ -356,10 +356,11 @@ def bench_moe_cfg4(ops, dev, stream, steps=10, warmup=3):
         ops.moe_gather(x, ws.perm["sorted_pairs"], k, ws.x_perm)
 
     def gemm1():
-        ops.moe_gemm_swiglu(ws.x_perm, gate_up, ws.perm["offsets"], ws.h)
+        ops.moe_gemm_swiglu(ws.x_perm, gate_up, ws.perm["offsets"], ws.h, counts=ws.perm["counts"])
 
     def gemm2():
-        ops.moe_gemm_down(ws.h, down, ws.perm["offsets"], ws.perm["sorted_pairs"], ws.weights, ws.y)
+        ops.moe_gemm_down(ws.h, down, ws.perm["offsets"], ws.perm["sorted_pairs"], ws.weights, ws.y,
+                          counts=ws.perm["counts"])
 
     def combine():
         ops.moe_combine(ws.y, k, out)

@@ -185,17 +185,20 @@ int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sorted_pai
  * expert e's segment [offsets[e], offsets[e+1]). Replaces the first fused_moe_kernel call plus silu_and_mul of
  * fused_experts_impl (servers/sgl/src/zonos3_sgl/layers/moe/fused_moe/fused_moe_impl.py:218-234).
  *   x_perm [capacity, D] bf16; gate_up [E, 2I, D] bf16 (gate rows first, zonos3.py:488-490); h [capacity, I] bf16
+ *   counts [E] (zb_moe_permute's) or NULL: with counts, decode-sized batches load only each segment's routed rows
+ *   (h rows past them hold garbage, like every padding row's).
  *   D a multiple of 64, I a multiple of 128, capacity a multiple of 128. */
 int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, int E, int D, int I,
-                       const int32_t* offsets, uint16_t* h, cudaStream_t stream);
+                       const int32_t* offsets, const int32_t* counts, uint16_t* h, cudaStream_t stream);
 
 /* GEMM2 of the routed experts on tcgen05 tensor cores with the routing weight fused:
  * y[p, :] = bf16((h[r] . down[e]^T) * weights[p]) for every row r with pair p = sorted_pairs[r] >= 0.
  * Replaces the second fused_moe_kernel call (MUL_ROUTED_WEIGHT) of fused_experts_impl (fused_moe_impl.py:236-259).
- *   h [capacity, I] bf16; down [E, D, I] bf16; weights [T*k] fp32; y [T*k, D] bf16.  I % 64 == 0, D % 128 == 0. */
+ *   h [capacity, I] bf16; down [E, D, I] bf16; weights [T*k] fp32; y [T*k, D] bf16; counts as for
+ *   zb_moe_gemm_swiglu.  I % 64 == 0, D % 128 == 0. */
 int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                     const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
-                     cudaStream_t stream);
+                     const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs, const float* weights,
+                     uint16_t* y, cudaStream_t stream);
 
 /* out[t, :] = bf16(sum over slots s of float(y[t*k + s, :])): the un-permute combine (the add / moe_sum_reduce of
  * fused_experts_impl, fused_moe_impl.py:267-288). out has row stride out_stride. */

@@ -58,9 +58,9 @@ SIGNATURES: dict[str, list] = {
     # x, x_stride, sorted_pairs, k, rows, D, out, stream
     "zb_moe_gather": [_p, _i64, _p, _i32, _i64, _i32, _p, _p],
     # x_perm, capacity, gate_up, E, D, I, offsets, h, stream
-    "zb_moe_gemm_swiglu": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p],
+    "zb_moe_gemm_swiglu": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p],
     # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, y, stream
-    "zb_moe_gemm_down": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p],
+    "zb_moe_gemm_down": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p],
     # y, T, k, D, out, out_stride, stream
     "zb_moe_combine": [_p, _i32, _i32, _i32, _p, _i64, _p],
     # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, T, k, out, out_stride, stream

@@ -25,7 +25,9 @@
 // it and the epilogue drops those rows. Decode-sized batches (a few dozen rows per expert) run a single-CTA shape of
 // the same kernel instead: tcgen05.mma.cta_group::1 with M = 128, N = 256 (the CTA loads its 128 A rows and all
 // 256 B rows, 48 KB per stage, 4 stages), because there the pair's M = 256 spends its tensor time on padding
-// rows: the 256 x 256 x K products per weight tile bound those GEMMs, not the weight stream. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
+// rows: the 256 x 256 x K products per weight tile bound those GEMMs, not the weight stream. Given the experts' row
+// counts, the single-CTA shape also loads only the rows a tile holds (32-row boxes); the MMA still reads 128 A rows,
+// and the rows past the last box are stale shared memory whose accumulator rows are padding rows of the segment. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
 // pairs running at one time share weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the
 // kernel sets a status bit, stops issuing, drains (bounded), frees TMEM and returns.
 #include <cuda.h>
@@ -61,6 +63,7 @@ enum Mode : int { kSwiGLU = 0, kDown = 1 };
 
 struct GemmParams {
   const int32_t* offsets;  // [E + 1] padded row offsets (multiples of BM)
+  const int32_t* counts;   // [E] routed rows of each expert, or null (every tile loads all 128 rows)
   int E;
   int K;                   // reduction length (multiple of BK)
   int n_tiles;             // output column tiles per expert
@@ -213,13 +216,14 @@ struct Shared {
   int abort;
   int item_start[kMaxExperts + 1];  // first work item of each expert (pair tiles x n-tiles)
   int row_off[kMaxExperts + 1];     // padded row offsets
+  int count[kMaxExperts];           // routed rows (counts, or the padded sizes)
 };
 constexpr uint32_t kSharedBytes = (sizeof(Shared) + 127) / 128 * 128;
 
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    GemmParams p) {
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a32,
+                    const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
   using Sh = Shape<PAIR>;
   constexpr int STAGES = Sh::STAGES, CTAS = Sh::CTAS, ROWS = Sh::ROWS;
   constexpr uint32_t STAGE_BYTES = Sh::STAGE_BYTES;
@@ -252,6 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     zb::fence_mbar_init();
   }
   for (int e = tid; e <= p.E; e += kThreads) sh->row_off[e] = p.offsets[e];
+  for (int e = tid; e < p.E; e += kThreads)
+    sh->count[e] = p.counts ? p.counts[e] : p.offsets[e + 1] - p.offsets[e];
   __syncthreads();
   if (tid == 0) {  // work items per expert: ceil(128-row tiles / CTAS) tiles x n-tiles
     int acc = 0;
@@ -297,6 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = row0 + (int)rank * BM;
         const int b_row = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step + (rank ? p.b_second_offset : 0);
         const int b_row2 = b_row + p.b_second_offset;  // the second B box (one CTA only)
+        // single CTA: 32-row A boxes covering the tile's routed rows (>= 1 for every tile of a segment)
+        const int a_boxes = PAIR ? 4 : (min(max(sh->count[e] - (row0 - sh->row_off[e]), 0), BM) + 31) / 32;
+        const uint32_t tx_bytes = CTAS * STAGE_BYTES - (uint32_t)(4 - a_boxes) * (A_BYTES / 4);
         for (int kb = 0; kb < k_blocks; ++kb, ++q) {
           const int s = q % STAGES;
           const uint32_t parity = ((q / STAGES) & 1) ^ 1;
@@ -305,10 +314,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t full_local = zb::smem_addr(&sh->full[s]);
-          if (leader) zb::mbar_arrive_expect_tx(full_local, CTAS * STAGE_BYTES);
+          if (leader) zb::mbar_arrive_expect_tx(full_local, tx_bytes);
           const uint32_t full_leader = PAIR ? zb::mapa_shared(full_local, 0) : full_local;
           const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
-          tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+          if (a_boxes == 4) {
+            tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+          } else {
+            for (int j = 0; j < a_boxes; ++j)
+              tma_load_2d<PAIR>(a_dst + j * (A_BYTES / 4), &tmap_a32, kb * BK, a_row + 32 * j, full_leader);
+          }
           tma_load_2d<PAIR>(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
           if (!PAIR) tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, &tmap_b, kb * BK, b_row2, full_leader);
         }
@@ -467,13 +481,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 row-major [rows, cols] tensor map with a [128 rows x 64 cols] box and 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems) {
+// 2-D bf16 row-major [rows, cols] tensor map with a [box_rows x 64 cols] box and 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+             uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return zb::fail(zb::kCudaError, "moe_gemm: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
-  cuuint32_t box[2] = {BK, 128};
+  cuuint32_t box[2] = {BK, box_rows};
   cuuint32_t estride[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estride,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -495,8 +510,8 @@ bool use_pair(int64_t capacity, int E) {
 }
 
 template <int MODE, bool PAIR>
-int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int64_t capacity,
-           cudaStream_t stream) {
+int launch(const CUtensorMap& a, const CUtensorMap& a32, const CUtensorMap& b, const GemmParams& p,
+           int64_t capacity, cudaStream_t stream) {
   auto kernel = moe_gemm_kernel<MODE, PAIR>;
   constexpr size_t kSmemBytes = smem_bytes<PAIR>();
   static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
@@ -545,7 +560,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int6
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, b, p));
+  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, a32, b, p));
   return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
 }
 
@@ -561,36 +576,38 @@ int check_common(const void* a, const int32_t* offsets, int E, int64_t capacity)
 }  // namespace
 
 ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, int E, int D, int I,
-                              const int32_t* offsets, uint16_t* h, cudaStream_t stream) {
+                              const int32_t* offsets, const int32_t* counts, uint16_t* h, cudaStream_t stream) {
   if (int rc = check_common(x_perm, offsets, E, capacity)) return rc;
   ZB_REQUIRE(gate_up && h, "moe_gemm_swiglu: null pointer");
   if (D % BK != 0 || I % 128 != 0)
     return zb::fail(zb::kUnsupported, "moe_gemm_swiglu: D=%d must be a multiple of 64 and I=%d of 128", D, I);
   ZB_REQUIRE_ALIGNED(gate_up, 16, "gate_up");
   ZB_REQUIRE_ALIGNED(h, 16, "h");
-  CUtensorMap ma, mb;
+  CUtensorMap ma, ma32, mb;
   if (int rc = make_map(&ma, x_perm, capacity, D, D)) return rc;
+  if (int rc = make_map(&ma32, x_perm, capacity, D, D, 32)) return rc;
   if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
-  GemmParams p{offsets, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I, nullptr,
-               nullptr, zb::device_status_ptr()};
-  return use_pair(capacity, E) ? launch<kSwiGLU, true>(ma, mb, p, capacity, stream)
-                                : launch<kSwiGLU, false>(ma, mb, p, capacity, stream);
+  GemmParams p{offsets, counts, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I,
+               nullptr, nullptr, zb::device_status_ptr()};
+  return use_pair(capacity, E) ? launch<kSwiGLU, true>(ma, ma32, mb, p, capacity, stream)
+                                : launch<kSwiGLU, false>(ma, ma32, mb, p, capacity, stream);
 }
 
 ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                            const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
-                            cudaStream_t stream) {
+                            const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                            const float* weights, uint16_t* y, cudaStream_t stream) {
   if (int rc = check_common(h, offsets, E, capacity)) return rc;
   ZB_REQUIRE(down && sorted_pairs && weights && y, "moe_gemm_down: null pointer");
   if (I % BK != 0 || D % 128 != 0)
     return zb::fail(zb::kUnsupported, "moe_gemm_down: I=%d must be a multiple of 64 and D=%d of 128", I, D);
   ZB_REQUIRE_ALIGNED(down, 16, "down");
   ZB_REQUIRE_ALIGNED(y, 16, "y");
-  CUtensorMap ma, mb;
+  CUtensorMap ma, ma32, mb;
   if (int rc = make_map(&ma, h, capacity, I, I)) return rc;
+  if (int rc = make_map(&ma32, h, capacity, I, I, 32)) return rc;
   if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
-  GemmParams p{offsets, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D, D,
-               sorted_pairs, weights, zb::device_status_ptr()};
-  return use_pair(capacity, E) ? launch<kDown, true>(ma, mb, p, capacity, stream)
-                                : launch<kDown, false>(ma, mb, p, capacity, stream);
+  GemmParams p{offsets, counts, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D,
+               D, sorted_pairs, weights, zb::device_status_ptr()};
+  return use_pair(capacity, E) ? launch<kDown, true>(ma, ma32, mb, p, capacity, stream)
+                                : launch<kDown, false>(ma, ma32, mb, p, capacity, stream);
 }

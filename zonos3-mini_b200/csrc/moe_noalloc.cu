@@ -19,8 +19,8 @@
 #include "common.cuh"
 
 ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                            const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, uint16_t* y,
-                            cudaStream_t stream);
+                            const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                            const float* weights, uint16_t* y, cudaStream_t stream);
 ZB_API int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_t out_stride,
                           cudaStream_t stream);
 
@@ -69,7 +69,8 @@ ZB_API int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, cons
   uint16_t* scratch = nullptr;
   if (int rc = scratch_address(&scratch)) return rc;
   ZB_CUDA(cudaMemsetAsync(scratch, 0, (size_t)elems * sizeof(uint16_t), stream));
-  if (int rc = zb_moe_gemm_down(h, capacity, down, E, D, I, offsets, sorted_pairs, weights, scratch, stream))
+  if (int rc = zb_moe_gemm_down(h, capacity, down, E, D, I, offsets, nullptr, sorted_pairs, weights, scratch,
+                                stream))
     return rc;
   return zb_moe_combine(scratch, T, k, D, out, out_stride, stream);
 }

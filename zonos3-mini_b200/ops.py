@@ -378,8 +378,9 @@ def moe_gather(x, sorted_pairs, top_k, out):
     return out
 
 
-def moe_gemm_swiglu(x_perm, gate_up, offsets, out):
-    """H = SwiGLU(x_perm @ gate_up[e].T) per expert segment (tcgen05 grouped GEMM, gate rows first)."""
+def moe_gemm_swiglu(x_perm, gate_up, offsets, out, counts=None):
+    """H = SwiGLU(x_perm @ gate_up[e].T) per expert segment (tcgen05 grouped GEMM, gate rows first). ``counts``
+    (the permutation's routed rows per expert) lets decode-sized batches skip the padding rows' loads."""
     dev = x_perm.device
     E, two_i, D = gate_up.shape
     for name, t in (("x_perm", x_perm), ("gate_up", gate_up), ("out", out)):
@@ -387,12 +388,13 @@ def moe_gemm_swiglu(x_perm, gate_up, offsets, out):
         _require(t.is_contiguous(), f"{name} must be contiguous")
     _require(x_perm.shape[1] == D and out.shape == (x_perm.shape[0], two_i // 2), "shape mismatch")
     _lib.call("zb_moe_gemm_swiglu", x_perm.data_ptr(), x_perm.shape[0], gate_up.data_ptr(), E, D, two_i // 2,
-              offsets.data_ptr(), out.data_ptr(), _stream(dev))
+              offsets.data_ptr(), None if counts is None else counts.data_ptr(), out.data_ptr(), _stream(dev))
     return out
 
 
-def moe_gemm_down(h, down, offsets, sorted_pairs, topk_weights, out):
-    """Y[pair] = (H[r] @ down[e].T) * weight[pair] for every non-padding row r (tcgen05 grouped GEMM)."""
+def moe_gemm_down(h, down, offsets, sorted_pairs, topk_weights, out, counts=None):
+    """Y[pair] = (H[r] @ down[e].T) * weight[pair] for every non-padding row r (tcgen05 grouped GEMM); ``counts``
+    as for :func:`moe_gemm_swiglu`."""
     dev = h.device
     E, D, I = down.shape
     for name, t in (("h", h), ("down", down), ("out", out)):
@@ -401,7 +403,8 @@ def moe_gemm_down(h, down, offsets, sorted_pairs, topk_weights, out):
     _check_cuda("topk_weights", topk_weights, torch.float32, dev)
     _require(h.shape[1] == I and out.shape == (topk_weights.numel(), D), "shape mismatch")
     _lib.call("zb_moe_gemm_down", h.data_ptr(), h.shape[0], down.data_ptr(), E, D, I, offsets.data_ptr(),
-              sorted_pairs.data_ptr(), topk_weights.data_ptr(), out.data_ptr(), _stream(dev))
+              None if counts is None else counts.data_ptr(), sorted_pairs.data_ptr(), topk_weights.data_ptr(),
+              out.data_ptr(), _stream(dev))
     return out
 
 
@@ -458,8 +461,8 @@ def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, ou
     ws = workspace
     perm = moe_permute(ids, E, capacity=ws.capacity, out=ws.perm)
     moe_gather(x, perm["sorted_pairs"], k, ws.x_perm)
-    moe_gemm_swiglu(ws.x_perm, gate_up, perm["offsets"], ws.h)
-    moe_gemm_down(ws.h, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.y)
+    moe_gemm_swiglu(ws.x_perm, gate_up, perm["offsets"], ws.h, counts=perm["counts"])
+    moe_gemm_down(ws.h, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.y, counts=perm["counts"])
     if out is None:
         out = torch.empty((T, D), device=x.device, dtype=torch.bfloat16)
     return moe_combine(ws.y, k, out)
