@@ -127,6 +127,7 @@ __device__ __forceinline__ void publish(float v, float* buf, uint64_t* bar, int 
 
 template <int C>
 __global__ void __launch_bounds__(kRouteThreads) attnres_route_kernel(RouteParams p) {
+  zb::pdl_enter();
   constexpr int kWarps = kRouteWarps;
   constexpr int kLaneVecs = C / 256;   // 16-byte vectors of a lane in the per-source sweeps
   // columns of a thread in the mix: 4 (C = 1024) or 2; with C = 256 only the first 128 threads mix
@@ -370,19 +371,7 @@ int launch(const RouteParams& p, cudaStream_t stream) {
   auto kernel = attnres_route_kernel<C>;
   if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int CL = p.D / C;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.T * CL));
-  cfg.blockDim = dim3(kRouteThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CL;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)(p.T * CL)), dim3(kRouteThreads), smem, stream, (unsigned)CL, p));
   return zb::check_launch("attnres_route");
 }
 
@@ -486,6 +475,7 @@ __device__ __forceinline__ void keys8(const uint4& x, uint64_t inv2, uint32_t (&
 
 template <int U, int kMaxThreads, int kMinBlocks>
 __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel(TabledParams p) {
+  zb::pdl_enter();
   static_assert(U == 16, "a round of U sources is one 16-wide transposed warp sum");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   static_assert(kMaxThreads >= 128, "the inverse-RMS registers cover 256 sources with >= 128 threads");
@@ -695,7 +685,7 @@ int launch_tabled(const TabledParams& p, cudaStream_t stream) {
   const size_t smem = TabledLayout(p.D / 256, p.S + 1).total;
   auto kernel = attnres_tabled_kernel<U, kMaxThreads, kMinBlocks>;
   if (smem > 48 * 1024) ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kernel<<<(unsigned)p.T, p.D / 8, smem, stream>>>(p);
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)p.T), dim3(p.D / 8), smem, stream, 1, p));
   return zb::check_launch("attnres_route_tabled");
 }
 

@@ -9,6 +9,8 @@
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <utility>
 #include <stdint.h>
 
 // Exported C-ABI symbol (the library builds with -fvisibility=hidden).
@@ -208,6 +210,17 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                : "memory");
 }
 
+// Programmatic dependent launch. Every kernel of the library is launched with zb::launch(), which lets it start
+// while the kernel before it in the stream is still running; its first statement is pdl_enter(): wait until that
+// kernel has completed and its writes are visible (griddepcontrol.wait; a no-op for a plain launch), then let the
+// next kernel start (griddepcontrol.launch_dependents). Nothing a kernel reads or writes in global memory is touched
+// before the wait, so the stream order of the memory effects is unchanged; what overlaps the previous kernel's tail
+// is the next kernel's launch and CTA setup.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -218,6 +231,33 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
   return v;
+}
+
+// Launches `kernel` on `stream` with programmatic stream serialisation allowed (see pdl_enter) and, when
+// cluster_x > 1, clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace zb

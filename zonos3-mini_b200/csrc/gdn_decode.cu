@@ -37,6 +37,7 @@ struct DecodeParams {
 
 template <int DK>
 __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(DecodeParams p) {
+  zb::pdl_enter();
   constexpr int LPR = DK / 16;                // lanes per value row
   constexpr int ROWS_PER_CTA = kThreads / LPR;
   const int lane = threadIdx.x % LPR;
@@ -128,10 +129,10 @@ ZB_API int zb_gdn_decode_step(const uint16_t* q, const uint16_t* k, const uint16
   const int64_t rows = (int64_t)B * H * dv;
   if (dk == 128) {
     const int64_t grid = (rows + (kThreads / 8) - 1) / (kThreads / 8);
-    gdn_decode_kernel<128><<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    ZB_CUDA(zb::launch(gdn_decode_kernel<128>, dim3((unsigned)grid), dim3(kThreads), 0, stream, 1, p));
   } else {
     const int64_t grid = (rows + (kThreads / 4) - 1) / (kThreads / 4);
-    gdn_decode_kernel<64><<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    ZB_CUDA(zb::launch(gdn_decode_kernel<64>, dim3((unsigned)grid), dim3(kThreads), 0, stream, 1, p));
   }
   return zb::check_launch("gdn_decode_step");
 }

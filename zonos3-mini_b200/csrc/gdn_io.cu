@@ -69,6 +69,7 @@ __device__ __forceinline__ void load_bf(const __nv_bfloat16* src, float (&out)[P
 // lane replaces its channels' history rows.
 template <int PL, bool kDecode>
 __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
+  zb::pdl_enter();
   const int64_t tok = blockIdx.x;
   const int part = blockIdx.y;
   const int h = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
 // New history of every sequence: its last W-1 conv inputs (shifted in after the old history when it is shorter).
 // Grid (sequence, channel block): a thread owns 8 consecutive channels (24 history entries, 48 contiguous bytes).
 __global__ void __launch_bounds__(256) gdn_conv_history_kernel(PrologueParams p) {
+  zb::pdl_enter();
   const int seq = blockIdx.x;
   const int64_t start = p.cu_seqlens[seq], len = p.cu_seqlens[seq + 1] - start;
   const int64_t slot = p.slots[seq];
@@ -239,24 +241,34 @@ struct EpilogueParams {
   int N, H, D;
 };
 
+// A warp per (token, head), PL = D / 32 consecutive channels per lane; o, z and the weight are all loaded (PL-wide
+// vectors) before the reduction.
+template <int PL>
 __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(EpilogueParams p) {
+  zb::pdl_enter();
   const int64_t unit = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;  // (token, head)
   const int lane = threadIdx.x % 32;
   if (unit >= (int64_t)p.N * p.H) return;
   const int64_t tok = unit / p.H;
   const int h = (int)(unit % p.H);
-  const int per_lane = p.D / 32;
-  float x[4], ss = 0.f;
-  for (int j = 0; j < per_lane; ++j) {
-    x[j] = __bfloat162float(p.o[unit * p.D + lane * per_lane + j]);
-    ss = fmaf(x[j], x[j], ss);
-  }
+  const int c = lane * PL;
+  float x[PL], zz[PL], w[PL];
+  load_bf<PL>(p.o + unit * p.D + c, x);
+  load_bf<PL>(p.z + tok * p.z_stride + h * p.D + c, zz);
+  load_bf<PL>(p.weight + c, w);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < PL; ++j) ss = fmaf(x[j], x[j], ss);
   const float r = rsqrtf(zb::warp_sum(ss) / (float)p.D + p.eps);
-  for (int j = 0; j < per_lane; ++j) {
-    const int c = lane * per_lane + j;
-    const float zz = __bfloat162float(p.z[tok * p.z_stride + h * p.D + c]);
-    const float w = __bfloat162float(p.weight[c]);
-    p.out[tok * (int64_t)p.H * p.D + h * p.D + c] = __float2bfloat16_rn(x[j] * r * w * silu(zz));
+  __nv_bfloat16* dst = p.out + tok * (int64_t)p.H * p.D + h * p.D + c;
+  if constexpr (PL == 4) {
+    const __nv_bfloat162 o0 = __floats2bfloat162_rn(x[0] * r * w[0] * silu(zz[0]), x[1] * r * w[1] * silu(zz[1]));
+    const __nv_bfloat162 o1 = __floats2bfloat162_rn(x[2] * r * w[2] * silu(zz[2]), x[3] * r * w[3] * silu(zz[3]));
+    *reinterpret_cast<uint2*>(dst) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&o0), *reinterpret_cast<const uint32_t*>(&o1));
+  } else {
+#pragma unroll
+    for (int j = 0; j < PL; ++j) dst[j] = __float2bfloat16_rn(x[j] * r * w[j] * silu(zz[j]));
   }
 }
 
@@ -290,15 +302,15 @@ ZB_API int zb_gdn_prologue(const uint16_t* mixed, int64_t mixed_stride, const ui
   const dim3 grid((unsigned)N, 3);
   const unsigned threads = 32u * (unsigned)H;
   switch (D / 32) {
-    case 1: gdn_prologue_kernel<1, false><<<grid, threads, 0, stream>>>(p); break;
-    case 2: gdn_prologue_kernel<2, false><<<grid, threads, 0, stream>>>(p); break;
-    case 4: gdn_prologue_kernel<4, false><<<grid, threads, 0, stream>>>(p); break;
+    case 1: ZB_CUDA(zb::launch(gdn_prologue_kernel<1, false>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
+    case 2: ZB_CUDA(zb::launch(gdn_prologue_kernel<2, false>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
+    case 4: ZB_CUDA(zb::launch(gdn_prologue_kernel<4, false>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
     default: return zb::fail(zb::kUnsupported, "gdn_prologue: head dim %d (32, 64 or 128)", D);
   }
   if (int rc = zb::check_launch("gdn_prologue")) return rc;
   const int channels = 3 * H * D;
   if (num_seqs > 0)
-    gdn_conv_history_kernel<<<dim3((unsigned)num_seqs, (unsigned)((channels / 8 + 255) / 256)), 256, 0, stream>>>(p);
+    ZB_CUDA(zb::launch(gdn_conv_history_kernel, dim3(dim3((unsigned)num_seqs, (unsigned)((channels / 8 + 255) / 256))), dim3(256), 0, stream, 1, p));
   return zb::check_launch("gdn_prologue(history)");
 }
 
@@ -327,9 +339,9 @@ ZB_API int zb_gdn_prologue_decode(const uint16_t* mixed, int64_t mixed_stride, c
   const dim3 grid((unsigned)N, 3);
   const unsigned threads = 32u * (unsigned)H;
   switch (D / 32) {
-    case 1: gdn_prologue_kernel<1, true><<<grid, threads, 0, stream>>>(p); break;
-    case 2: gdn_prologue_kernel<2, true><<<grid, threads, 0, stream>>>(p); break;
-    case 4: gdn_prologue_kernel<4, true><<<grid, threads, 0, stream>>>(p); break;
+    case 1: ZB_CUDA(zb::launch(gdn_prologue_kernel<1, true>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
+    case 2: ZB_CUDA(zb::launch(gdn_prologue_kernel<2, true>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
+    case 4: ZB_CUDA(zb::launch(gdn_prologue_kernel<4, true>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
     default: return zb::fail(zb::kUnsupported, "gdn_prologue_decode: head dim %d (32, 64 or 128)", D);
   }
   return zb::check_launch("gdn_prologue_decode");
@@ -345,7 +357,18 @@ ZB_API int zb_gdn_gated_norm(const uint16_t* o, const uint16_t* z, int64_t z_str
   EpilogueParams p{reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(z), z_stride,
                    reinterpret_cast<const __nv_bfloat16*>(weight), eps, reinterpret_cast<__nv_bfloat16*>(out), N, H,
                    D};
+  const int pl = D / 32;  // channels per lane, loaded as one vector of pl bf16
+  ZB_REQUIRE(z_stride % pl == 0, "gdn_gated_norm: z_stride %lld must be a multiple of %d", (long long)z_stride, pl);
+  for (const void* ptr : {(const void*)o, (const void*)z, (const void*)weight, (const void*)out}) {
+    ZB_REQUIRE_ALIGNED(ptr, 2 * pl, "gdn_gated_norm tensors");
+  }
   const int64_t units = (int64_t)N * H;
-  gdn_gated_norm_kernel<<<(unsigned)((units + 7) / 8), 256, 0, stream>>>(p);
+  const dim3 grid((unsigned)((units + 7) / 8));
+  switch (pl) {
+    case 1: ZB_CUDA(zb::launch(gdn_gated_norm_kernel<1>, grid, dim3(256), 0, stream, 1, p)); break;
+    case 2: ZB_CUDA(zb::launch(gdn_gated_norm_kernel<2>, grid, dim3(256), 0, stream, 1, p)); break;
+    case 4: ZB_CUDA(zb::launch(gdn_gated_norm_kernel<4>, grid, dim3(256), 0, stream, 1, p)); break;
+    default: return zb::fail(zb::kUnsupported, "gdn_gated_norm: head dim %d (32, 64 or 128)", D);
+  }
   return zb::check_launch("gdn_gated_norm");
 }

@@ -90,6 +90,7 @@ struct Smem {
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_prefill_kernel(PrefillParams p) {
+  zb::pdl_enter();
   using SM = Smem<D>;
   constexpr int LB = SM::LB, LC = SM::LC, LY = SM::LY;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -514,6 +515,6 @@ ZB_API int zb_gdn_chunk_prefill(const uint16_t* q, const uint16_t* k, const uint
   const size_t smem = sizeof(Smem<64>);
   ZB_CUDA(cudaFuncSetAttribute(gdn_chunk_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
-  gdn_chunk_prefill_kernel<64><<<dim3((unsigned)num_seqs, (unsigned)H), kThreads, smem, stream>>>(p);
+  ZB_CUDA(zb::launch(gdn_chunk_prefill_kernel<64>, dim3(dim3((unsigned)num_seqs, (unsigned)H)), dim3(kThreads), smem, stream, 1, p));
   return zb::check_launch("gdn_chunk_prefill");
 }

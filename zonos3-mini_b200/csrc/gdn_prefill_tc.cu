@@ -308,6 +308,7 @@ __device__ __forceinline__ void decay_epilogue(bool is_a, int t, const uint32_t 
 }
 
 __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepParams p) {
+  zb::pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = zb::smem_addr(smem_raw);
   const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
@@ -506,6 +507,7 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_prefill_prep_kernel(PrepPara
 }
 
 __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_state_kernel(StateParams p) {
+  zb::pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = zb::smem_addr(smem_raw);
   const uint32_t pad = (1024 - (raw_addr & 1023)) & 1023;
@@ -888,7 +890,7 @@ int gdn_prefill_tc_launch(const uint16_t* q, const uint16_t* k, const uint16_t* 
                   cu_seqlens, num_seqs, H, scale, static_cast<unsigned char*>(workspace), status};
     ZB_CUDA(cudaFuncSetAttribute(gdn_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPrepSmem));
-    gdn_prefill_prep_kernel<<<dim3((unsigned)ids, (unsigned)H), kPrepThreads, kPrepSmem, stream>>>(pp);
+    ZB_CUDA(zb::launch(gdn_prefill_prep_kernel, dim3(dim3((unsigned)ids, (unsigned)H)), dim3(kPrepThreads), kPrepSmem, stream, 1, pp));
     if (int rc = check_launch("gdn_chunk_prefill (prep)")) return rc;
   }
   StateParams sp{reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
@@ -896,7 +898,7 @@ int gdn_prefill_tc_launch(const uint16_t* q, const uint16_t* k, const uint16_t* 
                  reinterpret_cast<__nv_bfloat16*>(out), static_cast<const unsigned char*>(workspace), H, scale, status};
   ZB_CUDA(cudaFuncSetAttribute(gdn_prefill_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)kSmemBytes));
-  gdn_prefill_state_kernel<<<dim3((unsigned)num_seqs, (unsigned)H), kThreads, kSmemBytes, stream>>>(sp);
+  ZB_CUDA(zb::launch(gdn_prefill_state_kernel, dim3(dim3((unsigned)num_seqs, (unsigned)H)), dim3(kThreads), kSmemBytes, stream, 1, sp));
   return check_launch("gdn_chunk_prefill (state)");
 }
 

@@ -224,6 +224,7 @@ template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a32,
                     const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
+  zb::pdl_enter();
   using Sh = Shape<PAIR>;
   constexpr int STAGES = Sh::STAGES, CTAS = Sh::CTAS, ROWS = Sh::ROWS;
   constexpr uint32_t STAGE_BYTES = Sh::STAGE_BYTES;
@@ -553,14 +554,8 @@ int launch(const CUtensorMap& a, const CUtensorMap& a32, const CUtensorMap& b, c
   const int64_t upper_items = (capacity / Shape<PAIR>::ROWS + p.E) * p.n_tiles;
   const int units = (int)std::min<int64_t>(upper_items, max_units);
   if (units <= 0) return zb::kOk;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(Shape<PAIR>::CTAS * units));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, a, a32, b, p));
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)(Shape<PAIR>::CTAS * units)), dim3(kThreads), kSmemBytes, stream,
+                     (unsigned)Shape<PAIR>::CTAS, a, a32, b, p));
   return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
 }
 

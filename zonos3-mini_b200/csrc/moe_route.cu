@@ -326,6 +326,7 @@ size_t router_smem(int TOK, int NE, int D) {
 // the top-k of TOK / 8 tokens at once.
 template <int NH, int TOK>
 __global__ void __launch_bounds__(kRouterThreads) moe_router_kernel(RouterParams p) {
+  zb::pdl_enter();
   constexpr int NE = 32 * NH;           // experts covered by the CTA
   constexpr int MT = TOK / 16;          // token tiles
   constexpr int NG = 8 / MT;            // expert groups
@@ -466,7 +467,7 @@ int launch_router(const RouterParams& p, cudaStream_t stream) {
   auto kernel = moe_router_kernel<NH, TOK>;
   ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const unsigned grid = (unsigned)((p.T + TOK - 1) / TOK);
-  kernel<<<grid, kRouterThreads, smem, stream>>>(p);
+  ZB_CUDA(zb::launch(kernel, dim3(grid), dim3(kRouterThreads), smem, stream, 1, p));
   return zb::check_launch("moe_router");
 }
 
@@ -495,6 +496,7 @@ size_t router_split_smem(int NE, int DS) {
 
 template <int NH>
 __global__ void __launch_bounds__(kRouterThreads) moe_router_split_kernel(RouterParams p) {
+  zb::pdl_enter();
   constexpr int NE = 32 * NH;
   constexpr int TOK = kSplitTok;
   constexpr int MT = TOK / 16, NG = 8 / MT, NPW = NE / 8 / NG > 0 ? NE / 8 / NG : 1;
@@ -621,19 +623,8 @@ int launch_router_split(const RouterParams& p, cudaStream_t stream) {
   const size_t smem = router_split_smem(32 * NH, p.D / kSplit);
   auto kernel = moe_router_split_kernel<NH>;
   ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(((p.T + kSplitTok - 1) / kSplitTok) * kSplit));
-  cfg.blockDim = dim3(kRouterThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kSplit;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ZB_CUDA(cudaLaunchKernelEx(&cfg, kernel, p));
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)(((p.T + kSplitTok - 1) / kSplitTok) * kSplit)), dim3(kRouterThreads),
+                     smem, stream, (unsigned)kSplit, p));
   return zb::check_launch("moe_router(split)");
 }
 
@@ -647,6 +638,7 @@ struct SelectParams {
 };
 
 __global__ void __launch_bounds__(256) moe_select_kernel(SelectParams p) {
+  zb::pdl_enter();
   const int t = blockIdx.x * 8 + threadIdx.x / 32;
   if (t >= p.T) return;
   const int64_t base = (int64_t)t * p.E;
@@ -679,6 +671,7 @@ struct PermuteParams {
 
 // Pass 1: the expert histogram of each 256-pair slice (order-free shared-memory atomics).
 __global__ void __launch_bounds__(kPermThreads) moe_count_kernel(PermuteParams p) {
+  zb::pdl_enter();
   __shared__ int32_t h[kMaxExperts];
   for (int e = threadIdx.x; e < p.E; e += kPermThreads) h[e] = 0;
   __syncthreads();
@@ -696,6 +689,7 @@ __global__ void __launch_bounds__(kPermThreads) moe_count_kernel(PermuteParams p
 // slice, ranks among equal experts inside the warp come from match.any, and the per-(warp, expert) counts are
 // scanned across the warps. Pairs of one expert therefore keep ascending p (stable), with no atomics on order.
 __global__ void __launch_bounds__(kPermThreads) moe_scatter_kernel(PermuteParams p) {
+  zb::pdl_enter();
   __shared__ int32_t base[kMaxExperts];      // write cursor of this slice per expert
   __shared__ int32_t seg[kMaxExperts + 1];   // padded segment starts
   __shared__ int32_t total[kMaxExperts];
@@ -801,6 +795,7 @@ struct GatherParams {
 // an output (at decode most of the padded capacity is padding). A warp copies whole rows: the row's pair index is
 // read once, then every lane keeps 8 independent 16-byte loads in flight.
 __global__ void __launch_bounds__(256) moe_gather_kernel(GatherParams p) {
+  zb::pdl_enter();
   const int lane = threadIdx.x % 32;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int vec_per_row = p.D / 8;
@@ -834,13 +829,19 @@ struct CombineParams {
 // out[t] = bf16( sum over slots of float(y[t * k + slot]) ), slots in order (the server's moe_sum_reduce). A warp
 // sums whole token rows: every lane keeps the 16-byte vectors of 2 columns x up to 8 slots in flight.
 __global__ void __launch_bounds__(256) moe_combine_kernel(CombineParams p) {
+  zb::pdl_enter();
   const int lane = threadIdx.x % 32;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int vec_per_row = p.D / 8;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < p.T; t += warps) {
+  const int chunks = (vec_per_row + 63) / 64;  // 512-column pieces of a row: the warps' units
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; u < (int64_t)p.T * chunks;
+       u += warps) {
+    const int64_t t = u / chunks;
     const uint4* rows = reinterpret_cast<const uint4*>(p.y + t * p.k * p.D);
     uint4* dst = reinterpret_cast<uint4*>(p.out + t * p.out_stride);
-    for (int c0 = lane; c0 < vec_per_row; c0 += 64) {
+    {
+      const int c0 = (int)(u % chunks) * 64 + lane;
+      if (c0 >= vec_per_row) continue;
       const bool has1 = c0 + 32 < vec_per_row;
       float acc0[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, acc1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int s0 = 0; s0 < p.k; s0 += 8) {
@@ -885,8 +886,9 @@ ZB_API int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out,
   ZB_REQUIRE_ALIGNED(out, 16, "out");
   CombineParams p{reinterpret_cast<const __nv_bfloat16*>(y), T, k, D, reinterpret_cast<__nv_bfloat16*>(out),
                   out_stride};
-  const int64_t grid = std::min<int64_t>(((int64_t)T + 7) / 8, (int64_t)zb::sm_count() * 8);  // a warp per token
-  moe_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
+  const int64_t units = (int64_t)T * ((D / 8 + 63) / 64);  // a warp per 512-column piece of a token's row
+  const int64_t grid = std::min<int64_t>((units + 7) / 8, (int64_t)zb::sm_count() * 8);
+  ZB_CUDA(zb::launch(moe_combine_kernel, dim3((unsigned)grid), dim3(256), 0, stream, 1, p));
   return zb::check_launch("moe_combine");
 }
 
@@ -932,7 +934,7 @@ ZB_API int zb_moe_select(const void* logits, int logits_bf16, const float* bias,
   if (T == 0) return zb::kOk;
   ZB_REQUIRE(logits && ids && weights, "moe_select: null pointer");
   SelectParams p{logits, logits_bf16, bias, T, E, k, weight_mode, renormalize, ids, weights};
-  moe_select_kernel<<<(unsigned)((T + 7) / 8), 256, 0, stream>>>(p);
+  ZB_CUDA(zb::launch(moe_select_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, stream, 1, p));
   return zb::check_launch("moe_select");
 }
 
@@ -948,9 +950,9 @@ ZB_API int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, in
   ZB_REQUIRE(hist && counts && offsets && sorted_pairs && position && (P == 0 || ids), "moe_permute: null pointer");
   PermuteParams p{ids, (int)P, E, block, capacity, hist, counts, offsets, sorted_pairs, position};
   const unsigned slices = (unsigned)std::max<int64_t>(1, (P + kPermPairs - 1) / kPermPairs);
-  moe_count_kernel<<<slices, kPermThreads, 0, stream>>>(p);
+  ZB_CUDA(zb::launch(moe_count_kernel, dim3(slices), dim3(kPermThreads), 0, stream, 1, p));
   if (int rc = zb::check_launch("moe_permute(count)")) return rc;
-  moe_scatter_kernel<<<slices, kPermThreads, 0, stream>>>(p);
+  ZB_CUDA(zb::launch(moe_scatter_kernel, dim3(slices), dim3(kPermThreads), 0, stream, 1, p));
   return zb::check_launch("moe_permute(scatter)");
 }
 
@@ -966,6 +968,6 @@ ZB_API int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sor
   GatherParams p{reinterpret_cast<const __nv_bfloat16*>(x), x_stride, sorted_pairs, k, rows, D,
                  reinterpret_cast<__nv_bfloat16*>(out)};
   const int64_t grid = std::min<int64_t>((rows + 7) / 8, (int64_t)zb::sm_count() * 8);  // a warp per row
-  moe_gather_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
+  ZB_CUDA(zb::launch(moe_gather_kernel, dim3((unsigned)grid), dim3(256), 0, stream, 1, p));
   return zb::check_launch("moe_gather");
 }
