@@ -494,26 +494,25 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel
   uint2* wp = reinterpret_cast<uint2*>(smem_raw + lay.wp) + (size_t)warp * ns;
   uint4* stash = reinterpret_cast<uint4*>(smem_raw + lay.stash);
 
-  // every load that depends on nothing, issued first: the first U bank sources, the current source, this and the
-  // next route's query slices, the norm weight slice, the route's table row and the bank rows' inverse RMS
-  const __nv_bfloat16* bank_t = p.bank + t * D + c;
-  uint4 buf[U];
-#pragma unroll
-  for (int i = 0; i < U; ++i)
-    if (i < S) buf[i] = ld_nc_u4(bank_t + (int64_t)i * p.bank_stride);
-  uint4 cur = *reinterpret_cast<const uint4*>(p.source + t * D + c);
+  // every load that depends on nothing, issued first, in the order they are needed: the current source, this and
+  // the next route's query slices, the route's table row and the bank rows' inverse RMS (the critical path until the
+  // softmax), the norm weight slice (cp.async into shared memory: no register waits for it), and only then the first
+  // U bank sources, whose 16 MB over all CTAs would otherwise queue ahead of the current source's row
+  uint4 cur = ld_nc_u4(p.source + t * D + c);
   const __nv_bfloat16* q_c = p.queries + (int64_t)p.route * D + c;
-  const uint4 q_route = *reinterpret_cast<const uint4*>(q_c);
+  const uint4 q_route = ld_nc_u4(q_c);
   uint4 q_next = make_uint4(0u, 0u, 0u, 0u);
-  if (ahead) q_next = *reinterpret_cast<const uint4*>(q_c + D);
-  if (p.norm_weight) stash[blockDim.x + tid] = *reinterpret_cast<const uint4*>(p.norm_weight + c);
+  if (ahead) q_next = ld_nc_u4(q_c + D);
   constexpr int kPerLane = kMaxSources / 32;
   const float* trow = p.table + ((int64_t)p.route * p.T + t) * p.table_stride;
+  // lane-strided slots that hold a source (the same for every lane): the softmax works on these only
+  const int slots = (S + 1 + 31) / 32;
   float lv[kPerLane];
 #pragma unroll
   for (int i = 0; i < kPerLane; ++i) {
     const int s = lane + 32 * i;
-    lv[i] = s < S ? trow[s] : -INFINITY;
+    lv[i] = -INFINITY;
+    if (i < slots && s < S) lv[i] = trow[s];
   }
   // the bank rows' inverse RMS (for the look-ahead keys): loaded now, stored to shared memory once the logit work
   // has hidden the load
@@ -524,6 +523,18 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel
     const int s = tid + j * blockDim.x;
     inv_reg[j] = ahead && s < S ? p.inv_rms[t * p.inv_stride + s] : 0.f;
   }
+  if (p.norm_weight) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n cp.async.commit_group;" ::"r"(
+                     zb::smem_addr(&stash[blockDim.x + tid])),
+                 "l"(p.norm_weight + c)
+                 : "memory");
+  }
+  asm volatile("" ::: "memory");  // keep the loads above ahead of the bank prefetch
+  const __nv_bfloat16* bank_t = p.bank + t * D + c;
+  uint4 buf[U];
+#pragma unroll
+  for (int i = 0; i < U; ++i)
+    if (i < S) buf[i] = ld_nc_u4(bank_t + (int64_t)i * p.bank_stride);
 
   // inverse RMS of the current source (kept for the later routes when it becomes bank row S)
   const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
@@ -563,21 +574,25 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel
   float m = -INFINITY;
 #pragma unroll
   for (int i = 0; i < kPerLane; ++i) {
-    if (lane + 32 * i == S) lv[i] = lg_cur;
-    m = fmaxf(m, lv[i]);
+    if (i < slots) {
+      if (lane + 32 * i == S) lv[i] = lg_cur;
+      m = fmaxf(m, lv[i]);
+    }
   }
   m = zb::warp_max(m);
   float den = 0.f;
 #pragma unroll
   for (int i = 0; i < kPerLane; ++i) {
-    lv[i] = lane + 32 * i < ns ? expf(lv[i] - m) : 0.f;
-    den += lv[i];
+    if (i < slots) {
+      lv[i] = lane + 32 * i < ns ? expf(lv[i] - m) : 0.f;
+      den += lv[i];
+    }
   }
   den = zb::warp_sum(den);
 #pragma unroll
   for (int i = 0; i < kPerLane; ++i) {
     const int s = lane + 32 * i;
-    if (s < ns)
+    if (i < slots && s < ns)
       wp[s] = make_uint2((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lv[i] / den)) * 0x10001u,
                          __float_as_uint(s < S ? inv_s[s] : 0.f));
   }
@@ -652,6 +667,7 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) attnres_tabled_kernel
     float total = 0.f;
     for (int i = 0; i < nwarps; ++i) total += red_nrm[i];
     const float rn = rsqrtf(total * (1.0f / (float)D) + p.norm_eps);
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's norm weight slice (its own copy)
     const uint4 nw = stash[blockDim.x + tid];
     const uint32_t nww[4] = {nw.x, nw.y, nw.z, nw.w};
     float y[8];
