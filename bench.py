@@ -525,6 +525,48 @@ def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5)
     }
 
 
+def gqa_cfg5_inputs(dev, streams=256, prompt=128, context=1628, Hq=16, Hkv=4, hd=128, seed=5):
+    """cfg5 global-attention decode at the end of the run: `streams` requests, each with `context` cached keys
+    (the 128-token prompt, then 1500 decode steps). Slots as a token pool hands them out: each prompt a contiguous
+    block, then every decode step one slot per request (so a request's decode keys sit `streams` slots apart).
+    K/V N(0,1) bf16; q N(0,1) bf16."""
+    gen = torch.Generator().manual_seed(seed)
+    slots = streams * context
+    b = torch.arange(streams, dtype=torch.int64)[:, None]
+    pos = torch.arange(context, dtype=torch.int64)[None, :]
+    table = torch.where(pos < prompt, b * prompt + pos, streams * prompt + (pos - prompt) * streams + b)
+    k_cache = torch.randn(slots, Hkv, hd, generator=gen).bfloat16().to(dev)
+    v_cache = torch.randn(slots, Hkv, hd, generator=gen).bfloat16().to(dev)
+    q = torch.randn(streams, Hq, hd, generator=gen).bfloat16().to(dev)
+    seq = torch.full((streams,), context, dtype=torch.int32, device=dev)
+    return q, k_cache, v_cache, table.to(torch.int32).to(dev), seq
+
+
+def bench_gqa_decode_cfg5(ops, dev, stream, reps=5):
+    """cfg5 GQA decode attention (16 q / 4 kv heads at 128) for 256 streams at 1628 cached keys: 853 MB of K/V per
+    call, above L2, so replays need no flush. Unsplit (the reference's setting for this model) and with the
+    automatic split."""
+    streams, context, Hq, Hkv, hd = 256, 1628, 16, 4, 128
+    q, kc, vc, table, seq = gqa_cfg5_inputs(dev, streams, 128, context, Hq, Hkv, hd)
+    out = torch.empty_like(q)
+    nbytes = streams * context * Hkv * hd * 2 * 2 + table.numel() * 4 + 2 * q.numel() * 2
+    pk = peaks()
+    res = {"workload": f"cfg5 GQA decode attention: {streams} streams x {context} cached keys, {Hq} q / {Hkv} kv "
+                       f"heads at {hd}; slot-indexed cache (prompt blocks, then interleaved decode slots)",
+           "algorithmic_bytes": nbytes}
+    for name, splits in (("unsplit", 1), ("auto", 0), ("split2", 2)):
+        s, _ = ops.gqa_splits(streams, Hkv, context, splits, hd)
+        ws = torch.empty(streams * Hq * s * (hd + 2), device=dev, dtype=torch.float32)
+        ms = graph_ms(lambda: ops.gqa_decode(q, kc, vc, table, seq, num_splits=splits, out=out, workspace=ws),
+                      stream, reps)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"splits": s, "us": ms * 1e3, "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"]}
+    res["roofline"] = {"kernel": "gqa_decode_kernel", "bound": "hbm", "achieved": res["unsplit"]["achieved_gbs"],
+                       "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": res["unsplit"]["frac"],
+                       "peak_source": pk["source"]}
+    return res
+
+
 def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
     """cfg3: chunked prefill of B=8 sequences x T=2048 tokens, 16 heads, dk=dv=128, zero initial state, bf16 out and
     fp32 final state. Inputs (201 MB of q/k/v) exceed L2, so no flush is needed between replays."""
@@ -589,8 +631,8 @@ def cpu_reference(updates: int, streams=STREAMS):
 
 def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
-    updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, or cfg5
-    DeltaNet + MoE decode layers."""
+    updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5
+    DeltaNet + MoE decode layers, or cfg5 GQA decode attention."""
     ops = __import__("__graft_entry__").load_package().ops
     dev = torch.device("cuda", 0)
     if workload == "moe":
@@ -628,6 +670,14 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
             ops.gdn_chunk_prefill(q, k, v, g, beta, cu)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg3 chunked prefills done")
+        return
+    if workload == "gqa_decode":
+        q, kc, vc, table, seq = gqa_cfg5_inputs(dev)
+        out = torch.empty_like(q)
+        for _ in range(n):
+            ops.gqa_decode(q, kc, vc, table, seq, out=out)
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg5 GQA decode attention calls done")
         return
     if workload == "attnres":
         gen = torch.Generator().manual_seed(7)
@@ -668,7 +718,7 @@ def main():
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
     ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill",
-                                                                         "decode_layer"),
+                                                                         "decode_layer", "gqa_decode"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
@@ -716,6 +766,7 @@ def main():
                     "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
                     "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
                     "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
+                    "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
                     "decode_layer_cfg5": bench_decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev,
                                                                  stream),
                 }

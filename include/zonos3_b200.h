@@ -25,7 +25,8 @@ void zb_clear_error(void);
 int zb_version(void);
 
 /* Reads the current device's status word (bits set by kernels whose bounded device-side waits expired:
- * 1 = AttnRes source load, 2 = grouped GEMM pipeline, 4 = chunked prefill pipeline); clear != 0 resets it.
+ * 1 = AttnRes source load, 2 = grouped GEMM pipeline, 4 = chunked prefill pipeline, 8 = AttnRes exchange,
+ * 16 = decode attention pipeline); clear != 0 resets it.
  * Synchronous (a device-to-host copy); for diagnostics and tests, not for the hot path. No reference counterpart:
  * the reference's kernels have no device-side waits. */
 int zb_device_status(unsigned* flags, int clear);
@@ -211,10 +212,41 @@ int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_
  * library holds until exit, so T*k*D must be at most 4,194,304 (status 3 otherwise, nothing queued). Calls share
  * the array: each clears the rows it uses first, and calls that overlap on the GPU race. The first call on a
  * device looks up the array's address with that device current; make it before any stream capture. Allocates
- * nothing. Arguments as zb_moe_gemm_down (h .. weights) and zb_moe_combine (T, k, out, out_stride). */
+ * nothing. Arguments as zb_moe_gemm_down (h .. weights, without counts) and zb_moe_combine (T, k, out,
+ * out_stride). */
 int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
                                 const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, int T, int k,
                                 uint16_t* out, int64_t out_stride, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------ GQA decode attention (KV cache) */
+
+/* Copies row i of k and v ([N, Hkv*hd] bf16, row strides k_stride / v_stride) to slot slots[i] of k_cache and
+ * v_cache (slot s at s * slot_stride elements; a slot outside [0, num_slots) stores nothing). Replaces MHAKVCache.store_kv /
+ * store_cache (servers/sgl/src/zonos3_sgl/kvcache/mha_pool.py:58-67,
+ * servers/sgl/src/zonos3_sgl/kernel/csrc/jit/store.cu:28-50). Hkv*hd and the strides multiples of 8; caches, k and v
+ * 16-byte aligned. */
+int zb_kv_store(uint16_t* k_cache, uint16_t* v_cache, int64_t slot_stride, int64_t num_slots, const int32_t* slots,
+                const uint16_t* k, int64_t k_stride, const uint16_t* v, int64_t v_stride, int N, int Hkv, int hd,
+                cudaStream_t stream);
+
+/* Decode attention of one query row per request over its cached keys: out[b, h] = softmax(q[b, h] . K^T *
+ * softmax_scale) V over the seq_lens[b] positions of request b, whose slots are page_table[b, 0 .. seq_lens[b]);
+ * query head h reads KV head h / (Hq / Hkv). Replaces flash_attn_with_kvcache as the FA backend calls it for a decode
+ * batch (servers/sgl/src/zonos3_sgl/attention/fa.py:64-81, :171-212; one token per page).
+ *   q [B, Hq, hd] bf16 (request stride q_stride); k_cache / v_cache slot s, head g at s * slot_stride + g * hd,
+ *   s in [0, num_slots) (a table entry outside that range masks its key position, nothing is read for it);
+ *   page_table [B, table_stride] int32 whose first max_seq_len columns are read; seq_lens [B] int32, clamped to
+ *   max_seq_len (0, or every key masked: zero output); out [B, Hq, hd] bf16 (out_stride).
+ *   The key range of a request is cut into `splits` pieces of split_len positions (a multiple of 32; splits *
+ *   split_len must cover the longest seq_len, keys past it are not read); with splits > 1 the partials go to a
+ *   workspace of B * Hq * splits * (hd + 2) floats (4-byte each) and a second kernel merges them. The reference
+ *   runs this model's decode unsplit (fa.py:41-50), which splits = 1 matches. hd in {32, 64, 128}, Hq / Hkv in
+ *   {1, 2, 4, 8}. */
+int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, const uint16_t* v_cache,
+                  int64_t slot_stride, int64_t num_slots, const int32_t* page_table, int64_t table_stride,
+                  const int32_t* seq_lens, int max_seq_len, int B, int Hq, int Hkv, int hd, float softmax_scale,
+                  int splits, int split_len, float* workspace, int64_t workspace_bytes, uint16_t* out,
+                  int64_t out_stride, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

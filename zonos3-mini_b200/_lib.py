@@ -65,6 +65,12 @@ SIGNATURES: dict[str, list] = {
     "zb_moe_combine": [_p, _i32, _i32, _i32, _p, _i64, _p],
     # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, T, k, out, out_stride, stream
     "zb_moe_down_combine_noalloc": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _i32, _i32, _p, _i64, _p],
+    # k_cache, v_cache, slot_stride, num_slots, slots, k, k_stride, v, v_stride, N, Hkv, hd, stream
+    "zb_kv_store": [_p, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i32, _i32, _i32, _p],
+    # q, q_stride, k_cache, v_cache, slot_stride, num_slots, page_table, table_stride, seq_lens, max_seq_len, B, Hq,
+    # Hkv, hd, scale, splits, split_len, workspace, workspace_bytes, out, out_stride, stream
+    "zb_gqa_decode": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _p,
+                      _i64, _p, _i64, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None,
              "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64}

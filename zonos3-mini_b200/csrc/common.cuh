@@ -44,6 +44,7 @@ enum DeviceStatusBits : unsigned {
   kStatusGemmTimeout = 1u << 1,
   kStatusPrefillTimeout = 1u << 2,
   kStatusAttnresExchangeTimeout = 1u << 3,
+  kStatusAttnDecodeTimeout = 1u << 4,
 };
 
 }  // namespace zb

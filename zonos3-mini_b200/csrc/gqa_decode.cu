@@ -1,0 +1,641 @@
+// GQA decode attention over a slot-indexed KV cache, and the KV store that fills it.
+//
+// Reference: the global-attention layers' decode step — FlashAttention3's flash_attn_with_kvcache as the FA backend
+// calls it (servers/sgl/src/zonos3_sgl/attention/fa.py:64-81, :171-212: one query row per request, causal, K/V
+// looked up through the page table of token slots, cache_seqlens keys per request, softmax_scale = head_dim^-0.5)
+// and MHAKVCache.store_kv / store_cache (servers/sgl/src/zonos3_sgl/kvcache/mha_pool.py:58-67,
+// servers/sgl/src/zonos3_sgl/kernel/csrc/jit/store.cu:28-50: row i of k and v copied to slot out_loc[i]). The cache
+// holds one token per page: k_cache / v_cache [slots, Hkv, hd] with `slot_stride` elements between two slots (the
+// layer-first and the page-first pool layouts differ only in that stride).
+//
+// Head dim 128 (the model's attention) runs on the tensor cores: gqa_decode_tc_kernel below. Head dims 32 and 64
+// (the tiny configurations) run on CUDA cores: a CTA per (request, KV head, split of the key range); 4 warps take
+// 32-position tiles of the split in turn. A warp stages its tile's K and V rows in shared memory with cp.async (16-byte pieces, the slot of each row
+// from the page table), then lane j scores position j against every query head of the group (fp32 dot products
+// over the bf16 K row), the warp updates each head's running max and denominator (online softmax in base 2, the
+// scale folded into log2(e)), and lanes, each owning hd / 32 dimensions, accumulate p * V for every head. The 4
+// warps merge their (max, denominator, accumulator) through shared memory; with one split the CTA writes the
+// normalised bf16 output, with several each split writes its partial to the workspace and a combine kernel merges
+// them. fp32 throughout in this kernel (FA3 rounds P to bf16 before its P.V product, as the tensor-core kernel does;
+// the difference is within bf16 tolerance).
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 32;  // key positions of a warp tile
+
+// Dynamic shared memory of one CTA: the group's queries (fp32), each warp's K tile (rows padded by 16 bytes) and V
+// tile (bf16), the warps' running max and denominator per head.
+template <int HD, int G>
+struct AttnSmem {
+  static constexpr int KP = HD + 8;
+  static constexpr size_t q = 0;
+  static constexpr size_t k = q + (size_t)G * HD * 4;
+  static constexpr size_t v = k + (size_t)kWarps * kTile * KP * 2;
+  static constexpr size_t ml = v + (size_t)kWarps * kTile * HD * 2;
+  static constexpr size_t total = ml + (size_t)2 * kWarps * G * 4;
+  static_assert((size_t)kWarps * G * HD * 4 <= (size_t)kWarps * kTile * KP * 2, "warp merge fits the K tiles");
+};
+
+struct AttnParams {
+  const __nv_bfloat16* q;  // [B, Hq, hd], request stride q_stride
+  int64_t q_stride;
+  const __nv_bfloat16* k_cache;  // slot s, head h at (s * slot_stride + h * hd)
+  const __nv_bfloat16* v_cache;
+  int64_t slot_stride;
+  int64_t num_slots;          // slots of the cache; a table entry outside [0, num_slots) masks its key position
+  const int32_t* page_table;  // [B, table_stride]: slot of each key position
+  int64_t table_stride;
+  const int32_t* seq_lens;  // [B] keys per request (0: the request's output is zero), clamped to max_seq_len
+  int max_seq_len;          // columns of the page table
+  int B, Hq, Hkv;
+  float scale_log2;  // softmax_scale * log2(e)
+  int splits;
+  int split_len;  // key positions per split (a multiple of kTile)
+  float* part;    // [B, Hq, splits, hd + 2]: accumulator, running max (base 2), denominator
+  __nv_bfloat16* out;  // [B, Hq, hd], request stride out_stride
+  int64_t out_stride;
+  unsigned* status;  // device status word (a bounded wait that expired sets kStatusAttnDecodeTimeout)
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(zb::smem_addr(dst)), "l"(src) : "memory");
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnParams p) {
+  zb::pdl_enter();
+  using L = AttnSmem<HD, G>;
+  constexpr int KP = L::KP;         // padded K row (bf16): conflict-free 16-byte row reads
+  constexpr int DL = HD / 32;       // dimensions a lane owns in the P.V accumulation
+  constexpr int CH = HD * 2 / 16;   // 16-byte pieces of a row
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  auto q_s = reinterpret_cast<float(*)[HD]>(smem_raw + L::q);
+  auto k_s = reinterpret_cast<__nv_bfloat16(*)[kTile][KP]>(smem_raw + L::k);
+  auto v_s = reinterpret_cast<__nv_bfloat16(*)[kTile][HD]>(smem_raw + L::v);
+  auto m_s = reinterpret_cast<float(*)[G]>(smem_raw + L::ml);
+  auto l_s = reinterpret_cast<float(*)[G]>(smem_raw + L::ml + (size_t)kWarps * G * 4);
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int len = min(max(p.seq_lens[b], 0), p.max_seq_len);
+  const int begin = split * p.split_len, end = min(len, begin + p.split_len);
+
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int g = i / HD, d = i % HD;
+    q_s[g][d] = __bfloat162float(p.q[(int64_t)b * p.q_stride + (int64_t)(kvh * G + g) * HD + d]);
+  }
+  __syncthreads();
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DL; ++j) acc[g][j] = 0.f;
+  }
+  const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
+  for (int t0 = begin + warp * kTile; t0 < end; t0 += kWarps * kTile) {
+    const int pos = t0 + lane;
+    const int slot = pos < end ? table[pos] : -1;
+    const bool valid = slot >= 0 && slot < p.num_slots;
+    const unsigned live = __ballot_sync(0xffffffffu, valid);  // rows of the tile that hold a key
+    // stage the tile: row r's 16-byte pieces, two rows per pass of the warp for HD = 128
+    for (int i = lane; i < kTile * CH; i += 32) {
+      const int r = i / CH, c = i % CH;
+      const int rs = __shfl_sync(0xffffffffu, slot, r);  // every lane takes part in the shuffle
+      if ((live >> r) & 1u) {
+        const int64_t off = (int64_t)rs * p.slot_stride + (int64_t)kvh * HD + c * 8;
+        cp_async16(&k_s[warp][r][c * 8], p.k_cache + off);
+        cp_async16(&v_s[warp][r][c * 8], p.v_cache + off);
+      }
+    }
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    // scores of position `pos` for every head of the group
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) s[g] = 0.f;
+    if (valid) {
+#pragma unroll 4
+      for (int c = 0; c < CH; ++c) {
+        float kf[8];
+        zb::ld_bf16x8(&k_s[warp][lane][c * 8], kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&q_s[g][c * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&q_s[g][c * 8 + 4]);
+          s[g] = fmaf(qa.x, kf[0], s[g]);
+          s[g] = fmaf(qa.y, kf[1], s[g]);
+          s[g] = fmaf(qa.z, kf[2], s[g]);
+          s[g] = fmaf(qa.w, kf[3], s[g]);
+          s[g] = fmaf(qb.x, kf[4], s[g]);
+          s[g] = fmaf(qb.y, kf[5], s[g]);
+          s[g] = fmaf(qb.z, kf[6], s[g]);
+          s[g] = fmaf(qb.w, kf[7], s[g]);
+        }
+      }
+    }
+    // online softmax (base 2) and P.V
+    float pr[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float x = valid ? s[g] * p.scale_log2 : -INFINITY;
+      const float m_new = fmaxf(m[g], zb::warp_max(x));
+      // 0 on the first live tile (m = -inf); 1 while no key has been seen (both -inf)
+      const float corr = m_new == -INFINITY ? 1.f : exp2f(m[g] - m_new);
+      pr[g] = valid ? exp2f(x - m_new) : 0.f;
+      l[g] = l[g] * corr + zb::warp_sum(pr[g]);
+      m[g] = m_new;
+#pragma unroll
+      for (int j = 0; j < DL; ++j) acc[g][j] *= corr;
+    }
+    const int rows = min(kTile, end - t0);
+    for (int r = 0; r < rows; ++r) {
+      if (!((live >> r) & 1u)) continue;  // a masked row was not staged (warp-uniform)
+      float vf[DL];
+      if constexpr (DL == 4) {
+        zb::ld_bf16x4(&v_s[warp][r][lane * 4], vf);
+      } else {
+#pragma unroll
+        for (int j = 0; j < DL; ++j) vf[j] = __bfloat162float(v_s[warp][r][lane * DL + j]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pg = __shfl_sync(0xffffffffu, pr[g], r);
+#pragma unroll
+        for (int j = 0; j < DL; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
+      }
+    }
+    __syncwarp();  // the tile buffers are refilled next
+  }
+
+  // merge the warps: max, denominators and accumulators through shared memory (the K tiles are reused)
+  if (lane == 0)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m_s[warp][g] = m[g];
+      l_s[warp][g] = l[g];
+    }
+  __syncthreads();
+  float* acc_s = reinterpret_cast<float*>(&k_s[0][0][0]);  // [kWarps][G][HD] fp32 (fits: 4*G*HD*4 <= K tiles)
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < DL; ++j) acc_s[((size_t)warp * G + g) * HD + lane * DL + j] = acc[g][j];
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += kThreads) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = exp2f(m_s[w][g] - M);
+        L += f * l_s[w][g];
+        A += f * acc_s[((size_t)w * G + g) * HD + d];
+      }
+    }
+    const int h = kvh * G + g;
+    if (p.splits == 1) {
+      p.out[(int64_t)b * p.out_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+    } else {
+      float* part = p.part + (((int64_t)b * p.Hq + h) * p.splits + split) * (HD + 2);
+      part[d] = A;
+      if (d == 0) {
+        part[HD] = M;
+        part[HD + 1] = L;
+      }
+    }
+  }
+}
+
+// Merge of the splits of one (request, head): out = sum_s 2^(m_s - M) acc_s / sum_s 2^(m_s - M) l_s.
+template <int HD>
+__global__ void __launch_bounds__(HD) gqa_combine_kernel(AttnParams p) {
+  zb::pdl_enter();
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const float* part = p.part + ((int64_t)b * p.Hq + h) * p.splits * (HD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, part[s * (HD + 2) + HD]);
+  float L = 0.f, A = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.splits; ++s) {
+      const float f = exp2f(part[s * (HD + 2) + HD] - M);
+      L += f * part[s * (HD + 2) + HD + 1];
+      A += f * part[s * (HD + 2) + d];
+    }
+  }
+  p.out[(int64_t)b * p.out_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+}
+
+template <int HD, int G>
+int launch_attn(const AttnParams& p, cudaStream_t stream) {
+  constexpr size_t smem = AttnSmem<HD, G>::total;
+  auto kernel = gqa_decode_kernel<HD, G>;
+  static bool configured[64] = {false};  // the shared-memory attribute, set once per device
+  int dev = 0;
+  ZB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)p.splits, (unsigned)p.Hkv, (unsigned)p.B), dim3(kThreads), smem, stream,
+                     1, p));
+  if (int rc = zb::check_launch("gqa_decode")) return rc;
+  if (p.splits > 1) {
+    ZB_CUDA(zb::launch(gqa_combine_kernel<HD>, dim3((unsigned)p.Hq, (unsigned)p.B), dim3(HD), 0, stream, 1, p));
+    return zb::check_launch("gqa_decode(combine)");
+  }
+  return zb::kOk;
+}
+
+template <int HD>
+int dispatch_group(const AttnParams& p, int G, cudaStream_t stream) {
+  switch (G) {
+    case 1: return launch_attn<HD, 1>(p, stream);
+    case 2: return launch_attn<HD, 2>(p, stream);
+    case 4: return launch_attn<HD, 4>(p, stream);
+    case 8: return launch_attn<HD, 8>(p, stream);
+    default: return zb::fail(zb::kUnsupported, "gqa_decode: %d query heads per KV head (1, 2, 4 or 8)", G);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Head dim 128: both products on the tensor cores. A CTA per (request, KV head, split) streams the split's keys in
+// 128-position tiles through a 3-stage cp.async ring (each stage a 32 KB K tile, K-major, and a 32 KB V tile,
+// MN-major, both 128B-swizzled). Per tile: S^T = K Q^T (M = 128 positions, N = 16: the group's heads padded with
+// zero rows) into tensor memory; thread t reads the scores of position t; the tile's max per head goes through
+// shared memory; p = 2^(s log2e scale - m) is rounded to bf16 (as FlashAttention-3 rounds P) into a K-major P^T
+// operand; O^T += V^T P^T (M = 128 head dimensions, N = 16) accumulates in tensor memory. The running max is
+// raised only when a tile's max exceeds it by more than 2^8 (the stale max keeps every p <= 256, exact after the
+// final division), so the accumulator is rescaled (tensor-memory load, scale, store) only on such tiles. One
+// thread issues the MMAs; one commit per tile covers the previous tile's O^T update and this tile's S^T, whose
+// completion also frees the ring stage the next load overwrites.
+namespace tcattn {
+
+constexpr int kHD = 128;
+constexpr int kTilePos = 128;  // key positions of a tile (tensor-memory lanes of S^T)
+constexpr int kStages = 3;
+constexpr int kN = 16;  // MMA N: the group's query heads, zero-padded
+constexpr uint32_t kKBytes = kTilePos * kHD * 2;  // K-major: 2 blocks of 64 dims x 128 rows x 128 B
+constexpr uint32_t kVBytes = kTilePos * kHD * 2;  // MN-major atoms (8 positions x 64 dims), [pos / 8][dim / 64]
+constexpr uint32_t kVLbo = 1024, kVSbo = 2048;    // atom strides along dims (M) and positions (K)
+constexpr uint32_t kStageBytes = kKBytes + kVBytes;
+constexpr uint32_t kPBytes = kN * kTilePos * 2;  // P^T: 16 head rows x 128 positions, 2 K-major blocks
+constexpr uint32_t kQBytes = kN * kHD * 2;       // Q: 16 head rows x 128 dims, 2 K-major blocks
+constexpr uint32_t kBlk16 = kN * 128;            // one 64-wide K block of a 16-row operand
+constexpr uint32_t kOffP = kStages * kStageBytes;
+constexpr uint32_t kOffQ = kOffP + 2 * kPBytes;
+constexpr uint32_t kOffTail = kOffQ + kQBytes;
+constexpr uint32_t kColS = 0, kColO = 16, kTmemCols = 32;
+
+struct Tail {
+  float red[2][kWarps][kN];  // per-warp tile max of each head (double-buffered across tiles)
+  float lsum[kWarps][kN];    // per-warp denominators
+  uint64_t bar;              // MMA completion
+  uint32_t tmem;
+  int abort;
+};
+constexpr size_t kSmem = kOffTail + sizeof(Tail) + 1024;  // + slack to 1024-align the base
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+}  // namespace tcattn
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1) gqa_decode_tc_kernel(AttnParams p) {
+  using namespace tcattn;
+  namespace tc = zb::tc;
+  zb::pdl_enter();
+  extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 bytes below
+  const uint32_t raw = zb::smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* gbase = smem_raw + (base - raw);
+  Tail& tl = *reinterpret_cast<Tail*>(gbase + kOffTail);
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int len = min(max(p.seq_lens[b], 0), p.max_seq_len);
+  const int begin = split * p.split_len, end = min(len, begin + p.split_len);
+  const int ntiles = end > begin ? (end - begin + kTilePos - 1) / kTilePos : 0;
+  const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
+  const uint32_t bar = zb::smem_addr(&tl.bar);
+
+  // P^T buffers zeroed once (rows >= G stay zero); Q staged with rows >= G zero
+  for (int i = tid; i < (int)(2 * kPBytes / 16); i += kThreads) {
+    reinterpret_cast<uint4*>(gbase + kOffP)[i] = make_uint4(0, 0, 0, 0);
+  }
+  for (int i = tid; i < kN * 16; i += kThreads) {
+    const int r = i / 16, c = i % 16;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) {
+      v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride + (int64_t)(kvh * G + r) * kHD + c * 8);
+    }
+    *reinterpret_cast<uint4*>(gbase + kOffQ + (c / 8) * kBlk16 + tc::sw128(r, c % 8)) = v;
+  }
+  if (tid == 0) {
+    zb::mbar_init(bar, 1);
+    zb::fence_mbar_init();
+    tl.abort = 0;
+  }
+  if (warp == 0) tc::alloc(zb::smem_addr(&tl.tmem), kTmemCols);
+
+  // tile j -> ring stage j % kStages; this thread's row (32 * warp + lane) also records whether it holds a key
+  unsigned live = 0;
+  auto load_tile = [&](int j) {
+    if (j < ntiles) {
+      const uint32_t kb = base + (uint32_t)(j % kStages) * kStageBytes, vb = kb + kKBytes;
+      const int pos = begin + j * kTilePos + tid;
+      const int slot = pos < end ? table[pos] : -1;
+      const bool valid = slot >= 0 && slot < p.num_slots;
+      live = (live & ~(1u << (j % kStages))) | ((valid ? 1u : 0u) << (j % kStages));
+      const int mine = valid ? slot : -1;
+#pragma unroll 4
+      for (int it = 0; it < 16; ++it) {  // two rows per pass: 16 lanes x 16 bytes of each 256-byte row
+        const int rl = 2 * it + lane / 16, c = lane % 16;
+        const int rs = __shfl_sync(0xffffffffu, mine, rl);
+        const int r = 32 * warp + rl;
+        const bool ok = rs >= 0;
+        const int64_t off = (int64_t)(ok ? rs : 0) * p.slot_stride + (int64_t)kvh * kHD + c * 8;
+        cp_async16(kb + (uint32_t)(c / 8) * (kTilePos * 128) + tc::sw128(r, c % 8), p.k_cache + off, ok);
+        cp_async16(vb + (uint32_t)(r / 8) * kVSbo + (uint32_t)(c / 8) * kVLbo + tc::sw128(r % 8, c % 8),
+                   p.v_cache + off, ok);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int j = 0; j < kStages - 1; ++j) load_tile(j);
+  cp_async_wait<kStages - 2>();
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = tl.tmem;
+  const uint32_t tlane = tmem + ((uint32_t)(32 * warp) << 16);
+  constexpr uint32_t kIdS = tc::idesc_bf16(128, kN);
+  constexpr uint32_t kIdO = tc::idesc_bf16(128, kN, /*a_mn=*/true);
+  auto issue_s = [&](int j) {  // S^T(j) = K(j) Q^T
+    const uint32_t kb = base + (uint32_t)(j % kStages) * kStageBytes;
+#pragma unroll
+    for (int ks = 0; ks < kHD / 16; ++ks) {
+      tc::mma(tmem + kColS, tc::desc_kmajor(kb + (ks / 4) * (kTilePos * 128) + (ks % 4) * 32),
+              tc::desc_kmajor(base + kOffQ + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdS, ks > 0);
+    }
+  };
+  auto issue_o = [&](int j, bool accumulate) {  // O^T += V(j)^T P(j)^T
+    const uint32_t vb = base + (uint32_t)(j % kStages) * kStageBytes + kKBytes;
+    const uint32_t pb = base + kOffP + (uint32_t)(j & 1) * kPBytes;
+#pragma unroll
+    for (int ks = 0; ks < kTilePos / 16; ++ks) {
+      tc::mma(tmem + kColO, tc::desc_mnmajor(vb + ks * 2 * kVSbo, kVLbo, kVSbo),
+              tc::desc_kmajor(pb + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdO, accumulate || ks > 0);
+    }
+  };
+  if (tid == 0 && ntiles > 0) {
+    issue_s(0);
+    tc::commit(bar);
+  }
+
+  float m_run[G], l_part[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m_run[g] = -INFINITY;
+    l_part[g] = 0.f;
+  }
+  bool aborted = false;
+  for (int i = 0; i < ntiles; ++i) {
+    // S^T(i) and O^T(i - 1) complete: stage (i - 1) % kStages is free for tile i + kStages - 1
+    if (!aborted && !zb::mbar_wait_bounded(bar, (uint32_t)(i & 1), p.status, zb::kStatusAttnDecodeTimeout)) {
+      tl.abort = 1;
+    }
+    tc::fence_after();
+    load_tile(i + kStages - 1);
+    uint32_t sr[16];
+    tc::ld16(tlane + kColS, sr);
+    tc::ld_wait();
+    const bool valid = (live >> (i % kStages)) & 1u;
+    float x[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      x[g] = valid ? __uint_as_float(sr[g]) * p.scale_log2 : -INFINITY;
+      const float wm = zb::warp_max(x[g]);
+      if (lane == 0) tl.red[i & 1][warp][g] = wm;
+    }
+    __syncthreads();
+    aborted = *reinterpret_cast<volatile int*>(&tl.abort) != 0;
+    bool rescale = false;
+    float corr[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mt = tl.red[i & 1][0][g];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) mt = fmaxf(mt, tl.red[i & 1][w][g]);
+      corr[g] = 1.f;
+      if (mt > m_run[g] + 8.f) {  // never true while both are -inf
+        corr[g] = exp2f(m_run[g] - mt);  // 0 for the first tile with a key
+        m_run[g] = mt;
+        rescale = true;
+      }
+    }
+    if (rescale) {  // the same decision on every thread (same maxima, same history)
+#pragma unroll
+      for (int g = 0; g < G; ++g) l_part[g] *= corr[g];
+      if (i > 0) {
+        uint32_t o[16];
+        tc::ld16(tlane + kColO, o);
+        tc::ld_wait();
+#pragma unroll
+        for (int g = 0; g < G; ++g) o[g] = __float_as_uint(__uint_as_float(o[g]) * corr[g]);
+        tc::st16(tlane + kColO, o);
+        tc::st_wait();
+      }
+    }
+    unsigned char* pbuf = gbase + kOffP + (i & 1) * kPBytes + (tid / 64) * kBlk16 + (tid % 64 % 8) * 2;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float pv = x[g] == -INFINITY ? 0.f : exp2f(x[g] - m_run[g]);
+      l_part[g] += pv;
+      *reinterpret_cast<__nv_bfloat16*>(pbuf + tc::sw128(g, (tid % 64) / 8)) = __float2bfloat16_rn(pv);
+    }
+    cp_async_wait<kStages - 2>();  // tile i + 1 landed (this thread's pieces)
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (tid == 0) {
+      issue_o(i, i > 0);
+      if (i + 1 < ntiles) issue_s(i + 1);
+      tc::commit(bar);
+    }
+  }
+
+  float o_val[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o_val[g] = 0.f;
+  if (ntiles > 0) {
+    if (!aborted && !zb::mbar_wait_bounded(bar, (uint32_t)(ntiles & 1), p.status, zb::kStatusAttnDecodeTimeout)) {
+      tl.abort = 1;
+    }
+    tc::fence_after();
+    uint32_t o[16];
+    tc::ld16(tlane + kColO, o);
+    tc::ld_wait();
+#pragma unroll
+    for (int g = 0; g < G; ++g) o_val[g] = __uint_as_float(o[g]);
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float s = zb::warp_sum(l_part[g]);
+    if (lane == 0) tl.lsum[warp][g] = s;
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (*reinterpret_cast<volatile int*>(&tl.abort) == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) L += tl.lsum[w][g];
+      const int h = kvh * G + g;
+      if (p.splits == 1) {
+        p.out[(int64_t)b * p.out_stride + (int64_t)h * kHD + tid] = __float2bfloat16_rn(L > 0.f ? o_val[g] / L : 0.f);
+      } else {
+        float* part = p.part + (((int64_t)b * p.Hq + h) * p.splits + split) * (kHD + 2);
+        part[tid] = L > 0.f ? o_val[g] : 0.f;
+        if (tid == 0) {
+          part[kHD] = m_run[g];
+          part[kHD + 1] = L;
+        }
+      }
+    }
+  }
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int G>
+int launch_attn_tc(const AttnParams& p, cudaStream_t stream) {
+  auto kernel = gqa_decode_tc_kernel<G>;
+  static bool configured[64] = {false};  // the shared-memory attribute, set once per device
+  int dev = 0;
+  ZB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcattn::kSmem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  ZB_CUDA(zb::launch(kernel, dim3((unsigned)p.splits, (unsigned)p.Hkv, (unsigned)p.B), dim3(kThreads),
+                     tcattn::kSmem, stream, 1, p));
+  if (int rc = zb::check_launch("gqa_decode")) return rc;
+  if (p.splits > 1) {
+    ZB_CUDA(zb::launch(gqa_combine_kernel<128>, dim3((unsigned)p.Hq, (unsigned)p.B), dim3(128), 0, stream, 1, p));
+    return zb::check_launch("gqa_decode(combine)");
+  }
+  return zb::kOk;
+}
+
+struct StoreParams {
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t slot_stride;
+  int64_t num_slots;
+  const int32_t* slots;  // [N] destination slot of each row (outside [0, num_slots): not stored)
+  const __nv_bfloat16* k;  // [N, row] with row stride k_stride
+  const __nv_bfloat16* v;
+  int64_t k_stride, v_stride;
+  int N, row;  // row = Hkv * hd elements (a multiple of 8)
+};
+
+// A warp per (row, k or v): 16-byte pieces.
+__global__ void __launch_bounds__(256) kv_store_kernel(StoreParams p) {
+  zb::pdl_enter();
+  const int64_t unit = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (unit >= 2 * (int64_t)p.N) return;
+  const int64_t i = unit / 2;
+  const bool is_v = unit % 2;
+  const int slot = p.slots[i];
+  if (slot < 0 || slot >= p.num_slots) return;
+  const uint4* src = reinterpret_cast<const uint4*>((is_v ? p.v + i * p.v_stride : p.k + i * p.k_stride));
+  uint4* dst = reinterpret_cast<uint4*>((is_v ? p.v_cache : p.k_cache) + (int64_t)slot * p.slot_stride);
+  for (int c = lane; c < p.row / 8; c += 32) dst[c] = src[c];
+}
+
+}  // namespace
+
+ZB_API int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, const uint16_t* v_cache,
+                         int64_t slot_stride, int64_t num_slots, const int32_t* page_table, int64_t table_stride,
+                         const int32_t* seq_lens, int max_seq_len, int B, int Hq, int Hkv, int hd,
+                         float softmax_scale, int splits, int split_len, float* workspace, int64_t workspace_bytes,
+                         uint16_t* out, int64_t out_stride, cudaStream_t stream) {
+  ZB_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "gqa_decode: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  if (hd != 32 && hd != 64 && hd != 128) {
+    return zb::fail(zb::kUnsupported, "gqa_decode: head dim %d (32, 64 or 128)", hd);
+  }
+  if (B == 0) return zb::kOk;
+  ZB_REQUIRE(q && k_cache && v_cache && page_table && seq_lens && out, "gqa_decode: null pointer");
+  const int tile = hd == 128 ? tcattn::kTilePos : kTile;
+  ZB_REQUIRE(splits >= 1 && split_len > 0 && split_len % tile == 0,
+             "gqa_decode: splits %d >= 1 and split_len %d a positive multiple of %d", splits, split_len, tile);
+  ZB_REQUIRE(max_seq_len >= 0 && max_seq_len <= table_stride && (int64_t)splits * split_len >= max_seq_len &&
+                 num_slots >= 0,
+             "gqa_decode: max_seq_len %d must fit the table row (%lld) and the splits (%d x %d)", max_seq_len,
+             (long long)table_stride, splits, split_len);
+  const int64_t need = splits > 1 ? (int64_t)B * Hq * splits * (hd + 2) * 4 : 0;
+  ZB_REQUIRE(splits == 1 || (workspace && workspace_bytes >= need),
+             "gqa_decode: %d splits need a workspace of %lld bytes", splits, (long long)need);
+  ZB_REQUIRE(q_stride >= (int64_t)Hq * hd && out_stride >= (int64_t)Hq * hd && slot_stride >= (int64_t)Hkv * hd &&
+                 slot_stride % 8 == 0,
+             "gqa_decode: strides (q %lld, out %lld, slot %lld)", (long long)q_stride, (long long)out_stride,
+             (long long)slot_stride);
+  ZB_REQUIRE_ALIGNED(k_cache, 16, "gqa_decode k_cache");
+  ZB_REQUIRE_ALIGNED(v_cache, 16, "gqa_decode v_cache");
+  AttnParams p{reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
+               reinterpret_cast<const __nv_bfloat16*>(v_cache), slot_stride, num_slots, page_table, table_stride,
+               seq_lens, max_seq_len, B, Hq, Hkv, softmax_scale * 1.4426950408889634f, splits, split_len, workspace,
+               reinterpret_cast<__nv_bfloat16*>(out), out_stride, zb::device_status_ptr()};
+  const int G = Hq / Hkv;
+  if (hd == 128) {
+    ZB_REQUIRE(q_stride % 8 == 0, "gqa_decode: q_stride %lld must be a multiple of 8", (long long)q_stride);
+    ZB_REQUIRE_ALIGNED(q, 16, "gqa_decode q");
+    switch (G) {
+      case 1: return launch_attn_tc<1>(p, stream);
+      case 2: return launch_attn_tc<2>(p, stream);
+      case 4: return launch_attn_tc<4>(p, stream);
+      case 8: return launch_attn_tc<8>(p, stream);
+      default: return zb::fail(zb::kUnsupported, "gqa_decode: %d query heads per KV head (1, 2, 4 or 8)", G);
+    }
+  }
+  return hd == 64 ? dispatch_group<64>(p, G, stream) : dispatch_group<32>(p, G, stream);
+}
+
+ZB_API int zb_kv_store(uint16_t* k_cache, uint16_t* v_cache, int64_t slot_stride, int64_t num_slots,
+                       const int32_t* slots, const uint16_t* k, int64_t k_stride, const uint16_t* v, int64_t v_stride,
+                       int N, int Hkv, int hd, cudaStream_t stream) {
+  ZB_REQUIRE(N >= 0 && Hkv > 0 && hd > 0 && (Hkv * hd) % 8 == 0, "kv_store: bad sizes N=%d Hkv=%d hd=%d", N, Hkv, hd);
+  if (N == 0) return zb::kOk;
+  ZB_REQUIRE(k_cache && v_cache && slots && k && v, "kv_store: null pointer");
+  ZB_REQUIRE(slot_stride >= (int64_t)Hkv * hd && slot_stride % 8 == 0 && k_stride % 8 == 0 && v_stride % 8 == 0 &&
+                 k_stride >= (int64_t)Hkv * hd && v_stride >= (int64_t)Hkv * hd,
+             "kv_store: strides must cover a row and be multiples of 8 elements");
+  for (const void* ptr : {(const void*)k_cache, (const void*)v_cache, (const void*)k, (const void*)v}) {
+    ZB_REQUIRE_ALIGNED(ptr, 16, "kv_store tensors");
+  }
+  StoreParams p{reinterpret_cast<__nv_bfloat16*>(k_cache), reinterpret_cast<__nv_bfloat16*>(v_cache), slot_stride,
+                num_slots, slots, reinterpret_cast<const __nv_bfloat16*>(k), reinterpret_cast<const __nv_bfloat16*>(v), k_stride,
+                v_stride, N, Hkv * hd};
+  ZB_CUDA(zb::launch(kv_store_kernel, dim3((unsigned)((2 * (int64_t)N + 7) / 8)), dim3(256), 0, stream, 1, p));
+  return zb::check_launch("kv_store");
+}

@@ -621,3 +621,93 @@ def gdn_gated_norm(o, z, weight, eps=1e-5, out=None):
     _lib.call("zb_gdn_gated_norm", o.data_ptr(), z.data_ptr(), z.stride(0) if N > 1 else H * D, weight.data_ptr(),
               float(eps), N, H, D, out.data_ptr(), _stream(dev))
     return out
+
+
+# ------------------------------------------------------------------------------------- GQA decode attention
+
+
+def kv_store(k_cache, v_cache, slots, k, v):
+    """Row i of k and v ([N, Hkv, hd] bf16) into slot slots[i] of k_cache and v_cache ([slots, Hkv, hd] bf16, slot
+    stride allowed); a slot outside [0, slots) stores nothing. The store of MHAKVCache.store_kv
+    (servers/sgl/src/zonos3_sgl/kvcache/mha_pool.py:58-67, kernel/store.py:30-43)."""
+    dev = k.device
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache), ("k", k), ("v", v)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+    _check_cuda("slots", slots, torch.int32, dev)
+    N, Hkv, hd = k.shape
+    ks = _rows("k", k, (Hkv, hd))
+    vs = _rows("v", v, (Hkv, hd))
+    cs = _rows("k_cache", k_cache, (Hkv, hd))
+    _require(v_cache.shape == k_cache.shape and v_cache.stride() == k_cache.stride(),
+             "v_cache must match k_cache's shape and strides")
+    _require(slots.shape == (N,) and slots.is_contiguous(), f"slots must be a contiguous [{N}] tensor")
+    _lib.call("zb_kv_store", k_cache.data_ptr(), v_cache.data_ptr(), cs, k_cache.shape[0], slots.data_ptr(),
+              k.data_ptr(), ks, v.data_ptr(), vs, N, Hkv, hd, _stream(dev))
+
+
+def gqa_tile(head_dim: int) -> int:
+    """Key positions of one tile of the decode attention kernel (split lengths are multiples of it): 128 for head
+    dim 128 (tensor-core kernel), 32 otherwise."""
+    return 128 if head_dim == 128 else 32
+
+
+def gqa_splits(batch: int, kv_heads: int, max_len: int, num_splits: int = 1, head_dim: int = 128) -> tuple[int, int]:
+    """(splits, split_len) covering max_len keys. num_splits = 1 runs unsplit, as the reference does for this model
+    (servers/sgl/src/zonos3_sgl/attention/fa.py:41-50); 0 picks enough splits for about two CTAs per resident CTA
+    slot (148 SMs x 1 CTA for head dim 128, x 3 otherwise), at least 256 keys each; n > 1 forces n."""
+    max_len = max(int(max_len), 1)
+    tile = gqa_tile(head_dim)
+    if num_splits == 0:
+        slots = 148 * (1 if head_dim == 128 else 3)
+        want = -(-2 * slots // max(batch * kv_heads, 1))
+        num_splits = max(1, min(want, max_len // 256))
+    split_len = -(-max_len // num_splits)
+    split_len = -(-split_len // tile) * tile
+    return -(-max_len // split_len), split_len
+
+
+def gqa_decode(q, k_cache, v_cache, page_table, cache_seqlens, *, softmax_scale=None, num_splits=1, out=None,
+               workspace=None):
+    """Decode attention over a slot-indexed KV cache: the flash_attn_with_kvcache call of the FA backend for a
+    decode batch (servers/sgl/src/zonos3_sgl/attention/fa.py:64-81, :171-212; causal, one query row per request,
+    one token per page).
+
+    q [B, Hq, hd] bf16; k_cache, v_cache [slots, Hkv, hd] bf16 (slot stride allowed); page_table [B, max_pages]
+    int32 (slot of each key position; an entry outside [0, slots) masks that key); cache_seqlens [B] int32 (keys
+    per request, clamped to max_pages). Query head h
+    reads KV head h // (Hq / Hkv). softmax_scale defaults to hd ** -0.5. num_splits as :func:`gqa_splits`;
+    workspace: optional fp32 tensor of at least B * Hq * splits * (hd + 2) elements (allocated when absent and
+    needed). Returns out [B, Hq, hd] bf16."""
+    dev = q.device
+    _check_cuda("q", q, torch.bfloat16)
+    B, Hq, hd = q.shape
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+    _require(k_cache.dim() == 3 and k_cache.shape[2] == hd, f"k_cache must be [slots, Hkv, {hd}]")
+    Hkv = k_cache.shape[1]
+    _require(Hq % Hkv == 0, f"{Hq} query heads do not group over {Hkv} KV heads")
+    qs = _rows("q", q, (Hq, hd))
+    cs = _rows("k_cache", k_cache, (Hkv, hd))
+    _require(v_cache.shape == k_cache.shape and v_cache.stride() == k_cache.stride(),
+             "v_cache must match k_cache's shape and strides")
+    _check_cuda("page_table", page_table, torch.int32, dev)
+    _check_cuda("cache_seqlens", cache_seqlens, torch.int32, dev)
+    _require(page_table.dim() == 2 and page_table.shape[0] == B and page_table.stride(1) == 1,
+             f"page_table must be [{B}, max_pages] with contiguous rows")
+    _require(cache_seqlens.shape == (B,) and cache_seqlens.is_contiguous(), f"cache_seqlens must be [{B}]")
+    if out is None:
+        out = torch.empty(B, Hq, hd, device=dev, dtype=torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    os_ = _rows("out", out, (Hq, hd))
+    splits, split_len = gqa_splits(B, Hkv, page_table.shape[1], num_splits, hd)
+    need = B * Hq * splits * (hd + 2) if splits > 1 else 0
+    if need and (workspace is None or workspace.numel() < need):
+        workspace = torch.empty(need, device=dev, dtype=torch.float32)
+    if need:
+        _check_cuda("workspace", workspace, torch.float32, dev)
+    scale = float(hd ** -0.5 if softmax_scale is None else softmax_scale)
+    _lib.call("zb_gqa_decode", q.data_ptr(), qs, k_cache.data_ptr(), v_cache.data_ptr(), cs, k_cache.shape[0],
+              page_table.data_ptr(), page_table.stride(0) if B > 1 else page_table.shape[1], cache_seqlens.data_ptr(),
+              page_table.shape[1], B, Hq, Hkv, hd, scale, splits, split_len, workspace.data_ptr() if need else None,
+              need * 4, out.data_ptr(), os_, _stream(dev))
+    return out
