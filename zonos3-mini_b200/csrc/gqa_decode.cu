@@ -350,13 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_tc_kernel(AttnParams p
   }
   if (warp == 0) tc::alloc(zb::smem_addr(&tl.tmem), kTmemCols);
 
-  // tile j -> ring stage j % kStages; this thread's row (32 * warp + lane) also records whether it holds a key
+  // tile j -> ring stage j % kStages; this thread's row (32 * warp + lane) also records whether it holds a key.
+  // The slot of the thread's row is read one tile ahead, so its latency is off the path that issues the copies.
+  auto read_slot = [&](int j) {
+    const int pos = begin + j * kTilePos + tid;
+    return j < ntiles && pos < end ? table[pos] : -1;
+  };
   unsigned live = 0;
+  int slot_ahead = read_slot(0);
   auto load_tile = [&](int j) {
     if (j < ntiles) {
       const uint32_t kb = base + (uint32_t)(j % kStages) * kStageBytes, vb = kb + kKBytes;
-      const int pos = begin + j * kTilePos + tid;
-      const int slot = pos < end ? table[pos] : -1;
+      const int slot = slot_ahead;
+      slot_ahead = read_slot(j + 1);
       const bool valid = slot >= 0 && slot < p.num_slots;
       live = (live & ~(1u << (j % kStages))) | ((valid ? 1u : 0u) << (j % kStages));
       const int mine = valid ? slot : -1;
