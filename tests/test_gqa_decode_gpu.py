@@ -33,7 +33,8 @@ def _case(gen, B, Hq, Hkv, hd, lens, slots, width):
 def test_gqa_decode_matches_oracle(zb, Hq, Hkv, hd, num_splits):
     gen = torch.Generator().manual_seed(Hq * 131 + Hkv * 7 + hd + num_splits)
     lens = [0, 1, 31, 32, 33, 200, 1000, 517]
-    B, slots, width = len(lens), 4096, 1024
+    # table width 1100: unsplit, a unit spans 9 tiles (one unit per CTA); split, 3 tiles (persistent CTAs)
+    B, slots, width = len(lens), 4096, 1100
     q, kc, vc, table, seq = _case(gen, B, Hq, Hkv, hd, lens, slots, width)
     dev = torch.device("cuda")
     out = zb.ops.gqa_decode(q.to(dev), kc.to(dev), vc.to(dev), table.to(dev), seq.to(dev), num_splits=num_splits)
@@ -134,3 +135,22 @@ def test_gqa_decode_rising_scores_and_masked_tiles(zb, num_splits):
     out = zb.ops.gqa_decode(q.to(dev), kc.to(dev), vc.to(dev), table.to(dev), seq.to(dev), num_splits=num_splits)
     ref = attention.decode_attention(q, kc, vc, table, seq)
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("Hq,Hkv,num_splits", [(16, 4, 1), (16, 4, 3), (8, 8, 1)])
+def test_gqa_decode_many_units_per_cta(zb, Hq, Hkv, num_splits):
+    """More (request, KV head, split) units than SMs, so each persistent CTA walks several units of ragged
+    lengths (some empty, some a single partial tile) back to back."""
+    gen = torch.Generator().manual_seed(Hq + Hkv + num_splits)
+    B, hd, width = 96, 128, 640
+    lens = torch.randint(0, width + 1, (B,), generator=gen)
+    lens[::7] = 0
+    lens[1::11] = 1
+    lens[2::13] = width
+    lens = lens.tolist()
+    q, kc, vc, table, seq = _case(gen, B, Hq, Hkv, hd, lens, 20000, width)
+    dev = torch.device("cuda")
+    out = zb.ops.gqa_decode(q.to(dev), kc.to(dev), vc.to(dev), table.to(dev), seq.to(dev), num_splits=num_splits)
+    ref = attention.decode_attention(q, kc, vc, table, seq)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
+    assert all(out[b].float().abs().max().item() == 0.0 for b in range(B) if lens[b] == 0)

@@ -18,6 +18,8 @@
 // normalised bf16 output, with several each split writes its partial to the workspace and a combine kernel merges
 // them. fp32 throughout in this kernel (FA3 rounds P to bf16 before its P.V product, as the tensor-core kernel does;
 // the difference is within bf16 tolerance).
+#include <algorithm>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -265,56 +267,114 @@ int dispatch_group(const AttnParams& p, int G, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Head dim 128: both products on the tensor cores. A CTA per (request, KV head, split) streams the split's keys in
-// 128-position tiles through a 3-stage cp.async ring (each stage a 32 KB K tile, K-major, and a 32 KB V tile,
-// MN-major, both 128B-swizzled). Per tile: S^T = K Q^T (M = 128 positions, N = 16: the group's heads padded with
-// zero rows) into tensor memory; thread t reads the scores of position t; the tile's max per head goes through
-// shared memory; p = 2^(s log2e scale - m) is rounded to bf16 (as FlashAttention-3 rounds P) into a K-major P^T
-// operand; O^T += V^T P^T (M = 128 head dimensions, N = 16) accumulates in tensor memory. The running max is
-// raised only when a tile's max exceeds it by more than 2^8 (the stale max keeps every p <= 256, exact after the
-// final division), so the accumulator is rescaled (tensor-memory load, scale, store) only on such tiles. One
-// thread issues the MMAs; one commit per tile covers the previous tile's O^T update and this tile's S^T, whose
-// completion also frees the ring stage the next load overwrites.
+// Head dim 128: the tensor cores do both products. Warp-specialised, persistent CTAs (one per SM) walk their
+// (request, KV head, split) units back to back:
+//  - four loader warps read the page table one tile ahead and copy each 128-position tile's K and V rows
+//    (thread r: row r's slot; a warp moves two 256-byte rows per instruction in 16-byte pieces) into a 3-stage
+//    ring, 128B-swizzled; every loader thread's copies complete on the stage's mbarrier
+//    (cp.async.mbarrier.arrive.noinc), so no thread waits for its own copies; they also stage each unit's
+//    queries. (TMA tile::gather4 of the 128-byte rows measured 2.6x slower: request-bound.)
+//  - four consumer warps (thread t = position t of the tile, = dimension t of the output): S^T = K Q^T
+//    (M = 128 positions, N = 16: the group's heads zero-padded) lands in tensor memory; each thread reads its
+//    position's scores, the tile max per head goes through shared memory, p = 2^(s log2e scale - m) is rounded to
+//    bf16 (as FlashAttention-3 rounds P) into a K-major P^T operand, and O^T += V^T P^T (M = 128 dimensions,
+//    N = 16; V read MN-major) accumulates in tensor memory. The running max is raised only when a tile's max
+//    exceeds it by more than 2^8 (the stale max keeps every p <= 256 and cancels in the final division), so the
+//    accumulator is rescaled (tensor-memory load, scale, store) only on such tiles.
+// Consumer thread 0 issues the MMAs: O^T(t) then a commit to the stage's "empty" barrier (the loader refills it),
+// then S^T(t + 1) once its stage is full, then a commit to the scores barrier.
 namespace tcattn {
 
 constexpr int kHD = 128;
 constexpr int kTilePos = 128;  // key positions of a tile (tensor-memory lanes of S^T)
 constexpr int kStages = 3;
-constexpr int kN = 16;  // MMA N: the group's query heads, zero-padded
-constexpr uint32_t kKBytes = kTilePos * kHD * 2;  // K-major: 2 blocks of 64 dims x 128 rows x 128 B
-constexpr uint32_t kVBytes = kTilePos * kHD * 2;  // MN-major atoms (8 positions x 64 dims), [pos / 8][dim / 64]
-constexpr uint32_t kVLbo = 1024, kVSbo = 2048;    // atom strides along dims (M) and positions (K)
+constexpr int kN = 16;                         // MMA N: the group's query heads, zero-padded
+constexpr int kConsumers = 4;                  // consumer warps (0-3: one per tensor-memory lane quarter)
+constexpr int kLoaders = 4;                    // loader warps (4-7)
+constexpr int kThreadsTma = 32 * (kConsumers + kLoaders);
+constexpr uint32_t kBlkBytes = kTilePos * 128;  // one 64-dim block of a tile: 128 rows x 128 B
+constexpr uint32_t kKBytes = 2 * kBlkBytes;     // K tile (K-major for S^T)
+constexpr uint32_t kVBytes = 2 * kBlkBytes;     // V tile, same layout (MN-major for O^T)
 constexpr uint32_t kStageBytes = kKBytes + kVBytes;
 constexpr uint32_t kPBytes = kN * kTilePos * 2;  // P^T: 16 head rows x 128 positions, 2 K-major blocks
 constexpr uint32_t kQBytes = kN * kHD * 2;       // Q: 16 head rows x 128 dims, 2 K-major blocks
 constexpr uint32_t kBlk16 = kN * 128;            // one 64-wide K block of a 16-row operand
+constexpr int kQBufs = kStages;                  // a unit's queries stay until its last S^T completed
 constexpr uint32_t kOffP = kStages * kStageBytes;
 constexpr uint32_t kOffQ = kOffP + 2 * kPBytes;
-constexpr uint32_t kOffTail = kOffQ + kQBytes;
+constexpr uint32_t kOffTail = kOffQ + kQBufs * kQBytes;
 constexpr uint32_t kColS = 0, kColO = 16, kTmemCols = 32;
+constexpr int kMaxUnits = 64;  // units one CTA walks at most (the grid grows past one CTA per SM beyond that)
 
 struct Tail {
-  float red[2][kWarps][kN];  // per-warp tile max of each head (double-buffered across tiles)
-  float lsum[kWarps][kN];    // per-warp denominators
-  uint64_t bar;              // MMA completion
+  int ulen[kMaxUnits];               // key count of each of this CTA's units (clamped to max_seq_len)
+  unsigned mask[kStages][kLoaders];  // per stage: bit b of word w = position 32 w + b holds a key
+  float red[2][kConsumers][kN];      // per-warp tile max of each head (double-buffered across tiles)
+  float lsum[kConsumers][kN];        // per-warp denominators
+  uint64_t full[kStages];            // every loader thread's copies of the stage landed (+ the mask's arrival)
+  uint64_t empty[kStages];           // the stage's O^T update completed
+  uint64_t sbar;                     // S^T completed
   uint32_t tmem;
   int abort;
 };
 constexpr size_t kSmem = kOffTail + sizeof(Tail) + 1024;  // + slack to 1024-align the base
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+// 16 bytes global -> shared; valid == false writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid = true) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrives on `bar` once every cp.async this thread issued before has completed (counts as one expected arrival).
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
+
+// Bounded wait that gives up at once after any earlier expiry in the CTA (flag in shared memory).
+__device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, int* abort, unsigned* status) {
+  if (*reinterpret_cast<volatile int*>(abort) != 0) return false;
+  if (zb::mbar_wait_bounded(bar, parity, status, zb::kStatusAttnDecodeTimeout)) return true;
+  *reinterpret_cast<volatile int*>(abort) = 1;
+  return false;
 }
 
 }  // namespace tcattn
 
+// Work unit = (request, KV head, split); unit u -> b = u / (Hkv * splits), kvh = u / splits % Hkv,
+// split = u % splits. CTA c takes units c, c + gridDim.x, ... in order; a cursor walks their tiles.
+struct Cursor {
+  int u, j;  // unit (>= units: past the end) and tile within it
+  int b, kvh, split, begin, end, ntiles;
+};
+
+// ulen: the key counts of this CTA's units, staged in shared memory.
+__device__ __forceinline__ void unit_info(const AttnParams& p, const int* ulen, Cursor& c) {
+  c.split = c.u % p.splits;
+  c.kvh = c.u / p.splits % p.Hkv;
+  c.b = c.u / (p.splits * p.Hkv);
+  const int len = ulen[(c.u - (int)blockIdx.x) / (int)gridDim.x];
+  c.begin = c.split * p.split_len;
+  c.end = min(len, c.begin + p.split_len);
+  c.ntiles = c.end > c.begin ? (c.end - c.begin + tcattn::kTilePos - 1) / tcattn::kTilePos : 0;
+}
+// From unit c.u on, the first unit with a tile (c.u >= units when none is left).
+__device__ __forceinline__ void seek(const AttnParams& p, const int* ulen, Cursor& c, int units) {
+  for (; c.u < units; c.u += gridDim.x) {
+    unit_info(p, ulen, c);
+    if (c.ntiles > 0) return;
+  }
+}
+__device__ __forceinline__ void advance(const AttnParams& p, const int* ulen, Cursor& c, int units) {
+  if (++c.j == c.ntiles) {
+    c.j = 0;
+    c.u += gridDim.x;
+    seek(p, ulen, c, units);
+  }
+}
+
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1) gqa_decode_tc_kernel(AttnParams p) {
+__global__ void __launch_bounds__(tcattn::kThreadsTma, 1)
+    gqa_decode_tc_kernel(AttnParams p) {
   using namespace tcattn;
   namespace tc = zb::tc;
   zb::pdl_enter();
@@ -323,212 +383,275 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_tc_kernel(AttnParams p
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
   Tail& tl = *reinterpret_cast<Tail*>(gbase + kOffTail);
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int len = min(max(p.seq_lens[b], 0), p.max_seq_len);
-  const int begin = split * p.split_len, end = min(len, begin + p.split_len);
-  const int ntiles = end > begin ? (end - begin + kTilePos - 1) / kTilePos : 0;
-  const int32_t* table = p.page_table + (int64_t)b * p.table_stride;
-  const uint32_t bar = zb::smem_addr(&tl.bar);
+  const int units = p.B * p.Hkv * p.splits;
+  auto full = [&](int s) { return zb::smem_addr(&tl.full[s]); };
+  auto empty = [&](int s) { return zb::smem_addr(&tl.empty[s]); };
+  const uint32_t sbar = zb::smem_addr(&tl.sbar);
 
-  // P^T buffers zeroed once (rows >= G stay zero); Q staged with rows >= G zero
-  for (int i = tid; i < (int)(2 * kPBytes / 16); i += kThreads) {
+  // This CTA's key counts in one parallel read; units without keys get their zero output (or empty partial) now.
+  for (int i = tid; i < kMaxUnits; i += kThreadsTma) {
+    const int u = (int)blockIdx.x + i * (int)gridDim.x;
+    tl.ulen[i] = u < units ? min(max(p.seq_lens[u / (p.splits * p.Hkv)], 0), p.max_seq_len) : 0;
+  }
+  // P^T and Q buffers zeroed once (rows >= G stay zero)
+  for (int i = tid; i < (int)((2 * kPBytes + kQBufs * kQBytes) / 16); i += kThreadsTma) {
     reinterpret_cast<uint4*>(gbase + kOffP)[i] = make_uint4(0, 0, 0, 0);
   }
-  for (int i = tid; i < kN * 16; i += kThreads) {
-    const int r = i / 16, c = i % 16;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) {
-      v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride + (int64_t)(kvh * G + r) * kHD + c * 8);
-    }
-    *reinterpret_cast<uint4*>(gbase + kOffQ + (c / 8) * kBlk16 + tc::sw128(r, c % 8)) = v;
-  }
   if (tid == 0) {
-    zb::mbar_init(bar, 1);
+    for (int s = 0; s < kStages; ++s) {
+      zb::mbar_init(full(s), kLoaders * 32 + kLoaders);
+      zb::mbar_init(empty(s), 1);
+    }
+    zb::mbar_init(sbar, 1);
     zb::fence_mbar_init();
     tl.abort = 0;
   }
   if (warp == 0) tc::alloc(zb::smem_addr(&tl.tmem), kTmemCols);
-
-  // tile j -> ring stage j % kStages; this thread's row (32 * warp + lane) also records whether it holds a key.
-  // The slot of the thread's row is read one tile ahead, so its latency is off the path that issues the copies.
-  auto read_slot = [&](int j) {
-    const int pos = begin + j * kTilePos + tid;
-    return j < ntiles && pos < end ? table[pos] : -1;
-  };
-  unsigned live = 0;
-  int slot_ahead = read_slot(0);
-  auto load_tile = [&](int j) {
-    if (j < ntiles) {
-      const uint32_t kb = base + (uint32_t)(j % kStages) * kStageBytes, vb = kb + kKBytes;
-      const int slot = slot_ahead;
-      slot_ahead = read_slot(j + 1);
-      const bool valid = slot >= 0 && slot < p.num_slots;
-      live = (live & ~(1u << (j % kStages))) | ((valid ? 1u : 0u) << (j % kStages));
-      const int mine = valid ? slot : -1;
-#pragma unroll 4
-      for (int it = 0; it < 16; ++it) {  // two rows per pass: 16 lanes x 16 bytes of each 256-byte row
-        const int rl = 2 * it + lane / 16, c = lane % 16;
-        const int rs = __shfl_sync(0xffffffffu, mine, rl);
-        const int r = 32 * warp + rl;
-        const bool ok = rs >= 0;
-        const int64_t off = (int64_t)(ok ? rs : 0) * p.slot_stride + (int64_t)kvh * kHD + c * 8;
-        cp_async16(kb + (uint32_t)(c / 8) * (kTilePos * 128) + tc::sw128(r, c % 8), p.k_cache + off, ok);
-        cp_async16(vb + (uint32_t)(r / 8) * kVSbo + (uint32_t)(c / 8) * kVLbo + tc::sw128(r % 8, c % 8),
-                   p.v_cache + off, ok);
-      }
-    }
-    cp_async_commit();
-  };
-  for (int j = 0; j < kStages - 1; ++j) load_tile(j);
-  cp_async_wait<kStages - 2>();
-  tc::fence_proxy_async();
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  const uint32_t tmem = tl.tmem;
-  const uint32_t tlane = tmem + ((uint32_t)(32 * warp) << 16);
-  constexpr uint32_t kIdS = tc::idesc_bf16(128, kN);
-  constexpr uint32_t kIdO = tc::idesc_bf16(128, kN, /*a_mn=*/true);
-  auto issue_s = [&](int j) {  // S^T(j) = K(j) Q^T
-    const uint32_t kb = base + (uint32_t)(j % kStages) * kStageBytes;
+  const int* ulen = tl.ulen;
+  int total = 0;
+  if (warp < kConsumers) {
+    for (Cursor c{(int)blockIdx.x, 0}; c.u < units; c.u += gridDim.x) {
+      unit_info(p, ulen, c);
+      total += c.ntiles;
+      if (c.ntiles > 0) continue;
 #pragma unroll
-    for (int ks = 0; ks < kHD / 16; ++ks) {
-      tc::mma(tmem + kColS, tc::desc_kmajor(kb + (ks / 4) * (kTilePos * 128) + (ks % 4) * 32),
-              tc::desc_kmajor(base + kOffQ + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdS, ks > 0);
-    }
-  };
-  auto issue_o = [&](int j, bool accumulate) {  // O^T += V(j)^T P(j)^T
-    const uint32_t vb = base + (uint32_t)(j % kStages) * kStageBytes + kKBytes;
-    const uint32_t pb = base + kOffP + (uint32_t)(j & 1) * kPBytes;
-#pragma unroll
-    for (int ks = 0; ks < kTilePos / 16; ++ks) {
-      tc::mma(tmem + kColO, tc::desc_mnmajor(vb + ks * 2 * kVSbo, kVLbo, kVSbo),
-              tc::desc_kmajor(pb + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdO, accumulate || ks > 0);
-    }
-  };
-  if (tid == 0 && ntiles > 0) {
-    issue_s(0);
-    tc::commit(bar);
-  }
-
-  float m_run[G], l_part[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m_run[g] = -INFINITY;
-    l_part[g] = 0.f;
-  }
-  bool aborted = false;
-  for (int i = 0; i < ntiles; ++i) {
-    // S^T(i) and O^T(i - 1) complete: stage (i - 1) % kStages is free for tile i + kStages - 1
-    if (!aborted && !zb::mbar_wait_bounded(bar, (uint32_t)(i & 1), p.status, zb::kStatusAttnDecodeTimeout)) {
-      tl.abort = 1;
-    }
-    tc::fence_after();
-    load_tile(i + kStages - 1);
-    uint32_t sr[16];
-    tc::ld16(tlane + kColS, sr);
-    tc::ld_wait();
-    const bool valid = (live >> (i % kStages)) & 1u;
-    float x[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      x[g] = valid ? __uint_as_float(sr[g]) * p.scale_log2 : -INFINITY;
-      const float wm = zb::warp_max(x[g]);
-      if (lane == 0) tl.red[i & 1][warp][g] = wm;
-    }
-    __syncthreads();
-    aborted = *reinterpret_cast<volatile int*>(&tl.abort) != 0;
-    bool rescale = false;
-    float corr[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mt = tl.red[i & 1][0][g];
-#pragma unroll
-      for (int w = 1; w < kWarps; ++w) mt = fmaxf(mt, tl.red[i & 1][w][g]);
-      corr[g] = 1.f;
-      if (mt > m_run[g] + 8.f) {  // never true while both are -inf
-        corr[g] = exp2f(m_run[g] - mt);  // 0 for the first tile with a key
-        m_run[g] = mt;
-        rescale = true;
-      }
-    }
-    if (rescale) {  // the same decision on every thread (same maxima, same history)
-#pragma unroll
-      for (int g = 0; g < G; ++g) l_part[g] *= corr[g];
-      if (i > 0) {
-        uint32_t o[16];
-        tc::ld16(tlane + kColO, o);
-        tc::ld_wait();
-#pragma unroll
-        for (int g = 0; g < G; ++g) o[g] = __float_as_uint(__uint_as_float(o[g]) * corr[g]);
-        tc::st16(tlane + kColO, o);
-        tc::st_wait();
-      }
-    }
-    unsigned char* pbuf = gbase + kOffP + (i & 1) * kPBytes + (tid / 64) * kBlk16 + (tid % 64 % 8) * 2;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float pv = x[g] == -INFINITY ? 0.f : exp2f(x[g] - m_run[g]);
-      l_part[g] += pv;
-      *reinterpret_cast<__nv_bfloat16*>(pbuf + tc::sw128(g, (tid % 64) / 8)) = __float2bfloat16_rn(pv);
-    }
-    cp_async_wait<kStages - 2>();  // tile i + 1 landed (this thread's pieces)
-    tc::fence_proxy_async();
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
-    if (tid == 0) {
-      issue_o(i, i > 0);
-      if (i + 1 < ntiles) issue_s(i + 1);
-      tc::commit(bar);
-    }
-  }
-
-  float o_val[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) o_val[g] = 0.f;
-  if (ntiles > 0) {
-    if (!aborted && !zb::mbar_wait_bounded(bar, (uint32_t)(ntiles & 1), p.status, zb::kStatusAttnDecodeTimeout)) {
-      tl.abort = 1;
-    }
-    tc::fence_after();
-    uint32_t o[16];
-    tc::ld16(tlane + kColO, o);
-    tc::ld_wait();
-#pragma unroll
-    for (int g = 0; g < G; ++g) o_val[g] = __uint_as_float(o[g]);
-  }
-  cp_async_wait<0>();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float s = zb::warp_sum(l_part[g]);
-    if (lane == 0) tl.lsum[warp][g] = s;
-  }
-  tc::fence_before();
-  __syncthreads();
-  if (*reinterpret_cast<volatile int*>(&tl.abort) == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float L = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) L += tl.lsum[w][g];
-      const int h = kvh * G + g;
-      if (p.splits == 1) {
-        p.out[(int64_t)b * p.out_stride + (int64_t)h * kHD + tid] = __float2bfloat16_rn(L > 0.f ? o_val[g] / L : 0.f);
-      } else {
-        float* part = p.part + (((int64_t)b * p.Hq + h) * p.splits + split) * (kHD + 2);
-        part[tid] = L > 0.f ? o_val[g] : 0.f;
-        if (tid == 0) {
-          part[kHD] = m_run[g];
-          part[kHD + 1] = L;
+      for (int g = 0; g < G; ++g) {
+        const int h = c.kvh * G + g;
+        if (p.splits == 1) {
+          p.out[(int64_t)c.b * p.out_stride + (int64_t)h * kHD + tid] = __float2bfloat16_rn(0.f);
+        } else {
+          float* part = p.part + (((int64_t)c.b * p.Hq + h) * p.splits + c.split) * (kHD + 2);
+          part[tid] = 0.f;
+          if (tid == 0) {
+            part[kHD] = -INFINITY;
+            part[kHD + 1] = 0.f;
+          }
         }
       }
     }
   }
-  if (warp == 0) {
-    tc::fence_after();
-    tc::dealloc(tmem, kTmemCols);
+
+  if (warp >= kConsumers) {
+    // ------------------------------------------------------------------ loader warps
+    const int r = tid - kConsumers * 32, lw = r / 32;  // this thread's tile row; loader warp index
+    Cursor lc{(int)blockIdx.x, 0};
+    seek(p, ulen, lc, units);
+    auto read_slot = [&](const Cursor& c) {
+      const int pos = c.begin + c.j * kTilePos + r;
+      return c.u < units && pos < c.end ? p.page_table[(int64_t)c.b * p.table_stride + pos] : -1;
+    };
+    int ahead = read_slot(lc);
+    int unit_no = 0;
+    for (int j = 0; lc.u < units; ++j) {
+      const int stage = j % kStages;
+      if (j >= kStages) wait(empty(stage), (uint32_t)((j / kStages - 1) & 1), &tl.abort, p.status);
+      const bool valid = ahead >= 0 && ahead < p.num_slots;
+      const unsigned bits = __ballot_sync(0xffffffffu, valid);
+      const int mine = valid ? ahead : -1;
+      const uint32_t kb = base + (uint32_t)stage * kStageBytes, vb = kb + kKBytes;
+      const int64_t head = (int64_t)lc.kvh * kHD;
+#pragma unroll 4
+      for (int it = 0; it < 16; ++it) {  // two rows per pass: 16 lanes x 16 bytes of each 256-byte row
+        const int rl = 2 * it + lane / 16, c = lane % 16;
+        const int rs = __shfl_sync(0xffffffffu, mine, rl);
+        const bool ok = rs >= 0;  // a masked row is zero-filled: its p is 0, and 0 x V must stay 0
+        const int64_t off = (int64_t)(ok ? rs : 0) * p.slot_stride + head + c * 8;
+        const uint32_t o = (uint32_t)(c / 8) * kBlkBytes + tc::sw128(32 * lw + rl, c % 8);
+        cp_async16(kb + o, p.k_cache + off, ok);
+        cp_async16(vb + o, p.v_cache + off, ok);
+      }
+      if (lc.j == 0) {  // the unit's queries (rows < G) into its Q buffer
+        if (r < G * 16) {
+          const int qr = r / 16, c = r % 16;
+          cp_async16(base + kOffQ + (uint32_t)(unit_no % kQBufs) * kQBytes + (uint32_t)(c / 8) * kBlk16 +
+                         tc::sw128(qr, c % 8),
+                     p.q + (int64_t)lc.b * p.q_stride + (int64_t)(lc.kvh * G + qr) * kHD + c * 8);
+        }
+        ++unit_no;
+      }
+      cp_async_arrive(full(stage));
+      if (lane == 0) {  // the mask word, published by a plain (release) arrival of each loader warp
+        tl.mask[stage][lw] = bits;
+        zb::mbar_arrive(full(stage));
+      }
+      advance(p, ulen, lc, units);
+      ahead = read_slot(lc);
+    }
+  } else {
+    // ------------------------------------------------------------------ consumer warps
+    const uint32_t tmem = tl.tmem;
+    const uint32_t tlane = tmem + ((uint32_t)(32 * warp) << 16);
+    constexpr uint32_t kIdS = tc::idesc_bf16(128, kN);
+    constexpr uint32_t kIdO = tc::idesc_bf16(128, kN, /*a_mn=*/true);
+    auto issue_s = [&](int t, int qbuf) {  // S^T(t) = K(t) Q^T
+      const uint32_t kb = base + (uint32_t)(t % kStages) * kStageBytes;
+      const uint32_t qb = base + kOffQ + (uint32_t)qbuf * kQBytes;
+#pragma unroll
+      for (int ks = 0; ks < kHD / 16; ++ks) {
+        tc::mma(tmem + kColS, tc::desc_kmajor(kb + (ks / 4) * kBlkBytes + (ks % 4) * 32),
+                tc::desc_kmajor(qb + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdS, ks > 0);
+      }
+    };
+    auto issue_o = [&](int t, bool accumulate) {  // O^T (+)= V(t)^T P(t)^T; V atoms: 16 KB apart along dims
+      const uint32_t vb = base + (uint32_t)(t % kStages) * kStageBytes + kKBytes;
+      const uint32_t pb = base + kOffP + (uint32_t)(t & 1) * kPBytes;
+#pragma unroll
+      for (int ks = 0; ks < kTilePos / 16; ++ks) {
+        tc::mma(tmem + kColO, tc::desc_mnmajor(vb + ks * 2048, kBlkBytes, 1024),
+                tc::desc_kmajor(pb + (ks / 4) * kBlk16 + (ks % 4) * 32), kIdO, accumulate || ks > 0);
+      }
+    };
+    if (tid == 0 && total > 0) {
+      wait(full(0), 0, &tl.abort, p.status);
+      tc::fence_proxy_async();  // the loaders' copies (generic proxy) -> the tensor core's reads
+      tc::fence_after();
+      issue_s(0, 0);
+      tc::commit(sbar);
+    }
+
+    Cursor cc{(int)blockIdx.x, 0};
+    seek(p, ulen, cc, units);
+    Cursor done = cc;  // the unit whose accumulator is read next
+    int cunits = 0;
+    float m_run[G], l_part[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m_run[g] = -INFINITY;
+      l_part[g] = 0.f;
+    }
+    auto finish = [&](const Cursor& u, const float (&o)[G], const float (&m)[G]) {
+      if (*reinterpret_cast<volatile int*>(&tl.abort) != 0) return;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumers; ++w) L += tl.lsum[w][g];
+        const int h = u.kvh * G + g;
+        if (p.splits == 1) {
+          p.out[(int64_t)u.b * p.out_stride + (int64_t)h * kHD + tid] =
+              __float2bfloat16_rn(L > 0.f ? o[g] / L : 0.f);
+        } else {
+          float* part = p.part + (((int64_t)u.b * p.Hq + h) * p.splits + u.split) * (kHD + 2);
+          part[tid] = L > 0.f ? o[g] : 0.f;
+          if (tid == 0) {
+            part[kHD] = m[g];
+            part[kHD + 1] = L;
+          }
+        }
+      }
+    };
+    auto close_unit = [&](float (&o)[G], float (&m)[G]) {
+      uint32_t r[16];
+      tc::ld16(tlane + kColO, r);
+      tc::ld_wait();
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        o[g] = __uint_as_float(r[g]);
+        m[g] = m_run[g];
+        const float s = zb::warp_sum(l_part[g]);
+        if (lane == 0) tl.lsum[warp][g] = s;
+        m_run[g] = -INFINITY;
+        l_part[g] = 0.f;
+      }
+    };
+
+    for (int t = 0; t < total; ++t) {
+      const int stage = t % kStages;
+      // S^T(t) complete (and O^T(t - 1) before it); the stage's barrier also publishes its key mask
+      wait(sbar, (uint32_t)(t & 1), &tl.abort, p.status);
+      wait(full(stage), (uint32_t)((t / kStages) & 1), &tl.abort, p.status);
+      tc::fence_after();
+      const bool first = cc.j == 0;
+      float o_prev[G], m_prev[G];
+      if (first && t > 0) close_unit(o_prev, m_prev);
+      uint32_t sr[16];
+      tc::ld16(tlane + kColS, sr);
+      tc::ld_wait();
+      const bool valid = (tl.mask[stage][tid / 32] >> (tid % 32)) & 1u;
+      float x[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        x[g] = valid ? __uint_as_float(sr[g]) * p.scale_log2 : -INFINITY;
+        const float wm = zb::warp_max(x[g]);
+        if (lane == 0) tl.red[t & 1][warp][g] = wm;
+      }
+      consumer_sync();
+      if (first && t > 0) {
+        finish(done, o_prev, m_prev);
+        done = cc;
+      }
+      bool rescale = false;
+      float corr[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float mt = tl.red[t & 1][0][g];
+#pragma unroll
+        for (int w = 1; w < kConsumers; ++w) mt = fmaxf(mt, tl.red[t & 1][w][g]);
+        corr[g] = 1.f;
+        if (mt > m_run[g] + 8.f) {  // never true while both are -inf
+          corr[g] = exp2f(m_run[g] - mt);  // 0 for the unit's first tile with a key
+          m_run[g] = mt;
+          rescale = true;
+        }
+      }
+      if (rescale) {  // the same decision on every thread (same maxima, same history)
+#pragma unroll
+        for (int g = 0; g < G; ++g) l_part[g] *= corr[g];
+        if (!first) {  // a unit's first O^T update overwrites the accumulator
+          uint32_t o[16];
+          tc::ld16(tlane + kColO, o);
+          tc::ld_wait();
+#pragma unroll
+          for (int g = 0; g < G; ++g) o[g] = __float_as_uint(__uint_as_float(o[g]) * corr[g]);
+          tc::st16(tlane + kColO, o);
+          tc::st_wait();
+        }
+      }
+      unsigned char* pbuf = gbase + kOffP + (t & 1) * kPBytes + (tid / 64) * kBlk16 + (tid % 8) * 2;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pv = x[g] == -INFINITY ? 0.f : exp2f(x[g] - m_run[g]);
+        l_part[g] += pv;
+        *reinterpret_cast<__nv_bfloat16*>(pbuf + tc::sw128(g, (tid % 64) / 8)) = __float2bfloat16_rn(pv);
+      }
+      advance(p, ulen, cc, units);
+      const int next_q = cunits + (cc.j == 0 ? 1 : 0);  // Q buffer of tile t + 1's unit
+      tc::fence_proxy_async();
+      tc::fence_before();
+      consumer_sync();
+      tc::fence_after();
+      if (tid == 0) {
+        issue_o(t, !first);
+        tc::commit(empty(stage));
+        if (t + 1 < total) {
+          wait(full((t + 1) % kStages), (uint32_t)(((t + 1) / kStages) & 1), &tl.abort, p.status);
+          tc::fence_proxy_async();
+          tc::fence_after();
+          issue_s(t + 1, next_q % kQBufs);
+          tc::commit(sbar);
+        }
+      }
+      cunits = next_q;
+    }
+
+    if (total > 0) {
+      wait(empty((total - 1) % kStages), (uint32_t)(((total - 1) / kStages) & 1), &tl.abort, p.status);
+      tc::fence_after();
+      float o_last[G], m_last[G];
+      close_unit(o_last, m_last);
+      consumer_sync();
+      finish(done, o_last, m_last);
+    }
+    tc::fence_before();
+    consumer_sync();
+    if (warp == 0) {
+      tc::fence_after();
+      tc::dealloc(tmem, kTmemCols);
+    }
   }
 }
 
@@ -542,8 +665,11 @@ int launch_attn_tc(const AttnParams& p, cudaStream_t stream) {
     ZB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcattn::kSmem));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  ZB_CUDA(zb::launch(kernel, dim3((unsigned)p.splits, (unsigned)p.Hkv, (unsigned)p.B), dim3(kThreads),
-                     tcattn::kSmem, stream, 1, p));
+  // persistent: one CTA per SM (the ring takes most of its shared memory), each walking its units in turn
+  const int64_t units = (int64_t)p.B * p.Hkv * p.splits;
+  const int64_t per_cta_limit = (units + tcattn::kMaxUnits - 1) / tcattn::kMaxUnits;
+  const unsigned grid = (unsigned)std::max<int64_t>(std::min<int64_t>(units, zb::sm_count()), per_cta_limit);
+  ZB_CUDA(zb::launch(kernel, dim3(grid), dim3(tcattn::kThreadsTma), tcattn::kSmem, stream, 1, p));
   if (int rc = zb::check_launch("gqa_decode")) return rc;
   if (p.splits > 1) {
     ZB_CUDA(zb::launch(gqa_combine_kernel<128>, dim3((unsigned)p.Hq, (unsigned)p.B), dim3(128), 0, stream, 1, p));
@@ -615,6 +741,7 @@ ZB_API int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_
   const int G = Hq / Hkv;
   if (hd == 128) {
     ZB_REQUIRE(q_stride % 8 == 0, "gqa_decode: q_stride %lld must be a multiple of 8", (long long)q_stride);
+    ZB_REQUIRE(num_slots >= 1, "gqa_decode: an empty cache (num_slots %lld)", (long long)num_slots);
     ZB_REQUIRE_ALIGNED(q, 16, "gqa_decode q");
     switch (G) {
       case 1: return launch_attn_tc<1>(p, stream);
