@@ -561,7 +561,7 @@ def bench_gqa_decode_cfg5(ops, dev, stream, reps=5):
                       stream, reps)
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"splits": s, "us": ms * 1e3, "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"]}
-    res["roofline"] = {"kernel": "gqa_decode_kernel", "bound": "hbm", "achieved": res["unsplit"]["achieved_gbs"],
+    res["roofline"] = {"kernel": "gqa_decode_tc_kernel", "bound": "hbm", "achieved": res["unsplit"]["achieved_gbs"],
                        "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": res["unsplit"]["frac"],
                        "peak_source": pk["source"]}
     return res
