@@ -1,6 +1,7 @@
 """BASELINE config 1 end to end: a tiny random-init hybrid LM (hidden 256; layers [GDN, GDN, GQA, GDN]; GDN 4 heads
 of 64; MoE 8 experts top-2, SwiGLU 512, in every layer; Full AttnRes; vocab 1024) run on the B200 path (the
-drop-in OriginalGDN and MoEFeedForward modules, the AttnRes route kernel with the norms fused, bf16) against the
+drop-in OriginalGDN and MoEFeedForward modules, the AttnRes route kernel with the norms fused, the KV store and
+the decode attention of the GQA layer, bf16) against the
 fp32 oracle LM (oracle/lm.py, pinned to the reference Zonos3LM): a 64-token prompt then greedy decode steps.
 
 Bars: teacher-forced (both models fed the oracle's tokens) logits cosine >= 0.999 at every step; the greedy
@@ -28,12 +29,13 @@ class _W:
 class GQA:
     """The reference's gated GQA with KV cache (lm.py:511-537) in plain torch: not on the north_star path."""
 
-    def __init__(self, c, w, p, dev):
-        self.c = c
+    def __init__(self, c, w, p, dev, zb=None, max_tokens=1024):
+        self.c, self.zb, self.max_tokens = c, zb, max_tokens
         g = lambda n: w[p + n].to(dev, torch.bfloat16)  # noqa: E731
         self.wq, self.wkv, self.wo, self.gater = g("wq.weight"), g("wkv.weight"), g("wo.weight"), g("gater.weight")
         self.temp = w[p + "temp"].to(dev, torch.float32)
         self.k = self.v = None
+        self.kc = self.vc = None  # slot-indexed cache (slot = position) filled through zb.ops.kv_store
         self.position = 0
 
     def forward(self, x):
@@ -56,8 +58,23 @@ class GQA:
             return torch.stack((a * cos - b * sin, a * sin + b * cos), -1).flatten(-2).to(t.dtype)
 
         q, k = rope(q), rope(k)
-        self.k = k if self.k is None else torch.cat((self.k, k))
-        self.v = v if self.v is None else torch.cat((self.v, v))
+        if self.zb is not None:  # the B200 KV store and, for a decode row, the B200 decode attention
+            if self.kc is None:
+                self.kc = torch.zeros(self.max_tokens, nkv, hd, device=x.device, dtype=x.dtype)
+                self.vc = torch.zeros_like(self.kc)
+            slots = torch.arange(self.position, self.position + n, device=x.device, dtype=torch.int32)
+            self.zb.ops.kv_store(self.kc, self.vc, slots, k, v)
+            if n == 1:
+                table = torch.arange(self.max_tokens, device=x.device, dtype=torch.int32)[None]
+                seq = torch.tensor([self.position + 1], device=x.device, dtype=torch.int32)
+                out = self.zb.ops.gqa_decode(q, self.kc, self.vc, table, seq, softmax_scale=hd ** -0.5)
+                self.position += n
+                return F.linear((out * gate.unsqueeze(-1)).reshape(n, nh * hd), self.wo)
+            k, v = self.kc[: self.position + n], self.vc[: self.position + n]
+            self.k, self.v = k, v
+        else:
+            self.k = k if self.k is None else torch.cat((self.k, k))
+            self.v = v if self.v is None else torch.cat((self.v, v))
         rep = nh // nkv
         key = self.k.repeat_interleave(rep, 1).transpose(0, 1)
         value = self.v.repeat_interleave(rep, 1).transpose(0, 1)
@@ -96,7 +113,7 @@ class B200LM:
                 gdn.allocate_cache(1, dev, torch.bfloat16)
                 layer.attention = gdn
             else:
-                layer.attention = GQA(c, w, p + "attention.", dev)
+                layer.attention = GQA(c, w, p + "attention.", dev, zb)
             ff = zb.moe.MoEFeedForward(mcfg, i)
             ff.load_state_dict({k[len(p + "feed_forward."):]: v for k, v in w.items()
                                 if k.startswith(p + "feed_forward.")})
