@@ -525,6 +525,133 @@ def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5)
     }
 
 
+def full_step_cfg5(pkg, dev, streams=256, context=878, n_layers=24):
+    """Builds one cfg5 decode step of the whole 24-layer backbone for `streams` streams (one new row each): layers in
+    the 3:1 DeltaNet:GQA pattern (layer i is GQA when i % 4 == 3), an MoE FFN in every layer and the Full AttnRes
+    schedule (a route before every sublayer and a final one: 49 routes over the layer-output bank, queries
+    registered, norms fused). GQA layers: fused wq / wkv / gater projection, q / k RMS norm with |temp| and
+    interleaved RoPE (plain torch), then `ops.kv_store` of the new row and `ops.gqa_decode` over `context` cached
+    keys + the new one (the mid-run cache of a 128-token prompt + 1500 decode steps; prompt slots contiguous, decode
+    slots interleaved across streams), gate and wo. bf16 random-init weights N(0, 0.02), generated on the device.
+    Embedding and the multi-codebook head / sampler are not included. Returns (step, core, batch)."""
+    ops, core = pkg.ops, pkg.core
+    D, H, d, E, k, I = 2048, 16, 128, 64, 8, 768
+    Hq, Hkv, hd = 16, 4, 128
+    cfg = pkg.config.ModelConfig(hidden_size=D, gdn_num_heads=H, gdn_head_dim=d, moe_n_experts=E, moe_topk=k,
+                                 moe_intermediate_size=I, norm_topk_prob=True, use_training_router_weights=False)
+    gen = torch.Generator(device=dev).manual_seed(23)
+    rnd = lambda *shape, s=0.02: (s * torch.randn(*shape, generator=gen, device=dev)).bfloat16()  # noqa: E731
+    inner = H * d
+    tables = pkg.gdn.OriginalGDN.static_tables(dev, [streams])
+    slots = torch.arange(streams, device=dev, dtype=torch.int64)
+    layers = []
+    _, kc0, vc0, table_gq, seq_gq = gqa_cfg5_inputs(dev, streams, 128, context + 1, Hq, Hkv, hd)
+    n_slots = kc0.shape[0]
+    del kc0, vc0
+    out_loc = table_gq[:, context].contiguous()  # the new row's slot (the last entry of each request's table)
+    positions = torch.full((streams,), context, device=dev, dtype=torch.float32)
+    freqs = 10000.0 ** (-torch.arange(0, hd, 2, dtype=torch.float32, device=dev) / hd)
+    ang = positions[:, None] * freqs[None, :]
+    cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
+
+    def rope(t):
+        pr = t.float().reshape(*t.shape[:-1], hd // 2, 2)
+        a, b = pr[..., 0], pr[..., 1]
+        return torch.stack((a * cos - b * sin, a * sin + b * cos), -1).flatten(-2).to(t.dtype)
+
+    for i in range(n_layers):
+        if i % 4 == 3:
+            mixer = {"w": rnd(Hq * hd + 2 * Hkv * hd + Hq, D), "wo": rnd(D, Hq * hd), "temp": torch.ones(Hq, device=dev),
+                     "kc": rnd(n_slots, Hkv, hd, s=1.0), "vc": rnd(n_slots, Hkv, hd, s=1.0),
+                     "o": torch.empty(streams, Hq, hd, device=dev, dtype=torch.bfloat16)}
+        else:
+            mixer = pkg.gdn.OriginalGDN(cfg, i)
+            mixer.to(dev, torch.bfloat16)  # device-side parameters: the weights below load without a host trip
+            mixer.load_state_dict({"in_proj.weight": rnd(4 * inner + 2 * H, D),
+                                   "conv.weight": rnd(3 * inner, 1, 4, s=0.3), "out_weight": torch.ones(d).bfloat16(),
+                                   "A_log": torch.zeros(H), "dt_bias": torch.zeros(H), "wo.weight": rnd(D, inner)})
+            mixer.allocate_cache(streams, dev, torch.bfloat16)
+            mixer.enable_graph_decode(slots, tables)
+            mixer.set_static_mode(True)
+        moe = pkg.moe.MoEFeedForward(cfg, i)
+        moe.to(dev, torch.bfloat16)
+        moe.load_state_dict({"router.router_linear.weight": rnd(E, D),
+                             "router.rmsnorm_eda.weight": torch.ones(D, dtype=torch.bfloat16),
+                             "router.balancing_biases": torch.zeros(E), "experts.gate_up_proj": rnd(E, 2 * I, D),
+                             "experts.down_proj": rnd(E, D, I)})
+        layers.append((mixer, moe))
+
+    def gqa(m, x):
+        p = F.linear(x, m["w"])
+        q = p[:, : Hq * hd].view(streams, Hq, hd)
+        kk = p[:, Hq * hd: Hq * hd + Hkv * hd].reshape(streams, Hkv, hd)
+        v = p[:, Hq * hd + Hkv * hd: Hq * hd + 2 * Hkv * hd].reshape(streams, Hkv, hd)
+        gate = p[:, Hq * hd + 2 * Hkv * hd:].sigmoid()
+        q = rope((F.rms_norm(q.float(), (hd,), eps=1e-6) * m["temp"].abs().view(1, Hq, 1)).bfloat16())
+        kk = rope(F.rms_norm(kk.float(), (hd,), eps=1e-6).bfloat16())
+        ops.kv_store(m["kc"], m["vc"], out_loc, kk, v)
+        o = ops.gqa_decode(q, m["kc"], m["vc"], table_gq, seq_gq, out=m["o"])
+        return F.linear((o * gate.unsqueeze(-1)).reshape(streams, Hq * hd), m["wo"])
+
+    n_routes = 2 * n_layers + 1
+    bank = torch.empty(n_routes - 1, streams, D, device=dev, dtype=torch.bfloat16)
+    x0 = torch.randn(streams, D, generator=gen, device=dev).bfloat16()
+    queries = rnd(n_routes, D)
+    norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    table = torch.zeros(n_routes, streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
+    inv_rms = torch.ones(streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
+    h = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
+    final = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
+    batch = core.Batch(reqs=[core.Req(i, 1, cached_len=context) for i in range(streams)], is_decode=True,
+                       padded_size=streams)
+
+    def step():
+        # route r mixes bank[:r] + its source (x0, then each sublayer's output) and appends the source as bank[r];
+        # the final route does not append (forward_layers_full's schedule)
+        source = x0
+        for r in range(n_routes - 1):
+            ops.attnres_route_tabled(bank, r, source, queries, r, table, inv_rms, 1e-5, append_to=bank[r],
+                                     norm_weight=norm_w, out=h)
+            mixer, moe = layers[r // 2]
+            if r % 2 == 0:
+                source = gqa(mixer, h) if isinstance(mixer, dict) else mixer.forward(h)
+            else:
+                source, _ = moe.forward(h)
+        return ops.attnres_route_tabled(bank, n_routes - 1, source, queries, n_routes - 1, table, inv_rms, 1e-5,
+                                        norm_weight=norm_w, out=final)
+
+    return step, core, batch
+
+
+def bench_full_step_cfg5(pkg, dev, stream, streams=256, context=878, reps=3):
+    """cfg5: one decode step of the 24-layer backbone (full_step_cfg5) for 256 streams, captured in one CUDA graph.
+    Weights (15.6 GB of experts alone) far exceed L2; no flush needed."""
+    step, core, batch = full_step_cfg5(pkg, dev, streams, context)
+    with core.forward_batch(batch):
+        ms = graph_ms(step, stream, reps, warmup=2)
+    # Algorithmic bytes of the step (each read or write once): every expert's weights (2048 routed pairs over 64
+    # experts touch all of them), the DeltaNet states and conv histories read and written, the mixers' projection
+    # weights, the KV cache rows, the AttnRes bank reads (route r reads r + 1 rows) and writes.
+    D, H, d, E, I, Hq, Hkv, hd, n_gdn, n_gqa = 2048, 16, 128, 64, 768, 16, 4, 128, 18, 6
+    inner = H * d
+    nbytes = (24 * (E * 3 * I * D * 2 + E * D * 2)
+              + n_gdn * (streams * H * d * d * 4 * 2 + streams * 3 * inner * 3 * 2 * 2
+                         + ((4 * inner + 2 * H) * D + D * inner) * 2)
+              + n_gqa * (streams * (context + 1) * Hkv * hd * 2 * 2
+                         + ((Hq * hd + 2 * Hkv * hd + Hq) * D + D * Hq * hd) * 2)
+              + sum(r + 2 for r in range(49)) * streams * D * 2)
+    pk = peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {
+        "workload": f"cfg5 decode step of the backbone: {streams} streams, 24 layers (18 DeltaNet 16 x 128/128, "
+                    f"6 GQA 16/4 x 128 over {context} cached keys + the new one), MoE 64 experts top-8 I=768 in "
+                    "every layer, Full AttnRes (49 routes); embedding and head / sampler excluded; CUDA graph",
+        "step_ms": ms, "tokens_per_s": streams / (ms / 1e3),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / pk["hbm_gbs"], "algorithmic_bytes": nbytes, "peak_source": pk["source"]},
+    }
+
+
 def gqa_cfg5_inputs(dev, streams=256, prompt=128, context=1628, Hq=16, Hkv=4, hd=128, seed=5):
     """cfg5 global-attention decode at the end of the run: `streams` requests, each with `context` cached keys
     (the 128-token prompt, then 1500 decode steps). Slots as a token pool hands them out: each prompt a contiguous
@@ -632,7 +759,7 @@ def cpu_reference(updates: int, streams=STREAMS):
 def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
     updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5
-    DeltaNet + MoE decode layers, or cfg5 GQA decode attention."""
+    DeltaNet + MoE decode layers, cfg5 GQA decode attention, or cfg5 backbone decode steps."""
     ops = __import__("__graft_entry__").load_package().ops
     dev = torch.device("cuda", 0)
     if workload == "moe":
@@ -670,6 +797,14 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
             ops.gdn_chunk_prefill(q, k, v, g, beta, cu)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg3 chunked prefills done")
+        return
+    if workload == "full_step":
+        step, core, batch = full_step_cfg5(__import__("__graft_entry__").load_package(), dev)
+        with core.forward_batch(batch):
+            for _ in range(n):
+                step()
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg5 backbone decode steps done")
         return
     if workload == "gqa_decode":
         q, kc, vc, table, seq = gqa_cfg5_inputs(dev)
@@ -718,7 +853,8 @@ def main():
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
     ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill",
-                                                                         "decode_layer", "gqa_decode"),
+                                                                         "decode_layer", "gqa_decode",
+                                                                         "full_step"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
@@ -767,6 +903,7 @@ def main():
                     "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
                     "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
                     "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
+                    "full_step_cfg5": bench_full_step_cfg5(__import__("__graft_entry__").load_package(), dev, stream),
                     "decode_layer_cfg5": bench_decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev,
                                                                  stream),
                 }
