@@ -248,6 +248,25 @@ int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, 
                   int splits, int split_len, float* workspace, int64_t workspace_bytes, uint16_t* out,
                   int64_t out_stride, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------------------------- TTS sampler */
+
+/* Next audio codes from per-codebook logits [B, C, V] (rows of V, row stride row_stride elements; bf16 when
+ * logits_fp32 == 0, else fp32), one row per (request, codebook): invalid ids masked (audio_pad_id; ids >=
+ * codebook_size other than stop_ids[b]; ids past codebook_sizes[c] (NULL: codebook_size); the stop id while
+ * stop_blocked[b, c] (NULL: never)), stop_bias[b] added to the stop id (NULL: none), repetition penalty
+ * rep_penalties[b] over rep_ids[b, c, 0..W) (NULL / W = 0: none), then greedy argmax when `greedy` (every
+ * temperature <= 0) or temperature[b], top_k (0 or >= V: off), softmax, top_p (in (0, 1)), min_p (> 0) and one
+ * multinomial draw from Philox4x32-10 keyed by `seed` at counter (row, offset). top_k / top_p / min_p are the batch's
+ * min / max / max, as the reference reduces them on the host. out [B, C + 1] int32: the codes, then text_vocab.
+ * probs_out (NULL: not written) [B * C, V] fp32 receives each row's final distribution. V <= 16384.
+ * Replaces sample_tts (model/src/zonos3/tts/sampler.py:159-372; ids drawn from a different random stream than
+ * torch.multinomial, equal in distribution). */
+int zb_sample_tts(const void* logits, int logits_fp32, int64_t row_stride, int B, int C, int V,
+                  const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
+                  int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes, const uint8_t* stop_blocked,
+                  const float* stop_bias, const int32_t* rep_ids, int W, const float* rep_penalties, uint64_t seed,
+                  uint64_t offset, int text_vocab, int32_t* out, float* probs_out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,7 @@ implementation of the three hot-path parts, each function citing the reference f
   kernel's rounding points, servers/sgl/.../models/training_attnres_kernels.py:1268-1348)
 * ``oracle.moe``     — router, top-k, permutation and SwiGLU experts (lm.py:604-639; zonos3.py:746-828;
   layers/moe/fused_moe/layer.py:159-161)
+* ``oracle.sampler`` — the TTS sampler's masks, penalty and filters (model/src/zonos3/tts/sampler.py:59-372)
 * ``oracle.attention`` — decode attention over a slot-indexed KV cache and the KV store (lm.py:526-531;
   servers/sgl/.../attention/fa.py:64-81; servers/sgl/.../kernel/csrc/jit/store.cu:28-50)
 

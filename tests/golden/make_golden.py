@@ -19,6 +19,9 @@ reference at run time. What each file pins:
   layer, dense FFN then MoE, Full AttnRes, dim 32): every weight, a 12-row prompt and two 1-row decode calls, and
   the softcapped logits of all three calls.
 
+* ``sampler.npz``    — ``sample_tts`` (model/src/zonos3/tts/sampler.py:159-372): seeded logits with masks, stop
+  bias and repetition penalty, and the ids the reference drew (greedy and seeded multinomial) for four settings.
+
 ``python tests/golden/make_golden.py /path/to/reference [fixture ...]`` regenerates only the named fixtures.
 """
 
@@ -189,7 +192,46 @@ def lm_fixture(lm):
     np.savez_compressed(HERE / "lm_tiny.npz", **out)
 
 
-FIXTURES = {"gdn": "gdn_fixture", "attnres": "attnres_fixture", "moe": "moe_fixture", "lm": "lm_fixture"}
+SAMPLER_CASES = [  # (temperatures, top_ks, top_ps, min_ps)
+    ([0.0, 0.0, 0.0], [0, 0, 0], [1.0, 1.0, 1.0], [0.0, 0.0, 0.0]),
+    ([0.7, 1.0, 1.3], [20, 30, 40], [0.9, 0.8, 0.5], [0.0, 0.05, 0.0]),
+    ([1.0, 1.0, 1.0], [0, 0, 0], [0.95, 0.95, 0.95], [0.0, 0.0, 0.0]),
+    ([0.5, 0.5, 0.5], [5, 5, 5], [1.0, 1.0, 1.0], [0.1, 0.1, 0.1]),
+]
+
+
+def sampler_fixture(_lm):
+    """``sample_tts`` (model/src/zonos3/tts/sampler.py:159-372) on seeded fp32 logits [3, 4, 70] (codebook 64, EOA 64,
+    padding 65, span-end 66) with a stop-id mix, a repetition window, per-codebook sizes, a blocked stop and a stop
+    bias: the ids of each case with per-request generators seeded 100 + b."""
+    from zonos3.tts import sampler as ref
+
+    g = torch.Generator().manual_seed(0)
+    B, C, V = 3, 4, 70
+    logits = torch.randn(B, C, V, generator=g) * 3
+    stop = torch.tensor([64, 64, 66])
+    rep = torch.randint(0, V, (B, C, 5), generator=g)
+    pen = torch.tensor([1.0, 1.3, 2.0])
+    sizes = [64, 60, 64, 50]
+    blocked = torch.zeros(B, C, dtype=torch.bool)
+    blocked[1, 2] = True
+    bias = torch.tensor([0.0, 2.5, -1.0])
+    out = {"logits": logits.numpy(), "stop": stop.numpy(), "rep": rep.numpy(), "pen": pen.numpy(),
+           "sizes": np.array(sizes), "blocked": blocked.numpy(), "bias": bias.numpy()}
+    for n, (temps, tk, tp, mp) in enumerate(SAMPLER_CASES):
+        gens = [torch.Generator().manual_seed(100 + i) for i in range(B)]
+        ids = ref.sample_tts(logits.clone(), torch.tensor(temps, dtype=torch.float32), torch.tensor(tk),
+                             torch.tensor(tp), torch.tensor(mp), codebook_size=64, audio_pad_id=65,
+                             stop_token_ids=stop, repetition_token_ids=rep, repetition_penalties=pen,
+                             codebook_sizes=sizes, text_vocab=7, generators=gens, stop_blocked=blocked,
+                             stop_bias=bias)
+        out[f"case{n}"] = np.array([temps, tk, tp, mp], dtype=np.float64)
+        out[f"ids{n}"] = ids.numpy()
+    np.savez_compressed(HERE / "sampler.npz", **out)
+
+
+FIXTURES = {"gdn": "gdn_fixture", "attnres": "attnres_fixture", "moe": "moe_fixture", "lm": "lm_fixture",
+            "sampler": "sampler_fixture"}
 
 
 def main(reference: str, which: list[str]) -> None:

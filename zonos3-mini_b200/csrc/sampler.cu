@@ -1,0 +1,349 @@
+// The TTS sampler: next audio codes from per-codebook logits, on the device without a host round trip.
+//
+// Reference: sample_tts (model/src/zonos3/tts/sampler.py:159-372) as the server calls it once per decode step
+// (servers/sgl scheduler -> sample_tts on the head's softcapped logits [B, C, V]). Per (request b, codebook c) row,
+// in the reference's order:
+//   1. ids that may not be sampled -> -inf: the audio padding id, every special id (>= codebook_size) but the
+//      request's stop id, ordinary ids past the codebook's own size, the stop id while stop_blocked[b, c]
+//      (sampler.py:238-251); then + stop_bias[b] on the stop id (:252-253);
+//   2. repetition penalty over the request's recent ids of this codebook: a repeated id's logit is divided by the
+//      penalty when positive, multiplied otherwise (apply_repetition_penalty, :83-108);
+//   3. greedy (every temperature <= 0: argmax, first index of the maximum) or: / temperature, top-k (keep logits
+//      >= the k-th largest), softmax, top-p (keep an id when the probability mass strictly above it is <= top_p;
+//      ties at the cut-off are all kept), min-p (keep p >= min_p * max p), renormalisation after each filter
+//      (clamped at 1e-8), a row without mass falls back to its argmax, and one multinomial draw (:288-349).
+// top_k / top_p / min_p are the batch's (min, max, max) as the reference reduces them on the host.
+// The draw uses Philox4x32-10 (Salmon et al., SC'11) keyed by `seed`, counter (row, offset): a different random
+// stream from torch.multinomial's, so sampled ids match the reference in distribution, not draw for draw.
+//
+// One CTA of 256 threads per row; the row's logits live in shared memory (V <= kMaxVocab); the k-th largest
+// logit and the top-p cut-off are found by bisection on the float bits with block-wide counts / sums.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxVocab = 16384;
+
+struct SamplerParams {
+  const void* logits;  // [B, C, V] rows of V (row stride `row_stride` elements), bf16 or fp32
+  int logits_fp32;
+  int64_t row_stride;
+  int B, C, V;
+  const float* temperatures;  // [B]
+  int greedy;                 // every temperature <= 0
+  int top_k;                  // 0 or >= V: off
+  float top_p;                // off unless in (0, 1)
+  float min_p;                // off unless > 0
+  int codebook_size, audio_pad_id;
+  const int32_t* stop_ids;        // [B]
+  const int32_t* codebook_sizes;  // [C] or null
+  const uint8_t* stop_blocked;    // [B, C] or null
+  const float* stop_bias;         // [B] or null
+  const int32_t* rep_ids;         // [B, C, W] or null (ids outside [0, V) ignored)
+  int W;
+  const float* rep_penalties;  // [B] or null
+  uint64_t seed, offset;
+  int text_vocab;
+  int32_t* out;      // [B, C + 1]
+  float* probs_out;  // [B * C, V] or null: the final distribution (one-hot on greedy rows)
+};
+
+// ---------------------------------------------------------------------------------------------------- Philox
+
+__device__ __forceinline__ void philox_round(uint32_t (&c)[4], uint32_t k0, uint32_t k1) {
+  const uint32_t m0 = 0xD2511F53u, m1 = 0xCD9E8D57u;  // Philox4x32 multipliers (Salmon et al. 2011)
+  const uint32_t hi0 = __umulhi(m0, c[0]), lo0 = m0 * c[0];
+  const uint32_t hi1 = __umulhi(m1, c[2]), lo1 = m1 * c[2];
+  const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+  c[0] = n0;
+  c[1] = lo1;
+  c[2] = n2;
+  c[3] = lo0;
+}
+
+// First 32-bit output of Philox4x32-10 for counter (ctr_lo, ctr_hi) under key `key`.
+__device__ uint32_t philox(uint64_t key, uint64_t ctr_lo, uint64_t ctr_hi) {
+  uint32_t c[4] = {(uint32_t)ctr_lo, (uint32_t)(ctr_lo >> 32), (uint32_t)ctr_hi, (uint32_t)(ctr_hi >> 32)};
+  uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
+  const uint32_t w0 = 0x9E3779B9u, w1 = 0xBB67AE85u;  // Weyl key increments (Salmon et al. 2011)
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    philox_round(c, k0, k1);
+    k0 += w0;
+    k1 += w1;
+  }
+  return c[0];
+}
+
+// ---------------------------------------------------------------------------------------------------- block ops
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = zb::warp_sum(v);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();  // red is reused
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < kThreads / 32 ? red[lane] : 0.f;
+  return zb::warp_sum(t);
+}
+
+__device__ __forceinline__ int block_count(int v, float* red) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int* r = reinterpret_cast<int*>(red);
+  __syncthreads();
+  if (lane == 0) r[warp] = v;
+  __syncthreads();
+  int t = lane < kThreads / 32 ? r[lane] : 0;
+  for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  return t;
+}
+
+// (value, index) of the maximum, lowest index among equal maxima (-inf rows: index 0).
+__device__ __forceinline__ void block_argmax(const float* x, int V, float* red, float& best, int& best_i) {
+  float b = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += kThreads) {
+    if (x[i] > b || (x[i] == b && i < bi)) {
+      b = x[i];
+      bi = i;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, b, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ob > b || (ob == b && oi < bi)) {
+      b = ob;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int* ri = reinterpret_cast<int*>(red) + 32;
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = b;
+    ri[warp] = bi;
+  }
+  __syncthreads();
+  b = lane < kThreads / 32 ? red[lane] : -INFINITY;
+  bi = lane < kThreads / 32 ? ri[lane] : 0x7fffffff;
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, b, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ob > b || (ob == b && oi < bi)) {
+      b = ob;
+      bi = oi;
+    }
+  }
+  best = b;
+  best_i = bi == 0x7fffffff ? 0 : bi;
+}
+
+// Order-preserving map of a float to an unsigned key (larger float -> larger key).
+__device__ __forceinline__ uint32_t ordered(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
+  zb::pdl_enter();
+  extern __shared__ __align__(16) float x[];  // [V] logits, then probabilities
+  __shared__ float red[64];
+  __shared__ unsigned repeated[kMaxVocab / 32];
+  const int row = blockIdx.x, b = row / p.C, c = row % p.C, V = p.V, tid = threadIdx.x;
+
+  // 1. load, invalid ids, stop bias
+  const int stop = p.stop_ids[b];
+  const int limit = p.codebook_sizes ? p.codebook_sizes[c] : p.codebook_size;
+  const bool blocked = p.stop_blocked && p.stop_blocked[(int64_t)b * p.C + c];
+  const float bias = p.stop_bias ? p.stop_bias[b] : 0.f;
+  for (int i = tid; i < V; i += kThreads) {
+    float v = p.logits_fp32 ? reinterpret_cast<const float*>(p.logits)[(int64_t)row * p.row_stride + i]
+                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.logits)[(int64_t)row * p.row_stride + i]);
+    const bool invalid = i == p.audio_pad_id || (i >= p.codebook_size && i != stop) ||
+                         (i >= limit && i < p.codebook_size) || (blocked && i == stop);
+    if (invalid) v = -INFINITY;
+    if (i == stop) v += bias;
+    x[i] = v;
+  }
+  // 2. repetition penalty
+  if (p.rep_ids && p.rep_penalties && p.W > 0) {
+    for (int i = tid; i < (V + 31) / 32; i += kThreads) repeated[i] = 0u;
+    __syncthreads();
+    const int32_t* ids = p.rep_ids + ((int64_t)b * p.C + c) * p.W;
+    for (int w = tid; w < p.W; w += kThreads) {
+      const int id = ids[w];
+      if (id >= 0 && id < V) atomicOr(&repeated[id / 32], 1u << (id % 32));
+    }
+    __syncthreads();
+    const float pen = fmaxf(p.rep_penalties[b], 1.f);
+    for (int i = tid; i < V; i += kThreads) {
+      if ((repeated[i / 32] >> (i % 32)) & 1u) x[i] = x[i] > 0.f ? x[i] / pen : x[i] * pen;
+    }
+  }
+  __syncthreads();
+
+  int32_t* out = p.out + (int64_t)b * (p.C + 1);
+  if (c == 0 && tid == 0) out[p.C] = p.text_vocab;
+  float* probs = p.probs_out ? p.probs_out + (int64_t)row * V : nullptr;
+  if (p.greedy) {
+    float best;
+    int bi;
+    block_argmax(x, V, red, best, bi);
+    if (tid == 0) out[c] = bi;
+    if (probs) {
+      for (int i = tid; i < V; i += kThreads) probs[i] = i == bi ? 1.f : 0.f;
+    }
+    return;
+  }
+
+  // 3. temperature, top-k
+  const float temp = fmaxf(p.temperatures[b], 1e-8f);
+  for (int i = tid; i < V; i += kThreads) x[i] = x[i] / temp;
+  __syncthreads();
+  if (p.top_k > 0 && p.top_k < V) {
+    // the k-th largest logit: the largest key K with count(key >= K) >= k
+    uint32_t lo = 0u, hi = 0xffffffffu;  // answer in [lo, hi]
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo) / 2 + 1;
+      int cnt = 0;
+      for (int i = tid; i < V; i += kThreads) cnt += ordered(x[i]) >= mid ? 1 : 0;
+      if (block_count(cnt, red) >= p.top_k) lo = mid;
+      else hi = mid - 1;
+    }
+    for (int i = tid; i < V; i += kThreads) {
+      if (ordered(x[i]) < lo) x[i] = -INFINITY;
+    }
+    __syncthreads();
+  }
+  // the argmax after top-k (the fallback of a row without mass)
+  float mx;
+  int arg;
+  block_argmax(x, V, red, mx, arg);
+  // softmax
+  float part = 0.f;
+  for (int i = tid; i < V; i += kThreads) {
+    const float e = mx == -INFINITY ? 0.f : expf(x[i] - mx);
+    x[i] = e;
+    part += e;
+  }
+  float total = block_sum(part, red);
+  for (int i = tid; i < V; i += kThreads) x[i] = total > 0.f ? x[i] / total : 0.f;
+  __syncthreads();
+  // top-p: keep p_i when the mass strictly above p_i is <= top_p; the cut-off is the smallest value tau with
+  // mass(> tau) <= top_p (bisection on the bits of non-negative floats)
+  if (p.top_p > 0.f && p.top_p < 1.f) {
+    uint32_t lo = 0u, hi = 0x7f800000u;
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo) / 2;
+      float s = 0.f;
+      for (int i = tid; i < V; i += kThreads) s += __float_as_uint(x[i]) > mid ? x[i] : 0.f;
+      if (block_sum(s, red) <= p.top_p) hi = mid;
+      else lo = mid + 1;
+    }
+    float kept = 0.f;
+    for (int i = tid; i < V; i += kThreads) {
+      if (__float_as_uint(x[i]) < lo) x[i] = 0.f;
+      kept += x[i];
+    }
+    const float sum = fmaxf(block_sum(kept, red), 1e-8f);
+    for (int i = tid; i < V; i += kThreads) x[i] = x[i] / sum;
+    __syncthreads();
+  }
+  if (p.min_p > 0.f) {
+    float local = 0.f;
+    for (int i = tid; i < V; i += kThreads) local = fmaxf(local, x[i]);
+    local = zb::warp_max(local);
+    __syncthreads();
+    if (tid % 32 == 0) red[tid / 32] = local;
+    __syncthreads();
+    float top = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) top = fmaxf(top, red[w]);
+    const float cut = p.min_p * top;
+    float kept = 0.f;
+    for (int i = tid; i < V; i += kThreads) {
+      if (x[i] < cut) x[i] = 0.f;
+      kept += x[i];
+    }
+    const float sum = fmaxf(block_sum(kept, red), 1e-8f);
+    for (int i = tid; i < V; i += kThreads) x[i] = x[i] / sum;
+    __syncthreads();
+  }
+  // a row without mass: one-hot at the argmax
+  float mass = 0.f;
+  for (int i = tid; i < V; i += kThreads) mass += x[i];
+  mass = block_sum(mass, red);
+  if (!(mass > 0.f)) {
+    for (int i = tid; i < V; i += kThreads) x[i] = i == arg ? 1.f : 0.f;
+    mass = 1.f;
+    __syncthreads();
+  }
+  if (probs) {
+    for (int i = tid; i < V; i += kThreads) probs[i] = x[i];
+  }
+  // one draw: the first id whose inclusive prefix sum exceeds u * mass (contiguous chunks per thread)
+  const float u = (float)(philox(p.seed, (uint64_t)row, p.offset) >> 8) * (1.0f / 16777216.0f);
+  const float target = u * mass;
+  const int chunk = (V + kThreads - 1) / kThreads;
+  const int begin = min(tid * chunk, V), end = min(begin + chunk, V);
+  float local = 0.f;
+  for (int i = begin; i < end; ++i) local += x[i];
+  // exclusive scan of the chunk sums
+  float incl = local;
+  const int lane = tid % 32, warp = tid / 32;
+  for (int off = 1; off < 32; off <<= 1) {
+    const float o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  float before = 0.f;
+  for (int w = 0; w < warp; ++w) before += red[w];
+  float run = before + incl - local;
+  int pick = -1;
+  if (run <= target && target < run + local) {
+    for (int i = begin; i < end; ++i) {
+      run += x[i];
+      if (target < run && x[i] > 0.f) {
+        pick = i;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  int* slot = reinterpret_cast<int*>(red) + 40;
+  if (tid == 0) *slot = 0x7fffffff;
+  __syncthreads();
+  if (pick >= 0) atomicMin(slot, pick);
+  __syncthreads();
+  if (tid == 0) out[c] = *slot == 0x7fffffff ? arg : *slot;  // rounding past the last id: the argmax
+}
+
+}  // namespace
+
+ZB_API int zb_sample_tts(const void* logits, int logits_fp32, int64_t row_stride, int B, int C, int V,
+                         const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
+                         int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes,
+                         const uint8_t* stop_blocked, const float* stop_bias, const int32_t* rep_ids, int W,
+                         const float* rep_penalties, uint64_t seed, uint64_t offset, int text_vocab, int32_t* out,
+                         float* probs_out, cudaStream_t stream) {
+  ZB_REQUIRE(B >= 0 && C > 0 && V > 0 && V <= kMaxVocab, "sample_tts: sizes B=%d C=%d V=%d (V <= %d)", B, C, V,
+             kMaxVocab);
+  if (B == 0) return zb::kOk;
+  ZB_REQUIRE(logits && stop_ids && out && (greedy || temperatures), "sample_tts: null pointer");
+  ZB_REQUIRE(row_stride >= V, "sample_tts: row_stride %lld < V %d", (long long)row_stride, V);
+  ZB_REQUIRE(0 < codebook_size && codebook_size < V && codebook_size <= audio_pad_id && audio_pad_id < V,
+             "sample_tts: codebook_size %d / audio_pad_id %d for vocabulary %d", codebook_size, audio_pad_id, V);
+  ZB_REQUIRE(W >= 0 && (W == 0 || rep_ids), "sample_tts: repetition window %d without ids", W);
+  SamplerParams p{logits, logits_fp32, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size,
+                  audio_pad_id, stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed,
+                  offset, text_vocab, out, probs_out};
+  const size_t smem = (size_t)V * sizeof(float);
+  if (smem > 48 * 1024) {
+    ZB_CUDA(cudaFuncSetAttribute(sample_tts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  ZB_CUDA(zb::launch(sample_tts_kernel, dim3((unsigned)(B * C)), dim3(kThreads), smem, stream, 1, p));
+  return zb::check_launch("sample_tts");
+}

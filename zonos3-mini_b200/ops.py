@@ -711,3 +711,58 @@ def gqa_decode(q, k_cache, v_cache, page_table, cache_seqlens, *, softmax_scale=
               page_table.shape[1], B, Hq, Hkv, hd, scale, splits, split_len, workspace.data_ptr() if need else None,
               need * 4, out.data_ptr(), os_, _stream(dev))
     return out
+
+
+# ------------------------------------------------------------------------------------------------ TTS sampler
+
+
+def _host_list(t) -> list:
+    return t.tolist() if isinstance(t, torch.Tensor) else list(t)
+
+
+def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, audio_pad_id, stop_token_ids,
+               repetition_token_ids=None, repetition_penalties=None, codebook_sizes=None, text_vocab=0, seed=0,
+               offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None):
+    """Next codes from logits [B, C, V] (bf16 or fp32, CUDA): sample_tts (model/src/zonos3/tts/sampler.py:159-372)
+    as one kernel per (request, codebook) row, with the reference's masks, stop bias, repetition penalty, greedy
+    path and top-k / top-p / min-p filters. temperatures, top_ks, top_ps, min_ps, stop_token_ids: [B] tensors or
+    lists; their values pick host-side branches as in the reference (greedy when every temperature <= 0, the batch's
+    min top-k, max top-p and max min-p), so pass CPU tensors to keep the host from waiting on the GPU. The draw uses
+    Philox4x32-10 keyed by ``seed`` at counter (row, ``offset``): advance ``offset`` every step. Returns
+    [B, C + 1] int32 (codes, then ``text_vocab``); ``probs_out`` ([B * C, V] fp32) receives the final
+    distributions."""
+    _require(isinstance(logits, torch.Tensor) and logits.is_cuda, "logits must be a CUDA tensor")
+    _require(logits.dtype in (torch.bfloat16, torch.float32), "logits must be bf16 or fp32")
+    dev = logits.device
+    B, C, V = logits.shape
+    _require(logits.stride(2) == 1 and logits.stride(0) == C * logits.stride(1), "logits rows must be [B, C, V] "
+             "with contiguous rows and codebooks")
+    temps = _host_list(temperatures)
+    greedy = all(float(t) <= 0 for t in temps)
+    top_k = int(min(int(k) for k in _host_list(top_ks))) if B else 0
+    top_p = float(max(float(v) for v in _host_list(top_ps))) if B else 1.0
+    min_p = float(max(float(v) for v in _host_list(min_ps))) if B else 0.0
+    i32 = dict(device=dev, dtype=torch.int32)
+    f32 = dict(device=dev, dtype=torch.float32)
+    dev_t = lambda v, kw: v.to(**kw) if isinstance(v, torch.Tensor) else torch.tensor(v, **kw)  # noqa: E731
+    temp_d = dev_t(temperatures, f32)
+    stop_d = dev_t(stop_token_ids, i32)
+    sizes_d = None if codebook_sizes is None else dev_t(codebook_sizes, i32)
+    blocked_d = None if stop_blocked is None else dev_t(stop_blocked, dict(device=dev, dtype=torch.uint8))
+    bias_d = None if stop_bias is None else dev_t(stop_bias, f32)
+    W = 0
+    rep_d = pen_d = None
+    if repetition_token_ids is not None and repetition_penalties is not None and repetition_token_ids.numel():
+        rep_d = dev_t(repetition_token_ids, i32).contiguous()
+        _require(rep_d.shape[:2] == (B, C), f"repetition_token_ids must be [{B}, {C}, W]")
+        W = rep_d.shape[2]
+        pen_d = dev_t(repetition_penalties, f32)
+    if out is None:
+        out = torch.empty(B, C + 1, **i32)
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call("zb_sample_tts", logits.data_ptr(), int(logits.dtype == torch.float32), logits.stride(1), B, C, V,
+              temp_d.data_ptr(), int(greedy), top_k, top_p, min_p, int(codebook_size), int(audio_pad_id),
+              stop_d.data_ptr(), ptr(sizes_d), ptr(blocked_d), ptr(bias_d), ptr(rep_d), W, ptr(pen_d),
+              int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), int(text_vocab), out.data_ptr(), ptr(probs_out),
+              _stream(dev))
+    return out
