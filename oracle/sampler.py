@@ -39,8 +39,9 @@ def masked_logits(logits, *, codebook_size, audio_pad_id, stop_token_ids, codebo
 
 def final_probs(logits, temperatures, top_k, top_p, min_p, **mask_args):
     """(probs [B*C, V], greedy ids [B, C]) of sample_tts for batch-level top_k / top_p / min_p. Greedy rows (every
-    temperature <= 0) get a one-hot distribution. Top-p follows the reference's sorted-cumsum rule (for distinct
-    probabilities: keep an id when the mass strictly above it is <= top_p)."""
+    temperature <= 0) get a one-hot distribution. Top-p follows the reference's sorted-cumsum rule with a stable
+    sort: equal probabilities are ranked by index, as torch's CUDA sort of the production vocabulary (a stable
+    radix sort above 4096 entries) ranks them."""
     x = masked_logits(logits, **mask_args)
     B, C, V = x.shape
     temps = torch.as_tensor(temperatures).float()
@@ -53,7 +54,7 @@ def final_probs(logits, temperatures, top_k, top_p, min_p, **mask_args):
         flat = flat.masked_fill(flat < kth, float("-inf"))
     probs = torch.softmax(flat, -1)
     if 0.0 < top_p < 1.0:  # sorted cumulative mass before each id (= the mass strictly above it when distinct)
-        srt, idx = torch.sort(probs, dim=-1, descending=True)
+        srt, idx = torch.sort(probs, dim=-1, descending=True, stable=True)  # CUDA's sort of V > 4096 is stable
         srt = srt.masked_fill(torch.cumsum(srt, -1) - srt > top_p, 0.0)
         probs = probs.scatter(-1, idx, srt)
         probs = probs / probs.sum(-1, keepdim=True).clamp(min=1e-8)

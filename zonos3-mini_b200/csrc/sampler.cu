@@ -9,8 +9,9 @@
 //   2. repetition penalty over the request's recent ids of this codebook: a repeated id's logit is divided by the
 //      penalty when positive, multiplied otherwise (apply_repetition_penalty, :83-108);
 //   3. greedy (every temperature <= 0: argmax, first index of the maximum) or: / temperature, top-k (keep logits
-//      >= the k-th largest), softmax, top-p (keep an id when the probability mass strictly above it is <= top_p;
-//      ties at the cut-off are all kept), min-p (keep p >= min_p * max p), renormalisation after each filter
+//      >= the k-th largest), softmax, top-p (keep an id when the mass before it in a stable descending order --
+//      larger probabilities, then equal ones of lower index -- is <= top_p), min-p (keep p >= min_p * max p),
+//      renormalisation after each filter
 //      (clamped at 1e-8), a row without mass falls back to its argmax, and one multinomial draw (:288-349).
 // top_k / top_p / min_p are the batch's (min, max, max) as the reference reduces them on the host.
 // The draw uses Philox4x32-10 (Salmon et al., SC'11) keyed by `seed`, counter (row, offset): a different random
@@ -242,11 +243,39 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
       if (block_sum(s, red) <= p.top_p) hi = mid;
       else lo = mid + 1;
     }
-    float kept = 0.f;
-    for (int i = tid; i < V; i += kThreads) {
-      if (__float_as_uint(x[i]) < lo) x[i] = 0.f;
-      kept += x[i];
+    // ids equal to the cut-off value tau are kept in index order while the mass before them (everything above
+    // tau, then the earlier ties) stays <= top_p: the reference's stable descending sort keeps ties in index order
+    const float tau = __uint_as_float(lo);
+    float above = 0.f;
+    for (int i = tid; i < V; i += kThreads) above += x[i] > tau ? x[i] : 0.f;
+    above = block_sum(above, red);
+    const int chunk = (V + kThreads - 1) / kThreads;
+    const int cb = min(tid * chunk, V), ce = min(cb + chunk, V);
+    int ties = 0;
+    for (int i = cb; i < ce; ++i) ties += x[i] == tau ? 1 : 0;
+    int incl = ties;  // inclusive scan of the tie counts over the contiguous chunks
+    const int lane = tid % 32, warp = tid / 32;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
     }
+    int* wsum = reinterpret_cast<int*>(red) + 48;
+    __syncthreads();
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    int rank = incl - ties;
+    for (int w = 0; w < warp; ++w) rank += wsum[w];
+    for (int i = cb; i < ce; ++i) {
+      if (x[i] == tau) {
+        if (above + (float)rank * tau > p.top_p) x[i] = 0.f;
+        ++rank;
+      } else if (x[i] < tau) {
+        x[i] = 0.f;
+      }
+    }
+    __syncthreads();
+    float kept = 0.f;
+    for (int i = tid; i < V; i += kThreads) kept += x[i];
     const float sum = fmaxf(block_sum(kept, red), 1e-8f);
     for (int i = tid; i < V; i += kThreads) x[i] = x[i] / sum;
     __syncthreads();
