@@ -652,6 +652,30 @@ def bench_full_step_cfg5(pkg, dev, stream, streams=256, context=878, reps=3):
     }
 
 
+def bench_sampler_cfg5(ops, dev, stream, streams=256, codebooks=10, vocab=4098, reps=5):
+    """The TTS sampler for a cfg5 decode step: fp32 logits [256, 10, 4098] (N(0, 3)), temperature 0.8, top-k 50,
+    top-p 0.9, a 32-step repetition window with penalty 1.2; one row per CTA. The 42 MB of logits stay in L2 between
+    replays (as the head GEMM leaves them there)."""
+    gen = torch.Generator().manual_seed(8)
+    logits = (3 * torch.randn(streams, codebooks, vocab, generator=gen)).to(dev)
+    rep = torch.randint(0, vocab, (streams, codebooks, 32), generator=gen, dtype=torch.int32).to(dev)
+    pen = torch.full((streams,), 1.2, device=dev)
+    stop = torch.full((streams,), vocab - 2, dtype=torch.int32, device=dev)
+    temps = torch.full((streams,), 0.8)
+    temps_d = temps.to(dev)
+    out = torch.empty(streams, codebooks + 1, device=dev, dtype=torch.int32)
+
+    def sample():
+        ops.sample_tts(logits, temps, [50], [0.9], [0.0], codebook_size=vocab - 2, audio_pad_id=vocab - 1,
+                       stop_token_ids=stop, repetition_token_ids=rep, repetition_penalties=pen, seed=1, out=out,
+                       device_temperatures=temps_d)
+
+    ms = graph_ms(sample, stream, reps)
+    return {"workload": f"TTS sampler: {streams} streams x {codebooks} codebooks x {vocab} ids, fp32 logits, "
+                        "temperature 0.8, top-k 50, top-p 0.9, repetition window 32",
+            "us": ms * 1e3, "rows_per_s": streams * codebooks / (ms / 1e3)}
+
+
 def gqa_cfg5_inputs(dev, streams=256, prompt=128, context=1628, Hq=16, Hkv=4, hd=128, seed=5):
     """cfg5 global-attention decode at the end of the run: `streams` requests, each with `context` cached keys
     (the 128-token prompt, then 1500 decode steps). Slots as a token pool hands them out: each prompt a contiguous
@@ -903,6 +927,7 @@ def main():
                     "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
                     "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
                     "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
+                    "sampler_cfg5": bench_sampler_cfg5(ops, dev, stream),
                     "full_step_cfg5": bench_full_step_cfg5(__import__("__graft_entry__").load_package(), dev, stream),
                     "decode_layer_cfg5": bench_decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev,
                                                                  stream),

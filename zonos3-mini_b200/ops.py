@@ -722,7 +722,7 @@ def _host_list(t) -> list:
 
 def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, audio_pad_id, stop_token_ids,
                repetition_token_ids=None, repetition_penalties=None, codebook_sizes=None, text_vocab=0, seed=0,
-               offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None):
+               offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None, device_temperatures=None):
     """Next codes from logits [B, C, V] (bf16 or fp32, CUDA): sample_tts (model/src/zonos3/tts/sampler.py:159-372)
     as one kernel per (request, codebook) row, with the reference's masks, stop bias, repetition penalty, greedy
     path and top-k / top-p / min-p filters. temperatures, top_ks, top_ps, min_ps, stop_token_ids: [B] tensors or
@@ -730,7 +730,8 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
     min top-k, max top-p and max min-p), so pass CPU tensors to keep the host from waiting on the GPU. The draw uses
     Philox4x32-10 keyed by ``seed`` at counter (row, ``offset``): advance ``offset`` every step. Returns
     [B, C + 1] int32 (codes, then ``text_vocab``); ``probs_out`` ([B * C, V] fp32) receives the final
-    distributions."""
+    distributions. Per-row inputs already on the device (int32 stop ids, fp32 ``device_temperatures``, ...) are
+    used as they are, so a call can be captured in a CUDA graph."""
     _require(isinstance(logits, torch.Tensor) and logits.is_cuda, "logits must be a CUDA tensor")
     _require(logits.dtype in (torch.bfloat16, torch.float32), "logits must be bf16 or fp32")
     dev = logits.device
@@ -745,7 +746,7 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
     i32 = dict(device=dev, dtype=torch.int32)
     f32 = dict(device=dev, dtype=torch.float32)
     dev_t = lambda v, kw: v.to(**kw) if isinstance(v, torch.Tensor) else torch.tensor(v, **kw)  # noqa: E731
-    temp_d = dev_t(temperatures, f32)
+    temp_d = dev_t(temperatures if device_temperatures is None else device_temperatures, f32)
     stop_d = dev_t(stop_token_ids, i32)
     sizes_d = None if codebook_sizes is None else dev_t(codebook_sizes, i32)
     blocked_d = None if stop_blocked is None else dev_t(stop_blocked, dict(device=dev, dtype=torch.uint8))
