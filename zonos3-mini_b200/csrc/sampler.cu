@@ -17,8 +17,10 @@
 // The draw uses Philox4x32-10 (Salmon et al., SC'11) keyed by `seed`, counter (row, offset): a different random
 // stream from torch.multinomial's, so sampled ids match the reference in distribution, not draw for draw.
 //
-// One CTA of 256 threads per row; the row's logits live in shared memory (V <= kMaxVocab); the k-th largest
-// logit and the top-p cut-off are found by bisection on the float bits with block-wide counts / sums.
+// One CTA of 256 threads per row; the row's logits live in shared memory (V <= kMaxVocab). With a top-k of at most
+// 512 the k-th largest logit comes from a 4-pass radix select and the survivors are sorted (sample_sorted_topk);
+// otherwise the k-th largest logit and the top-p cut-off are found by bisection on the float bits with
+// block-wide counts / sums.
 #include "common.cuh"
 
 namespace {
@@ -147,6 +149,191 @@ __device__ __forceinline__ uint32_t ordered(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+constexpr int kMaxCand = 1024;  // survivors of top-k that the sorted path holds (k <= kSortedTopK, plus ties)
+constexpr int kSortedTopK = 512;
+
+// Inclusive block-wide scan of one int per thread (warp totals through `wsum`, 8 ints).
+__device__ __forceinline__ int block_scan_incl(int v, int* wsum) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += o;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[warp] = v;
+  __syncthreads();
+  for (int w = 0; w < warp; ++w) v += wsum[w];
+  return v;
+}
+__device__ __forceinline__ float block_scan_incl_f(float v, float* wsum) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  for (int off = 1; off < 32; off <<= 1) {
+    const float o = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += o;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[warp] = v;
+  __syncthreads();
+  for (int w = 0; w < warp; ++w) v += wsum[w];
+  return v;
+}
+
+// The sampling path after a small top-k (temperature already applied to x): the k-th largest logit by a 4-pass
+// radix select, the survivors (logit >= it) compacted in index order and bitonic-sorted by (logit descending,
+// index ascending) -- the order of the reference's stable descending sort --, then softmax, top-p with the
+// reference's rule (inclusive cumulative sum minus the id's own probability > top_p drops it), min-p, the
+// empty-row fallback and the draw, all on the short sorted list. Returns false (nothing written) when more than
+// kMaxCand ids tie into the top k.
+__device__ bool sample_sorted_topk(const SamplerParams& p, float* x, int row, int c, int32_t* out, float* probs,
+                                   float* cand_v, int* cand_i, int* ints, float* red) {
+  const int V = p.V, tid = threadIdx.x;
+  int* hist = ints;         // [256]
+  int* wsum = ints + 256;   // [8]
+  int* sel = ints + 264;    // [2]
+  uint32_t prefix = 0u, pmask = 0u;
+  int kk = p.top_k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist[tid] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += kThreads) {
+      const uint32_t key = ordered(x[i]);
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    const int v = hist[255 - tid];
+    const int s = block_scan_incl(v, wsum);  // ids whose digit is >= 255 - tid
+    if (s >= kk && s - v < kk) {
+      sel[0] = 255 - tid;
+      sel[1] = s - v;
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sel[0] << shift;
+    pmask |= 255u << shift;
+    kk -= sel[1];
+    __syncthreads();
+  }
+  // compact the survivors in index order (contiguous chunks per thread)
+  const int chunk = (V + kThreads - 1) / kThreads;
+  const int cb = min(tid * chunk, V), ce = min(cb + chunk, V);
+  int mine = 0;
+  for (int i = cb; i < ce; ++i) mine += ordered(x[i]) >= prefix ? 1 : 0;
+  const int incl = block_scan_incl(mine, wsum);
+  __shared__ int total_s;
+  if (tid == kThreads - 1) total_s = incl;  // the last thread's inclusive count is the total
+  __syncthreads();
+  const int total = total_s;
+  if (total > kMaxCand) return false;
+  int pos = incl - mine;
+  for (int i = cb; i < ce; ++i) {
+    if (ordered(x[i]) >= prefix) {
+      cand_v[pos] = x[i];
+      cand_i[pos] = i;
+      ++pos;
+    }
+  }
+  int P = 1;
+  while (P < total) P <<= 1;
+  for (int r = total + tid; r < P; r += kThreads) {
+    cand_v[r] = -INFINITY;
+    cand_i[r] = 0x7fffffff;
+  }
+  __syncthreads();
+  // bitonic sort: "a before b" when a.v > b.v, or equal values and a.i < b.i
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size / 2; stride > 0; stride >>= 1) {
+      for (int t = tid; t < P / 2; t += kThreads) {
+        const int i = 2 * t - (t & (stride - 1)), j = i + stride;
+        const bool desc = (i & size) == 0;  // this run sorts in "before" order
+        const float vi = cand_v[i], vj = cand_v[j];
+        const int ii = cand_i[i], ij = cand_i[j];
+        const bool j_before_i = vj > vi || (vj == vi && ij < ii);
+        if (j_before_i == desc) {
+          cand_v[i] = vj;
+          cand_v[j] = vi;
+          cand_i[i] = ij;
+          cand_i[j] = ii;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // softmax over the sorted survivors (4 consecutive positions per thread)
+  const float mx = cand_v[0];
+  const int q0 = 4 * tid;
+  float e[4], part = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = q0 + k;
+    e[k] = (r < total && mx != -INFINITY) ? expf(cand_v[r] - mx) : 0.f;
+    part += e[k];
+  }
+  const float sum = block_sum(part, red);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) e[k] = sum > 0.f ? e[k] / sum : 0.f;
+  if (p.top_p > 0.f && p.top_p < 1.f) {
+    float loc = e[0] + e[1] + e[2] + e[3];
+    float run = block_scan_incl_f(loc, reinterpret_cast<float*>(wsum)) - loc;
+    float kept = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      run += e[k];                       // the inclusive cumulative sum at this position
+      if (run - e[k] > p.top_p) e[k] = 0.f;  // minus its own probability: the mass before it
+      kept += e[k];
+    }
+    const float ksum = fmaxf(block_sum(kept, red), 1e-8f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) e[k] = e[k] / ksum;
+  }
+  if (p.min_p > 0.f) {
+    __shared__ float top_s;
+    if (tid == 0) top_s = e[0];  // the largest probability sits first
+    __syncthreads();
+    const float cut = p.min_p * top_s;
+    float kept = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (e[k] < cut) e[k] = 0.f;
+      kept += e[k];
+    }
+    const float ksum = fmaxf(block_sum(kept, red), 1e-8f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) e[k] = e[k] / ksum;
+  }
+  float mass = block_sum(e[0] + e[1] + e[2] + e[3], red);
+  if (!(mass > 0.f)) {  // a row without mass: one-hot at the argmax (the first survivor)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) e[k] = q0 + k == 0 ? 1.f : 0.f;
+    mass = 1.f;
+  }
+  if (probs) {
+    for (int i = tid; i < V; i += kThreads) probs[i] = 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (q0 + k < total) probs[cand_i[q0 + k]] = e[k];
+    }
+  }
+  // the draw over the sorted list
+  const float u = (float)(philox(p.seed, (uint64_t)row, p.offset) >> 8) * (1.0f / 16777216.0f);
+  const float target = u * mass;
+  const float loc = e[0] + e[1] + e[2] + e[3];
+  float run = block_scan_incl_f(loc, reinterpret_cast<float*>(wsum)) - loc;
+  int pick = -1;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    run += e[k];
+    if (pick < 0 && target < run && e[k] > 0.f) pick = q0 + k;
+  }
+  int* slot = sel;
+  __syncthreads();
+  if (tid == 0) *slot = 0x7fffffff;
+  __syncthreads();
+  if (pick >= 0) atomicMin(slot, pick);
+  __syncthreads();
+  if (tid == 0) out[c] = cand_i[*slot == 0x7fffffff ? 0 : *slot];
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
   zb::pdl_enter();
   extern __shared__ __align__(16) float x[];  // [V] logits, then probabilities
@@ -203,6 +390,12 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
   const float temp = fmaxf(p.temperatures[b], 1e-8f);
   for (int i = tid; i < V; i += kThreads) x[i] = x[i] / temp;
   __syncthreads();
+  if (p.top_k > 0 && p.top_k <= kSortedTopK && p.top_k < V) {
+    __shared__ float cand_v[kMaxCand];
+    __shared__ int cand_i[kMaxCand];
+    __shared__ int ints[272];
+    if (sample_sorted_topk(p, x, row, c, out, probs, cand_v, cand_i, ints, red)) return;
+  }
   if (p.top_k > 0 && p.top_k < V) {
     // the k-th largest logit: the largest key K with count(key >= K) >= k
     uint32_t lo = 0u, hi = 0xffffffffu;  // answer in [lo, hi]
