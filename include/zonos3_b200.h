@@ -251,7 +251,9 @@ int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, 
 /* ---------------------------------------------------------------------------------------------- TTS sampler */
 
 /* Next audio codes from per-codebook logits [B, C, V] (rows of V, row stride row_stride elements; bf16 when
- * logits_fp32 == 0, else fp32), one row per (request, codebook): invalid ids masked (audio_pad_id; ids >=
+ * logits_fp32 == 0, else fp32), one row per (request, codebook): softcap > 0 first applies the head's soft cap
+ * softcap * tanh(x / softcap) (MultiOutputHead + softcap, servers/sgl/src/zonos3_sgl/models/zonos3.py:1341-1360,
+ * rounded to bf16 after each op for bf16 logits, as torch evaluates it), then invalid ids masked (audio_pad_id; ids >=
  * codebook_size other than stop_ids[b]; ids past codebook_sizes[c] (NULL: codebook_size); the stop id while
  * stop_blocked[b, c] (NULL: never)), stop_bias[b] added to the stop id (NULL: none), repetition penalty
  * rep_penalties[b] over rep_ids[b, c, 0..W) (NULL / W = 0: none), then greedy argmax when `greedy` (every
@@ -261,7 +263,7 @@ int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, 
  * probs_out (NULL: not written) [B * C, V] fp32 receives each row's final distribution. V <= 16384.
  * Replaces sample_tts (model/src/zonos3/tts/sampler.py:159-372; ids drawn from a different random stream than
  * torch.multinomial, equal in distribution). */
-int zb_sample_tts(const void* logits, int logits_fp32, int64_t row_stride, int B, int C, int V,
+int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t row_stride, int B, int C, int V,
                   const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
                   int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes, const uint8_t* stop_blocked,
                   const float* stop_bias, const int32_t* rep_ids, int W, const float* rep_penalties, uint64_t seed,

@@ -130,3 +130,24 @@ def test_rejects_bad_arguments(zb):
     with pytest.raises(ValueError):
         zb.ops.sample_tts(logits[:, :, :100], [1.0], [0], [1.0], [0.0], codebook_size=100, audio_pad_id=101,
                           stop_token_ids=[100])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_softcap_matches_torch(zb, dtype):
+    """softcap = 15 on the raw head output: the same distribution as torch's soft cap (evaluated on the GPU in the
+    head's dtype, as compute_logits does) followed by the oracle; greedy ids identical."""
+    gen = torch.Generator().manual_seed(13)
+    logits, args = _inputs(gen, 4, 10, scale=20.0)
+    dev = torch.device("cuda")
+    raw = logits.to(dev, dtype)
+    capped = (15.0 * torch.tanh(raw / 15.0)).float().cpu()  # the reference's softcap in the head's dtype
+    kw = dict(codebook_size=CB, audio_pad_id=PAD, stop_token_ids=args["stop_token_ids"],
+              repetition_token_ids=args["repetition_token_ids"], repetition_penalties=args["repetition_penalties"],
+              codebook_sizes=args["codebook_sizes"], stop_blocked=args["stop_blocked"], stop_bias=args["stop_bias"])
+    probs = torch.empty(40, V, device=dev)
+    zb.ops.sample_tts(raw, [0.9] * 4, [0] * 4, [0.9] * 4, [0.0] * 4, softcap=15.0, probs_out=probs, **kw)
+    ref, _ = osam.final_probs(capped, [0.9] * 4, 0, 0.9, 0.0, **args)
+    torch.testing.assert_close(probs.cpu(), ref, atol=1e-5, rtol=1e-4)
+    ids = zb.ops.sample_tts(raw, [0.0] * 4, [0] * 4, [1.0] * 4, [0.0] * 4, softcap=15.0, **kw)
+    _, greedy = osam.final_probs(capped, [0.0] * 4, 0, 1.0, 0.0, **args)
+    assert torch.equal(ids[:, :10].cpu().long(), greedy.long())

@@ -70,10 +70,10 @@ SIGNATURES: dict[str, list] = {
     "zb_kv_store": [_p, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i32, _i32, _i32, _p],
     # q, q_stride, k_cache, v_cache, slot_stride, num_slots, page_table, table_stride, seq_lens, max_seq_len, B, Hq,
     # Hkv, hd, scale, splits, split_len, workspace, workspace_bytes, out, out_stride, stream
-    # logits, logits_fp32, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size, audio_pad_id,
+    # logits, logits_fp32, softcap, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size, audio_pad_id,
     # stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed, offset, text_vocab, out,
     # probs_out, stream
-    "zb_sample_tts": [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
+    "zb_sample_tts": [_p, _i32, _f32, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
                       _i32, _p, _u64, _u64, _i32, _p, _p, _p],
     "zb_gqa_decode": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _p,
                       _i64, _p, _i64, _p],

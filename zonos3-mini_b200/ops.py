@@ -722,7 +722,8 @@ def _host_list(t) -> list:
 
 def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, audio_pad_id, stop_token_ids,
                repetition_token_ids=None, repetition_penalties=None, codebook_sizes=None, text_vocab=0, seed=0,
-               offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None, device_temperatures=None):
+               offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None, device_temperatures=None,
+               softcap=0.0):
     """Next codes from logits [B, C, V] (bf16 or fp32, CUDA): sample_tts (model/src/zonos3/tts/sampler.py:159-372)
     as one kernel per (request, codebook) row, with the reference's masks, stop bias, repetition penalty, greedy
     path and top-k / top-p / min-p filters. temperatures, top_ks, top_ps, min_ps, stop_token_ids: [B] tensors or
@@ -731,7 +732,8 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
     Philox4x32-10 keyed by ``seed`` at counter (row, ``offset``): advance ``offset`` every step. Returns
     [B, C + 1] int32 (codes, then ``text_vocab``); ``probs_out`` ([B * C, V] fp32) receives the final
     distributions. Per-row inputs already on the device (int32 stop ids, fp32 ``device_temperatures``, ...) are
-    used as they are, so a call can be captured in a CUDA graph."""
+    used as they are, so a call can be captured in a CUDA graph. ``softcap`` > 0 applies the head's soft cap
+    (cap * tanh(x / cap), zonos3.py:1341-1360) to the raw head output first, with torch's bf16 rounding points."""
     _require(isinstance(logits, torch.Tensor) and logits.is_cuda, "logits must be a CUDA tensor")
     _require(logits.dtype in (torch.bfloat16, torch.float32), "logits must be bf16 or fp32")
     dev = logits.device
@@ -761,7 +763,8 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
     if out is None:
         out = torch.empty(B, C + 1, **i32)
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-    _lib.call("zb_sample_tts", logits.data_ptr(), int(logits.dtype == torch.float32), logits.stride(1), B, C, V,
+    _lib.call("zb_sample_tts", logits.data_ptr(), int(logits.dtype == torch.float32), float(softcap), logits.stride(1),
+              B, C, V,
               temp_d.data_ptr(), int(greedy), top_k, top_p, min_p, int(codebook_size), int(audio_pad_id),
               stop_d.data_ptr(), ptr(sizes_d), ptr(blocked_d), ptr(bias_d), ptr(rep_d), W, ptr(pen_d),
               int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), int(text_vocab), out.data_ptr(), ptr(probs_out),
