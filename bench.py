@@ -529,9 +529,9 @@ def full_step_cfg5(pkg, dev, streams=256, context=878, n_layers=24):
     """Builds one cfg5 decode step of the whole 24-layer backbone for `streams` streams (one new row each): layers in
     the 3:1 DeltaNet:GQA pattern (layer i is GQA when i % 4 == 3), an MoE FFN in every layer and the Full AttnRes
     schedule (a route before every sublayer and a final one: 49 routes over the layer-output bank, queries
-    registered, norms fused). GQA layers: fused wq / wkv / gater projection, q / k RMS norm with |temp| and
-    interleaved RoPE (plain torch), then `ops.kv_store` of the new row and `ops.gqa_decode` over `context` cached
-    keys + the new one (the mid-run cache of a 128-token prompt + 1500 decode steps; prompt slots contiguous, decode
+    registered, norms fused). GQA layers: fused wq / wkv / gater projection (cuBLAS), `ops.gqa_prologue_decode`
+    (q / k RMS norm with |temp|, interleaved RoPE and the KV store of the new row in one kernel), `ops.gqa_decode`
+    over `context` cached keys + the new one (the mid-run cache of a 128-token prompt + 1500 decode steps; prompt slots contiguous, decode
     slots interleaved across streams), gate and wo. bf16 random-init weights N(0, 0.02), generated on the device.
     Embedding and the multi-codebook head / sampler are not included. Returns (step, core, batch)."""
     ops, core = pkg.ops, pkg.core
@@ -549,20 +549,14 @@ def full_step_cfg5(pkg, dev, streams=256, context=878, n_layers=24):
     n_slots = kc0.shape[0]
     del kc0, vc0
     out_loc = table_gq[:, context].contiguous()  # the new row's slot (the last entry of each request's table)
-    positions = torch.full((streams,), context, device=dev, dtype=torch.float32)
-    freqs = 10000.0 ** (-torch.arange(0, hd, 2, dtype=torch.float32, device=dev) / hd)
-    ang = positions[:, None] * freqs[None, :]
-    cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
-
-    def rope(t):
-        pr = t.float().reshape(*t.shape[:-1], hd // 2, 2)
-        a, b = pr[..., 0], pr[..., 1]
-        return torch.stack((a * cos - b * sin, a * sin + b * cos), -1).flatten(-2).to(t.dtype)
+    pos_i32 = torch.full((streams,), context, device=dev, dtype=torch.int32)  # the new row's position
 
     for i in range(n_layers):
         if i % 4 == 3:
-            mixer = {"w": rnd(Hq * hd + 2 * Hkv * hd + Hq, D), "wo": rnd(D, Hq * hd), "temp": torch.ones(Hq, device=dev),
+            mixer = {"w": rnd(Hq * hd + 2 * Hkv * hd + Hq, D), "wo": rnd(D, Hq * hd),
+                     "temp": torch.ones(Hq, device=dev, dtype=torch.bfloat16),
                      "kc": rnd(n_slots, Hkv, hd, s=1.0), "vc": rnd(n_slots, Hkv, hd, s=1.0),
+                     "q": torch.empty(streams, Hq, hd, device=dev, dtype=torch.bfloat16),
                      "o": torch.empty(streams, Hq, hd, device=dev, dtype=torch.bfloat16)}
         else:
             mixer = pkg.gdn.OriginalGDN(cfg, i)
@@ -582,14 +576,10 @@ def full_step_cfg5(pkg, dev, streams=256, context=878, n_layers=24):
         layers.append((mixer, moe))
 
     def gqa(m, x):
-        p = F.linear(x, m["w"])
-        q = p[:, : Hq * hd].view(streams, Hq, hd)
-        kk = p[:, Hq * hd: Hq * hd + Hkv * hd].reshape(streams, Hkv, hd)
-        v = p[:, Hq * hd + Hkv * hd: Hq * hd + 2 * Hkv * hd].reshape(streams, Hkv, hd)
+        p = F.linear(x, m["w"])  # q | k | v | gate
         gate = p[:, Hq * hd + 2 * Hkv * hd:].sigmoid()
-        q = rope((F.rms_norm(q.float(), (hd,), eps=1e-6) * m["temp"].abs().view(1, Hq, 1)).bfloat16())
-        kk = rope(F.rms_norm(kk.float(), (hd,), eps=1e-6).bfloat16())
-        ops.kv_store(m["kc"], m["vc"], out_loc, kk, v)
+        q = ops.gqa_prologue_decode(p, m["temp"], pos_i32, m["kc"], m["vc"], out_loc, heads=Hq, kv_heads=Hkv,
+                                    q_out=m["q"])
         o = ops.gqa_decode(q, m["kc"], m["vc"], table_gq, seq_gq, out=m["o"])
         return F.linear((o * gate.unsqueeze(-1)).reshape(streams, Hq * hd), m["wo"])
 

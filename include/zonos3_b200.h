@@ -248,6 +248,17 @@ int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, 
                   int splits, int split_len, float* workspace, int64_t workspace_bytes, uint16_t* out,
                   int64_t out_stride, cudaStream_t stream);
 
+/* The attention layer's decode prologue: from the fused projection rows proj [N, Hq*hd | Hkv*hd | Hkv*hd | ...]
+ * (q | k | v, row stride proj_stride), q = bf16(RMSNorm(q, eps)) * bf16(|temp|) (rounded), k = bf16(RMSNorm(k, eps)),
+ * both rotated by interleaved RoPE at positions[t] (inverse frequency 1 / rope_theta^(2i / hd)); q to q_out
+ * [N, Hq, hd], k and v to slot out_loc[t] of the caches (slot stride slot_stride; a slot outside [0, num_slots)
+ * stores nothing). Replaces the q/k norm, temperature, rotary and store_kv steps of Attention.forward
+ * (servers/sgl/src/zonos3_sgl/models/zonos3.py:340-375). hd = 128; tensors 8-byte aligned, strides multiples of 4. */
+int zb_gqa_prologue_decode(const uint16_t* proj, int64_t proj_stride, const uint16_t* temp, const int32_t* positions,
+                           float rope_theta, float eps, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                           int64_t slot_stride, int64_t num_slots, const int32_t* out_loc, int N, int Hq, int Hkv,
+                           int hd, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- TTS sampler */
 
 /* Next audio codes from per-codebook logits [B, C, V] (rows of V, row stride row_stride elements; bf16 when

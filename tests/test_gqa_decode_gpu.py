@@ -154,3 +154,39 @@ def test_gqa_decode_many_units_per_cta(zb, Hq, Hkv, num_splits):
     ref = attention.decode_attention(q, kc, vc, table, seq)
     torch.testing.assert_close(out.float().cpu(), ref, atol=ATOL, rtol=RTOL)
     assert all(out[b].float().abs().max().item() == 0.0 for b in range(B) if lens[b] == 0)
+
+
+def test_gqa_prologue_matches_torch(zb):
+    """zb_gqa_prologue_decode against the server's steps in torch (F.rms_norm in bf16, x |temp|, interleaved RoPE
+    in fp32 as oracle/lm.py restates it, then the KV store): q and the stored k within bf16 rounding, v bit-exact,
+    out-of-range slots untouched."""
+    import torch.nn.functional as F
+    from oracle import lm as olm
+
+    gen = torch.Generator().manual_seed(17)
+    N, Hq, Hkv, hd, slots = 40, 16, 4, 128, 500
+    width = (Hq + 2 * Hkv) * hd + Hq  # q | k | v | gate columns, as the fused projection lays them out
+    proj = torch.randn(N, width, generator=gen).bfloat16()
+    temp = (torch.randn(Hq, generator=gen) * 2).bfloat16()
+    positions = torch.randint(0, 4000, (N,), generator=gen, dtype=torch.int32)
+    out_loc = torch.randperm(slots, generator=gen)[:N].to(torch.int32)
+    out_loc[3], out_loc[7] = -1, slots + 9
+    dev = torch.device("cuda")
+    kc = torch.zeros(slots, Hkv, hd, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    q = zb.ops.gqa_prologue_decode(proj.to(dev), temp.to(dev), positions.to(dev), kc, vc, out_loc.to(dev),
+                                   heads=Hq, kv_heads=Hkv)
+    qr = proj[:, : Hq * hd].view(N, Hq, hd)
+    kr = proj[:, Hq * hd: (Hq + Hkv) * hd].view(N, Hkv, hd)
+    vr = proj[:, (Hq + Hkv) * hd: (Hq + 2 * Hkv) * hd].reshape(N, Hkv, hd)
+    qn = F.rms_norm(qr.to(dev), (hd,), eps=1e-6) * temp.abs().to(dev).view(1, Hq, 1)
+    kn = F.rms_norm(kr.to(dev), (hd,), eps=1e-6)
+    q_ref = olm.rope_interleaved(qn.cpu(), positions.long(), 10000.0)
+    k_ref = olm.rope_interleaved(kn.cpu(), positions.long(), 10000.0)
+    torch.testing.assert_close(q.float().cpu(), q_ref.float(), atol=3e-2, rtol=2e-2)
+    ok = (out_loc >= 0) & (out_loc < slots)
+    torch.testing.assert_close(kc.float().cpu()[out_loc[ok].long()], k_ref[ok].float(), atol=3e-2, rtol=2e-2)
+    assert torch.equal(vc.cpu()[out_loc[ok].long()], vr[ok])
+    untouched = torch.ones(slots, dtype=torch.bool)
+    untouched[out_loc[ok].long()] = False
+    assert kc.cpu()[untouched].eq(0).all() and vc.cpu()[untouched].eq(0).all()

@@ -75,6 +75,9 @@ SIGNATURES: dict[str, list] = {
     # probs_out, stream
     "zb_sample_tts": [_p, _i32, _f32, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
                       _i32, _p, _u64, _u64, _i32, _p, _p, _p],
+    # proj, proj_stride, temp, positions, theta, eps, q_out, k_cache, v_cache, slot_stride, num_slots, out_loc, N,
+    # Hq, Hkv, hd, stream
+    "zb_gqa_prologue_decode": [_p, _i64, _p, _p, _f32, _f32, _p, _p, _p, _i64, _i64, _p, _i32, _i32, _i32, _i32, _p],
     "zb_gqa_decode": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _p,
                       _i64, _p, _i64, _p],
 }

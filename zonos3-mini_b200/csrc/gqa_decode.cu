@@ -772,3 +772,102 @@ ZB_API int zb_kv_store(uint16_t* k_cache, uint16_t* v_cache, int64_t slot_stride
   ZB_CUDA(zb::launch(kv_store_kernel, dim3((unsigned)((2 * (int64_t)N + 7) / 8)), dim3(256), 0, stream, 1, p));
   return zb::check_launch("kv_store");
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// The attention layer's decode prologue in one kernel: from the fused projection rows [N, Hq*hd | Hkv*hd | Hkv*hd]
+// (q | k | v, then anything after, row stride proj_stride), per token t and head: q = bf16(RMSNorm(q_h, eps)),
+// q = bf16(q * bf16(|temp_h|)), k = bf16(RMSNorm(k_g, eps)), both rotated by interleaved RoPE at positions[t]
+// (pairs (2i, 2i+1), inverse frequency 1 / theta^(2i / hd)), q written to q_out [N, Hq, hd], k and v written to
+// slot out_loc[t] of the caches (a slot outside [0, num_slots) stores nothing). Follows Attention.forward
+// (servers/sgl/src/zonos3_sgl/models/zonos3.py:340-375: rms_norm, |temp|, rotary with is_neox=False, store_kv).
+// A warp per (token, head), lane l owning dims 4l .. 4l+3 (two rotation pairs).
+namespace {
+
+struct PrologueParams {
+  const __nv_bfloat16* proj;
+  int64_t proj_stride;
+  const __nv_bfloat16* temp;  // [Hq]
+  const int32_t* positions;   // [N]
+  float theta, eps;
+  __nv_bfloat16* q_out;  // [N, Hq, 128]
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t slot_stride, num_slots;
+  const int32_t* out_loc;  // [N]
+  int N, Hq, Hkv;
+};
+
+__global__ void __launch_bounds__(256) gqa_prologue_kernel(PrologueParams p) {
+  zb::pdl_enter();
+  constexpr int HD = 128;
+  const int heads = p.Hq + 2 * p.Hkv;
+  const int64_t unit = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (unit >= (int64_t)p.N * heads) return;
+  const int t = (int)(unit / heads), h = (int)(unit % heads);
+  const int64_t slot = p.out_loc[t];
+  const bool store = slot >= 0 && slot < p.num_slots;
+  const __nv_bfloat16* src = p.proj + (int64_t)t * p.proj_stride + (int64_t)h * HD + 4 * lane;
+  float x[4];
+  zb::ld_bf16x4(src, x);
+  if (h >= p.Hq + p.Hkv) {  // v: copied into the cache
+    if (store) {
+      *reinterpret_cast<uint2*>(p.v_cache + slot * p.slot_stride + (int64_t)(h - p.Hq - p.Hkv) * HD + 4 * lane) =
+          *reinterpret_cast<const uint2*>(src);
+    }
+    return;
+  }
+  const float ss = zb::warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+  const float r = rsqrtf(ss / HD + p.eps);
+  const bool is_q = h < p.Hq;
+  const float tq = is_q ? zb::bf16_round(fabsf(__bfloat162float(p.temp[h]))) : 1.f;
+  float y[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    y[k] = zb::bf16_round(x[k] * r);
+    if (is_q) y[k] = zb::bf16_round(y[k] * tq);
+  }
+  const float pos = (float)p.positions[t];
+  uint32_t word[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = 2 * lane + k;  // rotation pair (dims 2i, 2i+1)
+    const float inv_freq = 1.0f / powf(p.theta, (float)(2 * i) / HD);
+    float sn, cs;
+    sincosf(pos * inv_freq, &sn, &cs);
+    const float a = y[2 * k], b = y[2 * k + 1];
+    const __nv_bfloat162 rot = __floats2bfloat162_rn(a * cs - b * sn, a * sn + b * cs);
+    word[k] = *reinterpret_cast<const uint32_t*>(&rot);
+  }
+  const uint2 packed = make_uint2(word[0], word[1]);
+  if (is_q) {
+    *reinterpret_cast<uint2*>(p.q_out + ((int64_t)t * p.Hq + h) * HD + 4 * lane) = packed;
+  } else if (store) {
+    *reinterpret_cast<uint2*>(p.k_cache + slot * p.slot_stride + (int64_t)(h - p.Hq) * HD + 4 * lane) = packed;
+  }
+}
+
+}  // namespace
+
+ZB_API int zb_gqa_prologue_decode(const uint16_t* proj, int64_t proj_stride, const uint16_t* temp,
+                                  const int32_t* positions, float rope_theta, float eps, uint16_t* q_out,
+                                  uint16_t* k_cache, uint16_t* v_cache, int64_t slot_stride, int64_t num_slots,
+                                  const int32_t* out_loc, int N, int Hq, int Hkv, int hd, cudaStream_t stream) {
+  ZB_REQUIRE(N >= 0 && Hq > 0 && Hkv > 0, "gqa_prologue_decode: sizes N=%d Hq=%d Hkv=%d", N, Hq, Hkv);
+  if (hd != 128) return zb::fail(zb::kUnsupported, "gqa_prologue_decode: head dim %d (128)", hd);
+  if (N == 0) return zb::kOk;
+  ZB_REQUIRE(proj && temp && positions && q_out && k_cache && v_cache && out_loc, "gqa_prologue_decode: null pointer");
+  ZB_REQUIRE(proj_stride >= (int64_t)(Hq + 2 * Hkv) * hd && proj_stride % 4 == 0 && slot_stride >= (int64_t)Hkv * hd &&
+                 slot_stride % 4 == 0,
+             "gqa_prologue_decode: strides (proj %lld, slot %lld)", (long long)proj_stride, (long long)slot_stride);
+  for (const void* ptr : {(const void*)proj, (const void*)q_out, (const void*)k_cache, (const void*)v_cache}) {
+    ZB_REQUIRE_ALIGNED(ptr, 8, "gqa_prologue_decode tensors");
+  }
+  PrologueParams p{reinterpret_cast<const __nv_bfloat16*>(proj), proj_stride,
+                   reinterpret_cast<const __nv_bfloat16*>(temp), positions, rope_theta, eps,
+                   reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<__nv_bfloat16*>(k_cache),
+                   reinterpret_cast<__nv_bfloat16*>(v_cache), slot_stride, num_slots, out_loc, N, Hq, Hkv};
+  const int64_t units = (int64_t)N * (Hq + 2 * Hkv);
+  ZB_CUDA(zb::launch(gqa_prologue_kernel, dim3((unsigned)((units + 7) / 8)), dim3(256), 0, stream, 1, p));
+  return zb::check_launch("gqa_prologue_decode");
+}

@@ -770,3 +770,33 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
               int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), int(text_vocab), out.data_ptr(), ptr(probs_out),
               _stream(dev))
     return out
+
+
+def gqa_prologue_decode(proj, temp, positions, k_cache, v_cache, out_loc, *, heads, kv_heads, rope_theta=10000.0,
+                        eps=1e-6, q_out=None):
+    """The attention layer's decode prologue (Attention.forward, servers/sgl/src/zonos3_sgl/models/zonos3.py:340-375)
+    in one kernel: proj [N, >= (heads + 2 kv_heads) * 128] bf16 holds q | k | v (rows contiguous, row stride
+    allowed); q gets RMSNorm (eps) x |temp| and interleaved RoPE at ``positions`` ([N] int32), k RMSNorm and RoPE;
+    k and v go to slot ``out_loc[t]`` of k_cache / v_cache ([slots, kv_heads, 128] bf16). Returns q [N, heads, 128]."""
+    dev = proj.device
+    _check_cuda("proj", proj, torch.bfloat16)
+    N = proj.shape[0]
+    hd = 128
+    _require(proj.dim() == 2 and proj.stride(1) == 1 and proj.shape[1] >= (heads + 2 * kv_heads) * hd,
+             "proj must be [N, >= (heads + 2 kv_heads) * 128] with contiguous rows")
+    for name, t in (("temp", temp), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+    _require(temp.numel() == heads and temp.is_contiguous(), f"temp must hold {heads} values")
+    _check_cuda("positions", positions, torch.int32, dev)
+    _check_cuda("out_loc", out_loc, torch.int32, dev)
+    _require(positions.shape == (N,) and out_loc.shape == (N,), "positions and out_loc must be [N]")
+    cs = _rows("k_cache", k_cache, (kv_heads, hd))
+    _require(v_cache.shape == k_cache.shape and v_cache.stride() == k_cache.stride(), "v_cache must match k_cache")
+    if q_out is None:
+        q_out = torch.empty(N, heads, hd, device=dev, dtype=torch.bfloat16)
+    _check_cuda("q_out", q_out, torch.bfloat16, dev)
+    _require(q_out.shape == (N, heads, hd) and q_out.is_contiguous(), f"q_out must be a contiguous [{N}, {heads}, 128]")
+    _lib.call("zb_gqa_prologue_decode", proj.data_ptr(), proj.stride(0) if N > 1 else proj.shape[1], temp.data_ptr(),
+              positions.data_ptr(), float(rope_theta), float(eps), q_out.data_ptr(), k_cache.data_ptr(),
+              v_cache.data_ptr(), cs, k_cache.shape[0], out_loc.data_ptr(), N, heads, kv_heads, hd, _stream(dev))
+    return q_out
