@@ -773,7 +773,7 @@ def cpu_reference(updates: int, streams=STREAMS):
 def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
     updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5
-    DeltaNet + MoE decode layers, cfg5 GQA decode attention, or cfg5 backbone decode steps."""
+    DeltaNet + MoE decode layers, cfg5 GQA decode attention, cfg5 backbone decode steps, or cfg5 sampler calls."""
     ops = __import__("__graft_entry__").load_package().ops
     dev = torch.device("cuda", 0)
     if workload == "moe":
@@ -811,6 +811,17 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
             ops.gdn_chunk_prefill(q, k, v, g, beta, cu)
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg3 chunked prefills done")
+        return
+    if workload == "sampler":
+        gen = torch.Generator().manual_seed(8)
+        logits = (3 * torch.randn(256, 10, 4098, generator=gen)).to(dev)
+        rep = torch.randint(0, 4098, (256, 10, 32), generator=gen, dtype=torch.int32).to(dev)
+        for i in range(n):
+            ops.sample_tts(logits, [0.8] * 256, [50], [0.9], [0.0], codebook_size=4096, audio_pad_id=4097,
+                           stop_token_ids=[4096] * 256, repetition_token_ids=rep,
+                           repetition_penalties=torch.full((256,), 1.2), seed=1, offset=i)
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg5 sampler calls done")
         return
     if workload == "full_step":
         step, core, batch = full_step_cfg5(__import__("__graft_entry__").load_package(), dev)
@@ -868,7 +879,7 @@ def main():
                     help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
     ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill",
                                                                          "decode_layer", "gqa_decode",
-                                                                         "full_step"),
+                                                                         "full_step", "sampler"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
