@@ -1,24 +1,36 @@
 """Benchmark of the ZONOS3-Mini hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Default workload ("cfg2"): gated-DeltaNet recurrent decode of 64 streams x 16 heads,
-dk = dv = 128, 512 sequential single-token state updates with per-step outputs. One bench step is that whole run.
-The 64 MB state of one layer fits in the 126 MB L2, while in the model every GDN layer owns a state and the rest
-of the step runs between two updates of it, so the bench keeps LAYERS = 4 independent layer states and updates
-them round-robin (256 MB of state, more than L2; no flush needed). An audio token is one decode update of one
-stream; value = streams x layers x 512 x K x N / max-over-ranks time.
+Default workload ("cfg5"): the decode step of the 24-layer hybrid LM (hidden 2048; 18 gated-
+DeltaNet layers of 16 heads at 128/128 and 6 GQA layers of 16 q / 4 kv heads at 128 in the 3:1 pattern; an MoE FFN
+of 64 experts, top-8, SwiGLU 768 in every layer; Full AttnRes; a 10-codebook head over 4098 ids) for 256 concurrent
+streams per GPU, run through the package's public API: ``Zonos3ForCausalLM`` and its captured ``DecodeGraph``
+(embedding -> 49 AttnRes routes and 48 sublayers -> head GEMM -> soft cap + TTS sampler -> the next step's ids).
+An audio token is one decode step of one stream (one 10-code frame); value = 256 x K x N / max-over-ranks time.
 
-Multi-GPU: one process per GPU (torchrun), each rank runs its own 64-stream replica (request sharding, no
-collective on the data path); the only collectives are the barrier and the max-reduction of the timings.
+The 1500-step generation of the config runs from the middle of its cache (878 keys: the 128-token prompt and 750
+decode steps) and each replay appends one more key per stream, as a decode loop does. Weights are random-init
+(N(0, 0.02)), generated on the device; the KV cache, DeltaNet states and conv histories are random too. Each step
+reads 15.6 GB of weights, far more than the 126 MB L2, so no flush is needed between steps.
 
-``--impl reference`` times the reference's CPU implementation of the same path (the per-token recurrence of
-model/src/zonos3/reference/lm.py:576-582, restated in oracle/gdn.py) on the host cores, on rank 0 only.
+``value``: graph replays only (ids, metadata, codes stay on the device; each replay feeds its codes back).
+``e2e``: ``DecodeGraph.step()`` per step: the ids and the attention metadata copied in from pinned host memory, the
+sampled codes copied back and the host synchronised before the next step's ids are built from them.
+
+Multi-GPU: one process per GPU (torchrun), each rank runs its own 256-stream replica (request sharding, no collective
+on the data path; weak scaling); the only collectives are the barrier and the max-reduction of the timings.
+
+``--impl reference`` times the reference's CPU implementation of the same step: the oracle port of Zonos3LM.forward
+(model/src/zonos3/reference/lm.py:660-735, restated in oracle/lm.py) on the host cores, one stream at a time (the
+reference processes one sequence per call) on a 4-layer slice of the cfg5 model and on its 0-layer remainder
+(embedding, final route, head), scaled to 24 layers.
 """
 
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -37,7 +49,18 @@ sys.path.insert(0, str(ROOT))
 METRIC = "audio tokens/sec per box"
 UNIT = "tokens/s"
 
-# cfg2
+# cfg5
+D5, LAYERS5 = 2048, 24
+GDN_H, GDN_D = 16, 128
+HQ, HKV, HD = 16, 4, 128
+E5, K5, I5 = 64, 8, 768
+CODEBOOKS, CODEBOOK_SIZE, TEXT_VOCAB = 10, 4096, 8192
+STREAMS5, PROMPT5, DECODE5 = 256, 128, 1500
+CONTEXT5 = PROMPT5 + DECODE5 // 2  # keys cached before the first timed step's new row
+MAX_LEN5 = PROMPT5 + DECODE5
+SAMPLING5 = dict(temperature=0.8, top_k=50, top_p=0.9, min_p=0.0, repetition_window=32, repetition_penalty=1.2)
+
+# cfg2 (operator line)
 STREAMS, HEADS, DK, DV, UPDATES = 64, 16, 128, 128, 512
 LAYERS = 4
 
@@ -134,7 +157,8 @@ def max_over_ranks(dist, value: float) -> float:
     return float(t.item())
 
 
-# --------------------------------------------------------------------------------------------- cfg2 workload
+
+# --------------------------------------------------------------------------------------------- cfg2 inputs
 
 
 def cfg2_inputs(seed: int, device, streams=STREAMS):
@@ -160,29 +184,115 @@ def bytes_per_update(streams=STREAMS) -> int:
     return streams * HEADS * (2 * DK * DV * 4 + (2 * DK + DV) * 2 + 2 * 4 + DV * 2)
 
 
+# --------------------------------------------------------------------------------------------- cfg5 decode step
+
+
+def cfg5_model_config(pkg, layers: int = LAYERS5):
+    return pkg.config.ModelConfig(
+        hidden_size=D5, num_layers=layers, gdn_num_heads=GDN_H, gdn_head_dim=GDN_D, moe_n_experts=E5, moe_topk=K5,
+        moe_intermediate_size=I5, moe_start_from_layer=0, norm_topk_prob=True, use_training_router_weights=True,
+        attention_pattern="gdn3_global1", num_qo_heads=HQ, num_kv_heads=HKV, head_dim=HD, n_codebooks=CODEBOOKS,
+        codebook_size=CODEBOOK_SIZE, text_vocab=TEXT_VOCAB, audio_pad_id=CODEBOOK_SIZE + 1, loss_softcap=15.0)
+
+
+def cfg5_page_table(streams: int, device, prompt: int = PROMPT5, max_len: int = MAX_LEN5):
+    """Slots as a token pool hands them out: each prompt one contiguous block, then every decode step one slot per
+    stream (a stream's decode keys sit `streams` slots apart). Returns (page_table [streams, max_len] int32,
+    number of slots)."""
+    b = torch.arange(streams, dtype=torch.int64)[:, None]
+    pos = torch.arange(max_len, dtype=torch.int64)[None, :]
+    table = torch.where(pos < prompt, b * prompt + pos, streams * prompt + (pos - prompt) * streams + b)
+    return table.to(torch.int32).to(device), streams * max_len
+
+
+def random_init_(model, seed: int, device) -> None:
+    """Seeded random init on the device, as oracle/lm.py random_weights draws it: matrices N(0, 0.02^2), conv
+    weights N(0, 0.3^2), norm weights and |temp| 1, A_log = dt_bias = balancing biases = 0."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    for name, t in model.state_dict().items():
+        if name.endswith(("norm.weight", "rmsnorm_eda.weight", "out_weight", ".temp")):
+            t.fill_(1.0)
+        elif name.endswith(("A_log", "dt_bias", "balancing_biases")):
+            t.zero_()
+        elif name.endswith("conv.weight"):
+            t.normal_(0.0, 0.3, generator=gen)
+        else:
+            t.normal_(0.0, 0.02, generator=gen)
+
+
+def build_cfg5(pkg, dev, streams: int = STREAMS5, layers: int = LAYERS5, seed: int = 0, context: int = CONTEXT5):
+    """The cfg5 model with random weights, its caches at `context` cached keys per stream (random KV rows,
+    DeltaNet states N(0, 0.01^2), conv histories N(0, 1)), and its captured decode step. Returns (model, graph)."""
+    cfg = cfg5_model_config(pkg, layers)
+    with torch.device(dev):
+        model = pkg.model.Zonos3ForCausalLM(cfg)
+    model.to(dev, torch.bfloat16)
+    random_init_(model, seed, dev)
+    table, kv_slots = cfg5_page_table(streams, dev)
+    pool = model.allocate_caches(streams, kv_slots, dev)
+    sampling = pkg.model.SamplingConfig(seed=seed, **SAMPLING5)
+    graph = pkg.model.DecodeGraph(model, pool, streams, table, sampling=sampling)
+    graph.capture()
+    gen = torch.Generator(device=dev).manual_seed(seed + 1)
+    pool.k_buffer.normal_(generator=gen)
+    pool.v_buffer.normal_(generator=gen)
+    for gdn in model.gdn_layers():
+        gdn._recurrent_state.normal_(0.0, 0.01, generator=gen)
+        gdn._conv_state.normal_(generator=gen)
+    ids = torch.randint(0, CODEBOOK_SIZE, (streams, CODEBOOKS + 1), generator=gen, device=dev, dtype=torch.int32)
+    ids[:, -1] = TEXT_VOCAB  # the text column of a decode row: the text pad id
+    graph.load(ids, torch.full((streams,), context, dtype=torch.int32, device=dev),
+               torch.full((streams,), context + 1, dtype=torch.int32, device=dev), table[:, context].contiguous())
+    torch.cuda.synchronize(dev)
+    return model, graph
+
+
+def cfg5_step_bytes(streams: int, context: int, layers: int = LAYERS5) -> int:
+    """Algorithmic bytes of one cfg5 decode step, each read or write counted once: every expert's weights (2048
+    routed pairs over 64 experts touch all of them) and the router weights; per DeltaNet layer the in_proj / wo
+    weights, the fp32 states and bf16 conv histories read and written; per GQA layer the projection weights and the
+    K / V rows of `context` + 1 keys (and their page-table entries); the AttnRes bank (route r reads r + 1 rows and
+    writes one); the embedding rows, the head weights and the bf16 logits written and read back."""
+    inner = GDN_H * GDN_D
+    n_gqa = layers // 4
+    n_gdn = layers - n_gqa
+    keys = context + 1
+    moe = layers * (E5 * 3 * I5 * D5 * 2 + E5 * D5 * 2)
+    gdn = n_gdn * (((4 * inner + 2 * GDN_H) * D5 + D5 * inner) * 2 + streams * GDN_H * GDN_D * GDN_D * 4 * 2
+                   + streams * 3 * inner * 3 * 2 * 2)
+    gqa = n_gqa * (((HQ * HD + 2 * HKV * HD + HQ) * D5 + D5 * HQ * HD) * 2 + streams * keys * (HKV * HD * 2 * 2 + 4))
+    routes = 2 * layers + 1
+    attnres = sum(r + 2 for r in range(routes)) * streams * D5 * 2
+    vocab = CODEBOOKS * (CODEBOOK_SIZE + 2)
+    head = streams * (CODEBOOKS + 1) * D5 * 2 + vocab * D5 * 2 + 2 * streams * vocab * 2
+    return moe + gdn + gqa + attnres + head
+
+
+def cfg5_config(world: int) -> dict:
+    return {
+        "workload": "cfg5 decode step: 256 streams per GPU, 24-layer hybrid LM (hidden 2048; 18 gated-DeltaNet "
+                    "16 x 128/128 + 6 GQA 16/4 x 128 over a 878..1628-key cache; MoE 64 experts top-8 SwiGLU 768 in "
+                    "every layer; Full AttnRes, 49 routes; head 10 x 4098 with soft cap 15; TTS sampler t=0.8 top-k 50 "
+                    "top-p 0.9 repetition window 32 x 1.2); embedding -> backbone -> head -> sampler in one CUDA graph",
+        "model": "ZONOS3-Mini cfg5 (random init; 7.9 B total / ~1.6 B active parameters)",
+        "streams_per_gpu": STREAMS5, "global_batch": STREAMS5 * world, "seq_len": MAX_LEN5,
+        "context_start": CONTEXT5, "layers": LAYERS5, "token": "one decode step of one stream (one 10-code frame)",
+        "l2": "no flush: each step reads 15.6 GB of weights (> 126 MB L2)",
+        "parallelism": f"replicas x{world} (request-sharded, no collective)",
+    }
+
+
 def run_ours(args, dist, rank, world, local):
     pkg = __import__("__graft_entry__").load_package()
-    ops = pkg.ops
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    seed = 1234 + rank
-    q, k, v, g, beta = cfg2_inputs(seed, dev)
-    states = [cfg2_state(seed + 1 + l, dev) for l in range(LAYERS)]
-    outs = torch.empty(LAYERS, UPDATES, STREAMS, HEADS, DV, device=dev, dtype=torch.bfloat16)
+    model, graph = build_cfg5(pkg, dev, seed=1234 + rank)
     stream = torch.cuda.Stream(dev)
-
-    def one_step():
-        for t in range(UPDATES):
-            for l in range(LAYERS):
-                ops.gdn_decode_step(q[t], k[t], v[t], g[t], beta[t], states[l], outs[l, t])
-
-    launches_per_step = UPDATES * LAYERS
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    total_steps = args.warmup + args.steps + args.warmup + args.e2e_steps
+    if CONTEXT5 + 1 + total_steps > MAX_LEN5:
+        raise SystemExit(f"{total_steps} steps would run past the {MAX_LEN5}-key cache")
     with torch.cuda.stream(stream):
-        one_step()  # eager warm-up (loads the library, first launch)
-        torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            one_step()
         for _ in range(args.warmup):
             graph.replay()
         torch.cuda.synchronize(dev)
@@ -198,78 +308,165 @@ def run_ours(args, dist, rank, world, local):
         barrier(dist)
         torch.cuda.synchronize(dev)
     elapsed_ms = max_over_ranks(dist, start.elapsed_time(stop))
-    del graph
+    status = pkg.ops.device_status()
 
-    # end to end through the public op with host buffers: every update copies its inputs from pinned host memory
-    # and reads its output back, all inside the timed region
-    host = [t.cpu().pin_memory() for t in (q, k, v, g, beta)]
-    host_out = torch.empty(UPDATES, STREAMS, HEADS, DV, dtype=torch.bfloat16).pin_memory()
-    dq = [torch.empty_like(t[0]) for t in (q, k, v, g, beta)]
-    h2d_update = sum(t[0].numel() * t.element_size() for t in host)
-    d2h_update = host_out[0].numel() * host_out.element_size()
-    e2e_steps = max(1, min(args.steps, 3))
+    # end to end through DecodeGraph.step: host ids + metadata in, codes out, host synchronised every step (the
+    # next step's ids are the codes just read back)
+    pos0 = int(graph.positions[0].item())
+    table = graph.page_table.cpu()
+    n_e2e = args.e2e_steps
+    host_ids = graph.input_ids.cpu().pin_memory()
+    host_codes = torch.empty(STREAMS5, CODEBOOKS + 1, dtype=torch.int32).pin_memory()
+    meta = []
+    for i in range(args.warmup + n_e2e):
+        p = pos0 + i
+        meta.append((torch.full((STREAMS5,), p, dtype=torch.int32).pin_memory(),
+                     torch.full((STREAMS5,), p + 1, dtype=torch.int32).pin_memory(),
+                     table[:, p].contiguous().pin_memory()))
+    h2d = host_ids.numel() * 4 + sum(t.numel() * 4 for t in meta[0])
+    d2h = host_codes.numel() * 4
+
+    def e2e_step(i):
+        graph.step(host_ids, host_codes, *meta[i])
+        torch.cuda.current_stream(dev).synchronize()
+        host_ids.copy_(host_codes[:, : host_ids.shape[1]])
+        host_ids[:, -1] = TEXT_VOCAB
+
     with torch.cuda.stream(stream):
-        def e2e_step():
-            for t in range(UPDATES):
-                for l in range(LAYERS):
-                    for dst, src in zip(dq, host):
-                        dst.copy_(src[t], non_blocking=True)
-                    o = ops.gdn_decode_step(dq[0], dq[1], dq[2], dq[3], dq[4], states[l], outs[l, t])
-                    host_out[t].copy_(o, non_blocking=True)
-        e2e_step()
-        torch.cuda.synchronize(dev)
+        for i in range(args.warmup):
+            e2e_step(i)
         barrier(dist)
+        torch.cuda.synchronize(dev)
         e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
+        for i in range(n_e2e):
+            e2e_step(args.warmup + i)
         e_stop.record(stream)
         torch.cuda.synchronize(dev)
         barrier(dist)
     e2e_ms = max_over_ranks(dist, e_start.elapsed_time(e_stop))
 
-    tokens_per_step = STREAMS * LAYERS * UPDATES
-    value = tokens_per_step * args.steps * world / (elapsed_ms / 1e3)
-    e2e_value = tokens_per_step * e2e_steps * world / (e2e_ms / 1e3)
+    step_ms = elapsed_ms / args.steps
+    context_mid = CONTEXT5 + args.warmup + args.steps // 2
+    nbytes = cfg5_step_bytes(STREAMS5, context_mid)
     pk = peaks()
-    bytes_launch = bytes_per_update()
-    launch_s = elapsed_ms / 1e3 / (args.steps * launches_per_step)
-    achieved = bytes_launch / launch_s / 1e9
+    achieved = nbytes / (step_ms / 1e3) / 1e9
     line = {
         "metric": METRIC,
-        "value": value,
+        "value": STREAMS5 * args.steps * world / (elapsed_ms / 1e3),
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": elapsed_ms / args.steps,
+        "ms_per_step": step_ms,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded cfg2 distributions; random state N(0, 0.01^2))",
-        "config": {
-            "workload": "cfg2 gated-DeltaNet recurrent decode: 64 streams x 16 heads, dk=dv=128, 512 sequential "
-                        "single-token updates with per-step outputs; 4 layer states round-robin",
-            "streams_per_gpu": STREAMS, "heads": HEADS, "dk": DK, "dv": DV, "updates_per_step": UPDATES,
-            "layer_states": LAYERS, "token": "one decode update of one stream",
-            "l2": "state working set 256 MB > 126 MB L2 (no flush)", "graph": "CUDA graph of one step",
-            "parallelism": f"replicas x{world} (request-sharded, no collective)",
-        },
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0, 0.02); random KV cache / DeltaNet states; sampled codes fed back)",
+        "config": cfg5_config(world),
         "roofline": {
-            "kernel": "gdn_decode_kernel<128>", "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
-            "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
-            "algorithmic_bytes_per_launch": bytes_launch, "avg_launch_us": launch_s * 1e6,
+            "kernel": "whole decode step (one CUDA graph)", "bound": "hbm", "achieved": achieved,
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "traffic": profiled_traffic("decode_step_cfg5.md"), "algorithmic_bytes_per_step": nbytes,
             "peak_source": pk["source"],
         },
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_update * LAYERS * UPDATES,
-                "d2h_bytes_per_step": d2h_update * LAYERS * UPDATES,
-                "path": "ops.gdn_decode_step per update with pinned-host copies in and out"},
-        "gpu_launches": args.steps * launches_per_step,
+        "e2e": {"value": STREAMS5 * n_e2e * world / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / n_e2e,
+                "path": "DecodeGraph.step: pinned host ids + positions / cache lengths / KV slots in, codes out, "
+                        "host sync per step"},
+        "gpu_launches": graph.launches_per_step * args.steps,
+        "launches_per_step": graph.launches_per_step,
+        "device_status": status,
         "clocks": clocks.summary(),
     }
-    line["roofline"]["traffic"] = profiled_traffic("gdn_decode_cfg2.md")
+    del graph, model
+    torch.cuda.empty_cache()
     return line
+
+
+# --------------------------------------------------------------------------------------------- CPU reference
+
+
+def cfg5_oracle_config(layers: int):
+    from oracle import lm as olm
+
+    return olm.LMConfig(dim=D5, n_layers=layers, gdn_period=4, gdn_heads=GDN_H, gdn_head_dim=GDN_D, n_heads=HQ,
+                        n_kv_heads=HKV, head_dim=HD, n_experts=E5, topk=K5, moe_hidden=I5, moe_routed_dim=D5,
+                        n_codebooks=CODEBOOKS, codebook_size=CODEBOOK_SIZE, text_rows=TEXT_VOCAB + 1)
+
+
+def cpu_reference_cfg5(samples: int, seed: int = 99):
+    """Time the reference's CPU forward (oracle/lm.py restating Zonos3LM.forward, lm.py:660-735, fp32) for one
+    stream's decode step at cfg5 shapes on this host's cores, from a cache of CONTEXT5 keys: `samples` steps of a
+    4-layer slice (3 DeltaNet + 1 GQA, one period of the 3:1 pattern) and of the 0-layer remainder (embedding,
+    final route, head). One 24-layer stream-step = t0 + 24 x (t4 - t0) / 4. Returns (tokens/s, threads, seconds,
+    per-stream-step seconds)."""
+    from oracle import lm as olm
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    c4 = cfg5_oracle_config(4)
+    w4 = olm.random_weights(c4, seed)
+    c0 = dataclasses.replace(c4, n_layers=0)
+    w0 = {k: v for k, v in w4.items() if not k.startswith("layers.")}
+    w0["block_attnres_queries"] = w4["block_attnres_queries"][-1:]
+    gen = torch.Generator().manual_seed(seed + 1)
+
+    def cache(c):
+        cc = olm.Cache(position=CONTEXT5)
+        for layer in range(c.n_layers):
+            if c.uses_gdn(layer):
+                cc.gdn_state[layer] = 0.01 * torch.randn(GDN_H, GDN_D, GDN_D, generator=gen)
+                cc.conv_state[layer] = torch.randn(3 * GDN_H * GDN_D, 3, generator=gen)
+            else:
+                cc.kv[layer] = (torch.randn(CONTEXT5, HKV, HD, generator=gen), torch.randn(CONTEXT5, HKV, HD, generator=gen))
+        return cc
+
+    caches = (cache(c4), cache(c0))
+    ids = torch.randint(0, CODEBOOK_SIZE, (1, CODEBOOKS + 1), generator=gen)
+    ids[:, -1] = TEXT_VOCAB
+    times = [0.0, 0.0]
+    t_all = time.perf_counter()
+    with torch.no_grad():
+        for i in range(samples + 1):  # the first sample of each model is a warm-up
+            for j, (c, w) in enumerate(((c4, w4), (c0, w0))):
+                t0 = time.perf_counter()
+                olm.forward(c, w, ids, caches[j])
+                if i:
+                    times[j] += time.perf_counter() - t0
+    t4, t0 = times[0] / samples, times[1] / samples
+    per_step = t0 + LAYERS5 * (t4 - t0) / 4
+    return 1.0 / per_step, torch.get_num_threads(), time.perf_counter() - t_all, per_step
+
+
+# --------------------------------------------------------------------------------------------- cfg2 operator
+
+
+def bench_gdn_decode_cfg2(ops, dev, stream, reps=3):
+    """cfg2: 512 sequential single-token gated-DeltaNet updates of 64 streams x 16 heads at 128/128 with per-step
+    outputs, cycling 4 independent layer states (256 MB > L2, as each layer owns its state in the model); one CUDA
+    graph of the 2048 launches."""
+    q, k, v, g, beta = cfg2_inputs(1234, dev)
+    states = [cfg2_state(1235 + l, dev) for l in range(LAYERS)]
+    outs = torch.empty(LAYERS, UPDATES, STREAMS, HEADS, DV, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        for t in range(UPDATES):
+            for l in range(LAYERS):
+                ops.gdn_decode_step(q[t], k[t], v[t], g[t], beta[t], states[l], outs[l, t])
+
+    ms = graph_ms(run, stream, reps=reps, warmup=2)
+    launches = UPDATES * LAYERS
+    launch_s = ms / 1e3 / launches
+    nbytes = bytes_per_update()
+    pk = peaks()
+    return {"workload": "cfg2 gated-DeltaNet recurrent decode: 64 streams x 16 heads, dk=dv=128, 512 updates x 4 "
+                        "layer states",
+            "ms": ms, "updates_per_s": STREAMS * launches / (ms / 1e3),
+            "roofline": {"kernel": "gdn_decode_kernel<128>", "bound": "hbm", "achieved": nbytes / launch_s / 1e9,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": nbytes / launch_s / 1e9 / pk["hbm_gbs"],
+                         "traffic": profiled_traffic("gdn_decode_cfg2.md"), "algorithmic_bytes_per_launch": nbytes,
+                         "avg_launch_us": launch_s * 1e6, "peak_source": pk["source"]}}
 
 
 # --------------------------------------------------------------------------------------------- operator timings
@@ -525,122 +722,6 @@ def bench_decode_layer_cfg5(pkg, dev, stream, streams=256, bank_rows=24, reps=5)
     }
 
 
-def full_step_cfg5(pkg, dev, streams=256, context=878, n_layers=24):
-    """Builds one cfg5 decode step of the whole 24-layer backbone for `streams` streams (one new row each): layers in
-    the 3:1 DeltaNet:GQA pattern (layer i is GQA when i % 4 == 3), an MoE FFN in every layer and the Full AttnRes
-    schedule (a route before every sublayer and a final one: 49 routes over the layer-output bank, queries
-    registered, norms fused). GQA layers: fused wq / wkv / gater projection (cuBLAS), `ops.gqa_prologue_decode`
-    (q / k RMS norm with |temp|, interleaved RoPE and the KV store of the new row in one kernel), `ops.gqa_decode`
-    over `context` cached keys + the new one (the mid-run cache of a 128-token prompt + 1500 decode steps; prompt slots contiguous, decode
-    slots interleaved across streams), gate and wo. bf16 random-init weights N(0, 0.02), generated on the device.
-    Embedding and the multi-codebook head / sampler are not included. Returns (step, core, batch)."""
-    ops, core = pkg.ops, pkg.core
-    D, H, d, E, k, I = 2048, 16, 128, 64, 8, 768
-    Hq, Hkv, hd = 16, 4, 128
-    cfg = pkg.config.ModelConfig(hidden_size=D, gdn_num_heads=H, gdn_head_dim=d, moe_n_experts=E, moe_topk=k,
-                                 moe_intermediate_size=I, norm_topk_prob=True, use_training_router_weights=False)
-    gen = torch.Generator(device=dev).manual_seed(23)
-    rnd = lambda *shape, s=0.02: (s * torch.randn(*shape, generator=gen, device=dev)).bfloat16()  # noqa: E731
-    inner = H * d
-    tables = pkg.gdn.OriginalGDN.static_tables(dev, [streams])
-    slots = torch.arange(streams, device=dev, dtype=torch.int64)
-    layers = []
-    _, kc0, vc0, table_gq, seq_gq = gqa_cfg5_inputs(dev, streams, 128, context + 1, Hq, Hkv, hd)
-    n_slots = kc0.shape[0]
-    del kc0, vc0
-    out_loc = table_gq[:, context].contiguous()  # the new row's slot (the last entry of each request's table)
-    pos_i32 = torch.full((streams,), context, device=dev, dtype=torch.int32)  # the new row's position
-
-    for i in range(n_layers):
-        if i % 4 == 3:
-            mixer = {"w": rnd(Hq * hd + 2 * Hkv * hd + Hq, D), "wo": rnd(D, Hq * hd),
-                     "temp": torch.ones(Hq, device=dev, dtype=torch.bfloat16),
-                     "kc": rnd(n_slots, Hkv, hd, s=1.0), "vc": rnd(n_slots, Hkv, hd, s=1.0),
-                     "q": torch.empty(streams, Hq, hd, device=dev, dtype=torch.bfloat16),
-                     "o": torch.empty(streams, Hq, hd, device=dev, dtype=torch.bfloat16)}
-        else:
-            mixer = pkg.gdn.OriginalGDN(cfg, i)
-            mixer.to(dev, torch.bfloat16)  # device-side parameters: the weights below load without a host trip
-            mixer.load_state_dict({"in_proj.weight": rnd(4 * inner + 2 * H, D),
-                                   "conv.weight": rnd(3 * inner, 1, 4, s=0.3), "out_weight": torch.ones(d).bfloat16(),
-                                   "A_log": torch.zeros(H), "dt_bias": torch.zeros(H), "wo.weight": rnd(D, inner)})
-            mixer.allocate_cache(streams, dev, torch.bfloat16)
-            mixer.enable_graph_decode(slots, tables)
-            mixer.set_static_mode(True)
-        moe = pkg.moe.MoEFeedForward(cfg, i)
-        moe.to(dev, torch.bfloat16)
-        moe.load_state_dict({"router.router_linear.weight": rnd(E, D),
-                             "router.rmsnorm_eda.weight": torch.ones(D, dtype=torch.bfloat16),
-                             "router.balancing_biases": torch.zeros(E), "experts.gate_up_proj": rnd(E, 2 * I, D),
-                             "experts.down_proj": rnd(E, D, I)})
-        layers.append((mixer, moe))
-
-    def gqa(m, x):
-        p = F.linear(x, m["w"])  # q | k | v | gate
-        gate = p[:, Hq * hd + 2 * Hkv * hd:].sigmoid()
-        q = ops.gqa_prologue_decode(p, m["temp"], pos_i32, m["kc"], m["vc"], out_loc, heads=Hq, kv_heads=Hkv,
-                                    q_out=m["q"])
-        o = ops.gqa_decode(q, m["kc"], m["vc"], table_gq, seq_gq, out=m["o"])
-        return F.linear((o * gate.unsqueeze(-1)).reshape(streams, Hq * hd), m["wo"])
-
-    n_routes = 2 * n_layers + 1
-    bank = torch.empty(n_routes - 1, streams, D, device=dev, dtype=torch.bfloat16)
-    x0 = torch.randn(streams, D, generator=gen, device=dev).bfloat16()
-    queries = rnd(n_routes, D)
-    norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
-    table = torch.zeros(n_routes, streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
-    inv_rms = torch.ones(streams, (n_routes + 3) // 4 * 4, device=dev, dtype=torch.float32)
-    h = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
-    final = torch.empty(streams, D, device=dev, dtype=torch.bfloat16)
-    batch = core.Batch(reqs=[core.Req(i, 1, cached_len=context) for i in range(streams)], is_decode=True,
-                       padded_size=streams)
-
-    def step():
-        # route r mixes bank[:r] + its source (x0, then each sublayer's output) and appends the source as bank[r];
-        # the final route does not append (forward_layers_full's schedule)
-        source = x0
-        for r in range(n_routes - 1):
-            ops.attnres_route_tabled(bank, r, source, queries, r, table, inv_rms, 1e-5, append_to=bank[r],
-                                     norm_weight=norm_w, out=h)
-            mixer, moe = layers[r // 2]
-            if r % 2 == 0:
-                source = gqa(mixer, h) if isinstance(mixer, dict) else mixer.forward(h)
-            else:
-                source, _ = moe.forward(h)
-        return ops.attnres_route_tabled(bank, n_routes - 1, source, queries, n_routes - 1, table, inv_rms, 1e-5,
-                                        norm_weight=norm_w, out=final)
-
-    return step, core, batch
-
-
-def bench_full_step_cfg5(pkg, dev, stream, streams=256, context=878, reps=3):
-    """cfg5: one decode step of the 24-layer backbone (full_step_cfg5) for 256 streams, captured in one CUDA graph.
-    Weights (15.6 GB of experts alone) far exceed L2; no flush needed."""
-    step, core, batch = full_step_cfg5(pkg, dev, streams, context)
-    with core.forward_batch(batch):
-        ms = graph_ms(step, stream, reps, warmup=2)
-    # Algorithmic bytes of the step (each read or write once): every expert's weights (2048 routed pairs over 64
-    # experts touch all of them), the DeltaNet states and conv histories read and written, the mixers' projection
-    # weights, the KV cache rows, the AttnRes bank reads (route r reads r + 1 rows) and writes.
-    D, H, d, E, I, Hq, Hkv, hd, n_gdn, n_gqa = 2048, 16, 128, 64, 768, 16, 4, 128, 18, 6
-    inner = H * d
-    nbytes = (24 * (E * 3 * I * D * 2 + E * D * 2)
-              + n_gdn * (streams * H * d * d * 4 * 2 + streams * 3 * inner * 3 * 2 * 2
-                         + ((4 * inner + 2 * H) * D + D * inner) * 2)
-              + n_gqa * (streams * (context + 1) * Hkv * hd * 2 * 2
-                         + ((Hq * hd + 2 * Hkv * hd + Hq) * D + D * Hq * hd) * 2)
-              + sum(r + 2 for r in range(49)) * streams * D * 2)
-    pk = peaks()
-    gbs = nbytes / (ms / 1e3) / 1e9
-    return {
-        "workload": f"cfg5 decode step of the backbone: {streams} streams, 24 layers (18 DeltaNet 16 x 128/128, "
-                    f"6 GQA 16/4 x 128 over {context} cached keys + the new one), MoE 64 experts top-8 I=768 in "
-                    "every layer, Full AttnRes (49 routes); embedding and head / sampler excluded; CUDA graph",
-        "step_ms": ms, "tokens_per_s": streams / (ms / 1e3),
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / pk["hbm_gbs"], "algorithmic_bytes": nbytes, "peak_source": pk["source"]},
-    }
-
 
 def bench_sampler_cfg5(ops, dev, stream, streams=256, codebooks=10, vocab=4098, reps=5):
     """The TTS sampler for a cfg5 decode step: fp32 logits [256, 10, 4098] (N(0, 3)), temperature 0.8, top-k 50,
@@ -741,41 +822,76 @@ def bench_gdn_prefill_cfg3(ops, dev, stream, reps=5):
     }
 
 
+
+
+# --------------------------------------------------------------------------------------------- summaries
+
+
 def profiled_traffic(summary: str):
-    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in the
-    committed summary under profiles/, or None."""
+    """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in the committed
+    summary under profiles/ (the line ``traffic_bytes_per_launch: N`` or ``traffic_bytes_per_step: N``), or None."""
     path = ROOT / "profiles" / summary
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(("traffic_bytes_per_launch:", "traffic_bytes_per_step:")):
             return int(line.split(":", 1)[1])
     return None
 
 
-def cpu_reference(updates: int, streams=STREAMS):
-    """Time the CPU recurrence (oracle/gdn.py restating lm.py:576-582) on this host's cores.
-    Returns (tokens/s, threads, seconds)."""
-    from oracle import gdn as ogdn
+def operator_lines(pkg, dev) -> dict:
+    """Every other hot-path operator on its own config (N=1): cfg2 DeltaNet decode, cfg4 MoE layer, the cfg5 AttnRes
+    schedule, cfg3 chunked prefill, cfg5 GQA decode attention, the cfg5 sampler and one cfg5 DeltaNet + MoE layer."""
+    ops = pkg.ops
+    stream = torch.cuda.Stream(dev)
+    return {
+        "gdn_decode_cfg2": bench_gdn_decode_cfg2(ops, dev, stream),
+        "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
+        "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
+        "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
+        "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
+        "sampler_cfg5": bench_sampler_cfg5(ops, dev, stream),
+        "decode_layer_cfg5": bench_decode_layer_cfg5(pkg, dev, stream),
+    }
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    q, k, v, g, beta = cfg2_inputs(99, "cpu", streams)
-    state = cfg2_state(98, "cpu", streams)
-    ogdn.recurrent_step(state, q[0], k[0], v[0], g[0], beta[0], DK ** -0.5)
-    t0 = time.perf_counter()
-    for t in range(updates):
-        state, _ = ogdn.recurrent_step(state, q[t % UPDATES], k[t % UPDATES], v[t % UPDATES], g[t % UPDATES],
-                                       beta[t % UPDATES], DK ** -0.5)
-    dt = time.perf_counter() - t0
-    return streams * updates / dt, torch.get_num_threads(), dt
+
+def operator_summary(ops_: dict) -> dict:
+    """The figure each operator is judged on, in a few keys."""
+    out = {}
+    for name, r in ops_.items():
+        item = {}
+        for key in ("ms", "ms_per_layer", "ms_per_step", "layer_ms", "us"):
+            if key in r:
+                item[key] = round(r[key], 4)
+        roof = r.get("roofline")
+        if roof:
+            item["achieved"] = round(roof["achieved"], 1)
+            item["unit"] = roof["unit"]
+            item["frac"] = round(roof["frac"], 3)
+        if "tensor" in r:
+            item["tensor_frac"] = round(r["tensor"]["frac_of_bf16_peak"], 3)
+        if "largest_route" in r:
+            item["largest_route_frac"] = round(r["largest_route"]["frac"], 3)
+        out[name] = item
+    return out
 
 
-def profile_launches(n: int, workload: str = "gdn_decode") -> None:
-    """n eager launches of a workload's kernels (the bench's own launches, without graphs or timing): cfg2 decode
-    updates cycling the layer states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5
-    DeltaNet + MoE decode layers, cfg5 GQA decode attention, cfg5 backbone decode steps, or cfg5 sampler calls."""
-    ops = __import__("__graft_entry__").load_package().ops
+def profile_launches(n: int, workload: str = "decode_step", layers: int = LAYERS5) -> None:
+    """n runs of a workload's kernels (the bench's own launches, without timing): cfg5 decode steps (graph replays of
+    the headline step; ``layers`` shrinks the model for a small ncu case), cfg2 decode updates cycling the layer
+    states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5 DeltaNet + MoE decode layers, cfg5
+    GQA decode attention or cfg5 sampler calls (eager launches)."""
+    pkg = __import__("__graft_entry__").load_package()
+    ops = pkg.ops
     dev = torch.device("cuda", 0)
+    if workload == "decode_step":
+        model, graph = build_cfg5(pkg, dev, layers=layers)
+        for _ in range(n):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} cfg5 decode steps ({layers} layers, {graph.launches_per_step} library launches each) "
+              f"done, status {ops.device_status()}")
+        return
     if workload == "moe":
         x, norm_w, w_r, gate_up, down = moe_cfg4_inputs(dev)
         T, D = x.shape
@@ -823,14 +939,6 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg5 sampler calls done")
         return
-    if workload == "full_step":
-        step, core, batch = full_step_cfg5(__import__("__graft_entry__").load_package(), dev)
-        with core.forward_batch(batch):
-            for _ in range(n):
-                step()
-        torch.cuda.synchronize(dev)
-        print(f"profile: {n} cfg5 backbone decode steps done")
-        return
     if workload == "gqa_decode":
         q, kc, vc, table, seq = gqa_cfg5_inputs(dev)
         out = torch.empty_like(q)
@@ -868,24 +976,27 @@ def profile_launches(n: int, workload: str = "gdn_decode") -> None:
     print(f"profile: {n} gdn_decode_step launches done")
 
 
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--cpu-updates", type=int, default=256, help="updates in the CPU-baseline sample")
+    ap.add_argument("--e2e-steps", type=int, default=10, help="timed steps of the end-to-end loop")
+    ap.add_argument("--cpu-samples", type=int, default=3, help="stream-steps in the CPU-baseline sample")
     ap.add_argument("--profile-launches", type=int, default=0,
-                    help="only run this many eager launches of the dominant kernel (for an ncu capture) and exit")
-    ap.add_argument("--profile-workload", default="gdn_decode", choices=("gdn_decode", "moe", "attnres", "prefill",
-                                                                         "decode_layer", "gqa_decode",
-                                                                         "full_step", "sampler"),
+                    help="only run this many steps / launches of a workload (for an ncu capture) and exit")
+    ap.add_argument("--profile-workload", default="decode_step",
+                    choices=("decode_step", "gdn_decode", "moe", "attnres", "prefill", "decode_layer", "gqa_decode",
+                             "sampler"),
                     help="workload whose launches --profile-launches runs")
+    ap.add_argument("--profile-layers", type=int, default=LAYERS5, help="layers of the decode_step profile model")
     ap.add_argument("--operators", type=int, default=1,
-                    help="also time the other hot-path operators (MoE cfg4, AttnRes) at N=1")
+                    help="also time the other hot-path operators on their own configs at N=1")
     args = ap.parse_args()
     if args.profile_launches:
-        profile_launches(args.profile_launches, args.profile_workload)
+        profile_launches(args.profile_launches, args.profile_workload, args.profile_layers)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -894,15 +1005,16 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        per_step_updates = 16
-        value, threads, dt = cpu_reference(per_step_updates * (args.steps + args.warmup))
-        sample = (f"{per_step_updates} of the 512 updates per step (x{args.steps + args.warmup} steps incl. warm-up), "
-                  f"64 streams x 16 heads, {dt:.1f} s")
+        samples = args.steps + args.warmup
+        value, threads, dt, per_step = cpu_reference_cfg5(samples)
+        sample = (f"{samples} stream-steps of a 4-layer slice (3 DeltaNet + 1 GQA) and of the 0-layer remainder of "
+                  f"the cfg5 model at {CONTEXT5} cached keys, one stream per call, scaled to 24 layers "
+                  f"({per_step * 1e3:.0f} ms per stream-step; {dt:.1f} s incl. init)")
         line = {
             "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded cfg2 distributions)",
-            "config": {"workload": "cfg2 gated-DeltaNet recurrent decode: 64 streams x 16 heads, dk=dv=128"},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * STREAMS5 * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init weights N(0, 0.02); random cache)", "config": cfg5_config(world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
@@ -913,26 +1025,20 @@ def main():
     try:
         line = run_ours(args, dist, rank, world, local)
         if rank == 0:
-            cpu_value, threads, dt = cpu_reference(args.cpu_updates)
+            value, threads, dt, per_step = cpu_reference_cfg5(args.cpu_samples)
             line["cpu_baseline"] = {
-                "value": cpu_value, "unit": UNIT, "cores": threads, "kind": "port",
-                "sample": f"{args.cpu_updates} sequential updates of 64 streams x 16 heads ({dt:.1f} s), "
-                          "oracle/gdn.py restating lm.py:576-582",
+                "value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{args.cpu_samples} stream-steps of a 4-layer slice and of the 0-layer remainder of the "
+                          f"cfg5 model (oracle/lm.py restating lm.py:660-735, fp32), scaled to 24 layers; "
+                          f"{per_step * 1e3:.0f} ms per stream-step ({dt:.1f} s incl. init)",
             }
             if args.operators and world == 1:
-                ops = __import__("__graft_entry__").load_package().ops
-                dev = torch.device("cuda", local)
-                stream = torch.cuda.Stream(dev)
-                line["operators"] = {
-                    "moe_cfg4": bench_moe_cfg4(ops, dev, stream),
-                    "attnres_cfg5_decode": bench_attnres_decode(ops, dev, stream),
-                    "gdn_prefill_cfg3": bench_gdn_prefill_cfg3(ops, dev, stream),
-                    "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
-                    "sampler_cfg5": bench_sampler_cfg5(ops, dev, stream),
-                    "full_step_cfg5": bench_full_step_cfg5(__import__("__graft_entry__").load_package(), dev, stream),
-                    "decode_layer_cfg5": bench_decode_layer_cfg5(__import__("__graft_entry__").load_package(), dev,
-                                                                 stream),
-                }
+                pkg = __import__("__graft_entry__").load_package()
+                full = operator_lines(pkg, torch.device("cuda", local))
+                print("operators (full): " + json.dumps(full), file=sys.stderr, flush=True)
+                line["operators"] = operator_summary(full)
+                for name, item in line["operators"].items():
+                    print(f"operator {name}: {json.dumps(item)}", flush=True)
             print(json.dumps(line), flush=True)
     finally:
         if dist is not None:

@@ -24,9 +24,14 @@ const char* zb_last_error(void);
 void zb_clear_error(void);
 int zb_version(void);
 
+/* Kernel launches this library has issued in this process (every device; a launch during stream capture counts
+ * once, when it is captured, not on each replay). For launch accounting of captured steps. No reference
+ * counterpart. */
+uint64_t zb_launch_count(void);
+
 /* Reads the current device's status word (bits set by kernels whose bounded device-side waits expired:
  * 1 = AttnRes source load, 2 = grouped GEMM pipeline, 4 = chunked prefill pipeline, 8 = AttnRes exchange,
- * 16 = decode attention pipeline); clear != 0 resets it.
+ * 16 = decode attention pipeline; 32 = an embedding id outside its table); clear != 0 resets it.
  * Synchronous (a device-to-host copy); for diagnostics and tests, not for the hot path. No reference counterpart:
  * the reference's kernels have no device-side waits. */
 int zb_device_status(unsigned* flags, int clear);
@@ -210,13 +215,16 @@ int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_
  * at start-up and forbids allocation afterwards, or a C / Go / Java binding with no device allocator of its own).
  * The intermediate rows live in a static device array of 4,194,304 bf16 elements (8 MiB) that every GPU loading the
  * library holds until exit, so T*k*D must be at most 4,194,304 (status 3 otherwise, nothing queued). Calls share
- * the array: each clears the rows it uses first, and calls that overlap on the GPU race. The first call on a
- * device looks up the array's address with that device current; make it before any stream capture. Allocates
- * nothing. Arguments as zb_moe_gemm_down (h .. weights, without counts) and zb_moe_combine (T, k, out,
- * out_stride). */
+ * the array: each clears the rows it uses first, and calls that overlap on the GPU race. Pair ids in sorted_pairs
+ * at or beyond T*k are dropped (sorted_pairs should come from zb_moe_permute with the same T and k). The first call
+ * on a device looks up the array's address with that device current; make it before any stream capture. The
+ * address is kept per device ordinal for the life of the process (one context per device). Allocates nothing.
+ * Arguments as zb_moe_gemm_down (h .. weights; counts NULL loads every row of each tile, the permutation's counts
+ * load only the routed rows) and zb_moe_combine (T, k, out, out_stride). */
 int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                                const int32_t* offsets, const int32_t* sorted_pairs, const float* weights, int T, int k,
-                                uint16_t* out, int64_t out_stride, cudaStream_t stream);
+                                const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                                const float* weights, int T, int k, uint16_t* out, int64_t out_stride,
+                                cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------ GQA decode attention (KV cache) */
 
@@ -269,7 +277,8 @@ int zb_gqa_prologue_decode(const uint16_t* proj, int64_t proj_stride, const uint
  * stop_blocked[b, c] (NULL: never)), stop_bias[b] added to the stop id (NULL: none), repetition penalty
  * rep_penalties[b] over rep_ids[b, c, 0..W) (NULL / W = 0: none), then greedy argmax when `greedy` (every
  * temperature <= 0) or temperature[b], top_k (0 or >= V: off), softmax, top_p (in (0, 1)), min_p (> 0) and one
- * multinomial draw from Philox4x32-10 keyed by `seed` at counter (row, offset). top_k / top_p / min_p are the batch's
+ * multinomial draw from Philox4x32-10 keyed by `seed` at counter (row, offset + *offset_dev; offset_dev NULL: + 0; a
+ * device counter lets a captured decode step draw fresh numbers on each replay). top_k / top_p / min_p are the batch's
  * min / max / max, as the reference reduces them on the host. out [B, C + 1] int32: the codes, then text_vocab.
  * probs_out (NULL: not written) [B * C, V] fp32 receives each row's final distribution. V <= 16384.
  * Replaces sample_tts (model/src/zonos3/tts/sampler.py:159-372; ids drawn from a different random stream than
@@ -278,7 +287,24 @@ int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t ro
                   const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
                   int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes, const uint8_t* stop_blocked,
                   const float* stop_bias, const int32_t* rep_ids, int W, const float* rep_penalties, uint64_t seed,
-                  uint64_t offset, int text_vocab, int32_t* out, float* probs_out, cudaStream_t stream);
+                  uint64_t offset, const uint64_t* offset_dev, int text_vocab, int32_t* out, float* probs_out,
+                  cudaStream_t stream);
+
+/* -------------------------------------------------------------------------------------------- input embedding */
+
+/* Input rows of the layer stack: x[t] = RMSNorm(sum over columns c of tables[c][ids[t, c]]; norm_weight, eps)
+ * (normalize != 0; else the plain sum). The columns' rows are added one at a time in bf16, each add rounded to bf16,
+ * as MultiEmbedding.forward sums them; the norm computes in fp32 and rounds once (norm_weight NULL = weightless, the
+ * release's emb_norm). Replaces MultiEmbedding.forward + emb_norm in Zonos3ForCausalLM.embed
+ * (servers/sgl/src/zonos3_sgl/models/zonos3.py:225-255, :1066-1070, :1163-1222).
+ *   ids        [N, ncols] int32 (device), row stride ids_stride; ncols in 1..16 (codebooks + the text column)
+ *   tables     HOST array of ncols device pointers, table c [table_rows[c], D] bf16 contiguous, 16-byte aligned
+ *   table_rows HOST array of ncols row counts; an id outside [0, table_rows[c]) reads a zero row and sets status bit
+ *              32 (zb_device_status)
+ *   out        [N, D] bf16, row stride out_stride (a multiple of 8); D a multiple of 8, at most 4096. */
+int zb_embed_norm(const int32_t* ids, int64_t ids_stride, int ncols, const uint16_t* const* tables,
+                  const int32_t* table_rows, const uint16_t* norm_weight, float eps, int normalize, int N, int D,
+                  uint16_t* out, int64_t out_stride, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,149 @@
+"""The decode step the bench times, at reduced size, against the oracle LM (oracle/lm.py, pinned to the reference
+Zonos3LM by tests/golden/lm_tiny.npz).
+
+Model: the cfg5 architecture shrunk (hidden 512; 4 layers in the 3:1 DeltaNet:GQA pattern; DeltaNet 4 heads at
+128/128; GQA 8 q / 2 kv heads at 128; MoE 16 experts top-4, SwiGLU 256, in every layer; Full AttnRes; 10 codebooks
+of 4096 codes + EOA + pad, text vocabulary 1024; soft cap 15), random weights N(0, 0.02). 16 streams with ragged
+prompts (9..24 rows) are prefilled in one eager forward (``Zonos3ForCausalLM.forward``), then decoded through the
+captured ``DecodeGraph`` (embedding kernel, the 4 layers and 9 routes, head GEMM, soft cap + greedy sampler) with
+the oracle's greedy codes fed in each step (teacher forcing), for 8 steps.
+
+Bars: the soft-capped logits against the oracle's (bf16 activations vs fp32): cosine >= 0.999 for every stream
+after the prefill; in decode steps >= 95 % of (stream, step) pairs at cosine >= 0.9999 and none below 0.995 (the
+typical pair is at 0.99998; a token whose router logits sit one bf16 step from a top-k tie can take another expert,
+which dips that one stream-step to ~0.998 and is gone the step after). Greedy codes equal to the argmax of the
+graph's own logits over the sampler's allowed ids (exact); agreement with the oracle's greedy codes on >= 95 % of
+(stream, step, codebook) slots (bf16 rounding can swap near-tied logits).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import lm as olm
+
+pytestmark = pytest.mark.gpu
+
+STREAMS, STEPS, MAX_LEN = 16, 8, 64
+TEXT_VOCAB = 1024
+
+
+def _configs(zb):
+    oc = olm.LMConfig(dim=512, n_layers=4, gdn_period=4, gdn_heads=4, gdn_head_dim=128, n_heads=8, n_kv_heads=2,
+                      head_dim=128, n_experts=16, topk=4, moe_hidden=256, moe_routed_dim=512, n_codebooks=10,
+                      codebook_size=4096, text_rows=TEXT_VOCAB + 1)
+    mc = zb.config.ModelConfig(hidden_size=512, num_layers=4, gdn_num_heads=4, gdn_head_dim=128, moe_n_experts=16,
+                               moe_topk=4, moe_intermediate_size=256, moe_start_from_layer=0, norm_topk_prob=False,
+                               use_training_router_weights=True, attention_pattern="gdn3_global1", num_qo_heads=8,
+                               num_kv_heads=2, head_dim=128, n_codebooks=10, codebook_size=4096, text_vocab=TEXT_VOCAB,
+                               audio_pad_id=4097, loss_softcap=15.0)
+    return oc, mc
+
+
+def _allowed_argmax(logits):
+    """Greedy code over the ids the sampler allows: codes and the end-of-audio id (the stop id), not the pad id."""
+    return logits[..., :4097].float().argmax(-1)
+
+
+def test_decode_graph_matches_oracle_lm(zb):
+    dev = torch.device("cuda")
+    oc, mc = _configs(zb)
+    w = olm.random_weights(oc, seed=3)
+    model = zb.model.Zonos3ForCausalLM(mc)
+    model.load_state_dict(dict(w))
+    model.to(dev, torch.bfloat16)
+    pool = model.allocate_caches(STREAMS, STREAMS * MAX_LEN, dev)
+    table = (torch.arange(STREAMS)[:, None] * MAX_LEN + torch.arange(MAX_LEN)[None]).to(torch.int32).to(dev)
+    sampling = zb.model.SamplingConfig(temperature=0.0, repetition_window=0, repetition_penalty=1.0)
+    graph = zb.model.DecodeGraph(model, pool, STREAMS, table, sampling=sampling)
+    graph.capture()  # before the streams are loaded, as the engine captures at start-up
+    assert graph.launches_per_step > 20
+
+    gen = torch.Generator().manual_seed(5)
+    lengths = [9 + (7 * b) % 16 for b in range(STREAMS)]
+    prompts = [torch.cat([torch.randint(0, 4096, (n, 10), generator=gen), torch.randint(0, TEXT_VOCAB, (n, 1),
+                                                                                       generator=gen)], 1)
+               for n in lengths]
+
+    # oracle: one sequence per stream
+    caches = [olm.Cache() for _ in range(STREAMS)]
+    ref = torch.stack([olm.forward(oc, w, p, c)[-1] for p, c in zip(prompts, caches)])
+
+    # B200: one ragged prefill of every stream
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + n)
+    ids = torch.cat(prompts).to(torch.int32).to(dev)
+    meta = zb.core.AttnMetadata(
+        positions=torch.cat([torch.arange(n) for n in lengths]).to(torch.int32).to(dev),
+        out_loc=torch.cat([table[b, :n] for b, n in enumerate(lengths)]).contiguous(),
+        page_table=table, cache_seqlens=torch.tensor(lengths, dtype=torch.int32, device=dev), cu_seqlens_q=cu)
+    batch = zb.core.Batch(reqs=[zb.core.Req(b, n, 0, uid=b) for b, n in enumerate(lengths)], is_decode=False,
+                          input_ids=ids, attn_metadata=meta)
+    zb.core.get_global_ctx().attn_backend = pool
+    with zb.core.forward_batch(batch):
+        got = model.forward()[torch.tensor(cu[1:]) - 1].float().cpu()
+
+    cos = F.cosine_similarity(got.flatten(1), ref.flatten(1), dim=1)
+    assert cos.min() >= 0.999, f"prefill logits cosine {cos.min():.5f}"
+    agree, total, worst, close = 0, 0, 1.0, []
+    for step in range(STEPS):
+        codes_ref = _allowed_argmax(ref)  # the oracle's greedy codes, fed to both models
+        nxt = torch.cat([codes_ref, torch.full((STREAMS, 1), TEXT_VOCAB)], 1)
+        ref = torch.stack([olm.forward(oc, w, nxt[b:b + 1], caches[b])[-1] for b in range(STREAMS)])
+        pos = torch.tensor(lengths, dtype=torch.int32) + step
+        graph.load(nxt.to(torch.int32).to(dev), pos.to(dev), (pos + 1).to(dev),
+                   table[torch.arange(STREAMS, device=dev), pos.long().to(dev)].contiguous())
+        codes = graph.replay()
+        torch.cuda.synchronize()
+        raw = graph.logits.view(STREAMS, 10, 4098)
+        got = 15.0 * torch.tanh(raw / 15.0)  # the soft cap at torch's bf16 rounding points, as the sampler applies it
+        assert torch.equal(codes[:, :10].cpu(), _allowed_argmax(got).cpu().to(torch.int32)), f"greedy codes, step {step}"
+        assert torch.equal(codes[:, 10].cpu(), torch.full((STREAMS,), TEXT_VOCAB, dtype=torch.int32))
+        cos = F.cosine_similarity(got.float().cpu().flatten(1), ref.flatten(1), dim=1)
+        worst = min(worst, cos.min().item())
+        close.append(cos >= 0.9999)
+        assert cos.min() >= 0.995, f"step {step}: logits cosine {cos.min():.5f}"
+        agree += (codes[:, :10].cpu().long() == _allowed_argmax(ref)).sum().item()
+        total += STREAMS * 10
+    frac = torch.cat(close).float().mean().item()
+    msg = f"greedy agreement {agree / total:.4f}, min cosine {worst:.5f}, {frac:.3f} of stream-steps >= 0.9999"
+    print(msg)
+    assert frac >= 0.95, msg
+    assert agree / total >= 0.95, msg
+    assert zb.ops.device_status() == 0
+
+
+def test_embed_norm_matches_torch(zb):
+    """The embedding kernel against MultiEmbedding.forward + emb_norm in torch on the GPU (sequential bf16 adds,
+    F.rms_norm): within one bf16 rounding, >= 99 % of elements identical; out-of-range ids read zeros and raise
+    the status bit."""
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(1)
+    D, N = 2048, 300
+    tables = [torch.randn(4098, D, generator=gen).bfloat16().to(dev) for _ in range(10)]
+    tables.append(torch.randn(1025, D, generator=gen).bfloat16().to(dev))
+    ids = torch.cat([torch.randint(0, 4098, (N, 10), generator=gen), torch.randint(0, 1025, (N, 1), generator=gen)], 1)
+    ids = ids.to(torch.int32).to(dev)
+    got = zb.ops.embed_norm(ids, tables, eps=1e-5)
+    x = F.embedding(ids[:, 0].long(), tables[0])
+    for c in range(1, 11):
+        x = x + F.embedding(ids[:, c].long(), tables[c])
+    plain = zb.ops.embed_norm(ids, tables, normalize=False)
+    assert torch.equal(plain, x), "the bf16 sum follows the reference's add order and roundings"
+    ref = F.rms_norm(x.float(), (D,), eps=1e-5).bfloat16()
+    assert (got.float() - ref.float()).abs().max().item() <= 2 ** -7 * ref.float().abs().max().item()
+    assert (got == ref).float().mean().item() >= 0.99
+    # an id outside its table
+    bad = ids[:2].clone()
+    bad[1, 3] = 5000
+    zb.ops.device_status()
+    out = zb.ops.embed_norm(bad, tables, normalize=False)
+    sum_row = F.embedding(bad[1, 0:1].long(), tables[0])
+    for c in range(1, 11):
+        if c != 3:
+            sum_row = sum_row + F.embedding(bad[1, c:c + 1].long(), tables[c])
+    assert torch.equal(out[1:2], sum_row)
+    assert zb.ops.device_status() & 32

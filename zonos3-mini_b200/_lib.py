@@ -24,6 +24,7 @@ SIGNATURES: dict[str, list] = {
     "zb_last_error": [],
     "zb_clear_error": [],
     "zb_version": [],
+    "zb_launch_count": [],
     "zb_device_status": [_p, _i32],
     # q, k, v, q_stride_b, k_stride_b, v_stride_b, g, beta, gb_stride_b, state, slots, num_slots,
     # out, out_stride_b, B, H, dk, dv, scale, stream
@@ -64,24 +65,27 @@ SIGNATURES: dict[str, list] = {
     "zb_moe_gemm_down": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p],
     # y, T, k, D, out, out_stride, stream
     "zb_moe_combine": [_p, _i32, _i32, _i32, _p, _i64, _p],
-    # h, capacity, down, E, D, I, offsets, sorted_pairs, weights, T, k, out, out_stride, stream
-    "zb_moe_down_combine_noalloc": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _i32, _i32, _p, _i64, _p],
+    # h, capacity, down, E, D, I, offsets, counts, sorted_pairs, weights, T, k, out, out_stride, stream
+    "zb_moe_down_combine_noalloc": [_p, _i64, _p, _i32, _i32, _i32, _p, _p, _p, _p, _i32, _i32, _p, _i64, _p],
     # k_cache, v_cache, slot_stride, num_slots, slots, k, k_stride, v, v_stride, N, Hkv, hd, stream
     "zb_kv_store": [_p, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i32, _i32, _i32, _p],
     # q, q_stride, k_cache, v_cache, slot_stride, num_slots, page_table, table_stride, seq_lens, max_seq_len, B, Hq,
     # Hkv, hd, scale, splits, split_len, workspace, workspace_bytes, out, out_stride, stream
     # logits, logits_fp32, softcap, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size, audio_pad_id,
-    # stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed, offset, text_vocab, out,
-    # probs_out, stream
+    # stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed, offset, offset_dev,
+    # text_vocab, out, probs_out, stream
     "zb_sample_tts": [_p, _i32, _f32, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
-                      _i32, _p, _u64, _u64, _i32, _p, _p, _p],
+                      _i32, _p, _u64, _u64, _p, _i32, _p, _p, _p],
+    # ids, ids_stride, ncols, tables (host array), table_rows (host array), norm_weight, eps, normalize, N, D, out,
+    # out_stride, stream
+    "zb_embed_norm": [_p, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _i32, _p, _i64, _p],
     # proj, proj_stride, temp, positions, theta, eps, q_out, k_cache, v_cache, slot_stride, num_slots, out_loc, N,
     # Hq, Hkv, hd, stream
     "zb_gqa_prologue_decode": [_p, _i64, _p, _p, _f32, _f32, _p, _p, _p, _i64, _i64, _p, _i32, _i32, _i32, _i32, _p],
     "zb_gqa_decode": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _p,
                       _i64, _p, _i64, _p],
 }
-_RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None,
+_RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None, "zb_launch_count": ctypes.c_uint64,
              "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64}
 
 _lock = threading.Lock()
@@ -110,6 +114,11 @@ def load() -> ctypes.CDLL:
                 fn.restype = _RESTYPES.get(name, ctypes.c_int)
             _lib = lib
     return _lib
+
+
+def launch_count() -> int:
+    """Kernel launches the library has issued in this process (captured launches count once)."""
+    return int(load().zb_launch_count())
 
 
 def last_error() -> str:

@@ -13,6 +13,8 @@ __device__ unsigned g_zb_device_status;
 
 namespace zb {
 
+std::atomic<uint64_t> g_launch_count{0};
+
 int fail(int code, const char* fmt, ...) {
   va_list args;
   va_start(args, fmt);
@@ -67,4 +69,6 @@ ZB_API const char* zb_last_error(void) { return g_last_error; }
 
 ZB_API void zb_clear_error(void) { g_last_error[0] = '\0'; }
 
-ZB_API int zb_version(void) { return 1; }
+ZB_API int zb_version(void) { return 2; }
+
+ZB_API uint64_t zb_launch_count(void) { return zb::g_launch_count.load(std::memory_order_relaxed); }

@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <utility>
 #include <stdint.h>
 
@@ -45,6 +46,7 @@ enum DeviceStatusBits : unsigned {
   kStatusPrefillTimeout = 1u << 2,
   kStatusAttnresExchangeTimeout = 1u << 3,
   kStatusAttnDecodeTimeout = 1u << 4,
+  kStatusEmbedIndex = 1u << 5,  // an embedding id outside its table (read as a zero row)
 };
 
 }  // namespace zb
@@ -234,8 +236,11 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Kernel launches the library has issued from this process (all devices, eager and captured alike).
+extern std::atomic<uint64_t> g_launch_count;
+
 // Launches `kernel` on `stream` with programmatic stream serialisation allowed (see pdl_enter) and, when
-// cluster_x > 1, clusters of cluster_x CTAs along x.
+// cluster_x > 1, clusters of cluster_x CTAs along x; counts the launch in g_launch_count.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                           unsigned cluster_x, Args&&... args) {
@@ -258,7 +263,9 @@ inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err == cudaSuccess) g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  return err;
 }
 
 }  // namespace zb

@@ -75,6 +75,7 @@ struct GemmParams {
   int out_cols;            // valid output columns (GEMM2: D, a multiple of 128; the last tile may be half)
   const int32_t* sorted_pairs;  // GEMM2
   const float* weights;         // GEMM2: [pairs]
+  int64_t pair_limit;           // GEMM2: pairs >= this are dropped (the rows of `out`)
   unsigned* status;
 };
 
@@ -394,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float w = 0.f;
       if (MODE == kDown) {
         pr = valid ? p.sorted_pairs[row] : -1;
+        if (pr >= p.pair_limit) pr = -1;  // never write past the rows of `out`
         w = pr >= 0 ? p.weights[pr] : 0.f;
       }
       bool ok = !*abort_flag &&
@@ -583,14 +585,17 @@ ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const ui
   if (int rc = make_map(&ma32, x_perm, capacity, D, D, 32)) return rc;
   if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
   GemmParams p{offsets, counts, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I,
-               nullptr, nullptr, zb::device_status_ptr()};
+               nullptr, nullptr, 0, zb::device_status_ptr()};
   return use_pair(capacity, E) ? launch<kSwiGLU, true>(ma, ma32, mb, p, capacity, stream)
                                 : launch<kSwiGLU, false>(ma, ma32, mb, p, capacity, stream);
 }
 
-ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                            const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
-                            const float* weights, uint16_t* y, cudaStream_t stream) {
+namespace zb {
+
+// The down projection with its pair rows bounded: a pair id >= pair_limit (a row `y` does not have) is dropped.
+int moe_gemm_down_bounded(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                          const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                          const float* weights, uint16_t* y, int64_t pair_limit, cudaStream_t stream) {
   if (int rc = check_common(h, offsets, E, capacity)) return rc;
   ZB_REQUIRE(down && sorted_pairs && weights && y, "moe_gemm_down: null pointer");
   if (I % BK != 0 || D % 128 != 0)
@@ -602,7 +607,17 @@ ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t*
   if (int rc = make_map(&ma32, h, capacity, I, I, 32)) return rc;
   if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
   GemmParams p{offsets, counts, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D,
-               D, sorted_pairs, weights, zb::device_status_ptr()};
+               D, sorted_pairs, weights, pair_limit, zb::device_status_ptr()};
   return use_pair(capacity, E) ? launch<kDown, true>(ma, ma32, mb, p, capacity, stream)
                                 : launch<kDown, false>(ma, ma32, mb, p, capacity, stream);
+}
+
+}  // namespace zb
+
+ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                            const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                            const float* weights, uint16_t* y, cudaStream_t stream) {
+  // a permutation of capacity rows holds pair ids below capacity (zb_moe_permute never writes more)
+  return zb::moe_gemm_down_bounded(h, capacity, down, E, D, I, offsets, counts, sorted_pairs, weights, y, capacity,
+                                   stream);
 }

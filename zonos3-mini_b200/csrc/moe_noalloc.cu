@@ -13,14 +13,22 @@
 // 256 decode streams x top-8 x hidden 2048); larger calls are rejected before any work is queued. Every GPU that
 // loads the library reserves the array until the process exits. All calls share it and it keeps the previous
 // call's contents, so each call clears the rows it uses first (a pair whose expert id is invalid then adds zero),
-// and two calls that overlap on the GPU (different streams running at the same time) race on it. The first call
-// on a device resolves the array's device address (cudaGetSymbolAddress) with that device current; make that first
-// call before any stream capture. No cudaMalloc, cudaFree or allocating library routine is called.
+// and two calls that overlap on the GPU (different streams running at the same time) race on it. The down projection
+// drops any pair id at or beyond T * k, so a permutation built for other sizes cannot write past the cleared rows
+// (or past the array). The first call on a device resolves the array's device address (cudaGetSymbolAddress) with
+// that device current; make that first call before any stream capture. The resolved address is kept per device
+// ordinal for the life of the process (one context per device, the CUDA runtime's primary context). No cudaMalloc,
+// cudaFree or allocating library routine is called.
+#include <atomic>
+
 #include "common.cuh"
 
-ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                            const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
-                            const float* weights, uint16_t* y, cudaStream_t stream);
+namespace zb {
+int moe_gemm_down_bounded(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
+                          const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                          const float* weights, uint16_t* y, int64_t pair_limit, cudaStream_t stream);
+}  // namespace zb
+
 ZB_API int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_t out_stride,
                           cudaStream_t stream);
 
@@ -34,30 +42,34 @@ static __device__ __align__(256) uint16_t g_moe_noalloc_scratch[kNoAllocScratchE
 
 constexpr int kMaxDevices = 64;
 
-// Device address of the scratch array on the current device, resolved once per device.
+// Device address of the scratch array on the current device, resolved once per device (first calls from several
+// host threads may each resolve it; they store the same address).
 int scratch_address(uint16_t** out) {
-  static uint16_t* cached[kMaxDevices] = {nullptr};
+  static std::atomic<uint16_t*> cached[kMaxDevices];
   int dev = 0;
   ZB_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices)
     return zb::fail(zb::kUnsupported, "moe_down_combine_noalloc: device ordinal %d (max %d)", dev, kMaxDevices - 1);
-  if (cached[dev] == nullptr) {
+  uint16_t* addr = cached[dev].load(std::memory_order_acquire);
+  if (addr == nullptr) {
     void* p = nullptr;
     cudaError_t err = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
     if (err != cudaSuccess || p == nullptr)
       return zb::fail(zb::kCudaError, "moe_down_combine_noalloc: cudaGetSymbolAddress failed: %s",
                       cudaGetErrorString(err));
-    cached[dev] = static_cast<uint16_t*>(p);
+    addr = static_cast<uint16_t*>(p);
+    cached[dev].store(addr, std::memory_order_release);
   }
-  *out = cached[dev];
+  *out = addr;
   return zb::kOk;
 }
 
 }  // namespace
 
 ZB_API int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, const uint16_t* down, int E, int D, int I,
-                                       const int32_t* offsets, const int32_t* sorted_pairs, const float* weights,
-                                       int T, int k, uint16_t* out, int64_t out_stride, cudaStream_t stream) {
+                                       const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                                       const float* weights, int T, int k, uint16_t* out, int64_t out_stride,
+                                       cudaStream_t stream) {
   ZB_REQUIRE(T >= 0 && k > 0 && D > 0, "moe_down_combine_noalloc: bad sizes T=%d k=%d D=%d", T, k, D);
   const int64_t elems = (int64_t)T * k * D;
   if (elems > kNoAllocScratchElems)
@@ -69,8 +81,8 @@ ZB_API int zb_moe_down_combine_noalloc(const uint16_t* h, int64_t capacity, cons
   uint16_t* scratch = nullptr;
   if (int rc = scratch_address(&scratch)) return rc;
   ZB_CUDA(cudaMemsetAsync(scratch, 0, (size_t)elems * sizeof(uint16_t), stream));
-  if (int rc = zb_moe_gemm_down(h, capacity, down, E, D, I, offsets, nullptr, sorted_pairs, weights, scratch,
-                                stream))
+  if (int rc = zb::moe_gemm_down_bounded(h, capacity, down, E, D, I, offsets, counts, sorted_pairs, weights, scratch,
+                                         (int64_t)T * k, stream))
     return rc;
   return zb_moe_combine(scratch, T, k, D, out, out_stride, stream);
 }

@@ -14,7 +14,8 @@
 //      renormalisation after each filter
 //      (clamped at 1e-8), a row without mass falls back to its argmax, and one multinomial draw (:288-349).
 // top_k / top_p / min_p are the batch's (min, max, max) as the reference reduces them on the host.
-// The draw uses Philox4x32-10 (Salmon et al., SC'11) keyed by `seed`, counter (row, offset): a different random
+// The draw uses Philox4x32-10 (Salmon et al., SC'11) keyed by `seed`, counter (row, offset + *offset_dev when a
+// device counter is given, so a captured decode step draws fresh numbers on every replay): a different random
 // stream from torch.multinomial's, so sampled ids match the reference in distribution, not draw for draw.
 //
 // One CTA of 256 threads per row; the row's logits live in shared memory (V <= kMaxVocab). With a top-k of at most
@@ -48,6 +49,7 @@ struct SamplerParams {
   int W;
   const float* rep_penalties;  // [B] or null
   uint64_t seed, offset;
+  const uint64_t* offset_dev;  // [1] or null: added to `offset` (a step counter a captured graph advances)
   int text_vocab;
   int32_t* out;      // [B, C + 1]
   float* probs_out;  // [B * C, V] or null: the final distribution (one-hot on greedy rows)
@@ -315,7 +317,8 @@ __device__ bool sample_sorted_topk(const SamplerParams& p, float* x, int row, in
     }
   }
   // the draw over the sorted list
-  const float u = (float)(philox(p.seed, (uint64_t)row, p.offset) >> 8) * (1.0f / 16777216.0f);
+  const uint64_t counter = p.offset + (p.offset_dev ? *p.offset_dev : 0ull);
+  const float u = (float)(philox(p.seed, (uint64_t)row, counter) >> 8) * (1.0f / 16777216.0f);
   const float target = u * mass;
   const float loc = e[0] + e[1] + e[2] + e[3];
   float run = block_scan_incl_f(loc, reinterpret_cast<float*>(wsum)) - loc;
@@ -516,7 +519,8 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
     for (int i = tid; i < V; i += kThreads) probs[i] = x[i];
   }
   // one draw: the first id whose inclusive prefix sum exceeds u * mass (contiguous chunks per thread)
-  const float u = (float)(philox(p.seed, (uint64_t)row, p.offset) >> 8) * (1.0f / 16777216.0f);
+  const uint64_t counter = p.offset + (p.offset_dev ? *p.offset_dev : 0ull);
+  const float u = (float)(philox(p.seed, (uint64_t)row, counter) >> 8) * (1.0f / 16777216.0f);
   const float target = u * mass;
   const int chunk = (V + kThreads - 1) / kThreads;
   const int begin = min(tid * chunk, V), end = min(begin + chunk, V);
@@ -560,8 +564,8 @@ ZB_API int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int
                          const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
                          int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes,
                          const uint8_t* stop_blocked, const float* stop_bias, const int32_t* rep_ids, int W,
-                         const float* rep_penalties, uint64_t seed, uint64_t offset, int text_vocab, int32_t* out,
-                         float* probs_out, cudaStream_t stream) {
+                         const float* rep_penalties, uint64_t seed, uint64_t offset, const uint64_t* offset_dev,
+                         int text_vocab, int32_t* out, float* probs_out, cudaStream_t stream) {
   ZB_REQUIRE(B >= 0 && C > 0 && V > 0 && V <= kMaxVocab, "sample_tts: sizes B=%d C=%d V=%d (V <= %d)", B, C, V,
              kMaxVocab);
   if (B == 0) return zb::kOk;
@@ -573,7 +577,7 @@ ZB_API int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int
   ZB_REQUIRE(softcap >= 0.f, "sample_tts: softcap %g", (double)softcap);
   SamplerParams p{logits, logits_fp32, softcap, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size,
                   audio_pad_id, stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed,
-                  offset, text_vocab, out, probs_out};
+                  offset, offset_dev, text_vocab, out, probs_out};
   const size_t smem = (size_t)V * sizeof(float);
   if (smem > 48 * 1024) {
     ZB_CUDA(cudaFuncSetAttribute(sample_tts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

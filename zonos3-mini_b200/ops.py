@@ -7,6 +7,8 @@ caller-provided tensors when given, so a wrapper allocates nothing inside a CUDA
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -723,13 +725,14 @@ def _host_list(t) -> list:
 def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, audio_pad_id, stop_token_ids,
                repetition_token_ids=None, repetition_penalties=None, codebook_sizes=None, text_vocab=0, seed=0,
                offset=0, stop_blocked=None, stop_bias=None, probs_out=None, out=None, device_temperatures=None,
-               softcap=0.0):
+               softcap=0.0, offset_dev=None):
     """Next codes from logits [B, C, V] (bf16 or fp32, CUDA): sample_tts (model/src/zonos3/tts/sampler.py:159-372)
     as one kernel per (request, codebook) row, with the reference's masks, stop bias, repetition penalty, greedy
     path and top-k / top-p / min-p filters. temperatures, top_ks, top_ps, min_ps, stop_token_ids: [B] tensors or
     lists; their values pick host-side branches as in the reference (greedy when every temperature <= 0, the batch's
     min top-k, max top-p and max min-p), so pass CPU tensors to keep the host from waiting on the GPU. The draw uses
-    Philox4x32-10 keyed by ``seed`` at counter (row, ``offset``): advance ``offset`` every step. Returns
+    Philox4x32-10 keyed by ``seed`` at counter (row, ``offset`` + ``offset_dev[0]``): advance ``offset`` every step,
+    or, inside a captured graph, the one-element int64 device counter ``offset_dev``. Returns
     [B, C + 1] int32 (codes, then ``text_vocab``); ``probs_out`` ([B * C, V] fp32) receives the final
     distributions. Per-row inputs already on the device (int32 stop ids, fp32 ``device_temperatures``, ...) are
     used as they are, so a call can be captured in a CUDA graph. ``softcap`` > 0 applies the head's soft cap
@@ -762,13 +765,49 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
         pen_d = dev_t(repetition_penalties, f32)
     if out is None:
         out = torch.empty(B, C + 1, **i32)
+    if offset_dev is not None:
+        _check_cuda("offset_dev", offset_dev, torch.int64, dev)
+        _require(offset_dev.numel() >= 1, "offset_dev must hold one counter")
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
     _lib.call("zb_sample_tts", logits.data_ptr(), int(logits.dtype == torch.float32), float(softcap), logits.stride(1),
               B, C, V,
               temp_d.data_ptr(), int(greedy), top_k, top_p, min_p, int(codebook_size), int(audio_pad_id),
               stop_d.data_ptr(), ptr(sizes_d), ptr(blocked_d), ptr(bias_d), ptr(rep_d), W, ptr(pen_d),
-              int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), int(text_vocab), out.data_ptr(), ptr(probs_out),
-              _stream(dev))
+              int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), ptr(offset_dev), int(text_vocab), out.data_ptr(),
+              ptr(probs_out), _stream(dev))
+    return out
+
+
+# ------------------------------------------------------------------------------------------- input embedding
+
+
+def embed_norm(ids, tables, *, eps=1e-5, norm_weight=None, normalize=True, out=None):
+    """Layer-stack input rows: RMSNorm(sum_c tables[c][ids[:, c]]) (MultiEmbedding.forward + emb_norm,
+    servers/sgl/src/zonos3_sgl/models/zonos3.py:225-255, :1218), one kernel. ids [N, C] int32 on the device (row
+    stride allowed); tables: C bf16 [rows_c, D] tensors; the columns are summed one add at a time in bf16 as the
+    reference does. An id outside its table reads zeros and sets bit 32 of ``device_status()``."""
+    _require(isinstance(ids, torch.Tensor) and ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 2,
+             "ids must be a [N, C] int32 CUDA tensor")
+    dev = ids.device
+    N, C = ids.shape
+    _require(ids.stride(1) == 1 or C == 1, "ids columns must be contiguous")
+    _require(len(tables) == C, f"{C} id columns need {C} tables, got {len(tables)}")
+    D = tables[0].shape[1]
+    for i, t in enumerate(tables):
+        _check_cuda(f"tables[{i}]", t, torch.bfloat16, dev)
+        _require(t.dim() == 2 and t.shape[1] == D and t.is_contiguous(), f"tables[{i}] must be a contiguous [rows, {D}]")
+    if norm_weight is not None:
+        _check_cuda("norm_weight", norm_weight, torch.bfloat16, dev)
+        _require(norm_weight.shape == (D,) and norm_weight.is_contiguous(), f"norm_weight must be [{D}]")
+    if out is None:
+        out = torch.empty(N, D, device=dev, dtype=torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    _require(out.shape == (N, D) and out.stride(1) == 1, f"out must be [{N}, {D}] with contiguous rows")
+    ptrs = (ctypes.c_void_p * C)(*[t.data_ptr() for t in tables])
+    rows = (ctypes.c_int32 * C)(*[t.shape[0] for t in tables])
+    _lib.call("zb_embed_norm", ids.data_ptr(), ids.stride(0) if N > 1 else C, C, ctypes.cast(ptrs, ctypes.c_void_p),
+              ctypes.cast(rows, ctypes.c_void_p), None if norm_weight is None else norm_weight.data_ptr(), float(eps),
+              int(bool(normalize)), N, D, out.data_ptr(), out.stride(0) if N > 1 else D, _stream(dev))
     return out
 
 
