@@ -585,10 +585,32 @@ def bench_moe_cfg4(ops, dev, stream, steps=10, warmup=3):
         "roofline": {"kernel": "moe_gemm_kernel (SwiGLU + Down)", "bound": "tensor", "achieved": tflops,
                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"],
                      "flops_per_layer": f1 + f2, "peak_source": pk["source"] + " burst"},
+        "cpu_baseline": dict(zip(("ms_per_layer", "cores", "sample"), cpu_moe_cfg4()), kind="port",
+                             path="oracle/moe.py router + experts_loop_fp32 (lm.py:610-637)"),
         "gemm_swiglu_tflops": f1 / (per["gemm_swiglu"] / 1e3) / 1e12,
         "gemm_down_tflops": f2 / (per["gemm_down"] / 1e3) / 1e12,
         "device_status": status,
     }
+
+
+def cpu_moe_cfg4(tokens: int = 64):
+    """The reference's CPU MoE layer (lm.py:610-637: router GEMM and top-k, then the per-(token, rank) expert loop,
+    restated in oracle/moe.py) on `tokens` of cfg4's 4096 tokens, fp32 on this host's cores; the layer time is
+    scaled by 4096 / tokens (tokens are independent). Returns (ms per 4096-token layer, threads, sample)."""
+    from oracle import moe as omoe
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, norm_w, w_r, gate_up, down = [t.float() for t in moe_cfg4_inputs("cpu")]
+    x = x[:tokens]
+    with torch.no_grad():
+        omoe.experts_loop_fp32(x[:1], gate_up, down, torch.zeros(1, 8, dtype=torch.int64), torch.ones(1, 8))
+        t0 = time.perf_counter()
+        logits = omoe.router_logits(x, norm_w, w_r, 1e-5)
+        ids, w = omoe.route(logits, torch.zeros(w_r.shape[0]), 8, weights="full_softmax", renormalize=True)
+        omoe.experts_loop_fp32(x, gate_up, down, ids, w)
+        dt = time.perf_counter() - t0
+    ms = dt * 1e3 * 4096 / tokens
+    return ms, torch.get_num_threads(), f"{tokens} of the 4096 tokens ({dt:.2f} s), scaled by {4096 // tokens}"
 
 
 def bench_attnres_decode(ops, dev, stream, tokens=256, dim=2048, layers=24, reps=3):
@@ -872,6 +894,8 @@ def operator_summary(ops_: dict) -> dict:
             item["tensor_frac"] = round(r["tensor"]["frac_of_bf16_peak"], 3)
         if "largest_route" in r:
             item["largest_route_frac"] = round(r["largest_route"]["frac"], 3)
+        if "cpu_baseline" in r:
+            item["cpu_ms"] = round(r["cpu_baseline"]["ms_per_layer"], 1)
         out[name] = item
     return out
 

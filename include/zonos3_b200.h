@@ -244,7 +244,9 @@ int zb_kv_store(uint16_t* k_cache, uint16_t* v_cache, int64_t slot_stride, int64
  *   q [B, Hq, hd] bf16 (request stride q_stride); k_cache / v_cache slot s, head g at s * slot_stride + g * hd,
  *   s in [0, num_slots) (a table entry outside that range masks its key position, nothing is read for it);
  *   page_table [B, table_stride] int32 whose first max_seq_len columns are read; seq_lens [B] int32, clamped to
- *   max_seq_len (0, or every key masked: zero output); out [B, Hq, hd] bf16 (out_stride).
+ *   max_seq_len (0, or every key masked: zero output); out [B, Hq, hd] bf16 (out_stride). gate (NULL: none)
+ *   [B, Hq] bf16 gate logits, request stride gate_stride: out = bf16(bf16(o) * bf16(sigmoid(gate))), the layer's
+ *   output gate (servers/sgl/src/zonos3_sgl/models/zonos3.py:326, :383-385) at torch's rounding points.
  *   The key range of a request is cut into `splits` pieces of split_len positions (a multiple of 32; splits *
  *   split_len must cover the longest seq_len, keys past it are not read); with splits > 1 the partials go to a
  *   workspace of B * Hq * splits * (hd + 2) floats (4-byte each) and a second kernel merges them. The reference
@@ -254,7 +256,7 @@ int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_cache, 
                   int64_t slot_stride, int64_t num_slots, const int32_t* page_table, int64_t table_stride,
                   const int32_t* seq_lens, int max_seq_len, int B, int Hq, int Hkv, int hd, float softmax_scale,
                   int splits, int split_len, float* workspace, int64_t workspace_bytes, uint16_t* out,
-                  int64_t out_stride, cudaStream_t stream);
+                  int64_t out_stride, const uint16_t* gate, int64_t gate_stride, cudaStream_t stream);
 
 /* The attention layer's decode prologue: from the fused projection rows proj [N, Hq*hd | Hkv*hd | Hkv*hd | ...]
  * (q | k | v, row stride proj_stride), q = bf16(RMSNorm(q, eps)) * bf16(|temp|) (rounded), k = bf16(RMSNorm(k, eps)),
@@ -269,7 +271,8 @@ int zb_gqa_prologue_decode(const uint16_t* proj, int64_t proj_stride, const uint
 
 /* ---------------------------------------------------------------------------------------------- TTS sampler */
 
-/* Next audio codes from per-codebook logits [B, C, V] (rows of V, row stride row_stride elements; bf16 when
+/* Next audio codes from per-codebook logits [B, C, V] (row (b, c) of V at b * batch_stride + c * row_stride elements,
+ * so a padded [B, >= C * V] head output can be read in place; bf16 when
  * logits_fp32 == 0, else fp32), one row per (request, codebook): softcap > 0 first applies the head's soft cap
  * softcap * tanh(x / softcap) (MultiOutputHead + softcap, servers/sgl/src/zonos3_sgl/models/zonos3.py:1341-1360,
  * rounded to bf16 after each op for bf16 logits, as torch evaluates it), then invalid ids masked (audio_pad_id; ids >=
@@ -283,7 +286,8 @@ int zb_gqa_prologue_decode(const uint16_t* proj, int64_t proj_stride, const uint
  * probs_out (NULL: not written) [B * C, V] fp32 receives each row's final distribution. V <= 16384.
  * Replaces sample_tts (model/src/zonos3/tts/sampler.py:159-372; ids drawn from a different random stream than
  * torch.multinomial, equal in distribution). */
-int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t row_stride, int B, int C, int V,
+int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t row_stride, int64_t batch_stride, int B,
+                  int C, int V,
                   const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
                   int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes, const uint8_t* stop_blocked,
                   const float* stop_bias, const int32_t* rep_ids, int W, const float* rep_penalties, uint64_t seed,

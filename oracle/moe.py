@@ -95,6 +95,21 @@ def experts_fp32(x, gate_up, down, ids, weights):
     return out
 
 
+def experts_loop_fp32(x, gate_up, down, ids, weights):
+    """The reference's expert loop as written (lm.py:622-637): for every token and every rank, gate_up = W13[e] x,
+    h = SiLU(first half) * second half, y = W2[e] h, out[token] += (y * w).to(x.dtype). One matrix-vector product
+    pair per (token, rank): the CPU path the reference runs, timed as the cfg4 CPU baseline."""
+    half = gate_up.shape[1] // 2
+    out = torch.zeros(x.shape[0], down.shape[1], dtype=x.dtype)
+    for token in range(x.shape[0]):
+        for rank in range(ids.shape[1]):
+            e = int(ids[token, rank])
+            gu = F.linear(x[token], gate_up[e])
+            h = F.silu(gu[:half]) * gu[half:]
+            out[token] += (F.linear(h, down[e]).float() * weights[token, rank]).to(x.dtype)
+    return out
+
+
 def experts_bf16(x, gate_up, down, ids, weights):
     """The server's bf16 rounding points (fused_moe_impl.py:218-289): GEMM1 output rounded to bf16, SiLU(gate)*up
     rounded (silu_and_mul), GEMM2 output times the routing weight rounded per (token, slot), then the k slots

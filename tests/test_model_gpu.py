@@ -98,7 +98,7 @@ def test_decode_graph_matches_oracle_lm(zb):
                    table[torch.arange(STREAMS, device=dev), pos.long().to(dev)].contiguous())
         codes = graph.replay()
         torch.cuda.synchronize()
-        raw = graph.logits.view(STREAMS, 10, 4098)
+        raw = graph.logits.unflatten(1, (10, 4098))
         got = 15.0 * torch.tanh(raw / 15.0)  # the soft cap at torch's bf16 rounding points, as the sampler applies it
         assert torch.equal(codes[:, :10].cpu(), _allowed_argmax(got).cpu().to(torch.int32)), f"greedy codes, step {step}"
         assert torch.equal(codes[:, 10].cpu(), torch.full((STREAMS,), TEXT_VOCAB, dtype=torch.int32))

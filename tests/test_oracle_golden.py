@@ -81,6 +81,9 @@ def test_moe_layer_matches_reference(golden):
     out = omoe.experts_fp32(latent_x, w["experts.gate_up_proj"], w["experts.down_proj"], ids, weights)
     y = torch.nn.functional.linear(out, w["latent_up.weight"])
     torch.testing.assert_close(y, g["y"], rtol=1e-5, atol=1e-6)
+    # the per-(token, rank) loop the reference runs, which the cfg4 CPU baseline times
+    loop = omoe.experts_loop_fp32(latent_x, w["experts.gate_up_proj"], w["experts.down_proj"], ids, weights)
+    torch.testing.assert_close(torch.nn.functional.linear(loop, w["latent_up.weight"]), g["y"], rtol=1e-5, atol=1e-6)
 
 
 def test_topk_tie_rule_agrees_wherever_the_reference_is_deterministic(golden):

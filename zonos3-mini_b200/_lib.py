@@ -70,11 +70,11 @@ SIGNATURES: dict[str, list] = {
     # k_cache, v_cache, slot_stride, num_slots, slots, k, k_stride, v, v_stride, N, Hkv, hd, stream
     "zb_kv_store": [_p, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i32, _i32, _i32, _p],
     # q, q_stride, k_cache, v_cache, slot_stride, num_slots, page_table, table_stride, seq_lens, max_seq_len, B, Hq,
-    # Hkv, hd, scale, splits, split_len, workspace, workspace_bytes, out, out_stride, stream
-    # logits, logits_fp32, softcap, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size, audio_pad_id,
+    # Hkv, hd, scale, splits, split_len, workspace, workspace_bytes, out, out_stride, gate, gate_stride, stream
+    # logits, logits_fp32, softcap, row_stride, batch_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size, audio_pad_id,
     # stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed, offset, offset_dev,
     # text_vocab, out, probs_out, stream
-    "zb_sample_tts": [_p, _i32, _f32, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
+    "zb_sample_tts": [_p, _i32, _f32, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _f32, _f32, _i32, _i32, _p, _p, _p, _p, _p,
                       _i32, _p, _u64, _u64, _p, _i32, _p, _p, _p],
     # ids, ids_stride, ncols, tables (host array), table_rows (host array), norm_weight, eps, normalize, N, D, out,
     # out_stride, stream
@@ -83,7 +83,7 @@ SIGNATURES: dict[str, list] = {
     # Hq, Hkv, hd, stream
     "zb_gqa_prologue_decode": [_p, _i64, _p, _p, _f32, _f32, _p, _p, _p, _i64, _i64, _p, _i32, _i32, _i32, _i32, _p],
     "zb_gqa_decode": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _p,
-                      _i64, _p, _i64, _p],
+                      _i64, _p, _i64, _p, _i64, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None, "zb_launch_count": ctypes.c_uint64,
              "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64}

@@ -8,9 +8,10 @@ forward(x [N, D] bf16) reads ``get_global_ctx().batch.attn_metadata`` and ``get_
     p = x @ [wq; wkv; gater]^T                              (one cuBLAS GEMM over the concatenated weights)
     decode:  q = zb_gqa_prologue_decode(p)                  (q / k RMSNorm eps 1e-6, q x |temp|, interleaved RoPE,
                                                              k and v stored at the rows' cache slots)
-             o = zb_gqa_decode(q, cache, page_table)        (tcgen05 decode attention, unsplit)
+             o = zb_gqa_decode(q, cache, page_table, gate)  (tcgen05 decode attention, unsplit, the output gate
+                                                             sigmoid(gate) applied in its store)
     prefill: the same prologue in torch, zb_kv_store, causal softmax attention per request in torch
-    y = (o * sigmoid(gate)) @ wo^T
+    y = (o * sigmoid(gate)) @ wo^T                          (prefill: the gate in torch)
 
 The prefill attention is plain torch: the north_star path is the decode step, and the reference runs its prefill
 attention through flash_attn_varlen_func (fa.py), a library kernel this package does not replace.
@@ -97,14 +98,13 @@ class Attention(BaseOP):
         n, H, Hkv, hd = x.shape[0], self.num_heads, self.num_kv_heads, self.head_dim
         p = F.linear(x, self._proj)  # q | k | v | gate
         kc, vc = pool.k(self._layer_id), pool.v(self._layer_id)
-        if batch.is_decode:
+        gate = p[:, (H + 2 * Hkv) * hd:]
+        if batch.is_decode:  # the output gate rides in the attention kernel's store
             q = ops.gqa_prologue_decode(p, self._temp, meta.positions, kc, vc, meta.out_loc, heads=H, kv_heads=Hkv,
                                         rope_theta=self._theta, eps=QK_NORM_EPS)
-            o = ops.gqa_decode(q, kc, vc, meta.page_table, meta.cache_seqlens, softmax_scale=hd ** -0.5)
+            o = ops.gqa_decode(q, kc, vc, meta.page_table, meta.cache_seqlens, softmax_scale=hd ** -0.5, gate=gate)
         else:
-            o = self._prefill(p, kc, vc, meta)
-        gate = torch.sigmoid(p[:, (H + 2 * Hkv) * hd:])
-        o = o.view(n, H, hd) * gate.unsqueeze(-1)
+            o = self._prefill(p, kc, vc, meta).view(n, H, hd) * torch.sigmoid(gate).unsqueeze(-1)
         return F.linear(o.reshape(n, H * hd), self.wo.weight)
 
     def _prefill(self, p, kc, vc, meta):

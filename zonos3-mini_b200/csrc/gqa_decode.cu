@@ -61,7 +61,19 @@ struct AttnParams {
   __nv_bfloat16* out;  // [B, Hq, hd], request stride out_stride
   int64_t out_stride;
   unsigned* status;  // device status word (a bounded wait that expired sets kStatusAttnDecodeTimeout)
+  const __nv_bfloat16* gate;  // [B, Hq] gate logits (request stride gate_stride) or null
+  int64_t gate_stride;
 };
+
+// out[b, h, d] = bf16(v), or with a gate bf16(bf16(v) * bf16(sigmoid(gate[b, h]))): the attention layer's output
+// gate o * sigmoid(gater(x)) (zonos3.py:326, :383-385) at torch's bf16 rounding points.
+__device__ __forceinline__ void store_out(const AttnParams& p, int64_t b, int h, int hd, int d, float v) {
+  if (p.gate) {
+    const float gl = __bfloat162float(p.gate[b * p.gate_stride + h]);
+    v = zb::bf16_round(v) * zb::bf16_round(1.0f / (1.0f + expf(-gl)));
+  }
+  p.out[b * p.out_stride + (int64_t)h * hd + d] = __float2bfloat16_rn(v);
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(zb::smem_addr(dst)), "l"(src) : "memory");
@@ -203,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnParams p) {
     }
     const int h = kvh * G + g;
     if (p.splits == 1) {
-      p.out[(int64_t)b * p.out_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+      store_out(p, b, h, HD, d, L > 0.f ? A / L : 0.f);
     } else {
       float* part = p.part + (((int64_t)b * p.Hq + h) * p.splits + split) * (HD + 2);
       part[d] = A;
@@ -231,7 +243,7 @@ __global__ void __launch_bounds__(HD) gqa_combine_kernel(AttnParams p) {
       A += f * part[s * (HD + 2) + d];
     }
   }
-  p.out[(int64_t)b * p.out_stride + (int64_t)h * HD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+  store_out(p, b, h, HD, d, L > 0.f ? A / L : 0.f);
 }
 
 template <int HD, int G>
@@ -422,7 +434,7 @@ __global__ void __launch_bounds__(tcattn::kThreadsTma, 1)
       for (int g = 0; g < G; ++g) {
         const int h = c.kvh * G + g;
         if (p.splits == 1) {
-          p.out[(int64_t)c.b * p.out_stride + (int64_t)h * kHD + tid] = __float2bfloat16_rn(0.f);
+          store_out(p, c.b, h, kHD, tid, 0.f);
         } else {
           float* part = p.part + (((int64_t)c.b * p.Hq + h) * p.splits + c.split) * (kHD + 2);
           part[tid] = 0.f;
@@ -532,8 +544,7 @@ __global__ void __launch_bounds__(tcattn::kThreadsTma, 1)
         for (int w = 0; w < kConsumers; ++w) L += tl.lsum[w][g];
         const int h = u.kvh * G + g;
         if (p.splits == 1) {
-          p.out[(int64_t)u.b * p.out_stride + (int64_t)h * kHD + tid] =
-              __float2bfloat16_rn(L > 0.f ? o[g] / L : 0.f);
+          store_out(p, u.b, h, kHD, tid, L > 0.f ? o[g] / L : 0.f);
         } else {
           float* part = p.part + (((int64_t)u.b * p.Hq + h) * p.splits + u.split) * (kHD + 2);
           part[tid] = L > 0.f ? o[g] : 0.f;
@@ -711,7 +722,8 @@ ZB_API int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_
                          int64_t slot_stride, int64_t num_slots, const int32_t* page_table, int64_t table_stride,
                          const int32_t* seq_lens, int max_seq_len, int B, int Hq, int Hkv, int hd,
                          float softmax_scale, int splits, int split_len, float* workspace, int64_t workspace_bytes,
-                         uint16_t* out, int64_t out_stride, cudaStream_t stream) {
+                         uint16_t* out, int64_t out_stride, const uint16_t* gate, int64_t gate_stride,
+                         cudaStream_t stream) {
   ZB_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "gqa_decode: bad heads Hq=%d Hkv=%d", Hq, Hkv);
   if (hd != 32 && hd != 64 && hd != 128) {
     return zb::fail(zb::kUnsupported, "gqa_decode: head dim %d (32, 64 or 128)", hd);
@@ -737,7 +749,9 @@ ZB_API int zb_gqa_decode(const uint16_t* q, int64_t q_stride, const uint16_t* k_
   AttnParams p{reinterpret_cast<const __nv_bfloat16*>(q), q_stride, reinterpret_cast<const __nv_bfloat16*>(k_cache),
                reinterpret_cast<const __nv_bfloat16*>(v_cache), slot_stride, num_slots, page_table, table_stride,
                seq_lens, max_seq_len, B, Hq, Hkv, softmax_scale * 1.4426950408889634f, splits, split_len, workspace,
-               reinterpret_cast<__nv_bfloat16*>(out), out_stride, zb::device_status_ptr()};
+               reinterpret_cast<__nv_bfloat16*>(out), out_stride, zb::device_status_ptr(),
+               reinterpret_cast<const __nv_bfloat16*>(gate), gate_stride};
+  ZB_REQUIRE(!gate || gate_stride >= Hq, "gqa_decode: gate_stride %lld < %d heads", (long long)gate_stride, Hq);
   const int G = Hq / Hkv;
   if (hd == 128) {
     ZB_REQUIRE(q_stride % 8 == 0, "gqa_decode: q_stride %lld must be a multiple of 8", (long long)q_stride);

@@ -30,10 +30,10 @@ constexpr int kThreads = 256;
 constexpr int kMaxVocab = 16384;
 
 struct SamplerParams {
-  const void* logits;  // [B, C, V] rows of V (row stride `row_stride` elements), bf16 or fp32
+  const void* logits;  // [B, C, V]: row (b, c) at b * batch_stride + c * row_stride elements; bf16 or fp32
   int logits_fp32;
   float softcap;  // > 0: logits = softcap * tanh(logits / softcap) first (the head's soft cap)
-  int64_t row_stride;
+  int64_t row_stride, batch_stride;
   int B, C, V;
   const float* temperatures;  // [B]
   int greedy;                 // every temperature <= 0
@@ -352,8 +352,9 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
   const float bias = p.stop_bias ? p.stop_bias[b] : 0.f;
   const float inv_cap = p.softcap > 0.f ? 1.0f / p.softcap : 0.f;
   for (int i = tid; i < V; i += kThreads) {
-    float v = p.logits_fp32 ? reinterpret_cast<const float*>(p.logits)[(int64_t)row * p.row_stride + i]
-                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.logits)[(int64_t)row * p.row_stride + i]);
+    const int64_t at = (int64_t)b * p.batch_stride + (int64_t)c * p.row_stride + i;
+    float v = p.logits_fp32 ? reinterpret_cast<const float*>(p.logits)[at]
+                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.logits)[at]);
     if (p.softcap > 0.f) {
       // cap * tanh(x / cap) as torch evaluates it on the head's dtype: the division by a scalar as a multiply by
       // its reciprocal, each of the three ops rounded to bf16 for bf16 logits
@@ -560,7 +561,8 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
 
 }  // namespace
 
-ZB_API int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t row_stride, int B, int C, int V,
+ZB_API int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int64_t row_stride, int64_t batch_stride,
+                         int B, int C, int V,
                          const float* temperatures, int greedy, int top_k, float top_p, float min_p, int codebook_size,
                          int audio_pad_id, const int32_t* stop_ids, const int32_t* codebook_sizes,
                          const uint8_t* stop_blocked, const float* stop_bias, const int32_t* rep_ids, int W,
@@ -571,11 +573,13 @@ ZB_API int zb_sample_tts(const void* logits, int logits_fp32, float softcap, int
   if (B == 0) return zb::kOk;
   ZB_REQUIRE(logits && stop_ids && out && (greedy || temperatures), "sample_tts: null pointer");
   ZB_REQUIRE(row_stride >= V, "sample_tts: row_stride %lld < V %d", (long long)row_stride, V);
+  ZB_REQUIRE(batch_stride >= (int64_t)(C - 1) * row_stride + V, "sample_tts: batch_stride %lld overlaps the rows",
+             (long long)batch_stride);
   ZB_REQUIRE(0 < codebook_size && codebook_size < V && codebook_size <= audio_pad_id && audio_pad_id < V,
              "sample_tts: codebook_size %d / audio_pad_id %d for vocabulary %d", codebook_size, audio_pad_id, V);
   ZB_REQUIRE(W >= 0 && (W == 0 || rep_ids), "sample_tts: repetition window %d without ids", W);
   ZB_REQUIRE(softcap >= 0.f, "sample_tts: softcap %g", (double)softcap);
-  SamplerParams p{logits, logits_fp32, softcap, row_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size,
+  SamplerParams p{logits, logits_fp32, softcap, row_stride, batch_stride, B, C, V, temperatures, greedy, top_k, top_p, min_p, codebook_size,
                   audio_pad_id, stop_ids, codebook_sizes, stop_blocked, stop_bias, rep_ids, W, rep_penalties, seed,
                   offset, offset_dev, text_vocab, out, probs_out};
   const size_t smem = (size_t)V * sizeof(float);

@@ -96,6 +96,7 @@ class Zonos3ForCausalLM(BaseOP):
         self.out_norm = Weight((D,))
         self.multi_output = Weight((self.n_codebooks * self.audio_vocab, D))
         self._attnres_states: dict = {}
+        self._head = None  # multi_output.weight padded to a multiple of 8 rows (prepare())
 
     @property
     def config(self):
@@ -108,10 +109,22 @@ class Zonos3ForCausalLM(BaseOP):
         return [layer.attention for layer in self.layers.op_list if isinstance(layer.attention, OriginalGDN)]
 
     def prepare(self) -> None:
-        """Concatenated attention projections (after the weights are loaded and on the device, before capture)."""
+        """Concatenated attention projections and the padded head (after the weights are loaded and on the device,
+        before capture)."""
         for layer in self.layers.op_list:
             if isinstance(layer.attention, Attention):
                 layer.attention.prepare()
+        # the head's 10 x 4098 = 40980 outputs make a 81,960-byte row, which is not 16-byte aligned: cuBLAS then falls
+        # back to a slow kernel (189 us instead of ~30 us at 256 rows); 4 zero rows make every logits row aligned
+        w = self.multi_output.weight
+        rows = (w.shape[0] + 7) // 8 * 8
+        self._head = torch.zeros(rows, w.shape[1], device=w.device, dtype=w.dtype)
+        self._head[: w.shape[0]].copy_(w)
+
+    @property
+    def head_rows(self) -> int:
+        """Columns of the padded head output (the logits row stride)."""
+        return (self.n_codebooks * self.audio_vocab + 7) // 8 * 8
 
     def allocate_caches(self, capacity: int, kv_slots: int, device) -> SlotKVPool:
         """Per-slot DeltaNet state pools of ``capacity`` streams and the KV pool of ``kv_slots`` token slots."""
@@ -200,7 +213,8 @@ class DecodeGraph:
         self.cache_seqlens = torch.ones(B, **i32)
         self.slots = (torch.arange(B, device=dev, dtype=torch.int64) if slots is None else slots).contiguous()
         self.x = torch.empty(B, c.hidden_size, device=dev, dtype=torch.bfloat16)
-        self.logits = torch.empty(B, self.C * self.V, device=dev, dtype=torch.bfloat16)
+        self.head_out = torch.empty(B, model.head_rows, device=dev, dtype=torch.bfloat16)  # row stride aligned
+        self.logits = self.head_out[:, : self.C * self.V]  # [B, C * V] view; the sampler reads it in place
         W = max(int(self.sampling.repetition_window), 0)
         self.history = torch.full((B, self.C, max(W, 1)), -1, **i32)
         self.W = W
@@ -223,8 +237,8 @@ class DecodeGraph:
         m, s = self.model, self.sampling
         x = m.embed(self.input_ids, out=self.x)
         h = m.forward_layers(x)
-        torch.matmul(h, m.multi_output.weight.t(), out=self.logits)
-        ops.sample_tts(self.logits.view(self.bs, self.C, self.V), [s.temperature] * self.bs, [s.top_k], [s.top_p],
+        torch.matmul(h, m._head.t(), out=self.head_out)
+        ops.sample_tts(self.logits.unflatten(1, (self.C, self.V)), [s.temperature] * self.bs, [s.top_k], [s.top_p],
                        [s.min_p], codebook_size=self.codebook_size, audio_pad_id=self.audio_pad_id,
                        stop_token_ids=self.stop_ids,
                        repetition_token_ids=self.history if self.W and s.repetition_penalty > 1.0 else None,

@@ -669,7 +669,7 @@ def gqa_splits(batch: int, kv_heads: int, max_len: int, num_splits: int = 1, hea
 
 
 def gqa_decode(q, k_cache, v_cache, page_table, cache_seqlens, *, softmax_scale=None, num_splits=1, out=None,
-               workspace=None):
+               workspace=None, gate=None):
     """Decode attention over a slot-indexed KV cache: the flash_attn_with_kvcache call of the FA backend for a
     decode batch (servers/sgl/src/zonos3_sgl/attention/fa.py:64-81, :171-212; causal, one query row per request,
     one token per page).
@@ -679,7 +679,9 @@ def gqa_decode(q, k_cache, v_cache, page_table, cache_seqlens, *, softmax_scale=
     per request, clamped to max_pages). Query head h
     reads KV head h // (Hq / Hkv). softmax_scale defaults to hd ** -0.5. num_splits as :func:`gqa_splits`;
     workspace: optional fp32 tensor of at least B * Hq * splits * (hd + 2) elements (allocated when absent and
-    needed). Returns out [B, Hq, hd] bf16."""
+    needed). gate: optional [B, Hq] bf16 gate logits (row stride allowed): the output is multiplied by
+    sigmoid(gate) per head, with torch's bf16 rounding points (the attention layer's output gate). Returns out
+    [B, Hq, hd] bf16."""
     dev = q.device
     _check_cuda("q", q, torch.bfloat16)
     B, Hq, hd = q.shape
@@ -708,10 +710,15 @@ def gqa_decode(q, k_cache, v_cache, page_table, cache_seqlens, *, softmax_scale=
     if need:
         _check_cuda("workspace", workspace, torch.float32, dev)
     scale = float(hd ** -0.5 if softmax_scale is None else softmax_scale)
+    gs = 0
+    if gate is not None:
+        _check_cuda("gate", gate, torch.bfloat16, dev)
+        _require(gate.dim() == 2 and gate.shape == (B, Hq) and gate.stride(1) == 1, f"gate must be [{B}, {Hq}]")
+        gs = gate.stride(0) if B > 1 else Hq
     _lib.call("zb_gqa_decode", q.data_ptr(), qs, k_cache.data_ptr(), v_cache.data_ptr(), cs, k_cache.shape[0],
               page_table.data_ptr(), page_table.stride(0) if B > 1 else page_table.shape[1], cache_seqlens.data_ptr(),
               page_table.shape[1], B, Hq, Hkv, hd, scale, splits, split_len, workspace.data_ptr() if need else None,
-              need * 4, out.data_ptr(), os_, _stream(dev))
+              need * 4, out.data_ptr(), os_, None if gate is None else gate.data_ptr(), gs, _stream(dev))
     return out
 
 
@@ -741,8 +748,8 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
     _require(logits.dtype in (torch.bfloat16, torch.float32), "logits must be bf16 or fp32")
     dev = logits.device
     B, C, V = logits.shape
-    _require(logits.stride(2) == 1 and logits.stride(0) == C * logits.stride(1), "logits rows must be [B, C, V] "
-             "with contiguous rows and codebooks")
+    _require(logits.stride(2) == 1 and logits.stride(1) >= V and logits.stride(0) >= (C - 1) * logits.stride(1) + V,
+             "logits must be [B, C, V] with contiguous, non-overlapping rows")
     temps = _host_list(temperatures)
     greedy = all(float(t) <= 0 for t in temps)
     top_k = int(min(int(k) for k in _host_list(top_ks))) if B else 0
@@ -770,7 +777,7 @@ def sample_tts(logits, temperatures, top_ks, top_ps, min_ps, *, codebook_size, a
         _require(offset_dev.numel() >= 1, "offset_dev must hold one counter")
     ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
     _lib.call("zb_sample_tts", logits.data_ptr(), int(logits.dtype == torch.float32), float(softcap), logits.stride(1),
-              B, C, V,
+              logits.stride(0), B, C, V,
               temp_d.data_ptr(), int(greedy), top_k, top_p, min_p, int(codebook_size), int(audio_pad_id),
               stop_d.data_ptr(), ptr(sizes_d), ptr(blocked_d), ptr(bias_d), ptr(rep_d), W, ptr(pen_d),
               int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), ptr(offset_dev), int(text_vocab), out.data_ptr(),
