@@ -74,3 +74,59 @@ def test_static_graph_decode_matches_oracle(zb, heads, head_dim):
     assert layer._recurrent_state[untouched].abs().max().item() == 0.0
     assert layer._conv_state[untouched].abs().max().item() == 0.0
     del graph
+
+
+def test_static_padded_prefill_captured_and_replayed(zb):
+    """The padded prefill of fresh requests (PrefillLayout whole = [1, 0, 2]: 128 + 64 + 192 rows, the reference's
+    _forward_prefill_static layout, gdn.py:62-104, :357-393) captured once in a CUDA graph and replayed twice with
+    other real lengths and other data, padding rows holding noise; every real output row, final state and conv
+    history against the oracle run per request (oracle/gdn.gdn_layer), then one decode step per request continuing
+    from the committed state."""
+    hidden, heads, head_dim = 256, 4, 128
+    dev = torch.device("cuda")
+    layer = fill_gdn(zb.gdn.OriginalGDN(gdn_config(zb, hidden, heads, head_dim), 0), seed=21)
+    layer.to(dev, torch.bfloat16)
+    layer.allocate_cache(8, dev, torch.bfloat16)
+    w32 = {k: v.float().cpu() for k, v in layer.state_dict().items()}
+    whole = [1, 0, 2]
+    layout = zb.gdn.PrefillLayout.build(whole, dev)
+    starts = layout.starts.tolist()
+    x_buf = torch.zeros(layout.rows, hidden, device=dev, dtype=torch.bfloat16)
+    slots_buf = torch.tensor([5, 0, 3], dtype=torch.int64, device=dev)
+    len_buf = torch.tensor([65, 1, 129], dtype=torch.int64, device=dev)
+    Req = zb.core.Req
+    inputs = zb.gdn.PrefillInputs(layout, slots_buf, len_buf)
+    batch = zb.core.Batch(reqs=[Req(5, 128, 0, uid=0), Req(0, 64, 0, uid=1), Req(3, 192, 0, uid=2)], is_decode=False,
+                          gdn_prefill=inputs)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream), zb.core.forward_batch(batch):
+        layer.forward(x_buf)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            y_buf = layer.forward(x_buf)
+    torch.cuda.current_stream().wait_stream(stream)
+    gen = torch.Generator().manual_seed(4)
+    for lengths in ([70, 2, 150], [128, 64, 129]):
+        xs = [torch.randn(n + 1, hidden, generator=gen).bfloat16() for n in lengths]  # the last row: a decode step
+        rows = torch.randn(layout.rows, hidden, generator=gen).bfloat16()  # padding rows hold noise
+        for s0, x, n in zip(starts, xs, lengths):
+            rows[s0:s0 + n] = x[:n]
+        x_buf.copy_(rows)
+        len_buf.copy_(torch.tensor(lengths))
+        graph.replay()
+        torch.cuda.synchronize()
+        layer.note_graph_forward([Req(s, n, 0, uid=i) for i, (s, n) in enumerate(zip([5, 0, 3], lengths))])
+        reqs = [Req(s, 1, n, uid=i) for i, (s, n) in enumerate(zip([5, 0, 3], lengths))]
+        with zb.core.forward_batch(zb.core.Batch(reqs=reqs, is_decode=True)):
+            step = layer.forward(torch.stack([x[n] for x, n in zip(xs, lengths)]).to(dev))
+        torch.cuda.synchronize()
+        for i, (x, n, s0, slot) in enumerate(zip(xs, lengths, starts, [5, 0, 3])):
+            ref_pre, conv, state = ogdn.gdn_layer(x[:n].float(), w32, heads=heads, head_dim=head_dim)
+            assert rel_err(y_buf[s0:s0 + n].float().cpu(), ref_pre) < TOL, (lengths, i)
+            ref_all, conv2, state2 = ogdn.gdn_layer(x.float(), w32, heads=heads, head_dim=head_dim)
+            assert rel_err(step[i].float().cpu(), ref_all[n]) < TOL, (lengths, i)
+            assert max_rel_err(layer._recurrent_state[slot].cpu(), state2) < TOL, (lengths, i)
+            assert rel_err(layer._conv_state[slot].float().cpu(), conv2) < TOL, (lengths, i)
+    del graph

@@ -60,3 +60,17 @@ def test_decode_step_bytes(zb):
     # one more cached key per stream adds its K and V rows in the 6 GQA layers and its page-table entry
     assert bench.cfg5_step_bytes(256, 879) - total == 6 * 256 * (4 * 128 * 2 * 2 + 4)
     assert inner == 2048
+
+
+def test_prefill_layout_and_chunk_tables(zb):
+    """PrefillLayout.build([1, 0, 2]) lays requests out as 128, 64 and 192 padded rows; chunk_tables gives the
+    reference's cu_seqlens and (sequence, chunk) indices (servers/sgl/src/zonos3_sgl/models/gdn.py:49-59)."""
+    layout = zb.gdn.PrefillLayout.build([1, 0, 2], "cpu")
+    assert layout.rows == 384
+    assert layout.starts.tolist() == [0, 128, 192] and layout.cu_seqlens.tolist() == [0, 128, 192, 384]
+    assert layout.seq_of_token.tolist() == [0] * 128 + [1] * 64 + [2] * 192
+    assert layout.row_in_seq.tolist() == list(range(128)) + list(range(64)) + list(range(192))
+    assert layout.fresh.tolist() == [1, 1, 1] and len(layout.tensors()) == 5
+    cu, chunks = zb.gdn.chunk_tables([70, 2, 129], "cpu")
+    assert cu.tolist() == [0, 70, 72, 201]
+    assert chunks.tolist() == [[0, 0], [0, 1], [1, 0], [2, 0], [2, 1], [2, 2]]

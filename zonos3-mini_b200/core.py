@@ -63,16 +63,30 @@ class Context:
 _CTX = Context()
 
 
+def _reference_context():
+    """The reference server's get_global_ctx (servers/sgl/src/zonos3_sgl/core.py) when that package imports, so the
+    modules dropped into the server read the server's batch; None otherwise (this package's own context)."""
+    try:
+        from zonos3_sgl.core import get_global_ctx as reference_ctx  # noqa: PLC0415
+    except Exception:  # the reference server is not installed (or its native dependencies are missing)
+        return None
+    return reference_ctx
+
+
+_REFERENCE_CTX = _reference_context()
+
+
 def get_global_ctx() -> Context:
-    return _CTX
+    return _REFERENCE_CTX() if _REFERENCE_CTX is not None else _CTX
 
 
 @contextlib.contextmanager
 def forward_batch(batch: Batch):
     """Make ``batch`` the current batch for the duration of one model forward."""
-    previous = _CTX.batch
-    _CTX.batch = batch
+    ctx = get_global_ctx()
+    previous = ctx.batch
+    ctx.batch = batch
     try:
         yield batch
     finally:
-        _CTX.batch = previous
+        ctx.batch = previous

@@ -19,6 +19,8 @@ nothing is gathered or scattered around the kernels.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 import torch.nn.functional as F
 
@@ -27,6 +29,71 @@ from .base import BaseOP, Weight
 from .core import get_global_ctx
 
 CONV_WIDTH = 4
+CHUNK = 64  # the chunk length of the reference's training kernel and of the padded prefill layout
+
+
+def chunk_tables(lengths: list[int], device) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cu_seqlens [n + 1], chunk indices [chunks, 2] = (sequence, chunk within it)) of packed sequences of
+    ``lengths`` rows, int32 on ``device`` in one copy (servers/sgl/src/zonos3_sgl/models/gdn.py:49-59). The B200
+    chunked prefill needs only cu_seqlens; the chunk indices are kept for callers of the reference interface."""
+    cu = [0]
+    chunks: list[int] = []
+    for i, n in enumerate(lengths):
+        cu.append(cu[-1] + n)
+        for j in range(-(-n // CHUNK)):
+            chunks += (i, j)
+    packed = torch.tensor(cu + chunks, dtype=torch.int32).to(device)
+    return packed[: len(cu)], packed[len(cu):].view(-1, 2)
+
+
+@dataclass(frozen=True)
+class PrefillLayout:
+    """Static tables of a padded prefill of fresh requests (the reference's PrefillLayout, gdn.py:62-104): request i
+    owns ``CHUNK * (whole[i] + 1)`` rows of the batch from ``starts[i]``, its real rows first (more than
+    ``CHUNK * whole[i]``, at most all of them), padding after. Every tensor's shape depends on ``whole`` only, so a
+    forward over the layout can be captured in a CUDA graph and replayed for any real lengths that fit it."""
+
+    whole: tuple[int, ...]
+    starts: torch.Tensor  # [b] int64: first batch row of each request
+    cu_seqlens: torch.Tensor  # [b + 1] int32: the padded blocks as packed sequences
+    seq_of_token: torch.Tensor  # [N] int32: request of each batch row
+    row_in_seq: torch.Tensor  # [N] int64: position of each batch row within its request's block
+    fresh: torch.Tensor  # [b] uint8 ones: every request starts from a zero state
+
+    @classmethod
+    def build(cls, whole: list[int], device) -> "PrefillLayout":
+        sizes = [CHUNK * (w + 1) for w in whole]
+        cu = [0]
+        for n in sizes:
+            cu.append(cu[-1] + n)
+        dev = torch.device(device)
+        return cls(
+            whole=tuple(int(w) for w in whole),
+            starts=torch.tensor(cu[:-1], dtype=torch.int64, device=dev),
+            cu_seqlens=torch.tensor(cu, dtype=torch.int32, device=dev),
+            seq_of_token=torch.tensor([i for i, n in enumerate(sizes) for _ in range(n)], dtype=torch.int32,
+                                      device=dev),
+            row_in_seq=torch.tensor([r for n in sizes for r in range(n)], dtype=torch.int64, device=dev),
+            fresh=torch.ones(len(sizes), dtype=torch.uint8, device=dev),
+        )
+
+    @property
+    def rows(self) -> int:
+        return sum(CHUNK * (w + 1) for w in self.whole)
+
+    def tensors(self) -> list[torch.Tensor]:
+        """The layout's device tables (what a graph replay reads)."""
+        return [self.starts, self.cu_seqlens, self.seq_of_token, self.row_in_seq, self.fresh]
+
+
+@dataclass
+class PrefillInputs:
+    """A padded prefill's GDN inputs (``batch.gdn_prefill``, gdn.py:107-113): the layout and the graph's per-replay
+    buffers."""
+
+    layout: PrefillLayout
+    slots: torch.Tensor  # [b] int64: the requests' state slots
+    lengths: torch.Tensor  # [b] int64: the requests' real rows
 
 
 class OriginalGDN(BaseOP):
@@ -94,8 +161,10 @@ class OriginalGDN(BaseOP):
         batch = get_global_ctx().batch
         if batch.is_decode and self._static_mode:
             return self._forward_decode_static(x, batch.padded_size)
+        if getattr(batch, "gdn_prefill", None) is not None:
+            return self._forward_prefill_static(x, batch.gdn_prefill)
         if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("GDN ragged path cannot be captured; graphs use the static decode path")
+            raise RuntimeError("GDN ragged path cannot be captured; graphs use the static decode / prefill paths")
         reqs = batch.reqs
         slots = [r.table_idx for r in reqs]
         lengths = [r.extend_len for r in reqs]
@@ -142,6 +211,41 @@ class OriginalGDN(BaseOP):
             raise RuntimeError(f"GDN static decode is not prepared for batch size {bs}")
         cu, sot = self._static[bs]
         return self._run(x, cu, sot, self._graph_slots[:bs], None, decode=True, any_fresh=False)
+
+    def _forward_prefill_static(self, x, inputs: PrefillInputs):
+        """A padded prefill of fresh requests (PrefillLayout): one chunked pass over every request's padded block
+        from a zero state. Padding rows are zeroed and enter the recurrence as identity updates (decay 1, beta 0),
+        so each request's final state is its state after its real rows; its conv history is rewritten from its last
+        CONV_WIDTH - 1 real rows (zeros before its first). Every shape depends on the layout only (capturable)."""
+        layout, slots = inputs.layout, inputs.slots
+        if x.shape[0] != layout.rows or slots.numel() != len(layout.whole):
+            raise RuntimeError(f"padded prefill of {x.shape[0]} rows does not match its layout ({layout.rows} rows, "
+                               f"{len(layout.whole)} requests)")
+        H, d = self._heads, self._head_dim
+        inner = H * d
+        lengths = inputs.lengths.to(torch.int64)
+        real = layout.row_in_seq < lengths.index_select(0, layout.seq_of_token.to(torch.int64))
+        x = x * real.unsqueeze(1).to(x.dtype)
+        mixed = F.linear(x, self.in_proj.weight)
+        q, k, v, g, beta = ops.gdn_prologue(mixed, self.conv.weight, self.A_log, self.dt_bias, layout.cu_seqlens,
+                                            layout.seq_of_token, slots, self._conv_state, heads=H, head_dim=d,
+                                            fresh=layout.fresh)
+        keep = real.unsqueeze(1)
+        g = g.masked_fill(~keep, 0.0)
+        beta = beta.masked_fill(~keep, 0.0)
+        self._recurrent_state.index_fill_(0, slots, 0.0)
+        o, _ = ops.gdn_chunk_prefill(q, k, v, g, beta, layout.cu_seqlens, initial_state=self._recurrent_state,
+                                     final_state=self._recurrent_state, state_slots=slots)
+        # conv history: the q/k/v channels of the last CONV_WIDTH - 1 real rows, oldest first
+        W1 = CONV_WIDTH - 1
+        offs = torch.arange(-W1, 0, device=x.device, dtype=torch.int64)
+        rows = layout.starts.unsqueeze(1) + lengths.unsqueeze(1) + offs.unsqueeze(0)  # [b, W1]
+        inside = rows >= layout.starts.unsqueeze(1)
+        hist = mixed[:, : 3 * inner].index_select(0, rows.clamp(min=0).reshape(-1)).view(-1, W1, 3 * inner)
+        hist = hist * inside.unsqueeze(2).to(hist.dtype)
+        self._conv_state.index_copy_(0, slots, hist.transpose(1, 2).to(self._conv_state.dtype))
+        gated = ops.gdn_gated_norm(o, mixed[:, 3 * inner:4 * inner], self.out_weight, 1e-5)
+        return F.linear(gated, self.wo.weight)
 
     def _run(self, x, cu, seq_of_token, slots, fresh, *, decode: bool, any_fresh: bool):
         H, d = self._heads, self._head_dim
