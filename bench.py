@@ -1033,7 +1033,7 @@ def main():
         value, threads, dt, per_step = cpu_reference_cfg5(samples)
         sample = (f"{samples} stream-steps of a 4-layer slice (3 DeltaNet + 1 GQA) and of the 0-layer remainder of "
                   f"the cfg5 model at {CONTEXT5} cached keys, one stream per call, scaled to 24 layers "
-                  f"({per_step * 1e3:.0f} ms per stream-step; {dt:.1f} s incl. init)")
+                  f"({per_step * 1e3:.0f} ms per stream-step; {dt:.1f} s of timed forwards)")
         line = {
             "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * STREAMS5 * 1e3,
@@ -1054,7 +1054,7 @@ def main():
                 "value": value, "unit": UNIT, "cores": threads, "kind": "port",
                 "sample": f"{args.cpu_samples} stream-steps of a 4-layer slice and of the 0-layer remainder of the "
                           f"cfg5 model (oracle/lm.py restating lm.py:660-735, fp32), scaled to 24 layers; "
-                          f"{per_step * 1e3:.0f} ms per stream-step ({dt:.1f} s incl. init)",
+                          f"{per_step * 1e3:.0f} ms per stream-step ({dt:.1f} s of timed forwards)",
             }
             if args.operators and world == 1:
                 pkg = __import__("__graft_entry__").load_package()
