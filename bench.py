@@ -346,6 +346,8 @@ def run_ours(args, dist, rank, world, local):
         barrier(dist)
     e2e_ms = max_over_ranks(dist, e_start.elapsed_time(e_stop))
 
+    strong = strong_scaling(pkg, model, graph, dist, rank, world, dev, stream, args) if world > 1 else None
+
     step_ms = elapsed_ms / args.steps
     context_mid = CONTEXT5 + args.warmup + args.steps // 2
     nbytes = cfg5_step_bytes(STREAMS5, context_mid)
@@ -375,6 +377,7 @@ def run_ours(args, dist, rank, world, local):
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / n_e2e,
                 "path": "DecodeGraph.step: pinned host ids + positions / cache lengths / KV slots in, codes out, "
                         "host sync per step"},
+        "strong_scaling": strong,
         "gpu_launches": graph.launches_per_step * args.steps,
         "launches_per_step": graph.launches_per_step,
         "device_status": status,
@@ -383,6 +386,38 @@ def run_ours(args, dist, rank, world, local):
     del graph, model
     torch.cuda.empty_cache()
     return line
+
+
+def strong_scaling(pkg, model, graph, dist, rank, world, dev, stream, args) -> dict:
+    """The config's 256 streams split over the ranks (replicas.shard: a contiguous share per GPU), each rank's share
+    decoded by its own captured step on the same model and caches; timed like the weak-scaling value (max over
+    ranks). Under strong scaling every GPU still reads all 15.6 GB of weights per step, so the box throughput grows
+    far slower than the GPU count."""
+    share = pkg.replicas.shard(STREAMS5, world, rank)
+    n = len(share)
+    table, _ = cfg5_page_table(n, dev)
+    sampling = pkg.model.SamplingConfig(seed=7 + rank, **SAMPLING5)
+    sub = pkg.model.DecodeGraph(model, graph.pool, n, table, sampling=sampling)
+    sub.capture()
+    ids = graph.input_ids[:n].clone()
+    pos = graph.positions[:n].clone()
+    sub.load(ids, pos, pos + 1, table[torch.arange(n, device=dev), pos.long()].contiguous())
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            sub.replay()
+        torch.cuda.synchronize(dev)
+        barrier(dist)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            sub.replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(dist)
+    ms = max_over_ranks(dist, a.elapsed_time(b))
+    del sub
+    return {"streams_total": STREAMS5, "streams_per_gpu": STREAMS5 // world, "ms_per_step": ms / args.steps,
+            "value": STREAMS5 * args.steps / (ms / 1e3), "unit": UNIT}
 
 
 # --------------------------------------------------------------------------------------------- CPU reference
