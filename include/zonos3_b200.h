@@ -310,6 +310,17 @@ int zb_embed_norm(const int32_t* ids, int64_t ids_stride, int ncols, const uint1
                   const int32_t* table_rows, const uint16_t* norm_weight, float eps, int normalize, int N, int D,
                   uint16_t* out, int64_t out_stride, cudaStream_t stream);
 
+/* The bookkeeping between two captured decode steps, in one single-block launch: ids[b, :ids_cols] = codes[b, ...]
+ * (the sampled codes, then the text column, become the next input row), history[b, c, *ring] = codes[b, c] for the
+ * first C codebooks (history NULL: none; W columns, *ring the next one), positions[b] += 1, seqlens[b] =
+ * min(seqlens[b] + 1, max_len), out_loc[b] = page_table[b, seqlens[b] - 1]; then *ring = (*ring + 1) % W and
+ * *counter += 1 (the sampler's draw counter). The engine does this on the host between steps (the scheduler builds
+ * the next batch's ids and attention metadata); here it stays on the device so that replays alone decode. No
+ * reference counterpart as a kernel. */
+int zb_decode_advance(const int32_t* codes, int codes_cols, int32_t* ids, int ids_cols, int32_t* history, int C, int W,
+                      int64_t* ring, int64_t* counter, int32_t* positions, int32_t* seqlens, int32_t* out_loc,
+                      const int32_t* page_table, int64_t table_stride, int max_len, int B, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -147,3 +147,35 @@ def test_embed_norm_matches_torch(zb):
             sum_row = sum_row + F.embedding(bad[1, c:c + 1].long(), tables[c])
     assert torch.equal(out[1:2], sum_row)
     assert zb.ops.device_status() & 32
+
+
+def test_decode_advance_matches_torch(zb):
+    """zb_decode_advance against the same bookkeeping in torch: next ids from the codes, the repetition window
+    column, positions, capped cache lengths, next KV slots, ring column and draw counter."""
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(2)
+    B, C, W, L = 37, 10, 5, 20
+    codes = torch.randint(0, 4098, (B, C + 1), generator=gen, dtype=torch.int32).to(dev)
+    table = torch.randint(0, 10 ** 6, (B, L), generator=gen, dtype=torch.int32).to(dev)
+    state = dict(ids=torch.zeros(B, C + 1, dtype=torch.int32), history=torch.randint(-1, 9, (B, C, W), generator=gen,
+                 dtype=torch.int32), ring=torch.tensor([3]), counter=torch.tensor([41]),
+                 positions=torch.randint(0, 18, (B,), generator=gen, dtype=torch.int32))
+    state["seqlens"] = (state["positions"] + 1).clamp(max=L)
+    state["seqlens"][:3] = L  # already at the table's width
+    got = {k: v.to(dev) for k, v in state.items()}
+    got["out_loc"] = torch.zeros(B, dtype=torch.int32, device=dev)
+    for _ in range(2):
+        zb.ops.decode_advance(codes, got["ids"], got["positions"], got["seqlens"], got["out_loc"], table,
+                              got["counter"], history=got["history"], ring=got["ring"])
+        ref = state
+        ref["ids"] = codes.cpu().clone()
+        ref["history"][:, :, int(ref["ring"])] = codes.cpu()[:, :C]
+        ref["ring"] = (ref["ring"] + 1) % W
+        ref["counter"] = ref["counter"] + 1
+        ref["positions"] = ref["positions"] + 1
+        ref["seqlens"] = (ref["seqlens"] + 1).clamp(max=L)
+        out_loc = table.cpu().gather(1, (ref["seqlens"] - 1).long().unsqueeze(1)).view(-1)
+        torch.cuda.synchronize()
+        for k in ("ids", "history", "ring", "counter", "positions", "seqlens"):
+            assert torch.equal(got[k].cpu(), ref[k]), k
+        assert torch.equal(got["out_loc"].cpu(), out_loc)

@@ -79,6 +79,9 @@ SIGNATURES: dict[str, list] = {
     # ids, ids_stride, ncols, tables (host array), table_rows (host array), norm_weight, eps, normalize, N, D, out,
     # out_stride, stream
     "zb_embed_norm": [_p, _i64, _i32, _p, _p, _p, _f32, _i32, _i32, _i32, _p, _i64, _p],
+    # codes, codes_cols, ids, ids_cols, history, C, W, ring, counter, positions, seqlens, out_loc, page_table,
+    # table_stride, max_len, B, stream
+    "zb_decode_advance": [_p, _i32, _p, _i32, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _p],
     # proj, proj_stride, temp, positions, theta, eps, q_out, k_cache, v_cache, slot_stride, num_slots, out_loc, N,
     # Hq, Hkv, hd, stream
     "zb_gqa_prologue_decode": [_p, _i64, _p, _p, _f32, _f32, _p, _p, _p, _i64, _i64, _p, _i32, _i32, _i32, _i32, _p],

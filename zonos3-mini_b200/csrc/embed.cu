@@ -8,6 +8,8 @@
 // (C + 1) table rows of a token are independent loads issued back to back; the sum of squares is a block reduction.
 // An id outside its table is read as a zero row and sets kStatusEmbedIndex in the library status word (the reference
 // raises there; a kernel cannot).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace {
@@ -137,4 +139,67 @@ ZB_API int zb_embed_norm(const int32_t* ids, int64_t ids_stride, int ncols, cons
   const unsigned threads = (unsigned)((D / 8 + 31) / 32 * 32);
   ZB_CUDA(zb::launch(embed_norm_kernel, dim3((unsigned)N), dim3(threads), 0, stream, 1, p));
   return zb::check_launch("embed_norm");
+}
+
+// ------------------------------------------------------------------------------------ decode-step bookkeeping
+
+namespace {
+
+struct AdvanceParams {
+  const int32_t* codes;  // [B, codes_cols] sampled codes (then the text column)
+  int codes_cols;
+  int32_t* ids;  // [B, ids_cols]: the next step's input ids
+  int ids_cols;
+  int32_t* history;  // [B, C, W] repetition window, or null
+  int C, W;
+  int64_t* ring;     // [1] next window column
+  int64_t* counter;  // [1] the sampler's draw counter
+  int32_t* positions;
+  int32_t* seqlens;
+  int32_t* out_loc;
+  const int32_t* page_table;  // [B, max_len]
+  int64_t table_stride;
+  int max_len;
+  int B;
+};
+
+// One block: every stream's next ids, its codes in the repetition window at the ring column, its position and
+// cache length + 1, its next KV slot from the page table; then the ring column and the draw counter advance.
+__global__ void __launch_bounds__(1024) decode_advance_kernel(AdvanceParams p) {
+  zb::pdl_enter();
+  const int64_t col = p.W > 0 ? *p.ring : 0;
+  for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+    const int32_t* cb = p.codes + (int64_t)b * p.codes_cols;
+    for (int j = 0; j < p.ids_cols; ++j) p.ids[(int64_t)b * p.ids_cols + j] = cb[j];
+    if (p.history)
+      for (int c = 0; c < p.C; ++c) p.history[((int64_t)b * p.C + c) * p.W + col] = cb[c];
+    p.positions[b] += 1;
+    const int len = min(p.seqlens[b] + 1, p.max_len);
+    p.seqlens[b] = len;
+    p.out_loc[b] = p.page_table[(int64_t)b * p.table_stride + len - 1];
+  }
+  __syncthreads();  // every thread has read the ring column
+  if (threadIdx.x == 0) {
+    if (p.W > 0) *p.ring = (col + 1) % p.W;
+    *p.counter += 1;
+  }
+}
+
+}  // namespace
+
+ZB_API int zb_decode_advance(const int32_t* codes, int codes_cols, int32_t* ids, int ids_cols, int32_t* history,
+                             int C, int W, int64_t* ring, int64_t* counter, int32_t* positions, int32_t* seqlens,
+                             int32_t* out_loc, const int32_t* page_table, int64_t table_stride, int max_len, int B,
+                             cudaStream_t stream) {
+  ZB_REQUIRE(B >= 0 && codes_cols > 0 && ids_cols > 0 && ids_cols <= codes_cols && C >= 0 && C <= codes_cols &&
+                 W >= 0 && max_len > 0 && table_stride >= max_len,
+             "decode_advance: bad sizes B=%d codes_cols=%d ids_cols=%d C=%d W=%d max_len=%d", B, codes_cols, ids_cols,
+             C, W, max_len);
+  if (B == 0) return zb::kOk;
+  ZB_REQUIRE(codes && ids && counter && positions && seqlens && out_loc && page_table && (!history || (W > 0 && ring)),
+             "decode_advance: null pointer");
+  AdvanceParams p{codes, codes_cols, ids, ids_cols, history, C, W, ring, counter, positions, seqlens, out_loc,
+                  page_table, table_stride, max_len, B};
+  ZB_CUDA(zb::launch(decode_advance_kernel, dim3(1), dim3((unsigned)std::min(B, 1024)), 0, stream, 1, p));
+  return zb::check_launch("decode_advance");
 }

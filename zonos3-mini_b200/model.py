@@ -245,15 +245,10 @@ class DecodeGraph:
                        repetition_penalties=self.penalties, text_vocab=self.text_pad, seed=s.seed,
                        offset_dev=self.counter, out=self.codes, device_temperatures=self.temperatures,
                        softcap=self.softcap)
-        # the next step's inputs, on the device
-        self.input_ids.copy_(self.codes[:, : self.input_ids.shape[1]])
-        if self.W:
-            self.history.index_copy_(2, self.ring, self.codes[:, : self.C].unsqueeze(-1))
-            self.ring.add_(1).remainder_(self.W)
-        self.counter.add_(1)
-        self.positions.add_(1)
-        self.cache_seqlens.add_(1).clamp_(max=self.page_table.shape[1])
-        torch.gather(self.page_table, 1, (self.cache_seqlens - 1).long().unsqueeze(1), out=self.out_loc.view(-1, 1))
+        # the next step's inputs, on the device (one kernel)
+        ops.decode_advance(self.codes, self.input_ids, self.positions, self.cache_seqlens, self.out_loc,
+                           self.page_table, self.counter, history=self.history if self.W else None,
+                           ring=self.ring if self.W else None)
 
     def _context(self):
         ctx = get_global_ctx()

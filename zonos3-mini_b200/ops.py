@@ -846,3 +846,29 @@ def gqa_prologue_decode(proj, temp, positions, k_cache, v_cache, out_loc, *, hea
               positions.data_ptr(), float(rope_theta), float(eps), q_out.data_ptr(), k_cache.data_ptr(),
               v_cache.data_ptr(), cs, k_cache.shape[0], out_loc.data_ptr(), N, heads, kv_heads, hd, _stream(dev))
     return q_out
+
+
+def decode_advance(codes, ids, positions, cache_seqlens, out_loc, page_table, counter, *, history=None, ring=None):
+    """The bookkeeping between two decode steps in one kernel (zb_decode_advance): the sampled codes [B, >= cols]
+    become the next ids [B, cols]; the first C codes enter the repetition window history [B, C, W] at column
+    ring[0]; positions and cache_seqlens advance by one (lengths capped at the page table's width); out_loc takes
+    each stream's next page-table slot; ring and the sampler's draw counter (int64 [1]) advance."""
+    dev = codes.device
+    for name, t in (("codes", codes), ("ids", ids), ("positions", positions), ("cache_seqlens", cache_seqlens),
+                    ("out_loc", out_loc), ("page_table", page_table)):
+        _check_cuda(name, t, torch.int32, dev)
+        _require(t.is_contiguous() or name == "page_table", f"{name} must be contiguous")
+    _check_cuda("counter", counter, torch.int64, dev)
+    B = codes.shape[0]
+    _require(ids.shape[0] == B and ids.shape[1] <= codes.shape[1], "ids must be [B, <= codes columns]")
+    _require(page_table.dim() == 2 and page_table.shape[0] == B and page_table.stride(1) == 1, "page_table [B, L]")
+    C = W = 0
+    if history is not None:
+        _check_cuda("history", history, torch.int32, dev)
+        _check_cuda("ring", ring, torch.int64, dev)
+        _require(history.dim() == 3 and history.shape[0] == B and history.is_contiguous(), "history [B, C, W]")
+        C, W = history.shape[1], history.shape[2]
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call("zb_decode_advance", codes.data_ptr(), codes.shape[1], ids.data_ptr(), ids.shape[1], ptr(history), C, W,
+              ptr(ring), counter.data_ptr(), positions.data_ptr(), cache_seqlens.data_ptr(), out_loc.data_ptr(),
+              page_table.data_ptr(), page_table.stride(0), page_table.shape[1], B, _stream(dev))
