@@ -108,6 +108,36 @@ int zb_gdn_prologue_decode(const uint16_t* mixed, int64_t mixed_stride, const ui
 int zb_gdn_gated_norm(const uint16_t* o, const uint16_t* z, int64_t z_stride, const uint16_t* weight, float eps, int N,
                       int H, int D, uint16_t* out, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------------- dense projections (tcgen05) */
+
+/* Device workspace bytes of a projection GEMM of T tokens, N output columns and reduction length K with column tile
+ * block_n (64, 128, 256; 0 = chosen from the shape) and `splits` K slices (0 = chosen): the split-K ticket counters
+ * (first, 256-byte padded) and fp32 partial tiles; 0 when the plan has one slice. */
+int64_t zb_proj_gemm_workspace_bytes(int T, int N, int K, int block_n, int splits);
+
+/* out[T, N] = bf16(x[T, K] . weight[N, K]^T), fp32 accumulation on tcgen05 CTA pairs. Replaces the F.linear
+ * calls of the decode step: OriginalGDN's wo (servers/sgl/src/zonos3_sgl/models/gdn.py:447), the attention layer's
+ * fused projection and wo (servers/sgl/src/zonos3_sgl/models/zonos3.py:326-390) and the multi-codebook head
+ * (zonos3.py:1341-1360). K a multiple of 128, N of 8; x / out row strides multiples of 8 elements. With more than one
+ * K slice, `workspace` (256-byte aligned, zb_proj_gemm_workspace_bytes) must start with its ticket bytes zeroed
+ * before the first launch; every launch leaves them zero. Launches sharing a workspace run in stream order. */
+int zb_proj_gemm(const uint16_t* x, int64_t x_stride, int T, int K, const uint16_t* weight, int N, uint16_t* out,
+                 int64_t out_stride, int block_n, int splits, void* workspace, int64_t workspace_bytes,
+                 cudaStream_t stream);
+
+/* The DeltaNet in_proj GEMM fused with its decode prologue: mixed = x . in_proj^T (in_proj [4*H*D + 2H, K]) is
+ * never stored; the GEMM's epilogue runs zb_gdn_prologue_decode's math on it (causal conv continuing conv_state row
+ * slots[t], which it shifts in place; SiLU; per-head L2 norm of q and k; g = -exp(A_log) * softplus(a + dt_bias),
+ * beta = sigmoid(b)) and stores z [T, H*D] for zb_gdn_gated_norm (z_stride = H*D). Same rounding points as the
+ * unfused in_proj + prologue. Replaces OriginalGDN's in_proj and prologue for a decode batch
+ * (servers/sgl/src/zonos3_sgl/models/gdn.py:399-434 through _forward_decode_static, :329-355). D = 64 or 128,
+ * H*D a multiple of 128, H <= 64; workspace as for zb_proj_gemm with N = 4*H*D + 2H and block_n = 128. */
+int zb_gdn_in_proj_decode(const uint16_t* x, int64_t x_stride, int T, int K, const uint16_t* in_proj,
+                          const uint16_t* conv_weight, const float* A_log, const float* dt_bias, const int64_t* slots,
+                          uint16_t* conv_state, int64_t conv_rows, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v,
+                          uint16_t* z, float* g, float* beta, int splits, void* workspace, int64_t workspace_bytes,
+                          cudaStream_t stream);
+
 /* ------------------------------------------------------------------------------------------- Full AttnRes */
 
 /* Full AttnRes route of every token over bank sources [0, S) plus, if `source` is non-NULL, `source` as the last

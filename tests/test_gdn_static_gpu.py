@@ -21,11 +21,14 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 
 
-@pytest.mark.parametrize("heads,head_dim", [(4, 128), (16, 128)])
-def test_static_graph_decode_matches_oracle(zb, heads, head_dim):
+@pytest.mark.parametrize("heads,head_dim,fused", [(4, 128, False), (16, 128, False), (4, 128, True),
+                                                 (16, 128, True)])
+def test_static_graph_decode_matches_oracle(zb, heads, head_dim, fused):
+    """fused: the decode rows run the fused in_proj + prologue kernel (OriginalGDN.fused_in_proj)."""
     hidden, capacity, bs, steps = 256, 8, 4, 8
     dev = torch.device("cuda")
     layer = fill_gdn(zb.gdn.OriginalGDN(gdn_config(zb, hidden, heads, head_dim), 0), seed=7 + heads)
+    layer.fused_in_proj = fused
     layer.to(dev, torch.bfloat16)
     layer.allocate_cache(capacity, dev, torch.bfloat16)
     w32 = {k: v.float().cpu() for k, v in layer.state_dict().items()}

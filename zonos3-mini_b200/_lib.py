@@ -43,6 +43,14 @@ SIGNATURES: dict[str, list] = {
     # mixed, mixed_stride, conv_weight, A_log, dt_bias, slots, conv_state, conv_rows, N, H, D, q, k, v, g, beta,
     # stream
     "zb_gdn_prologue_decode": [_p, _i64, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p],
+    # T, N, K, block_n, splits -> bytes (int64)
+    "zb_proj_gemm_workspace_bytes": [_i32, _i32, _i32, _i32, _i32],
+    # x, x_stride, T, K, weight, N, out, out_stride, block_n, splits, workspace, workspace_bytes, stream
+    "zb_proj_gemm": [_p, _i64, _i32, _i32, _p, _i32, _p, _i64, _i32, _i32, _p, _i64, _p],
+    # x, x_stride, T, K, in_proj, conv_weight, A_log, dt_bias, slots, conv_state, conv_rows, H, D, q, k, v, z, g,
+    # beta, splits, workspace, workspace_bytes, stream
+    "zb_gdn_in_proj_decode": [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p,
+                              _i32, _p, _i64, _p],
     # o, z, z_stride, weight, eps, N, H, D, out, stream
     "zb_gdn_gated_norm": [_p, _p, _i64, _p, _f32, _i32, _i32, _i32, _p, _p],
     # bank, bank_stride, S, source, append, query, eps, norm_weight, norm_eps, out, mix_out, T, D, stream
@@ -89,7 +97,7 @@ SIGNATURES: dict[str, list] = {
                       _i64, _p, _i64, _p, _i64, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None, "zb_launch_count": ctypes.c_uint64,
-             "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64}
+             "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64, "zb_proj_gemm_workspace_bytes": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -11,7 +11,7 @@ forward(x [N, D] bf16) reads ``get_global_ctx().batch.attn_metadata`` and ``get_
              o = zb_gqa_decode(q, cache, page_table, gate)  (tcgen05 decode attention, unsplit, the output gate
                                                              sigmoid(gate) applied in its store)
     prefill: the same prologue in torch, zb_kv_store, causal softmax attention per request in torch
-    y = (o * sigmoid(gate)) @ wo^T                          (prefill: the gate in torch)
+    y = (o * sigmoid(gate)) @ wo^T                          (cuBLAS; decode: the gate already applied)
 
 The prefill attention is plain torch: the north_star path is the decode step, and the reference runs its prefill
 attention through flash_attn_varlen_func (fa.py), a library kernel this package does not replace.
@@ -96,8 +96,8 @@ class Attention(BaseOP):
                 raise RuntimeError("Attention.prepare() must run before graph capture")
             self.prepare()
         n, H, Hkv, hd = x.shape[0], self.num_heads, self.num_kv_heads, self.head_dim
-        p = F.linear(x, self._proj)  # q | k | v | gate
         kc, vc = pool.k(self._layer_id), pool.v(self._layer_id)
+        p = F.linear(x, self._proj)  # q | k | v | gate
         gate = p[:, (H + 2 * Hkv) * hd:]
         if batch.is_decode:  # the output gate rides in the attention kernel's store
             q = ops.gqa_prologue_decode(p, self._temp, meta.positions, kc, vc, meta.out_loc, heads=H, kv_heads=Hkv,

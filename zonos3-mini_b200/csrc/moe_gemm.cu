@@ -30,12 +30,9 @@
 // and the rows past the last box are stale shared memory whose accumulator rows are padding rows of the segment. Work items are (expert, n-tile, m-tile) with the m-tile fastest, so the
 // pairs running at one time share weight tiles through L2. Every mbarrier wait is bounded (~1 s): on expiry the
 // kernel sets a status bit, stops issuing, drains (bounded), frees TMEM and returns.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 
-#include "common.cuh"
+#include "tc_pair.cuh"
 
 namespace {
 
@@ -79,129 +76,8 @@ struct GemmParams {
   unsigned* status;
 };
 
-// ------------------------------------------------------------------------------------------ PTX wrappers
-
-// Tensor load into this CTA's shared memory whose completed bytes count on `bar`, an mbarrier of either CTA of the
-// pair (here always the leader's). No multicast.
-template <bool PAIR>
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  if constexpr (PAIR) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-  } else {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-  }
-}
-
-// TMEM allocation (pair-wide: the same warp of both CTAs executes it; each CTA receives its base address).
-template <bool PAIR>
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  if constexpr (PAIR) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  } else {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-}
-
-template <bool PAIR>
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  if constexpr (PAIR) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-  } else {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-  }
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// MMA issued by one thread (of the leader CTA for a pair): D[M x N] from A and B in shared memory; for a pair over
-// both CTAs' TMEM from both CTAs' A and B halves at the same shared-memory offsets.
-template <bool PAIR>
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  if constexpr (PAIR) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-  } else {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-  }
-}
-
-// Arrives once on the mbarrier at offset `bar` (in each CTA of `mask`, for a pair) when every tcgen05.mma issued so
-// far by this thread has completed.
-template <bool PAIR>
-__device__ __forceinline__ void tc_commit(uint32_t bar, uint16_t mask) {
-  if constexpr (PAIR) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            bar),
-        "h"(mask)
-        : "memory");
-  } else {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-  }
-}
-
-// Plain arrival on an mbarrier of any CTA of the cluster (shared::cluster address).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
-}
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFF);          // start address
-  d |= (uint64_t)1 << 16;                          // leading byte offset (unused for swizzled K-major) = 16 B
-  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset: next 8-row group
-  d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 accumulator, M (256 for the pair, 128 for one
-// CTA), N = 256.
-template <int M>
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+using zb::tcp::mbar_arrive_cluster;
+using zb::tcp::tmem_ld32;
 
 // SiLU with the fast exponential and division: the product silu(gate) * up is rounded to bf16, where their
 // few-ulp fp32 error is far below the rounding step.
@@ -270,12 +146,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sh->item_start[p.E] = acc;
   }
-  if (warp == 1) tmem_alloc<PAIR>(zb::smem_addr(&sh->tmem_base), kTmemCols);
-  tc_fence_before();
+  if (warp == 1) zb::tcp::tmem_alloc<PAIR>(zb::smem_addr(&sh->tmem_base), kTmemCols);
+  zb::tcp::fence_before();
   __syncthreads();
   zb::cluster_arrive_relaxed();  // both CTAs' barriers are initialised before either signals the other's
   zb::cluster_wait();
-  tc_fence_after();
+  zb::tcp::fence_after();
   const uint32_t tmem_base = sh->tmem_base;
   const int total_items = sh->item_start[p.E];
   const int E = p.E;
@@ -320,13 +196,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t full_leader = PAIR ? zb::mapa_shared(full_local, 0) : full_local;
           const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
           if (a_boxes == 4) {
-            tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+            zb::tcp::tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
           } else {
             for (int j = 0; j < a_boxes; ++j)
-              tma_load_2d<PAIR>(a_dst + j * (A_BYTES / 4), &tmap_a32, kb * BK, a_row + 32 * j, full_leader);
+              zb::tcp::tma_load_2d<PAIR>(a_dst + j * (A_BYTES / 4), &tmap_a32, kb * BK, a_row + 32 * j,
+                                         full_leader);
           }
-          tma_load_2d<PAIR>(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
-          if (!PAIR) tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, &tmap_b, kb * BK, b_row2, full_leader);
+          zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
+          if (!PAIR)
+            zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, &tmap_b, kb * BK, b_row2, full_leader);
         }
       }
       if (leader) {  // drain: wait (bounded) for the copies still in flight before the CTA may exit
@@ -348,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        tc_fence_after();
+        zb::tcp::fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb, ++q) {
@@ -359,21 +237,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          zb::tcp::fence_after();
           const uint32_t a_addr = zb::smem_addr(stages + s * STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            tc_mma<PAIR>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
-                         kIdesc<ROWS>, (kb > 0 || kk > 0) ? 1u : 0u);
+            zb::tcp::mma<PAIR>(d_tmem, zb::tcp::desc_sw128(a_addr + kk * 32), zb::tcp::desc_sw128(b_addr + kk * 32),
+                               zb::tcp::idesc(ROWS, BN), (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit<PAIR>(zb::smem_addr(&sh->empty[s]), 0x3);  // stage s (of both CTAs of a pair) is free
+          zb::tcp::commit<PAIR>(zb::smem_addr(&sh->empty[s]), 0x3);  // stage s (of both CTAs of a pair) is free
         }
         if (!ok) break;
-        tc_commit<PAIR>(zb::smem_addr(&sh->tmem_full[acc]), 0x3);
+        zb::tcp::commit<PAIR>(zb::smem_addr(&sh->tmem_full[acc]), 0x3);
       }
       // every MMA issued by this thread has completed before TMEM is released
-      tc_commit<PAIR>(zb::smem_addr(&sh->drain), 0x1);
+      zb::tcp::commit<PAIR>(zb::smem_addr(&sh->drain), 0x1);
       zb::mbar_wait_bounded(zb::smem_addr(&sh->drain), 0, nullptr, 0, 200000000ull);
     }
   } else {
@@ -405,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         break;
       }
-      tc_fence_after();
+      zb::tcp::fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (MODE == kSwiGLU) {
         __nv_bfloat16* dst = p.out + row * p.out_stride + (int64_t)n * 128;
@@ -455,49 +333,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
       }
-      tc_fence_before();
+      zb::tcp::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(zb::mapa_shared(zb::smem_addr(&sh->tmem_empty[acc]), 0));
     }
   }
-  tc_fence_before();
+  zb::tcp::fence_before();
   __syncthreads();
   zb::cluster_arrive_relaxed();  // neither CTA frees TMEM or exits while the pair may still use it
   zb::cluster_wait();
   if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc<PAIR>(tmem_base, kTmemCols);
+    zb::tcp::fence_after();
+    zb::tcp::tmem_dealloc<PAIR>(tmem_base, kTmemCols);
   }
 }
 
 // ------------------------------------------------------------------------------------------ host side
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// 2-D bf16 row-major [rows, cols] tensor map with a [box_rows x 64 cols] box and 128-byte swizzle.
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
              uint32_t box_rows = 128) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return zb::fail(zb::kCudaError, "moe_gemm: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
-  cuuint32_t box[2] = {BK, box_rows};
-  cuuint32_t estride[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return zb::fail(zb::kCudaError, "moe_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return zb::kOk;
+  return zb::tcp::make_map(map, base, rows, cols, row_stride_elems, box_rows, "moe_gemm");
 }
 
 template <bool PAIR>

@@ -10,6 +10,11 @@ forward(x [N, D] bf16) reads ``get_global_ctx().batch`` like the reference. Per 
     gated = zb_gdn_gated_norm(o, z, out_weight)              (RMSNorm * SiLU(z))
     y = gated @ wo^T                                         (cuBLAS)
 
+``fused_in_proj = True`` (class or instance attribute) runs a decode batch's in_proj GEMM and prologue as one
+tcgen05 kernel instead (zb_gdn_in_proj_decode: the in_proj output never reaches global memory). It is off by
+default: on a B200 at the 256-stream decode shape the cuBLAS GEMM plus the prologue kernel take 18.8 us per layer
+and the fused kernel 31 us (its GEMM alone runs 13.7 us against cuBLAS's 9.7 us).
+
 State is exact per request: the recurrence is the reference oracle's per-token update (lm.py:576-582), so a
 decode step costs one state read + write instead of the server's 64-row window replay (gdn.py:329-355). The
 state pool is V-first fp32 [capacity, H, dv, dk] (LMCache.gdn_state's layout) and the conv history is
@@ -98,6 +103,7 @@ class PrefillInputs:
 
 class OriginalGDN(BaseOP):
     _fp32 = ("A_log", "dt_bias")
+    fused_in_proj = False  # decode: zb_gdn_in_proj_decode instead of cuBLAS in_proj + prologue (module docstring)
 
     def __init__(self, config, layer_id: int):
         H, d = getattr(config, "gdn_num_heads", 4), getattr(config, "gdn_head_dim", 128)
@@ -247,9 +253,19 @@ class OriginalGDN(BaseOP):
         gated = ops.gdn_gated_norm(o, mixed[:, 3 * inner:4 * inner], self.out_weight, 1e-5)
         return F.linear(gated, self.wo.weight)
 
+    def _fused_decode(self, x) -> bool:
+        """Whether a decode batch runs the fused in_proj + prologue kernel (opt-in; the shapes it takes)."""
+        H, d = self._heads, self._head_dim
+        return self.fused_in_proj and x.shape[1] % 128 == 0 and (H * d) % 128 == 0 and d in (64, 128) and H <= 64
+
     def _run(self, x, cu, seq_of_token, slots, fresh, *, decode: bool, any_fresh: bool):
         H, d = self._heads, self._head_dim
         inner = H * d
+        if decode and not any_fresh and self._fused_decode(x):
+            q, k, v, z, g, beta = ops.gdn_in_proj_decode(x, self.in_proj.weight, self.conv.weight, self.A_log,
+                                                         self.dt_bias, slots, self._conv_state, heads=H, head_dim=d)
+            o = ops.gdn_decode_step(q, k, v, g, beta, self._recurrent_state, slots=slots)
+            return F.linear(ops.gdn_gated_norm(o, z, self.out_weight, 1e-5), self.wo.weight)
         mixed = F.linear(x, self.in_proj.weight)
         if decode and not any_fresh:  # one token per request: the history update rides in the prologue kernel
             q, k, v, g, beta = ops.gdn_prologue_decode(mixed, self.conv.weight, self.A_log, self.dt_bias, slots,

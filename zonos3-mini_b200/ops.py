@@ -625,6 +625,108 @@ def gdn_gated_norm(o, z, weight, eps=1e-5, out=None):
     return out
 
 
+# ----------------------------------------------------------------------------- dense projections (tcgen05)
+
+_PROJ_WS: dict = {}  # device -> the current split-K workspace (uint8, ticket counters zero between launches)
+_PROJ_WS_RETIRED: list = []  # replaced workspaces stay alive: a captured graph may still hold their address
+
+
+def _proj_workspace(dev: torch.device, nbytes: int) -> torch.Tensor | None:
+    """The device's split-K workspace, grown (zeroed) when a launch needs more; launches use it in stream order."""
+    if nbytes <= 0:
+        return None
+    ws = _PROJ_WS.get(dev)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the projection GEMM's workspace must be sized before graph capture: run the step "
+                               "once eagerly (a warm-up) before capturing it")
+        if ws is not None:
+            _PROJ_WS_RETIRED.append(ws)
+        ws = torch.zeros(nbytes, device=dev, dtype=torch.uint8)
+        _PROJ_WS[dev] = ws
+    return ws
+
+
+def _proj_rows(name: str, x: torch.Tensor, K: int) -> int:
+    _check_cuda(name, x, torch.bfloat16)
+    _require(x.dim() == 2 and x.shape[1] == K and x.stride(1) == 1, f"{name} must be [T, {K}] with contiguous rows")
+    stride = x.stride(0) if x.shape[0] > 1 else K
+    _require(stride % 8 == 0 and x.data_ptr() % 16 == 0, f"{name}: rows must start on 16-byte boundaries")
+    return stride
+
+
+def proj_gemm(x, weight, out=None, *, block_n: int = 0, splits: int = 0):
+    """out = x @ weight^T on the tensor cores (tcgen05 CTA pairs, fp32 accumulation, one bf16 rounding): the decode
+    step's dense projections (F.linear of the DeltaNet / attention wo, the attention projection and the codebook
+    head; gdn.py:447, zonos3.py:326-390, :1341-1360). x [T, K] bf16, weight [N, K] bf16 contiguous, out [T, N] bf16
+    (a row stride allowed). ``block_n`` (64 / 128 / 256) and ``splits`` (K slices) pick the tiling; 0 = chosen from
+    the shape. K must be a multiple of 128 and N of 8."""
+    _check_cuda("weight", weight, torch.bfloat16)
+    dev = weight.device
+    _require(weight.dim() == 2 and weight.is_contiguous(), "weight must be a contiguous [N, K] tensor")
+    N, K = weight.shape
+    xs = _proj_rows("x", x, K)
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+    _check_cuda("out", out, torch.bfloat16, dev)
+    _require(out.dim() == 2 and out.shape == (T, N) and out.stride(1) == 1, f"out must be [{T}, {N}] with contiguous rows")
+    os_ = out.stride(0) if T > 1 else N
+    lib = _lib.load()
+    nbytes = int(lib.zb_proj_gemm_workspace_bytes(T, N, K, int(block_n), int(splits))) if T else 0
+    ws = _proj_workspace(dev, nbytes)
+    _lib.call("zb_proj_gemm", x.data_ptr(), xs, T, K, weight.data_ptr(), N, out.data_ptr(), os_, int(block_n),
+              int(splits), None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(dev))
+    return out
+
+
+def gdn_in_proj_decode(x, in_proj, conv_weight, A_log, dt_bias, slots, conv_state, *, heads, head_dim,
+                       splits: int = 0, q=None, k=None, v=None, z=None, g=None, beta=None):
+    """The DeltaNet in_proj GEMM fused with its decode prologue (gdn.py:399-434): row i of x is the new token of the
+    request whose conv history is row ``slots[i]`` of conv_state (outside [0, rows): a padding row, zero history,
+    nothing written). The in_proj output is never stored: the GEMM's epilogue runs the causal conv (shifting the
+    history in place), SiLU, the per-head L2 norm of q and k, g and beta, and stores z for the gated norm.
+    Returns (q, k, v [T, H, d] bf16, z [T, H*d] bf16, g, beta [T, H] fp32)."""
+    _check_cuda("in_proj", in_proj, torch.bfloat16)
+    dev = in_proj.device
+    H, D = heads, head_dim
+    inner = H * D
+    N, K = in_proj.shape
+    _require(N == 4 * inner + 2 * H and in_proj.is_contiguous(), f"in_proj must be a contiguous [{4 * inner + 2 * H}, K] tensor")
+    xs = _proj_rows("x", x, K)
+    T = x.shape[0]
+    _check_cuda("conv_weight", conv_weight, torch.bfloat16, dev)
+    _require(conv_weight.numel() == 3 * inner * 4 and conv_weight.is_contiguous(), "conv_weight must be [3*inner, 1, 4]")
+    _check_cuda("conv_state", conv_state, torch.bfloat16, dev)
+    _require(conv_state.dim() == 3 and conv_state.shape[1:] == (3 * inner, 3) and conv_state.is_contiguous(),
+             "conv_state must be a contiguous [rows, 3*inner, 3] tensor")
+    for name, t in (("A_log", A_log), ("dt_bias", dt_bias)):
+        _check_cuda(name, t, torch.float32, dev)
+    _check_cuda("slots", slots, torch.int64, dev)
+    _require(slots.numel() == T and slots.is_contiguous(), f"slots must hold one row per token ({T})")
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    q = torch.empty(T, H, D, **bf) if q is None else q
+    k = torch.empty(T, H, D, **bf) if k is None else k
+    v = torch.empty(T, H, D, **bf) if v is None else v
+    z = torch.empty(T, inner, **bf) if z is None else z
+    g = torch.empty(T, H, device=dev, dtype=torch.float32) if g is None else g
+    beta = torch.empty(T, H, device=dev, dtype=torch.float32) if beta is None else beta
+    for name, t in (("q", q), ("k", k), ("v", v), ("z", z)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+        _require(t.is_contiguous() and t.numel() == T * inner, f"{name} must be a contiguous [T, {inner}] buffer")
+    for name, t in (("g", g), ("beta", beta)):
+        _check_cuda(name, t, torch.float32, dev)
+        _require(t.is_contiguous() and t.numel() == T * H, f"{name} must be a contiguous [T, {H}] buffer")
+    lib = _lib.load()
+    nbytes = int(lib.zb_proj_gemm_workspace_bytes(T, N, K, 128, int(splits))) if T else 0  # its column tile
+    ws = _proj_workspace(dev, nbytes)
+    _lib.call("zb_gdn_in_proj_decode", x.data_ptr(), xs, T, K, in_proj.data_ptr(), conv_weight.data_ptr(),
+              A_log.data_ptr(), dt_bias.data_ptr(), slots.data_ptr(), conv_state.data_ptr(), conv_state.shape[0], H, D,
+              q.data_ptr(), k.data_ptr(), v.data_ptr(), z.data_ptr(), g.data_ptr(), beta.data_ptr(), int(splits),
+              None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(dev))
+    return q, k, v, z, g, beta
+
+
 # ------------------------------------------------------------------------------------- GQA decode attention
 
 
