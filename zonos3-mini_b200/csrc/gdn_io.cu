@@ -11,7 +11,8 @@
 // (the layout of LMCache.conv_state); a second small kernel then writes each sequence's new history (its last W-1
 // inputs), after every token has read the old one. Decode (one token per sequence, zb_gdn_prologue_decode): the CTA
 // that reads a sequence's history rows of its channels is their only reader, so it writes the shifted history
-// (the last W-2 entries and the token's input) itself and the second kernel is not launched.
+// (the last W-2 entries and the token's input) itself and the second kernel is not launched; for D = 64 / 128 it runs
+// gdn_prologue_decode8_kernel, 8 channels (16-byte vectors) per thread, so the step's 256 x 3 CTAs are one wave.
 //
 // Epilogue (replaces FLA layer_norm_gated_fwd, gdn.py:435-445; lm.py:585-587): gated = RMSNorm(o; out_weight,
 // 1e-5) * SiLU(z) per head, computed in fp32 and rounded once to bf16; one warp per (token, head).
@@ -181,6 +182,79 @@ __global__ void __launch_bounds__(1024) gdn_prologue_kernel(PrologueParams p) {
   }
 }
 
+// The decode prologue with 8 channels per thread: every input of a thread is one to four 16-byte loads (taps,
+// history, the token's in_proj row) issued together, and a (token, part) CTA of inner / 8 threads fits the whole
+// 256-stream step in one wave. A head's D channels are D / 8 consecutive lanes, so its L2 norm is a shuffle
+// reduction over that lane group. Same arithmetic per channel as gdn_prologue_kernel (taps oldest first).
+template <int D>
+__global__ void __launch_bounds__(1024) gdn_prologue_decode8_kernel(PrologueParams p) {
+  zb::pdl_enter();
+  constexpr int kLanesPerHead = D / 8;
+  const int64_t tok = blockIdx.x;
+  const int part = blockIdx.y;
+  const int inner = p.H * D;
+  const int c0 = threadIdx.x * 8;     // channel inside the part
+  const int ch0 = part * inner + c0;  // conv channel
+  const int64_t slot = p.slots[tok];
+  const bool padding = slot < 0 || slot >= p.rows;  // graph padding row: zero history, never written
+  uint4 wq[4], hq[3];
+  const uint4* wp = reinterpret_cast<const uint4*>(p.conv_w + (int64_t)ch0 * kW);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) wq[u] = __ldg(wp + u);
+  uint4* hp = reinterpret_cast<uint4*>(p.conv_state + ((padding ? 0 : slot) * 3 * inner + ch0) * (kW - 1));
+  if (!padding) {
+#pragma unroll
+    for (int u = 0; u < 3; ++u) hq[u] = hp[u];
+  } else {
+#pragma unroll
+    for (int u = 0; u < 3; ++u) hq[u] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  const uint4 xq = *reinterpret_cast<const uint4*>(p.mixed + tok * p.mixed_stride + ch0);
+  const __nv_bfloat16* wt = reinterpret_cast<const __nv_bfloat16*>(wq);  // [8 channels][W]
+  const __nv_bfloat16* hist = reinterpret_cast<const __nv_bfloat16*>(hq);  // [8 channels][W-1]
+  const __nv_bfloat16* xin = reinterpret_cast<const __nv_bfloat16*>(&xq);
+  float acc[8];
+  float ss = 0.f;
+  uint4 nq[3];
+  __nv_bfloat16* nh = reinterpret_cast<__nv_bfloat16*>(nq);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kW - 1; ++w)
+      a = fmaf(__bfloat162float(wt[j * kW + w]), __bfloat162float(hist[j * (kW - 1) + w]), a);
+    a = fmaf(__bfloat162float(wt[j * kW + kW - 1]), __bfloat162float(xin[j]), a);
+    acc[j] = zb::bf16_round(silu(a));  // the conv output is an activation of the model dtype
+    ss = fmaf(acc[j], acc[j], ss);
+#pragma unroll
+    for (int e = 0; e < kW - 2; ++e) nh[j * (kW - 1) + e] = hist[j * (kW - 1) + e + 1];
+    nh[j * (kW - 1) + kW - 2] = xin[j];
+  }
+  if (!padding) {
+#pragma unroll
+    for (int u = 0; u < 3; ++u) hp[u] = nq[u];
+  }
+  float scale = 1.f;
+  if (part < 2) {
+#pragma unroll
+    for (int off = kLanesPerHead / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    scale = rsqrtf(ss + 1e-6f);
+  }
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = acc[j] * scale;
+  __nv_bfloat16* dst = (part == 0 ? p.q : part == 1 ? p.k : p.v) + tok * inner + c0;
+  *reinterpret_cast<uint4*>(dst) = zb::pack_bf16x8(o);
+  if (part == 0 && threadIdx.x < p.H) {
+    const int hh = threadIdx.x;
+    const __nv_bfloat16* row = p.mixed + tok * p.mixed_stride;
+    const float av = __bfloat162float(row[4 * inner + hh]);
+    const float bv = __bfloat162float(row[4 * inner + p.H + hh]);
+    p.g[tok * p.H + hh] = -expf(p.A_log[hh]) * softplus(av + p.dt_bias[hh]);
+    p.beta[tok * p.H + hh] = 1.f / (1.f + expf(-bv));
+  }
+}
+
 // New history of every sequence: its last W-1 conv inputs (shifted in after the old history when it is shorter).
 // Grid (sequence, channel block): a thread owns 8 consecutive channels (24 history entries, 48 contiguous bytes).
 __global__ void __launch_bounds__(256) gdn_conv_history_kernel(PrologueParams p) {
@@ -337,6 +411,16 @@ ZB_API int zb_gdn_prologue_decode(const uint16_t* mixed, int64_t mixed_stride, c
                    reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k),
                    reinterpret_cast<__nv_bfloat16*>(v), g, beta, N, H, D};
   const dim3 grid((unsigned)N, 3);
+  const int inner = H * D;
+  if ((D == 64 || D == 128) && inner % 256 == 0 && inner <= 8192 && mixed_stride % 8 == 0) {
+    // 8 channels per thread, one wave (mixed rows 16-byte aligned: the row stride a multiple of 8)
+    const unsigned threads8 = (unsigned)(inner / 8);
+    if (D == 64)
+      ZB_CUDA(zb::launch(gdn_prologue_decode8_kernel<64>, grid, dim3(threads8), 0, stream, 1, p));
+    else
+      ZB_CUDA(zb::launch(gdn_prologue_decode8_kernel<128>, grid, dim3(threads8), 0, stream, 1, p));
+    return zb::check_launch("gdn_prologue_decode");
+  }
   const unsigned threads = 32u * (unsigned)H;
   switch (D / 32) {
     case 1: ZB_CUDA(zb::launch(gdn_prologue_kernel<1, true>, dim3(grid), dim3(threads), 0, stream, 1, p)); break;
