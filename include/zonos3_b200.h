@@ -236,6 +236,17 @@ int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t* down, 
                      const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs, const float* weights,
                      uint16_t* y, cudaStream_t stream);
 
+/* Both expert GEMMs (zb_moe_gemm_swiglu, then zb_moe_gemm_down on its h) in one call. At decode sizes (the
+ * single-CTA shape) they run as one persistent launch: a down tile of expert e starts as soon as every SwiGLU tile of
+ * e has stored its h rows, so the SwiGLU GEMM's last partial wave overlaps the down GEMM. flags [E + 1] uint32 are
+ * those per-expert counters: zero before the first call, left zero by every call (a bounded wait that expired, status
+ * bit 2, may leave them non-zero: re-zero them then). Larger batches make the two pair-shape launches. The grid never
+ * exceeds the CTAs the GPU holds at once, which the counters rely on. Replaces both fused_moe_kernel calls of
+ * fused_experts_impl (fused_moe_impl.py:218-259). D % 128 == 0, I % 128 == 0. */
+int zb_moe_gemms(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, const uint16_t* down, int E,
+                 int D, int I, const int32_t* offsets, const int32_t* counts, const int32_t* sorted_pairs,
+                 const float* weights, uint16_t* h, uint16_t* y, uint32_t* flags, cudaStream_t stream);
+
 /* out[t, :] = bf16(sum over slots s of float(y[t*k + s, :])): the un-permute combine (the add / moe_sum_reduce of
  * fused_experts_impl, fused_moe_impl.py:267-288). out has row stride out_stride. */
 int zb_moe_combine(const uint16_t* y, int T, int k, int D, uint16_t* out, int64_t out_stride, cudaStream_t stream);

@@ -228,3 +228,42 @@ def test_router_ids_from_x(zb, T, mode, renorm, bias_scale):
     print(report)
     assert not bad_sel.any() and order.all(), report
     assert mismatch.float().mean().item() < 0.02, report
+
+
+@pytest.mark.parametrize("T,D,E,k,I,skew", [(256, 2048, 64, 8, 768, False), (256, 1024, 16, 4, 256, True),
+                                            (1, 256, 8, 2, 128, False)])
+def test_fused_decode_gemms_match_the_two_launches(zb, T, D, E, k, I, skew):
+    """zb_moe_gemms at decode sizes (one persistent launch: the down tiles of an expert wait for its SwiGLU tiles'
+    counters) against the two separate launches on the same permutation: h and y bit-identical (same tiles, same
+    accumulation order), on three consecutive calls (the counters must return to zero), with a skewed routing that
+    gives some experts two 128-row tiles."""
+    ops = zb.ops
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(T + E)
+    x = torch.randn(T, D, generator=gen).bfloat16().to(dev)
+    if skew:
+        ids = torch.stack([torch.randperm(E, generator=gen)[:k] if t % 2 else torch.arange(k) for t in range(T)])
+    else:
+        ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)])
+    ids = ids.to(torch.int32).to(dev)
+    w = torch.softmax(torch.randn(T, k, generator=gen), -1).to(dev)
+    gate_up, down = expert_weights(E, D, I, seed=T + 1)
+    gate_up, down = gate_up.to(dev), down.to(dev)
+    ws = ops.MoEWorkspace(T, k, E, D, I, dev)
+    perm = ops.moe_permute(ids, E, capacity=ws.capacity, out=ws.perm)
+    ops.moe_gather(x, perm["sorted_pairs"], k, ws.x_perm)
+    h_ref = torch.zeros_like(ws.h)
+    y_ref = torch.zeros_like(ws.y)
+    ops.moe_gemm_swiglu(ws.x_perm, gate_up, perm["offsets"], h_ref, counts=perm["counts"])
+    ops.moe_gemm_down(h_ref, down, perm["offsets"], perm["sorted_pairs"], w, y_ref, counts=perm["counts"])
+    valid = perm["sorted_pairs"] >= 0
+    for _ in range(3):
+        ws.h.zero_()
+        ws.y.zero_()
+        ops.moe_gemms(ws.x_perm, gate_up, down, perm["offsets"], perm["sorted_pairs"], w, ws.h, ws.y, ws.flags,
+                      counts=perm["counts"])
+        torch.cuda.synchronize()
+        assert torch.equal(ws.h[valid], h_ref[valid])
+        assert torch.equal(ws.y, y_ref)
+        assert int(ws.flags.abs().sum().item()) == 0, "the per-expert counters must return to zero"
+    assert ops.device_status() == 0

@@ -56,7 +56,9 @@ constexpr int kMaxStages = 6;
 constexpr int kTmemCols = 512;
 constexpr int kMaxExperts = 128;
 
-enum Mode : int { kSwiGLU = 0, kDown = 1 };
+// kFused: the SwiGLU GEMM (phase 0) and the down GEMM (phase 1) in one persistent launch of the single-CTA shape;
+// a down tile of expert e starts once every SwiGLU tile of e has published its H columns (per-expert counters).
+enum Mode : int { kSwiGLU = 0, kDown = 1, kFused = 2 };
 
 struct GemmParams {
   const int32_t* offsets;  // [E + 1] padded row offsets (multiples of BM)
@@ -74,7 +76,31 @@ struct GemmParams {
   const float* weights;         // GEMM2: [pairs]
   int64_t pair_limit;           // GEMM2: pairs >= this are dropped (the rows of `out`)
   unsigned* status;
+  // kFused: the down GEMM's geometry (phase 1); the fields above describe the SwiGLU GEMM (phase 0)
+  int K1, n_tiles1;
+  int64_t b_rows1;
+  int b_second1, b_step1;
+  __nv_bfloat16* out1;
+  int64_t out_stride1;
+  int out_cols1;
+  unsigned* flags;  // [E + 1]: per expert, SwiGLU epilogue warps done; [E]: CTAs done (zero between launches)
 };
+
+// The geometry of one phase's work items.
+struct Phase {
+  int mode, K, n_tiles;
+  int64_t b_rows;
+  int b_second, b_step;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int out_cols;
+};
+__device__ __forceinline__ Phase phase_of(const GemmParams& p, int MODE, int ph) {
+  if (MODE == kFused && ph == 1)
+    return Phase{kDown, p.K1, p.n_tiles1, p.b_rows1, p.b_second1, p.b_step1, p.out1, p.out_stride1, p.out_cols1};
+  return Phase{MODE == kFused ? (int)kSwiGLU : MODE, p.K, p.n_tiles, p.b_rows_per_expert, p.b_second_offset,
+               p.b_tile_step, p.out, p.out_stride, p.out_cols};
+}
 
 using zb::tcp::mbar_arrive_cluster;
 using zb::tcp::tmem_ld32;
@@ -92,15 +118,33 @@ struct Shared {
   uint32_t tmem_base;
   int abort;
   int item_start[kMaxExperts + 1];  // first work item of each expert (pair tiles x n-tiles)
+  int item_start1[kMaxExperts + 1]; // kFused: the same for the down GEMM's items (after all SwiGLU items)
   int row_off[kMaxExperts + 1];     // padded row offsets
   int count[kMaxExperts];           // routed rows (counts, or the padded sizes)
 };
 constexpr uint32_t kSharedBytes = (sizeof(Shared) + 127) / 128 * 128;
 
+// Waits until *counter >= target (acquire), for at most ~1 s; on expiry records kStatusGemmTimeout and returns false.
+__device__ bool wait_counter(const unsigned* counter, unsigned target, unsigned* status) {
+  const uint64_t start = zb::globaltimer_ns();
+  for (;;) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    if (v >= target) return true;
+    if (zb::globaltimer_ns() - start > 1000000000ull) {
+      if (status) atomicOr(status, zb::kStatusGemmTimeout);
+      return false;
+    }
+    __nanosleep(128);
+  }
+}
+
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a32,
-                    const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_a1,
+                    const __grid_constant__ CUtensorMap tmap_a1_32, const __grid_constant__ CUtensorMap tmap_b1,
+                    GemmParams p) {
   zb::pdl_enter();
   using Sh = Shape<PAIR>;
   constexpr int STAGES = Sh::STAGES, CTAS = Sh::CTAS, ROWS = Sh::ROWS;
@@ -145,6 +189,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc += (m128 + CTAS - 1) / CTAS * p.n_tiles;
     }
     sh->item_start[p.E] = acc;
+    if (MODE == kFused) {
+      for (int e = 0; e < p.E; ++e) {
+        sh->item_start1[e] = acc;
+        acc += (sh->row_off[e + 1] - sh->row_off[e]) / BM * p.n_tiles1;
+      }
+      sh->item_start1[p.E] = acc;
+    }
   }
   if (warp == 1) zb::tcp::tmem_alloc<PAIR>(zb::smem_addr(&sh->tmem_base), kTmemCols);
   zb::tcp::fence_before();
@@ -153,21 +204,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   zb::cluster_wait();
   zb::tcp::fence_after();
   const uint32_t tmem_base = sh->tmem_base;
-  const int total_items = sh->item_start[p.E];
   const int E = p.E;
-  const int k_blocks = p.K / BK;
+  const int items0 = sh->item_start[E];
+  const int total_items = MODE == kFused ? sh->item_start1[E] : items0;
 
-  // item -> (expert, n-tile, first row of the 256-row pair tile)
-  auto decode = [&](int item, int& e, int& n, int& row0) {
-    int lo = 0, hi = E;  // largest e with item_start[e] <= item
+  // item -> (phase, expert, n-tile, first row of the 256-row pair tile)
+  auto decode = [&](int item, int& ph, int& e, int& n, int& row0) {
+    ph = (MODE == kFused && item >= items0) ? 1 : 0;
+    const int* starts = ph ? sh->item_start1 : sh->item_start;
+    const int ntl = ph ? p.n_tiles1 : p.n_tiles;
+    int lo = 0, hi = E;  // largest e with starts[e] <= item
     while (hi - lo > 1) {
       const int mid = (lo + hi) / 2;
-      if (sh->item_start[mid] <= item) lo = mid; else hi = mid;
+      if (starts[mid] <= item) lo = mid; else hi = mid;
     }
     e = lo;
-    while (e + 1 < E && sh->item_start[e + 1] <= item) ++e;  // skip experts without tiles
-    const int m_tiles = (sh->item_start[e + 1] - sh->item_start[e]) / p.n_tiles;
-    const int local = item - sh->item_start[e];
+    while (e + 1 < E && starts[e + 1] <= item) ++e;  // skip experts without tiles
+    const int m_tiles = (starts[e + 1] - starts[e]) / ntl;
+    const int local = item - starts[e];
     n = local / m_tiles;
     row0 = sh->row_off[e] + (local % m_tiles) * ROWS;
   };
@@ -176,11 +230,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // producer of this CTA's halves; bytes complete on the leader's full barrier
       uint32_t q = 0;
       for (int item = pair; item < total_items && !*abort_flag; item += npairs) {
-        int e, n, row0;
-        decode(item, e, n, row0);
+        int ph, e, n, row0;
+        decode(item, ph, e, n, row0);
+        const Phase g = phase_of(p, MODE, ph);
+        const CUtensorMap* ma = ph ? &tmap_a1 : &tmap_a;
+        const CUtensorMap* ma32 = ph ? &tmap_a1_32 : &tmap_a32;
+        const CUtensorMap* mb = ph ? &tmap_b1 : &tmap_b;
+        const int k_blocks = g.K / BK;
         const int a_row = row0 + (int)rank * BM;
-        const int b_row = (int)(e * p.b_rows_per_expert) + n * p.b_tile_step + (rank ? p.b_second_offset : 0);
-        const int b_row2 = b_row + p.b_second_offset;  // the second B box (one CTA only)
+        const int b_row = (int)(e * g.b_rows) + n * g.b_step + (rank ? g.b_second : 0);
+        const int b_row2 = b_row + g.b_second;  // the second B box (one CTA only)
+        if (MODE == kFused && ph == 1) {
+          // the down tile reads H rows of expert e: wait (bounded) until every SwiGLU tile of e has published them
+          const unsigned target = (unsigned)(kEpilogueWarps * p.n_tiles * ((sh->row_off[e + 1] - sh->row_off[e]) / BM));
+          if (!wait_counter(p.flags + e, target, p.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // the tensor loads below see those rows
+        }
         // single CTA: 32-row A boxes covering the tile's routed rows (>= 1 for every tile of a segment)
         const int a_boxes = PAIR ? 4 : (min(max(sh->count[e] - (row0 - sh->row_off[e]), 0), BM) + 31) / 32;
         const uint32_t tx_bytes = CTAS * STAGE_BYTES - (uint32_t)(4 - a_boxes) * (A_BYTES / 4);
@@ -196,15 +264,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t full_leader = PAIR ? zb::mapa_shared(full_local, 0) : full_local;
           const uint32_t a_dst = zb::smem_addr(stages + s * STAGE_BYTES);
           if (a_boxes == 4) {
-            zb::tcp::tma_load_2d<PAIR>(a_dst, &tmap_a, kb * BK, a_row, full_leader);
+            zb::tcp::tma_load_2d<PAIR>(a_dst, ma, kb * BK, a_row, full_leader);
           } else {
             for (int j = 0; j < a_boxes; ++j)
-              zb::tcp::tma_load_2d<PAIR>(a_dst + j * (A_BYTES / 4), &tmap_a32, kb * BK, a_row + 32 * j,
-                                         full_leader);
+              zb::tcp::tma_load_2d<PAIR>(a_dst + j * (A_BYTES / 4), ma32, kb * BK, a_row + 32 * j, full_leader);
           }
-          zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES, &tmap_b, kb * BK, b_row, full_leader);
-          if (!PAIR)
-            zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, &tmap_b, kb * BK, b_row2, full_leader);
+          zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES, mb, kb * BK, b_row, full_leader);
+          if (!PAIR) zb::tcp::tma_load_2d<PAIR>(a_dst + A_BYTES + BOX_BYTES, mb, kb * BK, b_row2, full_leader);
         }
       }
       if (leader) {  // drain: wait (bounded) for the copies still in flight before the CTA may exit
@@ -228,6 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         zb::tcp::fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        int ph, e_, n_, row0_;
+        decode(item, ph, e_, n_, row0_);
+        const int k_blocks = phase_of(p, MODE, ph).K / BK;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb, ++q) {
           const int s = q % STAGES;
@@ -265,13 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t use = it >> 1;
       // the tile's rows (and, for the down projection, their pairs and routing weights) are looked up while the
       // MMAs still run
-      int e, n, row0;
-      decode(item, e, n, row0);
+      int ph, e, n, row0;
+      decode(item, ph, e, n, row0);
+      const Phase g = phase_of(p, MODE, ph);
       const int64_t row = row0 + row_in_tile;
       const bool valid = row < sh->row_off[e + 1];  // rows past the expert's group belong to the next expert
       int pr = -1;
       float w = 0.f;
-      if (MODE == kDown) {
+      if (g.mode == kDown) {
         pr = valid ? p.sorted_pairs[row] : -1;
         if (pr >= p.pair_limit) pr = -1;  // never write past the rows of `out`
         w = pr >= 0 ? p.weights[pr] : 0.f;
@@ -285,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       zb::tcp::fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if (MODE == kSwiGLU) {
-        __nv_bfloat16* dst = p.out + row * p.out_stride + (int64_t)n * 128;
+      if (g.mode == kSwiGLU) {
+        __nv_bfloat16* dst = g.out + row * g.out_stride + (int64_t)n * 128;
 #pragma unroll 1
         for (int c = chalf * 64; c < chalf * 64 + 64; c += 32) {
           float gate[32], up[32];
@@ -303,6 +373,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        if (MODE == kFused) {  // publish this warp's H columns of expert e to the down tiles (release)
+          __threadfence();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.flags + e) : "memory");
+        }
       } else {
         // rows go to scattered pair slots: each 32-column chunk of the warp's 32 rows is staged in shared memory
         // (16-byte units swizzled by row so that neither the row-wise writes nor the column-wise reads conflict)
@@ -310,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         unsigned char* stg = out_stage + (warp - 2) * kStageOutBytes;
         const int sub = lane & 3, rsub = lane >> 2;
 #pragma unroll 1
-        for (int c = chalf * (BN / 2); c < chalf * (BN / 2) + BN / 2 && n * BN + c < p.out_cols; c += 32) {
+        for (int c = chalf * (BN / 2); c < chalf * (BN / 2) + BN / 2 && n * BN + c < g.out_cols; c += 32) {
           float y[32];
           tmem_ld32(t_row + c, y);
 #pragma unroll
@@ -328,7 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rp = __shfl_sync(0xffffffffu, pr, r);
             const int unit = 4 * (r & 1) + (sub ^ ((r >> 1) & 3));
             const uint4 v = *reinterpret_cast<const uint4*>(stg + (r >> 1) * 128 + unit * 16);
-            if (rp >= 0) *reinterpret_cast<uint4*>(p.out + (int64_t)rp * p.out_stride + (int64_t)n * BN + c + 8 * sub) = v;
+            if (rp >= 0)
+              *reinterpret_cast<uint4*>(g.out + (int64_t)rp * g.out_stride + (int64_t)n * BN + c + 8 * sub) = v;
           }
           __syncwarp();
         }
@@ -345,6 +422,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     zb::tcp::fence_after();
     zb::tcp::tmem_dealloc<PAIR>(tmem_base, kTmemCols);
+  }
+  if (MODE == kFused && tid == 0) {  // the last CTA to finish zeroes the counters for the next launch
+    __threadfence();
+    if (atomicAdd(p.flags + E, 1u) == gridDim.x - 1)
+      for (int e = 0; e <= E; ++e) reinterpret_cast<volatile unsigned*>(p.flags)[e] = 0u;
   }
 }
 
@@ -367,9 +449,13 @@ bool use_pair(int64_t capacity, int E) {
   return routed > (int64_t)E * 96;
 }
 
+// The tensor maps of a launch: A (128- and 32-row boxes) and B of the GEMM, and for kFused those of the down GEMM.
+struct Maps {
+  CUtensorMap a, a32, b, a1, a1_32, b1;
+};
+
 template <int MODE, bool PAIR>
-int launch(const CUtensorMap& a, const CUtensorMap& a32, const CUtensorMap& b, const GemmParams& p,
-           int64_t capacity, cudaStream_t stream) {
+int launch(const Maps& m, const GemmParams& p, int64_t capacity, cudaStream_t stream) {
   auto kernel = moe_gemm_kernel<MODE, PAIR>;
   constexpr size_t kSmemBytes = smem_bytes<PAIR>();
   static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
@@ -407,13 +493,15 @@ int launch(const CUtensorMap& a, const CUtensorMap& a32, const CUtensorMap& b, c
     if (max_units < 1) return zb::fail(zb::kUnsupported, "moe_gemm: no CTA (pair) fits on this GPU");
     if (dev >= 0 && dev < 64) resident[dev] = max_units;
   }
-  // tiles: at most capacity / tile rows plus one per expert
-  const int64_t upper_items = (capacity / Shape<PAIR>::ROWS + p.E) * p.n_tiles;
+  // tiles: at most capacity / tile rows plus one per expert (kFused: of both GEMMs). kFused waits on other CTAs'
+  // tiles, so it relies on every CTA of the grid being resident at once (the grid never exceeds max_units).
+  const int64_t upper_items =
+      (capacity / Shape<PAIR>::ROWS + p.E) * (p.n_tiles + (MODE == kFused ? p.n_tiles1 : 0));
   const int units = (int)std::min<int64_t>(upper_items, max_units);
   if (units <= 0) return zb::kOk;
   ZB_CUDA(zb::launch(kernel, dim3((unsigned)(Shape<PAIR>::CTAS * units)), dim3(kThreads), kSmemBytes, stream,
-                     (unsigned)Shape<PAIR>::CTAS, a, a32, b, p));
-  return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : "moe_gemm_down");
+                     (unsigned)Shape<PAIR>::CTAS, m.a, m.a32, m.b, m.a1, m.a1_32, m.b1, p));
+  return zb::check_launch(MODE == kSwiGLU ? "moe_gemm_swiglu" : MODE == kDown ? "moe_gemm_down" : "moe_gemm_fused");
 }
 
 int check_common(const void* a, const int32_t* offsets, int E, int64_t capacity) {
@@ -435,14 +523,15 @@ ZB_API int zb_moe_gemm_swiglu(const uint16_t* x_perm, int64_t capacity, const ui
     return zb::fail(zb::kUnsupported, "moe_gemm_swiglu: D=%d must be a multiple of 64 and I=%d of 128", D, I);
   ZB_REQUIRE_ALIGNED(gate_up, 16, "gate_up");
   ZB_REQUIRE_ALIGNED(h, 16, "h");
-  CUtensorMap ma, ma32, mb;
-  if (int rc = make_map(&ma, x_perm, capacity, D, D)) return rc;
-  if (int rc = make_map(&ma32, x_perm, capacity, D, D, 32)) return rc;
-  if (int rc = make_map(&mb, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
+  Maps m;
+  if (int rc = make_map(&m.a, x_perm, capacity, D, D)) return rc;
+  if (int rc = make_map(&m.a32, x_perm, capacity, D, D, 32)) return rc;
+  if (int rc = make_map(&m.b, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
+  m.a1 = m.a, m.a1_32 = m.a32, m.b1 = m.b;
   GemmParams p{offsets, counts, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I,
                nullptr, nullptr, 0, zb::device_status_ptr()};
-  return use_pair(capacity, E) ? launch<kSwiGLU, true>(ma, ma32, mb, p, capacity, stream)
-                                : launch<kSwiGLU, false>(ma, ma32, mb, p, capacity, stream);
+  return use_pair(capacity, E) ? launch<kSwiGLU, true>(m, p, capacity, stream)
+                                : launch<kSwiGLU, false>(m, p, capacity, stream);
 }
 
 namespace zb {
@@ -457,14 +546,15 @@ int moe_gemm_down_bounded(const uint16_t* h, int64_t capacity, const uint16_t* d
     return zb::fail(zb::kUnsupported, "moe_gemm_down: I=%d must be a multiple of 64 and D=%d of 128", I, D);
   ZB_REQUIRE_ALIGNED(down, 16, "down");
   ZB_REQUIRE_ALIGNED(y, 16, "y");
-  CUtensorMap ma, ma32, mb;
-  if (int rc = make_map(&ma, h, capacity, I, I)) return rc;
-  if (int rc = make_map(&ma32, h, capacity, I, I, 32)) return rc;
-  if (int rc = make_map(&mb, down, (int64_t)E * D, I, I)) return rc;
+  Maps m;
+  if (int rc = make_map(&m.a, h, capacity, I, I)) return rc;
+  if (int rc = make_map(&m.a32, h, capacity, I, I, 32)) return rc;
+  if (int rc = make_map(&m.b, down, (int64_t)E * D, I, I)) return rc;
+  m.a1 = m.a, m.a1_32 = m.a32, m.b1 = m.b;
   GemmParams p{offsets, counts, E, I, (D + BN - 1) / BN, (int64_t)D, 128, BN, reinterpret_cast<__nv_bfloat16*>(y), D,
                D, sorted_pairs, weights, pair_limit, zb::device_status_ptr()};
-  return use_pair(capacity, E) ? launch<kDown, true>(ma, ma32, mb, p, capacity, stream)
-                                : launch<kDown, false>(ma, ma32, mb, p, capacity, stream);
+  return use_pair(capacity, E) ? launch<kDown, true>(m, p, capacity, stream)
+                                : launch<kDown, false>(m, p, capacity, stream);
 }
 
 }  // namespace zb
@@ -475,4 +565,40 @@ ZB_API int zb_moe_gemm_down(const uint16_t* h, int64_t capacity, const uint16_t*
   // a permutation of capacity rows holds pair ids below capacity (zb_moe_permute never writes more)
   return zb::moe_gemm_down_bounded(h, capacity, down, E, D, I, offsets, counts, sorted_pairs, weights, y, capacity,
                                    stream);
+}
+
+ZB_API int zb_moe_gemms(const uint16_t* x_perm, int64_t capacity, const uint16_t* gate_up, const uint16_t* down,
+                        int E, int D, int I, const int32_t* offsets, const int32_t* counts,
+                        const int32_t* sorted_pairs, const float* weights, uint16_t* h, uint16_t* y, uint32_t* flags,
+                        cudaStream_t stream) {
+  if (int rc = check_common(x_perm, offsets, E, capacity)) return rc;
+  if (use_pair(capacity, E)) {  // prefill-sized batches: the two pair-shape launches
+    if (int rc = zb_moe_gemm_swiglu(x_perm, capacity, gate_up, E, D, I, offsets, counts, h, stream)) return rc;
+    return zb_moe_gemm_down(h, capacity, down, E, D, I, offsets, counts, sorted_pairs, weights, y, stream);
+  }
+  ZB_REQUIRE(gate_up && down && sorted_pairs && weights && h && y && flags, "moe_gemms: null pointer");
+  if (D % BK != 0 || I % BK != 0 || I % 128 != 0 || D % 128 != 0)
+    return zb::fail(zb::kUnsupported, "moe_gemms: D=%d and I=%d must be multiples of 128", D, I);
+  for (const void* ptr : {(const void*)gate_up, (const void*)down, (const void*)h, (const void*)y}) {
+    ZB_REQUIRE_ALIGNED(ptr, 16, "moe_gemms tensors");
+  }
+  Maps m;
+  if (int rc = make_map(&m.a, x_perm, capacity, D, D)) return rc;
+  if (int rc = make_map(&m.a32, x_perm, capacity, D, D, 32)) return rc;
+  if (int rc = make_map(&m.b, gate_up, (int64_t)E * 2 * I, D, D)) return rc;
+  if (int rc = make_map(&m.a1, h, capacity, I, I)) return rc;
+  if (int rc = make_map(&m.a1_32, h, capacity, I, I, 32)) return rc;
+  if (int rc = make_map(&m.b1, down, (int64_t)E * D, I, I)) return rc;
+  GemmParams p{offsets, counts, E, D, I / 128, 2 * (int64_t)I, I, 128, reinterpret_cast<__nv_bfloat16*>(h), I, I,
+               sorted_pairs, weights, capacity, zb::device_status_ptr()};
+  p.K1 = I;
+  p.n_tiles1 = (D + BN - 1) / BN;
+  p.b_rows1 = D;
+  p.b_second1 = 128;
+  p.b_step1 = BN;
+  p.out1 = reinterpret_cast<__nv_bfloat16*>(y);
+  p.out_stride1 = D;
+  p.out_cols1 = D;
+  p.flags = flags;
+  return launch<kFused, false>(m, p, capacity, stream);
 }

@@ -410,6 +410,28 @@ def moe_gemm_down(h, down, offsets, sorted_pairs, topk_weights, out, counts=None
     return out
 
 
+def moe_gemms(x_perm, gate_up, down, offsets, sorted_pairs, topk_weights, h, y, flags, counts=None):
+    """Both grouped GEMMs of the experts: H = SwiGLU(x_perm @ gate_up[e].T), then Y[pair] = (H @ down[e].T) * w.
+    Decode-sized batches run them as one persistent launch, a down tile of expert e starting as soon as every
+    SwiGLU tile of e has stored its H rows; ``flags`` ([E + 1] int32, zero before the first call, left zero) are
+    those per-expert counters. Larger batches run the two launches of :func:`moe_gemm_swiglu` /
+    :func:`moe_gemm_down`."""
+    dev = x_perm.device
+    E, two_i, D = gate_up.shape
+    I = two_i // 2
+    for name, t in (("x_perm", x_perm), ("gate_up", gate_up), ("down", down), ("h", h), ("y", y)):
+        _check_cuda(name, t, torch.bfloat16, dev)
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _check_cuda("topk_weights", topk_weights, torch.float32, dev)
+    _check_cuda("flags", flags, torch.int32, dev)
+    _require(tuple(down.shape) == (E, D, I) and x_perm.shape[1] == D and h.shape == (x_perm.shape[0], I)
+             and y.shape == (topk_weights.numel(), D) and flags.numel() >= E + 1, "shape mismatch")
+    _lib.call("zb_moe_gemms", x_perm.data_ptr(), x_perm.shape[0], gate_up.data_ptr(), down.data_ptr(), E, D, I,
+              offsets.data_ptr(), None if counts is None else counts.data_ptr(), sorted_pairs.data_ptr(),
+              topk_weights.data_ptr(), h.data_ptr(), y.data_ptr(), flags.data_ptr(), _stream(dev))
+    return y
+
+
 def moe_combine(y, top_k, out):
     """out[t] = sum over slots of y[t * k + slot] (fp32 sum, bf16 result)."""
     dev = y.device
@@ -444,6 +466,7 @@ class MoEWorkspace:
         self.x_perm = torch.empty(cap, hidden, **bf)
         self.h = torch.empty(cap, intermediate, **bf)
         self.y = torch.empty(tokens * top_k, hidden, **bf)
+        self.flags = torch.zeros(num_experts + 1, **i32)  # moe_gemms' per-expert counters (left zero by it)
 
     @classmethod
     def for_shape(cls, cache: dict, tokens, top_k, num_experts, hidden, intermediate, device):
@@ -455,16 +478,16 @@ class MoEWorkspace:
 
 
 def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, out=None):
-    """Routed SwiGLU experts for precomputed (ids, weights): permute -> gather -> GEMM1+SwiGLU -> GEMM2*w ->
-    combine. x [T, D] bf16; gate_up [E, 2I, D]; down [E, D, I]. Returns out [T, D] bf16."""
+    """Routed SwiGLU experts for precomputed (ids, weights): permute -> gather -> GEMM1+SwiGLU -> GEMM2*w (one
+    launch at decode sizes) -> combine. x [T, D] bf16; gate_up [E, 2I, D]; down [E, D, I]. Returns out [T, D] bf16."""
     T, D = x.shape
     E = gate_up.shape[0]
     k = ids.shape[1]
     ws = workspace
     perm = moe_permute(ids, E, capacity=ws.capacity, out=ws.perm)
     moe_gather(x, perm["sorted_pairs"], k, ws.x_perm)
-    moe_gemm_swiglu(ws.x_perm, gate_up, perm["offsets"], ws.h, counts=perm["counts"])
-    moe_gemm_down(ws.h, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.y, counts=perm["counts"])
+    moe_gemms(ws.x_perm, gate_up, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.h, ws.y, ws.flags,
+              counts=perm["counts"])
     if out is None:
         out = torch.empty((T, D), device=x.device, dtype=torch.bfloat16)
     return moe_combine(ws.y, k, out)
