@@ -209,6 +209,14 @@ int zb_moe_select(const void* logits, int logits_bf16, const float* bias, int T,
 int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
                    int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position, cudaStream_t stream);
 
+/* zb_moe_permute and zb_moe_gather (below) in two launches instead of three: the scatter launch also copies
+ * x_perm[position[i]] = x[i / k] for every routed pair (x [T, D] bf16, row stride x_stride; x_perm [capacity, D]
+ * bf16, padding rows left as they are). Same outputs as the two calls. Replaces moe_align_block_size plus the row
+ * gather of fused_moe_kernel (fused_moe_impl.py:28-86; kernel/triton/fused_moe.py:145). */
+int zb_moe_permute_gather(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
+                          int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position,
+                          const uint16_t* x, int64_t x_stride, int D, uint16_t* x_perm, cudaStream_t stream);
+
 /* out[r] = x[sorted_pairs[r] / k] for r < rows where sorted_pairs[r] >= 0: the A operand of the grouped GEMM, the
  * row gather fused_moe_kernel does through `offs_token // top_k` (servers/sgl/src/zonos3_sgl/kernel/triton/
  * fused_moe.py:145). Padding rows (sorted_pairs[r] < 0) are left as they are: the reference masks them to zero,

@@ -267,3 +267,27 @@ def test_fused_decode_gemms_match_the_two_launches(zb, T, D, E, k, I, skew):
         assert torch.equal(ws.y, y_ref)
         assert int(ws.flags.abs().sum().item()) == 0, "the per-expert counters must return to zero"
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("T,E,k,D", [(256, 64, 8, 2048), (4096, 64, 8, 512), (5, 16, 2, 256), (100, 128, 8, 1024)])
+def test_permute_gather_matches_the_separate_calls(zb, T, E, k, D):
+    """zb_moe_permute_gather (the row copies folded into the scatter launch) against zb_moe_permute + zb_moe_gather:
+    every permutation output identical and every routed row of x_perm identical; invalid ids (-1, E) dropped."""
+    ops = zb.ops
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(T + E + D)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(T)]).to(torch.int32)
+    ids[::7, 0] = -1
+    ids[::11, -1] = E
+    ids = ids.to(dev)
+    x = torch.randn(T, D, generator=gen).bfloat16().to(dev)
+    cap = ops.moe_capacity(T, k, E)
+    ref = ops.moe_permute(ids, E, capacity=cap)
+    xp_ref = torch.zeros(cap, D, device=dev, dtype=torch.bfloat16)
+    ops.moe_gather(x, ref["sorted_pairs"], k, xp_ref)
+    xp = torch.zeros(cap, D, device=dev, dtype=torch.bfloat16)
+    got = ops.moe_permute_gather(ids, E, x, xp, capacity=cap)
+    torch.cuda.synchronize()
+    for name in ("counts", "offsets", "sorted_pairs", "position"):
+        assert torch.equal(got[name], ref[name]), name
+    assert torch.equal(xp, xp_ref)

@@ -43,6 +43,8 @@ SIGNATURES: dict[str, list] = {
     # mixed, mixed_stride, conv_weight, A_log, dt_bias, slots, conv_state, conv_rows, N, H, D, q, k, v, g, beta,
     # stream
     "zb_gdn_prologue_decode": [_p, _i64, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p],
+    # ids, T, k, E, block, capacity, hist, counts, offsets, sorted_pairs, position, x, x_stride, D, x_perm, stream
+    "zb_moe_permute_gather": [_p, _i32, _i32, _i32, _i32, _i64, _p, _p, _p, _p, _p, _p, _i64, _i32, _p, _p],
     # x_perm, capacity, gate_up, down, E, D, I, offsets, counts, sorted_pairs, weights, h, y, flags, stream
     "zb_moe_gemms": [_p, _i64, _p, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p],
     # T, N, K, block_n, splits -> bytes (int64)

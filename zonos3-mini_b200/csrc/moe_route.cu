@@ -667,6 +667,12 @@ struct PermuteParams {
   int32_t* offsets;       // [E + 1] padded segment starts; offsets[E] = padded rows in use
   int32_t* sorted_pairs;  // [capacity], -1 = padding
   int32_t* position;      // [P]
+  // optional gather folded into the scatter: x_perm[position[i]] = x[i / k] (x_perm null: no gather)
+  const __nv_bfloat16* x;
+  int64_t x_stride;
+  int k, D;
+  __nv_bfloat16* x_perm;
+  int groups;  // blocks per 256-pair slice: each ranks the slice and copies 256 / groups of its rows
 };
 
 // Pass 1: the expert histogram of each 256-pair slice (order-free shared-memory atomics).
@@ -694,8 +700,11 @@ __global__ void __launch_bounds__(kPermThreads) moe_scatter_kernel(PermuteParams
   __shared__ int32_t seg[kMaxExperts + 1];   // padded segment starts
   __shared__ int32_t total[kMaxExperts];
   __shared__ int32_t wcount[kPermThreads / 32][kMaxExperts];
+  __shared__ int32_t pos_s[kPermPairs];
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int nslices = gridDim.x, me = blockIdx.x;
+  const int G = p.groups;  // the slice's blocks: block 0 writes the permutation, every block copies its rows
+  const int nslices = gridDim.x / G, me = blockIdx.x / G, sub = blockIdx.x % G;
+  const bool writer = sub == 0;
   {  // totals and this slice's prefix per expert: thread (group g, expert e) sums a strided share of the slices
     int* part_all = &wcount[0][0];  // reused as [groups][E] partial sums before the rank pass
     int* part_before = part_all + kMaxExperts * 4;
@@ -760,23 +769,52 @@ __global__ void __launch_bounds__(kPermThreads) moe_scatter_kernel(PermuteParams
   const int rank = __popc(peers & ((1u << lane) - 1u));
   if (ok && rank == 0) wcount[warp][e] = __popc(peers);
   __syncthreads();
+  int pos = -1;
   if (ok) {
-    int pos = seg[e] + base[e] + rank;
+    pos = seg[e] + base[e] + rank;
     for (int w = 0; w < warp; ++w) pos += wcount[w][e];
-    p.sorted_pairs[pos] = i;
-    p.position[i] = pos;
-  } else if (live) {
-    p.position[i] = -1;
   }
-  // padding rows of every segment (expert e handled by slice e % nslices), then rows past the last segment
-  for (int x = me; x < p.E; x += nslices) {
-    for (int r = seg[x] + total[x] + tid; r < seg[x + 1]; r += kPermThreads) p.sorted_pairs[r] = -1;
+  if (writer) {
+    if (ok) p.sorted_pairs[pos] = i;
+    if (live) p.position[i] = pos;
+    // padding rows of every segment (expert e handled by slice e % nslices), then rows past the last segment
+    for (int x = me; x < p.E; x += nslices) {
+      for (int r = seg[x] + total[x] + tid; r < seg[x + 1]; r += kPermThreads) p.sorted_pairs[r] = -1;
+    }
+    for (int64_t r = seg[p.E] + (int64_t)me * kPermThreads + tid; r < p.capacity;
+         r += (int64_t)nslices * kPermThreads)
+      p.sorted_pairs[r] = -1;
+    if (me == 0) {
+      for (int x = tid; x < p.E; x += kPermThreads) p.counts[x] = total[x];
+      for (int x = tid; x <= p.E; x += kPermThreads) p.offsets[x] = seg[x];
+    }
   }
-  for (int64_t r = seg[p.E] + (int64_t)me * kPermThreads + tid; r < p.capacity; r += (int64_t)nslices * kPermThreads)
-    p.sorted_pairs[r] = -1;
-  if (me == 0) {
-    for (int x = tid; x < p.E; x += kPermThreads) p.counts[x] = total[x];
-    for (int x = tid; x <= p.E; x += kPermThreads) p.offsets[x] = seg[x];
+  if (p.x_perm == nullptr) return;
+  // the gather: this block's share of the slice's rows, a warp per row (8 independent 16-byte loads per lane in
+  // flight); padding rows of x_perm are not written (the grouped GEMMs drop their results)
+  pos_s[tid] = pos;
+  __syncthreads();
+  const int per = kPermPairs / G;
+  const int vec_per_row = p.D / 8;
+  for (int j = warp; j < per; j += kPermThreads / 32) {
+    const int il = sub * per + j;
+    const int dst_row = pos_s[il];
+    if (dst_row < 0) continue;
+    const int pair = me * kPermPairs + il;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)(pair / p.k) * p.x_stride);
+    uint4* dst = reinterpret_cast<uint4*>(p.x_perm + (int64_t)dst_row * p.D);
+    for (int c0 = lane; c0 < vec_per_row; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + 32 * u;
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < vec_per_row) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + 32 * u < vec_per_row) dst[c0 + 32 * u] = v[u];
+    }
   }
 }
 
@@ -949,11 +987,41 @@ ZB_API int zb_moe_permute(const int32_t* ids, int T, int k, int E, int block, in
   ZB_REQUIRE(P < (1ll << 30), "moe_permute: %lld pairs", (long long)P);
   ZB_REQUIRE(hist && counts && offsets && sorted_pairs && position && (P == 0 || ids), "moe_permute: null pointer");
   PermuteParams p{ids, (int)P, E, block, capacity, hist, counts, offsets, sorted_pairs, position};
+  p.groups = 1;
   const unsigned slices = (unsigned)std::max<int64_t>(1, (P + kPermPairs - 1) / kPermPairs);
   ZB_CUDA(zb::launch(moe_count_kernel, dim3(slices), dim3(kPermThreads), 0, stream, 1, p));
   if (int rc = zb::check_launch("moe_permute(count)")) return rc;
   ZB_CUDA(zb::launch(moe_scatter_kernel, dim3(slices), dim3(kPermThreads), 0, stream, 1, p));
   return zb::check_launch("moe_permute(scatter)");
+}
+
+ZB_API int zb_moe_permute_gather(const int32_t* ids, int T, int k, int E, int block, int64_t capacity, int32_t* hist,
+                                 int32_t* counts, int32_t* offsets, int32_t* sorted_pairs, int32_t* position,
+                                 const uint16_t* x, int64_t x_stride, int D, uint16_t* x_perm, cudaStream_t stream) {
+  ZB_REQUIRE(T >= 0 && k > 0 && E > 0 && block > 0, "moe_permute_gather: bad sizes T=%d k=%d E=%d block=%d", T, k, E,
+             block);
+  if (E > kMaxExperts) return zb::fail(zb::kUnsupported, "moe_permute_gather: E=%d (max %d)", E, kMaxExperts);
+  const int64_t P = (int64_t)T * k;
+  const int64_t need = ((P + (int64_t)E * (block - 1)) + block - 1) / block * block;
+  ZB_REQUIRE(capacity >= need, "moe_permute_gather: capacity %lld < %lld padded rows", (long long)capacity,
+             (long long)need);
+  ZB_REQUIRE(P < (1ll << 30), "moe_permute_gather: %lld pairs", (long long)P);
+  ZB_REQUIRE(hist && counts && offsets && sorted_pairs && position && x_perm && (P == 0 || (ids && x)),
+             "moe_permute_gather: null pointer");
+  ZB_REQUIRE(D > 0 && D % 8 == 0 && x_stride >= D && x_stride % 8 == 0, "moe_permute_gather: D=%d, x_stride %lld", D,
+             (long long)x_stride);
+  ZB_REQUIRE_ALIGNED(x, 16, "x");
+  ZB_REQUIRE_ALIGNED(x_perm, 16, "x_perm");
+  PermuteParams p{ids, (int)P, E, block, capacity, hist, counts, offsets, sorted_pairs, position,
+                  reinterpret_cast<const __nv_bfloat16*>(x), x_stride, k, D, reinterpret_cast<__nv_bfloat16*>(x_perm),
+                  1};
+  const int64_t slices = std::max<int64_t>(1, (P + kPermPairs - 1) / kPermPairs);
+  // blocks per slice: about two per SM over the whole grid, a power of two dividing the slice's 256 pairs
+  while (p.groups < 32 && slices * p.groups * 2 <= 2 * zb::sm_count()) p.groups *= 2;
+  ZB_CUDA(zb::launch(moe_count_kernel, dim3((unsigned)slices), dim3(kPermThreads), 0, stream, 1, p));
+  if (int rc = zb::check_launch("moe_permute_gather(count)")) return rc;
+  ZB_CUDA(zb::launch(moe_scatter_kernel, dim3((unsigned)(slices * p.groups)), dim3(kPermThreads), 0, stream, 1, p));
+  return zb::check_launch("moe_permute_gather(scatter + gather)");
 }
 
 ZB_API int zb_moe_gather(const uint16_t* x, int64_t x_stride, const int32_t* sorted_pairs, int k, int64_t rows,

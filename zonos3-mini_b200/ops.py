@@ -369,6 +369,37 @@ def moe_permute(ids, num_experts, *, block=GEMM_BLOCK, capacity=None, out=None):
     return out
 
 
+def moe_permute_gather(ids, num_experts, x, x_perm, *, block=GEMM_BLOCK, capacity=None, out=None):
+    """:func:`moe_permute` with :func:`moe_gather` folded into its scatter launch: also writes x_perm[position[i]] =
+    x[i // k] for every routed pair (padding rows untouched). Returns the permutation dict."""
+    _check_cuda("ids", ids, torch.int32)
+    dev = ids.device
+    T, k = ids.shape
+    _require(ids.is_contiguous(), "ids must be contiguous")
+    _check_cuda("x", x, torch.bfloat16, dev)
+    _check_cuda("x_perm", x_perm, torch.bfloat16, dev)
+    D = x.shape[1]
+    _require(x.dim() == 2 and x.shape[0] == T and x.stride(1) == 1, "x must be [T, D] with contiguous rows")
+    _require(x_perm.is_contiguous() and x_perm.shape[1] == D, "x_perm must be a contiguous [capacity, D] buffer")
+    if capacity is None:
+        capacity = moe_capacity(T, k, num_experts, block)
+    _require(x_perm.shape[0] >= capacity, "x_perm has fewer rows than the capacity")
+    if out is None:
+        out = {
+            "counts": torch.empty(num_experts, device=dev, dtype=torch.int32),
+            "offsets": torch.empty(num_experts + 1, device=dev, dtype=torch.int32),
+            "sorted_pairs": torch.empty(capacity, device=dev, dtype=torch.int32),
+            "position": torch.empty(T * k, device=dev, dtype=torch.int32),
+            "hist": torch.empty(permute_hist_size(T * k, num_experts), device=dev, dtype=torch.int32),
+        }
+    _require(out["hist"].numel() >= permute_hist_size(T * k, num_experts), "permutation scratch too small")
+    _lib.call("zb_moe_permute_gather", ids.data_ptr(), T, k, num_experts, block, capacity, out["hist"].data_ptr(),
+              out["counts"].data_ptr(), out["offsets"].data_ptr(), out["sorted_pairs"].data_ptr(),
+              out["position"].data_ptr(), x.data_ptr(), x.stride(0) if T > 1 else D, D, x_perm.data_ptr(),
+              _stream(dev))
+    return out
+
+
 def moe_gather(x, sorted_pairs, top_k, out):
     """out[r] = x[sorted_pairs[r] // k] for live rows; padding rows (sorted_pairs < 0) are left as they are."""
     dev = x.device
@@ -478,14 +509,13 @@ class MoEWorkspace:
 
 
 def moe_experts(x, gate_up, down, ids, topk_weights, workspace: MoEWorkspace, out=None):
-    """Routed SwiGLU experts for precomputed (ids, weights): permute -> gather -> GEMM1+SwiGLU -> GEMM2*w (one
-    launch at decode sizes) -> combine. x [T, D] bf16; gate_up [E, 2I, D]; down [E, D, I]. Returns out [T, D] bf16."""
+    """Routed SwiGLU experts for precomputed (ids, weights): permute + gather (count, then scatter with the row copies)
+    -> GEMM1+SwiGLU -> GEMM2*w (one launch at decode sizes) -> combine. x [T, D] bf16; gate_up [E, 2I, D]; down [E, D, I]. Returns out [T, D] bf16."""
     T, D = x.shape
     E = gate_up.shape[0]
     k = ids.shape[1]
     ws = workspace
-    perm = moe_permute(ids, E, capacity=ws.capacity, out=ws.perm)
-    moe_gather(x, perm["sorted_pairs"], k, ws.x_perm)
+    perm = moe_permute_gather(ids, E, x, ws.x_perm, capacity=ws.capacity, out=ws.perm)
     moe_gemms(ws.x_perm, gate_up, down, perm["offsets"], perm["sorted_pairs"], topk_weights, ws.h, ws.y, ws.flags,
               counts=perm["counts"])
     if out is None:
