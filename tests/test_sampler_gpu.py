@@ -5,7 +5,9 @@
   penalty, temperature, top-k, top-p and min-p, on fp32 and bf16 logits of the production vocabulary (4098);
 * greedy ids equal to the ids the reference drew (tests/golden/sampler.npz) and to the oracle's argmax;
 * sampled ids: never an id of zero probability, and the frequencies of 24,000 draws within 5 sigma of the oracle's
-  probabilities (the draw uses its own Philox stream, so ids match the reference in distribution only)."""
+  probabilities (the draw uses its own Philox stream, so ids match the reference in distribution only);
+* rows with more ties at the k-th value than the sorted top-k path holds, and a codebook with fewer finite logits
+  than k: their distributions against the oracle as well."""
 
 from __future__ import annotations
 
@@ -151,3 +153,22 @@ def test_fused_softcap_matches_torch(zb, dtype):
     ids = zb.ops.sample_tts(raw, [0.0] * 4, [0] * 4, [1.0] * 4, [0.0] * 4, softcap=15.0, **kw)
     _, greedy = osam.final_probs(capped, [0.0] * 4, 0, 1.0, 0.0, **args)
     assert torch.equal(ids[:, :10].cpu().long(), greedy.long())
+
+
+def test_tied_rows_and_short_codebooks(zb):
+    """Top-k 50 with 300 ids tied at the largest logit (every tie survives the top-k), and a codebook whose size
+    leaves fewer finite logits than k (the k-th value is -inf, so every id survives the top-k and the mass decides);
+    beside ordinary rows. Every row's distribution against the oracle."""
+    gen = torch.Generator().manual_seed(12)
+    B, C = 3, 10
+    logits, args = _inputs(gen, B, C)
+    logits[0, 2, 100:400] = 20.0  # 300 ids tied at the top
+    args["codebook_sizes"] = [CB] * 4 + [20] + [CB] * (C - 5)  # codebook 4: 20 finite ids (+ the stop id)
+    args["repetition_token_ids"] = None
+    args["repetition_penalties"] = None
+    out, probs = _run(zb, logits, [0.9] * B, 50, 0.95, 0.0, args)
+    ref, _ = osam.final_probs(logits, [0.9] * B, 50, 0.95, 0.0, **args)
+    torch.testing.assert_close(probs, ref, atol=1e-5, rtol=1e-4)
+    ids = out[:, :C].reshape(-1)
+    assert (ids >= 0).all()
+    assert (ref[torch.arange(B * C), ids.long()] > 0).all()
