@@ -416,8 +416,16 @@ def strong_scaling(pkg, model, graph, dist, rank, world, dev, stream, args) -> d
         barrier(dist)
     ms = max_over_ranks(dist, a.elapsed_time(b))
     del sub
+    # per GPU: the share's algorithmic bytes (all expert weights are still read) against the HBM copy peak
+    step_s = ms / args.steps / 1e3
+    nbytes = cfg5_step_bytes(STREAMS5 // world, CONTEXT5)
+    pk = peaks()
     return {"streams_total": STREAMS5, "streams_per_gpu": STREAMS5 // world, "ms_per_step": ms / args.steps,
-            "value": STREAMS5 * args.steps / (ms / 1e3), "unit": UNIT}
+            "value": STREAMS5 * args.steps / (ms / 1e3), "unit": UNIT,
+            "per_gpu_roofline": {"bound": "hbm", "bytes_per_step": nbytes, "achieved": nbytes / step_s / 1e9,
+                                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": nbytes / step_s / 1e9 / pk["hbm_gbs"],
+                                 "limiter": "every GPU reads all 15.6 GB of weights per step whatever its share of "
+                                            "streams; at small shares the latency of the step's ~240 launches"}}
 
 
 # --------------------------------------------------------------------------------------------- CPU reference
