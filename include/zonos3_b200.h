@@ -370,6 +370,44 @@ int zb_decode_advance(const int32_t* codes, int codes_cols, int32_t* ids, int id
                       int64_t* ring, int64_t* counter, int32_t* positions, int32_t* seqlens, int32_t* out_loc,
                       const int32_t* page_table, int64_t table_stride, int max_len, int B, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------- codec DSP tail (iSTFT head, resampler) */
+
+/* Twiddle table out[e] = (cos, sin)(2 pi e / n), e in [0, n), interleaved float64 (16-byte aligned); 2 <= n <= 8192.
+ * The head stream builds one per branch once (no reference counterpart: torch.fft.irfft plans its own). */
+int zb_istft_twiddles(int n, double* out, cudaStream_t stream);
+
+/* One push of the two-branch centred iSTFT head + FIR mixer for `streams` lock-step streams, or its flush
+ * (IstftHeadStream.push / .flush, model/src/zonos3/codec/stream_host.py:39-101 and the torch twin
+ * stream_device.py:58-124; float64 arithmetic, float32 output).
+ *   y0, y1        [streams, cols, n_b + 2] float32 (y_is_f64 == 0) or float64, contiguous: per frame the
+ *                 log-magnitude of n_b/2 + 1 bins (clamped at max_log_mag before exp), then the phase
+ *   window_b      [n_b] float64; twiddle_b the zb_istft_twiddles table of n_b; mixer [2, taps] float64, taps odd
+ *   carry_b       [2, streams, n_b - hop] float64: overlap-add sums carried between pushes; half carry_parity holds
+ *                 the current carry and the push writes the next one into the other half (the caller flips the parity
+ *                 after each push); zero before the first push
+ *   ring_b        [streams, ring_size] float64 mixer-input history (power-of-two size, zero before the first push)
+ *   frames_before head frames pushed before this call; mix_from / mix_to the mixer outputs to emit (the caller's
+ *                 stream position and the reference's emission bound); flush: cols == 0, mix_to = frames * hop
+ *   scratch       >= streams * cols * (n0 + n1) float64 frame scratch; out [streams, mix_to - mix_from] float32.
+ * n_b even, a multiple of hop with n_b / hop >= 2, n_b <= 8192. */
+int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int streams, int cols, int n0, int n1, int hop,
+                       const double* window0, const double* window1, const double* twiddle0, const double* twiddle1,
+                       double max_log_mag, const double* mixer, int taps, double* carry0, double* carry1,
+                       int carry_parity, double* ring0, double* ring1, int ring_size, int64_t frames_before,
+                       int64_t mix_from, int64_t mix_to, int flush, double* scratch, int64_t scratch_elems, float* out,
+                       cudaStream_t stream);
+
+/* One push (count > 0) or flush (count == 0) of the polyphase sinc resampler for `streams` lock-step streams
+ * (ResamplerStream.push / .flush, model/src/zonos3/codec/stream_host.py:136-171, stream_device.py:169-197):
+ * x [streams, count] (row stride x_stride; float32, or float64 when x_is_f64) is appended to the input ring
+ * [streams, ring_size] float64 (power-of-two size) at n_in_before, then blocks [block_from, block_to) are emitted:
+ * out[s, (b - block_from) * new + i] = sum_k kernel[i][k] * x[b * orig + k - width], inputs outside [0, n_in) zero,
+ * the first out_count per stream (out [streams, out_count] float32). kernel_t is the kernel transposed, [2 * width +
+ * orig, new] float64. */
+int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int streams, int count, double* ring,
+                     int ring_size, int64_t n_in_before, const double* kernel_t, int orig, int new_freq, int width,
+                     int64_t block_from, int64_t block_to, int64_t out_count, float* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

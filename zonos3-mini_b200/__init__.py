@@ -6,6 +6,6 @@ The directory name is not a Python identifier, so it is imported under the alias
 (``__graft_entry__.load_package`` registers it).
 """
 
-from . import _lib, attention, attnres, base, config, core, gdn, model, moe, ops, replicas  # noqa: F401
+from . import _lib, attention, attnres, base, config, core, gdn, model, moe, ops, replicas, vocoder  # noqa: F401
 
-__all__ = ["attention", "attnres", "base", "config", "core", "gdn", "model", "moe", "ops", "replicas"]
+__all__ = ["attention", "attnres", "base", "config", "core", "gdn", "model", "moe", "ops", "replicas", "vocoder"]
