@@ -32,6 +32,7 @@ from __future__ import annotations
 import argparse
 import dataclasses
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -40,6 +41,7 @@ import tempfile
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -812,6 +814,76 @@ def bench_sampler_cfg5(ops, dev, stream, streams=256, codebooks=10, vocab=4098, 
             "us": ms * 1e3, "rows_per_s": streams * codebooks / (ms / 1e3)}
 
 
+def vocoder_inputs(streams: int, frames: int, seed: int = 12):
+    """Head frames of the codec's two iSTFT branches (n_fft 736 / 2208, hop 184): log-magnitudes N(-3, 1.5), phases
+    U(-pi, pi), float32 [streams, frames, n + 2]; periodic Hann windows, a 127-tap mixer, the 44160 -> 44100 Hz sinc
+    kernel."""
+    from oracle.istft import sinc_resample_kernel  # the kernel's construction only; nothing timed runs the oracle
+
+    rng = np.random.default_rng(seed)
+    ys = []
+    for n in (736, 2208):
+        bins = n // 2 + 1
+        ys.append(np.concatenate([rng.normal(-3.0, 1.5, (streams, frames, bins)),
+                                  rng.uniform(-np.pi, np.pi, (streams, frames, bins))], -1).astype(np.float32))
+    windows = [torch.hann_window(n, periodic=True).numpy() for n in (736, 2208)]
+    mixer = rng.normal(0, 0.05, (2, 127)).astype(np.float32)
+    mixer[0, 63] += 1.0
+    kernel, width, orig, new = sinc_resample_kernel(44160, 44100, 16, 0.99)
+    return ys, windows, mixer, (kernel, orig, new, width)
+
+
+def bench_vocoder_tail(pkg, dev, streams=256, frames=240, chunk=4, reps=3):
+    """The codec's DSP tail (two-branch iSTFT head + FIR mixer + 44.1 kHz resampler, float64) for 256 lock-step streams
+    and one second of audio each (240 head frames): pushed at once, and pushed 4 frames at a time as a streaming decode
+    does; fresh streams each rep, timed with CUDA events from the first push to the flush."""
+    voc = pkg.vocoder
+    ys, windows, mixer, (kernel, orig, new, width) = vocoder_inputs(streams, frames)
+    y0, y1 = (torch.from_numpy(y).to(dev) for y in ys)
+
+    def run(step):
+        head = voc.IstftHeadStream((736, 2208), 184, windows, mixer, math.log(100.0), dev, streams=streams,
+                                   max_cols=step)
+        res = voc.ResamplerStream(kernel, orig, new, width, dev, streams=streams)
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        n = 0
+        for c0 in range(0, frames, step):
+            n += res.push(head.push(y0[:, c0:c0 + step], y1[:, c0:c0 + step])).shape[1]
+        n += res.push(head.flush()).shape[1] + res.flush().shape[1]
+        end.record()
+        torch.cuda.synchronize(dev)
+        return start.elapsed_time(end), n
+
+    out = {"workload": f"codec DSP tail: {streams} streams x {frames} head frames (1 s of 44.1 kHz audio each), "
+                       "n_fft 736 + 2208, hop 184, 127-tap mixer, 736 -> 735 sinc resampler (770 taps), float64"}
+    for label, step in (("bulk", frames), ("stream4", chunk)):
+        run(step)
+        ms = min(run(step)[0] for _ in range(reps))
+        samples = run(step)[1]
+        out[label] = {"ms": ms, "samples_per_s": streams * samples / (ms / 1e3),
+                      "realtime_x": streams * samples / 44100 / (ms / 1e3)}
+    out["ms"] = out["bulk"]["ms"]
+    out["cpu_baseline"] = cpu_vocoder_tail(ys, windows, mixer, (kernel, orig, new, width), streams)
+    return out
+
+
+def cpu_vocoder_tail(ys, windows, mixer, res_args, streams, sample_streams=4):
+    """The oracle's whole-signal decode (NumPy float64: irfft per frame, overlap-add, mixer, resampler) of a few of the
+    same streams, timed on one host thread and scaled to all streams."""
+    from oracle import istft
+
+    kernel, orig, new, width = res_args
+    t0 = time.perf_counter()
+    for s in range(sample_streams):
+        full = istft.istft_decode(ys[0][s], ys[1][s], (736, 2208), 184, windows, mixer, math.log(100.0))
+        istft.resample(full.astype(np.float32), kernel, orig, new, width, -(-new * len(full) // orig))
+    dt = time.perf_counter() - t0
+    return {"ms_per_layer": dt / sample_streams * streams * 1e3, "sample_streams": sample_streams, "cores": 1,
+            "kind": "port"}
+
+
 def gqa_cfg5_inputs(dev, streams=256, prompt=128, context=1628, Hq=16, Hkv=4, hd=128, seed=5):
     """cfg5 global-attention decode at the end of the run: `streams` requests, each with `context` cached keys
     (the 128-token prompt, then 1500 decode steps). Slots as a token pool hands them out: each prompt a contiguous
@@ -917,6 +989,7 @@ def operator_lines(pkg, dev) -> dict:
         "gqa_decode_cfg5": bench_gqa_decode_cfg5(ops, dev, stream),
         "sampler_cfg5": bench_sampler_cfg5(ops, dev, stream),
         "decode_layer_cfg5": bench_decode_layer_cfg5(pkg, dev, stream),
+        "vocoder_tail": bench_vocoder_tail(pkg, dev),
     }
 
 
@@ -939,6 +1012,9 @@ def operator_summary(ops_: dict) -> dict:
             item["largest_route_frac"] = round(r["largest_route"]["frac"], 3)
         if "cpu_baseline" in r:
             item["cpu_ms"] = round(r["cpu_baseline"]["ms_per_layer"], 1)
+        for key in ("bulk", "stream4"):
+            if key in r:
+                item[key] = {"ms": round(r[key]["ms"], 3), "realtime_x": round(r[key]["realtime_x"])}
         out[name] = item
     return out
 
