@@ -379,8 +379,9 @@ int zb_istft_twiddles(int n, double* out, cudaStream_t stream);
 /* One push of the two-branch centred iSTFT head + FIR mixer for `streams` lock-step streams, or its flush
  * (IstftHeadStream.push / .flush, model/src/zonos3/codec/stream_host.py:39-101 and the torch twin
  * stream_device.py:58-124; float64 arithmetic, float32 output).
- *   y0, y1        [streams, cols, n_b + 2] float32 (y_is_f64 == 0) or float64, contiguous: per frame the
- *                 log-magnitude of n_b/2 + 1 bins (clamped at max_log_mag before exp), then the phase
+ *   y0, y1        [streams, cols, n_b + 2] float32 (y_is_f64 == 0) or float64, each stream's frames contiguous rows
+ *                 and streams y_b_stride elements apart: per frame the log-magnitude of n_b/2 + 1 bins (clamped at
+ *                 max_log_mag before exp), then the phase
  *   window_b      [n_b] float64; twiddle_b the zb_istft_twiddles table of n_b; mixer [2, taps] float64, taps odd
  *   carry_b       [2, streams, n_b - hop] float64: overlap-add sums carried between pushes; half carry_parity holds
  *                 the current carry and the push writes the next one into the other half (the caller flips the parity
@@ -390,7 +391,8 @@ int zb_istft_twiddles(int n, double* out, cudaStream_t stream);
  *                 stream position and the reference's emission bound); flush: cols == 0, mix_to = frames * hop
  *   scratch       >= streams * cols * (n0 + n1) float64 frame scratch; out [streams, mix_to - mix_from] float32.
  * n_b even, a multiple of hop with n_b / hop >= 2, n_b <= 8192. */
-int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int streams, int cols, int n0, int n1, int hop,
+int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1, int64_t y1_stride, int y_is_f64,
+                       int streams, int cols, int n0, int n1, int hop,
                        const double* window0, const double* window1, const double* twiddle0, const double* twiddle1,
                        double max_log_mag, const double* mixer, int taps, double* carry0, double* carry1,
                        int carry_parity, double* ring0, double* ring1, int ring_size, int64_t frames_before,

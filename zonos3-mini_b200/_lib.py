@@ -101,10 +101,10 @@ SIGNATURES: dict[str, list] = {
                       _i64, _p, _i64, _p, _i64, _p],
     # n, out (complex float64 [n]), stream
     "zb_istft_twiddles": [_i32, _p, _p],
-    # y0, y1, y_is_f64, streams, cols, n0, n1, hop, window0, window1, twiddle0, twiddle1, max_log_mag, mixer, taps,
-    # carry0, carry1, carry_parity, ring0, ring1, ring_size, frames_before, mix_from, mix_to, flush, scratch,
-    # scratch_elems, out, stream
-    "zb_istft_head_push": [_p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, ctypes.c_double, _p, _i32,
+    # y0, y0_stride, y1, y1_stride, y_is_f64, streams, cols, n0, n1, hop, window0, window1, twiddle0, twiddle1,
+    # max_log_mag, mixer, taps, carry0, carry1, carry_parity, ring0, ring1, ring_size, frames_before, mix_from, mix_to,
+    # flush, scratch, scratch_elems, out, stream
+    "zb_istft_head_push": [_p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, ctypes.c_double, _p, _i32,
                            _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i32, _p, _i64, _p, _p],
     # x, x_is_f64, x_stride, streams, count, ring, ring_size, n_in_before, kernel_t, orig, new, width, block_from,
     # block_to, out_count, out, stream

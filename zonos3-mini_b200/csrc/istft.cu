@@ -13,10 +13,10 @@
 //                         pushes plus this push's frames; positions below frames * hop are final and go, divided by
 //                         the overlap-added squared window and without the n/2 centre padding, into the branch's
 //                         mixer-input ring; the rest become the next carry.
-//   istft_mix_kernel      one thread per emitted sample: the K-tap correlation over both branches' rings.
+//   istft_mix_kernel      the K-tap correlation over both branches' rings, 8 consecutive outputs per thread.
 //   resample_append_kernel / resample_kernel   the resampler's input ring, then out[b*new + i] =
-//                         sum_k kernel[i][k] * x[b*orig + k - width], a CTA holding the input windows of 8 (stream,
-//                         block) pairs in shared memory and one output phase per thread (kernel stored transposed).
+//                         sum_k kernel[i][k] * x[b*orig + k - width] as a tiled float64 GEMM over (stream, block)
+//                         pairs x output phases (the input windows gathered from the ring while the tiles stage).
 #include <algorithm>
 #include <vector>
 
@@ -29,7 +29,9 @@ constexpr int kFrameThreads = 256;
 constexpr int kMaxN = 8192;  // (n + 1) complex float64 values of shared memory per frame CTA
 
 struct FrameBranch {
-  const void* y;           // [frames, n + 2] float32 or float64: log-magnitude for n/2 + 1 bins, then phase
+  const void* y;           // [streams][cols][n + 2] float32 or float64 (stream stride y_stride): log-magnitude for
+                           // n/2 + 1 bins, then phase
+  int64_t y_stride;
   const double* window;    // [n]
   const double2* twiddle;  // [n]: e^{2 pi i e / n}
   double* out;             // [frames, n] windowed frames
@@ -40,7 +42,7 @@ struct FrameBranch {
 
 struct FrameParams {
   FrameBranch br[2];
-  int frames;
+  int cols;
   int y_f64;
   double max_log_mag;
 };
@@ -55,15 +57,197 @@ __device__ __forceinline__ double2 cmad(double2 acc, double2 a, double2 b) {
   return acc;
 }
 
+__device__ __forceinline__ double2 cadd(double2 a, double2 b) { return make_double2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ double2 csub(double2 a, double2 b) { return make_double2(a.x - b.x, a.y - b.y); }
+
+// Roots of unity (cos, sin)(2 pi k / R), k < R, as compile-time constants: Taylor series of cos and sin on arguments
+// reduced to [-pi/2, pi/2] (cos x = -cos(x - pi), sin x = -sin(x - pi)); within a few float64 ulps.
+constexpr double kPi = 3.14159265358979323846264338327950288;
+
+constexpr double taylor_cos(double x) {
+  double term = 1.0, sum = 1.0;
+  for (int k = 1; k <= 14; ++k) {
+    term *= -x * x / ((2.0 * k - 1.0) * (2.0 * k));
+    sum += term;
+  }
+  return sum;
+}
+
+constexpr double taylor_sin(double x) {
+  double term = x, sum = x;
+  for (int k = 1; k <= 14; ++k) {
+    term *= -x * x / ((2.0 * k) * (2.0 * k + 1.0));
+    sum += term;
+  }
+  return sum;
+}
+
+template <int R>
+struct UnitRoots {
+  double c[R];
+  double s[R];
+  constexpr UnitRoots() : c(), s() {
+    for (int k = 0; k < R; ++k) {
+      double a = 2.0 * kPi * k / R;  // [0, 2 pi)
+      if (a > kPi) a -= 2.0 * kPi;   // (-pi, pi]
+      const double sign = (a > kPi / 2 || a < -kPi / 2) ? -1.0 : 1.0;
+      const double r = a > kPi / 2 ? a - kPi : (a < -kPi / 2 ? a + kPi : a);
+      c[k] = sign * taylor_cos(r);
+      s[k] = sign * taylor_sin(r);
+    }
+  }
+};
+
+__constant__ UnitRoots<23> kRoots23 = UnitRoots<23>();
+
+template <int R>
+__device__ __forceinline__ const UnitRoots<R>& const_roots() {
+  static_assert(R == 23, "a constant root table exists for radix 23");
+  return kRoots23;
+}
+
+// Length-R inverse DFTs (out[q * stride] = sum_r x_r e^{2 pi i r q / R}) of one Stockham butterfly.
+__device__ __forceinline__ void dft2_store(double2 x0, double2 x1, double2* out, int stride) {
+  out[0] = cadd(x0, x1);
+  out[stride] = csub(x0, x1);
+}
+
+__device__ __forceinline__ void dft4_store(double2 x0, double2 x1, double2 x2, double2 x3, double2* out, int stride) {
+  const double2 a = cadd(x0, x2), b = csub(x0, x2), c = cadd(x1, x3), d = csub(x1, x3);
+  out[0] = cadd(a, c);
+  out[2 * stride] = csub(a, c);
+  out[stride] = make_double2(b.x - d.y, b.y + d.x);      // b + i d
+  out[3 * stride] = make_double2(b.x + d.y, b.y - d.x);  // b - i d
+}
+
+// One Stockham pass of radix R over M points (Ns = product of the radices before it): butterfly j reads
+// src[j + r M/R], multiplies input r by W^(r (j mod Ns) M/(Ns R)) (W = e^{2 pi i / M}, the table's entry 2 r b; r b < M
+// because j mod Ns < Ns), takes the length-R inverse DFT and writes output q to (j / Ns) Ns R + (j mod Ns) + q Ns.
+//
+// Odd R pairs the inputs: with u_r = x_r + x_{R-r}, v_r = x_r - x_{R-r} (r = 1..H, H = (R - 1) / 2),
+//   y_q = x_0 + sum_r u_r cos(2 pi r q / R) + i sum_r v_r sin(2 pi r q / R),  y_{R-q} the same with -i,
+// so a pair of outputs costs 4H multiply-adds.
+template <int R>
+__device__ __forceinline__ void stockham_pass(const double2* src, double2* dst, int M, int Ns, const double2* tw) {
+  const int MR = M / R;
+  const int span = M / (Ns * R);
+  for (int j = threadIdx.x; j < MR; j += blockDim.x) {
+    const int jq = j / Ns, jn = j - jq * Ns;
+    const int b = jn * span;
+    double2* out = dst + jq * Ns * R + jn;
+    auto input = [&](int r) {
+      const double2 v = src[j + r * MR];
+      return (r == 0 || b == 0) ? v : cmul(v, __ldg(tw + 2 * r * b));
+    };
+    if constexpr (R == 2) {
+      dft2_store(input(0), input(1), out, Ns);
+    } else if constexpr (R == 4) {
+      dft4_store(input(0), input(1), input(2), input(3), out, Ns);
+    } else {
+      static_assert(R % 2 == 1, "odd radix");
+      constexpr int H = (R - 1) / 2;
+      const double2 x0 = src[j];
+      if constexpr (H <= 3) {  // one sweep, roots as compile-time constants
+        constexpr UnitRoots<R> w{};
+        double2 A[H], B[H];
+        double2 y0 = x0;
+#pragma unroll
+        for (int g = 0; g < H; ++g) A[g] = x0, B[g] = make_double2(0.0, 0.0);
+#pragma unroll
+        for (int r = 1; r <= H; ++r) {
+          const double2 a = input(r), c = input(R - r);
+          const double2 u = cadd(a, c), v = csub(a, c);
+          y0 = cadd(y0, u);
+#pragma unroll
+          for (int g = 0; g < H; ++g) {
+            const double cs = w.c[(r * (g + 1)) % R], sn = w.s[(r * (g + 1)) % R];
+            A[g].x = fma(u.x, cs, A[g].x);
+            A[g].y = fma(u.y, cs, A[g].y);
+            B[g].x = fma(v.x, sn, B[g].x);
+            B[g].y = fma(v.y, sn, B[g].y);
+          }
+        }
+        out[0] = y0;
+#pragma unroll
+        for (int g = 0; g < H; ++g) {
+          out[(g + 1) * Ns] = make_double2(A[g].x - B[g].y, A[g].y + B[g].x);
+          out[(R - g - 1) * Ns] = make_double2(A[g].x + B[g].y, A[g].y - B[g].x);
+        }
+      } else {  // sweeps of G output pairs (a runtime loop, so the inputs are re-read rather than all held), roots from
+                // the constant bank (every lane reads the same entry)
+        constexpr int G = 4;
+        const UnitRoots<R>& w = const_roots<R>();
+        double2 y0 = x0;
+#pragma unroll 1
+        for (int q0 = 1; q0 <= H; q0 += G) {
+          double2 A[G], B[G];
+#pragma unroll
+          for (int g = 0; g < G; ++g) A[g] = x0, B[g] = make_double2(0.0, 0.0);
+          int e[G];  // (r * q) mod R for the current r
+#pragma unroll
+          for (int g = 0; g < G; ++g) e[g] = 0;
+#pragma unroll
+          for (int r = 1; r <= H; ++r) {
+            const double2 a = input(r), c = input(R - r);
+            const double2 u = cadd(a, c), v = csub(a, c);
+            if (q0 == 1) y0 = cadd(y0, u);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              e[g] += q0 + g;
+              if (e[g] >= R) e[g] -= R;
+              const double cs = w.c[e[g]], sn = w.s[e[g]];
+              A[g].x = fma(u.x, cs, A[g].x);
+              A[g].y = fma(u.y, cs, A[g].y);
+              B[g].x = fma(v.x, sn, B[g].x);
+              B[g].y = fma(v.y, sn, B[g].y);
+            }
+          }
+          if (q0 == 1) out[0] = y0;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const int q = q0 + g;
+            if (q <= H) {
+              out[q * Ns] = make_double2(A[g].x - B[g].y, A[g].y + B[g].x);
+              out[(R - q) * Ns] = make_double2(A[g].x + B[g].y, A[g].y - B[g].x);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// Any other radix: each output summed directly, the powers W^(r s) by recurrence re-anchored on the table every 16
+// terms (output q of butterfly j is sum_r src[j + r M/R] W^(r s), s = (j mod Ns) M/(Ns R) + q M/R).
+__device__ void generic_pass(const double2* src, double2* dst, int M, int Ns, int R, const double2* tw) {
+  const int MR = M / R;
+  const int span = M / (Ns * R);
+  for (int t = threadIdx.x; t < M; t += blockDim.x) {
+    const int j = t % MR, q = t / MR;
+    const int jn = j % Ns;
+    const int s = (jn * span + q * MR) % M;
+    const double2 w = __ldg(tw + 2 * s);
+    double2 acc = src[j];
+    double2 cur = w;
+    int e = s;
+    for (int r = 1; r < R; ++r) {
+      if ((r & 15) == 0) cur = __ldg(tw + 2 * e);
+      acc = cmad(acc, src[j + r * MR], cur);
+      cur = cmul(cur, w);
+      e += s;
+      if (e >= M) e -= M;
+    }
+    dst[(j / Ns) * Ns * R + jn + q * Ns] = acc;
+  }
+}
+
 // Windowed inverse real DFT of one head frame of one branch (stream_host.py:55-63):
 //   X[k] = exp(min(lm_k, max_log_mag)) * (cos ph_k, sin ph_k), imaginary parts of bins 0 and n/2 zeroed;
 //   x[t] = (1/n) sum_{k<n} X[k] w^{kt} with the Hermitian extension, w = e^{2 pi i / n};  frame = x * window.
 // With M = n/2: z[m] = x[2m] + i x[2m+1] = (1/n) sum_{k<M} Z[k] W^{km}, W = w^2, where
 //   Z[k] = (X[k] + conj X[M-k]) + i w^k (X[k] - conj X[M-k]).
-// The length-M inverse DFT runs one Stockham pass per radix R of M's factorisation (Ns = product of the radices
-// before it): output q of butterfly j is sum_r src[j + r M/R] W^{r s}, s = (j mod Ns) M/(Ns R) + q M/R, stored at
-// (j / Ns) Ns R + (j mod Ns) + q Ns. The powers W^{r s} come from a recurrence re-anchored on the exact table every
-// 16 terms.
+// The length-M inverse DFT runs one Stockham pass per radix R of M's factorisation (stockham_pass: radices 2, 3, 4,
+// 5, 7 and 23 as unrolled butterflies with compile-time roots; generic_pass for any other factor).
 __global__ void __launch_bounds__(kFrameThreads) istft_frames_kernel(FrameParams p) {
   zb::pdl_enter();
   const FrameBranch& b = p.br[blockIdx.y];
@@ -76,12 +260,13 @@ __global__ void __launch_bounds__(kFrameThreads) istft_frames_kernel(FrameParams
 
   for (int k = threadIdx.x; k < bins; k += blockDim.x) {
     double lm, ph;
+    const int64_t row_off = (frame / p.cols) * b.y_stride + (frame % p.cols) * (n + 2);
     if (p.y_f64) {
-      const double* row = static_cast<const double*>(b.y) + frame * (n + 2);
+      const double* row = static_cast<const double*>(b.y) + row_off;
       lm = row[k];
       ph = row[bins + k];
     } else {
-      const float* row = static_cast<const float*>(b.y) + frame * (n + 2);
+      const float* row = static_cast<const float*>(b.y) + row_off;
       lm = (double)row[k];
       ph = (double)row[bins + k];
     }
@@ -105,24 +290,14 @@ __global__ void __launch_bounds__(kFrameThreads) istft_frames_kernel(FrameParams
   int Ns = 1;
   for (int st = 0; st < b.nstages; ++st) {
     const int R = b.radix[st];
-    const int MR = M / R;
-    const int span = M / (Ns * R);
-    for (int t = threadIdx.x; t < M; t += blockDim.x) {
-      const int j = t % MR, q = t / MR;
-      const int jn = j % Ns;
-      const int s = (jn * span + q * MR) % M;
-      const double2 w = __ldg(tw + 2 * s);
-      double2 acc = src[j];
-      double2 cur = w;
-      int e = s;
-      for (int r = 1; r < R; ++r) {
-        if ((r & 15) == 0) cur = __ldg(tw + 2 * e);
-        acc = cmad(acc, src[j + r * MR], cur);
-        cur = cmul(cur, w);
-        e += s;
-        if (e >= M) e -= M;
-      }
-      dst[(j / Ns) * Ns * R + jn + q * Ns] = acc;
+    switch (R) {
+      case 2: stockham_pass<2>(src, dst, M, Ns, tw); break;
+      case 3: stockham_pass<3>(src, dst, M, Ns, tw); break;
+      case 4: stockham_pass<4>(src, dst, M, Ns, tw); break;
+      case 5: stockham_pass<5>(src, dst, M, Ns, tw); break;
+      case 7: stockham_pass<7>(src, dst, M, Ns, tw); break;
+      case 23: stockham_pass<23>(src, dst, M, Ns, tw); break;
+      default: generic_pass(src, dst, M, Ns, R, tw); break;
     }
     __syncthreads();
     double2* tmp = src;
@@ -211,38 +386,70 @@ struct MixParams {
   int K, ring_mask;
 };
 
-constexpr int kMixTile = 256;
+constexpr int kMixOuts = 8;                       // consecutive outputs per thread
+constexpr int kMixThreads = 128;
+constexpr int kMixTile = kMixThreads * kMixOuts;  // outputs per CTA
 constexpr int kMaxTaps = 1023;
 
-// y[m] = sum_c sum_k mixer[c][k] * in_c[m + k] for m in [mix_from, mix_to) (stream_host.py:115-127): a CTA stages
-// its tile's inputs (tile + K - 1 values of each branch) and the taps in shared memory.
-__global__ void __launch_bounds__(kMixTile) istft_mix_kernel(MixParams p) {
+// Shared-memory index of input i with one pad slot per 8: thread t reads 8t + c, which lands on 9t + c + c/8, an odd
+// stride of doubles, so the lanes of a half-warp hit distinct bank pairs.
+__device__ __forceinline__ int mix_pad(int i) { return i + (i >> 3); }
+
+// y[m] = sum_c sum_k mixer[c][k] * in_c[m + k] for m in [mix_from, mix_to) (stream_host.py:115-127). A CTA stages its
+// tile's inputs (kMixTile + K - 1 values of each branch, zero past what the tile needs) and the taps (zero-padded to a
+// multiple of 8) in shared memory; a thread owns 8 consecutive outputs and, per 8 taps, reads 15 inputs of each branch
+// once and applies all 8 taps to all 8 outputs from registers.
+__global__ void __launch_bounds__(kMixThreads) istft_mix_kernel(MixParams p) {
   zb::pdl_enter();
   extern __shared__ double msm[];
   const int K = p.K;
-  const int width = kMixTile + K - 1;
-  double* taps = msm;           // [2K]
-  double* in0 = msm + 2 * K;    // [width]
-  double* in1 = in0 + width;    // [width]
+  const int Kp = (K + 7) & ~7;
+  const int width = kMixTile + Kp + 8;
+  const int padded = mix_pad(width) + 1;
+  double* taps = msm;         // [2][Kp]
+  double* in0 = msm + 2 * Kp;  // [padded]
+  double* in1 = in0 + padded;  // [padded]
   const int s = blockIdx.y;
   const int64_t m0 = p.mix_from + (int64_t)blockIdx.x * kMixTile;
   const int64_t ring = (int64_t)p.ring_mask + 1;
-  for (int i = threadIdx.x; i < 2 * K; i += blockDim.x) taps[i] = p.mixer[i];
+  for (int i = threadIdx.x; i < 2 * Kp; i += blockDim.x) {
+    const int c = i / Kp, k = i - c * Kp;
+    taps[i] = k < K ? p.mixer[c * K + k] : 0.0;
+  }
   for (int i = threadIdx.x; i < width; i += blockDim.x) {
     const int64_t idx = m0 + i;
     const bool live = idx < p.limit && idx < p.mix_to + K - 1;
-    in0[i] = live ? p.ring0[s * ring + (idx & p.ring_mask)] : 0.0;
-    in1[i] = live ? p.ring1[s * ring + (idx & p.ring_mask)] : 0.0;
+    in0[mix_pad(i)] = live ? p.ring0[s * ring + (idx & p.ring_mask)] : 0.0;
+    in1[mix_pad(i)] = live ? p.ring1[s * ring + (idx & p.ring_mask)] : 0.0;
   }
   __syncthreads();
-  const int64_t m = m0 + threadIdx.x;
-  if (m >= p.mix_to) return;
-  double y0 = 0.0, y1 = 0.0;
-  for (int k = 0; k < K; ++k) {
-    y0 = fma(taps[k], in0[threadIdx.x + k], y0);
-    y1 = fma(taps[K + k], in1[threadIdx.x + k], y1);
+  const int base = threadIdx.x * kMixOuts;
+  if (m0 + base >= p.mix_to) return;
+  double acc[kMixOuts];
+#pragma unroll
+  for (int u = 0; u < kMixOuts; ++u) acc[u] = 0.0;
+  for (int k0 = 0; k0 < Kp; k0 += 8) {
+    double v0[15], v1[15];
+#pragma unroll
+    for (int i = 0; i < 15; ++i) {
+      v0[i] = in0[mix_pad(base + k0 + i)];
+      v1[i] = in1[mix_pad(base + k0 + i)];
+    }
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const double t0 = taps[k0 + kk], t1 = taps[Kp + k0 + kk];
+#pragma unroll
+      for (int u = 0; u < kMixOuts; ++u) {
+        acc[u] = fma(t0, v0[u + kk], acc[u]);
+        acc[u] = fma(t1, v1[u + kk], acc[u]);
+      }
+    }
   }
-  p.out[(int64_t)s * (p.mix_to - p.mix_from) + (m - p.mix_from)] = (float)(y0 + y1);
+  float* out = p.out + (int64_t)s * (p.mix_to - p.mix_from) + (m0 - p.mix_from) + base;
+  const int64_t left = p.mix_to - (m0 + base);
+#pragma unroll
+  for (int u = 0; u < kMixOuts; ++u)
+    if (u < left) out[u] = (float)acc[u];
 }
 
 __global__ void istft_twiddle_kernel(int n, double2* out) {
@@ -288,8 +495,10 @@ __global__ void __launch_bounds__(256) resample_append_kernel(AppendParams p) {
   p.ring[(int64_t)s * (p.ring_mask + 1) + ((p.n_in_before + t) & p.ring_mask)] = v;
 }
 
-constexpr int kResPairs = 8;     // (stream, block) input windows per CTA
-constexpr int kResThreads = 128;  // output phases per CTA
+constexpr int kResBM = 32;      // (stream, block) pairs per CTA
+constexpr int kResBN = 64;      // output phases per CTA
+constexpr int kResBK = 16;      // taps per step
+constexpr int kResThreads = 128;  // 8 x 16 threads, 4 x 4 outputs each
 
 struct ResampleParams {
   const double* ring;      // [streams, ring]
@@ -304,45 +513,98 @@ struct ResampleParams {
   int ring_mask;
 };
 
-// out[b * new + i] = sum_k kernel[i][k] * x[b * orig + k - width] (stream_host.py:145-171), inputs outside
-// [0, n_in) reading zero. A CTA loads the kl-sample input windows of up to 8 (stream, block) pairs into shared memory;
-// thread i then walks the kernel's column i (kernel_t row k, coalesced across the CTA's phases) once for all pairs.
+// out[b * new + i] = sum_k kernel[i][k] * x[b * orig + k - width] (stream_host.py:145-171), inputs outside [0, n_in)
+// zero, as a float64 GEMM C[pairs, new] = A[pairs, kl] K^T with the rows of A the input windows of the (stream,
+// block) pairs, read from the ring as the tiles are staged. A CTA owns a 32-pair x 64-phase tile and walks the taps
+// 16 at a time: the next step's A and K^T tiles are fetched into registers while the current ones, in shared memory
+// (A transposed), feed 4 x 4 outputs per thread.
 __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p) {
   zb::pdl_enter();
-  extern __shared__ double rsm[];  // [kResPairs][kl]
-  const int kl = p.kl;
-  const int64_t pair0 = (int64_t)blockIdx.y * kResPairs;
+  __shared__ __align__(16) double As[kResBK][kResBM + 2];  // padded: the staging stores spread over the banks
+  __shared__ __align__(16) double Bs[kResBK][kResBN];
+  const int tid = threadIdx.x;
+  const int64_t pair0 = (int64_t)blockIdx.y * kResBM;
+  const int i0 = blockIdx.x * kResBN;
   const int64_t pairs_total = (int64_t)p.streams * p.nblocks;
-  const int pairs = (int)min((int64_t)kResPairs, pairs_total - pair0);
   const int64_t ring = (int64_t)p.ring_mask + 1;
-  for (int g = 0; g < pairs; ++g) {
-    const int64_t pr = pair0 + g;
-    const int64_t s = pr / p.nblocks;
-    const int64_t blk = p.block_from + pr % p.nblocks;
-    const int64_t start = blk * p.orig - p.width;
-    for (int k = threadIdx.x; k < kl; k += blockDim.x) {
-      const int64_t t = start + k;
-      rsm[g * kl + k] = (t >= 0 && t < p.n_in) ? p.ring[s * ring + (t & p.ring_mask)] : 0.0;
+
+  // A staging: element e = tid + 128 u (u < 4) of the [32 pairs][16 taps] tile: pair e / 16, tap e % 16
+  const int a_tap = tid % kResBK;
+  int64_t a_row[4], a_start[4];
+  bool a_live[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t pr = pair0 + (tid + kResThreads * u) / kResBK;
+    a_live[u] = pr < pairs_total;
+    const int64_t sidx = a_live[u] ? pr / p.nblocks : 0;
+    const int64_t blk = p.block_from + (a_live[u] ? pr % p.nblocks : 0);
+    a_row[u] = sidx * ring;
+    a_start[u] = blk * p.orig - p.width;
+  }
+  // B staging: element e = tid + 128 u (u < 8) of the [16 taps][64 phases] tile
+  const int b_col = tid % kResBN;
+  const int b_tap0 = tid / kResBN;  // 0 or 1; taps b_tap0 + 2 u
+  const bool b_live = i0 + b_col < p.nnew;
+
+  double ra[4], rb[8];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + a_tap;
+      const int64_t t = a_start[u] + k;
+      ra[u] = (a_live[u] && k < p.kl && t >= 0 && t < p.n_in) ? p.ring[a_row[u] + (t & p.ring_mask)] : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + b_tap0 + 2 * u;
+      rb[u] = (b_live && k < p.kl) ? __ldg(p.kernel_t + (int64_t)k * p.nnew + i0 + b_col) : 0.0;
+    }
+  };
+  auto stage = [&]() {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) As[a_tap][(tid + kResThreads * u) / kResBK] = ra[u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) Bs[b_tap0 + 2 * u][b_col] = rb[u];
+  };
+
+  const int tr = tid / 16, tc = tid % 16;  // pairs tr*4.., phases tc*4..
+  double acc[4][4];
+#pragma unroll
+  for (int x = 0; x < 4; ++x)
+#pragma unroll
+    for (int y = 0; y < 4; ++y) acc[x][y] = 0.0;
+
+  fetch(0);
+  for (int k0 = 0; k0 < p.kl; k0 += kResBK) {
+    __syncthreads();  // the previous step's tiles are consumed
+    stage();
+    __syncthreads();
+    if (k0 + kResBK < p.kl) fetch(k0 + kResBK);
+#pragma unroll
+    for (int k = 0; k < kResBK; ++k) {
+      const double2 a01 = *reinterpret_cast<const double2*>(&As[k][tr * 4]);
+      const double2 a23 = *reinterpret_cast<const double2*>(&As[k][tr * 4 + 2]);
+      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[k][tc * 4]);
+      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[k][tc * 4 + 2]);
+      const double av[4] = {a01.x, a01.y, a23.x, a23.y}, bv[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = fma(av[x], bv[y], acc[x][y]);
     }
   }
-  __syncthreads();
-  const int i = blockIdx.x * kResThreads + threadIdx.x;
-  if (i >= p.nnew) return;
-  double acc[kResPairs];
 #pragma unroll
-  for (int g = 0; g < kResPairs; ++g) acc[g] = 0.0;
-  const double* col = p.kernel_t + i;
-#pragma unroll 4
-  for (int k = 0; k < kl; ++k) {
-    const double kv = __ldg(col + (int64_t)k * p.nnew);
+  for (int x = 0; x < 4; ++x) {
+    const int64_t pr = pair0 + tr * 4 + x;
+    if (pr >= pairs_total) break;
+    const int64_t sidx = pr / p.nblocks;
+    const int64_t o0 = (pr % p.nblocks) * p.nnew;
 #pragma unroll
-    for (int g = 0; g < kResPairs; ++g) acc[g] = fma(kv, rsm[g * kl + k], acc[g]);
-  }
-  for (int g = 0; g < pairs; ++g) {
-    const int64_t pr = pair0 + g;
-    const int64_t s = pr / p.nblocks;
-    const int64_t o = (pr % p.nblocks) * p.nnew + i;
-    if (o < p.out_count) p.out[s * p.out_count + o] = (float)acc[g];
+    for (int y = 0; y < 4; ++y) {
+      const int i = i0 + tc * 4 + y;
+      const int64_t o = o0 + i;
+      if (i < p.nnew && o < p.out_count) p.out[sidx * p.out_count + o] = (float)acc[x][y];
+    }
   }
 }
 
@@ -356,7 +618,8 @@ ZB_API int zb_istft_twiddles(int n, double* out, cudaStream_t stream) {
   return zb::check_launch("istft_twiddles");
 }
 
-ZB_API int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int streams, int cols, int n0, int n1,
+ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1, int64_t y1_stride, int y_is_f64,
+                              int streams, int cols, int n0, int n1,
                               int hop, const double* window0, const double* window1, const double* twiddle0,
                               const double* twiddle1, double max_log_mag, const double* mixer, int taps,
                               double* carry0, double* carry1, int carry_parity, double* ring0, double* ring1,
@@ -400,11 +663,15 @@ ZB_API int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int 
     ZB_REQUIRE_ALIGNED(twiddle1, 16, "istft_head_push twiddle1");
     FrameParams fp{};
     const void* ys[2] = {y0, y1};
+    const int64_t ystrides[2] = {y0_stride, y1_stride};
     const double* wins[2] = {window0, window1};
     const double* tws[2] = {twiddle0, twiddle1};
     double* outs[2] = {scratch, scratch + (int64_t)streams * cols * n0};
     for (int b = 0; b < 2; ++b) {
+      ZB_REQUIRE(streams == 1 || ystrides[b] >= (int64_t)cols * (ns[b] + 2),
+                 "istft_head_push: branch %d stream stride %lld below cols * (n + 2)", b, (long long)ystrides[b]);
       fp.br[b].y = ys[b];
+      fp.br[b].y_stride = ystrides[b];
       fp.br[b].window = wins[b];
       fp.br[b].twiddle = reinterpret_cast<const double2*>(tws[b]);
       fp.br[b].out = outs[b];
@@ -412,7 +679,7 @@ ZB_API int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int 
       fp.br[b].nstages = radix_plan(ns[b] / 2, fp.br[b].radix);
       if (fp.br[b].nstages < 0) return zb::fail(zb::kUnsupported, "istft_head_push: n_fft %d has too many factors", ns[b]);
     }
-    fp.frames = streams * cols;
+    fp.cols = cols;
     fp.y_f64 = y_is_f64 != 0;
     fp.max_log_mag = max_log_mag;
     const size_t smem = (size_t)(std::max(n0, n1) + 1) * sizeof(double2);
@@ -450,10 +717,12 @@ ZB_API int zb_istft_head_push(const void* y0, const void* y1, int y_is_f64, int 
   if (mix_to == mix_from) return zb::kOk;
   ZB_REQUIRE(out, "istft_head_push: null output");
   MixParams mp{ring0, ring1, mixer, out, mix_from, mix_to, flush ? h + L : INT64_MAX, taps, ring_size - 1};
-  const size_t msmem = (size_t)(2 * taps + 2 * (kMixTile + taps - 1)) * sizeof(double);
+  const int Kp = (taps + 7) & ~7;
+  const int width = kMixTile + Kp + 8;
+  const size_t msmem = (size_t)(2 * Kp + 2 * (width + (width >> 3) + 1)) * sizeof(double);
   ZB_CUDA(cudaFuncSetAttribute(istft_mix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
   ZB_CUDA(zb::launch(istft_mix_kernel, dim3((unsigned)((mix_to - mix_from + kMixTile - 1) / kMixTile), (unsigned)streams),
-                     dim3(kMixTile), msmem, stream, 1, mp));
+                     dim3(kMixThreads), msmem, stream, 1, mp));
   return zb::check_launch("istft_mix");
 }
 
@@ -471,8 +740,6 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
              "resample_push: blocks [%lld, %lld) with %lld outputs", (long long)block_from, (long long)block_to,
              (long long)out_count);
   const int kl = 2 * width + orig;
-  const size_t smem = (size_t)kResPairs * kl * sizeof(double);
-  if (smem > 227 * 1024) return zb::fail(zb::kUnsupported, "resample_push: kernel of %d taps too long", kl);
   const int64_t n_in = n_in_before + count;
   if (count > 0) {
     ZB_REQUIRE(x && x_stride >= count, "resample_push: null input or row stride %lld < %d", (long long)x_stride,
@@ -505,9 +772,10 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
   rp.kl = kl;
   rp.ring_mask = ring_size - 1;
   const int64_t pairs = (int64_t)streams * rp.nblocks;
-  ZB_CUDA(cudaFuncSetAttribute(resample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  ZB_REQUIRE((pairs + kResBM - 1) / kResBM < 65536, "resample_push: %lld (stream, block) pairs in one call",
+             (long long)pairs);
   ZB_CUDA(zb::launch(resample_kernel,
-                     dim3((unsigned)((new_freq + kResThreads - 1) / kResThreads), (unsigned)((pairs + kResPairs - 1) / kResPairs)),
-                     dim3(kResThreads), smem, stream, 1, rp));
+                     dim3((unsigned)((new_freq + kResBN - 1) / kResBN), (unsigned)((pairs + kResBM - 1) / kResBM)),
+                     dim3(kResThreads), 0, stream, 1, rp));
   return zb::check_launch("resample");
 }

@@ -34,7 +34,10 @@ def _frames_input(y, device):
     y = torch.as_tensor(y)
     if y.dtype not in (torch.float32, torch.float64):
         y = y.float()
-    return y.to(device).contiguous()
+    y = y.to(device)
+    if y.ndim != 3 or y.stride(2) != 1 or y.stride(1) != y.shape[2]:  # rows of a stream must be contiguous
+        y = y.contiguous()
+    return y
 
 
 class IstftHeadStream:
@@ -96,9 +99,10 @@ class IstftHeadStream:
         """Mixer outputs whose taps are all final after `frames` frames (stream_host.py:117-121)."""
         return max(self.mix_next, frames * self.hop - max(self.n_ffts) // 2 - self.h)
 
-    def _call(self, y0, y1, y_f64: int, cols: int, mix_to: int, flush: int, out) -> None:
+    def _call(self, ys, y_f64: int, cols: int, mix_to: int, flush: int, out) -> None:
+        (y0, s0), (y1, s1) = ((None, 0), (None, 0)) if ys is None else [(y.data_ptr(), y.stride(0)) for y in ys]
         _lib.call(
-            "zb_istft_head_push", y0, y1, y_f64, self.streams, cols, self.n_ffts[0], self.n_ffts[1], self.hop,
+            "zb_istft_head_push", y0, s0, y1, s1, y_f64, self.streams, cols, self.n_ffts[0], self.n_ffts[1], self.hop,
             self.windows[0].data_ptr(), self.windows[1].data_ptr(), self.twiddles[0].data_ptr(),
             self.twiddles[1].data_ptr(), self.max_log_mag, self.mixer.data_ptr(), self.K, self.carry[0].data_ptr(),
             self.carry[1].data_ptr(), self.parity, self.rings[0].data_ptr(), self.rings[1].data_ptr(), self.ring_size,
@@ -132,10 +136,10 @@ class IstftHeadStream:
         with torch.cuda.device(self.device):
             for c0 in range(0, cols, self.max_cols):
                 c = min(self.max_cols, cols - c0)
-                parts = [y[:, c0:c0 + c].contiguous() for y in ys]
+                parts = [y[:, c0:c0 + c] for y in ys]  # frame rows stay contiguous; streams keep their stride
                 mix_to = self._emitted(self.frames + c)
                 out = torch.empty(self.streams, mix_to - self.mix_next, dtype=torch.float32, device=self.device)
-                self._call(parts[0].data_ptr(), parts[1].data_ptr(), y_f64, c, mix_to, 0, out)
+                self._call(parts, y_f64, c, mix_to, 0, out)
                 self.frames += c
                 self.parity ^= 1
                 self.mix_next = mix_to
@@ -151,7 +155,7 @@ class IstftHeadStream:
         mix_to = self.frames * self.hop
         out = torch.empty(self.streams, mix_to - self.mix_next, dtype=torch.float32, device=self.device)
         with torch.cuda.device(self.device):
-            self._call(None, None, 0, 0, mix_to, 1, out)
+            self._call(None, 0, 0, mix_to, 1, out)
         self.mix_next = mix_to
         return out[0] if self.streams == 1 else out
 
