@@ -147,71 +147,80 @@ __device__ __forceinline__ void stockham_pass(const double2* src, double2* dst, 
       static_assert(R % 2 == 1, "odd radix");
       constexpr int H = (R - 1) / 2;
       const double2 x0 = src[j];
-      if constexpr (H <= 3) {  // one sweep, roots as compile-time constants
-        constexpr UnitRoots<R> w{};
-        double2 A[H], B[H];
-        double2 y0 = x0;
+      static_assert(H <= 3, "radices above 7 take odd_first_pass or generic_pass");
+      constexpr UnitRoots<R> w{};
+      double2 A[H], B[H];
+      double2 y0 = x0;
 #pragma unroll
-        for (int g = 0; g < H; ++g) A[g] = x0, B[g] = make_double2(0.0, 0.0);
+      for (int g = 0; g < H; ++g) A[g] = x0, B[g] = make_double2(0.0, 0.0);
 #pragma unroll
-        for (int r = 1; r <= H; ++r) {
-          const double2 a = input(r), c = input(R - r);
-          const double2 u = cadd(a, c), v = csub(a, c);
-          y0 = cadd(y0, u);
-#pragma unroll
-          for (int g = 0; g < H; ++g) {
-            const double cs = w.c[(r * (g + 1)) % R], sn = w.s[(r * (g + 1)) % R];
-            A[g].x = fma(u.x, cs, A[g].x);
-            A[g].y = fma(u.y, cs, A[g].y);
-            B[g].x = fma(v.x, sn, B[g].x);
-            B[g].y = fma(v.y, sn, B[g].y);
-          }
-        }
-        out[0] = y0;
+      for (int r = 1; r <= H; ++r) {
+        const double2 a = input(r), c = input(R - r);
+        const double2 u = cadd(a, c), v = csub(a, c);
+        y0 = cadd(y0, u);
 #pragma unroll
         for (int g = 0; g < H; ++g) {
-          out[(g + 1) * Ns] = make_double2(A[g].x - B[g].y, A[g].y + B[g].x);
-          out[(R - g - 1) * Ns] = make_double2(A[g].x + B[g].y, A[g].y - B[g].x);
+          const double cs = w.c[(r * (g + 1)) % R], sn = w.s[(r * (g + 1)) % R];
+          A[g].x = fma(u.x, cs, A[g].x);
+          A[g].y = fma(u.y, cs, A[g].y);
+          B[g].x = fma(v.x, sn, B[g].x);
+          B[g].y = fma(v.y, sn, B[g].y);
         }
-      } else {  // sweeps of G output pairs (a runtime loop, so the inputs are re-read rather than all held), roots from
-                // the constant bank (every lane reads the same entry)
-        constexpr int G = 4;
-        const UnitRoots<R>& w = const_roots<R>();
-        double2 y0 = x0;
+      }
+      out[0] = y0;
+#pragma unroll
+      for (int g = 0; g < H; ++g) {
+        out[(g + 1) * Ns] = make_double2(A[g].x - B[g].y, A[g].y + B[g].x);
+        out[(R - g - 1) * Ns] = make_double2(A[g].x + B[g].y, A[g].y - B[g].x);
+      }
+    }
+  }
+}
+
+// The first pass (Ns = 1, so no twiddles) of a large odd radix R: each butterfly's H = (R - 1) / 2 output pairs are
+// split into groups of G, one (group, butterfly) item per thread, so that ceil(H / G) * M / R items rather than M / R
+// butterflies spread over the block. Item w = g * (M / R) + j reads butterfly j's R inputs from shared memory, forms
+// u_r, v_r and accumulates its G pairs (y_q = x_0 + sum_r u_r cos + i sum_r v_r sin, y_{R-q} with -i; group 0 also
+// y_0 = x_0 + sum_r u_r), the roots from the constant bank; outputs go to j R + q.
+template <int R, int G>
+__device__ __forceinline__ void odd_first_pass(const double2* src, double2* dst, int M) {
+  constexpr int H = (R - 1) / 2;
+  constexpr int NG = (H + G - 1) / G;
+  const UnitRoots<R>& w = const_roots<R>();
+  const int MR = M / R;
+  for (int item = threadIdx.x; item < NG * MR; item += blockDim.x) {
+    const int g = item / MR, j = item - g * MR;
+    const int q0 = 1 + g * G;
+    const double2 x0 = src[j];
+    double2 A[G], B[G];
+    int e[G];
+#pragma unroll
+    for (int k = 0; k < G; ++k) A[k] = x0, B[k] = make_double2(0.0, 0.0), e[k] = 0;
+    double2 y0 = x0;
 #pragma unroll 1
-        for (int q0 = 1; q0 <= H; q0 += G) {
-          double2 A[G], B[G];
+    for (int r = 1; r <= H; ++r) {
+      const double2 a = src[j + r * MR], c = src[j + (R - r) * MR];
+      const double2 u = cadd(a, c), v = csub(a, c);
+      y0 = cadd(y0, u);
 #pragma unroll
-          for (int g = 0; g < G; ++g) A[g] = x0, B[g] = make_double2(0.0, 0.0);
-          int e[G];  // (r * q) mod R for the current r
+      for (int k = 0; k < G; ++k) {
+        e[k] += q0 + k;  // r (q0 + k) mod R
+        if (e[k] >= R) e[k] -= R;
+        const double cs = w.c[e[k]], sn = w.s[e[k]];
+        A[k].x = fma(u.x, cs, A[k].x);
+        A[k].y = fma(u.y, cs, A[k].y);
+        B[k].x = fma(v.x, sn, B[k].x);
+        B[k].y = fma(v.y, sn, B[k].y);
+      }
+    }
+    double2* out = dst + j * R;
+    if (g == 0) out[0] = y0;
 #pragma unroll
-          for (int g = 0; g < G; ++g) e[g] = 0;
-#pragma unroll
-          for (int r = 1; r <= H; ++r) {
-            const double2 a = input(r), c = input(R - r);
-            const double2 u = cadd(a, c), v = csub(a, c);
-            if (q0 == 1) y0 = cadd(y0, u);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-              e[g] += q0 + g;
-              if (e[g] >= R) e[g] -= R;
-              const double cs = w.c[e[g]], sn = w.s[e[g]];
-              A[g].x = fma(u.x, cs, A[g].x);
-              A[g].y = fma(u.y, cs, A[g].y);
-              B[g].x = fma(v.x, sn, B[g].x);
-              B[g].y = fma(v.y, sn, B[g].y);
-            }
-          }
-          if (q0 == 1) out[0] = y0;
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const int q = q0 + g;
-            if (q <= H) {
-              out[q * Ns] = make_double2(A[g].x - B[g].y, A[g].y + B[g].x);
-              out[(R - q) * Ns] = make_double2(A[g].x + B[g].y, A[g].y - B[g].x);
-            }
-          }
-        }
+    for (int k = 0; k < G; ++k) {
+      const int q = q0 + k;
+      if (q <= H) {
+        out[q] = make_double2(A[k].x - B[k].y, A[k].y + B[k].x);
+        out[R - q] = make_double2(A[k].x + B[k].y, A[k].y - B[k].x);
       }
     }
   }
@@ -247,8 +256,9 @@ __device__ void generic_pass(const double2* src, double2* dst, int M, int Ns, in
 // With M = n/2: z[m] = x[2m] + i x[2m+1] = (1/n) sum_{k<M} Z[k] W^{km}, W = w^2, where
 //   Z[k] = (X[k] + conj X[M-k]) + i w^k (X[k] - conj X[M-k]).
 // The length-M inverse DFT runs one Stockham pass per radix R of M's factorisation (stockham_pass: radices 2, 3, 4,
-// 5, 7 and 23 as unrolled butterflies with compile-time roots; generic_pass for any other factor).
-__global__ void __launch_bounds__(kFrameThreads) istft_frames_kernel(FrameParams p) {
+// 5 and 7 as unrolled butterflies with compile-time roots; odd_first_pass for a leading 23; generic_pass for any
+// other factor).
+__global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_kernel(FrameParams p) {
   zb::pdl_enter();
   const FrameBranch& b = p.br[blockIdx.y];
   const int n = b.n, M = n / 2, bins = M + 1;
@@ -290,14 +300,17 @@ __global__ void __launch_bounds__(kFrameThreads) istft_frames_kernel(FrameParams
   int Ns = 1;
   for (int st = 0; st < b.nstages; ++st) {
     const int R = b.radix[st];
-    switch (R) {
-      case 2: stockham_pass<2>(src, dst, M, Ns, tw); break;
-      case 3: stockham_pass<3>(src, dst, M, Ns, tw); break;
-      case 4: stockham_pass<4>(src, dst, M, Ns, tw); break;
-      case 5: stockham_pass<5>(src, dst, M, Ns, tw); break;
-      case 7: stockham_pass<7>(src, dst, M, Ns, tw); break;
-      case 23: stockham_pass<23>(src, dst, M, Ns, tw); break;
-      default: generic_pass(src, dst, M, Ns, R, tw); break;
+    if (R == 23 && Ns == 1) {
+      odd_first_pass<23, 3>(src, dst, M);
+    } else {
+      switch (R) {
+        case 2: stockham_pass<2>(src, dst, M, Ns, tw); break;
+        case 3: stockham_pass<3>(src, dst, M, Ns, tw); break;
+        case 4: stockham_pass<4>(src, dst, M, Ns, tw); break;
+        case 5: stockham_pass<5>(src, dst, M, Ns, tw); break;
+        case 7: stockham_pass<7>(src, dst, M, Ns, tw); break;
+        default: generic_pass(src, dst, M, Ns, R, tw); break;
+      }
     }
     __syncthreads();
     double2* tmp = src;
@@ -460,7 +473,7 @@ __global__ void istft_twiddle_kernel(int n, double2* out) {
   out[e] = make_double2(c, s);
 }
 
-// Radices of M: fours, then a two, then odd factors ascending.
+// Radices of M: fours, then a two, then odd factors ascending; the largest moves to the front when it is above 7.
 int radix_plan(int M, int* radix) {
   int k = 0;
   while (M % 4 == 0 && M > 4 && k < kMaxStages) radix[k++] = 4, M /= 4;
@@ -468,7 +481,13 @@ int radix_plan(int M, int* radix) {
   for (int f = 3; f * f <= M && k < kMaxStages; f += 2)
     while (M % f == 0 && M > f && k < kMaxStages) radix[k++] = f, M /= f;
   if (k < kMaxStages && M > 1) radix[k++] = M;
-  return k < kMaxStages ? k : -1;
+  if (k >= kMaxStages) return -1;
+  // a factor above 7 runs first, where it needs no twiddles (odd_first_pass for 23, generic_pass otherwise)
+  int big = 0;
+  for (int i = 1; i < k; ++i)
+    if (radix[i] > radix[big]) big = i;
+  if (radix[big] > 7) std::swap(radix[0], radix[big]);
+  return k;
 }
 
 }  // namespace
