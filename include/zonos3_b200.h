@@ -405,10 +405,13 @@ int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1, int64_
  * [streams, ring_size] float64 (power-of-two size) at n_in_before, then blocks [block_from, block_to) are emitted:
  * out[s, (b - block_from) * new + i] = sum_k kernel[i][k] * x[b * orig + k - width], inputs outside [0, n_in) zero,
  * the first out_count per stream (out [streams, out_count] float32). kernel_t is the kernel transposed, [2 * width +
- * orig, new] float64. */
+ * orig, new] float64. workspace (16-byte aligned float64, or NULL) lets a call with few (stream, block) pairs split
+ * the taps over more CTAs: up to 8 * streams * (block_to - block_from) * new elements are used; the slices are summed
+ * in a fixed order, so the output does not depend on the split. */
 int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int streams, int count, double* ring,
                      int ring_size, int64_t n_in_before, const double* kernel_t, int orig, int new_freq, int width,
-                     int64_t block_from, int64_t block_to, int64_t out_count, float* out, cudaStream_t stream);
+                     int64_t block_from, int64_t block_to, int64_t out_count, float* out, double* workspace,
+                     int64_t workspace_elems, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -107,8 +107,9 @@ SIGNATURES: dict[str, list] = {
     "zb_istft_head_push": [_p, _i64, _p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p, _p, ctypes.c_double, _p, _i32,
                            _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i32, _p, _i64, _p, _p],
     # x, x_is_f64, x_stride, streams, count, ring, ring_size, n_in_before, kernel_t, orig, new, width, block_from,
-    # block_to, out_count, out, stream
-    "zb_resample_push": [_p, _i32, _i64, _i32, _i32, _p, _i32, _i64, _p, _i32, _i32, _i32, _i64, _i64, _i64, _p, _p],
+    # block_to, out_count, out, workspace, workspace_elems, stream
+    "zb_resample_push": [_p, _i32, _i64, _i32, _i32, _p, _i32, _i64, _p, _i32, _i32, _i32, _i64, _i64, _i64, _p, _p,
+                         _i64, _p],
 }
 _RESTYPES = {"zb_last_error": ctypes.c_char_p, "zb_clear_error": None, "zb_launch_count": ctypes.c_uint64,
              "zb_gdn_chunk_prefill_workspace_bytes": ctypes.c_int64, "zb_proj_gemm_workspace_bytes": ctypes.c_int64}

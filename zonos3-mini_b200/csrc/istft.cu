@@ -530,24 +530,35 @@ struct ResampleParams {
   int streams;
   int orig, nnew, width, kl;
   int ring_mask;
+  double* partial;  // split taps: [slices, streams * nblocks, new] per-slice sums (null: one slice, written directly)
+  int kchunk;       // taps per slice (a multiple of kResBK)
 };
 
 // out[b * new + i] = sum_k kernel[i][k] * x[b * orig + k - width] (stream_host.py:145-171), inputs outside [0, n_in)
 // zero, as a float64 GEMM C[pairs, new] = A[pairs, kl] K^T with the rows of A the input windows of the (stream,
 // block) pairs, read from the ring as the tiles are staged. A CTA owns a 32-pair x 64-phase tile and walks the taps
-// 16 at a time: the next step's A and K^T tiles are fetched into registers while the current ones, in shared memory
-// (A transposed), feed 4 x 4 outputs per thread.
+// 16 at a time: the next step's A and K^T tiles are copied (cp.async, zero-filled outside the data) into the other
+// shared-memory buffer while the current ones (A transposed) feed 4 x 4 outputs per thread. When few tiles would cover the GPU, the taps split into slices
+// (blockIdx.z) whose sums resample_reduce_kernel adds in slice order, so the result does not depend on timing.
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool live) {
+  // 8-byte global -> shared copy; a dead element copies nothing and zero-fills (src-size 0)
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(zb::smem_addr(dst)), "l"(src),
+               "r"(live ? 8 : 0)
+               : "memory");
+}
+
 __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p) {
   zb::pdl_enter();
-  __shared__ __align__(16) double As[kResBK][kResBM + 2];  // padded: the staging stores spread over the banks
-  __shared__ __align__(16) double Bs[kResBK][kResBN];
+  __shared__ __align__(16) double As[2][kResBK][kResBM + 2];  // [buffer][tap][pair], padded rows
+  __shared__ __align__(16) double Bs[2][kResBK][kResBN];      // [buffer][tap][phase]
   const int tid = threadIdx.x;
   const int64_t pair0 = (int64_t)blockIdx.y * kResBM;
   const int i0 = blockIdx.x * kResBN;
   const int64_t pairs_total = (int64_t)p.streams * p.nblocks;
   const int64_t ring = (int64_t)p.ring_mask + 1;
 
-  // A staging: element e = tid + 128 u (u < 4) of the [32 pairs][16 taps] tile: pair e / 16, tap e % 16
+  // A staging: element e = tid + 128 u (u < 4) of the [32 pairs][16 taps] tile: pair e / 16, tap e % 16 (16 lanes
+  // read 16 consecutive taps of one window)
   const int a_tap = tid % kResBK;
   int64_t a_row[4], a_start[4];
   bool a_live[4];
@@ -564,67 +575,100 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
   const int b_col = tid % kResBN;
   const int b_tap0 = tid / kResBN;  // 0 or 1; taps b_tap0 + 2 u
   const bool b_live = i0 + b_col < p.nnew;
+  const int k_begin = blockIdx.z * p.kchunk;
+  const int k_end = min(p.kl, k_begin + p.kchunk);
 
-  double ra[4], rb[8];
-  auto fetch = [&](int k0) {
+  auto issue = [&](int k0, int buf) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int k = k0 + a_tap;
       const int64_t t = a_start[u] + k;
-      ra[u] = (a_live[u] && k < p.kl && t >= 0 && t < p.n_in) ? p.ring[a_row[u] + (t & p.ring_mask)] : 0.0;
+      const bool live = a_live[u] && k < k_end && t >= 0 && t < p.n_in;
+      cp_async8(&As[buf][a_tap][(tid + kResThreads * u) / kResBK], live ? p.ring + a_row[u] + (t & p.ring_mask) : p.ring,
+                live);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int k = k0 + b_tap0 + 2 * u;
-      rb[u] = (b_live && k < p.kl) ? __ldg(p.kernel_t + (int64_t)k * p.nnew + i0 + b_col) : 0.0;
+      const bool live = b_live && k < k_end;
+      cp_async8(&Bs[buf][b_tap0 + 2 * u][b_col], live ? p.kernel_t + (int64_t)k * p.nnew + i0 + b_col : p.kernel_t,
+                live);
     }
-  };
-  auto stage = [&]() {
-#pragma unroll
-    for (int u = 0; u < 4; ++u) As[a_tap][(tid + kResThreads * u) / kResBK] = ra[u];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) Bs[b_tap0 + 2 * u][b_col] = rb[u];
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
-  const int tr = tid / 16, tc = tid % 16;  // pairs tr*4.., phases tc*4..
+  // thread (tr, tc): pairs tr*4 .. tr*4+3, phases {2tc, 2tc+1, 32+2tc, 33+2tc} (each fragment load is a contiguous
+  // 16 bytes per lane, so a half-warp's 256 bytes hit every bank once)
+  const int tr = tid / 16, tc = tid % 16;
   double acc[4][4];
 #pragma unroll
   for (int x = 0; x < 4; ++x)
 #pragma unroll
     for (int y = 0; y < 4; ++y) acc[x][y] = 0.0;
 
-  fetch(0);
-  for (int k0 = 0; k0 < p.kl; k0 += kResBK) {
-    __syncthreads();  // the previous step's tiles are consumed
-    stage();
+  const int steps = (k_end - k_begin + kResBK - 1) / kResBK;
+  issue(k_begin, 0);
+  for (int st = 0; st < steps; ++st) {
+    const int buf = st & 1;
+    if (st + 1 < steps) {
+      issue(k_begin + (st + 1) * kResBK, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this step's group has landed
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
     __syncthreads();
-    if (k0 + kResBK < p.kl) fetch(k0 + kResBK);
 #pragma unroll
     for (int k = 0; k < kResBK; ++k) {
-      const double2 a01 = *reinterpret_cast<const double2*>(&As[k][tr * 4]);
-      const double2 a23 = *reinterpret_cast<const double2*>(&As[k][tr * 4 + 2]);
-      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[k][tc * 4]);
-      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[k][tc * 4 + 2]);
+      const double2 a01 = *reinterpret_cast<const double2*>(&As[buf][k][tr * 4]);
+      const double2 a23 = *reinterpret_cast<const double2*>(&As[buf][k][tr * 4 + 2]);
+      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[buf][k][tc * 2]);
+      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[buf][k][32 + tc * 2]);
       const double av[4] = {a01.x, a01.y, a23.x, a23.y}, bv[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = fma(av[x], bv[y], acc[x][y]);
     }
+    __syncthreads();  // this buffer is refilled two steps on
   }
 #pragma unroll
   for (int x = 0; x < 4; ++x) {
     const int64_t pr = pair0 + tr * 4 + x;
     if (pr >= pairs_total) break;
+    if (p.partial) {
+      double* dst = p.partial + ((int64_t)blockIdx.z * pairs_total + pr) * p.nnew;
+#pragma unroll
+      for (int y = 0; y < 4; ++y) {
+        const int i = i0 + (y < 2 ? tc * 2 + y : 32 + tc * 2 + y - 2);
+        if (i < p.nnew) dst[i] = acc[x][y];
+      }
+      continue;
+    }
     const int64_t sidx = pr / p.nblocks;
     const int64_t o0 = (pr % p.nblocks) * p.nnew;
 #pragma unroll
     for (int y = 0; y < 4; ++y) {
-      const int i = i0 + tc * 4 + y;
+      const int i = i0 + (y < 2 ? tc * 2 + y : 32 + tc * 2 + y - 2);
       const int64_t o = o0 + i;
       if (i < p.nnew && o < p.out_count) p.out[sidx * p.out_count + o] = (float)acc[x][y];
     }
   }
+}
+
+// Sums the tap slices of resample_kernel in slice order: out[s, o] for o < out_count, o = (pair's block) * new + i.
+__global__ void __launch_bounds__(256) resample_reduce_kernel(ResampleParams p, int slices) {
+  zb::pdl_enter();
+  const int64_t pairs_total = (int64_t)p.streams * p.nblocks;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= pairs_total * p.nnew) return;
+  const int64_t pr = idx / p.nnew;
+  const int i = (int)(idx - pr * p.nnew);
+  const int64_t sidx = pr / p.nblocks;
+  const int64_t o = (pr % p.nblocks) * p.nnew + i;
+  if (o >= p.out_count) return;
+  double v = 0.0;
+  for (int z = 0; z < slices; ++z) v += p.partial[((int64_t)z * pairs_total + pr) * p.nnew + i];
+  p.out[sidx * p.out_count + o] = (float)v;
 }
 
 }  // namespace
@@ -748,7 +792,7 @@ ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1,
 ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int streams, int count, double* ring,
                             int ring_size, int64_t n_in_before, const double* kernel_t, int orig, int new_freq,
                             int width, int64_t block_from, int64_t block_to, int64_t out_count, float* out,
-                            cudaStream_t stream) {
+                            double* workspace, int64_t workspace_elems, cudaStream_t stream) {
   ZB_REQUIRE(streams >= 1 && count >= 0 && n_in_before >= 0 && orig >= 1 && new_freq >= 1 && width >= 0,
              "resample_push: streams=%d count=%d orig=%d new=%d width=%d", streams, count, orig, new_freq, width);
   ZB_REQUIRE(ring && kernel_t, "resample_push: null ring or kernel");
@@ -793,8 +837,22 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
   const int64_t pairs = (int64_t)streams * rp.nblocks;
   ZB_REQUIRE((pairs + kResBM - 1) / kResBM < 65536, "resample_push: %lld (stream, block) pairs in one call",
              (long long)pairs);
+  // split the taps while the tiles alone would leave most of the GPU idle (four resample CTAs fit an SM)
+  const int64_t tiles = (int64_t)((new_freq + kResBN - 1) / kResBN) * ((pairs + kResBM - 1) / kResBM);
+  const int steps = (kl + kResBK - 1) / kResBK;
+  int slices = (int)std::min<int64_t>({8, steps, std::max<int64_t>(1, 4 * zb::sm_count() / tiles)});
+  if (!workspace || workspace_elems < (int64_t)slices * pairs * new_freq) slices = 1;
+  rp.kchunk = (steps + slices - 1) / slices * kResBK;
+  slices = (kl + rp.kchunk - 1) / rp.kchunk;
+  rp.partial = slices > 1 ? workspace : nullptr;
+  if (slices > 1) ZB_REQUIRE_ALIGNED(workspace, 16, "resample_push workspace");
   ZB_CUDA(zb::launch(resample_kernel,
-                     dim3((unsigned)((new_freq + kResBN - 1) / kResBN), (unsigned)((pairs + kResBM - 1) / kResBM)),
+                     dim3((unsigned)((new_freq + kResBN - 1) / kResBN), (unsigned)((pairs + kResBM - 1) / kResBM),
+                          (unsigned)slices),
                      dim3(kResThreads), 0, stream, 1, rp));
-  return zb::check_launch("resample");
+  if (int rc = zb::check_launch("resample")) return rc;
+  if (slices == 1) return zb::kOk;
+  const int64_t n = pairs * new_freq;
+  ZB_CUDA(zb::launch(resample_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream, 1, rp, slices));
+  return zb::check_launch("resample_reduce");
 }

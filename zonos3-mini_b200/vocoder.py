@@ -64,7 +64,7 @@ class IstftHeadStream:
         self.K = self.mixer.shape[1]
         self.h = (self.K - 1) // 2
         self.streams = int(streams)
-        self.max_cols = int(max_cols)
+        self.max_cols = int(max_cols)  # longer pushes run as several calls of at most max_cols frames
         if self.streams < 1 or self.max_cols < 1:
             raise ValueError("istft: streams and max_cols must be positive")
         self.ring_size = _next_pow2(self.max_cols * self.hop + 2 * self.K + max(self.n_ffts))
@@ -84,7 +84,8 @@ class IstftHeadStream:
         self.done = False
 
     def copy(self) -> "IstftHeadStream":
-        """An independent twin: the carries and rings are copied; constants and the frame scratch are shared."""
+        """An independent twin: the carries and rings are copied; constants and the frame scratch are shared (so the
+        twins run on one CUDA stream, as the reference's run on one device)."""
         twin = object.__new__(IstftHeadStream)
         twin.__dict__.update(self.__dict__)
         twin.carry = [t.clone() for t in self.carry]
@@ -181,13 +182,24 @@ class ResamplerStream:
         self.ring = torch.zeros(self.streams, self.ring_size, dtype=torch.float64, device=self.device)
         self.n_in = 0  # samples pushed
         self.next_block = 0
+        self._ws = None
 
     def copy(self) -> "ResamplerStream":
         """An independent twin (the input ring is copied; the kernel is shared)."""
         twin = object.__new__(ResamplerStream)
         twin.__dict__.update(self.__dict__)
         twin.ring = self.ring.clone()
+        twin._ws = None
         return twin
+
+    def _workspace(self, elems: int) -> torch.Tensor | None:
+        """Float64 scratch for the tap-split of a call with few (stream, block) pairs; calls too large for the
+        cached buffer (above 2^22 elements) run unsplit, where the tiles alone fill the GPU."""
+        if elems > 1 << 22:
+            return None
+        if self._ws is None or self._ws.numel() < elems:
+            self._ws = torch.empty(elems, dtype=torch.float64, device=self.device)
+        return self._ws
 
     def _out(self, count: int) -> torch.Tensor:
         return torch.empty(self.streams, count, dtype=torch.float32, device=self.device)
@@ -207,9 +219,11 @@ class ResamplerStream:
             out_count = total - self.next_block * N
         out = self._out(out_count)
         x_ptr, x_f64, x_stride = (None, 0, 0) if x is None else (x.data_ptr(), int(x.dtype == torch.float64), x.stride(0))
+        ws = self._workspace(8 * self.streams * (end - self.next_block) * N) if out_count else None
         _lib.call("zb_resample_push", x_ptr, x_f64, x_stride, self.streams, count, self.ring.data_ptr(),
                   self.ring_size, self.n_in, self.kernel_t.data_ptr(), O, N, W, self.next_block, end, out_count,
-                  out.data_ptr() if out_count else None, _stream(self.device))
+                  out.data_ptr() if out_count else None, ws.data_ptr() if ws is not None else None,
+                  ws.numel() if ws is not None else 0, _stream(self.device))
         self.n_in = n_in
         self.next_block = end
         return out
