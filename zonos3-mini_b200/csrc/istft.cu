@@ -38,6 +38,7 @@ struct FrameBranch {
   int n;
   int nstages;
   int radix[kMaxStages];
+  uint32_t ns_magic[kMaxStages];  // ceil(2^32 / Ns) of each pass (0 when Ns = 1): j / Ns = umulhi(j, magic), j < 2^16
 };
 
 struct FrameParams {
@@ -98,14 +99,6 @@ struct UnitRoots {
   }
 };
 
-__constant__ UnitRoots<23> kRoots23 = UnitRoots<23>();
-
-template <int R>
-__device__ __forceinline__ const UnitRoots<R>& const_roots() {
-  static_assert(R == 23, "a constant root table exists for radix 23");
-  return kRoots23;
-}
-
 // Length-R inverse DFTs (out[q * stride] = sum_r x_r e^{2 pi i r q / R}) of one Stockham butterfly.
 __device__ __forceinline__ void dft2_store(double2 x0, double2 x1, double2* out, int stride) {
   out[0] = cadd(x0, x1);
@@ -128,11 +121,12 @@ __device__ __forceinline__ void dft4_store(double2 x0, double2 x1, double2 x2, d
 //   y_q = x_0 + sum_r u_r cos(2 pi r q / R) + i sum_r v_r sin(2 pi r q / R),  y_{R-q} the same with -i,
 // so a pair of outputs costs 4H multiply-adds.
 template <int R>
-__device__ __forceinline__ void stockham_pass(const double2* src, double2* dst, int M, int Ns, const double2* tw) {
+__device__ __forceinline__ void stockham_pass(const double2* src, double2* dst, int M, int Ns, uint32_t magic,
+                                              const double2* tw) {
   const int MR = M / R;
   const int span = M / (Ns * R);
   for (int j = threadIdx.x; j < MR; j += blockDim.x) {
-    const int jq = j / Ns, jn = j - jq * Ns;
+    const int jq = magic ? (int)__umulhi((unsigned)j, magic) : j, jn = j - jq * Ns;
     const int b = jn * span;
     double2* out = dst + jq * Ns * R + jn;
     auto input = [&](int r) {
@@ -179,49 +173,63 @@ __device__ __forceinline__ void stockham_pass(const double2* src, double2* dst, 
 
 // The first pass (Ns = 1, so no twiddles) of a large odd radix R: each butterfly's H = (R - 1) / 2 output pairs are
 // split into groups of G, one (group, butterfly) item per thread, so that ceil(H / G) * M / R items rather than M / R
-// butterflies spread over the block. Item w = g * (M / R) + j reads butterfly j's R inputs from shared memory, forms
-// u_r, v_r and accumulates its G pairs (y_q = x_0 + sum_r u_r cos + i sum_r v_r sin, y_{R-q} with -i; group 0 also
-// y_0 = x_0 + sum_r u_r), the roots from the constant bank; outputs go to j R + q.
-template <int R, int G>
-__device__ __forceinline__ void odd_first_pass(const double2* src, double2* dst, int M) {
+// butterflies spread over the block. Items run group-major with the butterflies of a group padded to whole warps, so
+// a warp's group is uniform and its roots are compile-time constants (odd_first_group<g>). An item reads butterfly
+// j's R inputs from shared memory, forms u_r, v_r and accumulates its G pairs (y_q = x_0 + sum_r u_r cos + i sum_r
+// v_r sin, y_{R-q} with -i; group 0 also y_0 = x_0 + sum_r u_r); outputs go to j R + q.
+template <int R, int G, int g>
+__device__ __forceinline__ void odd_first_group(const double2* src, double2* dst, int MR, int j) {
   constexpr int H = (R - 1) / 2;
-  constexpr int NG = (H + G - 1) / G;
-  const UnitRoots<R>& w = const_roots<R>();
-  const int MR = M / R;
-  for (int item = threadIdx.x; item < NG * MR; item += blockDim.x) {
-    const int g = item / MR, j = item - g * MR;
-    const int q0 = 1 + g * G;
-    const double2 x0 = src[j];
-    double2 A[G], B[G];
-    int e[G];
+  constexpr int q0 = 1 + g * G;
+  constexpr UnitRoots<R> w{};
+  const double2 x0 = src[j];
+  double2 A[G], B[G];
 #pragma unroll
-    for (int k = 0; k < G; ++k) A[k] = x0, B[k] = make_double2(0.0, 0.0), e[k] = 0;
-    double2 y0 = x0;
-#pragma unroll 1
-    for (int r = 1; r <= H; ++r) {
-      const double2 a = src[j + r * MR], c = src[j + (R - r) * MR];
-      const double2 u = cadd(a, c), v = csub(a, c);
-      y0 = cadd(y0, u);
+  for (int k = 0; k < G; ++k) A[k] = x0, B[k] = make_double2(0.0, 0.0);
+  double2 y0 = x0;
 #pragma unroll
-      for (int k = 0; k < G; ++k) {
-        e[k] += q0 + k;  // r (q0 + k) mod R
-        if (e[k] >= R) e[k] -= R;
-        const double cs = w.c[e[k]], sn = w.s[e[k]];
+  for (int r = 1; r <= H; ++r) {
+    const double2 a = src[j + r * MR], c = src[j + (R - r) * MR];
+    const double2 u = cadd(a, c), v = csub(a, c);
+    if (g == 0) y0 = cadd(y0, u);
+#pragma unroll
+    for (int k = 0; k < G; ++k) {
+      if (q0 + k <= H) {
+        const double cs = w.c[(r * (q0 + k)) % R], sn = w.s[(r * (q0 + k)) % R];
         A[k].x = fma(u.x, cs, A[k].x);
         A[k].y = fma(u.y, cs, A[k].y);
         B[k].x = fma(v.x, sn, B[k].x);
         B[k].y = fma(v.y, sn, B[k].y);
       }
     }
-    double2* out = dst + j * R;
-    if (g == 0) out[0] = y0;
+  }
+  double2* out = dst + j * R;
+  if (g == 0) out[0] = y0;
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const int q = q0 + k;
-      if (q <= H) {
-        out[q] = make_double2(A[k].x - B[k].y, A[k].y + B[k].x);
-        out[R - q] = make_double2(A[k].x + B[k].y, A[k].y - B[k].x);
-      }
+  for (int k = 0; k < G; ++k) {
+    const int q = q0 + k;
+    if (q <= H) {
+      out[q] = make_double2(A[k].x - B[k].y, A[k].y + B[k].x);
+      out[R - q] = make_double2(A[k].x + B[k].y, A[k].y - B[k].x);
+    }
+  }
+}
+
+template <int R, int G>
+__device__ __forceinline__ void odd_first_pass(const double2* src, double2* dst, int M) {
+  constexpr int H = (R - 1) / 2;
+  constexpr int NG = (H + G - 1) / G;
+  static_assert(NG <= 4, "odd_first_pass dispatches at most four groups");
+  const int MR = M / R;
+  const int MRp = (MR + 31) & ~31;  // butterflies of a group, padded to whole warps
+  for (int item = threadIdx.x; item < NG * MRp; item += blockDim.x) {
+    const int g = item / MRp, j = item - g * MRp;
+    if (j >= MR) continue;
+    switch (g) {  // uniform within a warp
+      case 0: odd_first_group<R, G, 0>(src, dst, MR, j); break;
+      case 1: if constexpr (NG > 1) odd_first_group<R, G, 1>(src, dst, MR, j); break;
+      case 2: if constexpr (NG > 2) odd_first_group<R, G, 2>(src, dst, MR, j); break;
+      default: if constexpr (NG > 3) odd_first_group<R, G, 3>(src, dst, MR, j); break;
     }
   }
 }
@@ -304,11 +312,11 @@ __global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_kernel(FramePar
       odd_first_pass<23, 3>(src, dst, M);
     } else {
       switch (R) {
-        case 2: stockham_pass<2>(src, dst, M, Ns, tw); break;
-        case 3: stockham_pass<3>(src, dst, M, Ns, tw); break;
-        case 4: stockham_pass<4>(src, dst, M, Ns, tw); break;
-        case 5: stockham_pass<5>(src, dst, M, Ns, tw); break;
-        case 7: stockham_pass<7>(src, dst, M, Ns, tw); break;
+        case 2: stockham_pass<2>(src, dst, M, Ns, b.ns_magic[st], tw); break;
+        case 3: stockham_pass<3>(src, dst, M, Ns, b.ns_magic[st], tw); break;
+        case 4: stockham_pass<4>(src, dst, M, Ns, b.ns_magic[st], tw); break;
+        case 5: stockham_pass<5>(src, dst, M, Ns, b.ns_magic[st], tw); break;
+        case 7: stockham_pass<7>(src, dst, M, Ns, b.ns_magic[st], tw); break;
         default: generic_pass(src, dst, M, Ns, R, tw); break;
       }
     }
@@ -741,6 +749,8 @@ ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1,
       fp.br[b].n = ns[b];
       fp.br[b].nstages = radix_plan(ns[b] / 2, fp.br[b].radix);
       if (fp.br[b].nstages < 0) return zb::fail(zb::kUnsupported, "istft_head_push: n_fft %d has too many factors", ns[b]);
+      for (int st = 0, Ns = 1; st < fp.br[b].nstages; Ns *= fp.br[b].radix[st++])
+        fp.br[b].ns_magic[st] = Ns == 1 ? 0u : (uint32_t)(((1ull << 32) + Ns - 1) / Ns);
     }
     fp.cols = cols;
     fp.y_f64 = y_is_f64 != 0;
