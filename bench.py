@@ -1019,11 +1019,11 @@ def operator_summary(ops_: dict) -> dict:
     return out
 
 
-def profile_launches(n: int, workload: str = "decode_step", layers: int = LAYERS5) -> None:
+def profile_launches(n: int, workload: str = "decode_step", layers: int = LAYERS5, streams: int = 0) -> None:
     """n runs of a workload's kernels (the bench's own launches, without timing): cfg5 decode steps (graph replays of
     the headline step; ``layers`` shrinks the model for a small ncu case), cfg2 decode updates cycling the layer
     states, cfg4 MoE layers, the largest cfg5 AttnRes route, cfg3 prefill, cfg5 DeltaNet + MoE decode layers, cfg5
-    GQA decode attention or cfg5 sampler calls (eager launches)."""
+    GQA decode attention, cfg5 sampler calls (eager launches) or the vocoder DSP tail's two bench cases."""
     pkg = __import__("__graft_entry__").load_package()
     ops = pkg.ops
     dev = torch.device("cuda", 0)
@@ -1034,6 +1034,23 @@ def profile_launches(n: int, workload: str = "decode_step", layers: int = LAYERS
         torch.cuda.synchronize(dev)
         print(f"profile: {n} cfg5 decode steps ({layers} layers, {graph.launches_per_step} library launches each) "
               f"done, status {ops.device_status()}")
+        return
+    if workload == "vocoder_tail":
+        voc = pkg.vocoder
+        S = streams or 256
+        ys, windows, mixer, (kernel, orig, new, width) = vocoder_inputs(S, 240)
+        y0, y1 = (torch.from_numpy(y).to(dev) for y in ys)
+        for _ in range(n):
+            for step in (240, 4):  # one push of the whole second, then 4-frame pushes
+                head = voc.IstftHeadStream((736, 2208), 184, windows, mixer, math.log(100.0), dev, streams=S,
+                                           max_cols=step)
+                res = voc.ResamplerStream(kernel, orig, new, width, dev, streams=S)
+                for c0 in range(0, 240, step):
+                    res.push(head.push(y0[:, c0:c0 + step], y1[:, c0:c0 + step]))
+                res.push(head.flush())
+                res.flush()
+        torch.cuda.synchronize(dev)
+        print(f"profile: {n} x (one 240-frame push + 60 four-frame pushes) of {S} vocoder streams done")
         return
     if workload == "moe":
         x, norm_w, w_r, gate_up, down = moe_cfg4_inputs(dev)
@@ -1132,14 +1149,15 @@ def main():
                     help="only run this many steps / launches of a workload (for an ncu capture) and exit")
     ap.add_argument("--profile-workload", default="decode_step",
                     choices=("decode_step", "gdn_decode", "moe", "attnres", "prefill", "decode_layer", "gqa_decode",
-                             "sampler"),
+                             "sampler", "vocoder_tail"),
                     help="workload whose launches --profile-launches runs")
     ap.add_argument("--profile-layers", type=int, default=LAYERS5, help="layers of the decode_step profile model")
+    ap.add_argument("--profile-streams", type=int, default=0, help="streams of the vocoder_tail profile (0: 256)")
     ap.add_argument("--operators", type=int, default=1,
                     help="also time the other hot-path operators on their own configs at N=1")
     args = ap.parse_args()
     if args.profile_launches:
-        profile_launches(args.profile_launches, args.profile_workload, args.profile_layers)
+        profile_launches(args.profile_launches, args.profile_workload, args.profile_layers, args.profile_streams)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
