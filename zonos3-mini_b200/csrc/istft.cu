@@ -13,6 +13,9 @@
 //                         pushes plus this push's frames; positions below frames * hop are final and go, divided by
 //                         the overlap-added squared window and without the n/2 centre padding, into the branch's
 //                         mixer-input ring; the rest become the next carry.
+//   istft_frames_group_kernel / istft_group_seams_kernel   pushes of 32 frames or more: a CTA per group of 16+
+//                         frames synthesises them in turn and overlap-adds them itself (an L2-resident span), so the
+//                         frames never round-trip through HBM; a second kernel joins the groups' overlapping edges.
 //   istft_mix_kernel      the K-tap correlation over both branches' rings, 8 consecutive outputs per thread.
 //   resample_append_kernel / resample_kernel   the resampler's input ring, then out[b*new + i] =
 //                         sum_k kernel[i][k] * x[b*orig + k - width] as a tiled float64 GEMM over (stream, block)
@@ -43,6 +46,7 @@ struct FrameBranch {
 
 struct FrameParams {
   FrameBranch br[2];
+  int first;  // branch of blockIdx.y == 0: the longer n_fft, so its (slower) CTAs are dispatched first
   int cols;
   int y_f64;
   double max_log_mag;
@@ -266,19 +270,18 @@ __device__ void generic_pass(const double2* src, double2* dst, int M, int Ns, in
 // The length-M inverse DFT runs one Stockham pass per radix R of M's factorisation (stockham_pass: radices 2, 3, 4,
 // 5 and 7 as unrolled butterflies with compile-time roots; odd_first_pass for a leading 23; generic_pass for any
 // other factor).
-__global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_kernel(FrameParams p) {
-  zb::pdl_enter();
-  const FrameBranch& b = p.br[blockIdx.y];
+// Synthesises head frame `frame` (= stream * cols + column) of branch b in shared memory (sm: (n + 1) complex values);
+// returns the buffer that holds z[m] = n (x[2m] + i x[2m+1]) (the caller applies 1/n and the window). Ends with a
+// block barrier.
+__device__ __forceinline__ const double2* synth_frame(const FrameParams& p, const FrameBranch& b, int64_t frame,
+                                                      double2* sm) {
   const int n = b.n, M = n / 2, bins = M + 1;
-  const int64_t frame = blockIdx.x;
-  extern __shared__ double2 sm[];
   double2* X = sm;          // [M + 1], later the second Stockham buffer
   double2* A = sm + M + 1;  // [M]
   const double2* tw = b.twiddle;
-
+  const int64_t row_off = (frame / p.cols) * b.y_stride + (frame % p.cols) * (n + 2);
   for (int k = threadIdx.x; k < bins; k += blockDim.x) {
     double lm, ph;
-    const int64_t row_off = (frame / p.cols) * b.y_stride + (frame % p.cols) * (n + 2);
     if (p.y_f64) {
       const double* row = static_cast<const double*>(b.y) + row_off;
       lm = row[k];
@@ -326,13 +329,22 @@ __global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_kernel(FramePar
     dst = tmp;
     Ns *= R;
   }
+  return src;
+}
 
+__global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_kernel(FrameParams p) {
+  zb::pdl_enter();
+  const FrameBranch& b = p.br[blockIdx.y ^ p.first];
+  const int n = b.n, M = n / 2;
+  const int64_t frame = blockIdx.x;
+  extern __shared__ double2 sm[];
+  const double2* z = synth_frame(p, b, frame, sm);
   const double inv_n = 1.0 / (double)n;
   double* out = b.out + frame * n;
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    const double2 z = src[m];
+    const double2 v = z[m];
     const double2 win = *reinterpret_cast<const double2*>(b.window + 2 * m);
-    *reinterpret_cast<double2*>(out + 2 * m) = make_double2(z.x * inv_n * win.x, z.y * inv_n * win.y);
+    *reinterpret_cast<double2*>(out + 2 * m) = make_double2(v.x * inv_n * win.x, v.y * inv_n * win.y);
   }
 }
 
@@ -355,6 +367,25 @@ struct OlaParams {
 };
 
 __device__ __forceinline__ int64_t ceil_div_pos(int64_t a, int64_t b) { return a <= 0 ? 0 : (a + b - 1) / b; }
+
+// A final overlap-add position `pos` of a branch (stream_host.py:104-113): divided by the overlap-added squared window
+// of frames max(0, ceil((pos - n + 1) / hop)) .. min(total - 1, pos / hop), written to the mixer input at
+// h + pos - n/2 unless it is centre padding (pos < n/2) or, at flush, past what the mixer reads (index >= keep).
+__device__ __forceinline__ void finalize_sample(int64_t pos, double v, const double* window, int n, int hop,
+                                                int64_t total, int h, int64_t keep, double* ring, int ring_mask) {
+  if (pos < n / 2) return;
+  const int64_t idx = h + pos - n / 2;
+  if (idx >= keep) return;
+  const int64_t e_lo = ceil_div_pos(pos - n + 1, hop);
+  const int64_t e_hi = min(total - 1, pos / hop);
+  double env = 0.0;
+  for (int64_t c = e_lo; c <= e_hi; ++c) {
+    const double w = window[pos - c * hop];
+    env += w * w;
+  }
+  ring[idx & ring_mask] = v / env;
+}
+
 
 // One thread per overlap-add position P0 + t of one branch of one stream (stream_host.py:64-79 and :104-113):
 // t < n - hop carries the partial sum of earlier pushes; this push's frames c cover [P0 + c hop, P0 + c hop + n).
@@ -380,21 +411,105 @@ __global__ void __launch_bounds__(256) istft_ola_kernel(OlaParams p) {
     for (int64_t c = c_lo; c <= c_hi; ++c) v += fr[c * n + (t - c * hop)];
   }
   if (p.flush || pos < P1) {
-    const int64_t total = p.frames_before + p.cols;
-    const int64_t e_lo = ceil_div_pos(pos - n + 1, hop);
-    const int64_t e_hi = min(total - 1, pos / hop);
-    double env = 0.0;
-    for (int64_t c = e_lo; c <= e_hi; ++c) {
-      const double w = b.window[pos - c * hop];
-      env += w * w;
-    }
-    if (pos >= n / 2) {
-      const int64_t idx = p.h + pos - n / 2;
-      if (!p.flush || idx < p.keep) b.ring[(int64_t)s * (p.ring_mask + 1) + (idx & p.ring_mask)] = v / env;
-    }
+    finalize_sample(pos, v, b.window, n, hop, p.frames_before + p.cols, p.h, p.flush ? p.keep : INT64_MAX,
+                    b.ring + (int64_t)s * (p.ring_mask + 1), p.ring_mask);
   } else {
     b.carry_out[(int64_t)s * carry + (pos - P1)] = v;
   }
+}
+
+constexpr int kGroupFrames = 16;  // frames a group CTA overlap-adds itself (>= (n - hop) / hop of the codec's branches)
+
+struct GroupBranch {
+  double* acc;           // [streams, ngroups, acc_len]: each group's overlap-add span
+  const double* window;  // [n]
+  const double* carry_in;  // [streams, n - hop]
+  double* carry_out;       // [streams, n - hop]
+  double* ring;            // [streams, ring]
+};
+
+struct GroupParams {
+  FrameParams f;
+  GroupBranch g[2];
+  int64_t acc_len;  // doubles per group span (even)
+  int ngroups;      // groups per stream: frames [g * kGroupFrames, ...), the last one takes the remainder
+  int hop, h;
+  int64_t frames_before;
+  int ring_mask;
+};
+
+__device__ __forceinline__ int group_begin(int g) { return g * kGroupFrames; }
+__device__ __forceinline__ int group_end(const GroupParams& p, int g) {
+  return g == p.ngroups - 1 ? p.f.cols : (g + 1) * kGroupFrames;
+}
+
+// A long push without the frame scratch round trip: one CTA per (stream, group of >= 16 consecutive frames, branch)
+// synthesises its frames in order (synth_frame) and overlap-adds each windowed frame into its group's span
+// [0, size hop + n - hop) of a global accumulator (written, then read back, by this CTA alone, so it stays in L2);
+// the frames of the group are the only contributors to [n - hop, size hop), which it finalises itself. The first
+// n - hop positions (the previous group's tail or the carried sums overlap there) and the last n - hop ones are left
+// to istft_group_seams_kernel.
+__global__ void __launch_bounds__(kFrameThreads, 4) istft_frames_group_kernel(GroupParams p) {
+  zb::pdl_enter();
+  const FrameBranch& b = p.f.br[blockIdx.y ^ p.f.first];
+  const GroupBranch& gb = p.g[blockIdx.y ^ p.f.first];
+  const int n = b.n, M = n / 2, hop = p.hop;
+  const int s = blockIdx.x / p.ngroups, g = blockIdx.x - s * p.ngroups;
+  const int c0 = group_begin(g), size = group_end(p, g) - c0;
+  double* span = gb.acc + (int64_t)blockIdx.x * p.acc_len;
+  extern __shared__ double2 sm[];
+  const double inv_n = 1.0 / (double)n;
+  for (int i = 0; i < size; ++i) {
+    const double2* z = synth_frame(p.f, b, (int64_t)s * p.f.cols + c0 + i, sm);
+    double* dst = span + (int64_t)i * hop;
+    for (int m = threadIdx.x; m < M; m += blockDim.x) {
+      const double2 v = z[m];
+      const double2 win = *reinterpret_cast<const double2*>(b.window + 2 * m);
+      double2 add = make_double2(v.x * inv_n * win.x, v.y * inv_n * win.y);
+      if (i > 0 && 2 * m < n - hop) {  // already holds the earlier frames of the group
+        const double2 old = *reinterpret_cast<const double2*>(dst + 2 * m);
+        add.x += old.x;
+        add.y += old.y;
+      }
+      *reinterpret_cast<double2*>(dst + 2 * m) = add;
+    }
+    __syncthreads();  // the span's updates are visible, and shared memory is free, before the next frame
+  }
+  const int64_t P0 = (p.frames_before + c0) * hop;
+  const int64_t total = p.frames_before + p.f.cols;
+  double* ring = gb.ring + (int64_t)s * (p.ring_mask + 1);
+  for (int t = n - hop + threadIdx.x; t < size * hop; t += blockDim.x)
+    finalize_sample(P0 + t, span[t], gb.window, n, hop, total, p.h, INT64_MAX, ring, p.ring_mask);
+}
+
+// The seams of a grouped push, one thread per position: seam 0 = the carried sums + group 0's first n - hop
+// positions; seam g = group g-1's last n - hop + group g's first n - hop; both final. Seam ngroups = the last group's
+// last n - hop positions, the next push's carry.
+__global__ void __launch_bounds__(256) istft_group_seams_kernel(GroupParams p) {
+  zb::pdl_enter();
+  const GroupBranch& gb = p.g[blockIdx.z];
+  const int n = p.f.br[blockIdx.z].n, hop = p.hop, carry = n - hop;
+  const int s = blockIdx.y;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)(p.ngroups + 1) * carry) return;
+  const int seam = (int)(idx / carry), t = (int)(idx - (int64_t)seam * carry);
+  const double* acc = gb.acc + (int64_t)s * p.ngroups * p.acc_len;
+  if (seam == p.ngroups) {
+    const int g = p.ngroups - 1;
+    const int size = group_end(p, g) - group_begin(g);
+    gb.carry_out[(int64_t)s * carry + t] = acc[(int64_t)g * p.acc_len + (int64_t)size * hop + t];
+    return;
+  }
+  double v = acc[(int64_t)seam * p.acc_len + t];
+  if (seam == 0) {
+    v += gb.carry_in[(int64_t)s * carry + t];
+  } else {
+    const int size = group_end(p, seam - 1) - group_begin(seam - 1);
+    v += acc[(int64_t)(seam - 1) * p.acc_len + (int64_t)size * hop + t];
+  }
+  const int64_t pos = (p.frames_before + group_begin(seam)) * hop + t;
+  finalize_sample(pos, v, gb.window, n, hop, p.frames_before + p.f.cols, p.h, INT64_MAX,
+                  gb.ring + (int64_t)s * (p.ring_mask + 1), p.ring_mask);
 }
 
 struct MixParams {
@@ -723,10 +838,18 @@ ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1,
   ZB_REQUIRE(newest - mix_from <= ring_size,
              "istft_head_push: ring of %d samples cannot hold mixer inputs [%lld, %lld)", ring_size,
              (long long)mix_from, (long long)newest);
+  // A push of at least two groups of frames overlap-adds in the frame CTAs (istft_frames_group_kernel) when the
+  // scratch holds the groups' spans, the hop is even (16-byte accesses) and a group covers an n_fft; otherwise the
+  // frames go through the scratch to istft_ola_kernel.
+  const int ngroups = cols / kGroupFrames;
+  const int64_t acc_len = ((int64_t)(2 * kGroupFrames - 1) * hop + std::max(n0, n1) - hop + 1) & ~(int64_t)1;
+  const bool grouped = !flush && ngroups >= 2 && hop % 2 == 0 && std::max(n0, n1) <= (kGroupFrames + 1) * hop &&
+                       scratch_elems >= 2 * (int64_t)streams * ngroups * acc_len;
   if (!flush) {
     ZB_REQUIRE(y0 && y1 && scratch, "istft_head_push: null frames or scratch");
-    ZB_REQUIRE(scratch_elems >= (int64_t)streams * cols * (n0 + n1), "istft_head_push: scratch of %lld < %lld",
-               (long long)scratch_elems, (long long)streams * cols * (n0 + n1));
+    ZB_REQUIRE(grouped || scratch_elems >= (int64_t)streams * cols * (n0 + n1),
+               "istft_head_push: scratch of %lld < %lld", (long long)scratch_elems,
+               (long long)streams * cols * (n0 + n1));
     ZB_REQUIRE_ALIGNED(scratch, 16, "istft_head_push scratch");
     ZB_REQUIRE_ALIGNED(window0, 16, "istft_head_push window0");
     ZB_REQUIRE_ALIGNED(window1, 16, "istft_head_push window1");
@@ -752,41 +875,73 @@ ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1,
       for (int st = 0, Ns = 1; st < fp.br[b].nstages; Ns *= fp.br[b].radix[st++])
         fp.br[b].ns_magic[st] = Ns == 1 ? 0u : (uint32_t)(((1ull << 32) + Ns - 1) / Ns);
     }
+    fp.first = n1 > n0 ? 1 : 0;
     fp.cols = cols;
     fp.y_f64 = y_is_f64 != 0;
     fp.max_log_mag = max_log_mag;
     const size_t smem = (size_t)(std::max(n0, n1) + 1) * sizeof(double2);
-    ZB_CUDA(cudaFuncSetAttribute(istft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    ZB_CUDA(zb::launch(istft_frames_kernel, dim3((unsigned)(streams * cols), 2), dim3(kFrameThreads), smem, stream, 1,
-                       fp));
-    if (int rc = zb::check_launch("istft_frames")) return rc;
+    if (grouped) {
+      GroupParams gp{};
+      gp.f = fp;
+      double* carries[2] = {carry0, carry1};
+      double* rings[2] = {ring0, ring1};
+      for (int b = 0; b < 2; ++b) {
+        const int64_t c = ns[b] - hop;
+        gp.g[b].acc = scratch + (int64_t)b * streams * ngroups * acc_len;
+        gp.g[b].window = wins[b];
+        gp.g[b].carry_in = carries[b] + (int64_t)carry_parity * streams * c;
+        gp.g[b].carry_out = carries[b] + (int64_t)(1 - carry_parity) * streams * c;
+        gp.g[b].ring = rings[b];
+      }
+      gp.acc_len = acc_len;
+      gp.ngroups = ngroups;
+      gp.hop = hop;
+      gp.h = h;
+      gp.frames_before = frames_before;
+      gp.ring_mask = ring_size - 1;
+      ZB_CUDA(cudaFuncSetAttribute(istft_frames_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      ZB_CUDA(zb::launch(istft_frames_group_kernel, dim3((unsigned)(streams * ngroups), 2), dim3(kFrameThreads), smem,
+                         stream, 1, gp));
+      if (int rc = zb::check_launch("istft_frames_group")) return rc;
+      const int64_t seam_positions = (int64_t)(ngroups + 1) * (std::max(n0, n1) - hop);
+      ZB_CUDA(zb::launch(istft_group_seams_kernel, dim3((unsigned)((seam_positions + 255) / 256), (unsigned)streams, 2),
+                         dim3(256), 0, stream, 1, gp));
+      if (int rc = zb::check_launch("istft_group_seams")) return rc;
+    } else {
+      ZB_CUDA(cudaFuncSetAttribute(istft_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      ZB_CUDA(zb::launch(istft_frames_kernel, dim3((unsigned)(streams * cols), 2), dim3(kFrameThreads), smem, stream,
+                         1, fp));
+      if (int rc = zb::check_launch("istft_frames")) return rc;
+    }
   }
-  OlaParams op{};
-  double* carries[2] = {carry0, carry1};
-  double* rings[2] = {ring0, ring1};
-  const double* wins[2] = {window0, window1};
-  int64_t span = 0;
-  for (int b = 0; b < 2; ++b) {
-    const int64_t c = ns[b] - hop;
-    op.br[b].frames = scratch ? scratch + (b ? (int64_t)streams * cols * n0 : 0) : nullptr;
-    op.br[b].window = wins[b];
-    op.br[b].carry_in = carries[b] + (int64_t)carry_parity * streams * c;
-    op.br[b].carry_out = carries[b] + (int64_t)(1 - carry_parity) * streams * c;
-    op.br[b].ring = rings[b];
-    op.br[b].n = ns[b];
-    span = std::max(span, flush ? c : (int64_t)cols * hop + c);
+  if (!grouped) {
+    OlaParams op{};
+    double* carries[2] = {carry0, carry1};
+    double* rings[2] = {ring0, ring1};
+    const double* wins[2] = {window0, window1};
+    int64_t span = 0;
+    for (int b = 0; b < 2; ++b) {
+      const int64_t c = ns[b] - hop;
+      op.br[b].frames = scratch ? scratch + (b ? (int64_t)streams * cols * n0 : 0) : nullptr;
+      op.br[b].window = wins[b];
+      op.br[b].carry_in = carries[b] + (int64_t)carry_parity * streams * c;
+      op.br[b].carry_out = carries[b] + (int64_t)(1 - carry_parity) * streams * c;
+      op.br[b].ring = rings[b];
+      op.br[b].n = ns[b];
+      span = std::max(span, flush ? c : (int64_t)cols * hop + c);
+    }
+    op.streams = streams;
+    op.cols = cols;
+    op.hop = hop;
+    op.h = h;
+    op.frames_before = frames_before;
+    op.keep = h + L;
+    op.ring_mask = ring_size - 1;
+    op.flush = flush != 0;
+    ZB_CUDA(zb::launch(istft_ola_kernel, dim3((unsigned)((span + 255) / 256), (unsigned)streams, 2), dim3(256), 0, stream,
+                       1, op));
+    if (int rc = zb::check_launch("istft_ola")) return rc;
   }
-  op.streams = streams;
-  op.cols = cols;
-  op.hop = hop;
-  op.h = h;
-  op.frames_before = frames_before;
-  op.keep = h + L;
-  op.ring_mask = ring_size - 1;
-  op.flush = flush != 0;
-  ZB_CUDA(zb::launch(istft_ola_kernel, dim3((unsigned)((span + 255) / 256), (unsigned)streams, 2), dim3(256), 0, stream,
-                     1, op));
-  if (int rc = zb::check_launch("istft_ola")) return rc;
   if (mix_to == mix_from) return zb::kOk;
   ZB_REQUIRE(out, "istft_head_push: null output");
   MixParams mp{ring0, ring1, mixer, out, mix_from, mix_to, flush ? h + L : INT64_MAX, taps, ring_size - 1};
