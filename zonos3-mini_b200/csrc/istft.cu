@@ -280,7 +280,7 @@ __device__ __forceinline__ const double2* synth_frame(const FrameParams& p, cons
   double2* A = sm + M + 1;  // [M]
   const double2* tw = b.twiddle;
   const int64_t row_off = (frame / p.cols) * b.y_stride + (frame % p.cols) * (n + 2);
-  for (int k = threadIdx.x; k < bins; k += blockDim.x) {
+  auto bin = [&](int k) {  // X[k] = exp(min(lm, max)) (cos ph, sin ph), imaginary part zero at DC and Nyquist
     double lm, ph;
     if (p.y_f64) {
       const double* row = static_cast<const double*>(b.y) + row_off;
@@ -294,15 +294,24 @@ __device__ __forceinline__ const double2* synth_frame(const FrameParams& p, cons
     const double mag = exp(fmin(lm, p.max_log_mag));
     double s, c;
     sincos(ph, &s, &c);
-    X[k] = make_double2(mag * c, (k == 0 || k == M) ? 0.0 : mag * s);
-  }
-  __syncthreads();
-  for (int k = threadIdx.x; k < M; k += blockDim.x) {
-    const double2 xk = X[k], xc = X[M - k];
-    const double2 e = make_double2(xk.x + xc.x, xk.y - xc.y);  // X[k] + conj X[M-k]
-    const double2 d = make_double2(xk.x - xc.x, xk.y + xc.y);  // X[k] - conj X[M-k]
-    const double2 o = cmul(__ldg(tw + k), d);
-    A[k] = make_double2(e.x - o.y, e.y + o.x);
+    return make_double2(mag * c, (k == 0 || k == M) ? 0.0 : mag * s);
+  };
+  // thread k forms the pair (k, M - k) of the packed spectrum from bins k and M - k:
+  //   Z[k] = (X[k] + conj X[M-k]) + i w^k (X[k] - conj X[M-k]), and the same with k and M - k exchanged
+  for (int k = threadIdx.x; k <= M / 2; k += blockDim.x) {
+    const double2 xk = bin(k), xc = bin(M - k);
+    {
+      const double2 e = make_double2(xk.x + xc.x, xk.y - xc.y);
+      const double2 d = make_double2(xk.x - xc.x, xk.y + xc.y);
+      const double2 o = cmul(__ldg(tw + k), d);
+      A[k] = make_double2(e.x - o.y, e.y + o.x);
+    }
+    if (k != 0 && 2 * k != M) {
+      const double2 e = make_double2(xc.x + xk.x, xc.y - xk.y);
+      const double2 d = make_double2(xc.x - xk.x, xc.y + xk.y);
+      const double2 o = cmul(__ldg(tw + (M - k)), d);
+      A[M - k] = make_double2(e.x - o.y, e.y + o.x);
+    }
   }
   __syncthreads();
 
