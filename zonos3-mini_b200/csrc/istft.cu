@@ -821,8 +821,8 @@ ZB_API int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1,
                               int ring_size, int64_t frames_before, int64_t mix_from, int64_t mix_to, int flush,
                               double* scratch, int64_t scratch_elems, float* out, cudaStream_t stream) {
   const int ns[2] = {n0, n1};
-  ZB_REQUIRE(streams >= 1 && cols >= 0 && hop >= 1 && frames_before >= 0,
-             "istft_head_push: streams=%d cols=%d hop=%d frames_before=%lld", streams, cols, hop,
+  ZB_REQUIRE(streams >= 1 && streams <= 65535 && cols >= 0 && hop >= 1 && frames_before >= 0,
+             "istft_head_push: streams=%d (1..65535) cols=%d hop=%d frames_before=%lld", streams, cols, hop,
              (long long)frames_before);
   for (int b = 0; b < 2; ++b) {
     ZB_REQUIRE(ns[b] % 2 == 0 && ns[b] % hop == 0 && ns[b] / hop >= 2,
@@ -967,8 +967,10 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
                             int ring_size, int64_t n_in_before, const double* kernel_t, int orig, int new_freq,
                             int width, int64_t block_from, int64_t block_to, int64_t out_count, float* out,
                             double* workspace, int64_t workspace_elems, cudaStream_t stream) {
-  ZB_REQUIRE(streams >= 1 && count >= 0 && n_in_before >= 0 && orig >= 1 && new_freq >= 1 && width >= 0,
-             "resample_push: streams=%d count=%d orig=%d new=%d width=%d", streams, count, orig, new_freq, width);
+  ZB_REQUIRE(streams >= 1 && streams <= 65535 && count >= 0 && n_in_before >= 0 && orig >= 1 && new_freq >= 1 &&
+                 width >= 0,
+             "resample_push: streams=%d (1..65535) count=%d orig=%d new=%d width=%d", streams, count, orig, new_freq,
+             width);
   ZB_REQUIRE(ring && kernel_t, "resample_push: null ring or kernel");
   ZB_REQUIRE(ring_size >= 1 && (ring_size & (ring_size - 1)) == 0, "resample_push: ring %d not a power of two",
              ring_size);
