@@ -647,9 +647,9 @@ __global__ void __launch_bounds__(256) resample_append_kernel(AppendParams p) {
 }
 
 constexpr int kResBM = 32;      // (stream, block) pairs per CTA
-constexpr int kResBN = 64;      // output phases per CTA
+constexpr int kResBNMax = 128;  // output phases per CTA: 16 x TN (TN = 4 or 8 per thread)      // output phases per CTA
 constexpr int kResBK = 16;      // taps per step
-constexpr int kResThreads = 128;  // 8 x 16 threads, 4 x 4 outputs each
+constexpr int kResThreads = 128;  // 8 x 16 threads, 4 x TN outputs each
 
 struct ResampleParams {
   const double* ring;      // [streams, ring]
@@ -668,9 +668,9 @@ struct ResampleParams {
 
 // out[b * new + i] = sum_k kernel[i][k] * x[b * orig + k - width] (stream_host.py:145-171), inputs outside [0, n_in)
 // zero, as a float64 GEMM C[pairs, new] = A[pairs, kl] K^T with the rows of A the input windows of the (stream,
-// block) pairs, read from the ring as the tiles are staged. A CTA owns a 32-pair x 64-phase tile and walks the taps
+// block) pairs, read from the ring as the tiles are staged. A CTA owns a 32-pair x 128-phase tile and walks the taps
 // 16 at a time: the next step's A and K^T tiles are copied (cp.async, zero-filled outside the data) into the other
-// shared-memory buffer while the current ones (A transposed) feed 4 x 4 outputs per thread. When few tiles would cover the GPU, the taps split into slices
+// shared-memory buffer while the current ones (A transposed) feed 4 x 8 outputs per thread. When few tiles would cover the GPU, the taps split into slices
 // (blockIdx.z) whose sums resample_reduce_kernel adds in slice order, so the result does not depend on timing.
 __device__ __forceinline__ void cp_async8(double* dst, const double* src, bool live) {
   // 8-byte global -> shared copy; a dead element copies nothing and zero-fills (src-size 0)
@@ -679,10 +679,12 @@ __device__ __forceinline__ void cp_async8(double* dst, const double* src, bool l
                : "memory");
 }
 
-__global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p) {
+template <int TN>
+__global__ void __launch_bounds__(kResThreads, TN == 4 ? 5 : 4) resample_kernel(ResampleParams p) {
+  constexpr int kResBN = 16 * TN;
   zb::pdl_enter();
   __shared__ __align__(16) double As[2][kResBK][kResBM + 2];  // [buffer][tap][pair], padded rows
-  __shared__ __align__(16) double Bs[2][kResBK][kResBN];      // [buffer][tap][phase]
+  __shared__ __align__(16) double Bs[2][kResBK][kResBN];  // [buffer][tap][phase]
   const int tid = threadIdx.x;
   const int64_t pair0 = (int64_t)blockIdx.y * kResBM;
   const int i0 = blockIdx.x * kResBN;
@@ -703,9 +705,9 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
     a_row[u] = sidx * ring;
     a_start[u] = blk * p.orig - p.width;
   }
-  // B staging: element e = tid + 128 u (u < 8) of the [16 taps][64 phases] tile
-  const int b_col = tid % kResBN;
-  const int b_tap0 = tid / kResBN;  // 0 or 1; taps b_tap0 + 2 u
+  // B staging: element e = tid + 128 u of the [16 taps][16 TN phases] tile: phase e % BN, tap e / BN
+  constexpr int kBStep = kResThreads / kResBN;  // taps between a thread's consecutive elements
+  const int b_col = tid % kResBN, b_tap0 = tid / kResBN;
   const bool b_live = i0 + b_col < p.nnew;
   const int k_begin = blockIdx.z * p.kchunk;
   const int k_end = min(p.kl, k_begin + p.kchunk);
@@ -720,23 +722,23 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
                 live);
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int k = k0 + b_tap0 + 2 * u;
+    for (int u = 0; u < kResBK / kBStep; ++u) {
+      const int tap = b_tap0 + kBStep * u;
+      const int k = k0 + tap;
       const bool live = b_live && k < k_end;
-      cp_async8(&Bs[buf][b_tap0 + 2 * u][b_col], live ? p.kernel_t + (int64_t)k * p.nnew + i0 + b_col : p.kernel_t,
-                live);
+      cp_async8(&Bs[buf][tap][b_col], live ? p.kernel_t + (int64_t)k * p.nnew + i0 + b_col : p.kernel_t, live);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
-  // thread (tr, tc): pairs tr*4 .. tr*4+3, phases {2tc, 2tc+1, 32+2tc, 33+2tc} (each fragment load is a contiguous
-  // 16 bytes per lane, so a half-warp's 256 bytes hit every bank once)
+  // thread (tr, tc): pairs tr*4 .. tr*4+3, phases 32 q + 2 tc + {0, 1} for q < TN / 2 (each fragment load is a
+  // contiguous 16 bytes per lane, so a half-warp's 256 bytes hit every bank once)
   const int tr = tid / 16, tc = tid % 16;
-  double acc[4][4];
+  double acc[4][TN];
 #pragma unroll
   for (int x = 0; x < 4; ++x)
 #pragma unroll
-    for (int y = 0; y < 4; ++y) acc[x][y] = 0.0;
+    for (int y = 0; y < TN; ++y) acc[x][y] = 0.0;
 
   const int steps = (k_end - k_begin + kResBK - 1) / kResBK;
   issue(k_begin, 0);
@@ -753,13 +755,18 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
     for (int k = 0; k < kResBK; ++k) {
       const double2 a01 = *reinterpret_cast<const double2*>(&As[buf][k][tr * 4]);
       const double2 a23 = *reinterpret_cast<const double2*>(&As[buf][k][tr * 4 + 2]);
-      const double2 b01 = *reinterpret_cast<const double2*>(&Bs[buf][k][tc * 2]);
-      const double2 b23 = *reinterpret_cast<const double2*>(&Bs[buf][k][32 + tc * 2]);
-      const double av[4] = {a01.x, a01.y, a23.x, a23.y}, bv[4] = {b01.x, b01.y, b23.x, b23.y};
+      double bv[TN];
+#pragma unroll
+      for (int q = 0; q < TN / 2; ++q) {
+        const double2 b = *reinterpret_cast<const double2*>(&Bs[buf][k][32 * q + tc * 2]);
+        bv[2 * q] = b.x;
+        bv[2 * q + 1] = b.y;
+      }
+      const double av[4] = {a01.x, a01.y, a23.x, a23.y};
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) acc[x][y] = fma(av[x], bv[y], acc[x][y]);
+        for (int y = 0; y < TN; ++y) acc[x][y] = fma(av[x], bv[y], acc[x][y]);
     }
     __syncthreads();  // this buffer is refilled two steps on
   }
@@ -770,8 +777,8 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
     if (p.partial) {
       double* dst = p.partial + ((int64_t)blockIdx.z * pairs_total + pr) * p.nnew;
 #pragma unroll
-      for (int y = 0; y < 4; ++y) {
-        const int i = i0 + (y < 2 ? tc * 2 + y : 32 + tc * 2 + y - 2);
+      for (int y = 0; y < TN; ++y) {
+        const int i = i0 + 32 * (y >> 1) + tc * 2 + (y & 1);
         if (i < p.nnew) dst[i] = acc[x][y];
       }
       continue;
@@ -779,8 +786,8 @@ __global__ void __launch_bounds__(kResThreads) resample_kernel(ResampleParams p)
     const int64_t sidx = pr / p.nblocks;
     const int64_t o0 = (pr % p.nblocks) * p.nnew;
 #pragma unroll
-    for (int y = 0; y < 4; ++y) {
-      const int i = i0 + (y < 2 ? tc * 2 + y : 32 + tc * 2 + y - 2);
+    for (int y = 0; y < TN; ++y) {
+      const int i = i0 + 32 * (y >> 1) + tc * 2 + (y & 1);
       const int64_t o = o0 + i;
       if (i < p.nnew && o < p.out_count) p.out[sidx * p.out_count + o] = (float)acc[x][y];
     }
@@ -1013,8 +1020,12 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
   const int64_t pairs = (int64_t)streams * rp.nblocks;
   ZB_REQUIRE((pairs + kResBM - 1) / kResBM < 65536, "resample_push: %lld (stream, block) pairs in one call",
              (long long)pairs);
+  // 4 x 8 outputs per thread when the tiles cover the GPU several times over, else 4 x 4 (twice the CTAs); then
   // split the taps while the tiles alone would leave most of the GPU idle (four resample CTAs fit an SM)
-  const int64_t tiles = (int64_t)((new_freq + kResBN - 1) / kResBN) * ((pairs + kResBM - 1) / kResBM);
+  const int64_t pair_tiles = (pairs + kResBM - 1) / kResBM;
+  const bool wide = pair_tiles * ((new_freq + kResBNMax - 1) / kResBNMax) >= 8 * zb::sm_count();
+  const int bn = wide ? kResBNMax : kResBNMax / 2;
+  const int64_t tiles = (int64_t)((new_freq + bn - 1) / bn) * pair_tiles;
   const int steps = (kl + kResBK - 1) / kResBK;
   int slices = (int)std::min<int64_t>({8, steps, std::max<int64_t>(1, 4 * zb::sm_count() / tiles)});
   if (!workspace || workspace_elems < (int64_t)slices * pairs * new_freq) slices = 1;
@@ -1022,10 +1033,12 @@ ZB_API int zb_resample_push(const void* x, int x_is_f64, int64_t x_stride, int s
   slices = (kl + rp.kchunk - 1) / rp.kchunk;
   rp.partial = slices > 1 ? workspace : nullptr;
   if (slices > 1) ZB_REQUIRE_ALIGNED(workspace, 16, "resample_push workspace");
-  ZB_CUDA(zb::launch(resample_kernel,
-                     dim3((unsigned)((new_freq + kResBN - 1) / kResBN), (unsigned)((pairs + kResBM - 1) / kResBM),
-                          (unsigned)slices),
-                     dim3(kResThreads), 0, stream, 1, rp));
+  const dim3 rgrid((unsigned)((new_freq + bn - 1) / bn), (unsigned)pair_tiles, (unsigned)slices);
+  if (wide) {
+    ZB_CUDA(zb::launch(resample_kernel<8>, rgrid, dim3(kResThreads), 0, stream, 1, rp));
+  } else {
+    ZB_CUDA(zb::launch(resample_kernel<4>, rgrid, dim3(kResThreads), 0, stream, 1, rp));
+  }
   if (int rc = zb::check_launch("resample")) return rc;
   if (slices == 1) return zb::kOk;
   const int64_t n = pairs * new_freq;
