@@ -272,15 +272,13 @@ def cfg5_step_bytes(streams: int, context: int, layers: int = LAYERS5) -> int:
 
 def cfg5_config(world: int) -> dict:
     return {
-        "workload": "cfg5 decode step: 256 streams per GPU, 24-layer hybrid LM (hidden 2048; 18 gated-DeltaNet "
-                    "16 x 128/128 + 6 GQA 16/4 x 128 over a 878..1628-key cache; MoE 64 experts top-8 SwiGLU 768 in "
-                    "every layer; Full AttnRes, 49 routes; head 10 x 4098 with soft cap 15; TTS sampler t=0.8 top-k 50 "
-                    "top-p 0.9 repetition window 32 x 1.2); embedding -> backbone -> head -> sampler in one CUDA graph",
-        "model": "ZONOS3-Mini cfg5 (random init; 7.9 B total / ~1.6 B active parameters)",
+        "workload": "cfg5 decode step, one CUDA graph: embedding, 24 layers (18 DeltaNet + 6 GQA, MoE 64 x top-8, "
+                    "Full AttnRes), head + soft cap, TTS sampler",
+        "model": "ZONOS3-Mini cfg5 (random init, 7.9 B params)",
         "streams_per_gpu": STREAMS5, "global_batch": STREAMS5 * world, "seq_len": MAX_LEN5,
-        "context_start": CONTEXT5, "layers": LAYERS5, "token": "one decode step of one stream (one 10-code frame)",
-        "l2": "no flush: each step reads 15.6 GB of weights (> 126 MB L2)",
-        "parallelism": f"replicas x{world} (request-sharded, no collective)",
+        "context_start": CONTEXT5, "layers": LAYERS5, "token": "one decode step of one stream",
+        "l2": "no flush (15.6 GB of weights per step)",
+        "parallelism": f"replicas x{world}",
     }
 
 
@@ -367,18 +365,17 @@ def run_ours(args, dist, rank, world, local):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (random-init weights N(0, 0.02); random KV cache / DeltaNet states; sampled codes fed back)",
+        "data": "synthetic (random-init weights, random caches, sampled codes fed back)",
         "config": cfg5_config(world),
         "roofline": {
-            "kernel": "whole decode step (one CUDA graph)", "bound": "hbm", "achieved": achieved,
+            "kernel": "decode step (one graph)", "bound": "hbm", "achieved": achieved,
             "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
             "traffic": profiled_traffic("decode_step_cfg5.md"), "algorithmic_bytes_per_step": nbytes,
             "peak_source": pk["source"],
         },
         "e2e": {"value": STREAMS5 * n_e2e * world / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / n_e2e,
-                "path": "DecodeGraph.step: pinned host ids + positions / cache lengths / KV slots in, codes out, "
-                        "host sync per step"},
+                "path": "DecodeGraph.step: host ids in, codes out, sync per step"},
         "strong_scaling": strong,
         "gpu_launches": graph.launches_per_step * args.steps,
         "launches_per_step": graph.launches_per_step,
@@ -1189,9 +1186,8 @@ def main():
             value, threads, dt, per_step = cpu_reference_cfg5(args.cpu_samples)
             line["cpu_baseline"] = {
                 "value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                "sample": f"{args.cpu_samples} stream-steps of a 4-layer slice and of the 0-layer remainder of the "
-                          f"cfg5 model (oracle/lm.py restating lm.py:660-735, fp32), scaled to 24 layers; "
-                          f"{per_step * 1e3:.0f} ms per stream-step ({dt:.1f} s of timed forwards)",
+                "sample": f"{args.cpu_samples} stream-steps of oracle/lm.py (fp32; 4-layer slice + remainder, "
+                          f"scaled to 24 layers): {per_step * 1e3:.0f} ms each",
             }
             if args.operators and world == 1:
                 pkg = __import__("__graft_entry__").load_package()
