@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Default workload ("cfg5"): the decode step of the 24-layer hybrid LM (hidden 2048; 18 gated-
+Default workload (the benchmark's config 5, "cfg5"): the decode step of the 24-layer hybrid LM (hidden 2048; 18 gated-
 DeltaNet layers of 16 heads at 128/128 and 6 GQA layers of 16 q / 4 kv heads at 128 in the 3:1 pattern; an MoE FFN
 of 64 experts, top-8, SwiGLU 768 in every layer; Full AttnRes; a 10-codebook head over 4098 ids) for 256 concurrent
 streams per GPU, run through the package's public API: ``Zonos3ForCausalLM`` and its captured ``DecodeGraph``

@@ -1,6 +1,6 @@
 """Whole-LM oracle (CPU, float32): a restatement of ``Zonos3LM.forward`` (model/src/zonos3/reference/lm.py:660-735)
 with the architecture sizes as parameters, so it expresses both the reference's own model (layer 0 dense, GDN fixed
-at 4 heads of 128, lm.py:28, :332) and BASELINE config 1 (MoE in every layer, GDN 4 heads of 64).
+at 4 heads of 128, lm.py:28, :332) and the benchmark's config 1 (MoE in every layer, GDN 4 heads of 64).
 
 Covered: summed multi-codebook + text embeddings, weightless embedding RMSNorm, the Full AttnRes schedule (a route
 before every sublayer and a final one, lm.py:699-721), GDN layers (oracle.gdn.gdn_layer), global GQA attention

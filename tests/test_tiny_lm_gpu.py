@@ -1,4 +1,4 @@
-"""BASELINE config 1 end to end: a tiny random-init hybrid LM (hidden 256; layers [GDN, GDN, GQA, GDN]; GDN 4 heads
+"""The benchmark's config 1 end to end: a tiny random-init hybrid LM (hidden 256; layers [GDN, GDN, GQA, GDN]; GDN 4 heads
 of 64; MoE 8 experts top-2, SwiGLU 512, in every layer; Full AttnRes; vocab 1024) run on the B200 path (the
 drop-in OriginalGDN and MoEFeedForward modules, the AttnRes route kernel with the norms fused, the KV store and
 the decode attention of the GQA layer, bf16) against the

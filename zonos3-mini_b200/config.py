@@ -2,7 +2,7 @@
 model/src/zonos3/models/config.py: hidden_size, rms_norm_eps, the moe_* fields, get_routed_moe_dim :52,
 get_num_experts_per_tok :180; the attention, vocabulary and soft-cap fields :82-106, audio_vocab_size :176), plus
 the GDN head count / width that the release hard-codes (4 x 128, servers/sgl/src/zonos3_sgl/models/gdn.py:136-141)
-and the BASELINE configs change (16 x 128, 4 x 64)."""
+and the benchmark configs change (16 x 128, 4 x 64)."""
 
 from __future__ import annotations
 
