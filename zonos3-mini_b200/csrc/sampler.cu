@@ -181,12 +181,158 @@ __device__ __forceinline__ float block_scan_incl_f(float v, float* wsum) {
   return v;
 }
 
+// The tail of sample_sorted_topk in warp 0 alone (no block barriers), for `count` <= 64 candidates that hold every
+// survivor of the top k (candidates in any order; those past the k-th largest are dropped here): the candidates,
+// NS per lane (position j = 32 slot + lane), bitonic-sorted by (logit descending, index ascending) with shuffles;
+// the survivors are the positions whose logit is >= the k-th largest (ties at the cut all kept); then the same
+// softmax, top-p, min-p, empty-row fallback and draw as the block version, with warp scans in position order. The
+// other warps only help zero the probability row when one is written.
+template <int NS>  // 2: up to 64 candidates
+__device__ bool sorted_tail_warp(const SamplerParams& p, const float* cand_v, const int* cand_i, int count, int row,
+                                 int c, int32_t* out, float* probs) {
+  static_assert(NS == 2, "the sort pairs slots only at stride 32");
+  const int tid = threadIdx.x, lane = tid % 32;
+  if (probs) {
+    for (int i = tid; i < p.V; i += kThreads) probs[i] = 0.f;
+    __syncthreads();
+  }
+  if (tid >= 32) return true;
+  auto before = [](float va, int ia, float vb, int ib) { return va > vb || (va == vb && ia < ib); };
+  float v[NS];
+  int id[NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    const int j = 32 * s + lane;
+    v[s] = j < count ? cand_v[j] : -INFINITY;
+    id[s] = j < count ? cand_i[j] : 0x7fffffff;
+  }
+  auto cas = [&](float& va, int& ia, float& vb, int& ib, bool desc) {  // a is the lower position
+    if (before(vb, ib, va, ia) == desc) {
+      const float tv = va;
+      const int ti = ia;
+      va = vb;
+      ia = ib;
+      vb = tv;
+      ib = ti;
+    }
+  };
+#pragma unroll
+  for (int size = 2; size <= 32 * NS; size <<= 1) {
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride >>= 1) {
+      if (stride == 32) {  // partner in the other slot of the same lane: the run of 64 positions
+        cas(v[0], id[0], v[1], id[1], (lane & size) == 0);
+      } else {
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const int j = 32 * s + lane;
+          const float ov = __shfl_xor_sync(0xffffffffu, v[s], stride);
+          const int oi = __shfl_xor_sync(0xffffffffu, id[s], stride);
+          const bool desc = (j & size) == 0;  // this run sorts in "before" order
+          const bool take = (j & stride) == 0 ? before(ov, oi, v[s], id[s]) == desc   // lower: the run's pick
+                                              : before(v[s], id[s], ov, oi) == desc;  // upper: the other one
+          if (take) {
+            v[s] = ov;
+            id[s] = oi;
+          }
+        }
+      }
+    }
+  }
+  // survivors: positions < total, total = k plus the ties of the k-th largest logit that follow it
+  const int k = min(p.top_k, count);
+  const float kth = __shfl_sync(0xffffffffu, v[(k - 1) / 32], (k - 1) % 32);
+  int total = 0;
+#pragma unroll
+  for (int s = 0; s < NS; ++s) total += __popc(__ballot_sync(0xffffffffu, 32 * s + lane < count && v[s] >= kth));
+  auto scan = [&](const float* e, float* run) {  // inclusive cumulative sums in position order
+    float carry = 0.f;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      float x = e[s];
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float o = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += o;
+      }
+      run[s] = x + carry;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+  };
+  auto wsum = [&](const float* e) {
+    float t = 0.f;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) t += e[s];
+    return zb::warp_sum(t);
+  };
+  const float mx = __shfl_sync(0xffffffffu, v[0], 0);
+  float e[NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) e[s] = (32 * s + lane < total && mx != -INFINITY) ? expf(v[s] - mx) : 0.f;
+  const float sum = wsum(e);
+#pragma unroll
+  for (int s = 0; s < NS; ++s) e[s] = sum > 0.f ? e[s] / sum : 0.f;
+  if (p.top_p > 0.f && p.top_p < 1.f) {
+    float run[NS];
+    scan(e, run);
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+      if (run[s] - e[s] > p.top_p) e[s] = 0.f;  // the mass before it
+    const float ksum = fmaxf(wsum(e), 1e-8f);
+#pragma unroll
+    for (int s = 0; s < NS; ++s) e[s] = e[s] / ksum;
+  }
+  if (p.min_p > 0.f) {
+    const float cut = p.min_p * __shfl_sync(0xffffffffu, e[0], 0);  // the largest probability sits first
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+      if (e[s] < cut) e[s] = 0.f;
+    const float ksum = fmaxf(wsum(e), 1e-8f);
+#pragma unroll
+    for (int s = 0; s < NS; ++s) e[s] = e[s] / ksum;
+  }
+  float mass = wsum(e);
+  if (!(mass > 0.f)) {  // a row without mass: one-hot at the argmax (the first survivor)
+#pragma unroll
+    for (int s = 0; s < NS; ++s) e[s] = (s == 0 && lane == 0) ? 1.f : 0.f;
+    mass = 1.f;
+  }
+  if (probs) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+      if (32 * s + lane < total) probs[id[s]] = e[s];
+  }
+  const uint64_t counter = p.offset + (p.offset_dev ? *p.offset_dev : 0ull);
+  const float u = (float)(philox(p.seed, (uint64_t)row, counter) >> 8) * (1.0f / 16777216.0f);
+  const float target = u * mass;
+  float run[NS];
+  scan(e, run);
+  int pick = 0;
+  bool found = false;
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    const unsigned m = __ballot_sync(0xffffffffu, target < run[s] && e[s] > 0.f);
+    if (!found && m) {
+      pick = 32 * s + __ffs(m) - 1;
+      found = true;
+    }
+  }
+  int chosen = 0;
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    const int o = __shfl_sync(0xffffffffu, id[s], pick & 31);
+    if (pick / 32 == s) chosen = o;
+  }
+  if (lane == 0) out[c] = chosen;
+  return true;
+}
+
 // The sampling path after a small top-k (temperature already applied to x): the k-th largest logit by a 4-pass
 // radix select, the survivors (logit >= it) compacted in index order and bitonic-sorted by (logit descending,
 // index ascending) -- the order of the reference's stable descending sort --, then softmax, top-p with the
 // reference's rule (inclusive cumulative sum minus the id's own probability > top_p drops it), min-p, the
-// empty-row fallback and the draw, all on the short sorted list. Returns false (nothing written) when more than
-// kMaxCand ids tie into the top k.
+// empty-row fallback and the draw, all on the short sorted list (sorted_tail_warp in one warp for at most 64
+// survivors). Returns false (nothing written) when more than kMaxCand ids tie into the top k.
 __device__ bool sample_sorted_topk(const SamplerParams& p, float* x, int row, int c, int32_t* out, float* probs,
                                    float* cand_v, int* cand_i, int* ints, float* red) {
   const int V = p.V, tid = threadIdx.x;
@@ -233,6 +379,10 @@ __device__ bool sample_sorted_topk(const SamplerParams& p, float* x, int row, in
       cand_i[pos] = i;
       ++pos;
     }
+  }
+  if (total <= 64) {
+    __syncthreads();  // the compacted survivors are in shared memory
+    return sorted_tail_warp<2>(p, cand_v, cand_i, total, row, c, out, probs);
   }
   int P = 1;
   while (P < total) P <<= 1;
