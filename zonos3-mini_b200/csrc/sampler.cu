@@ -339,28 +339,41 @@ __device__ bool sample_sorted_topk(const SamplerParams& p, float* x, int row, in
   int* hist = ints;         // [256]
   int* wsum = ints + 256;   // [8]
   int* sel = ints + 264;    // [2]
+  int* wsum2 = ints + 272;  // [8], the other scan buffer
   uint32_t prefix = 0u, pmask = 0u;
   int kk = p.top_k;
+  hist[tid] = 0;
+  __syncthreads();
   for (int shift = 24; shift >= 0; shift -= 8) {
-    hist[tid] = 0;
-    __syncthreads();
     for (int i = tid; i < V; i += kThreads) {
       const uint32_t key = ordered(x[i]);
       if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
     }
     __syncthreads();
     const int v = hist[255 - tid];
-    const int s = block_scan_incl(v, wsum);  // ids whose digit is >= 255 - tid
-    if (s >= kk && s - v < kk) {
-      sel[0] = 255 - tid;
-      sel[1] = s - v;
+    hist[255 - tid] = 0;  // each bin is read by its own thread only: cleared for the next pass
+    // inclusive scan over the digits from the top (scan buffers alternate between passes, so the barrier that
+    // guards a buffer's reuse is the previous pass's last one)
+    int sc = v;
+    const int lane = tid % 32, warp = tid / 32;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, sc, off);
+      if (lane >= off) sc += o;
     }
+    int* ws = (shift & 8) ? wsum2 : wsum;
+    if (lane == 31) ws[warp] = sc;
     __syncthreads();
+    for (int w = 0; w < warp; ++w) sc += ws[w];  // ids whose digit is >= 255 - tid
+    if (sc >= kk && sc - v < kk) {
+      sel[0] = 255 - tid;
+      sel[1] = sc - v;
+    }
+    __syncthreads();  // sel is read by every thread before the next pass's scan can write it again
     prefix |= (uint32_t)sel[0] << shift;
     pmask |= 255u << shift;
     kk -= sel[1];
-    __syncthreads();
   }
+  __syncthreads();  // sel and the scan buffers are free for the compaction's scan
   // compact the survivors in index order (contiguous chunks per thread)
   const int chunk = (V + kThreads - 1) / kThreads;
   const int cb = min(tid * chunk, V), ce = min(cb + chunk, V);
@@ -558,7 +571,7 @@ __global__ void __launch_bounds__(kThreads) sample_tts_kernel(SamplerParams p) {
   if (p.top_k > 0 && p.top_k <= kSortedTopK && p.top_k < V) {
     __shared__ float cand_v[kMaxCand];
     __shared__ int cand_i[kMaxCand];
-    __shared__ int ints[272];
+    __shared__ int ints[280];
     if (sample_sorted_topk(p, x, row, c, out, probs, cand_v, cand_i, ints, red)) return;
   }
   if (p.top_k > 0 && p.top_k < V) {
