@@ -181,6 +181,30 @@ def test_float64_inputs_and_generic_radices(voc):
         close(got, want)
 
 
+@pytest.mark.parametrize("n_ffts,hop,taps", [((1024, 8192), 512, 31), ((96, 288), 48, 9)])
+def test_other_sizes_and_both_overlap_add_paths(voc, n_ffts, hop, taps):
+    """Sizes beyond the codec's: n_fft 8192 (the largest the kernels take: half length 4096 = 4^6, 131 KB of shared
+    memory per frame CTA) with 1024, and 96 / 288 (half lengths 48 = 4^2 * 3 and 144 = 4^2 * 9 -> 3 * 3: radix 3 twice);
+    pushes of 3 and 40 frames (the second through the grouped overlap-add) and the flush, against the oracle."""
+    rng = np.random.default_rng(13)
+    windows = [0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n) / n) for n in n_ffts]
+    mixer = rng.normal(0, 0.1, (2, taps))
+    mixer[0, taps // 2] += 1.0
+    kernel = rng.normal(0, 0.2, (2, 2 * 4 + 3))
+    dev = torch.device("cuda:0")
+    chunks = [frames(rng, k, n_ffts, streams=3) for k in (3, 40)]
+    head = voc.IstftHeadStream(n_ffts, hop, windows, mixer, 1.5, dev, streams=3)
+    res = voc.ResamplerStream(kernel, 3, 2, 4, dev, streams=3)
+    outs = [res.push(head.push(torch.as_tensor(y0).cuda(), torch.as_tensor(y1).cuda())) for y0, y1 in chunks]
+    outs.append(torch.cat([res.push(head.flush()), res.flush()], 1))
+    torch.cuda.synchronize()
+    for s_ in range(3):
+        _, want_r = istft.stream_outputs([c[0][s_] for c in chunks], [c[1][s_] for c in chunks], n_ffts, hop,
+                                         windows, mixer, 1.5, kernel, 3, 2, 4)
+        for got, want in zip(outs, want_r):
+            close(got[s_], want)
+
+
 def test_stream_errors(voc, codec):
     head, res = make(voc, codec)
     assert head.flush().numel() == 0  # nothing pushed: nothing to flush
