@@ -107,6 +107,20 @@ def test_golden_stream(voc, stream_golden, codec):
     close(ress[n], golden["res_flush"])
 
 
+def test_stream_tail_chains_as_the_codec_does(voc, stream_golden, codec):
+    """StreamTail (head then resampler per push; head flush through the resampler, then its flush) on the golden
+    pushes: the reference's resampler outputs."""
+    golden = stream_golden
+    tail = voc.StreamTail(*make(voc, codec))
+    n = len(golden["chunks"])
+    for c in range(n):
+        close(tail.push(torch.as_tensor(golden[f"y0_{c}"]).cuda(), torch.as_tensor(golden[f"y1_{c}"]).cuda()),
+              golden[f"res_{c}"])
+    close(tail.flush(), golden["res_flush"])
+    with pytest.raises(ValueError, match="share"):
+        voc.StreamTail(make(voc, codec, streams=2)[0], make(voc, codec)[1])
+
+
 @pytest.mark.parametrize("max_cols,max_push", [(64, 1 << 16), (5, 700)])
 def test_long_stream_matches_oracle(voc, codec, max_cols, max_push):
     """Two seconds of frames in uneven chunks; small max_cols / max_push split pushes and wrap the rings many times."""

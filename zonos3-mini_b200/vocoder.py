@@ -249,3 +249,23 @@ class ResamplerStream:
         with torch.cuda.device(self.device):
             out = self._run(None, 0, True)
         return out[0] if self.streams == 1 else out
+
+
+class StreamTail:
+    """The head stream and the resampler chained as the codec's decode loop chains them
+    (model/src/zonos3/codec/istft_head_a_20261002/stream.py:205-215 per chunk, :211-214 at the end): each push returns
+    the 44.1 kHz samples now final, `flush()` the rest."""
+
+    def __init__(self, head: IstftHeadStream, resampler: ResamplerStream):
+        if head.streams != resampler.streams or head.device != resampler.device:
+            raise ValueError("stream tail: the head and the resampler must share their device and stream count")
+        self.head, self.resampler = head, resampler
+
+    def push(self, y0, y1) -> torch.Tensor:
+        return self.resampler.push(self.head.push(y0, y1))
+
+    def flush(self) -> torch.Tensor:
+        return torch.cat([self.resampler.push(self.head.flush()), self.resampler.flush()], dim=-1)
+
+    def copy(self) -> "StreamTail":
+        return StreamTail(self.head.copy(), self.resampler.copy())
