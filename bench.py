@@ -833,24 +833,30 @@ def vocoder_inputs(streams: int, frames: int, seed: int = 12):
 def bench_vocoder_tail(pkg, dev, streams=256, frames=240, chunk=4, reps=3):
     """The codec's DSP tail (two-branch iSTFT head + FIR mixer + 44.1 kHz resampler, float64) for 256 lock-step streams
     and one second of audio each (240 head frames): pushed at once, and pushed 4 frames at a time as a streaming decode
-    does; fresh streams each rep, timed with CUDA events from the first push to the flush."""
+    does (also end to end as the codec's stream runs: the frames are the trunk's output on the device, each push's
+    samples are read back to the host); fresh streams each rep, timed with CUDA events from the first push to the
+    flush."""
     voc = pkg.vocoder
     ys, windows, mixer, (kernel, orig, new, width) = vocoder_inputs(streams, frames)
     y0, y1 = (torch.from_numpy(y).to(dev) for y in ys)
 
-    def run(step):
+    def run(step, host=False):
         head = voc.IstftHeadStream((736, 2208), 184, windows, mixer, math.log(100.0), dev, streams=streams,
                                    max_cols=step)
         res = voc.ResamplerStream(kernel, orig, new, width, dev, streams=streams)
         torch.cuda.synchronize(dev)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        n = 0
+        n, outs = 0, []
         for c0 in range(0, frames, step):
-            n += res.push(head.push(y0[:, c0:c0 + step], y1[:, c0:c0 + step])).shape[1]
-        n += res.push(head.flush()).shape[1] + res.flush().shape[1]
+            o = res.push(head.push(y0[:, c0:c0 + step], y1[:, c0:c0 + step]))
+            outs.append(o.to("cpu", non_blocking=True) if host else o)  # e2e: each push's samples read back
+        outs += [res.push(head.flush()), res.flush()]
+        if host:
+            outs[-2:] = [o.to("cpu", non_blocking=True) for o in outs[-2:]]
         end.record()
         torch.cuda.synchronize(dev)
+        n = sum(o.shape[1] for o in outs)
         return start.elapsed_time(end), n
 
     out = {"workload": f"codec DSP tail: {streams} streams x {frames} head frames (1 s of 44.1 kHz audio each), "
@@ -861,6 +867,12 @@ def bench_vocoder_tail(pkg, dev, streams=256, frames=240, chunk=4, reps=3):
         samples = run(step)[1]
         out[label] = {"ms": ms, "samples_per_s": streams * samples / (ms / 1e3),
                       "realtime_x": streams * samples / 44100 / (ms / 1e3)}
+    run(chunk, host=True)
+    ms = min(run(chunk, host=True)[0] for _ in range(reps))
+    samples = run(chunk, host=True)[1]
+    out["stream4_e2e"] = {"ms": ms, "samples_per_s": streams * samples / (ms / 1e3),
+                          "realtime_x": streams * samples / 44100 / (ms / 1e3),
+                          "h2d_bytes": 0, "d2h_bytes": streams * samples * 4}
     out["ms"] = out["bulk"]["ms"]
     out["cpu_baseline"] = cpu_vocoder_tail(ys, windows, mixer, (kernel, orig, new, width), streams)
     return out
@@ -1009,7 +1021,7 @@ def operator_summary(ops_: dict) -> dict:
             item["largest_route_frac"] = round(r["largest_route"]["frac"], 3)
         if "cpu_baseline" in r:
             item["cpu_ms"] = round(r["cpu_baseline"]["ms_per_layer"], 1)
-        for key in ("bulk", "stream4"):
+        for key in ("bulk", "stream4", "stream4_e2e"):
             if key in r:
                 item[key] = {"ms": round(r[key]["ms"], 3), "realtime_x": round(r[key]["realtime_x"])}
         out[name] = item
