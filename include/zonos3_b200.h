@@ -389,7 +389,10 @@ int zb_istft_twiddles(int n, double* out, cudaStream_t stream);
  *   ring_b        [streams, ring_size] float64 mixer-input history (power-of-two size, zero before the first push)
  *   frames_before head frames pushed before this call; mix_from / mix_to the mixer outputs to emit (the caller's
  *                 stream position and the reference's emission bound); flush: cols == 0, mix_to = frames * hop
- *   scratch       >= streams * cols * (n0 + n1) float64 frame scratch; out [streams, mix_to - mix_from] float32.
+ *   scratch       float64, streams * cols * (n0 + n1) elements always suffice: the synthesised frames, or for a push
+ *                 of 32 frames or more with an even hop (n_b <= 17 hop) the overlap-add spans of its 16-frame groups,
+ *                 which the frame kernels add up themselves (then less is enough: 2 * streams * (cols / 16) *
+ *                 (31 hop + max(n) - hop) elements); out [streams, mix_to - mix_from] float32.
  * n_b even, a multiple of hop with n_b / hop >= 2, n_b <= 8192. */
 int zb_istft_head_push(const void* y0, int64_t y0_stride, const void* y1, int64_t y1_stride, int y_is_f64,
                        int streams, int cols, int n0, int n1, int hop,
